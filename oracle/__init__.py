@@ -1,0 +1,320 @@
+"""ctypes bindings of the CPU oracle (``libditch_oracle.so``).
+
+TEST INFRASTRUCTURE ONLY: the oracle is the parity checker for the CUDA
+product and the timed CPU baseline. Only ``tests/``, ``__graft_entry__.smoke()``
+and ``bench.py``'s CPU-baseline leg import this package.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+f32p = C.POINTER(C.c_float)
+u16p = C.POINTER(C.c_uint16)
+u8p = C.POINTER(C.c_uint8)
+u32p = C.POINTER(C.c_uint32)
+f64p = C.POINTER(C.c_double)
+szp = C.POINTER(C.c_size_t)
+
+
+class Config(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_int), ("hidden", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
+        ("head_dim", C.c_int), ("inter", C.c_int), ("vocab", C.c_int), ("eps", C.c_float),
+        ("rope_theta", C.c_double), ("qk_norm", C.c_int), ("rope_scaling", C.c_int),
+        ("rope_factor", C.c_double), ("rope_low_ff", C.c_double), ("rope_high_ff", C.c_double),
+        ("rope_orig_max", C.c_double), ("n_experts", C.c_int), ("top_k", C.c_int),
+        ("moe_inter", C.c_int), ("norm_topk", C.c_int),
+    ]
+
+
+class Layer(C.Structure):
+    _fields_ = [
+        ("input_norm", f32p), ("post_norm", f32p),
+        ("q", f32p), ("k", f32p), ("v", f32p), ("o", f32p),
+        ("qb", f32p), ("kb", f32p), ("vb", f32p),
+        ("q_norm", f32p), ("k_norm", f32p),
+        ("gate", f32p), ("up", f32p), ("down", f32p),
+        ("router", f32p), ("e_gate", f32p), ("e_up", f32p), ("e_down", f32p),
+        ("o_da", f32p), ("o_db", f32p), ("o_rank", C.c_size_t),
+        ("down_da", f32p), ("down_db", f32p), ("down_rank", C.c_size_t),
+        ("e_down_da", C.POINTER(f32p)), ("e_down_db", C.POINTER(f32p)),
+    ]
+
+
+class Model(C.Structure):
+    _fields_ = [("c", Config), ("embed", f32p), ("final_norm", f32p), ("lm_head", f32p),
+                ("layers", C.POINTER(Layer))]
+
+
+class Params(C.Structure):
+    _fields_ = [("max_weight", C.c_float), ("max_weight_position", C.c_float),
+                ("min_weight", C.c_float), ("min_weight_distance", C.c_float)]
+
+
+def lib():
+    """Loads the oracle library (built by ``make -C oracle``)."""
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(_HERE, "libditch_oracle.so")
+        if not os.path.exists(path):
+            raise RuntimeError("oracle not built: run `make -C oracle`")
+        L = C.CDLL(path)
+        L.or_f32_to_bf16.restype = C.c_uint16
+        L.or_f32_to_bf16.argtypes = [C.c_float]
+        L.or_bf16_to_f32.restype = C.c_float
+        L.or_bf16_to_f32.argtypes = [C.c_uint16]
+        L.or_f16_to_f32.restype = C.c_float
+        L.or_f16_to_f32.argtypes = [C.c_uint16]
+        L.or_dot.restype = C.c_float
+        L.or_dot.argtypes = [f32p, f32p, C.c_size_t]
+        L.or_matmul_t.argtypes = [f32p, f32p, C.c_size_t, f32p, C.c_size_t, C.c_size_t, f32p, f32p, C.c_size_t]
+        L.or_matvec_t_multi.argtypes = [f32p, f32p, C.c_size_t, C.c_size_t, f32p, C.c_size_t]
+        L.or_row_norms.argtypes = [f32p, f32p, C.c_size_t, C.c_size_t]
+        L.or_rmsnorm.argtypes = [f32p, f32p, f32p, C.c_size_t, C.c_float]
+        L.or_softmax_inplace.argtypes = [f32p, C.c_size_t]
+        L.or_log_softmax.argtypes = [f32p, f32p, C.c_size_t]
+        L.or_gated_silu.argtypes = [f32p, f32p, f32p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t]
+        L.or_rope_table.argtypes = [f32p, f32p, C.c_size_t, C.c_size_t, C.c_double, C.c_int,
+                                    C.c_double, C.c_double, C.c_double, C.c_double]
+        L.or_dequant_ggml.restype = C.c_int
+        L.or_dequant_ggml.argtypes = [C.c_int, u8p, f32p, C.c_size_t]
+        L.or_ggml_block_size.restype = C.c_size_t
+        L.or_ggml_block_size.argtypes = [C.c_int]
+        L.or_ggml_block_bytes.restype = C.c_size_t
+        L.or_ggml_block_bytes.argtypes = [C.c_int]
+        L.or_quant_q8_0.argtypes = [f32p, u8p, C.c_size_t]
+        L.or_quant_q4_k.argtypes = [f32p, u8p, C.c_size_t]
+        L.or_e4m3_value.restype = C.c_float
+        L.or_e4m3_value.argtypes = [C.c_uint8]
+        L.or_e8m0_scale.restype = C.c_float
+        L.or_e8m0_scale.argtypes = [C.c_uint8]
+        L.or_dequant_fp8.argtypes = [u8p, f32p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, u16p]
+        L.or_dequant_int_packed.argtypes = [u32p, C.c_size_t, f32p, u32p, u32p, C.c_size_t,
+                                            C.c_size_t, C.c_int, C.c_size_t, u16p]
+        L.or_dequant_mxfp4_packed.argtypes = [u8p, u8p, C.c_size_t, C.c_size_t, u16p]
+        L.or_dequant_mxfp4_transposed.argtypes = [u8p, u8p, C.c_size_t, C.c_size_t, u16p]
+        L.or_unpack_field.restype = C.c_uint32
+        L.or_unpack_field.argtypes = [u32p, C.c_size_t, C.c_int]
+        L.or_quant_fp8_block.argtypes = [f32p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, u8p, f32p]
+        L.or_quant_mxfp4_packed.argtypes = [f32p, C.c_size_t, C.c_size_t, u8p, u8p]
+        L.or_quant_int_packed.argtypes = [f32p, C.c_size_t, C.c_size_t, C.c_int, C.c_size_t, u32p, f32p, u32p]
+        L.or_forward.restype = C.c_int
+        L.or_forward.argtypes = [C.POINTER(Model), u32p, u32p, u32p, C.c_size_t, szp, C.c_size_t,
+                                 f32p, szp, C.c_size_t, f32p]
+        L.or_kernel_weight.restype = C.c_int
+        L.or_kernel_weight.argtypes = [Params, C.c_size_t, f32p]
+        L.or_compute_directions.argtypes = [f32p, f32p, C.c_size_t, C.c_size_t, C.c_int, f32p]
+        L.or_compute_delta_none.argtypes = [f32p, C.c_size_t, C.c_size_t, f32p, C.c_float, f32p, f32p]
+        L.or_materialize.argtypes = [f32p, C.c_size_t, C.c_size_t, f32p, f32p, C.c_size_t, f32p]
+        L.or_score_down.restype = C.c_float
+        L.or_score_down.argtypes = [f32p, C.c_size_t, C.c_size_t, f32p]
+        L.or_rank_scores.argtypes = [f32p, C.c_size_t, u32p]
+        L.or_residual_sums.argtypes = [f32p, C.c_size_t, C.c_size_t, C.c_size_t, szp, szp, C.c_size_t, f64p]
+        L.or_kl_first_token.restype = C.c_double
+        L.or_kl_first_token.argtypes = [f32p, f32p, C.c_size_t, C.c_size_t, f64p]
+        L.or_set_threads.argtypes = [C.c_int]
+        L.or_get_threads.restype = C.c_int
+        _LIB = L
+    return _LIB
+
+
+def ptr(a, t=f32p):
+    """Pointer to a C-contiguous numpy array (None stays NULL)."""
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "array must be C-contiguous"
+    return a.ctypes.data_as(t)
+
+
+def f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ---- thin numpy wrappers --------------------------------------------------
+
+def bf16_bits_to_f32(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x):
+    """src/tensor.zig:423-430 in numpy (round to nearest even, NaN kept quiet)."""
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    nan = (b & 0x7FFFFFFF) > 0x7F800000
+    r = ((b + np.uint32(0x7FFF) + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(nan, ((b >> 16) | 0x40).astype(np.uint16), r)
+
+
+def matmul_t(x, w, da=None, db=None):
+    x, w = f32(x), f32(w)
+    n, cols = x.shape
+    rows = w.shape[0]
+    out = np.zeros((n, rows), np.float32)
+    rank = 0 if da is None else da.reshape(-1, cols).shape[0]
+    da = None if da is None else f32(da)
+    db = None if db is None else f32(db)
+    lib().or_matmul_t(ptr(out), ptr(x), n, ptr(w), rows, cols, ptr(da), ptr(db), rank)
+    return out
+
+
+def matvec_t_multi(w, y):
+    w, y = f32(w), f32(y).reshape(-1, w.shape[0])
+    out = np.zeros((y.shape[0], w.shape[1]), np.float32)
+    lib().or_matvec_t_multi(ptr(out), ptr(w), w.shape[0], w.shape[1], ptr(y), y.shape[0])
+    return out
+
+
+def row_norms(w):
+    w = f32(w)
+    out = np.zeros(w.shape[0], np.float32)
+    lib().or_row_norms(ptr(out), ptr(w), w.shape[0], w.shape[1])
+    return out
+
+
+def dequant_ggml(dtype, raw, n):
+    raw = np.ascontiguousarray(raw, np.uint8)
+    out = np.zeros(n, np.float32)
+    if lib().or_dequant_ggml(dtype, ptr(raw, u8p), ptr(out), n) != 0:
+        raise ValueError("bad ggml dtype or size")
+    return out
+
+
+def quant_q8_0(x):
+    x = f32(x).ravel()
+    out = np.zeros(x.size // 32 * 34, np.uint8)
+    lib().or_quant_q8_0(ptr(x), ptr(out, u8p), x.size)
+    return out
+
+
+def quant_q4_k(x):
+    x = f32(x).ravel()
+    out = np.zeros(x.size // 256 * 144, np.uint8)
+    lib().or_quant_q4_k(ptr(x), ptr(out, u8p), x.size)
+    return out
+
+
+def dequant_fp8(codes, scales, br, bc):
+    codes = np.ascontiguousarray(codes, np.uint8)
+    scales = f32(scales)
+    rows, cols = codes.shape
+    out = np.zeros((rows, cols), np.uint16)
+    lib().or_dequant_fp8(ptr(codes, u8p), ptr(scales), rows, cols, br, bc, ptr(out, u16p))
+    return out
+
+
+def dequant_int_packed(packed, scales, zeros, rows, cols, bits, group, g_idx=None):
+    packed = np.ascontiguousarray(packed).view(np.uint32)
+    scales = f32(scales)
+    zeros = None if zeros is None else np.ascontiguousarray(zeros).view(np.uint32)
+    g_idx = None if g_idx is None else np.ascontiguousarray(g_idx).astype(np.uint32)
+    out = np.zeros((rows, cols), np.uint16)
+    lib().or_dequant_int_packed(ptr(packed, u32p), packed.shape[-1], ptr(scales), ptr(zeros, u32p),
+                                ptr(g_idx, u32p), rows, cols, bits, group, ptr(out, u16p))
+    return out
+
+
+def dequant_mxfp4_packed(blocks, scales, rows, cols):
+    blocks = np.ascontiguousarray(blocks, np.uint8)
+    scales = np.ascontiguousarray(scales, np.uint8)
+    out = np.zeros((rows, cols), np.uint16)
+    lib().or_dequant_mxfp4_packed(ptr(blocks, u8p), ptr(scales, u8p), rows, cols, ptr(out, u16p))
+    return out
+
+
+def quant_fp8_block(w, br=128, bc=128):
+    w = f32(w)
+    rows, cols = w.shape
+    codes = np.zeros((rows, cols), np.uint8)
+    scales = np.zeros((-(-rows // br), -(-cols // bc)), np.float32)
+    lib().or_quant_fp8_block(ptr(w), rows, cols, br, bc, ptr(codes, u8p), ptr(scales))
+    return codes, scales
+
+
+def quant_mxfp4_packed(w):
+    w = f32(w)
+    rows, cols = w.shape
+    blocks = np.zeros((rows, cols // 2), np.uint8)
+    scales = np.zeros((rows, cols // 32), np.uint8)
+    lib().or_quant_mxfp4_packed(ptr(w), rows, cols, ptr(blocks, u8p), ptr(scales, u8p))
+    return blocks, scales
+
+
+def quant_int_packed(w, bits=4, group=128):
+    w = f32(w)
+    rows, cols = w.shape
+    wpr = -(-cols * bits // 32)
+    packed = np.zeros((rows, wpr), np.uint32)
+    scales = np.zeros((rows, cols // group), np.float32)
+    zeros = np.zeros((-(-rows * bits // 32), cols // group), np.uint32)
+    lib().or_quant_int_packed(ptr(w), rows, cols, bits, group, ptr(packed, u32p), ptr(scales), ptr(zeros, u32p))
+    return packed, scales, zeros
+
+
+def kernel_weight(p, layer):
+    out = C.c_float(0)
+    ok = lib().or_kernel_weight(Params(*p), layer, C.byref(out))
+    return float(out.value) if ok else None
+
+
+def compute_directions(good, bad, orthogonalize=True):
+    good, bad = f32(good), f32(bad)
+    entries, hidden = good.shape
+    out = np.zeros_like(good)
+    lib().or_compute_directions(ptr(good), ptr(bad), entries, hidden, int(orthogonalize), ptr(out))
+    return out
+
+
+def compute_delta_none(w, v, lam):
+    w, v = f32(w), f32(v)
+    a = np.zeros(w.shape[1], np.float32)
+    b = np.zeros(w.shape[0], np.float32)
+    lib().or_compute_delta_none(ptr(w), w.shape[0], w.shape[1], ptr(v), lam, ptr(a), ptr(b))
+    return a, b
+
+
+def materialize(w, a, b):
+    w = f32(w)
+    a, b = f32(a).reshape(-1, w.shape[1]), f32(b).reshape(w.shape[0], -1)
+    out = np.zeros_like(w)
+    lib().or_materialize(ptr(w), w.shape[0], w.shape[1], ptr(a), ptr(b), a.shape[0], ptr(out))
+    return out
+
+
+def score_down(w, v):
+    w, v = f32(w), f32(v)
+    return float(lib().or_score_down(ptr(w), w.shape[0], w.shape[1], ptr(v)))
+
+
+def rank_scores(scores):
+    s = f32(scores)
+    out = np.zeros(s.size, np.uint32)
+    lib().or_rank_scores(ptr(s), s.size, ptr(out, u32p))
+    return out
+
+
+def kl_first_token(baseline_logp, logits):
+    b, l = f32(baseline_logp), f32(logits)
+    per = np.zeros(b.shape[0], np.float64)
+    v = lib().or_kl_first_token(ptr(b), ptr(l), b.shape[0], b.shape[1], ptr(per, f64p))
+    return v, per
+
+
+def log_softmax(x):
+    x = f32(x)
+    out = np.zeros_like(x)
+    for i in range(x.shape[0]):
+        lib().or_log_softmax(ptr(out[i]), ptr(x[i]), x.shape[1])
+    return out
+
+
+def residual_sums(res, first_capture, take):
+    res = f32(res)
+    entries, nc, hidden = res.shape
+    fc = np.ascontiguousarray(first_capture, np.uintp)
+    tk = np.ascontiguousarray(take, np.uintp)
+    sums = np.zeros((entries, hidden), np.float64)
+    lib().or_residual_sums(ptr(res), entries, nc, hidden, ptr(fc, szp), ptr(tk, szp), len(tk), ptr(sums, f64p))
+    return sums

@@ -1,0 +1,114 @@
+"""The oracle forward over a model given as f32 numpy weights.
+
+TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).
+
+Weights use canonical names shared with the CUDA product's loader:
+``embed``, ``final_norm``, ``lm_head`` and per layer ``L{i}.input_norm``,
+``L{i}.post_norm``, ``L{i}.q|k|v|o``, ``L{i}.qb|kb|vb``, ``L{i}.q_norm|k_norm``,
+``L{i}.gate|up|down`` (dense) or ``L{i}.router`` + ``L{i}.e_gate|e_up|e_down``
+(``[E][..][..]`` stacks, MoE).
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import Config, Layer, Model, f32, f32p, lib, ptr, szp, u32p
+
+
+class OracleModel:
+    def __init__(self, spec, weights):
+        self.spec = spec
+        self.w = {k: f32(v) for k, v in weights.items()}
+        self._keep = []
+        self.deltas = {}  # (layer, "o"|"down"|("e", e)) -> (a [cols], b [rows])
+
+    def set_delta(self, layer, comp, a, b):
+        self.deltas[(layer, comp)] = (f32(a), f32(b))
+
+    def reset_deltas(self):
+        self.deltas = {}
+
+    def _build(self):
+        s = self.spec
+        cfg = Config(
+            n_layers=s["n_layers"], hidden=s["hidden"], heads=s["heads"], kv_heads=s["kv_heads"],
+            head_dim=s["head_dim"], inter=s["inter"], vocab=s["vocab"], eps=s["eps"],
+            rope_theta=s["rope_theta"], qk_norm=int(s.get("qk_norm", 0)),
+            rope_scaling=int(s.get("rope_scaling", 0)), rope_factor=s.get("rope_factor", 1.0),
+            rope_low_ff=s.get("rope_low_ff", 1.0), rope_high_ff=s.get("rope_high_ff", 1.0),
+            rope_orig_max=s.get("rope_orig_max", 1.0), n_experts=s.get("n_experts", 0),
+            top_k=s.get("top_k", 0), moe_inter=s.get("moe_inter", 0),
+            norm_topk=int(s.get("norm_topk", 1)))
+        layers = (Layer * s["n_layers"])()
+        keep = []
+
+        def g(name):
+            a = self.w.get(name)
+            return None if a is None else ptr(a)
+
+        for i in range(s["n_layers"]):
+            L = layers[i]
+            for f in ("input_norm", "post_norm", "q", "k", "v", "o", "qb", "kb", "vb", "q_norm",
+                      "k_norm", "gate", "up", "down", "router", "e_gate", "e_up", "e_down"):
+                setattr(L, f, g(f"L{i}.{f}"))
+            if (i, "o") in self.deltas:
+                a, b = self.deltas[(i, "o")]
+                L.o_da, L.o_db, L.o_rank = ptr(a), ptr(b), 1
+            if (i, "down") in self.deltas:
+                a, b = self.deltas[(i, "down")]
+                L.down_da, L.down_db, L.down_rank = ptr(a), ptr(b), 1
+            E = s.get("n_experts", 0)
+            if E and f"L{i}.router" in self.w:
+                da = (f32p * E)()
+                db = (f32p * E)()
+                for e in range(E):
+                    if (i, ("e", e)) in self.deltas:
+                        a, b = self.deltas[(i, ("e", e))]
+                        da[e], db[e] = ptr(a), ptr(b)
+                L.e_down_da = C.cast(da, C.POINTER(f32p))
+                L.e_down_db = C.cast(db, C.POINTER(f32p))
+                keep += [da, db]
+        m = Model(c=cfg, embed=g("embed"), final_norm=g("final_norm"), lm_head=g("lm_head"),
+                  layers=C.cast(layers, C.POINTER(Layer)))
+        self._keep = [layers, keep]
+        return m
+
+    def forward(self, tokens, row_b, row_pos, capture_rows=(), logit_rows=()):
+        """Returns (residuals [L+1][nc][H], logits [nl][V])."""
+        s = self.spec
+        m = self._build()
+        tokens = np.ascontiguousarray(tokens, np.uint32)
+        rb = np.ascontiguousarray(row_b, np.uint32)
+        rp = np.ascontiguousarray(row_pos, np.uint32)
+        cap = np.ascontiguousarray(capture_rows, np.uintp)
+        lr = np.ascontiguousarray(logit_rows, np.uintp)
+        res = np.zeros((s["n_layers"] + 1, len(cap), s["hidden"]), np.float32)
+        logits = np.zeros((len(lr), s["vocab"]), np.float32)
+        rc = lib().or_forward(C.byref(m), ptr(tokens, u32p), ptr(rb, u32p), ptr(rp, u32p), len(tokens),
+                              ptr(cap, szp) if len(cap) else None, len(cap), ptr(res) if len(cap) else None,
+                              ptr(lr, szp) if len(lr) else None, len(lr), ptr(logits) if len(lr) else None)
+        if rc != 0:
+            raise ValueError("oracle forward failed (token id outside the embedding table?)")
+        return res, logits
+
+
+def flatten_batch(prompts, window=1):
+    """Flattens prompts into (tokens, row_b, row_pos, capture, first_capture,
+    take, last_rows) as src/engine.zig:392-410 does."""
+    tokens, rb, rp, capture, first, take, last = [], [], [], [], [], [], []
+    idx = 0
+    for b, p in enumerate(prompts):
+        tk = min(window, len(p))
+        first.append(len(capture))
+        take.append(tk)
+        for pos, t in enumerate(p):
+            tokens.append(t)
+            rb.append(b)
+            rp.append(pos)
+            if pos + tk >= len(p):
+                capture.append(idx)
+            idx += 1
+        last.append(idx - 1)
+    return (np.array(tokens, np.uint32), np.array(rb, np.uint32), np.array(rp, np.uint32),
+            np.array(capture, np.uintp), np.array(first, np.uintp), np.array(take, np.uintp),
+            np.array(last, np.uintp))

@@ -1,0 +1,126 @@
+"""Loads the committed golden fixtures (tests/golden/<family>.npz) into a
+model spec, f32 weights for the oracle and the raw stored tensors for the
+CUDA product's loader."""
+import json
+import os
+
+import numpy as np
+
+import oracle
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+class Golden:
+    def __init__(self, family):
+        z = np.load(os.path.join(GOLDEN, family + ".npz"))
+        self.family = family
+        self.config = json.loads(bytes(z["config_json"]).decode())
+        self.dtypes = json.loads(bytes(z["dtypes_json"]).decode())
+        self.raw = {k[2:]: z[k] for k in z.files if k.startswith("t/")}
+        self.cases = []
+        for i in range(int(z["n_cases"][0])):
+            self.cases.append({
+                "ids": z[f"case{i}/ids"],
+                "last_logits": z[f"case{i}/last_logits"],
+                "last_hidden": z[f"case{i}/last_hidden"],
+                "argmax": int(z[f"case{i}/argmax"][0]),
+            })
+        self.spec = self._spec()
+        self.block = None
+        q = self.config.get("quantization_config")
+        if q and q.get("quant_method") == "fp8":
+            self.block = tuple(q["weight_block_size"])
+        if q and q.get("quant_method") == "compressed-tensors":
+            w = q["config_groups"]["group_0"]["weights"]
+            self.int_bits, self.int_group = w["num_bits"], w["group_size"]
+
+    def _spec(self):
+        c = self.config
+        hd = c.get("head_dim") or c["hidden_size"] // c["num_attention_heads"]
+        s = dict(n_layers=c["num_hidden_layers"], hidden=c["hidden_size"], heads=c["num_attention_heads"],
+                 kv_heads=c["num_key_value_heads"], head_dim=hd, inter=c["intermediate_size"],
+                 vocab=c["vocab_size"], eps=c["rms_norm_eps"], rope_theta=c["rope_theta"],
+                 qk_norm=int(c["model_type"] in ("qwen3", "qwen3_moe")),
+                 tied=bool(c.get("tie_word_embeddings", False)))
+        rs = c.get("rope_scaling")
+        if rs and rs.get("rope_type") == "llama3":
+            s.update(rope_scaling=1, rope_factor=rs["factor"], rope_low_ff=rs["low_freq_factor"],
+                     rope_high_ff=rs["high_freq_factor"], rope_orig_max=rs["original_max_position_embeddings"])
+        if c["model_type"] == "qwen3_moe":
+            s.update(n_experts=c["num_experts"], top_k=c["num_experts_per_tok"], moe_inter=c["moe_intermediate_size"],
+                     norm_topk=int(c.get("norm_topk_prob", True)))
+            mlp_only = set(c.get("mlp_only_layers", []))
+            step = c.get("decoder_sparse_step", 1)
+            s["moe_layers"] = [(i not in mlp_only) and (i + 1) % step == 0 for i in range(s["n_layers"])]
+        return s
+
+    # ---- decoding to f32 (the oracle's view of every weight) ----
+    def _dense(self, name):
+        """f32 values of a stored weight, decoded like src/dequant.zig does at load."""
+        if name in self.raw:
+            dt = self.dtypes[name]
+            a = self.raw[name]
+            if dt == "BF16":
+                return oracle.bf16_bits_to_f32(a)
+            if dt == "F32":
+                return a.astype(np.float32)
+            if dt == "F8_E4M3":
+                br, bc = self.block
+                bits = oracle.dequant_fp8(a, self.raw[name + "_scale_inv"], br, bc)
+                return oracle.bf16_bits_to_f32(bits)
+            raise ValueError(f"unsupported dtype {dt} for {name}")
+        base = name[: -len(".weight")]
+        if base + ".weight_packed" in self.raw:
+            rows, cols = (int(v) for v in self.raw[base + ".weight_shape"])
+            scales = oracle.bf16_bits_to_f32(self.raw[base + ".weight_scale"])
+            zeros = self.raw.get(base + ".weight_zero_point")
+            bits = oracle.dequant_int_packed(self.raw[base + ".weight_packed"], scales, zeros, rows, cols,
+                                             self.int_bits, self.int_group)
+            return oracle.bf16_bits_to_f32(bits)
+        raise KeyError(name)
+
+    def hf_names(self):
+        """canonical name -> HF tensor name."""
+        s = self.spec
+        m = {"embed": "model.embed_tokens.weight", "final_norm": "model.norm.weight",
+             "lm_head": "model.embed_tokens.weight" if s["tied"] else "lm_head.weight"}
+        for i in range(s["n_layers"]):
+            p = f"model.layers.{i}."
+            m.update({f"L{i}.input_norm": p + "input_layernorm.weight",
+                      f"L{i}.post_norm": p + "post_attention_layernorm.weight"})
+            for a, b in (("q", "q_proj"), ("k", "k_proj"), ("v", "v_proj"), ("o", "o_proj")):
+                m[f"L{i}.{a}"] = p + f"self_attn.{b}.weight"
+            for a, b in (("qb", "q_proj"), ("kb", "k_proj"), ("vb", "v_proj")):
+                m[f"L{i}.{a}"] = p + f"self_attn.{b}.bias"
+            m[f"L{i}.q_norm"] = p + "self_attn.q_norm.weight"
+            m[f"L{i}.k_norm"] = p + "self_attn.k_norm.weight"
+            if s.get("moe_layers") and s["moe_layers"][i]:
+                m[f"L{i}.router"] = p + "mlp.gate.weight"
+            else:
+                for a in ("gate", "up", "down"):
+                    m[f"L{i}.{a}"] = p + f"mlp.{a}_proj.weight"
+        return m
+
+    def has(self, hf):
+        base = hf[: -len(".weight")] if hf.endswith(".weight") else hf
+        return hf in self.raw or base + ".weight_packed" in self.raw
+
+    def f32_weights(self):
+        s = self.spec
+        out = {}
+        for canon, hf in self.hf_names().items():
+            if self.has(hf):
+                out[canon] = self._dense(hf)
+        if s.get("moe_layers"):
+            for i in range(s["n_layers"]):
+                if not s["moe_layers"][i]:
+                    continue
+                p = f"model.layers.{i}.mlp.experts."
+                for a in ("gate", "up", "down"):
+                    out[f"L{i}.e_{a}"] = np.stack([self._dense(p + f"{e}.{a}_proj.weight")
+                                                   for e in range(s["n_experts"])])
+        return out
+
+    def prompts(self):
+        return [c["ids"].astype(np.uint32) for c in self.cases]
