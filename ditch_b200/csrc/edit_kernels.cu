@@ -1,0 +1,507 @@
+// Bandwidth-bound kernels of the edit, the scorers and the residual
+// reduction: GEMV-T (A = v^T W), row norms, the in-place rank-1 update, the
+// fused log-softmax / KL, and the f64 residual sums and directions.
+#include "kernels.cuh"
+
+namespace ditch {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide reductions (blockDim.x a multiple of 32, <= 1024).
+__device__ float block_sum(float v, float *sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    float t = lane < nw ? sh[lane] : 0.0f;
+    return warp_sum(t);
+}
+
+__device__ double block_sum_d(double v, double *sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum_d(v);
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    double t = lane < nw ? sh[lane] : 0.0;
+    return warp_sum_d(t);
+}
+
+__device__ float block_max(float v, float *sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    float t = lane < nw ? sh[lane] : -INFINITY;
+    return warp_max(t);
+}
+
+constexpr int kGemvThreads = 256;
+
+inline int row_splits(int rows, int col_blocks) {
+    const int target = 4 * 148;
+    int s = (target + col_blocks - 1) / col_blocks;
+    s = s < 1 ? 1 : s;
+    const int max_s = (rows + 15) / 16;  // at least 16 rows per split
+    return s > max_s ? (max_s < 1 ? 1 : max_s) : s;
+}
+
+// out[c] += sum_{r in split} v[r] W[r][c]; thread = 8 consecutive bf16 columns.
+__global__ void k_gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, int rows_per) {
+    const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
+    if (c0 >= cols) return;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c0 + 8 <= cols && (cols & 7) == 0) {
+        for (int r = r0; r < r1; r++) {
+            const float vr = v[r];
+            if (vr == 0.0f) continue;  // rows with y == 0 are skipped (src/tensor.zig:1065-1068)
+            uint4 q = __ldg(reinterpret_cast<const uint4 *>(w + (long long)r * cols + c0));
+            const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                acc[2 * j] = fmaf(vr, __uint_as_float(wd[j] << 16), acc[2 * j]);
+                acc[2 * j + 1] = fmaf(vr, __uint_as_float(wd[j] & 0xffff0000u), acc[2 * j + 1]);
+            }
+        }
+    } else {
+        for (int r = r0; r < r1; r++) {
+            const float vr = v[r];
+            if (vr == 0.0f) continue;
+            for (int j = 0; j < 8 && c0 + j < cols; j++)
+                acc[j] = fmaf(vr, bf16_bits_to_f32(w[(long long)r * cols + c0 + j]), acc[j]);
+        }
+    }
+    for (int j = 0; j < 8 && c0 + j < cols; j++) atomicAdd(out + c0 + j, acc[j]);
+}
+
+__global__ void k_gemv_t_f32(const float *w, int rows, int cols, const float *v, float *out, int rows_per) {
+    const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
+    if (c0 >= cols) return;
+    float acc[4] = {0, 0, 0, 0};
+    for (int r = r0; r < r1; r++) {
+        const float vr = v[r];
+        if (vr == 0.0f) continue;
+        if (c0 + 4 <= cols && (cols & 3) == 0) {
+            float4 q = __ldg(reinterpret_cast<const float4 *>(w + (long long)r * cols + c0));
+            acc[0] = fmaf(vr, q.x, acc[0]);
+            acc[1] = fmaf(vr, q.y, acc[1]);
+            acc[2] = fmaf(vr, q.z, acc[2]);
+            acc[3] = fmaf(vr, q.w, acc[3]);
+        } else {
+            for (int j = 0; j < 4 && c0 + j < cols; j++) acc[j] = fmaf(vr, w[(long long)r * cols + c0 + j], acc[j]);
+        }
+    }
+    for (int j = 0; j < 4 && c0 + j < cols; j++) atomicAdd(out + c0 + j, acc[j]);
+}
+
+__device__ __forceinline__ void e4m3x4(uint32_t w, float *f) {
+    uint32_t h01, h23;
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+        : "=r"(h01), "=r"(h23)
+        : "r"(w));
+    float2 a = __half22float2(*reinterpret_cast<__half2 *>(&h01));
+    float2 b = __half22float2(*reinterpret_cast<__half2 *>(&h23));
+    f[0] = a.x;
+    f[1] = a.y;
+    f[2] = b.x;
+    f[3] = b.y;
+}
+
+// FP8 weights: each element is the decoded bf16 value bf16(code * scale),
+// as the reference's materialised weight (src/dequant.zig:505-511).
+__global__ void k_gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int cols, int br, int bc,
+                             int scols, const float *v, float *out, int rows_per) {
+    const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 16;
+    const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
+    if (c0 >= cols) return;
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) acc[j] = 0.0f;
+    const bool vec = (cols & 15) == 0 && (bc & 15) == 0;
+    for (int r = r0; r < r1; r++) {
+        const float vr = v[r];
+        if (vr == 0.0f) continue;
+        const float *srow = scales + (long long)(r / br) * scols;
+        if (vec) {
+            const float s = srow[c0 / bc];
+            uint4 q = __ldg(reinterpret_cast<const uint4 *>(codes + (long long)r * cols + c0));
+            const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float f[4];
+                e4m3x4(wd[j], f);
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    acc[4 * j + e] = fmaf(vr, bf16_bits_to_f32(f32_to_bf16_bits(f[e] * s)), acc[4 * j + e]);
+            }
+        } else {
+            for (int j = 0; j < 16 && c0 + j < cols; j++) {
+                float f[4];
+                e4m3x4(codes[(long long)r * cols + c0 + j], f);
+                acc[j] = fmaf(vr, bf16_bits_to_f32(f32_to_bf16_bits(f[0] * srow[(c0 + j) / bc])), acc[j]);
+            }
+        }
+    }
+    for (int j = 0; j < 16 && c0 + j < cols; j++) atomicAdd(out + c0 + j, acc[j]);
+}
+
+__device__ __constant__ float kE2M1e[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f,
+                                            -0.f, -0.5f, -1.f, -1.5f, -2.f, -3.f, -4.f, -6.f};
+
+__device__ __forceinline__ float mx_scale(uint32_t b) { return __uint_as_float(b == 0 ? 0x00400000u : (b << 23)); }
+
+// MXFP4 (natural layout); a thread covers one 32-element block of a row.
+__global__ void k_gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, const float *v,
+                               float *out, int rows_per) {
+    const int blk = blockIdx.x * blockDim.x + threadIdx.x;
+    const int nblk = cols / 32;
+    const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
+    if (blk >= nblk) return;
+    float acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; j++) acc[j] = 0.0f;
+    for (int r = r0; r < r1; r++) {
+        const float vr = v[r];
+        if (vr == 0.0f) continue;
+        const float s = mx_scale(scales[(long long)r * nblk + blk]);
+        uint4 q = __ldg(reinterpret_cast<const uint4 *>(blocks + (long long)r * (cols / 2) + blk * 16));
+        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const uint32_t byte = (wd[j / 4] >> (8 * (j & 3))) & 0xff;
+            acc[2 * j] = fmaf(vr, kE2M1e[byte & 0xf] * s, acc[2 * j]);
+            acc[2 * j + 1] = fmaf(vr, kE2M1e[byte >> 4] * s, acc[2 * j + 1]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++) atomicAdd(out + blk * 32 + j, acc[j]);
+}
+
+template <typename LOAD>
+__global__ void k_row_norms(int rows, int cols, float *out, LOAD load) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float s = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+        const float x = load(row, c);
+        s = fmaf(x, x, s);
+    }
+    s = warp_sum(s);
+    if (lane == 0) out[row] = sqrtf(s);
+}
+
+struct LoadBf16 {
+    const uint16_t *w;
+    int cols;
+    __device__ float operator()(int r, int c) const { return bf16_bits_to_f32(w[(long long)r * cols + c]); }
+};
+struct LoadF32 {
+    const float *w;
+    int cols;
+    __device__ float operator()(int r, int c) const { return w[(long long)r * cols + c]; }
+};
+struct LoadMxfp4 {
+    const uint8_t *b, *s;
+    int cols;
+    __device__ float operator()(int r, int c) const {
+        const uint8_t byte = b[(long long)r * (cols / 2) + c / 2];
+        return kE2M1e[(c & 1) ? (byte >> 4) : (byte & 0xf)] * mx_scale(s[(long long)r * (cols / 32) + c / 32]);
+    }
+};
+
+__global__ void k_rank1_bf16(uint16_t *w, int rows, int cols, const float *b, const float *a) {
+    const long long total8 = (long long)rows * cols / 8;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total8;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long e0 = i * 8;
+        const int r = (int)(e0 / cols), c0 = (int)(e0 % cols);
+        const float br = b[r];
+        uint4 *p = reinterpret_cast<uint4 *>(w + e0);
+        uint4 q = *p;
+        uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float lo = fmaf(br, a[c0 + 2 * j], __uint_as_float(wd[j] << 16));
+            const float hi = fmaf(br, a[c0 + 2 * j + 1], __uint_as_float(wd[j] & 0xffff0000u));
+            wd[j] = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+        }
+        *p = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    }
+}
+
+__global__ void k_rank1_bf16_scalar(uint16_t *w, int rows, int cols, const float *b, const float *a) {
+    const long long total = (long long)rows * cols;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(e / cols), c = (int)(e % cols);
+        w[e] = f32_to_bf16_bits(fmaf(b[r], a[c], bf16_bits_to_f32(w[e])));
+    }
+}
+
+__global__ void k_scale_vec(const float *v, float lambda, int n, float *b) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) b[i] = -lambda * v[i];
+}
+
+// ---- scoring ----
+__device__ float row_lse(const float *x, int vocab, float *shf, double *shd) {
+    float m = -INFINITY;
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) m = fmaxf(m, x[j]);
+    m = block_max(m, shf);
+    double s = 0.0;
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) s += exp((double)(x[j] - m));
+    s = block_sum_d(s, shd);
+    return m + (float)log(s);
+}
+
+__global__ void k_log_softmax(const float *x, int vocab, float *out) {
+    __shared__ float shf[32];
+    __shared__ double shd[32];
+    const float *xr = x + (long long)blockIdx.x * vocab;
+    const float lse = row_lse(xr, vocab, shf, shd);
+    float *o = out + (long long)blockIdx.x * vocab;
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) o[j] = xr[j] - lse;
+}
+
+__global__ void k_kl(const float *base, const float *logits, int vocab, double *kl) {
+    __shared__ float shf[32];
+    __shared__ double shd[32];
+    const float *xr = logits + (long long)blockIdx.x * vocab;
+    const float *lb = base + (long long)blockIdx.x * vocab;
+    const float lse = row_lse(xr, vocab, shf, shd);
+    double s = 0.0;
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+        const double b = (double)lb[j];
+        const float lt = xr[j] - lse;
+        s += exp(b) * (b - (double)lt);
+    }
+    s = block_sum_d(s, shd);
+    if (threadIdx.x == 0) kl[blockIdx.x] = s;
+}
+
+// ---- capture and directions ----
+// One thread per (entry, 4 hidden coordinates); prompts in order.
+__global__ void k_residual_sums(const float *res, int entries, int nc, int hidden, const int *first, const int *take,
+                                int prompts, double *sums) {
+    const int h4 = hidden / 4;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool vec = (hidden & 3) == 0;
+    const int per_entry = vec ? h4 : hidden;
+    if (idx >= entries * per_entry) return;
+    const int l = idx / per_entry, j = idx % per_entry;
+    if (vec) {
+        double s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+        for (int b = 0; b < prompts; b++) {
+            const int tk = take[b];
+            const float inv = 1.0f / (float)(tk > 0 ? tk : 1);
+            float v0 = 0, v1 = 0, v2 = 0, v3 = 0;
+            for (int t = 0; t < tk; t++) {
+                const float4 r = *reinterpret_cast<const float4 *>(res + ((long long)l * nc + first[b] + t) * hidden + 4 * j);
+                v0 = v0 + inv * r.x;
+                v1 = v1 + inv * r.y;
+                v2 = v2 + inv * r.z;
+                v3 = v3 + inv * r.w;
+            }
+            s0 += v0;
+            s1 += v1;
+            s2 += v2;
+            s3 += v3;
+        }
+        double *o = sums + (long long)l * hidden + 4 * j;
+        o[0] += s0;
+        o[1] += s1;
+        o[2] += s2;
+        o[3] += s3;
+    } else {
+        double s = 0;
+        for (int b = 0; b < prompts; b++) {
+            const int tk = take[b];
+            const float inv = 1.0f / (float)(tk > 0 ? tk : 1);
+            float v = 0;
+            for (int t = 0; t < tk; t++) v = v + inv * res[((long long)l * nc + first[b] + t) * hidden + j];
+            s += v;
+        }
+        sums[(long long)l * hidden + j] += s;
+    }
+}
+
+// One block per entry: means, difference, normalisation, orthogonalisation.
+__global__ void k_directions(const double *gs, double gc, const double *bs, double bc, int hidden, int ortho,
+                             float *dirs, float *gmean, float *bmean) {
+    __shared__ float sh[32];
+    const int e = blockIdx.x;
+    float *d = dirs + (long long)e * hidden;
+    const double *g = gs + (long long)e * hidden, *b = bs + (long long)e * hidden;
+    const double gcn = gc > 1 ? gc : 1, bcn = bc > 1 ? bc : 1;
+    float ss = 0.0f, gg = 0.0f;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        const float gm = (float)(g[i] / gcn), bm = (float)(b[i] / bcn);
+        if (gmean) gmean[(long long)e * hidden + i] = gm;
+        if (bmean) bmean[(long long)e * hidden + i] = bm;
+        const float v = bm - gm;
+        d[i] = v;
+        ss = fmaf(v, v, ss);
+        gg = fmaf(gm, gm, gg);
+    }
+    const float nd = sqrtf(block_sum(ss, sh));
+    const float ng = sqrtf(block_sum(gg, sh));
+    const float sd = nd > 1e-12f ? 1.0f / nd : 1.0f;
+    const float sg = ng > 1e-12f ? 1.0f / ng : 1.0f;
+    if (!ortho) {
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) d[i] = d[i] * sd;
+        return;
+    }
+    float pr = 0.0f;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        d[i] = d[i] * sd;
+        pr = fmaf(d[i], (float)(g[i] / gcn) * sg, pr);
+    }
+    const float proj = block_sum(pr, sh);
+    float s2 = 0.0f;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        const float v = d[i] + (-proj) * ((float)(g[i] / gcn) * sg);
+        d[i] = v;
+        s2 = fmaf(v, v, s2);
+    }
+    const float n2 = sqrtf(block_sum(s2, sh));
+    const float s3 = n2 > 1e-12f ? 1.0f / n2 : 1.0f;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) d[i] = d[i] * s3;
+}
+
+}  // namespace
+
+cudaError_t gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    const int cb = (cols + kGemvThreads * 8 - 1) / (kGemvThreads * 8);
+    const int sp = row_splits(rows, cb);
+    const int per = (rows + sp - 1) / sp;
+    k_gemv_t_bf16<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(w, rows, cols, v, out, per);
+    return cudaGetLastError();
+}
+
+cudaError_t gemv_t_f32(const float *w, int rows, int cols, const float *v, float *out, cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    const int cb = (cols + kGemvThreads * 4 - 1) / (kGemvThreads * 4);
+    const int sp = row_splits(rows, cb);
+    const int per = (rows + sp - 1) / sp;
+    k_gemv_t_f32<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(w, rows, cols, v, out, per);
+    return cudaGetLastError();
+}
+
+cudaError_t gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int cols, int br, int bc,
+                       const float *v, float *out, cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    const int cb = (cols + kGemvThreads * 16 - 1) / (kGemvThreads * 16);
+    const int sp = row_splits(rows, cb);
+    const int per = (rows + sp - 1) / sp;
+    k_gemv_t_fp8<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(codes, scales, rows, cols, br, bc,
+                                                                          (cols + bc - 1) / bc, v, out, per);
+    return cudaGetLastError();
+}
+
+cudaError_t gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, const float *v,
+                         float *out, cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    if (cols % 32) return cudaErrorInvalidValue;
+    const int nblk = cols / 32;
+    const int cb = (nblk + 127) / 128;
+    const int sp = row_splits(rows, cb);
+    const int per = (rows + sp - 1) / sp;
+    k_gemv_t_mxfp4<<<dim3(cb, (rows + per - 1) / per), 128, 0, st>>>(blocks, scales, rows, cols, v, out, per);
+    return cudaGetLastError();
+}
+
+cudaError_t row_norms_bf16(const uint16_t *w, int rows, int cols, float *out, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_row_norms<<<(rows + 7) / 8, 256, 0, st>>>(rows, cols, out, LoadBf16{w, cols});
+    return cudaGetLastError();
+}
+
+cudaError_t row_norms_f32(const float *w, int rows, int cols, float *out, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_row_norms<<<(rows + 7) / 8, 256, 0, st>>>(rows, cols, out, LoadF32{w, cols});
+    return cudaGetLastError();
+}
+
+cudaError_t row_norms_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, float *out,
+                            cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_row_norms<<<(rows + 7) / 8, 256, 0, st>>>(rows, cols, out, LoadMxfp4{blocks, scales, cols});
+    return cudaGetLastError();
+}
+
+cudaError_t rank1_update_bf16(uint16_t *w, int rows, int cols, const float *b, const float *a, cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    if ((cols & 7) == 0) {
+        const long long n8 = (long long)rows * cols / 8;
+        const int blocks = (int)std::min<long long>((n8 + 255) / 256, 148LL * 16);
+        k_rank1_bf16<<<blocks, 256, 0, st>>>(w, rows, cols, b, a);
+    } else {
+        const long long n = (long long)rows * cols;
+        const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
+        k_rank1_bf16_scalar<<<blocks, 256, 0, st>>>(w, rows, cols, b, a);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t scale_vec(const float *v, float lambda, int n, float *b, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_scale_vec<<<(n + 255) / 256, 256, 0, st>>>(v, lambda, n, b);
+    return cudaGetLastError();
+}
+
+cudaError_t log_softmax_rows(const float *x, int rows, int vocab, float *out, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_log_softmax<<<rows, 1024, 0, st>>>(x, vocab, out);
+    return cudaGetLastError();
+}
+
+cudaError_t kl_rows(const float *baseline, const float *logits, int rows, int vocab, double *kl, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_kl<<<rows, 1024, 0, st>>>(baseline, logits, vocab, kl);
+    return cudaGetLastError();
+}
+
+cudaError_t residual_sums(const float *res, int entries, int nc, int hidden, const int *first, const int *take,
+                          int prompts, double *sums, cudaStream_t st) {
+    const int per = (hidden & 3) == 0 ? hidden / 4 : hidden;
+    const int total = entries * per;
+    if (total <= 0) return cudaSuccess;
+    k_residual_sums<<<(total + 127) / 128, 128, 0, st>>>(res, entries, nc, hidden, first, take, prompts, sums);
+    return cudaGetLastError();
+}
+
+cudaError_t directions_from_sums(const double *good_sums, double good_count, const double *bad_sums,
+                                 double bad_count, int entries, int hidden, int orthogonalize, float *dirs,
+                                 float *good_mean, float *bad_mean, cudaStream_t st) {
+    if (entries <= 0) return cudaSuccess;
+    k_directions<<<entries, 256, 0, st>>>(good_sums, good_count, bad_sums, bad_count, hidden, orthogonalize, dirs,
+                                          good_mean, bad_mean);
+    return cudaGetLastError();
+}
+
+}  // namespace ditch

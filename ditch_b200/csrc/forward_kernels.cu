@@ -1,0 +1,301 @@
+// Forward-pass kernels around the GEMMs: embedding gather, RMSNorm with the
+// residual capture fused in, causal GQA attention with RoPE and q/k norms,
+// and the x . A row dot of a rank-1 delta.
+#include "kernels.cuh"
+
+namespace ditch {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// One warp per row. Token ids past the table set status (the reference's
+// embedRowIndex error, src/model.zig:2547) and leave the row zero.
+__global__ void k_embed(const void *table, int table_bf16, const uint32_t *tokens, int n, int hidden, float *x,
+                        const int *cap_slot, float *res, int *status, int vocab) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    const uint32_t t = tokens[row];
+    float *xr = x + (long long)row * hidden;
+    const int slot = cap_slot ? cap_slot[row] : -1;
+    float *cr = slot >= 0 ? res + (long long)slot * hidden : nullptr;
+    if (t >= (uint32_t)vocab) {
+        if (lane == 0 && status) atomicExch(status, kKernelBadArgument);
+        for (int i = lane; i < hidden; i += 32) xr[i] = 0.0f;
+        return;
+    }
+    for (int i = lane; i < hidden; i += 32) {
+        const float v = table_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(table)[(long long)t * hidden + i])
+                                   : reinterpret_cast<const float *>(table)[(long long)t * hidden + i];
+        xr[i] = v;
+        if (cr) cr[i] = v;
+    }
+}
+
+// RMSNorm of one f32 row (src/tensor.zig:1167-1179: inv = 1/sqrt(mean(x^2) + eps),
+// out = x * inv * w) to bf16; the captured copy is the un-normalised row.
+template <int HIDDEN_MAX>
+__global__ void k_rmsnorm_bf16(const float *x, const float *w, int n, int hidden, float eps, uint16_t *h,
+                               const int *cap_slot, float *res, const int *row_index) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    const int src = row_index ? row_index[row] : row;
+    const float *xr = x + (long long)src * hidden;
+    float ss = 0.0f;
+    if ((hidden & 3) == 0) {
+        for (int i = lane * 4; i < hidden; i += 128) {
+            float4 v = *reinterpret_cast<const float4 *>(xr + i);
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    } else {
+        for (int i = lane; i < hidden; i += 32) ss += xr[i] * xr[i];
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)hidden + eps);
+    uint16_t *hr = h + (long long)row * hidden;
+    const int slot = cap_slot ? cap_slot[src] : -1;
+    float *cr = slot >= 0 ? res + (long long)slot * hidden : nullptr;
+    for (int i = lane; i < hidden; i += 32) {
+        const float v = xr[i];
+        hr[i] = f32_to_bf16_bits(v * inv * w[i]);
+        if (cr) cr[i] = v;
+    }
+}
+
+__global__ void k_rmsnorm_f32(const float *x, const float *w, int n, int len, float eps, int gemma, float *out) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    const float *xr = x + (long long)row * len;
+    float ss = 0.0f;
+    for (int i = lane; i < len; i += 32) ss += xr[i] * xr[i];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)len + eps);
+    float *o = out + (long long)row * len;
+    for (int i = lane; i < len; i += 32) {
+        float v = xr[i] * inv;
+        if (w) v *= gemma ? (1.0f + w[i]) : w[i];
+        o[i] = v;
+    }
+}
+
+// ---- attention ----------------------------------------------------------
+// Block = (prompt, kv head). Keys and values of the prompt's rows for this kv
+// head are roped / normed once into shared memory in chunks of kKeyChunk;
+// each warp takes (query row, q head) pairs and runs an online softmax over
+// the causal key range.
+constexpr int kKeyChunk = 64;
+constexpr int kAttnWarps = 8;
+
+__device__ __forceinline__ void rope_neox_inplace(float *v, int hd, int pos, const float *cos_t, const float *sin_t,
+                                                  int lane) {
+    const int half = hd / 2;
+    const float *c = cos_t + (long long)pos * half;
+    const float *s = sin_t + (long long)pos * half;
+    // lanes split the half; x1 = v[i], x2 = v[i + half]
+    for (int i = lane; i < half; i += 32) {
+        const float x1 = v[i], x2 = v[i + half];
+        v[i] = x1 * c[i] - x2 * s[i];
+        v[i + half] = x2 * c[i] + x1 * s[i];
+    }
+}
+
+__device__ __forceinline__ void rms_inplace(float *v, int hd, const float *w, float eps, int lane) {
+    float ss = 0.0f;
+    for (int i = lane; i < hd; i += 32) ss += v[i] * v[i];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) v[i] = v[i] * inv * w[i];
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnParams p) {
+    extern __shared__ float sm[];
+    const int b = blockIdx.x, kvh = blockIdx.y;
+    const int hd = p.head_dim, nh = p.heads, nkv = p.kv_heads;
+    const int qd = nh * hd, kvd = nkv * hd, width = qd + 2 * kvd;
+    const int groups = nh / nkv;
+    const int start = p.seq_start[b], len = p.seq_len[b];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int ks = hd + 1;  // padded key stride (bank-conflict-free row reads)
+    float *kbuf = sm;                                  // [kKeyChunk][hd + 1]
+    float *vbuf = kbuf + kKeyChunk * ks;               // [kKeyChunk][hd]
+    float *qbuf = vbuf + kKeyChunk * hd;               // [kAttnWarps][hd]
+    float *pbuf = qbuf + kAttnWarps * hd;              // [kAttnWarps][kKeyChunk]
+    float *obuf = pbuf + kAttnWarps * kKeyChunk;       // [kAttnWarps][hd] accumulators
+    float *q = qbuf + warp * hd;
+    float *pw = pbuf + warp * kKeyChunk;
+    float *acc = obuf + warp * hd;
+
+    // Each warp owns query tasks t = warp, warp + kAttnWarps, ... over (row, head in group).
+    const int tasks = len * groups;
+    for (int t0 = 0; t0 < tasks; t0 += kAttnWarps) {
+        const int t = t0 + warp;
+        const bool active = t < tasks;
+        const int qi = active ? t / groups : 0;
+        const int h = kvh * groups + (active ? t % groups : 0);
+        float m = -INFINITY, l = 0.0f;
+        if (active) {
+            const float *src = p.qkv + (long long)(start + qi) * width + h * hd;
+            for (int i = lane; i < hd; i += 32) {
+                q[i] = src[i];
+                acc[i] = 0.0f;
+            }
+            __syncwarp();
+            if (p.q_norm) rms_inplace(q, hd, p.q_norm, p.eps, lane);
+            rope_neox_inplace(q, hd, qi, p.rope_cos, p.rope_sin, lane);
+            __syncwarp();
+        }
+        // The causal range of this batch of tasks spans keys [0, max qi].
+        const int last_q = min(len - 1, (min(t0 + kAttnWarps, tasks) - 1) / groups);
+        for (int k0 = 0; k0 <= last_q; k0 += kKeyChunk) {
+            const int nk = min(kKeyChunk, last_q + 1 - k0);
+            __syncthreads();
+            // Stage roped / normed keys and values for this chunk (all warps).
+            for (int kr = warp; kr < nk; kr += kAttnWarps) {
+                const float *row = p.qkv + (long long)(start + k0 + kr) * width;
+                float *kd = kbuf + kr * ks;
+                for (int i = lane; i < hd; i += 32) {
+                    kd[i] = row[qd + kvh * hd + i];
+                    vbuf[kr * hd + i] = row[qd + kvd + kvh * hd + i];
+                }
+                __syncwarp();
+                if (p.k_norm) rms_inplace(kd, hd, p.k_norm, p.eps, lane);
+                rope_neox_inplace(kd, hd, k0 + kr, p.rope_cos, p.rope_sin, lane);
+                __syncwarp();
+            }
+            __syncthreads();
+            if (active && k0 <= qi) {
+                const int nvalid = min(nk, qi - k0 + 1);
+                // scores: lanes over keys
+                float cmax = -INFINITY;
+                for (int kr = lane; kr < kKeyChunk; kr += 32) {
+                    float s = -INFINITY;
+                    if (kr < nvalid) {
+                        const float *kd = kbuf + kr * ks;
+                        float d = 0.0f;
+                        for (int i = 0; i < hd; i++) d = fmaf(q[i], kd[i], d);
+                        s = d * p.scale;
+                    }
+                    pw[kr] = s;
+                    cmax = fmaxf(cmax, s);
+                }
+                cmax = warp_max(cmax);
+                const float mnew = fmaxf(m, cmax);
+                const float corr = (m == -INFINITY) ? 0.0f : expf(m - mnew);
+                float csum = 0.0f;
+                for (int kr = lane; kr < kKeyChunk; kr += 32) {
+                    const float e = kr < nvalid ? expf(pw[kr] - mnew) : 0.0f;
+                    pw[kr] = e;
+                    csum += e;
+                }
+                csum = warp_sum(csum);
+                l = l * corr + csum;
+                m = mnew;
+                __syncwarp();
+                for (int i = lane; i < hd; i += 32) {
+                    float a = acc[i] * corr;
+                    for (int kr = 0; kr < nvalid; kr++) a = fmaf(pw[kr], vbuf[kr * hd + i], a);
+                    acc[i] = a;
+                }
+                __syncwarp();
+            }
+        }
+        if (active) {
+            const float inv = 1.0f / l;
+            uint16_t *dst = p.out + (long long)(start + qi) * qd + h * hd;
+            for (int i = lane; i < hd; i += 32) dst[i] = f32_to_bf16_bits(acc[i] * inv);
+        }
+        __syncwarp();
+    }
+}
+
+// xa[m] = sum_k act[m][k] * a[k], one warp per row.
+__global__ void k_rowdot_bf16(const uint16_t *act, const float *a, int m, int k, float *xa) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= m) return;
+    const uint16_t *r = act + (long long)row * k;
+    float s = 0.0f;
+    if ((k & 7) == 0) {
+        for (int i = lane * 8; i < k; i += 256) {
+            uint4 v = *reinterpret_cast<const uint4 *>(r + i);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                s = fmaf(__uint_as_float(w[j] << 16), a[i + 2 * j], s);
+                s = fmaf(__uint_as_float(w[j] & 0xffff0000u), a[i + 2 * j + 1], s);
+            }
+        }
+    } else {
+        for (int i = lane; i < k; i += 32) s = fmaf(bf16_bits_to_f32(r[i]), a[i], s);
+    }
+    s = warp_sum(s);
+    if (lane == 0) xa[row] = s;
+}
+
+}  // namespace
+
+cudaError_t embed_rows(const void *table, int table_bf16, const uint32_t *tokens, int n, int hidden, float *x,
+                       const int *cap_slot, float *res, int *status, int vocab, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_embed<<<(n + 7) / 8, 256, 0, st>>>(table, table_bf16, tokens, n, hidden, x, cap_slot, res, status, vocab);
+    return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_rows_bf16(const float *x, const float *w, int n, int hidden, float eps, uint16_t *h,
+                              const int *cap_slot, float *res, const int *row_index, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_rmsnorm_bf16<0><<<(n + 7) / 8, 256, 0, st>>>(x, w, n, hidden, eps, h, cap_slot, res, row_index);
+    return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_rows_f32(const float *x, const float *w, int n, int len, float eps, int gemma, float *out,
+                             cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_rmsnorm_f32<<<(n + 7) / 8, 256, 0, st>>>(x, w, n, len, eps, gemma, out);
+    return cudaGetLastError();
+}
+
+cudaError_t gather_rmsnorm_bf16(const float *x, const int *rows, int n, int hidden, float eps, const float *w,
+                                uint16_t *h, cudaStream_t st) {
+    return rmsnorm_rows_bf16(x, w, n, hidden, eps, h, nullptr, nullptr, rows, st);
+}
+
+cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st) {
+    if (p.n_prompts <= 0) return cudaSuccess;
+    if (p.heads % p.kv_heads) return cudaErrorInvalidValue;
+    const int hd = p.head_dim;
+    const size_t smem = sizeof(float) * (kKeyChunk * (hd + 1) + kKeyChunk * hd + kAttnWarps * hd +
+                                         kAttnWarps * kKeyChunk + kAttnWarps * hd);
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    dim3 grid(p.n_prompts, p.kv_heads);
+    k_attention<<<grid, kAttnWarps * 32, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t rowdot_bf16(const uint16_t *act, const float *a, int m, int k, float *xa, cudaStream_t st) {
+    if (m <= 0) return cudaSuccess;
+    k_rowdot_bf16<<<(m + 7) / 8, 256, 0, st>>>(act, a, m, k, xa);
+    return cudaGetLastError();
+}
+
+}  // namespace ditch

@@ -1,0 +1,78 @@
+// tcgen05/TMEM GEMM for ditch's weight products (`tensor.matmulT`,
+// src/tensor.zig:1023-1045): out[m][n] = x[m][:] . W[n][:] over K.
+//
+// Orientation: the WEIGHT is the MMA's M operand (128 weight rows per tile,
+// TMEM lane = weight row) and the TOKENS are the N operand (BN tokens per
+// tile). That makes the epilogue store coalesced (a warp writes 32
+// consecutive output features of one token) and lets small token counts
+// use a narrow N instead of padding a 128-row M tile.
+//
+// Weight formats:
+//   kFmtBf16  - bf16 weight tiles loaded by TMA straight into the swizzled
+//               operand layout;
+//   kFmtFp8   - E4M3 codes with f32 block scales (src/dequant.zig:477-514):
+//               TMA stages the raw code tile, four transform warps expand it
+//               to bf16(code * scale) in the swizzled operand layout;
+//   kFmtMxfp4 - E2M1 nibbles with E8M0 scales per 32 (src/dequant.zig:643-673);
+//   kFmtInt4  - compressed-tensors pack-quantized INT4 with f32 group scales
+//               and packed zero points (src/dequant.zig:518-597);
+//   kFmtQ8_0, kFmtQ4K - ggml blocks (src/quant.zig:81-85, 148-173), decoded
+//               to f32 and rounded to bf16 for the MMA.
+#pragma once
+
+#include "common.cuh"
+
+namespace ditch {
+
+enum WeightFormat : int {
+    kFmtBf16 = 0,
+    kFmtFp8 = 1,
+    kFmtMxfp4 = 2,
+    kFmtInt4 = 3,
+    kFmtQ8_0 = 4,
+    kFmtQ4K = 5,
+};
+
+// Epilogue flags.
+enum EpilogueFlags : int {
+    kEpiOutBf16 = 1,     // store bf16 instead of f32
+    kEpiResidual = 2,    // out (f32) += result, in place (the residual add)
+    kEpiSwiglu = 4,      // dual accumulators: out = silu(gate) * up (bf16)
+    kEpiAtomic = 8,      // split-K: atomically add f32 partial sums
+};
+
+struct GemmParams {
+    int m_w;       // valid weight rows (output features)
+    int n_tok;     // valid tokens
+    int k;         // reduction length
+    int w_tiles, t_tiles, k_tiles, k_splits;
+    int a2_row_offset;  // dual mode: row offset of the up weight in the A2 map
+    int a_row0;         // first weight row (a slab of a stacked tensor)
+    void *out;
+    long long ldo;      // row stride of out, in elements
+    int flags;
+    const float *bias;  // [m_w] or null
+    const float *xa;    // [n_tok]: x . a of a rank-1 delta, or null
+    const float *db;    // [m_w]:  B of the delta (-lambda v)
+    // quantised weights: per-format side data
+    const float *scales;     // fp8 block scales [rows/br][scols]; int4 [rows][groups]
+    const uint8_t *scales_u8;  // mxfp4 E8M0 scales [rows][k/32]
+    const uint32_t *zeros;   // int4 packed zero points [ceil(rows*4/32)][groups]
+    const uint8_t *raw;      // ggml blocks: raw rows (read with plain loads)
+    long long raw_row_bytes;
+    int blk_rows, blk_cols, scale_cols;  // fp8 block shape; int4 group in blk_cols
+    int *status;
+};
+
+// Host side: launches one GEMM on `stream`. Returns a CUDA error code.
+struct GemmOperand {
+    const void *ptr;    // device pointer of the operand (or raw codes)
+    int rows;           // rows of the whole tensor (for the TMA map)
+    int cols;           // K (elements)
+    long long row_bytes;
+};
+
+cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, const GemmOperand &b,
+                        GemmParams p, int num_sms, cudaStream_t stream);
+
+}  // namespace ditch

@@ -1,0 +1,121 @@
+// Bandwidth-bound and small kernels of the trial path (everything that is not
+// a weight GEMM). Each launcher runs on the given stream and returns the
+// launch's CUDA error code.
+#pragma once
+
+#include "common.cuh"
+
+namespace ditch {
+
+// ---- standalone decoders (bit-exact restatements of the reference) --------
+// bf16(e4m3[code] * scale[r / br][c / bc])             src/dequant.zig:477-514
+cudaError_t dequant_fp8_bf16(const uint8_t *codes, const float *scales, int rows, int cols, int br, int bc,
+                             uint16_t *out, cudaStream_t st);
+// pack-quantized INT (any bits <= 8), optional zeros and g_idx   dequant.zig:518-597
+cudaError_t dequant_int_bf16(const uint32_t *packed, long long wpr, const float *scales, const uint32_t *zeros,
+                             const uint32_t *g_idx, int groups, int rows, int cols, int bits, int group,
+                             uint16_t *out, cudaStream_t st);
+// natural-layout MXFP4                                   dequant.zig:643-673
+cudaError_t dequant_mxfp4_bf16(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, uint16_t *out,
+                               cudaStream_t st);
+// gpt-oss transposed MXFP4                               dequant.zig:603-637
+cudaError_t dequant_mxfp4t_bf16(const uint8_t *blocks, const uint8_t *scales, int src_rows, int src_cols,
+                                uint16_t *out, cudaStream_t st);
+// ggml blocks to f32 (dtype codes of src/tensor.zig:11-32)  quant.zig:57-209
+cudaError_t dequant_ggml_f32(int dtype, const uint8_t *src, long long n, float *out, cudaStream_t st);
+// ggml blocks to bf16 (the GEMM operand of a GGUF weight)
+cudaError_t dequant_ggml_bf16(int dtype, const uint8_t *src, long long n, uint16_t *out, cudaStream_t st);
+
+cudaError_t f32_to_bf16(const float *src, uint16_t *dst, long long n, cudaStream_t st);
+cudaError_t bf16_to_f32(const uint16_t *src, float *dst, long long n, cudaStream_t st);
+cudaError_t f16_to_f32(const uint16_t *src, float *dst, long long n, cudaStream_t st);
+
+// ---- forward pieces -------------------------------------------------------
+// x[i] = embed[tokens[i]] (bf16 or f32 table); entry-0 capture of rows with
+// cap_slot[i] >= 0 into res[cap_slot][H].
+cudaError_t embed_rows(const void *table, int table_bf16, const uint32_t *tokens, int n, int hidden, float *x,
+                       const int *cap_slot, float *res, int *status, int vocab, cudaStream_t st);
+
+// h = bf16(rmsnorm(x) * w) per row; rows with cap_slot[i] >= 0 are also
+// copied (pre-norm, f32) to res[cap_slot][H] (the residual capture of the
+// previous layer's output, src/model.zig:4856-4862).
+cudaError_t rmsnorm_rows_bf16(const float *x, const float *w, int n, int hidden, float eps, uint16_t *h,
+                              const int *cap_slot, float *res, const int *row_index, cudaStream_t st);
+// f32 in/out RMSNorm of n rows (the VTable rmsnormRows, src/tensor.zig:1167-1179).
+cudaError_t rmsnorm_rows_f32(const float *x, const float *w, int n, int len, float eps, int gemma, float *out,
+                             cudaStream_t st);
+// Gather rows then RMSNorm to bf16 (final norm of the logit rows).
+cudaError_t gather_rmsnorm_bf16(const float *x, const int *rows, int n, int hidden, float eps, const float *w,
+                                uint16_t *h, cudaStream_t st);
+
+struct AttnParams {
+    const float *qkv;       // [n][qd + 2 kvd] (q | k | v), biases already added
+    uint16_t *out;          // [n][qd] bf16
+    const int *seq_start;   // per prompt: first row
+    const int *seq_len;     // per prompt: rows
+    int n_prompts;
+    int heads, kv_heads, head_dim;
+    const float *rope_cos, *rope_sin;  // [max_pos][head_dim / 2]
+    const float *q_norm, *k_norm;      // per-head RMSNorm weights or null
+    float eps, scale;
+    int *status;
+};
+// Causal attention within each prompt with GQA, RoPE (neox) and optional q/k
+// norms (src/model.zig:4226-4374, attentionWorker 2935-2986).
+cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st);
+
+// xa[m] = sum_k act[m][k] * a[k] (act bf16, a f32): the x . A term of a rank-1
+// delta (src/tensor.zig:1036-1042).
+cudaError_t rowdot_bf16(const uint16_t *act, const float *a, int m, int k, float *xa, cudaStream_t st);
+
+// ---- edit (src/abliterate.zig:264-280) and ranking (src/moe.zig:1239-1306) --
+// out[c] = sum_r v[r] W[r][c] over a weight in its stored format (bf16 or
+// FP8 blocks); out must be zeroed (split-K partial sums are atomically added).
+cudaError_t gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, cudaStream_t st);
+cudaError_t gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int cols, int br, int bc,
+                       const float *v, float *out, cudaStream_t st);
+cudaError_t gemv_t_f32(const float *w, int rows, int cols, const float *v, float *out, cudaStream_t st);
+cudaError_t gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, const float *v,
+                         float *out, cudaStream_t st);
+// out[r] = ||W_r||_2
+cudaError_t row_norms_bf16(const uint16_t *w, int rows, int cols, float *out, cudaStream_t st);
+cudaError_t row_norms_f32(const float *w, int rows, int cols, float *out, cudaStream_t st);
+cudaError_t row_norms_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, float *out,
+                            cudaStream_t st);
+// W[r][c] = bf16(W[r][c] + b[r] * a[c]) in place (the materialised edit
+// W <- W - alpha r (r^T W) with b = -alpha r, a = r^T W).
+cudaError_t rank1_update_bf16(uint16_t *w, int rows, int cols, const float *b, const float *a, cudaStream_t st);
+// b[i] = -lambda * v[i]
+cudaError_t scale_vec(const float *v, float lambda, int n, float *b, cudaStream_t st);
+
+// ---- scoring ----------------------------------------------------------------
+// Per row: logSoftmax with an f64 sum (src/tensor.zig:1203-1210).
+cudaError_t log_softmax_rows(const float *x, int rows, int vocab, float *out, cudaStream_t st);
+// Per row: sum_j exp(lb_j) (lb_j - logsoftmax(x)_j) in f64 (src/scorers.zig:378-402).
+cudaError_t kl_rows(const float *baseline, const float *logits, int rows, int vocab, double *kl, cudaStream_t st);
+
+// ---- capture and directions -------------------------------------------------
+// sums[l][h] += mean over take[b] captures of prompt b (f64), per prompt and
+// entry (src/engine.zig:414-431).
+cudaError_t residual_sums(const float *res, int entries, int nc, int hidden, const int *first, const int *take,
+                          int prompts, double *sums, cudaStream_t st);
+// dirs[e] = normalize(bad - good) (orthogonalised against normalize(good)),
+// from f64 sums and counts (src/abliterate.zig:88-109, engine.zig:334-336).
+cudaError_t directions_from_sums(const double *good_sums, double good_count, const double *bad_sums,
+                                 double bad_count, int entries, int hidden, int orthogonalize, float *dirs,
+                                 float *good_mean, float *bad_mean, cudaStream_t st);
+
+// ---- element-wise entries of the compute seam (src/compute.zig:90-117) -------
+cudaError_t softmax_rows_f32(float *x, int n, int len, cudaStream_t st);
+cudaError_t gated_silu_f32(const float *gate, const float *up, int n, int len, long long in_stride,
+                           long long out_stride, float *out, cudaStream_t st);
+cudaError_t rope_rows_f32(float *x, int n, int dim, const float *cos, const float *sin, int half, const uint32_t *pos,
+                          int style, cudaStream_t st);
+cudaError_t attention_scores_f32(float *scores, const float *q, int hd, const float *k, int n_keys, long long stride,
+                                 float scale, cudaStream_t st);
+cudaError_t attention_values_f32(float *out, const float *scores, int n_keys, const float *v, int vd,
+                                 long long stride, cudaStream_t st);
+cudaError_t layernorm_rows_f32(const float *x, const float *w, const float *b, int n, int len, float eps,
+                               int one_plus, float *out, cudaStream_t st);
+
+}  // namespace ditch

@@ -1,0 +1,127 @@
+// The resident model: weights in HBM in their GEMM-ready storage, the
+// forward's workspace, the per-layer rank-1 edits, the refusal directions and
+// the KL prompts with their baseline log-probabilities.
+#pragma once
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "device.cuh"
+
+namespace ditch {
+
+// A weight matrix (or a stack of `slabs` expert matrices) in the storage the
+// GEMM reads: bf16, or a quantised format decoded inside the GEMM.
+struct Mat {
+    int fmt = kFmtBf16;
+    int rows = 0, cols = 0, slabs = 1;  // rows per slab
+    long long row_bytes = 0;
+    DevBuf data;    // bf16 [slabs*rows][cols] | E4M3 codes | MXFP4 nibbles | INT4 words
+    DevBuf scales;  // FP8 f32 [slabs*srows][scols] | MXFP4 u8 [slabs*rows][cols/32] | INT4 f32 [slabs*rows][groups]
+    DevBuf zeros;   // INT4 packed zero points [slabs*rows/8][groups]
+    int br = 0, bc = 0, scols = 0, groups = 0, group = 0;
+    bool empty() const { return data.ptr == nullptr; }
+    size_t bytes() const { return data.bytes + scales.bytes + zeros.bytes; }
+};
+
+struct Layer {
+    DevBuf input_norm, post_norm, q_norm, k_norm;  // f32
+    Mat qkv;                                       // [qd + 2 kvd][H]
+    DevBuf qkv_bias;                               // f32 [qd + 2 kvd] or empty
+    Mat o;                                         // [H][qd]
+    Mat gate_up;                                   // [2 I][H]: gate rows then up rows
+    Mat down;                                      // [H][I]
+    bool moe = false;
+    Mat router;                                    // [E][H] (bf16)
+    Mat e_gate_up;                                 // [E][2 mi][H]: per expert gate rows then up rows
+    Mat e_down;                                    // [E][H][mi]
+    // none-mode deltas (src/abliterate.zig:270-280): out += (x . a) b
+    bool o_edit = false, down_edit = false;
+    DevBuf o_a, o_b, down_a, down_b;               // f32 [qd], [H], [I], [H]
+    std::vector<uint8_t> e_edit;                   // per expert
+    DevBuf e_a, e_b;                               // f32 [E][mi], [E][H]
+    DevBuf e_edit_dev;                             // int [E]
+};
+
+struct Config {
+    int n_layers, hidden, heads, kv_heads, head_dim, inter, vocab;
+    float eps;
+    double rope_theta;
+    int rope_scaling;
+    double rope_factor, rope_low_ff, rope_high_ff, rope_orig_max;
+    int qk_norm;
+    int n_experts, top_k, moe_inter, norm_topk;
+    std::vector<uint8_t> moe_layers;
+    int max_seq;
+    int qd() const { return heads * head_dim; }
+    int kvd() const { return kv_heads * head_dim; }
+    int qkv_width() const { return qd() + 2 * kvd(); }
+};
+
+// One flattened batch of prompts on the device.
+struct Batch {
+    int n = 0, prompts = 0;
+    DevBuf tokens, seq_start, seq_len, cap_slot, logit_rows;
+    std::vector<int> h_start, h_len;
+};
+
+}  // namespace ditch
+
+struct ditch_cuda_model {
+    ditch_cuda_device *dev = nullptr;
+    ditch::Config cfg;
+    ditch::DevBuf embed;
+    bool embed_bf16 = true;
+    ditch::DevBuf final_norm;
+    ditch::Mat lm_head;
+    std::vector<ditch::Layer> layers;
+    ditch::DevBuf rope_cos, rope_sin;
+    int rope_len = 0;
+    // workspace
+    int ws_tokens = 0;
+    ditch::DevBuf x, h, qkv, att, act, xa;
+    ditch::DevBuf res, hl, logits;
+    // MoE workspace
+    ditch::DevBuf moe_logits, moe_sel, moe_w, moe_counts, moe_offsets, moe_pos, moe_tok, moe_xg, moe_act, moe_eo,
+        moe_xa, moe_sched;
+    int moe_cap = 0;
+    // directions
+    ditch::DevBuf dirs;
+    std::vector<float> h_dirs;
+    int dir_entries = 0;
+    ditch::DevBuf vtmp;  // interpolated direction
+    // KL prompts
+    ditch::Batch kl;
+    ditch::DevBuf kl_base, kl_vals;
+    bool kl_ready = false;
+    std::vector<size_t> kl_offsets;
+    std::vector<uint32_t> kl_tokens_host;
+    ditch::Batch work;   // scratch batch for forward / residual passes
+    ditch::DevBuf sums;  // f64 residual sums
+    uint64_t bytes = 0;
+};
+
+namespace ditch {
+
+// Builds a device batch from flattened prompts (tokens + offsets); capture
+// rows = the last `window` tokens of every prompt (window 0 = none); logit
+// rows = each prompt's last token when `logits` is set.
+int make_batch(ditch_cuda_model *m, Batch &b, const uint32_t *tokens, const size_t *offsets, size_t n_prompts,
+               size_t window, bool logits, std::vector<int> *first_capture, std::vector<int> *take);
+
+// The forward over a device batch: residual capture into m->res ([L+1][nc][H])
+// when nc > 0, logits of the batch's logit rows into m->logits when nl > 0.
+int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl);
+
+int ensure_workspace(ditch_cuda_model *m, int n_tokens, int nc, int nl);
+
+// MoE MLP of layer `li` on h (bf16 [n][H]); adds the routed output into x.
+int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n);
+
+// GEMM with a resident weight as the A operand.
+int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
+                void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
+                int a2_row_offset);
+
+}  // namespace ditch

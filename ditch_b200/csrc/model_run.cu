@@ -1,0 +1,682 @@
+// Resident-model execution: batches, the forward (src/model.zig:4619-4959),
+// the residual pass and directions, the none-mode edit and the KL scorer.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <array>
+#include <numeric>
+
+#include "model.cuh"
+
+using namespace ditch;
+
+namespace {
+
+#define REQUIRE(cond, ...)             \
+    do {                               \
+        if (!(cond)) {                 \
+            set_error(__VA_ARGS__);    \
+            return DITCH_CUDA_INVALID; \
+        }                              \
+    } while (0)
+
+__global__ void k_capture_rows(const float *x, const int *cap_slot, int n, int hidden, float *res) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    const int slot = cap_slot[row];
+    if (slot < 0) return;
+    for (int i = lane; i < hidden; i += 32) res[(long long)slot * hidden + i] = x[(long long)row * hidden + i];
+}
+
+template <class T>
+cudaError_t upload_vec(DevBuf &buf, const std::vector<T> &v, cudaStream_t st) {
+    cudaError_t e = buf.reserve(std::max<size_t>(v.size() * sizeof(T), 4));
+    if (e != cudaSuccess || v.empty()) return e;
+    return cudaMemcpyAsync(buf.ptr, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, st);
+}
+
+// kernelWeight (src/abliterate.zig:134-140), f32 arithmetic as the reference.
+bool kernel_weight(const ditch_cuda_params &p, size_t layer, float *out) {
+    const float distance = std::fabs((float)layer - p.max_weight_position);
+    if (distance > p.min_weight_distance) return false;
+    const float w = p.max_weight + (distance / p.min_weight_distance) * (p.min_weight - p.max_weight);
+    if (w == 0.0f) return false;
+    *out = w;
+    return true;
+}
+
+// GEMV-T over one slab of a resident weight: out[cols] = v^T W (out zeroed here).
+int gemv_t_mat(ditch_cuda_model *m, const Mat &w, int row0, int rows, const float *v, float *out) {
+    ditch_cuda_device *dev = m->dev;
+    DITCH_CUDA(cudaMemsetAsync(out, 0, (size_t)w.cols * 4, dev->stream));
+    switch (w.fmt) {
+    case kFmtBf16:
+        DITCH_LAUNCH(dev, gemv_t_bf16(w.data.as<uint16_t>() + (size_t)row0 * w.cols, rows, w.cols, v, out, dev->stream));
+        break;
+    case kFmtFp8:
+        DITCH_LAUNCH(dev, gemv_t_fp8(w.data.as<uint8_t>() + (size_t)row0 * w.cols,
+                                     w.scales.as<float>() + (size_t)(row0 / w.br) * w.scols, rows, w.cols, w.br, w.bc,
+                                     v, out, dev->stream));
+        break;
+    case kFmtMxfp4:
+        DITCH_LAUNCH(dev, gemv_t_mxfp4(w.data.as<uint8_t>() + (size_t)row0 * w.cols / 2,
+                                       w.scales.as<uint8_t>() + (size_t)row0 * w.cols / 32, rows, w.cols, v, out,
+                                       dev->stream));
+        break;
+    case kFmtInt4: {
+        DevBuf tmp;
+        DITCH_CUDA(tmp.reserve((size_t)rows * w.cols * 2));
+        DITCH_LAUNCH(dev, dequant_int_bf16(w.data.as<uint32_t>() + (size_t)row0 * w.cols / 8, w.cols / 8,
+                                           w.scales.as<float>() + (size_t)row0 * w.groups,
+                                           w.zeros.as<uint32_t>() + (size_t)(row0 / 8) * w.groups, nullptr, w.groups,
+                                           rows, w.cols, 4, w.group, tmp.as<uint16_t>(), dev->stream));
+        DITCH_LAUNCH(dev, gemv_t_bf16(tmp.as<uint16_t>(), rows, w.cols, v, out, dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+        break;
+    }
+    default:
+        set_error("edit: weight format %d not supported", w.fmt);
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    return DITCH_CUDA_OK;
+}
+
+// interpolateBasis with k = 1 (src/abliterate.zig:119-131, orthonormalize 409-423).
+std::vector<float> interpolate(const std::vector<float> &dirs, int entries, int hidden, float di) {
+    const float shifted = di + 1.0f;
+    const int idx = (int)std::floor(shifted);
+    const float frac = shifted - std::floor(shifted);
+    const float *a = dirs.data() + (size_t)std::min(idx, entries - 1) * hidden;
+    const float *b = dirs.data() + (size_t)std::min(idx + 1, entries - 1) * hidden;
+    std::vector<float> out(hidden);
+    for (int i = 0; i < hidden; i++) out[i] = a[i] + frac * (b[i] - a[i]);
+    double s = 0;
+    for (float x : out) s += (double)x * x;
+    const float nrm = (float)std::sqrt(s);
+    for (float &x : out) x = nrm > 1e-20f ? x * (1.0f / nrm) : 0.0f;
+    return out;
+}
+
+}  // namespace
+
+namespace ditch {
+
+int ensure_workspace(ditch_cuda_model *m, int n, int nc, int nl) {
+    const Config &c = m->cfg;
+    const size_t N = (size_t)std::max(n, 1), H = c.hidden;
+    const size_t inter = std::max(c.inter, 1);
+    DITCH_CUDA(m->x.reserve(N * H * 4));
+    DITCH_CUDA(m->h.reserve(N * H * 2));
+    DITCH_CUDA(m->qkv.reserve(N * c.qkv_width() * 4));
+    DITCH_CUDA(m->att.reserve(N * c.qd() * 2));
+    DITCH_CUDA(m->act.reserve(N * inter * 2));
+    DITCH_CUDA(m->xa.reserve(N * 4));
+    if (nc > 0) DITCH_CUDA(m->res.reserve((size_t)(c.n_layers + 1) * nc * H * 4));
+    if (nl > 0) {
+        DITCH_CUDA(m->hl.reserve((size_t)nl * H * 2));
+        DITCH_CUDA(m->logits.reserve((size_t)nl * c.vocab * 4));
+    }
+    return DITCH_CUDA_OK;
+}
+
+int make_batch(ditch_cuda_model *m, Batch &b, const uint32_t *tokens, const size_t *offsets, size_t n_prompts,
+               size_t window, bool logits, std::vector<int> *first_capture, std::vector<int> *take) {
+    REQUIRE(tokens && offsets, "null prompts");
+    const size_t n = offsets[n_prompts] - offsets[0];
+    REQUIRE(n < (1u << 30), "too many tokens");
+    b.n = (int)n;
+    b.prompts = (int)n_prompts;
+    b.h_start.resize(n_prompts);
+    b.h_len.resize(n_prompts);
+    std::vector<int> cap(n, -1), lrows;
+    int slot = 0;
+    if (first_capture) first_capture->assign(n_prompts, 0);
+    if (take) take->assign(n_prompts, 0);
+    for (size_t p = 0; p < n_prompts; p++) {
+        REQUIRE(offsets[p + 1] > offsets[p], "prompt %zu is empty", p);
+        const int start = (int)(offsets[p] - offsets[0]), len = (int)(offsets[p + 1] - offsets[p]);
+        REQUIRE(len <= m->rope_len, "prompt %zu has %d tokens; the model was loaded for %d", p, len, m->rope_len);
+        b.h_start[p] = start;
+        b.h_len[p] = len;
+        const int tk = (int)std::min<size_t>(window, (size_t)len);
+        if (first_capture) (*first_capture)[p] = slot;
+        if (take) (*take)[p] = tk;
+        for (int pos = len - tk; pos < len; pos++) cap[start + pos] = slot++;
+        if (logits) lrows.push_back(start + len - 1);
+    }
+    cudaStream_t st = m->dev->stream;
+    DITCH_CUDA(b.tokens.reserve(std::max<size_t>(n * 4, 4)));
+    DITCH_CUDA(cudaMemcpyAsync(b.tokens.ptr, tokens + offsets[0], n * 4, cudaMemcpyHostToDevice, st));
+    DITCH_CUDA(upload_vec(b.seq_start, b.h_start, st));
+    DITCH_CUDA(upload_vec(b.seq_len, b.h_len, st));
+    DITCH_CUDA(upload_vec(b.cap_slot, cap, st));
+    DITCH_CUDA(upload_vec(b.logit_rows, lrows, st));
+    return DITCH_CUDA_OK;
+}
+
+int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
+                void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
+                int a2_row_offset) {
+    if (n_tok <= 0 || m_rows <= 0) return DITCH_CUDA_OK;
+    GemmOperand A{w.data.ptr, w.rows * w.slabs, w.cols, w.row_bytes};
+    GemmOperand B{act, n_tok, w.cols, (long long)w.cols * 2};
+    GemmParams p{};
+    p.m_w = m_rows;
+    p.n_tok = n_tok;
+    p.k = w.cols;
+    p.k_splits = 1;
+    p.a2_row_offset = a2_row_offset;
+    p.a_row0 = slab_row0;
+    p.out = out;
+    p.ldo = ldo;
+    p.flags = flags;
+    p.bias = bias;
+    p.xa = xa;
+    p.db = db;
+    if (w.fmt == kFmtFp8) {
+        p.scales = w.scales.as<float>();
+        p.blk_rows = w.br;
+        p.blk_cols = w.bc;
+        p.scale_cols = w.scols;
+    } else if (w.fmt == kFmtMxfp4) {
+        p.scales_u8 = w.scales.as<uint8_t>();
+    } else if (w.fmt == kFmtInt4) {
+        p.scales = w.scales.as<float>();
+        p.zeros = w.zeros.as<uint32_t>();
+        p.blk_cols = w.group;
+        p.scale_cols = w.groups;
+    }
+    cudaError_t e = run_gemm(m->dev, w.fmt, A, (flags & kEpiSwiglu) ? &A : nullptr, B, p);
+    if (e != cudaSuccess) return cuda_status(e, "gemm");
+    return DITCH_CUDA_OK;
+}
+
+int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
+    const Config &c = m->cfg;
+    ditch_cuda_device *dev = m->dev;
+    cudaStream_t st = dev->stream;
+    const int n = b.n, H = c.hidden, qd = c.qd(), W = c.qkv_width();
+    int s;
+    if ((s = ensure_workspace(m, n, nc, nl))) return s;
+    float *x = m->x.as<float>();
+    uint16_t *h = m->h.as<uint16_t>();
+    float *res = nc > 0 ? m->res.as<float>() : nullptr;
+    const int *cap = nc > 0 ? b.cap_slot.as<int>() : nullptr;
+    const size_t entry = (size_t)nc * H;
+    DITCH_LAUNCH(dev, embed_rows(m->embed.ptr, m->embed_bf16 ? 1 : 0, b.tokens.as<uint32_t>(), n, H, x, cap, res,
+                                 dev->status, c.vocab, st));
+    for (int li = 0; li < c.n_layers; li++) {
+        Layer &L = m->layers[li];
+        // input norm; entry li (the previous layer's output) is captured here
+        DITCH_LAUNCH(dev, rmsnorm_rows_bf16(x, L.input_norm.as<float>(), n, H, c.eps, h, li > 0 ? cap : nullptr,
+                                            li > 0 && res ? res + (size_t)li * entry : nullptr, nullptr, st));
+        if ((s = gemm_weight(m, L.qkv, 0, W, h, n, m->qkv.ptr, W, 0, L.qkv_bias.as<float>(), nullptr, nullptr, 0)))
+            return s;
+        AttnParams ap{};
+        ap.qkv = m->qkv.as<float>();
+        ap.out = m->att.as<uint16_t>();
+        ap.seq_start = b.seq_start.as<int>();
+        ap.seq_len = b.seq_len.as<int>();
+        ap.n_prompts = b.prompts;
+        ap.heads = c.heads;
+        ap.kv_heads = c.kv_heads;
+        ap.head_dim = c.head_dim;
+        ap.rope_cos = m->rope_cos.as<float>();
+        ap.rope_sin = m->rope_sin.as<float>();
+        ap.q_norm = c.qk_norm ? L.q_norm.as<float>() : nullptr;
+        ap.k_norm = c.qk_norm ? L.k_norm.as<float>() : nullptr;
+        ap.eps = c.eps;
+        ap.scale = 1.0f / std::sqrt((float)c.head_dim);
+        ap.status = dev->status;
+        DITCH_LAUNCH(dev, attention_prefill(ap, st));
+        if (L.o_edit) DITCH_LAUNCH(dev, rowdot_bf16(m->att.as<uint16_t>(), L.o_a.as<float>(), n, qd, m->xa.as<float>(), st));
+        if ((s = gemm_weight(m, L.o, 0, H, m->att.as<uint16_t>(), n, x, H, kEpiResidual, nullptr,
+                             L.o_edit ? m->xa.as<float>() : nullptr, L.o_edit ? L.o_b.as<float>() : nullptr, 0)))
+            return s;
+        DITCH_LAUNCH(dev, rmsnorm_rows_bf16(x, L.post_norm.as<float>(), n, H, c.eps, h, nullptr, nullptr, nullptr, st));
+        if (L.moe) {
+            if ((s = moe_mlp(m, L, li, n))) return s;
+        } else {
+            const int I = c.inter;
+            if ((s = gemm_weight(m, L.gate_up, 0, I, h, n, m->act.ptr, I, kEpiSwiglu, nullptr, nullptr, nullptr, I)))
+                return s;
+            if (L.down_edit)
+                DITCH_LAUNCH(dev, rowdot_bf16(m->act.as<uint16_t>(), L.down_a.as<float>(), n, I, m->xa.as<float>(), st));
+            if ((s = gemm_weight(m, L.down, 0, H, m->act.as<uint16_t>(), n, x, H, kEpiResidual, nullptr,
+                                 L.down_edit ? m->xa.as<float>() : nullptr, L.down_edit ? L.down_b.as<float>() : nullptr,
+                                 0)))
+                return s;
+        }
+    }
+    if (res) {
+        k_capture_rows<<<(n + 7) / 8, 256, 0, st>>>(x, cap, n, H, res + (size_t)c.n_layers * entry);
+        DITCH_LAUNCH(dev, cudaGetLastError());
+    }
+    if (nl > 0) {
+        DITCH_LAUNCH(dev, gather_rmsnorm_bf16(x, b.logit_rows.as<int>(), nl, H, c.eps, m->final_norm.as<float>(),
+                                              m->hl.as<uint16_t>(), st));
+        if ((s = gemm_weight(m, m->lm_head, 0, c.vocab, m->hl.as<uint16_t>(), nl, m->logits.ptr, c.vocab, 0, nullptr,
+                             nullptr, nullptr, 0)))
+            return s;
+    }
+    return DITCH_CUDA_OK;
+}
+
+}  // namespace ditch
+
+namespace {
+
+int apply_component_edit(ditch_cuda_model *m, int li, bool is_o, const float *v, float lambda) {
+    ditch_cuda_device *dev = m->dev;
+    Layer &L = m->layers[li];
+    const int H = m->cfg.hidden;
+    int s;
+    if (is_o) {
+        if ((s = gemv_t_mat(m, L.o, 0, H, v, L.o_a.as<float>()))) return s;
+        DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.o_b.as<float>(), dev->stream));
+        L.o_edit = true;
+    } else {
+        if ((s = gemv_t_mat(m, L.down, 0, H, v, L.down_a.as<float>()))) return s;
+        DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.down_b.as<float>(), dev->stream));
+        L.down_edit = true;
+    }
+    return DITCH_CUDA_OK;
+}
+
+int apply_expert_delta(ditch_cuda_model *m, int li, int e, const float *v, float lambda) {
+    ditch_cuda_device *dev = m->dev;
+    Layer &L = m->layers[li];
+    const int H = m->cfg.hidden, mi = m->cfg.moe_inter;
+    int s;
+    if ((s = gemv_t_mat(m, L.e_down, e * H, H, v, L.e_a.as<float>() + (size_t)e * mi))) return s;
+    DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.e_b.as<float>() + (size_t)e * H, dev->stream));
+    L.e_edit[e] = 1;
+    return DITCH_CUDA_OK;
+}
+
+int upload_expert_flags(ditch_cuda_model *m) {
+    for (Layer &L : m->layers) {
+        if (!L.moe) continue;
+        std::vector<int> f(L.e_edit.begin(), L.e_edit.end());
+        DITCH_CUDA(cudaMemcpyAsync(L.e_edit_dev.ptr, f.data(), f.size() * 4, cudaMemcpyHostToDevice, m->dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(m->dev->stream));
+    }
+    return DITCH_CUDA_OK;
+}
+
+void clear_edits(ditch_cuda_model *m) {
+    for (Layer &L : m->layers) {
+        L.o_edit = L.down_edit = false;
+        std::fill(L.e_edit.begin(), L.e_edit.end(), 0);
+    }
+}
+
+// The direction for layer li: dirs[li + 1] or the interpolated one.
+const float *direction_for(ditch_cuda_model *m, int li, bool use_di) {
+    return use_di ? m->vtmp.as<float>() : m->dirs.as<float>() + (size_t)(li + 1) * m->cfg.hidden;
+}
+
+int prepare_direction(ditch_cuda_model *m, float di, bool use_di) {
+    REQUIRE(m->dir_entries >= (use_di ? 1 : m->cfg.n_layers + 1), "directions not set (need %d entries)",
+            m->cfg.n_layers + 1);
+    if (use_di) {
+        std::vector<float> v = interpolate(m->h_dirs, m->dir_entries, m->cfg.hidden, di);
+        DITCH_CUDA(cudaMemcpyAsync(m->vtmp.ptr, v.data(), v.size() * 4, cudaMemcpyHostToDevice, m->dev->stream));
+    }
+    return DITCH_CUDA_OK;
+}
+
+// Scores of every routed expert of `li` against v (device f32 [H]).
+int expert_scores(ditch_cuda_model *m, int li, const float *v, std::vector<float> &scores) {
+    ditch_cuda_device *dev = m->dev;
+    Layer &L = m->layers[li];
+    const int E = m->cfg.n_experts, H = m->cfg.hidden, mi = m->cfg.moe_inter;
+    DevBuf proj, norms;
+    DITCH_CUDA(proj.reserve((size_t)E * mi * 4));
+    DITCH_CUDA(norms.reserve((size_t)E * H * 4));
+    int s;
+    for (int e = 0; e < E; e++)
+        if ((s = gemv_t_mat(m, L.e_down, e * H, H, v, proj.as<float>() + (size_t)e * mi))) return s;
+    const Mat &w = L.e_down;
+    if (w.fmt == kFmtBf16) {
+        DITCH_LAUNCH(dev, row_norms_bf16(w.data.as<uint16_t>(), E * H, mi, norms.as<float>(), dev->stream));
+    } else if (w.fmt == kFmtMxfp4) {
+        DITCH_LAUNCH(dev, row_norms_mxfp4(w.data.as<uint8_t>(), w.scales.as<uint8_t>(), E * H, mi, norms.as<float>(),
+                                          dev->stream));
+    } else {
+        DevBuf tmp;
+        DITCH_CUDA(tmp.reserve((size_t)H * mi * 2));
+        for (int e = 0; e < E; e++) {
+            if (w.fmt == kFmtFp8) {
+                DITCH_LAUNCH(dev, dequant_fp8_bf16(w.data.as<uint8_t>() + (size_t)e * H * mi,
+                                                   w.scales.as<float>() + (size_t)(e * H / w.br) * w.scols, H, mi, w.br,
+                                                   w.bc, tmp.as<uint16_t>(), dev->stream));
+            } else {
+                DITCH_LAUNCH(dev, dequant_int_bf16(w.data.as<uint32_t>() + (size_t)e * H * mi / 8, mi / 8,
+                                                   w.scales.as<float>() + (size_t)e * H * w.groups,
+                                                   w.zeros.as<uint32_t>() + (size_t)(e * H / 8) * w.groups, nullptr,
+                                                   w.groups, H, mi, 4, w.group, tmp.as<uint16_t>(), dev->stream));
+            }
+            DITCH_LAUNCH(dev, row_norms_bf16(tmp.as<uint16_t>(), H, mi, norms.as<float>() + (size_t)e * H, dev->stream));
+        }
+    }
+    std::vector<float> hp((size_t)E * mi), hn((size_t)E * H);
+    DITCH_CUDA(cudaMemcpyAsync(hp.data(), proj.ptr, hp.size() * 4, cudaMemcpyDeviceToHost, dev->stream));
+    DITCH_CUDA(cudaMemcpyAsync(hn.data(), norms.ptr, hn.size() * 4, cudaMemcpyDeviceToHost, dev->stream));
+    DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+    scores.assign(E, 0.0f);
+    for (int e = 0; e < E; e++) {
+        float fro = 0.0f, pn = 0.0f;
+        for (int r = 0; r < H; r++) fro = std::fma(hn[(size_t)e * H + r], hn[(size_t)e * H + r], fro);
+        for (int j = 0; j < mi; j++) pn = std::fma(hp[(size_t)e * mi + j], hp[(size_t)e * mi + j], pn);
+        fro = std::sqrt(fro);
+        scores[e] = fro > 0 ? std::sqrt(pn) / fro : 0.0f;
+    }
+    return DITCH_CUDA_OK;
+}
+
+std::vector<uint32_t> rank(const std::vector<float> &s) {
+    std::vector<uint32_t> order(s.size());
+    std::iota(order.begin(), order.end(), 0u);
+    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) {
+        if (s[a] != s[b]) return s[a] > s[b];
+        return a < b;
+    });
+    return order;
+}
+
+int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down, float di,
+                int use_di, bool selective, size_t n_experts, float strength) {
+    const Config &c = m->cfg;
+    clear_edits(m);
+    int s;
+    if ((s = prepare_direction(m, di, use_di != 0))) return s;
+    for (int li = 0; li < c.n_layers; li++) {
+        const float *v = direction_for(m, li, use_di != 0);
+        float lambda;
+        if (attn_o && kernel_weight(*attn_o, li, &lambda))
+            if ((s = apply_component_edit(m, li, true, v, lambda))) return s;
+        if (!mlp_down || !kernel_weight(*mlp_down, li, &lambda)) continue;
+        Layer &L = m->layers[li];
+        if (!L.moe) {
+            if ((s = apply_component_edit(m, li, false, v, lambda))) return s;
+            continue;
+        }
+        const int E = c.n_experts;
+        if (!selective || n_experts == 0) {
+            for (int e = 0; e < E; e++)
+                if ((s = apply_expert_delta(m, li, e, v, lambda))) return s;
+            continue;
+        }
+        const float weight = std::max(0.0f, lambda * strength);
+        const size_t n = std::min<size_t>(n_experts, (size_t)E);
+        if (weight == 0.0f || n == 0) continue;
+        std::vector<float> scores;
+        if ((s = expert_scores(m, li, v, scores))) return s;
+        std::vector<uint32_t> order = rank(scores);
+        for (size_t j = 0; j < n; j++)
+            if ((s = apply_expert_delta(m, li, (int)order[j], v, weight))) return s;
+    }
+    if ((s = upload_expert_flags(m))) return s;
+    return check_status(m->dev, "apply_edit");
+}
+
+int kl_score_impl(ditch_cuda_model *m, double *kl) {
+    ditch_cuda_device *dev = m->dev;
+    const int P = m->kl.prompts, V = m->cfg.vocab;
+    int s;
+    if ((s = forward_batch(m, m->kl, 0, P))) return s;
+    DITCH_CUDA(m->kl_vals.reserve((size_t)P * 8));
+    DITCH_LAUNCH(dev, kl_rows(m->kl_base.as<float>(), m->logits.as<float>(), P, V, m->kl_vals.as<double>(), dev->stream));
+    std::vector<double> per(P);
+    DITCH_CUDA(cudaMemcpyAsync(per.data(), m->kl_vals.ptr, (size_t)P * 8, cudaMemcpyDeviceToHost, dev->stream));
+    if ((s = check_status(dev, "kl_score"))) return s;
+    double total = 0.0;
+    for (int p = 0; p < P; p++) total += per[p];  // prompt order, as src/scorers.zig:385-400
+    *kl = total / (double)std::max(P, 1);
+    return DITCH_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ditch_cuda_forward(ditch_cuda_model *m, const uint32_t *tokens, const uint32_t *row_b, const uint32_t *row_pos,
+                       size_t n, const size_t *capture_rows, size_t nc, float *residuals, const size_t *logit_rows,
+                       size_t nl, float *logits) {
+    clear_error();
+    REQUIRE(m && tokens && row_b && row_pos, "null argument");
+    REQUIRE(nc == 0 || (capture_rows && residuals), "capture rows without an output");
+    REQUIRE(nl == 0 || (logit_rows && logits), "logit rows without an output");
+    if (n == 0) return DITCH_CUDA_OK;
+    ditch_cuda_device *dev = m->dev;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    // The device forward reads each prompt's keys from the call itself: rows
+    // of a batch slot must be contiguous with positions 0, 1, ... (the layout
+    // src/engine.zig:392-410 builds). Anything else is left to the CPU.
+    std::vector<size_t> offsets{0};
+    for (size_t i = 0; i < n; i++) {
+        const bool new_prompt = i == 0 || row_b[i] != row_b[i - 1];
+        if (new_prompt && i > 0) offsets.push_back(i);
+        if ((new_prompt && row_pos[i] != 0) || (!new_prompt && row_pos[i] != row_pos[i - 1] + 1)) {
+            set_error("rows are not contiguous prompts starting at position 0");
+            return DITCH_CUDA_UNSUPPORTED;
+        }
+    }
+    offsets.push_back(n);
+    const size_t P = offsets.size() - 1;
+    for (size_t i = 1; i < P; i++)
+        for (size_t j = 0; j < i; j++)
+            if (row_b[offsets[i]] == row_b[offsets[j]]) {
+                set_error("a batch slot appears twice");
+                return DITCH_CUDA_UNSUPPORTED;
+            }
+    for (size_t i = 0; i < nc; i++) REQUIRE(capture_rows[i] < n, "capture row out of range");
+    for (size_t i = 0; i < nl; i++) REQUIRE(logit_rows[i] < n, "logit row out of range");
+    Batch &b = m->work;
+    int s;
+    if ((s = make_batch(m, b, tokens, offsets.data(), P, 0, false, nullptr, nullptr))) return s;
+    std::vector<int> cap(n, -1), lr(nl);
+    for (size_t i = 0; i < nc; i++) cap[capture_rows[i]] = (int)i;
+    for (size_t i = 0; i < nl; i++) lr[i] = (int)logit_rows[i];
+    DITCH_CUDA(upload_vec(b.cap_slot, cap, dev->stream));
+    DITCH_CUDA(upload_vec(b.logit_rows, lr, dev->stream));
+    if ((s = forward_batch(m, b, (int)nc, (int)nl))) return s;
+    const Config &c = m->cfg;
+    if (nc) {
+        // a row captured twice keeps one slot: fill duplicates from it
+        std::vector<float> res((size_t)(c.n_layers + 1) * nc * c.hidden);
+        DITCH_CUDA(cudaMemcpyAsync(res.data(), m->res.ptr, res.size() * 4, cudaMemcpyDeviceToHost, dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+        for (int l = 0; l <= c.n_layers; l++)
+            for (size_t i = 0; i < nc; i++) {
+                const int slot = cap[capture_rows[i]];
+                memcpy(residuals + ((size_t)l * nc + i) * c.hidden, res.data() + ((size_t)l * nc + slot) * c.hidden,
+                       (size_t)c.hidden * 4);
+            }
+    }
+    if (nl) DITCH_CUDA(cudaMemcpyAsync(logits, m->logits.ptr, nl * (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, dev->stream));
+    return check_status(dev, "forward");
+}
+
+int ditch_cuda_residual_sums(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets,
+                             size_t n_prompts, size_t window, size_t batch_size, double *sums, uint64_t *count) {
+    clear_error();
+    REQUIRE(m && tokens && prompt_offsets && sums && count, "null argument");
+    ditch_cuda_device *dev = m->dev;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    const Config &c = m->cfg;
+    const size_t entries = c.n_layers + 1, H = c.hidden;
+    const size_t w = std::max<size_t>(window, 1);
+    const size_t bs = batch_size ? batch_size : std::max<size_t>(n_prompts, 1);
+    DITCH_CUDA(m->sums.reserve(entries * H * 8));
+    DITCH_CUDA(cudaMemsetAsync(m->sums.ptr, 0, entries * H * 8, dev->stream));
+    DevBuf dfirst, dtake;
+    int s;
+    for (size_t start = 0; start < n_prompts; start += bs) {
+        const size_t np = std::min(bs, n_prompts - start);
+        std::vector<int> first, take;
+        if ((s = make_batch(m, m->work, tokens, prompt_offsets + start, np, w, false, &first, &take))) return s;
+        int nc = 0;
+        for (int t : take) nc += t;
+        if ((s = forward_batch(m, m->work, nc, 0))) return s;
+        DITCH_CUDA(upload_vec(dfirst, first, dev->stream));
+        DITCH_CUDA(upload_vec(dtake, take, dev->stream));
+        DITCH_LAUNCH(dev, residual_sums(m->res.as<float>(), (int)entries, nc, (int)H, dfirst.as<int>(), dtake.as<int>(),
+                                        (int)np, m->sums.as<double>(), dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+    }
+    std::vector<double> hs(entries * H);
+    DITCH_CUDA(cudaMemcpyAsync(hs.data(), m->sums.ptr, hs.size() * 8, cudaMemcpyDeviceToHost, dev->stream));
+    if ((s = check_status(dev, "residual_sums"))) return s;
+    for (size_t i = 0; i < hs.size(); i++) sums[i] += hs[i];
+    *count += n_prompts;
+    return DITCH_CUDA_OK;
+}
+
+int ditch_cuda_directions(ditch_cuda_model *m, const double *good_sums, uint64_t good_count, const double *bad_sums,
+                          uint64_t bad_count, int orthogonalize, float *dirs) {
+    clear_error();
+    REQUIRE(m && good_sums && bad_sums, "null argument");
+    ditch_cuda_device *dev = m->dev;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    const Config &c = m->cfg;
+    const size_t entries = c.n_layers + 1, H = c.hidden;
+    DevBuf g, b;
+    DITCH_CUDA(g.reserve(entries * H * 8));
+    DITCH_CUDA(b.reserve(entries * H * 8));
+    DITCH_CUDA(cudaMemcpyAsync(g.ptr, good_sums, entries * H * 8, cudaMemcpyHostToDevice, dev->stream));
+    DITCH_CUDA(cudaMemcpyAsync(b.ptr, bad_sums, entries * H * 8, cudaMemcpyHostToDevice, dev->stream));
+    DITCH_LAUNCH(dev, directions_from_sums(g.as<double>(), (double)good_count, b.as<double>(), (double)bad_count,
+                                           (int)entries, (int)H, orthogonalize, m->dirs.as<float>(), nullptr, nullptr,
+                                           dev->stream));
+    m->h_dirs.resize(entries * H);
+    DITCH_CUDA(cudaMemcpyAsync(m->h_dirs.data(), m->dirs.ptr, entries * H * 4, cudaMemcpyDeviceToHost, dev->stream));
+    int s = check_status(dev, "directions");
+    if (s) return s;
+    m->dir_entries = (int)entries;
+    if (dirs) memcpy(dirs, m->h_dirs.data(), entries * H * 4);
+    return DITCH_CUDA_OK;
+}
+
+int ditch_cuda_set_directions(ditch_cuda_model *m, const float *dirs, size_t entries) {
+    clear_error();
+    REQUIRE(m && dirs && entries > 0, "bad argument");
+    ditch_cuda_device *dev = m->dev;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    const size_t H = m->cfg.hidden;
+    DITCH_CUDA(m->dirs.reserve(entries * H * 4));
+    DITCH_CUDA(cudaMemcpy(m->dirs.ptr, dirs, entries * H * 4, cudaMemcpyHostToDevice));
+    m->h_dirs.assign(dirs, dirs + entries * H);
+    m->dir_entries = (int)entries;
+    return DITCH_CUDA_OK;
+}
+
+int ditch_cuda_apply_edit(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down,
+                          float direction_index, int use_direction_index) {
+    clear_error();
+    REQUIRE(m, "null model");
+    std::lock_guard<std::mutex> lk(m->dev->mu);
+    DITCH_CUDA(cudaSetDevice(m->dev->ordinal));
+    return edit_common(m, attn_o, mlp_down, direction_index, use_direction_index, false, 0, 1.0f);
+}
+
+int ditch_cuda_apply_expert_edit(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down,
+                                 float direction_index, int use_direction_index, size_t n_experts, float strength) {
+    clear_error();
+    REQUIRE(m, "null model");
+    std::lock_guard<std::mutex> lk(m->dev->mu);
+    DITCH_CUDA(cudaSetDevice(m->dev->ordinal));
+    return edit_common(m, attn_o, mlp_down, direction_index, use_direction_index, true, n_experts, strength);
+}
+
+int ditch_cuda_reset_edits(ditch_cuda_model *m) {
+    clear_error();
+    REQUIRE(m, "null model");
+    std::lock_guard<std::mutex> lk(m->dev->mu);
+    DITCH_CUDA(cudaSetDevice(m->dev->ordinal));
+    clear_edits(m);
+    return upload_expert_flags(m);
+}
+
+int ditch_cuda_rank_experts(ditch_cuda_model *m, size_t layer, const float *v, uint32_t *order, float *scores) {
+    clear_error();
+    REQUIRE(m && v, "null argument");
+    REQUIRE(layer < (size_t)m->cfg.n_layers && m->layers[layer].moe, "layer %zu is not an MoE layer", layer);
+    std::lock_guard<std::mutex> lk(m->dev->mu);
+    DITCH_CUDA(cudaSetDevice(m->dev->ordinal));
+    DITCH_CUDA(cudaMemcpy(m->vtmp.ptr, v, (size_t)m->cfg.hidden * 4, cudaMemcpyHostToDevice));
+    std::vector<float> s;
+    int st = expert_scores(m, (int)layer, m->vtmp.as<float>(), s);
+    if (st) return st;
+    std::vector<uint32_t> o = rank(s);
+    if (order) memcpy(order, o.data(), o.size() * 4);
+    if (scores) memcpy(scores, s.data(), s.size() * 4);
+    return DITCH_CUDA_OK;
+}
+
+int ditch_cuda_kl_init(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets, size_t n_prompts) {
+    clear_error();
+    REQUIRE(m && tokens && prompt_offsets && n_prompts > 0, "bad argument");
+    ditch_cuda_device *dev = m->dev;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    int s;
+    if ((s = make_batch(m, m->kl, tokens, prompt_offsets, n_prompts, 0, true, nullptr, nullptr))) return s;
+    m->kl_offsets.assign(prompt_offsets, prompt_offsets + n_prompts + 1);
+    m->kl_tokens_host.assign(tokens + prompt_offsets[0], tokens + prompt_offsets[n_prompts]);
+    // the baseline is the unedited model: suspend edits for this forward
+    std::vector<std::array<bool, 2>> flags;
+    for (Layer &L : m->layers) flags.push_back({L.o_edit, L.down_edit});
+    std::vector<std::vector<uint8_t>> eflags;
+    for (Layer &L : m->layers) eflags.push_back(L.e_edit);
+    clear_edits(m);
+    if ((s = upload_expert_flags(m))) return s;
+    const int P = (int)n_prompts, V = m->cfg.vocab;
+    s = forward_batch(m, m->kl, 0, P);
+    for (size_t i = 0; i < m->layers.size(); i++) {
+        m->layers[i].o_edit = flags[i][0];
+        m->layers[i].down_edit = flags[i][1];
+        m->layers[i].e_edit = eflags[i];
+    }
+    if (s) return s;
+    if ((s = upload_expert_flags(m))) return s;
+    DITCH_CUDA(m->kl_base.reserve((size_t)P * V * 4));
+    DITCH_LAUNCH(dev, log_softmax_rows(m->logits.as<float>(), P, V, m->kl_base.as<float>(), dev->stream));
+    if ((s = check_status(dev, "kl_init"))) return s;
+    m->kl_ready = true;
+    return DITCH_CUDA_OK;
+}
+
+int ditch_cuda_kl_score(ditch_cuda_model *m, double *kl) {
+    clear_error();
+    REQUIRE(m && kl, "null argument");
+    REQUIRE(m->kl_ready, "ditch_cuda_kl_init has not run");
+    std::lock_guard<std::mutex> lk(m->dev->mu);
+    DITCH_CUDA(cudaSetDevice(m->dev->ordinal));
+    return kl_score_impl(m, kl);
+}
+
+int ditch_cuda_kl_score_prompts(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets,
+                                size_t n_prompts, double *kl) {
+    clear_error();
+    REQUIRE(m && kl && tokens && prompt_offsets, "null argument");
+    REQUIRE(m->kl_ready, "ditch_cuda_kl_init has not run");
+    REQUIRE(n_prompts + 1 == m->kl_offsets.size(), "prompt count differs from ditch_cuda_kl_init");
+    for (size_t i = 0; i <= n_prompts; i++)
+        REQUIRE(prompt_offsets[i] - prompt_offsets[0] == m->kl_offsets[i] - m->kl_offsets[0],
+                "prompt lengths differ from ditch_cuda_kl_init");
+    std::lock_guard<std::mutex> lk(m->dev->mu);
+    DITCH_CUDA(cudaSetDevice(m->dev->ordinal));
+    const size_t n = prompt_offsets[n_prompts] - prompt_offsets[0];
+    DITCH_CUDA(cudaMemcpyAsync(m->kl.tokens.ptr, tokens + prompt_offsets[0], n * 4, cudaMemcpyHostToDevice,
+                               m->dev->stream));
+    return kl_score_impl(m, kl);
+}
+
+}  // extern "C"

@@ -1,0 +1,262 @@
+/* ditch_cuda: a B200 (sm_100a) backend for ditch's trial-evaluation hot path.
+ *
+ * A plain C ABI (no C++ or torch types) for a `--device cuda` backend behind
+ * ditch's compute seam (src/compute.zig). Two layers:
+ *
+ *   1. The per-op entries of `compute.VTable` (src/compute.zig:90-117): host
+ *      slices in, host slices out, "upload, compute, drop" per weight tile
+ *      (the contract of src/vulkan/backend.zig:223-244), with an optional
+ *      device-side residency cache of weight tiles (compute.Residency,
+ *      src/compute.zig:580-693).
+ *   2. Coarse entries for a model kept resident in HBM: the batched forward
+ *      with residual capture and logit rows (model.forward,
+ *      src/model.zig:4619-4853), the residual-mean pass
+ *      (engine.getResidualMeanObserved, src/engine.zig:314-438), directions
+ *      (abliterate.computeDirections, src/abliterate.zig:88-109), the
+ *      none-mode edit (abliterate.apply, src/abliterate.zig:148-280), expert
+ *      ranking (moe.rankScores, src/moe.zig:1239-1306) and the first-token KL
+ *      (KlDivergence.init / score, src/scorers.zig:311-402).
+ *
+ * Errors mirror compute.Error (src/compute.zig:54-60): every entry returns a
+ * status; DITCH_CUDA_UNSUPPORTED means "the caller runs the CPU kernel" (the
+ * seam's fallback, which lives in ditch, never in this library).
+ * ditch_cuda_last_error() describes the last failure on this thread.
+ *
+ * Threading: a device handle serialises its calls with a mutex (ditch may
+ * call from any pool thread, src/compute.zig:161-163).
+ */
+#ifndef DITCH_CUDA_H
+#define DITCH_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes: compute.Error (src/compute.zig:54-60) ---- */
+#define DITCH_CUDA_OK 0
+#define DITCH_CUDA_UNSUPPORTED 1   /* error.Unsupported: shape or dtype not taken */
+#define DITCH_CUDA_DEVICE_FAILED 2 /* error.DeviceFailed */
+#define DITCH_CUDA_OUT_OF_MEMORY 3 /* error.OutOfMemory */
+#define DITCH_CUDA_INVALID 4       /* invalid argument */
+
+/* Weight dtypes: tensor.DType order (src/tensor.zig:11-32). */
+#define DITCH_DTYPE_F32 0
+#define DITCH_DTYPE_F16 1
+#define DITCH_DTYPE_BF16 2
+#define DITCH_DTYPE_Q8_0 5
+#define DITCH_DTYPE_Q4_0 6
+#define DITCH_DTYPE_Q4_1 7
+#define DITCH_DTYPE_Q5_0 8
+#define DITCH_DTYPE_Q5_1 9
+#define DITCH_DTYPE_Q4_K 10
+#define DITCH_DTYPE_Q6_K 11
+#define DITCH_DTYPE_Q8_K 12
+
+typedef struct ditch_cuda_device ditch_cuda_device;
+typedef struct ditch_cuda_model ditch_cuda_model;
+
+/* Text of the last failure on the calling thread (empty when none). */
+const char *ditch_cuda_last_error(void);
+/* Number of usable CUDA devices (0 when no driver or GPU is present). */
+int ditch_cuda_device_count(void);
+/* Library version string. */
+const char *ditch_cuda_version(void);
+
+/* ---- device: compute.select(.cuda) / Device.deinit (src/compute.zig:224-279) ----
+ * memory_budget: bytes the residency cache may keep (0 = upload every tile,
+ * compute and drop it), like `--gpu-memory`. */
+int ditch_cuda_open(int ordinal, uint64_t memory_budget, ditch_cuda_device **out);
+void ditch_cuda_close(ditch_cuda_device *dev);
+/* VTable.forgetWeights: drops every resident weight tile. */
+void ditch_cuda_forget_weights(ditch_cuda_device *dev);
+/* compute.served: weight-tile operations this device served. */
+uint64_t ditch_cuda_served(const ditch_cuda_device *dev);
+/* Host-stable weight addresses (compute.weights_stable, src/compute.zig:165-172):
+ * residency is keyed by host address only while this is set. */
+void ditch_cuda_set_weights_stable(ditch_cuda_device *dev, int stable);
+
+/* ---- per-op VTable entries (src/compute.zig:90-117), host buffers ----
+ * Weight = {data, dtype, rows, cols} (src/tensor.zig:517-521), w_len bytes.
+ * f32 / f16 weights and f32 inputs run as a split-bf16 (hi + lo) product on
+ * the tensor cores, accurate to about 2^-16 relative; bf16 weights exactly. */
+int ditch_cuda_matmul_t(ditch_cuda_device *dev, float *out, const float *x, size_t n, const uint8_t *w,
+                        size_t w_len, int dtype, size_t rows, size_t cols);
+int ditch_cuda_matvec_t_multi(ditch_cuda_device *dev, float *out, const uint8_t *w, size_t w_len, int dtype,
+                              size_t rows, size_t cols, const float *y, size_t q);
+int ditch_cuda_row_norms(ditch_cuda_device *dev, float *out, const uint8_t *w, size_t w_len, int dtype, size_t rows,
+                         size_t cols);
+int ditch_cuda_attention_scores(ditch_cuda_device *dev, float *scores, size_t n_keys, const float *q, size_t hd,
+                                const float *k, size_t k_len, size_t stride, float scale);
+int ditch_cuda_attention_values(ditch_cuda_device *dev, float *out, size_t vd, const float *scores, size_t n_keys,
+                                const float *v, size_t v_len, size_t stride);
+/* act: tensor.Activation code; 0 = silu is implemented, others UNSUPPORTED. */
+int ditch_cuda_gated_activation(ditch_cuda_device *dev, uint32_t act, float *out, const float *gate, const float *up,
+                                size_t n, size_t len, size_t in_stride, size_t out_stride);
+int ditch_cuda_rmsnorm_rows(ditch_cuda_device *dev, float *out, const float *x, const float *weight, size_t w_len,
+                            size_t n, size_t len, float eps, int gemma_style);
+int ditch_cuda_layernorm_rows(ditch_cuda_device *dev, float *out, const float *x, const float *weight, size_t w_len,
+                              const float *bias, size_t n, size_t len, float eps, int one_plus);
+int ditch_cuda_softmax_rows(ditch_cuda_device *dev, float *x, size_t n, size_t len);
+/* style 0 = neox (rotate half), 1 = gptj (interleaved); tables [table_len][half]. */
+int ditch_cuda_rope_rows(ditch_cuda_device *dev, float *x, size_t n, size_t dim, const float *cos_t,
+                         const float *sin_t, size_t table_len, size_t half, const uint32_t *pos, int style);
+
+/* ---- standalone decoders, bit-exact against src/dequant.zig / src/quant.zig ----
+ * Host buffers in, host buffers out. */
+/* bf16(e4m3[code] * scale[r / br][c / bc]), scales f32 (src/dequant.zig:477-514). */
+int ditch_cuda_dequant_fp8(ditch_cuda_device *dev, const uint8_t *codes, const float *scales, size_t rows,
+                           size_t cols, size_t br, size_t bc, uint16_t *out_bf16);
+/* compressed-tensors pack-quantized INT (src/dequant.zig:518-597): packed
+ * [rows][words_per_row] u32, scales f32 [rows][groups], zeros NULL or
+ * [ceil(rows*bits/32)][groups] u32, g_idx NULL or [cols]. */
+int ditch_cuda_dequant_int(ditch_cuda_device *dev, const uint32_t *packed, size_t words_per_row, const float *scales,
+                           size_t groups, const uint32_t *zeros, const uint32_t *g_idx, size_t rows, size_t cols,
+                           int bits, size_t group, uint16_t *out_bf16);
+/* MXFP4, natural layout (src/dequant.zig:643-673) or the transposed gpt-oss
+ * layout (transposed = 1, src/dequant.zig:603-637; rows/cols are the source's). */
+int ditch_cuda_dequant_mxfp4(ditch_cuda_device *dev, const uint8_t *blocks, const uint8_t *scales, size_t rows,
+                             size_t cols, int transposed, uint16_t *out_bf16);
+/* ggml blocks to f32 (quant.dequantize, src/quant.zig:57-79). */
+int ditch_cuda_dequant_ggml(ditch_cuda_device *dev, int dtype, const uint8_t *src, size_t src_len, size_t n,
+                            float *out_f32);
+
+/* ---- resident model ---- */
+typedef struct {
+    int n_layers, hidden, heads, kv_heads, head_dim, inter, vocab;
+    float eps;
+    double rope_theta;
+    int rope_scaling; /* 0 none, 1 llama3 (src/model.zig:2222-2235) */
+    double rope_factor, rope_low_ff, rope_high_ff, rope_orig_max;
+    int qk_norm; /* per-head q/k RMSNorm before RoPE (Qwen3) */
+    int n_experts, top_k, moe_inter, norm_topk;
+    const uint8_t *moe_layers; /* [n_layers]: 1 = routed-expert MLP; NULL = dense model */
+    int max_seq;               /* longest prompt (RoPE table rows) */
+} ditch_cuda_model_config;
+
+/* Storage formats of a resident tensor. */
+#define DITCH_FMT_F32 0
+#define DITCH_FMT_BF16 1
+#define DITCH_FMT_F16 2
+#define DITCH_FMT_FP8_BLOCK 3 /* E4M3 codes + f32 scales [ceil(rows/br)][ceil(cols/bc)] */
+#define DITCH_FMT_INT_PACKED 4 /* u32 words + scales (f32 or bf16) + optional packed zeros */
+#define DITCH_FMT_MXFP4 5      /* natural layout nibbles [rows][cols/2] + E8M0 [rows][cols/32] */
+#define DITCH_FMT_Q8_0 6
+#define DITCH_FMT_Q4_K 7
+
+#define DITCH_SCALE_F32 0
+#define DITCH_SCALE_BF16 1
+
+/* One tensor of the model. Canonical names: "embed", "final_norm", "lm_head",
+ * and per layer i "L<i>.input_norm", "L<i>.post_norm", "L<i>.q|k|v|o",
+ * "L<i>.qb|kb|vb", "L<i>.q_norm|k_norm", "L<i>.gate|up|down" (dense MLP),
+ * "L<i>.router" and the expert stacks "L<i>.e_gate|e_up|e_down" ([slabs =
+ * experts][rows][cols]). Host memory (or device memory when on_device is
+ * set), read during the call only. */
+typedef struct {
+    const char *name;
+    int format;
+    size_t slabs, rows, cols;
+    const void *data;
+    size_t data_bytes;
+    const void *scales;
+    size_t scales_bytes;
+    int scales_dtype;
+    const void *zeros;
+    size_t zeros_bytes;
+    int block_rows, block_cols; /* FP8 block; INT: block_cols = group size */
+    int bits;                   /* INT: bits per field */
+    int on_device;              /* 1: data / scales / zeros are device pointers of this GPU */
+} ditch_cuda_tensor;
+
+int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config *cfg, const ditch_cuda_tensor *tensors,
+                          size_t n_tensors, ditch_cuda_model **out);
+void ditch_cuda_model_free(ditch_cuda_model *m);
+/* Device bytes the resident model holds. */
+uint64_t ditch_cuda_model_bytes(const ditch_cuda_model *m);
+
+/* model.forward (src/model.zig:4619) with ForwardOptions (3136-3144): rows
+ * {b, pos} per token (every prompt's rows contiguous, positions 0..len-1);
+ * residuals [L+1][nc][H] for capture_rows (entry 0 = embedding, entry l =
+ * output of layer l-1); logits [nl][V] for logit_rows. NULL outputs skip. */
+int ditch_cuda_forward(ditch_cuda_model *m, const uint32_t *tokens, const uint32_t *row_b, const uint32_t *row_pos,
+                       size_t n, const size_t *capture_rows, size_t nc, float *residuals, const size_t *logit_rows,
+                       size_t nl, float *logits);
+
+/* engine.getResidualMeanObserved (src/engine.zig:314-438) without winsorising:
+ * prompts given as concatenated tokens with prompt_offsets[n_prompts + 1];
+ * the last `window` tokens of every prompt are averaged and summed in f64
+ * into sums [L+1][H] (added to); *count += prompts seen. batch_size bounds
+ * the prompts per forward (0 = all). */
+int ditch_cuda_residual_sums(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets,
+                             size_t n_prompts, size_t window, size_t batch_size, double *sums, uint64_t *count);
+
+/* abliterate.computeDirections (src/abliterate.zig:88-109) from the f64 sums
+ * of the good and bad passes; dirs [L+1][H] is returned and kept resident
+ * for the edits. */
+int ditch_cuda_directions(ditch_cuda_model *m, const double *good_sums, uint64_t good_count, const double *bad_sums,
+                          uint64_t bad_count, int orthogonalize, float *dirs);
+/* Uploads directions [entries][H] computed elsewhere. */
+int ditch_cuda_set_directions(ditch_cuda_model *m, const float *dirs, size_t entries);
+
+/* abliterate.Params (src/abliterate.zig:40-45). */
+typedef struct {
+    float max_weight, max_weight_position, min_weight, min_weight_distance;
+} ditch_cuda_params;
+
+/* abliterate.apply, row_normalization none (src/abliterate.zig:148-280): per
+ * layer, lambda = kernelWeight(p, layer); v = dirs[layer + 1] or the
+ * interpolated direction (direction_index >= 0, interpolateBasis :119-131);
+ * A = v^T W, B = -lambda v on o_proj (attn_o) and down_proj (mlp_down; every
+ * expert's down projection on an MoE layer, the broad edit). NULL params =
+ * component untouched. The deltas act inside the GEMM epilogues; weights are
+ * not modified. */
+int ditch_cuda_apply_edit(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down,
+                          float direction_index, int use_direction_index);
+/* moe.applyExpertSelective, ranked selection (src/moe.zig:1373-1477): the
+ * o_proj edit as above, then per MoE layer the top n_experts experts by
+ * ||v^T W_down|| / ||W_down||_F get lambda * strength. */
+int ditch_cuda_apply_expert_edit(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down,
+                                 float direction_index, int use_direction_index, size_t n_experts, float strength);
+/* model.resetDeltas (src/model.zig:2348-2369). */
+int ditch_cuda_reset_edits(ditch_cuda_model *m);
+/* moe.scoreDown per routed expert of `layer` and rankScores (descending,
+ * ties by index): order [E], scores [E] (either may be NULL). */
+int ditch_cuda_rank_experts(ditch_cuda_model *m, size_t layer, const float *v, uint32_t *order, float *scores);
+
+/* KlDivergence.init with kl_tokens = 1 (src/scorers.zig:311-369): the prompts
+ * stay resident with the unedited model's first-token log-probabilities. */
+int ditch_cuda_kl_init(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets, size_t n_prompts);
+/* KlDivergence.score (src/scorers.zig:378-402) under the current edits on the
+ * resident prompts: mean over prompts of sum_j exp(lb_j)(lb_j - lt_j), f64. */
+int ditch_cuda_kl_score(ditch_cuda_model *m, double *kl);
+/* Same, uploading the prompts from host memory in the call (they must be the
+ * prompts given to ditch_cuda_kl_init). */
+int ditch_cuda_kl_score_prompts(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets,
+                                size_t n_prompts, double *kl);
+
+/* The materialised rank-1 weight edit W <- W - alpha r (r^T W) on a bf16
+ * matrix in device memory (GEMV-T then rank-1 update; the edited matrix of
+ * src/abliterate.zig:544-552 rounded to bf16). r is a device f32 [rows]. */
+int ditch_cuda_edit_weight_bf16(ditch_cuda_device *dev, void *w, size_t rows, size_t cols, const float *r,
+                                float alpha);
+
+/* ---- timing support (CUDA events on the device's stream) ---- */
+/* Accumulated device time and launch count of the weight GEMMs since the
+ * last reset (when enabled), for roofline reporting. */
+int ditch_cuda_set_profiling(ditch_cuda_device *dev, int enabled);
+int ditch_cuda_gemm_stats(ditch_cuda_device *dev, double *ms, uint64_t *launches, double *flops);
+int ditch_cuda_reset_stats(ditch_cuda_device *dev);
+/* Number of kernels this library launched since the last reset. */
+uint64_t ditch_cuda_launches(const ditch_cuda_device *dev);
+/* Records an event pair around work issued between start and stop. */
+int ditch_cuda_timer_start(ditch_cuda_device *dev);
+int ditch_cuda_timer_stop(ditch_cuda_device *dev, float *ms);
+int ditch_cuda_synchronize(ditch_cuda_device *dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -124,3 +124,48 @@ class Golden:
 
     def prompts(self):
         return [c["ids"].astype(np.uint32) for c in self.cases]
+
+    # ---- the stored tensors, for the CUDA product's loader ----
+    def _cuda_tensor(self, canon, hf, slabs=1, stack=None):
+        from ditch_b200 import Tensor
+        from ditch_b200.cuda import SCALE_BF16, SCALE_F32
+        names = stack or [hf]
+        first = names[0]
+        base = first[: -len(".weight")]
+        if first in self.raw:
+            dt = self.dtypes[first]
+            a = np.stack([self.raw[n] for n in names]) if stack else self.raw[first]
+            rows, cols = (a.shape[-2], a.shape[-1]) if a.ndim >= 2 else (a.shape[0], 1)
+            if dt == "BF16":
+                return Tensor(canon, "bf16", rows, cols, a, slabs=slabs)
+            if dt == "F32":
+                return Tensor(canon, "f32", rows, cols, a, slabs=slabs)
+            if dt == "F8_E4M3":
+                br, bc = self.block
+                sc = np.stack([self.raw[n + "_scale_inv"] for n in names]) if stack else self.raw[first + "_scale_inv"]
+                return Tensor(canon, "fp8", rows, cols, a, slabs=slabs, scales=sc.astype(np.float32),
+                              scales_dtype=SCALE_F32, block_rows=br, block_cols=bc)
+            raise ValueError(dt)
+        if base + ".weight_packed" in self.raw:
+            rows, cols = (int(v) for v in self.raw[base + ".weight_shape"])
+            return Tensor(canon, "int", rows, cols, self.raw[base + ".weight_packed"],
+                          scales=self.raw[base + ".weight_scale"], scales_dtype=SCALE_BF16,
+                          zeros=self.raw.get(base + ".weight_zero_point"), block_cols=self.int_group,
+                          bits=self.int_bits)
+        raise KeyError(hf)
+
+    def cuda_tensors(self):
+        s = self.spec
+        out = []
+        for canon, hf in self.hf_names().items():
+            if self.has(hf):
+                out.append(self._cuda_tensor(canon, hf))
+        if s.get("moe_layers"):
+            for i in range(s["n_layers"]):
+                if not s["moe_layers"][i]:
+                    continue
+                p = f"model.layers.{i}.mlp.experts."
+                for a in ("gate", "up", "down"):
+                    names = [p + f"{e}.{a}_proj.weight" for e in range(s["n_experts"])]
+                    out.append(self._cuda_tensor(f"L{i}.e_{a}", None, slabs=s["n_experts"], stack=names))
+        return out

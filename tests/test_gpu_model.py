@@ -1,0 +1,130 @@
+"""The resident model (forward, capture, edit, KL, directions) on the GPU
+against the reference fixtures and the oracle.
+
+Tolerance: the device forward runs its weight products as bf16 tensor-core
+MMAs with f32 accumulation (activations rounded to bf16 at every GEMM input,
+the residual stream kept in f32), against ditch's all-f32 CPU engine. The
+bound used here is max abs error <= FWD_ATOL + FWD_RTOL * max|reference| per
+compared vector; the reference's own fixture check is 2e-3 max abs on f32
+(src/model_test.zig:62, 70).
+"""
+import numpy as np
+import pytest
+
+import ditch_b200
+import oracle
+from golden_loader import Golden
+from oracle.model import OracleModel, flatten_batch
+
+pytestmark = pytest.mark.gpu
+
+FWD_ATOL, FWD_RTOL = 2e-3, 2e-2
+DENSE = ["qwen2", "llama", "qwen3", "qwen2_fp8", "qwen2_int4"]
+
+
+def bound(want):
+    return FWD_ATOL + FWD_RTOL * float(np.abs(want).max())
+
+
+def load(device, family):
+    g = Golden(family)
+    return g, ditch_b200.Model(device, g.spec, g.cuda_tensors(), max_seq=64)
+
+
+@pytest.mark.parametrize("family", DENSE)
+def test_fixture_forward(device, family):
+    g, m = load(device, family)
+    toks, rb, rp, cap, first, take, last = flatten_batch(g.prompts())
+    res, logits = m.forward(toks, rb, rp, cap, last)
+    om = OracleModel(g.spec, g.f32_weights())
+    ores, ologits = om.forward(toks, rb, rp, cap, last)
+    for i, c in enumerate(g.cases):
+        assert np.abs(logits[i] - c["last_logits"]).max() <= bound(c["last_logits"])
+        assert np.abs(res[:, i] - c["last_hidden"]).max() <= bound(c["last_hidden"])
+        assert np.abs(logits[i] - ologits[i]).max() <= bound(ologits[i])
+        assert int(np.argmax(logits[i])) == c["argmax"]
+    m.close()
+
+
+def test_forward_rejects_bad_rows_and_tokens(device):
+    g, m = load(device, "qwen2")
+    with pytest.raises(ditch_b200.Unsupported):
+        m.forward([1, 2, 3], [0, 0, 0], [0, 2, 3], [], [2])  # positions not contiguous
+    with pytest.raises(ditch_b200.DitchCudaError):
+        m.forward([1, 2, 99999], [0, 0, 0], [0, 1, 2], [], [2])  # token outside the table
+    res, logits = m.forward([1, 2, 3], [0, 0, 0], [0, 1, 2], [], [2])  # the context is still usable
+    assert np.isfinite(logits).all()
+    m.close()
+
+
+@pytest.mark.parametrize("family", ["qwen2", "qwen2_fp8"])
+def test_edit_and_kl(device, family):
+    """abliterate.apply (none mode) + KlDivergence on device vs the oracle with the same deltas."""
+    g, m = load(device, family)
+    s = g.spec
+    prompts = g.prompts()
+    rng = np.random.default_rng(5)
+    dirs = rng.standard_normal((s["n_layers"] + 1, s["hidden"])).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    m.set_directions(dirs)
+    m.kl_init(prompts)
+    assert abs(m.kl_score()) < 1e-6  # base model: KL 0 (src/scorers.zig:839-926)
+    po = (1.2, 0.0, 0.5, 3.0)
+    pd = (0.8, 1.0, 0.3, 2.0)
+    m.apply_edit(po, pd)
+    kl = m.kl_score()
+    assert kl > 0
+    # the oracle with deltas from its own GEMV of the f32 weights
+    w = g.f32_weights()
+    om = OracleModel(s, w)
+    for li in range(s["n_layers"]):
+        v = dirs[li + 1]
+        for comp, p, name in (("o", po, "o"), ("down", pd, "down")):
+            lam = oracle.kernel_weight(p, li)
+            if lam is None:
+                continue
+            a, b = oracle.compute_delta_none(w[f"L{li}.{name}"], v, lam)
+            om.set_delta(li, comp, a, b)
+    toks, rb, rp, cap, first, take, last = flatten_batch(prompts)
+    _, base_logits = OracleModel(s, w).forward(toks, rb, rp, (), last)
+    _, ed_logits = om.forward(toks, rb, rp, (), last)
+    okl, _ = oracle.kl_first_token(oracle.log_softmax(base_logits), ed_logits)
+    assert abs(kl - okl) <= 2e-3 + 0.05 * abs(okl), (kl, okl)
+    # the e2e entry (prompts uploaded in the call) gives the same value
+    tokens = np.concatenate(prompts).astype(np.uint32)
+    offs = np.zeros(len(prompts) + 1, np.uintp)
+    offs[1:] = np.cumsum([len(p) for p in prompts])
+    assert m.kl_score_prompts(tokens, offs, len(prompts)) == kl
+    m.reset_edits()
+    assert abs(m.kl_score()) < 1e-6
+    # interpolated global direction (direction_index)
+    m.apply_edit(po, pd, direction_index=0.6)
+    assert m.kl_score() > 0
+    m.close()
+
+
+def test_residual_sums_and_directions(device):
+    """engine.getResidualMeanObserved + computeDirections vs the oracle."""
+    g, m = load(device, "qwen2")
+    s = g.spec
+    rng = np.random.default_rng(11)
+    good = [rng.integers(0, s["vocab"], rng.integers(3, 12)).astype(np.uint32) for _ in range(5)]
+    bad = [rng.integers(0, s["vocab"], rng.integers(3, 12)).astype(np.uint32) for _ in range(6)]
+    om = OracleModel(s, g.f32_weights())
+    for window in (1, 3):
+        sums = {}
+        for name, ps in (("good", good), ("bad", bad)):
+            dsum, count = m.residual_sums(ps, window=window, batch_size=4)
+            assert count == len(ps)
+            toks, rb, rp, cap, first, take, last = flatten_batch(ps, window)
+            res, _ = om.forward(toks, rb, rp, cap, ())
+            osum = oracle.residual_sums(res, first, take)
+            assert np.abs(dsum - osum).max() <= bound(osum)
+            sums[name] = (dsum, count, osum)
+        dirs = m.directions(sums["good"][0], sums["good"][1], sums["bad"][0], sums["bad"][1], True)
+        gm = (sums["good"][2] / len(good)).astype(np.float32)
+        bm = (sums["bad"][2] / len(bad)).astype(np.float32)
+        odirs = oracle.compute_directions(gm, bm, True)
+        cos = np.sum(dirs * odirs, axis=1)
+        assert cos.min() > 0.99, cos
+    m.close()
