@@ -1,0 +1,431 @@
+"""Trial-evaluation benchmark of ditch's hot path on B200.
+
+Workload (per GPU, weak scaling): a Llama-3-8B-shaped decoder (32 layers,
+hidden 4096, 32/8 heads, SwiGLU 14336, vocab 128256, RoPE theta 5e5) with
+random N(0, 0.02) weights quantised to FP8 E4M3 with 128x128 f32 block scales
+(embedding, LM head and norms bf16), 128 prompts x 64 uniform random token
+ids. Synthetic data: there is no network for checkpoints; the reference's
+config is itself synthetic.
+
+One-off per study (reported, not timed as a step): residual capture over a
+good and a bad batch (128 prompts each), an all-reduce of the f64 residual sums
+across ranks, and the refusal directions.
+
+One step = one trial: decode a seeded parameter vector (src/search.zig:108-139),
+the none-mode rank-1 edit of every o_proj and down_proj (A = v^T W on the FP8
+weights, src/abliterate.zig:264-280), the edited forward of the 128 KL prompts
+with the deltas in the GEMM epilogues, and the first-token KL against the
+unedited model (src/scorers.zig:378-402), all-reduced across ranks.
+
+value = forward tokens per trial x ranks x steps / max-over-ranks device time.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+C2 = dict(n_layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=14336, vocab=128256, eps=1e-5,
+          rope_theta=5e5)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ditch_b200", choices=["ditch_b200", "reference"])
+    ap.add_argument("--prompts", type=int, default=128)
+    ap.add_argument("--seq", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=C2["n_layers"])
+    ap.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline sample budget (seconds)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=1234)
+    return ap.parse_args()
+
+
+def dist_setup(gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        pg = dist
+    return world, rank, local, pg
+
+
+def trial_params(rng, n_layers):
+    """A seeded TPE-like parameter vector decoded as src/search.zig:108-139."""
+    out = []
+    for _ in range(2):  # attn.o_proj, mlp.down_proj
+        max_w = float(rng.uniform(0.8, 1.5))
+        max_pos = float(rng.uniform(0.6 * (n_layers - 1), n_layers - 1))
+        min_frac = float(rng.uniform(0.0, 1.0))
+        min_dist = float(rng.uniform(1.0, 0.6 * (n_layers - 1)))
+        out.append((max_w, max_pos, min_frac * max_w, min_dist))
+    scope_global = rng.random() < 0.5
+    di = float(rng.uniform(0.4, 0.9) * (n_layers - 1)) if scope_global else None
+    return out[0], out[1], di
+
+
+# ---- synthetic model on the device (torch is the device-memory plumbing here) ----
+def fp8_block_quant(w, block=128):
+    """FP8 E4M3 with f32 block scales amax/448 (tools/make_fixture.py:109-127), on the GPU."""
+    import torch
+
+    rows, cols = w.shape
+    rb, cb = -(-rows // block), -(-cols // block)
+    wp = torch.nn.functional.pad(w.float(), (0, cb * block - cols, 0, rb * block - rows))
+    blocks = wp.view(rb, block, cb, block)
+    amax = blocks.abs().amax(dim=(1, 3)).clamp_min(1e-12)
+    scale = (amax / 448.0).float()
+    q = (blocks / scale[:, None, :, None]).to(torch.float8_e4m3fn)
+    codes = q.view(rb * block, cb * block)[:rows, :cols].contiguous().view(torch.uint8)
+    return codes, scale.contiguous()
+
+
+def build_c2_model(dev, spec, seed, max_seq):
+    import torch
+
+    import ditch_b200
+    from ditch_b200 import Tensor
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    H, I, V, L = spec["hidden"], spec["inter"], spec["vocab"], spec["n_layers"]
+    qd, kvd = spec["heads"] * spec["head_dim"], spec["kv_heads"] * spec["head_dim"]
+    keep, tensors = [], []
+
+    def bf16(shape):
+        return (torch.randn(shape, generator=g, device="cuda", dtype=torch.float32) * 0.02).to(torch.bfloat16)
+
+    def add_fp8(name, rows, cols):
+        w = bf16((rows, cols))
+        codes, scale = fp8_block_quant(w)
+        del w
+        keep.extend([codes, scale])
+        tensors.append(Tensor(name, "fp8", rows, cols, codes, scales=scale, block_rows=128, block_cols=128))
+
+    ones = torch.ones(H, dtype=torch.bfloat16, device="cuda")
+    keep.append(ones)
+    emb = bf16((V, H))
+    lm = bf16((V, H))
+    keep.extend([emb, lm])
+    tensors += [Tensor("embed", "bf16", V, H, emb), Tensor("lm_head", "bf16", V, H, lm),
+                Tensor("final_norm", "bf16", H, 1, ones)]
+    model = None
+    for i in range(L):
+        tensors += [Tensor(f"L{i}.input_norm", "bf16", H, 1, ones), Tensor(f"L{i}.post_norm", "bf16", H, 1, ones)]
+        add_fp8(f"L{i}.q", qd, H)
+        add_fp8(f"L{i}.k", kvd, H)
+        add_fp8(f"L{i}.v", kvd, H)
+        add_fp8(f"L{i}.o", H, qd)
+        add_fp8(f"L{i}.gate", I, H)
+        add_fp8(f"L{i}.up", I, H)
+        add_fp8(f"L{i}.down", H, I)
+    torch.cuda.synchronize()
+    model = ditch_b200.Model(dev, spec, tensors, max_seq=max_seq)
+    del keep, tensors
+    torch.cuda.empty_cache()
+    return model
+
+
+# ---- clocks ----
+class Clocks:
+    def __init__(self, index):
+        self.p = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{index}.csv")
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(index), "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        load = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---- CPU baseline: the oracle (a C restatement of ditch's CPU engine) ----
+def cpu_baseline(args, prompts=None):
+    """Times ditch's CPU engine restated in C (oracle/, f32, VL=16 FMA, all
+    host threads) on a bounded sample: one decoder layer of the C2 shape over
+    a few prompts, the LM head rows, the per-layer edit GEMVs and the KL rows,
+    extrapolated to the whole trial (32 layers, `--prompts` prompts). Weights
+    are random f32 (timing does not depend on values; the FP8 decode happens
+    once at load in the reference's mapped mode and is not timed)."""
+    import oracle
+    from oracle.model import OracleModel, flatten_batch
+
+    L = oracle.lib()
+    cores = L.or_get_threads()
+    spec = dict(C2, n_layers=1)
+    H, I, V = spec["hidden"], spec["inter"], spec["vocab"]
+    qd, kvd = spec["heads"] * spec["head_dim"], spec["kv_heads"] * spec["head_dim"]
+    rng = np.random.default_rng(args.seed)
+
+    def w(r, c):
+        return (rng.standard_normal((r, c), dtype=np.float32) * 0.02)
+
+    big = w(V, H)
+    ones = np.ones(H, np.float32)
+    weights = {"embed": big, "lm_head": big, "final_norm": ones, "L0.input_norm": ones, "L0.post_norm": ones,
+               "L0.q": w(qd, H), "L0.k": w(kvd, H), "L0.v": w(kvd, H), "L0.o": w(H, qd), "L0.gate": w(I, H),
+               "L0.up": w(I, H), "L0.down": w(H, I)}
+    m = OracleModel(spec, weights)
+    p_cpu = 2
+    sample = [rng.integers(0, V, args.seq).astype(np.uint32) for _ in range(p_cpu)]
+    toks, rb, rp, cap, first, take, last = flatten_batch(sample)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        m.forward(toks, rb, rp, (), ())
+        reps += 1
+        if time.perf_counter() - t0 > args.cpu_sample_s * 0.5 or reps >= 8:
+            break
+    t_layer = (time.perf_counter() - t0) / reps
+    hl = rng.standard_normal((p_cpu, H), dtype=np.float32)
+    t0 = time.perf_counter()
+    logits = oracle.matmul_t(hl, big)
+    t_lm = time.perf_counter() - t0
+    base = oracle.log_softmax(logits)
+    t0 = time.perf_counter()
+    oracle.kl_first_token(base, logits)
+    t_kl = time.perf_counter() - t0
+    v = rng.standard_normal(H).astype(np.float32)
+    t0 = time.perf_counter()
+    oracle.compute_delta_none(weights["L0.o"], v, 1.0)
+    oracle.compute_delta_none(weights["L0.down"], v, 1.0)
+    t_edit = time.perf_counter() - t0
+    scale = args.prompts / p_cpu
+    nl = args.layers
+    s_trial = nl * t_layer * scale + (t_lm + t_kl) * scale + nl * t_edit
+    tokens = args.prompts * args.seq
+    return {
+        "value": tokens / s_trial, "unit": "tokens/s", "cores": cores, "kind": "port",
+        "s_per_trial": s_trial,
+        "sample": (f"oracle (C restatement of ditch's f32 CPU engine), {cores} threads: 1 C2 decoder layer over "
+                   f"{p_cpu} prompts x {args.seq} tokens ({reps} reps, {t_layer:.3f} s), LM head + KL on {p_cpu} "
+                   f"rows, o/down edit GEMVs of one layer; extrapolated to {nl} layers x {args.prompts} prompts"),
+    }
+
+
+def reference_arm(args):
+    cb = cpu_baseline(args)
+    tokens = args.prompts * args.seq
+    v = cb["value"]
+    line = {
+        "impl": "reference", "metric": "trial-eval forward tokens/s", "value": round(v, 3), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(tokens / v * 1000.0, 3), "s_per_trial": round(cb["s_per_trial"], 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(args),
+        "cpu_baseline": cb,
+        "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "ditch is Zig and no zig toolchain exists on this image; the reference arm times the C restatement "
+                "of its CPU engine (oracle/), checked against ditch's own fixtures",
+    }
+    return line
+
+
+def config_block(args):
+    return {"workload": "C2: Llama-3-8B-shaped, FP8 E4M3 128x128 block-scaled weights, trial = none-mode rank-1 "
+                        "edit of o_proj/down_proj + edited forward + first-token KL",
+            "layers": args.layers, "prompts_per_gpu": args.prompts, "seq_len": args.seq, "vocab": C2["vocab"],
+            "parallelism": f"dp{args.gpus} (prompt batches)",
+            "l2": "inputs larger than L2 (7 GB of FP8 weights read per trial)"}
+
+
+def all_reduce(dist, arr, op="sum"):
+    """All-reduce of a numpy array across ranks (NCCL over the GPUs)."""
+    if dist is None:
+        return arr
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(arr)).cuda()
+    dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX)
+    return t.cpu().numpy()
+
+
+def traffic_from_profiles():
+    """Per-launch DRAM bytes of the dominant GEMM from the committed ncu summary."""
+    import re
+
+    p = os.path.join(ROOT, "profiles", "gemm_fp8_c2.md")
+    if not os.path.exists(p):
+        return None, None
+    m = re.search(r"traffic_bytes_per_gflop:\s*([0-9.eE+-]+)", open(p).read())
+    return (float(m.group(1)), p) if m else (None, None)
+
+
+def main():
+    args = parse()
+    world, rank, local, dist = dist_setup(args.gpus)
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(reference_arm(args)), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    import torch
+
+    import ditch_b200
+
+    torch.cuda.set_device(local)
+    dev = ditch_b200.Device(local)
+    spec = dict(C2, n_layers=args.layers)
+    L, V, P, S = spec["n_layers"], spec["vocab"], args.prompts, args.seq
+    t0 = time.time()
+    model = build_c2_model(dev, spec, args.seed, max_seq=S)  # identical weights on every rank
+    load_s = time.time() - t0
+
+    rng = np.random.default_rng(args.seed + 1000 * (rank + 1))
+    good = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
+    bad = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
+    kl_prompts = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
+
+    # one-off per study: capture, cross-rank residual sums, directions
+    dev.synchronize()
+    dev.timer_start()
+    gs, gc = model.residual_sums(good, window=1, batch_size=P)
+    bs, bc = model.residual_sums(bad, window=1, batch_size=P)
+    gs, bs = all_reduce(dist, gs), all_reduce(dist, bs)
+    counts = all_reduce(dist, np.array([gc, bc], np.float64))
+    model.directions(gs, int(counts[0]), bs, int(counts[1]), True)
+    capture_ms = dev.timer_stop()
+    model.kl_init(kl_prompts)
+
+    tokens_flat = np.concatenate(kl_prompts).astype(np.uint32)
+    offs = np.zeros(P + 1, np.uintp)
+    offs[1:] = np.cumsum([len(p) for p in kl_prompts])
+    trial_rng = np.random.default_rng(args.seed + 7)  # same trials on every rank
+    kls = []
+
+    def step(e2e):
+        po, pd, di = trial_params(trial_rng, L)
+        model.apply_edit(po, pd, di)
+        kl = model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score()
+        tot = all_reduce(dist, np.array([kl * P, P], np.float64))
+        kls.append(tot[0] / tot[1])
+
+    def timed(e2e, steps):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        dev.synchronize()
+        dev.timer_start()
+        for _ in range(steps):
+            step(e2e)
+        ms = dev.timer_stop()
+        return float(all_reduce(dist, np.array([ms], np.float64), op="max")[0])
+
+    for _ in range(args.warmup):
+        step(False)
+    dev.set_profiling(True)
+    dev.reset_stats()
+    clocks = Clocks(local)
+    ms = timed(False, args.steps)
+    clk = clocks.stop()
+    gemm_ms, gemm_launches, gemm_flops = dev.gemm_stats()
+    launches = dev.launches()
+    dev.set_profiling(False)
+    for _ in range(max(1, args.warmup // 2)):
+        step(True)
+    ms_e2e = timed(True, args.steps)
+
+    tokens = P * S
+    value = tokens * world * args.steps / (ms / 1000.0)
+    value_e2e = tokens * world * args.steps / (ms_e2e / 1000.0)
+    hbm, tf_burst, tf_sust, src = measured_peaks()
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
+    tpg, tsrc = traffic_from_profiles()
+    traffic = tpg * gemm_flops / 1e9 / max(gemm_launches, 1) if tpg else None
+    line = {
+        "metric": "trial-eval forward tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "s_per_trial": round(ms / args.steps / 1000.0, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8-e4m3 weights, bf16 MMA, f32 accumulate", "data": "synthetic",
+        "config": config_block(args),
+        "e2e": {"value": round(value_e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(tokens * 4 + (P + 1) * 8),
+                "d2h_bytes_per_step": int(P * 8), "ms_per_step": round(ms_e2e / args.steps, 3)},
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05, FP8-decoding operand path)",
+                     "achieved": round(achieved, 1), "peak": tf_sust, "unit": "TFLOP/s",
+                     "frac": round(achieved / tf_sust, 4), "peak_source": f"{src} bf16 sustained",
+                     "traffic": traffic, "traffic_source": tsrc,
+                     "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
+                     "gemm_share_of_step": round(gemm_ms / ms, 4) if ms > 0 else None,
+                     "gemm_tflop_per_step": round(gemm_flops / args.steps / 1e12, 3)},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "one_off": {"load_s": round(load_s, 2), "capture_and_directions_ms": round(capture_ms, 2)},
+        "kl_last": kls[-1] if kls else None,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(args)
+        line["cpu_baseline"] = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in cb.items()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    dev.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

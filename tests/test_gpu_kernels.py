@@ -16,10 +16,11 @@ pytestmark = pytest.mark.gpu
 rng = np.random.default_rng(20261201)
 
 
-def close(got, want, atol, rtol):
-    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
-    bound = atol + rtol * np.abs(want.astype(np.float64))
-    assert np.all(err <= bound), f"max err {err.max():.3g} (bound {bound[np.argmax(err - bound)]:.3g})"
+def close(got, want, atol, rtol, extra=0.0):
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64)).ravel()
+    bound = (atol + rtol * np.abs(want.astype(np.float64)) + extra).ravel()
+    worst = int(np.argmax(err - bound))
+    assert np.all(err <= bound), f"max err {err.max():.3g}; worst {err[worst]:.3g} vs bound {bound[worst]:.3g}"
 
 
 def same_bits(a, b):
@@ -109,7 +110,11 @@ def test_matmul_t_matches_oracle(device, n, rows, cols, dtype):
         raw = w32.astype(np.float16)
         wref = raw.astype(np.float32)
     got = device.matmul_t(x, raw, dtype, rows, cols)
-    close(got, oracle.matmul_t(x, wref), 1e-4 * max(1.0, np.sqrt(cols) / 8), 1e-3)
+    # Split-bf16 drops x_lo * W_lo (|x_lo| <= 2^-9 |x|, |W_lo| <= 2^-9 |W|) and
+    # accumulates in f32 on the tensor cores: on top of the selftest bound, an
+    # error of at most 8e-6 * sum_k |x_k| |W_k| (the dot's condition) is allowed.
+    cond = np.abs(x).astype(np.float64) @ np.abs(wref).astype(np.float64).T
+    close(got, oracle.matmul_t(x, wref), 1e-4, 1e-3, 8e-6 * cond)
 
 
 @pytest.mark.parametrize("dtype", ["q8_0", "q4_k"])
