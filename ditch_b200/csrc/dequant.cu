@@ -242,6 +242,22 @@ __global__ void k_dequant_ggml(int dt, const uint8_t *src, long long n, void *ou
     }
 }
 
+__global__ void k_split(const float *src, int rows, int cols, int cp, int nseg, int pattern, uint16_t *dst) {
+    const long long total = (long long)rows * cp;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(e / cp), c = (int)(e % cp);
+        uint16_t hi = 0, lo = 0;
+        if (c < cols) {
+            const float v = src[(long long)r * cols + c];
+            hi = f32_to_bf16_bits(v);
+            lo = f32_to_bf16_bits(v - bf16_bits_to_f32(hi));
+        }
+        for (int s = 0; s < nseg; s++)
+            dst[(long long)r * nseg * cp + (long long)s * cp + c] = ((pattern >> s) & 1) ? lo : hi;
+    }
+}
+
 __global__ void k_f32_to_bf16(const float *src, uint16_t *dst, long long n) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         dst[i] = f32_to_bf16_bits(src[i]);
@@ -302,6 +318,13 @@ cudaError_t dequant_ggml_f32(int dtype, const uint8_t *src, long long n, float *
 cudaError_t dequant_ggml_bf16(int dtype, const uint8_t *src, long long n, uint16_t *out, cudaStream_t st) {
     if (dtype < 5 || dtype > 12 || n % ggml_bs(dtype)) return cudaErrorInvalidValue;
     k_dequant_ggml<true><<<blocks_for(n, 1), kThreads, 0, st>>>(dtype, src, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t split_bf16(const float *src, int rows, int cols, int cp, int nseg, int pattern, uint16_t *dst,
+                       cudaStream_t st) {
+    if (rows <= 0 || cp <= 0) return cudaSuccess;
+    k_split<<<blocks_for((long long)rows * cp, 1), kThreads, 0, st>>>(src, rows, cols, cp, nseg, pattern, dst);
     return cudaGetLastError();
 }
 

@@ -79,6 +79,45 @@ __device__ __forceinline__ SmemLayout<C> carve(uint8_t *smem_raw) {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
+// Where a tile's operands and outputs live, in dense or grouped mode.
+struct TileInfo {
+    int wt;        // weight tile within the matrix (slab)
+    int tok0;      // first token row (of the B operand and of the output)
+    int tok_cnt;   // valid token rows
+    int a_row0;    // first weight row of the matrix (slab) in the A map
+    int e;         // expert (grouped mode), else -1
+    int kt0, kt1;  // k-tiles of this tile's split
+    bool first_split;
+};
+
+template <int BN>
+__device__ __forceinline__ TileInfo tile_info(const GemmParams &p, int tile, int kt_per_split) {
+    TileInfo t;
+    if (p.sched) {
+        const int4 s = p.sched[tile];
+        t.e = s.x;
+        t.tok0 = s.y;
+        t.tok_cnt = s.z;
+        t.wt = s.w;
+        t.a_row0 = p.a_row0 + s.x * p.slab_rows;
+        t.kt0 = 0;
+        t.kt1 = p.k_tiles;
+        t.first_split = true;
+        return t;
+    }
+    const int split = tile % p.k_splits;
+    const int rest = tile / p.k_splits;
+    t.e = -1;
+    t.wt = rest / p.t_tiles;
+    t.tok0 = (rest % p.t_tiles) * BN;
+    t.tok_cnt = min(BN, p.n_tok - t.tok0);
+    t.a_row0 = p.a_row0;
+    t.kt0 = split * kt_per_split;
+    t.kt1 = min(p.k_tiles, t.kt0 + kt_per_split);
+    t.first_split = split == 0;
+    return t;
+}
+
 // ---- weight decode into the swizzled operand layout ------------------------
 // Thread `r` (0..127) of the transform warps writes row r of the 128 x 64 bf16
 // tile: eight 16-byte chunks, chunk j at (j ^ (r & 7)) within its 128-byte row.
@@ -103,6 +142,10 @@ __device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *arow_tile
     uint8_t *arow = arow_tile + r * 128;
     const int rs = (r >> 1) & 3;  // 64B swizzle of the raw tile
     const float *srow = p.scales + (long long)(grow / p.blk_rows) * p.scale_cols;
+    // Block columns that are a multiple of the 64-wide k-tile share one scale
+    // per tile (the 128 x 128 blocks of the BASELINE checkpoints).
+    const bool one_scale = (p.blk_cols & 63) == 0;
+    const float s_tile = one_scale ? __ldg(srow + k0 / p.blk_cols) : 0.0f;
 #pragma unroll
     for (int c = 0; c < 4; c++) {
         uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ rs) << 4));
@@ -111,7 +154,7 @@ __device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *arow_tile
         for (int h = 0; h < 2; h++) {
             const int j = 2 * c + h;
             int col = k0 + 8 * j;
-            float s = (col < p.k) ? __ldg(srow + col / p.blk_cols) : 0.0f;
+            float s = one_scale ? s_tile : ((col < p.k) ? __ldg(srow + col / p.blk_cols) : 0.0f);
             float f[8];
             e4m3x4_to_f32(words[2 * h], f);
             e4m3x4_to_f32(words[2 * h + 1], f + 4);
@@ -230,7 +273,7 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *L.tmem_base;
 
-    const int tiles = p.w_tiles * p.t_tiles * p.k_splits;
+    const int tiles = p.sched ? *p.n_sched : p.w_tiles * p.t_tiles * p.k_splits;
     const int kt_per_split = (p.k_tiles + p.k_splits - 1) / p.k_splits;
 
     if (warp == 0) {
@@ -238,27 +281,24 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         if (lane == 0) {
             int it = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
-                const int split = tile % p.k_splits;
-                const int rest = tile / p.k_splits;
-                const int wt = rest / p.t_tiles, tt = rest % p.t_tiles;
-                const int kt0 = split * kt_per_split;
-                const int kt1 = min(p.k_tiles, kt0 + kt_per_split);
-                for (int kt = kt0; kt < kt1; kt++, it++) {
+                const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
+                const int arow = ti.a_row0 + ti.wt * BM;
+                for (int kt = ti.kt0; kt < ti.kt1; kt++, it++) {
                     const int s = it % C::kStages;
                     const uint32_t ph = (it / C::kStages) & 1;
                     if (!mbar_wait(&L.empty[s], ph ^ 1, abort, p.status)) break;
                     if (C::kQuant) {
                         mbar_arrive_expect_tx(&L.rawfull[s], C::kNA * C::kRawBytes);
                         const int xb = kt * (FMT == kFmtFp8 ? BK : BK / 2);  // raw bytes along K
-                        tma_load_2d(&tmA, &L.rawfull[s], L.raw(s, 0), xb, p.a_row0 + wt * BM);
-                        if (DUAL) tma_load_2d(&tmA2, &L.rawfull[s], L.raw(s, 1), xb, p.a_row0 + wt * BM + p.a2_row_offset);
+                        tma_load_2d(&tmA, &L.rawfull[s], L.raw(s, 0), xb, arow);
+                        if (DUAL) tma_load_2d(&tmA2, &L.rawfull[s], L.raw(s, 1), xb, arow + p.a2_row_offset);
                         mbar_arrive_expect_tx(&L.full[s], C::kBBytes);
                     } else {
                         mbar_arrive_expect_tx(&L.full[s], C::kNA * C::kABytes + C::kBBytes);
-                        tma_load_2d(&tmA, &L.full[s], L.a(s, 0), kt * BK, p.a_row0 + wt * BM);
-                        if (DUAL) tma_load_2d(&tmA2, &L.full[s], L.a(s, 1), kt * BK, p.a_row0 + wt * BM + p.a2_row_offset);
+                        tma_load_2d(&tmA, &L.full[s], L.a(s, 0), kt * BK, arow);
+                        if (DUAL) tma_load_2d(&tmA2, &L.full[s], L.a(s, 1), kt * BK, arow + p.a2_row_offset);
                     }
-                    tma_load_2d(&tmB, &L.full[s], L.b(s), kt * BK, tt * BN);
+                    tma_load_2d(&tmB, &L.full[s], L.b(s), kt * BK, ti.tok0);
                 }
             }
         }
@@ -268,9 +308,8 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
             constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
             int it = 0, local = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, local++) {
-                const int split = tile % p.k_splits;
-                const int kt0 = split * kt_per_split;
-                const int kt1 = min(p.k_tiles, kt0 + kt_per_split);
+                const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
+                const int kt0 = ti.kt0, kt1 = ti.kt1;
                 const int buf = local & 1;
                 const uint32_t use_ph = (local >> 1) & 1;
                 if (!mbar_wait(&L.tempty[buf], use_ph ^ 1, abort, p.status)) break;
@@ -307,17 +346,22 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         int local = 0;
         for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, local++) {
-            const bool first_split = (tile % p.k_splits) == 0;  // bias and delta once per output
-            const int rest = tile / p.k_splits;
-            const int wt = rest / p.t_tiles, tt = rest % p.t_tiles;
+            const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
+            const bool first_split = ti.first_split;  // bias and delta once per output
             const int buf = local & 1;
             const uint32_t use_ph = (local >> 1) & 1;
             if (!mbar_wait(&L.tfull[buf], use_ph, abort, p.status)) break;
             tc_fence_after();
-            const int n = wt * BM + q * 32 + lane;  // weight row = output feature
+            const int n = ti.wt * BM + q * 32 + lane;  // weight row = output feature
             const bool n_ok = n < p.m_w;
             const float bias = (p.bias && n_ok && first_split) ? p.bias[n] : 0.0f;
-            const float dbn = (p.db && n_ok && first_split) ? p.db[n] : 0.0f;
+            bool delta = p.db && n_ok && first_split;
+            const float *dbp = p.db;
+            if (delta && ti.e >= 0) {
+                delta = p.e_flags == nullptr || p.e_flags[ti.e] != 0;
+                dbp = p.db + ti.e * p.db_stride;
+            }
+            const float dbn = delta ? dbp[n] : 0.0f;
             const uint32_t tbase = tmem + buf * C::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -325,11 +369,12 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                 tmem_ld32(tbase + c0, v);
                 float u[32];
                 if (DUAL) tmem_ld32(tbase + BN + c0, u);
-                const int m0 = tt * BN + c0;
+                const int m0 = ti.tok0 + c0;
+                const int m_end = ti.tok0 + ti.tok_cnt;
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
                     const int m = m0 + j;
-                    if (!n_ok || m >= p.n_tok) continue;
+                    if (!n_ok || m >= m_end) continue;
                     float r = v[j];
                     if (p.xa && dbn != 0.0f) r += p.xa[m] * dbn;
                     r += bias;
@@ -360,13 +405,10 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         const int xw = warp - (2 + kEpiWarps);
         int it = 0;
         for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
-            const int split = tile % p.k_splits;
-            const int rest = tile / p.k_splits;
-            const int wt = rest / p.t_tiles;
-            const int kt0 = split * kt_per_split;
-            const int kt1 = min(p.k_tiles, kt0 + kt_per_split);
+            const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
+            const int wt = ti.wt;
             bool ok = true;
-            for (int kt = kt0; kt < kt1; kt++, it++) {
+            for (int kt = ti.kt0; kt < ti.kt1; kt++, it++) {
                 const int s = it % C::kStages;
                 const uint32_t ph = (it / C::kStages) & 1;
                 if (!mbar_wait(&L.rawfull[s], ph, abort, p.status)) {
@@ -375,8 +417,8 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                 }
 #pragma unroll
                 for (int i = 0; i < C::kNA; i++) {
-                    int grow = p.a_row0 + wt * BM + r + (i ? p.a2_row_offset : 0);
-                    int vrow = min(grow, p.a_row0 + (i ? p.a2_row_offset : 0) + p.m_w - 1);  // clamp side-data reads
+                    int grow = ti.a_row0 + wt * BM + r + (i ? p.a2_row_offset : 0);
+                    int vrow = min(grow, ti.a_row0 + (i ? p.a2_row_offset : 0) + p.m_w - 1);  // clamp side-data reads
                     if (FMT == kFmtFp8) xform_fp8(L.raw(s, i), L.a(s, i), r, vrow, kt * BK, p);
                     if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(s, i), L.a(s, i), r, vrow, kt * BK, p);
                     if (FMT == kFmtInt4) xform_int4(L.raw(s, i), L.a(s, i), r, vrow, kt * BK, p);
@@ -471,8 +513,11 @@ cudaError_t launch_t(const GemmOperand &a, const GemmOperand *a2, const GemmOper
     p.t_tiles = (p.n_tok + BN - 1) / BN;
     if (p.k_splits < 1) p.k_splits = 1;
     if (p.k_splits > p.k_tiles) p.k_splits = p.k_tiles;
+    if (p.sched) p.k_splits = 1;  // grouped tiles are whole-K
     const int tiles = p.w_tiles * p.t_tiles * p.k_splits;
-    const int grid = std::min(tiles, num_sms);
+    // grouped mode: the tile count is on the device; the grid is persistent
+    const int grid = p.sched ? num_sms : std::min(tiles, num_sms);
+    if (grid <= 0) return cudaSuccess;
     gemm_kernel<BN, DUAL, FMT><<<grid, C::kThreads, C::kSmemBytes, stream>>>(ma, ma2, mb, p);
     return cudaGetLastError();
 }
@@ -495,17 +540,27 @@ cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, co
                         int num_sms, cudaStream_t stream) {
     const bool dual = (p.flags & kEpiSwiglu) != 0;
     if (dual && !a2) return cudaErrorInvalidValue;
-    // Narrow token tiles for small batches (decode-like calls stay
-    // weight-bandwidth bound and need no padding to 256 tokens).
+    const int bn = p.bn ? p.bn : gemm_token_tile(p.n_tok, dual);
     if (dual) {
-        if (p.n_tok <= 32) return dispatch_fmt<32, true>(fmt, a, a2, b, p, num_sms, stream);
-        if (p.n_tok <= 64) return dispatch_fmt<64, true>(fmt, a, a2, b, p, num_sms, stream);
-        return dispatch_fmt<128, true>(fmt, a, a2, b, p, num_sms, stream);
+        if (bn == 32) return dispatch_fmt<32, true>(fmt, a, a2, b, p, num_sms, stream);
+        if (bn == 64) return dispatch_fmt<64, true>(fmt, a, a2, b, p, num_sms, stream);
+        if (bn == 128) return dispatch_fmt<128, true>(fmt, a, a2, b, p, num_sms, stream);
+        return cudaErrorInvalidValue;
     }
-    if (p.n_tok <= 32) return dispatch_fmt<32, false>(fmt, a, a2, b, p, num_sms, stream);
-    if (p.n_tok <= 64) return dispatch_fmt<64, false>(fmt, a, a2, b, p, num_sms, stream);
-    if (p.n_tok <= 128) return dispatch_fmt<128, false>(fmt, a, a2, b, p, num_sms, stream);
-    return dispatch_fmt<256, false>(fmt, a, a2, b, p, num_sms, stream);
+    if (bn == 32) return dispatch_fmt<32, false>(fmt, a, a2, b, p, num_sms, stream);
+    if (bn == 64) return dispatch_fmt<64, false>(fmt, a, a2, b, p, num_sms, stream);
+    if (bn == 128) return dispatch_fmt<128, false>(fmt, a, a2, b, p, num_sms, stream);
+    if (bn == 256) return dispatch_fmt<256, false>(fmt, a, a2, b, p, num_sms, stream);
+    return cudaErrorInvalidValue;
+}
+
+// Narrow token tiles for small batches (decode-like calls stay weight-
+// bandwidth bound and need no padding to 256 tokens).
+int gemm_token_tile(int n_tok, bool dual) {
+    if (n_tok <= 32) return 32;
+    if (n_tok <= 64) return 64;
+    if (dual || n_tok <= 128) return 128;
+    return 256;
 }
 
 }  // namespace ditch

@@ -62,7 +62,19 @@ struct GemmParams {
     long long raw_row_bytes;
     int blk_rows, blk_cols, scale_cols;  // fp8 block shape; int4 group in blk_cols
     int *status;
+    // Grouped mode (token-sorted routed experts): one entry per output tile,
+    // (expert, first token row, token rows, weight tile); the weight rows of
+    // expert e start at a_row0 + e * slab_rows. Null sched = dense mode.
+    const int4 *sched;
+    const int *n_sched;
+    int slab_rows;
+    const int *e_flags;   // per expert: apply the rank-1 delta (xa, db) only when set
+    long long db_stride;  // db of expert e at db + e * db_stride
+    int bn;               // token tile (32, 64, 128, 256); 0 = chosen from n_tok
 };
+
+// Token tile width the GEMM uses for n_tok tokens (dual = SwiGLU mode).
+int gemm_token_tile(int n_tok, bool dual);
 
 // Host side: launches one GEMM on `stream`. Returns a CUDA error code.
 struct GemmOperand {

@@ -26,6 +26,12 @@ cudaError_t dequant_ggml_f32(int dtype, const uint8_t *src, long long n, float *
 // ggml blocks to bf16 (the GEMM operand of a GGUF weight)
 cudaError_t dequant_ggml_bf16(int dtype, const uint8_t *src, long long n, uint16_t *out, cudaStream_t st);
 
+// Split f32 rows into bf16 segments of width cp (zero padded): segment s is
+// the high part bf16(v) (pattern bit s = 0) or the residual bf16(v - hi) (1).
+// A product over concatenated segments [xh | xh | xl] . [Wh | Wl | Wh]^T is
+// then accurate to about 2^-16 relative on bf16 tensor cores.
+cudaError_t split_bf16(const float *src, int rows, int cols, int cp, int nseg, int pattern, uint16_t *dst,
+                       cudaStream_t st);
 cudaError_t f32_to_bf16(const float *src, uint16_t *dst, long long n, cudaStream_t st);
 cudaError_t bf16_to_f32(const uint16_t *src, float *dst, long long n, cudaStream_t st);
 cudaError_t f16_to_f32(const uint16_t *src, float *dst, long long n, cudaStream_t st);

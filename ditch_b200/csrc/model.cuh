@@ -34,6 +34,7 @@ struct Layer {
     Mat down;                                      // [H][I]
     bool moe = false;
     Mat router;                                    // [E][H] (bf16)
+    Mat router3;                                   // [E][3 cp]: split-bf16 [hi | lo | hi] of the router
     Mat e_gate_up;                                 // [E][2 mi][H]: per expert gate rows then up rows
     Mat e_down;                                    // [E][H][mi]
     // none-mode deltas (src/abliterate.zig:270-280): out += (x . a) b
@@ -83,9 +84,8 @@ struct ditch_cuda_model {
     ditch::DevBuf x, h, qkv, att, act, xa;
     ditch::DevBuf res, hl, logits;
     // MoE workspace
-    ditch::DevBuf moe_logits, moe_sel, moe_w, moe_counts, moe_offsets, moe_pos, moe_tok, moe_xg, moe_act, moe_eo,
-        moe_xa, moe_sched;
-    int moe_cap = 0;
+    ditch::DevBuf moe_h3, moe_logits, moe_sel, moe_w, moe_counts, moe_offsets, moe_perm, moe_pw, moe_pexp, moe_slot,
+        moe_xg, moe_act, moe_eo, moe_xa, moe_sched_gu, moe_sched_d, moe_nsched;
     // directions
     ditch::DevBuf dirs;
     std::vector<float> h_dirs;
@@ -116,12 +116,35 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl);
 
 int ensure_workspace(ditch_cuda_model *m, int n_tokens, int nc, int nl);
 
-// MoE MLP of layer `li` on h (bf16 [n][H]); adds the routed output into x.
+// MoE MLP of layer `li`: post-norm of x, routing, experts, combine into x.
 int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n);
+
+// The split-bf16 router operand from f32 router weights [E][hidden] (device).
+int build_router_split(ditch_cuda_device *dev, const float *router_f32, int E, int hidden, Mat &out);
 
 // GEMM with a resident weight as the A operand.
 int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
                 void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
                 int a2_row_offset);
+
+// Options beyond the dense single-matrix product: split-K, or the grouped
+// (per-expert) tile schedule of the routed-expert path.
+struct GemmExtra {
+    int k_splits = 1;
+    const int4 *sched = nullptr;
+    const int *n_sched = nullptr;
+    int slab_rows = 0;
+    const int *e_flags = nullptr;
+    long long db_stride = 0;
+    int bn = 0;
+};
+
+int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
+             void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
+             int a2_row_offset, const GemmExtra *ex);
+
+// Builds a GEMM operand from one tensor of the C ABI (quantised formats the
+// GEMM decodes stay quantised; others are decoded to bf16 once).
+int build_weight(ditch_cuda_device *dev, const ditch_cuda_tensor *t, Mat &out);
 
 }  // namespace ditch

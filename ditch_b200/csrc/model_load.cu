@@ -427,6 +427,18 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
             REQUIRE(eu->slabs == (size_t)E && eu->rows == (size_t)mi && eu->cols == (size_t)H, "layer %d: e_up shape", i);
             REQUIRE(ed->slabs == (size_t)E && ed->rows == (size_t)H && ed->cols == (size_t)mi, "layer %d: e_down shape", i);
             if ((st = build_mat(m.get(), {Seg{r, 0}}, 1, L.router, "router"))) return st;
+            {
+                // f32 router weights for the split-precision router product
+                DevBuf rf;
+                DITCH_CUDA(rf.reserve((size_t)E * H * 4));
+                if (r->format == DITCH_FMT_F32) {
+                    DITCH_CUDA(copy_in(m.get(), rf.ptr, r->data, 0, (size_t)E * H * 4, r));
+                } else {
+                    DITCH_LAUNCH(dev, bf16_to_f32(L.router.data.as<uint16_t>(), rf.as<float>(), (long long)E * H,
+                                                  dev->stream));
+                }
+                if ((st = build_router_split(dev, rf.as<float>(), E, H, L.router3))) return st;
+            }
             std::vector<Seg> gu, dn;
             for (int e = 0; e < E; e++) {
                 gu.push_back(Seg{eg, e});
@@ -476,5 +488,103 @@ void ditch_cuda_model_free(ditch_cuda_model *m) {
 }
 
 uint64_t ditch_cuda_model_bytes(const ditch_cuda_model *m) { return m ? m->bytes : 0; }
+
+}  // extern "C"
+
+namespace ditch {
+
+int build_weight(ditch_cuda_device *dev, const ditch_cuda_tensor *t, Mat &out) {
+    ditch_cuda_model tmp;  // the loader helpers only need the device
+    tmp.dev = dev;
+    std::vector<Seg> segs;
+    const int slabs = (int)std::max<size_t>(t->slabs, 1);
+    for (int s = 0; s < slabs; s++) segs.push_back(Seg{t, s});
+    return build_mat(&tmp, segs, slabs, out, t->name ? t->name : "weight");
+}
+
+}  // namespace ditch
+
+struct ditch_cuda_weight {
+    ditch_cuda_device *dev;
+    ditch::Mat mat;
+};
+
+extern "C" {
+
+int ditch_cuda_weight_load(ditch_cuda_device *dev, const ditch_cuda_tensor *t, ditch_cuda_weight **out) {
+    clear_error();
+    REQUIRE(dev && t && out, "null argument");
+    *out = nullptr;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    std::unique_ptr<ditch_cuda_weight> w(new ditch_cuda_weight());
+    w->dev = dev;
+    int st = build_weight(dev, t, w->mat);
+    if (st) return st;
+    *out = w.release();
+    return DITCH_CUDA_OK;
+}
+
+void ditch_cuda_weight_free(ditch_cuda_weight *w) {
+    if (!w) return;
+    std::lock_guard<std::mutex> lk(w->dev->mu);
+    cudaSetDevice(w->dev->ordinal);
+    cudaStreamSynchronize(w->dev->stream);
+    delete w;
+}
+
+int ditch_cuda_weight_format(const ditch_cuda_weight *w) { return w ? w->mat.fmt : -1; }
+
+int ditch_cuda_weight_gemm(ditch_cuda_weight *w, const void *x, size_t m, float *out, int k_splits) {
+    clear_error();
+    REQUIRE(w && x && out, "null argument");
+    if (m == 0) return DITCH_CUDA_OK;
+    ditch_cuda_device *dev = w->dev;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    const Mat &mat = w->mat;
+    REQUIRE(mat.slabs == 1, "stacked weights take the grouped path");
+    GemmExtra ex;
+    ex.k_splits = std::max(k_splits, 1);
+    int flags = 0;
+    if (ex.k_splits > 1) {
+        DITCH_CUDA(cudaMemsetAsync(out, 0, m * (size_t)mat.rows * 4, dev->stream));
+        flags = kEpiAtomic;
+    }
+    return gemm_mat(dev, mat, 0, mat.rows, static_cast<const uint16_t *>(x), (int)m, out, mat.rows, flags, nullptr,
+                    nullptr, nullptr, 0, &ex);
+}
+
+int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out) {
+    clear_error();
+    REQUIRE(w && out, "null argument");
+    ditch_cuda_device *dev = w->dev;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    const Mat &mt = w->mat;
+    const int rows = mt.rows * mt.slabs;
+    switch (mt.fmt) {
+    case kFmtBf16:
+        DITCH_CUDA(cudaMemcpyAsync(out, mt.data.ptr, (size_t)rows * mt.cols * 2, cudaMemcpyDeviceToDevice, dev->stream));
+        break;
+    case kFmtFp8:
+        DITCH_LAUNCH(dev, dequant_fp8_bf16(mt.data.as<uint8_t>(), mt.scales.as<float>(), rows, mt.cols, mt.br, mt.bc,
+                                           out, dev->stream));
+        break;
+    case kFmtMxfp4:
+        DITCH_LAUNCH(dev, dequant_mxfp4_bf16(mt.data.as<uint8_t>(), mt.scales.as<uint8_t>(), rows, mt.cols, out,
+                                             dev->stream));
+        break;
+    case kFmtInt4:
+        DITCH_LAUNCH(dev, dequant_int_bf16(mt.data.as<uint32_t>(), mt.cols / 8, mt.scales.as<float>(),
+                                           mt.zeros.as<uint32_t>(), nullptr, mt.groups, rows, mt.cols, 4, mt.group, out,
+                                           dev->stream));
+        break;
+    default:
+        set_error("weight format %d cannot be decoded", mt.fmt);
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    return DITCH_CUDA_OK;
+}
 
 }  // extern "C"

@@ -158,6 +158,12 @@ int make_batch(ditch_cuda_model *m, Batch &b, const uint32_t *tokens, const size
 int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
                 void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
                 int a2_row_offset) {
+    return gemm_mat(m->dev, w, slab_row0, m_rows, act, n_tok, out, ldo, flags, bias, xa, db, a2_row_offset, nullptr);
+}
+
+int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
+             void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
+             int a2_row_offset, const GemmExtra *ex) {
     if (n_tok <= 0 || m_rows <= 0) return DITCH_CUDA_OK;
     GemmOperand A{w.data.ptr, w.rows * w.slabs, w.cols, w.row_bytes};
     GemmOperand B{act, n_tok, w.cols, (long long)w.cols * 2};
@@ -166,6 +172,15 @@ int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, co
     p.n_tok = n_tok;
     p.k = w.cols;
     p.k_splits = 1;
+    if (ex) {
+        p.k_splits = ex->k_splits > 0 ? ex->k_splits : 1;
+        p.sched = ex->sched;
+        p.n_sched = ex->n_sched;
+        p.slab_rows = ex->slab_rows;
+        p.e_flags = ex->e_flags;
+        p.db_stride = ex->db_stride;
+        p.bn = ex->bn;
+    }
     p.a2_row_offset = a2_row_offset;
     p.a_row0 = slab_row0;
     p.out = out;
@@ -187,7 +202,7 @@ int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, co
         p.blk_cols = w.group;
         p.scale_cols = w.groups;
     }
-    cudaError_t e = run_gemm(m->dev, w.fmt, A, (flags & kEpiSwiglu) ? &A : nullptr, B, p);
+    cudaError_t e = run_gemm(dev, w.fmt, A, (flags & kEpiSwiglu) ? &A : nullptr, B, p);
     if (e != cudaSuccess) return cuda_status(e, "gemm");
     return DITCH_CUDA_OK;
 }
@@ -234,10 +249,10 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
         if ((s = gemm_weight(m, L.o, 0, H, m->att.as<uint16_t>(), n, x, H, kEpiResidual, nullptr,
                              L.o_edit ? m->xa.as<float>() : nullptr, L.o_edit ? L.o_b.as<float>() : nullptr, 0)))
             return s;
-        DITCH_LAUNCH(dev, rmsnorm_rows_bf16(x, L.post_norm.as<float>(), n, H, c.eps, h, nullptr, nullptr, nullptr, st));
         if (L.moe) {
             if ((s = moe_mlp(m, L, li, n))) return s;
         } else {
+            DITCH_LAUNCH(dev, rmsnorm_rows_bf16(x, L.post_norm.as<float>(), n, H, c.eps, h, nullptr, nullptr, nullptr, st));
             const int I = c.inter;
             if ((s = gemm_weight(m, L.gate_up, 0, I, h, n, m->act.ptr, I, kEpiSwiglu, nullptr, nullptr, nullptr, I)))
                 return s;

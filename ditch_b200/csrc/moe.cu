@@ -1,15 +1,387 @@
-// Routed-expert MLP (src/moe.zig:998-1228).
+// Routed-expert MLP (src/moe.zig:998-1228, softmax top-k path) on the device:
+//   1. router logits as a split-bf16 tcgen05 GEMM (about 2^-16 relative, so
+//      the top-k picks agree with ditch's f32 router but for exact ties);
+//   2. per token: softmax, top-k (the first maximum wins ties,
+//      src/moe.zig:971-985), renormalisation (norm_topk_prob);
+//   3. a stable counting sort of the (token, slot) pairs by expert: experts in
+//      index order, tokens in order within an expert (the reference's
+//      gather order, src/moe.zig:1144-1152);
+//   4. the expert MLPs as two grouped GEMMs over the sorted rows (SwiGLU
+//      gate/up with the decode of MXFP4 / FP8 / INT4 experts fused into the
+//      operand load, then down with the per-expert rank-1 delta);
+//   5. the weighted combine, each token's experts summed in index order
+//      (acc += w * out, src/moe.zig:1197-1199), added to the residual.
+#include <algorithm>
+
 #include "model.cuh"
 
 namespace ditch {
 
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// RMSNorm (src/tensor.zig:1167-1179) written as [hi | hi | lo] bf16 segments
+// of width cp: the activation side of the split-precision router product.
+__global__ void k_rmsnorm_split3(const float *x, const float *w, int n, int hidden, int cp, float eps, uint16_t *h3) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    const float *xr = x + (long long)row * hidden;
+    float ss = 0.0f;
+    for (int i = lane; i < hidden; i += 32) ss += xr[i] * xr[i];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)hidden + eps);
+    uint16_t *o = h3 + (long long)row * 3 * cp;
+    for (int i = lane; i < cp; i += 32) {
+        uint16_t hi = 0, lo = 0;
+        if (i < hidden) {
+            const float v = xr[i] * inv * w[i];
+            hi = f32_to_bf16_bits(v);
+            lo = f32_to_bf16_bits(v - bf16_bits_to_f32(hi));
+        }
+        o[i] = hi;
+        o[cp + i] = hi;
+        o[2 * cp + i] = lo;
+    }
+}
+
+// Softmax over the E router logits, top-k, renormalisation; one warp per token.
+constexpr int kMaxExpertsPerLane = 32;  // E <= 1024
+
+__global__ void k_route(const float *logits, int n, int E, int k, int norm_topk, int *sel, float *wts) {
+    const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (t >= n) return;
+    const float *row = logits + (long long)t * E;
+    float p[kMaxExpertsPerLane];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; j++) {
+        const int e = j * 32 + lane;
+        p[j] = e < E ? row[e] : -INFINITY;
+        m = fmaxf(m, p[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; j++) {
+        const int e = j * 32 + lane;
+        p[j] = e < E ? expf(p[j] - m) : 0.0f;
+        s += p[j];
+    }
+    s = warp_sum(s);
+    const float inv = 1.0f / s;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; j++) p[j] *= inv;
+    // top-k: the largest probability, ties to the lowest expert index
+    bool taken[kMaxExpertsPerLane];
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; j++) taken[j] = (j * 32 + lane) >= E;
+    float selw[16];
+    int sele[16];
+    for (int q = 0; q < k; q++) {
+        float bv = -INFINITY;
+        int be = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < kMaxExpertsPerLane; j++) {
+            const int e = j * 32 + lane;
+            if (!taken[j] && (p[j] > bv || (p[j] == bv && e < be))) {
+                bv = p[j];
+                be = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) {
+                bv = ov;
+                be = oe;
+            }
+        }
+        sele[q] = be;
+        selw[q] = bv;
+        if ((be & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < kMaxExpertsPerLane; j++)
+                if (j == (be >> 5)) taken[j] = true;
+        }
+    }
+    if (lane == 0) {
+        float sum = 0.0f;
+        for (int q = 0; q < k; q++) sum += selw[q];
+        for (int q = 0; q < k; q++) {
+            sel[(long long)t * k + q] = sele[q];
+            wts[(long long)t * k + q] = (norm_topk && sum > 0.0f) ? selw[q] / sum : selw[q];
+        }
+    }
+}
+
+__global__ void k_count(const int *sel, int nk, int *counts) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nk; i += gridDim.x * blockDim.x) atomicAdd(counts + sel[i], 1);
+}
+
+// One block: expert offsets and the two grouped-GEMM tile schedules
+// (expert-major, then token chunk, then weight tile).
+__global__ void k_schedule(const int *counts, int E, int bn_gu, int wt_gu, int bn_d, int wt_d, int *offsets,
+                           int4 *sched_gu, int *n_gu, int4 *sched_d, int *n_d) {
+    __shared__ int s_cnt[1024], s_off[1024], s_tgu[1024], s_td[1024];
+    const int e = threadIdx.x;
+    const int c = e < E ? counts[e] : 0;
+    s_cnt[e] = c;
+    s_tgu[e] = e < E ? (c + bn_gu - 1) / bn_gu * wt_gu : 0;
+    s_td[e] = e < E ? (c + bn_d - 1) / bn_d * wt_d : 0;
+    __syncthreads();
+    if (e == 0) {  // E <= 1024: a serial scan is cheap next to the GEMMs
+        int a = 0, b = 0, d = 0;
+        for (int i = 0; i < E; i++) {
+            s_off[i] = a;
+            a += s_cnt[i];
+            const int tg = s_tgu[i], td = s_td[i];
+            s_tgu[i] = b;
+            b += tg;
+            s_td[i] = d;
+            d += td;
+        }
+        offsets[E] = a;
+        *n_gu = b;
+        *n_d = d;
+    }
+    __syncthreads();
+    if (e >= E) return;
+    offsets[e] = s_off[e];
+    int tile = s_tgu[e];
+    for (int ch = 0; ch * bn_gu < c; ch++)
+        for (int w = 0; w < wt_gu; w++) sched_gu[tile++] = make_int4(e, s_off[e] + ch * bn_gu, min(bn_gu, c - ch * bn_gu), w);
+    tile = s_td[e];
+    for (int ch = 0; ch * bn_d < c; ch++)
+        for (int w = 0; w < wt_d; w++) sched_d[tile++] = make_int4(e, s_off[e] + ch * bn_d, min(bn_d, c - ch * bn_d), w);
+}
+
+// Stable scatter: block e walks all (token, slot) pairs in order and places
+// those routed to expert e at offsets[e] + rank.
+__global__ void k_scatter(const int *sel, const float *wts, int nk, int k, const int *offsets, int *perm, float *pw,
+                          int *pexp, int *slot) {
+    __shared__ int warp_tot[32];
+    __shared__ int base;
+    const int e = blockIdx.x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (threadIdx.x == 0) base = offsets[e];
+    __syncthreads();
+    for (int i0 = 0; i0 < nk; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const bool hit = i < nk && sel[i] == e;
+        const unsigned ball = __ballot_sync(0xffffffffu, hit);
+        const int within = __popc(ball & ((1u << lane) - 1));
+        if (lane == 0) warp_tot[w] = __popc(ball);
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int j = 0; j < nw; j++) {
+            if (j < w) before += warp_tot[j];
+            total += warp_tot[j];
+        }
+        if (hit) {
+            const int pos = base + before + within;
+            perm[pos] = i / k;
+            pw[pos] = wts[i];
+            pexp[pos] = e;
+            slot[i] = pos;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) base += total;
+        __syncthreads();
+    }
+}
+
+// dst[pos][0..H) = src[perm[pos]][0..H) (bf16 rows, source row stride `ss`).
+__global__ void k_gather_rows(const uint16_t *src, long long ss, const int *perm, int rows, int hidden, uint16_t *dst) {
+    const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const uint16_t *s = src + (long long)perm[r] * ss;
+    uint16_t *d = dst + (long long)r * hidden;
+    if ((hidden & 7) == 0 && (ss & 7) == 0) {
+        for (int i = lane * 8; i < hidden; i += 256)
+            *reinterpret_cast<uint4 *>(d + i) = *reinterpret_cast<const uint4 *>(s + i);
+    } else {
+        for (int i = lane; i < hidden; i += 32) d[i] = s[i];
+    }
+}
+
+// xa[pos] = act[pos] . a[e(pos)] for experts with an edit (the x . A term of
+// the per-expert rank-1 delta), 0 otherwise.
+__global__ void k_rowdot_grouped(const uint16_t *act, const float *e_a, const int *pexp, const int *e_flags, int rows,
+                                 int mi, float *xa) {
+    const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int e = pexp[r];
+    if (!e_flags[e]) {
+        if (lane == 0) xa[r] = 0.0f;
+        return;
+    }
+    const uint16_t *ar = act + (long long)r * mi;
+    const float *a = e_a + (long long)e * mi;
+    float s = 0.0f;
+    for (int i = lane; i < mi; i += 32) s = fmaf(bf16_bits_to_f32(ar[i]), a[i], s);
+    s = warp_sum(s);
+    if (lane == 0) xa[r] = s;
+}
+
+// x[t] += sum over t's experts in index order of w * eo[slot], accumulated
+// from zero as src/moe.zig:1197-1199 (acc += w * out), then added to x.
+__global__ void k_combine(const float *eo, const int *sel, const float *wts, const int *slot, int n, int k, int hidden,
+                          float *x) {
+    const int t = blockIdx.x;
+    __shared__ int order[16];
+    if (threadIdx.x == 0) {
+        int e[16];
+        for (int q = 0; q < k; q++) {
+            order[q] = q;
+            e[q] = sel[(long long)t * k + q];
+        }
+        for (int a = 1; a < k; a++) {  // insertion sort by expert index
+            const int oq = order[a], ev = e[a];
+            int b = a;
+            while (b > 0 && e[b - 1] > ev) {
+                e[b] = e[b - 1];
+                order[b] = order[b - 1];
+                b--;
+            }
+            e[b] = ev;
+            order[b] = oq;
+        }
+    }
+    __syncthreads();
+    float *xr = x + (long long)t * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        float acc = 0.0f;
+        for (int q = 0; q < k; q++) {
+            const int j = order[q];
+            const long long idx = (long long)t * k + j;
+            acc = acc + wts[idx] * eo[(long long)slot[idx] * hidden + i];
+        }
+        xr[i] = xr[i] + acc;
+    }
+}
+
+int tile_for(int avg, bool dual) {
+    if (avg <= 32) return 32;
+    if (avg <= 64) return 64;
+    if (dual || avg <= 160) return 128;
+    return 256;
+}
+
+}  // namespace
+
+int build_router_split(ditch_cuda_device *dev, const float *router_f32, int E, int hidden, Mat &out) {
+    const int cp = (hidden + 63) / 64 * 64;
+    out.fmt = kFmtBf16;
+    out.rows = E;
+    out.cols = 3 * cp;
+    out.slabs = 1;
+    out.row_bytes = (long long)out.cols * 2;
+    DITCH_CUDA(out.data.reserve((size_t)E * out.cols * 2));
+    // weights [Wh | Wl | Wh] against activations [xh | xh | xl]
+    DITCH_LAUNCH(dev, split_bf16(router_f32, E, hidden, cp, 3, 2, out.data.as<uint16_t>(), dev->stream));
+    DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+    return DITCH_CUDA_OK;
+}
+
 int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
-    (void)m;
-    (void)L;
     (void)li;
-    (void)n;
-    set_error("MoE layers are not available in this build");
-    return DITCH_CUDA_UNSUPPORTED;
+    ditch_cuda_device *dev = m->dev;
+    cudaStream_t st = dev->stream;
+    const Config &c = m->cfg;
+    const int H = c.hidden, E = c.n_experts, k = c.top_k, mi = c.moe_inter;
+    if (E > 1024 || k > 16) {
+        set_error("MoE with %d experts / top-%d is not supported (<= 1024 / 16)", E, k);
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    const int nk = n * k;
+    const int cp = (H + 63) / 64 * 64;
+    const int avg = (nk + E - 1) / E;
+    const int bn_gu = tile_for(avg, true), bn_d = tile_for(avg, false);
+    const int wt_gu = (mi + 127) / 128, wt_d = (H + 127) / 128;
+    const int max_gu = (nk / bn_gu + E) * wt_gu, max_d = (nk / bn_d + E) * wt_d;
+    DITCH_CUDA(m->moe_h3.reserve((size_t)n * 3 * cp * 2));
+    DITCH_CUDA(m->moe_logits.reserve((size_t)n * E * 4));
+    DITCH_CUDA(m->moe_sel.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_w.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_counts.reserve((size_t)E * 4));
+    DITCH_CUDA(m->moe_offsets.reserve((size_t)(E + 1) * 4 + 8));
+    DITCH_CUDA(m->moe_perm.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_pw.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_pexp.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_slot.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_xg.reserve((size_t)nk * H * 2));
+    DITCH_CUDA(m->moe_act.reserve((size_t)nk * mi * 2));
+    DITCH_CUDA(m->moe_eo.reserve((size_t)nk * H * 4));
+    DITCH_CUDA(m->moe_xa.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_sched_gu.reserve((size_t)max_gu * 16));
+    DITCH_CUDA(m->moe_sched_d.reserve((size_t)max_d * 16));
+    DITCH_CUDA(m->moe_nsched.reserve(16));
+    int *n_gu = m->moe_nsched.as<int>(), *n_d = n_gu + 1;
+
+    k_rmsnorm_split3<<<(n + 7) / 8, 256, 0, st>>>(m->x.as<float>(), L.post_norm.as<float>(), n, H, cp, c.eps,
+                                                   m->moe_h3.as<uint16_t>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    int s;
+    if ((s = gemm_mat(dev, L.router3, 0, E, m->moe_h3.as<uint16_t>(), n, m->moe_logits.ptr, E, 0, nullptr, nullptr,
+                      nullptr, 0, nullptr)))
+        return s;
+    k_route<<<(n + 7) / 8, 256, 0, st>>>(m->moe_logits.as<float>(), n, E, k, c.norm_topk, m->moe_sel.as<int>(),
+                                         m->moe_w.as<float>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    DITCH_CUDA(cudaMemsetAsync(m->moe_counts.ptr, 0, (size_t)E * 4, st));
+    k_count<<<std::min((nk + 255) / 256, 1024), 256, 0, st>>>(m->moe_sel.as<int>(), nk, m->moe_counts.as<int>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    k_schedule<<<1, 1024, 0, st>>>(m->moe_counts.as<int>(), E, bn_gu, wt_gu, bn_d, wt_d, m->moe_offsets.as<int>(),
+                                   m->moe_sched_gu.as<int4>(), n_gu, m->moe_sched_d.as<int4>(), n_d);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    k_scatter<<<E, 512, 0, st>>>(m->moe_sel.as<int>(), m->moe_w.as<float>(), nk, k, m->moe_offsets.as<int>(),
+                                 m->moe_perm.as<int>(), m->moe_pw.as<float>(), m->moe_pexp.as<int>(),
+                                 m->moe_slot.as<int>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    k_gather_rows<<<(nk + 7) / 8, 256, 0, st>>>(m->moe_h3.as<uint16_t>(), 3LL * cp, m->moe_perm.as<int>(), nk, H,
+                                                m->moe_xg.as<uint16_t>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    GemmExtra gu;
+    gu.sched = m->moe_sched_gu.as<int4>();
+    gu.n_sched = n_gu;
+    gu.slab_rows = 2 * mi;
+    gu.bn = bn_gu;
+    if ((s = gemm_mat(dev, L.e_gate_up, 0, mi, m->moe_xg.as<uint16_t>(), nk, m->moe_act.ptr, mi, kEpiSwiglu, nullptr,
+                      nullptr, nullptr, mi, &gu)))
+        return s;
+    bool any_edit = false;
+    for (uint8_t f : L.e_edit) any_edit |= f != 0;
+    if (any_edit) {
+        k_rowdot_grouped<<<(nk + 7) / 8, 256, 0, st>>>(m->moe_act.as<uint16_t>(), L.e_a.as<float>(),
+                                                       m->moe_pexp.as<int>(), L.e_edit_dev.as<int>(), nk, mi,
+                                                       m->moe_xa.as<float>());
+        DITCH_LAUNCH(dev, cudaGetLastError());
+    }
+    GemmExtra dn;
+    dn.sched = m->moe_sched_d.as<int4>();
+    dn.n_sched = n_d;
+    dn.slab_rows = H;
+    dn.bn = bn_d;
+    dn.e_flags = L.e_edit_dev.as<int>();
+    dn.db_stride = H;
+    if ((s = gemm_mat(dev, L.e_down, 0, H, m->moe_act.as<uint16_t>(), nk, m->moe_eo.ptr, H, 0, nullptr,
+                      any_edit ? m->moe_xa.as<float>() : nullptr, any_edit ? L.e_b.as<float>() : nullptr, 0, &dn)))
+        return s;
+    k_combine<<<n, 256, 0, st>>>(m->moe_eo.as<float>(), m->moe_sel.as<int>(), m->moe_w.as<float>(),
+                                 m->moe_slot.as<int>(), n, k, H, m->x.as<float>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    return DITCH_CUDA_OK;
 }
 
 }  // namespace ditch

@@ -110,6 +110,11 @@ SIGNATURES = {
     "ditch_cuda_kl_score": (C.c_int, [vp, f64p]),
     "ditch_cuda_kl_score_prompts": (C.c_int, [vp, u32p, C.POINTER(sz), sz, f64p]),
     "ditch_cuda_edit_weight_bf16": (C.c_int, [vp, vp, sz, sz, vp, C.c_float]),
+    "ditch_cuda_weight_load": (C.c_int, [vp, C.POINTER(TensorDesc), C.POINTER(vp)]),
+    "ditch_cuda_weight_free": (None, [vp]),
+    "ditch_cuda_weight_format": (C.c_int, [vp]),
+    "ditch_cuda_weight_gemm": (C.c_int, [vp, vp, sz, vp, C.c_int]),
+    "ditch_cuda_weight_decode": (C.c_int, [vp, vp]),
     "ditch_cuda_set_profiling": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_gemm_stats": (C.c_int, [vp, f64p, u64p, f64p]),
     "ditch_cuda_reset_stats": (C.c_int, [vp]),
@@ -359,6 +364,42 @@ class Tensor:
         keep.append(name)
         return TensorDesc(name, FMT[self.fmt], self.slabs, self.rows, self.cols, d, db, s, sb, self.scales_dtype, z,
                           zb, self.block_rows, self.block_cols, self.bits, dev)
+
+
+class Weight:
+    """One resident weight and its dequant-fused GEMM (device pointers in/out)."""
+
+    FORMATS = {0: "bf16", 1: "fp8", 2: "mxfp4", 3: "int4"}
+
+    def __init__(self, device, tensor):
+        self.dev = device
+        keep = []
+        d = tensor.desc(keep)
+        h = vp()
+        check(lib().ditch_cuda_weight_load(device.h, C.byref(d), C.byref(h)))
+        self.h = h
+        self.rows, self.cols = tensor.rows, tensor.cols
+
+    def format(self):
+        return self.FORMATS.get(lib().ditch_cuda_weight_format(self.h), "?")
+
+    def gemm(self, x_ptr, m, out_ptr, k_splits=1):
+        """out[m][rows] (f32) = x[m][cols] (bf16) . W^T, asynchronous on the device stream."""
+        check(lib().ditch_cuda_weight_gemm(self.h, x_ptr, m, out_ptr, k_splits))
+
+    def decode(self, out_ptr):
+        check(lib().ditch_cuda_weight_decode(self.h, out_ptr))
+
+    def close(self):
+        if self.h:
+            lib().ditch_cuda_weight_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Model:

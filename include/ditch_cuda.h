@@ -243,6 +243,23 @@ int ditch_cuda_kl_score_prompts(ditch_cuda_model *m, const uint32_t *tokens, con
 int ditch_cuda_edit_weight_bf16(ditch_cuda_device *dev, void *w, size_t rows, size_t cols, const float *r,
                                 float alpha);
 
+/* ---- one resident weight and its dequant-fused GEMM ----
+ * The product behind `matmulT` (src/tensor.zig:1023-1045) for one weight
+ * kept in HBM in its stored format: FP8 blocks, MXFP4 and INT4 groups of 64k
+ * are decoded inside the GEMM's operand load (src/dequant.zig:477-673
+ * element rules); other formats are decoded to bf16 once at load. */
+typedef struct ditch_cuda_weight ditch_cuda_weight;
+int ditch_cuda_weight_load(ditch_cuda_device *dev, const ditch_cuda_tensor *t, ditch_cuda_weight **out);
+void ditch_cuda_weight_free(ditch_cuda_weight *w);
+/* 0 bf16, 1 FP8 block, 2 MXFP4, 3 INT4 (how the GEMM reads the weight). */
+int ditch_cuda_weight_format(const ditch_cuda_weight *w);
+/* out[m][rows] f32 = x[m][cols] . W^T with x bf16; x and out are device
+ * pointers on the device's stream (asynchronous). k_splits > 1 splits K
+ * (partial sums added atomically; out is zeroed first). */
+int ditch_cuda_weight_gemm(ditch_cuda_weight *w, const void *x_bf16, size_t m, float *out, int k_splits);
+/* The decoded weight [rows][cols] bf16 into device memory (asynchronous). */
+int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out_bf16);
+
 /* ---- timing support (CUDA events on the device's stream) ---- */
 /* Accumulated device time and launch count of the weight GEMMs since the
  * last reset (when enabled), for roofline reporting. */

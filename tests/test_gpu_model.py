@@ -19,7 +19,7 @@ from oracle.model import OracleModel, flatten_batch
 pytestmark = pytest.mark.gpu
 
 FWD_ATOL, FWD_RTOL = 2e-3, 2e-2
-DENSE = ["qwen2", "llama", "qwen3", "qwen2_fp8", "qwen2_int4"]
+DENSE = ["qwen2", "llama", "qwen3", "qwen2_fp8", "qwen2_int4", "qwen3_moe"]
 
 
 def bound(want):
@@ -100,6 +100,67 @@ def test_edit_and_kl(device, family):
     # interpolated global direction (direction_index)
     m.apply_edit(po, pd, direction_index=0.6)
     assert m.kl_score() > 0
+    m.close()
+
+
+def test_moe_expert_ranking_and_edits(device):
+    """moe.rankScores / scoreDown and the broad and selective expert edits vs the oracle."""
+    g, m = load(device, "qwen3_moe")
+    s = g.spec
+    w = g.f32_weights()
+    rng = np.random.default_rng(9)
+    dirs = rng.standard_normal((s["n_layers"] + 1, s["hidden"])).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    m.set_directions(dirs)
+    moe_layers = [i for i in range(s["n_layers"]) if s["moe_layers"][i]]
+    for li in moe_layers:
+        v = dirs[li + 1]
+        order, scores = m.rank_experts(li, v)
+        osc = np.array([oracle.score_down(w[f"L{li}.e_down"][e], v) for e in range(s["n_experts"])], np.float32)
+        np.testing.assert_allclose(scores, osc, rtol=1e-4, atol=1e-6)
+        np.testing.assert_array_equal(order, oracle.rank_scores(osc))
+    prompts = g.prompts()
+    toks, rb, rp, cap, first, take, last = flatten_batch(prompts)
+    m.kl_init(prompts)
+    po, pd = (1.0, 1.0, 0.5, 2.0), (1.1, 1.0, 0.4, 2.0)
+
+    def oracle_kl(selected):
+        om = OracleModel(s, w)
+        for li in range(s["n_layers"]):
+            v = dirs[li + 1]
+            lam = oracle.kernel_weight(po, li)
+            if lam is not None:
+                a, b = oracle.compute_delta_none(w[f"L{li}.o"], v, lam)
+                om.set_delta(li, "o", a, b)
+            lam = oracle.kernel_weight(pd, li)
+            if lam is None:
+                continue
+            if not s["moe_layers"][li]:
+                a, b = oracle.compute_delta_none(w[f"L{li}.down"], v, lam)
+                om.set_delta(li, "down", a, b)
+                continue
+            for e, weight in selected(li, v, lam):
+                a, b = oracle.compute_delta_none(w[f"L{li}.e_down"][e], v, weight)
+                om.set_delta(li, ("e", e), a, b)
+        _, base = OracleModel(s, w).forward(toks, rb, rp, (), last)
+        _, ed = om.forward(toks, rb, rp, (), last)
+        return oracle.kl_first_token(oracle.log_softmax(base), ed)[0]
+
+    # broad: every expert's down projection gets the layer's lambda
+    m.apply_edit(po, pd)
+    want = oracle_kl(lambda li, v, lam: [(e, lam) for e in range(s["n_experts"])])
+    got = m.kl_score()
+    assert abs(got - want) <= 2e-3 + 0.05 * abs(want), (got, want)
+    # selective: the top-2 ranked experts get lambda * strength
+    m.apply_expert_edit(po, pd, n_experts=2, strength=0.7)
+
+    def top2(li, v, lam):
+        sc = np.array([oracle.score_down(w[f"L{li}.e_down"][e], v) for e in range(s["n_experts"])], np.float32)
+        return [(int(e), lam * 0.7) for e in oracle.rank_scores(sc)[:2]]
+
+    want = oracle_kl(top2)
+    got = m.kl_score()
+    assert abs(got - want) <= 2e-3 + 0.05 * abs(want), (got, want)
     m.close()
 
 
