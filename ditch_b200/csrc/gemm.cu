@@ -2,17 +2,21 @@
 // fused weight decode. See gemm.cuh for the contract.
 //
 // Roles (one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: weight tile (or its raw quantised codes) and
-//               token tile into a ring of shared-memory stages;
+//   warp 0      TMA producer: the token tile and the weight tile (bf16) or its
+//               raw quantised codes into rings of shared-memory stages;
 //   warp 1      TMEM allocator and MMA issuer (one elected lane): 4 x
-//               tcgen05.mma (K = 16 each) per 64-wide k-stage, commits to
-//               free the stage and, after the last k-stage, to hand the
-//               accumulator to the epilogue;
+//               tcgen05.mma (K = 16 each) per 64-wide k-stage (two per kk in
+//               SwiGLU mode: gate and up), commits to free the stage and,
+//               after the last k-stage, to hand the accumulator over;
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (double-buffered in
-//               TMEM so the next tile's MMAs overlap this tile's stores),
-//               fused bias / rank-1 delta / residual add / SwiGLU, stores;
-//   warps 6-9   (quantised weights only) transform: expand the raw tile into
-//               bf16 in the 128B-swizzled K-major operand layout.
+//               TMEM when it fits, so the next tile's MMAs overlap these
+//               stores), fused bias / rank-1 delta / residual add / SwiGLU;
+//   warps 6-13  (quantised weights only) transform: expand the raw tile into
+//               bf16 in the 128B-swizzled K-major operand layout, two threads
+//               per weight row.
+//
+// Shared memory: S stages of [A_0 | A_1 (SwiGLU) | B] and R stages of the raw
+// quantised tiles [raw_0 | raw_1]; every buffer 1024-byte aligned.
 #include "gemm.cuh"
 
 #include <algorithm>
@@ -25,7 +29,8 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kEpiWarps = 4;
-constexpr int kXformWarps = 4;
+constexpr int kXformWarps = 8;
+constexpr int kSmemBudget = 224 * 1024;
 
 template <int BN, bool DUAL, int FMT>
 struct Cfg {
@@ -34,30 +39,33 @@ struct Cfg {
     static constexpr int kABytes = BM * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kRawBytes = FMT == kFmtFp8 ? BM * BK : (FMT == kFmtMxfp4 || FMT == kFmtInt4) ? BM * BK / 2 : 0;
-    static constexpr int kStageBytes = kNA * (kABytes + kRawBytes) + kBBytes;
-    static constexpr int kStagesRaw = (220 * 1024) / kStageBytes;
-    static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+    static constexpr int kStageBytes = kNA * kABytes + kBBytes;
+    static constexpr int kRawStageBytes = kNA * kRawBytes;
+    static constexpr int kRawStages = kQuant ? 3 : 0;
+    static constexpr int kStagesFit = (kSmemBudget - kRawStages * kRawStageBytes) / kStageBytes;
+    static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
     static constexpr int kAccCols = kNA * BN;
-    static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
+    static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
+    static constexpr int kTmemColsRaw = kAccBufs * kAccCols;
+    static constexpr int kTmemCols = kTmemColsRaw < 32 ? 32 : kTmemColsRaw;
     static constexpr int kWarps = 2 + kEpiWarps + (kQuant ? kXformWarps : 0);
     static constexpr int kThreads = kWarps * 32;
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kRawStages * kRawStageBytes + 1024 + 256;
+    static_assert(kStages >= 2, "shared memory too small for two stages");
     static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
     static_assert((kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation must be a power of two");
 };
 
-// Stage s holds [A_0 | A_1 (dual) | B | raw_0 | raw_1 (dual)]; every operand
-// buffer is 1024-byte aligned (the 128B swizzle atom).
 template <class C>
 struct SmemLayout {
     uint8_t *base;
-    uint64_t *full, *empty, *rawfull, *tfull, *tempty;
+    uint64_t *full, *empty, *rawfull, *rawempty, *tfull, *tempty;
     uint32_t *tmem_base;
     int *abort;
     __device__ __forceinline__ uint8_t *a(int s, int i) const { return base + s * C::kStageBytes + i * C::kABytes; }
     __device__ __forceinline__ uint8_t *b(int s) const { return base + s * C::kStageBytes + C::kNA * C::kABytes; }
     __device__ __forceinline__ uint8_t *raw(int s, int i) const {
-        return base + s * C::kStageBytes + C::kNA * C::kABytes + C::kBBytes + i * C::kRawBytes;
+        return base + C::kStages * C::kStageBytes + s * C::kRawStageBytes + i * C::kRawBytes;
     }
 };
 
@@ -66,13 +74,15 @@ __device__ __forceinline__ SmemLayout<C> carve(uint8_t *smem_raw) {
     SmemLayout<C> L;
     uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
     L.base = reinterpret_cast<uint8_t *>(base);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(L.base + C::kStages * C::kStageBytes);
+    uint64_t *bars =
+        reinterpret_cast<uint64_t *>(L.base + C::kStages * C::kStageBytes + C::kRawStages * C::kRawStageBytes);
     L.full = bars;
     L.empty = bars + C::kStages;
     L.rawfull = bars + 2 * C::kStages;
-    L.tfull = bars + 3 * C::kStages;
-    L.tempty = bars + 3 * C::kStages + 2;
-    L.tmem_base = reinterpret_cast<uint32_t *>(bars + 3 * C::kStages + 4);
+    L.rawempty = L.rawfull + C::kRawStages;
+    L.tfull = L.rawempty + C::kRawStages;
+    L.tempty = L.tfull + 2;
+    L.tmem_base = reinterpret_cast<uint32_t *>(L.tempty + 2);
     L.abort = reinterpret_cast<int *>(L.tmem_base + 1);
     return L;
 }
@@ -119,119 +129,127 @@ __device__ __forceinline__ TileInfo tile_info(const GemmParams &p, int tile, int
 }
 
 // ---- weight decode into the swizzled operand layout ------------------------
-// Thread `r` (0..127) of the transform warps writes row r of the 128 x 64 bf16
-// tile: eight 16-byte chunks, chunk j at (j ^ (r & 7)) within its 128-byte row.
+// Transform thread t (0..255) owns row r = t & 127 of the 128 x 64 bf16 tile and
+// half h = t >> 7 of it: output chunks 4h .. 4h + 3 (16 bytes = 8 elements
+// each); chunk j lands at (j ^ (r & 7)) within the row's 128 bytes.
 
-__device__ __forceinline__ void e4m3x4_to_f32(uint32_t w, float *f) {
-    uint32_t h01, h23;
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
-        : "=r"(h01), "=r"(h23)
-        : "r"(w));
-    float2 a = __half22float2(*reinterpret_cast<__half2 *>(&h01));
-    float2 b = __half22float2(*reinterpret_cast<__half2 *>(&h23));
-    f[0] = a.x;
-    f[1] = a.y;
-    f[2] = b.x;
-    f[3] = b.y;
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+    uint64_t ra, rb, rd;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+    float2 d;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+    return d;
+}
+
+// Two E4M3 codes (low byte first) to two f32, exactly (via f16x2).
+__device__ __forceinline__ float2 e4m3x2_f32(uint32_t two) {
+    uint32_t h;
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, lo;\n\t}" : "=r"(h) : "r"(two));
+    return __half22float2(*reinterpret_cast<__half2 *>(&h));
+}
+
+// bf16x2 of (a, b) * s, each product rounded to f32 first (the reference's
+// f32 multiply then round-to-nearest-even to bf16).
+__device__ __forceinline__ uint32_t scale_pack(float2 v, float s) {
+    const float2 r = mul2(v, make_float2(s, s));
+    return pack_bf16x2(r.x, r.y);
 }
 
 // FP8 E4M3 with f32 block scales: bf16(code * scale[row / br][col / bc]).
-__device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *arow_tile, int r, int grow, int k0,
+// Raw tile: 128 rows x 64 bytes, TMA 64B swizzle (chunk c at c ^ ((r >> 1) & 3)).
+__device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *atile, int r, int h, int grow, int k0,
                                           const GemmParams &p) {
-    uint8_t *arow = arow_tile + r * 128;
-    const int rs = (r >> 1) & 3;  // 64B swizzle of the raw tile
+    uint8_t *arow = atile + r * 128;
+    const int rs = (r >> 1) & 3;
     const float *srow = p.scales + (long long)(grow / p.blk_rows) * p.scale_cols;
     // Block columns that are a multiple of the 64-wide k-tile share one scale
     // per tile (the 128 x 128 blocks of the BASELINE checkpoints).
     const bool one_scale = (p.blk_cols & 63) == 0;
     const float s_tile = one_scale ? __ldg(srow + k0 / p.blk_cols) : 0.0f;
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-        uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ rs) << 4));
-        uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    for (int cc = 0; cc < 2; cc++) {
+        const int c = 2 * h + cc;  // raw 16-byte chunk: output chunks 2c, 2c + 1
+        const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ rs) << 4));
+        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int j = 2 * c + h;
-            int col = k0 + 8 * j;
-            float s = one_scale ? s_tile : ((col < p.k) ? __ldg(srow + col / p.blk_cols) : 0.0f);
-            float f[8];
-            e4m3x4_to_f32(words[2 * h], f);
-            e4m3x4_to_f32(words[2 * h + 1], f + 4);
+        for (int half = 0; half < 2; half++) {
+            const int j = 2 * c + half;
+            const int col = k0 + 8 * j;
+            const float s = one_scale ? s_tile : ((col < p.k) ? __ldg(srow + col / p.blk_cols) : 0.0f);
+            const uint32_t w0 = words[2 * half], w1 = words[2 * half + 1];
             uint4 o;
-            o.x = pack_bf16x2(f[0] * s, f[1] * s);
-            o.y = pack_bf16x2(f[2] * s, f[3] * s);
-            o.z = pack_bf16x2(f[4] * s, f[5] * s);
-            o.w = pack_bf16x2(f[6] * s, f[7] * s);
+            o.x = scale_pack(e4m3x2_f32(w0 & 0xffff), s);
+            o.y = scale_pack(e4m3x2_f32(w0 >> 16), s);
+            o.z = scale_pack(e4m3x2_f32(w1 & 0xffff), s);
+            o.w = scale_pack(e4m3x2_f32(w1 >> 16), s);
             *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
         }
     }
 }
-
-__device__ __constant__ float kE2M1[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f,
-                                           -0.f, -0.5f, -1.f, -1.5f, -2.f, -3.f, -4.f, -6.f};
 
 __device__ __forceinline__ float e8m0_scale(uint32_t b) {
     return __uint_as_float(b == 0 ? 0x00400000u : (b << 23));
 }
 
+// Two E2M1 nibbles (one byte, low nibble first) to two f32, exactly (via f16x2).
+__device__ __forceinline__ float2 e2m1x2_f32(uint32_t byte) {
+    uint32_t h;
+    asm("{\n\t.reg .b8 b;\n\tcvt.u8.u32 b, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b;\n\t}" : "=r"(h) : "r"(byte));
+    return __half22float2(*reinterpret_cast<__half2 *>(&h));
+}
+
 // MXFP4 (natural layout): bf16(e2m1[nibble] * 2^(e - 127)), low nibble first.
-__device__ __forceinline__ void xform_mxfp4(const uint8_t *raw, uint8_t *arow_tile, int r, int grow, int k0,
+// Raw tile: 128 rows x 32 bytes (no swizzle); half h reads 16 bytes = 32 elements.
+__device__ __forceinline__ void xform_mxfp4(const uint8_t *raw, uint8_t *atile, int r, int h, int grow, int k0,
                                             const GemmParams &p) {
-    uint8_t *arow = arow_tile + r * 128;
+    uint8_t *arow = atile + r * 128;
     const uint8_t *srow = p.scales_u8 + (long long)grow * (p.k / 32);
+    const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    const int blk = (k0 >> 5) + h;
+    const float s = (blk * 32 < p.k) ? e8m0_scale(__ldg(srow + blk)) : 0.0f;
 #pragma unroll
-    for (int c = 0; c < 2; c++) {  // 2 x 16 raw bytes = 64 elements
-        uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + c * 16);
-        uint32_t words[4] = {q.x, q.y, q.z, q.w};
-        const int blk = (k0 >> 5) + c;
-        float s = (blk * 32 < p.k) ? e8m0_scale(__ldg(srow + blk)) : 0.0f;
-#pragma unroll
-        for (int h = 0; h < 4; h++) {  // one word = 8 elements = one output chunk
-            const int j = 4 * c + h;
-            uint32_t w = words[h];
-            uint4 o;
-            uint32_t *op = &o.x;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                uint32_t byte = (w >> (8 * e)) & 0xff;
-                op[e] = pack_bf16x2(kE2M1[byte & 0xf] * s, kE2M1[byte >> 4] * s);
-            }
-            *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
-        }
+    for (int jj = 0; jj < 4; jj++) {  // one word = 8 elements = one output chunk
+        const int j = 4 * h + jj;
+        const uint32_t w = words[jj];
+        uint4 o;
+        o.x = scale_pack(e2m1x2_f32(w & 0xff), s);
+        o.y = scale_pack(e2m1x2_f32((w >> 8) & 0xff), s);
+        o.z = scale_pack(e2m1x2_f32((w >> 16) & 0xff), s);
+        o.w = scale_pack(e2m1x2_f32(w >> 24), s);
+        *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
     }
 }
 
-// INT4 pack-quantized, contiguous groups: bf16(f32(q - zp) * scale[row][g]).
-__device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *arow_tile, int r, int grow, int k0,
+// INT4 pack-quantized, contiguous groups (a multiple of 64):
+// bf16(f32(q - zp) * scale[row][g]).
+__device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *atile, int r, int h, int grow, int k0,
                                            const GemmParams &p) {
-    uint8_t *arow = arow_tile + r * 128;
+    uint8_t *arow = atile + r * 128;
     const int groups = p.scale_cols;
-    const int g = k0 / p.blk_cols;  // a 64-wide k-tile lies in one group (group % 64 == 0)
-    float s = (k0 < p.k) ? __ldg(p.scales + (long long)grow * groups + g) : 0.0f;
+    const int g = k0 / p.blk_cols;
+    const float s = (k0 < p.k) ? __ldg(p.scales + (long long)grow * groups + g) : 0.0f;
     int zq = 8;
     if (p.zeros) {
-        uint32_t zw = __ldg(p.zeros + (long long)(grow >> 3) * groups + g);
+        const uint32_t zw = __ldg(p.zeros + (long long)(grow >> 3) * groups + g);
         zq = (zw >> ((grow & 7) * 4)) & 0xf;
     }
+    const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
-        uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + c * 16);
-        uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    for (int jj = 0; jj < 4; jj++) {
+        const int j = 4 * h + jj;
+        const uint32_t w = words[jj];
+        uint32_t o[4];
 #pragma unroll
-        for (int h = 0; h < 4; h++) {
-            const int j = 4 * c + h;
-            uint32_t w = words[h];
-            uint4 o;
-            uint32_t *op = &o.x;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                int lo = (int)((w >> (8 * e)) & 0xf) - zq;
-                int hi = (int)((w >> (8 * e + 4)) & 0xf) - zq;
-                op[e] = pack_bf16x2((float)lo * s, (float)hi * s);
-            }
-            *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
+        for (int e = 0; e < 4; e++) {
+            const int lo = (int)((w >> (8 * e)) & 0xf) - zq;
+            const int hi = (int)((w >> (8 * e + 4)) & 0xf) - zq;
+            o[e] = scale_pack(make_float2((float)lo, (float)hi), s);
         }
+        *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
 
@@ -250,7 +268,10 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         for (int s = 0; s < C::kStages; s++) {
             mbar_init(&L.full[s], 1 + (C::kQuant ? kXformWarps : 0));
             mbar_init(&L.empty[s], 1);
+        }
+        for (int s = 0; s < C::kRawStages; s++) {
             mbar_init(&L.rawfull[s], 1);
+            mbar_init(&L.rawempty[s], kXformWarps);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&L.tfull[b], 1);
@@ -288,10 +309,13 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                     const uint32_t ph = (it / C::kStages) & 1;
                     if (!mbar_wait(&L.empty[s], ph ^ 1, abort, p.status)) break;
                     if (C::kQuant) {
-                        mbar_arrive_expect_tx(&L.rawfull[s], C::kNA * C::kRawBytes);
+                        const int rs = it % C::kRawStages;
+                        const uint32_t rph = (it / C::kRawStages) & 1;
+                        if (!mbar_wait(&L.rawempty[rs], rph ^ 1, abort, p.status)) break;
+                        mbar_arrive_expect_tx(&L.rawfull[rs], C::kRawStageBytes);
                         const int xb = kt * (FMT == kFmtFp8 ? BK : BK / 2);  // raw bytes along K
-                        tma_load_2d(&tmA, &L.rawfull[s], L.raw(s, 0), xb, arow);
-                        if (DUAL) tma_load_2d(&tmA2, &L.rawfull[s], L.raw(s, 1), xb, arow + p.a2_row_offset);
+                        tma_load_2d(&tmA, &L.rawfull[rs], L.raw(rs, 0), xb, arow);
+                        if (DUAL) tma_load_2d(&tmA2, &L.rawfull[rs], L.raw(rs, 1), xb, arow + p.a2_row_offset);
                         mbar_arrive_expect_tx(&L.full[s], C::kBBytes);
                     } else {
                         mbar_arrive_expect_tx(&L.full[s], C::kNA * C::kABytes + C::kBBytes);
@@ -309,14 +333,13 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
             int it = 0, local = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, local++) {
                 const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
-                const int kt0 = ti.kt0, kt1 = ti.kt1;
-                const int buf = local & 1;
-                const uint32_t use_ph = (local >> 1) & 1;
+                const int buf = local % C::kAccBufs;
+                const uint32_t use_ph = (local / C::kAccBufs) & 1;
                 if (!mbar_wait(&L.tempty[buf], use_ph ^ 1, abort, p.status)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + buf * C::kAccCols;
                 bool ok = true;
-                for (int kt = kt0; kt < kt1; kt++, it++) {
+                for (int kt = ti.kt0; kt < ti.kt1; kt++, it++) {
                     const int s = it % C::kStages;
                     const uint32_t ph = (it / C::kStages) & 1;
                     if (!mbar_wait(&L.full[s], ph, abort, p.status)) {
@@ -326,14 +349,12 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                     tc_fence_after();
                     const uint64_t adesc = sw128_kmajor_desc(smem_u32(L.a(s, 0)));
                     const uint64_t bdesc = sw128_kmajor_desc(smem_u32(L.b(s)));
+                    const uint64_t a2desc = DUAL ? sw128_kmajor_desc(smem_u32(L.a(s, 1))) : 0;
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++) {
-                        const uint32_t acc = (kt > kt0 || kk > 0) ? 1u : 0u;
+                        const uint32_t acc = (kt > ti.kt0 || kk > 0) ? 1u : 0u;
                         tc_mma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, acc);
-                        if (DUAL) {
-                            const uint64_t a2desc = sw128_kmajor_desc(smem_u32(L.a(s, 1)));
-                            tc_mma_bf16(d + BN, a2desc + 2 * kk, bdesc + 2 * kk, idesc, acc);
-                        }
+                        if (DUAL) tc_mma_bf16(d + BN, a2desc + 2 * kk, bdesc + 2 * kk, idesc, acc);
                     }
                     tc_commit(&L.empty[s]);
                 }
@@ -348,8 +369,8 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, local++) {
             const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
             const bool first_split = ti.first_split;  // bias and delta once per output
-            const int buf = local & 1;
-            const uint32_t use_ph = (local >> 1) & 1;
+            const int buf = local % C::kAccBufs;
+            const uint32_t use_ph = (local / C::kAccBufs) & 1;
             if (!mbar_wait(&L.tfull[buf], use_ph, abort, p.status)) break;
             tc_fence_after();
             const int n = ti.wt * BM + q * 32 + lane;  // weight row = output feature
@@ -363,14 +384,15 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
             }
             const float dbn = delta ? dbp[n] : 0.0f;
             const uint32_t tbase = tmem + buf * C::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+            const int m_end = ti.tok0 + ti.tok_cnt;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
+                if (ti.tok0 + c0 >= m_end) break;  // warp-uniform: no valid token left
                 float v[32];
                 tmem_ld32(tbase + c0, v);
                 float u[32];
                 if (DUAL) tmem_ld32(tbase + BN + c0, u);
                 const int m0 = ti.tok0 + c0;
-                const int m_end = ti.tok0 + ti.tok_cnt;
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
                     const int m = m0 + j;
@@ -380,9 +402,7 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                     r += bias;
                     const long long o = (long long)m * p.ldo + n;
                     if (DUAL) {
-                        float g = r;
-                        float up = u[j];
-                        reinterpret_cast<uint16_t *>(p.out)[o] = f32_to_bf16_bits(silu_f(g) * up);
+                        reinterpret_cast<uint16_t *>(p.out)[o] = f32_to_bf16_bits(silu_f(r) * u[j]);
                     } else if (p.flags & kEpiAtomic) {
                         atomicAdd(reinterpret_cast<float *>(p.out) + o, r);
                     } else if (p.flags & kEpiResidual) {
@@ -401,34 +421,37 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         }
     } else if (C::kQuant) {
         // ---------------- weight transform ----------------
-        const int r = threadIdx.x - (2 + kEpiWarps) * 32;  // 0..127: tile row
-        const int xw = warp - (2 + kEpiWarps);
+        const int t = threadIdx.x - (2 + kEpiWarps) * 32;  // 0..255
+        const int r = t & 127, h = t >> 7;
         int it = 0;
         for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
             const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
-            const int wt = ti.wt;
             bool ok = true;
             for (int kt = ti.kt0; kt < ti.kt1; kt++, it++) {
                 const int s = it % C::kStages;
-                const uint32_t ph = (it / C::kStages) & 1;
-                if (!mbar_wait(&L.rawfull[s], ph, abort, p.status)) {
+                const int rs = it % C::kRawStages;
+                const uint32_t rph = (it / C::kRawStages) & 1;
+                if (!mbar_wait(&L.rawfull[rs], rph, abort, p.status)) {
                     ok = false;
                     break;
                 }
 #pragma unroll
                 for (int i = 0; i < C::kNA; i++) {
-                    int grow = ti.a_row0 + wt * BM + r + (i ? p.a2_row_offset : 0);
-                    int vrow = min(grow, ti.a_row0 + (i ? p.a2_row_offset : 0) + p.m_w - 1);  // clamp side-data reads
-                    if (FMT == kFmtFp8) xform_fp8(L.raw(s, i), L.a(s, i), r, vrow, kt * BK, p);
-                    if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(s, i), L.a(s, i), r, vrow, kt * BK, p);
-                    if (FMT == kFmtInt4) xform_int4(L.raw(s, i), L.a(s, i), r, vrow, kt * BK, p);
+                    const int off = i ? p.a2_row_offset : 0;
+                    const int grow = ti.a_row0 + ti.wt * BM + r + off;
+                    const int vrow = min(grow, ti.a_row0 + off + p.m_w - 1);  // clamp side-data reads
+                    if (FMT == kFmtFp8) xform_fp8(L.raw(rs, i), L.a(s, i), r, h, vrow, kt * BK, p);
+                    if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(rs, i), L.a(s, i), r, h, vrow, kt * BK, p);
+                    if (FMT == kFmtInt4) xform_int4(L.raw(rs, i), L.a(s, i), r, h, vrow, kt * BK, p);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&L.full[s]);
+                if (lane == 0) {
+                    mbar_arrive(&L.rawempty[rs]);
+                    mbar_arrive(&L.full[s]);
+                }
             }
             if (!ok) break;
-            (void)xw;
         }
     }
 
@@ -460,16 +483,15 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// A 2D map over a row-major [rows][inner] tensor of `elem_bytes` elements.
-bool make_map(CUtensorMap *map, const void *ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
-              uint64_t rows, uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+// A 2D map over a row-major [rows][inner] tensor.
+bool make_map(CUtensorMap *map, const void *ptr, CUtensorMapDataType dt, uint64_t inner, uint64_t rows,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {inner, rows};
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t box[2] = {box_inner, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    (void)elem_bytes;
     CUresult r = fn(map, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -482,23 +504,22 @@ cudaError_t launch_t(const GemmOperand &a, const GemmOperand *a2, const GemmOper
     CUtensorMap ma, ma2, mb;
     bool ok;
     if (FMT == kFmtBf16) {
-        ok = make_map(&ma, a.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.cols, a.rows, a.row_bytes, BK, BM,
+        ok = make_map(&ma, a.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.cols, a.rows, a.row_bytes, BK, BM,
                       CU_TENSOR_MAP_SWIZZLE_128B);
         if (ok && DUAL)
-            ok = make_map(&ma2, a2->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a2->cols, a2->rows, a2->row_bytes, BK,
-                          BM, CU_TENSOR_MAP_SWIZZLE_128B);
+            ok = make_map(&ma2, a2->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a2->cols, a2->rows, a2->row_bytes, BK, BM,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
         const uint32_t raw_inner = FMT == kFmtFp8 ? BK : BK / 2;  // bytes per row per k-tile
         const CUtensorMapSwizzle sw = FMT == kFmtFp8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
-        ok = make_map(&ma, a.ptr, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.row_bytes, a.rows, a.row_bytes, raw_inner, BM,
-                      sw);
+        ok = make_map(&ma, a.ptr, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.row_bytes, a.rows, a.row_bytes, raw_inner, BM, sw);
         if (ok && DUAL)
-            ok = make_map(&ma2, a2->ptr, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a2->row_bytes, a2->rows, a2->row_bytes,
+            ok = make_map(&ma2, a2->ptr, CU_TENSOR_MAP_DATA_TYPE_UINT8, a2->row_bytes, a2->rows, a2->row_bytes,
                           raw_inner, BM, sw);
     }
     if (!DUAL) ma2 = ma;
     if (ok)
-        ok = make_map(&mb, b.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b.cols, b.rows, b.row_bytes, BK, BN,
+        ok = make_map(&mb, b.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b.cols, b.rows, b.row_bytes, BK, BN,
                       CU_TENSOR_MAP_SWIZZLE_128B);
     if (!ok) return cudaErrorInvalidValue;
     static bool attr_set = false;
@@ -536,15 +557,26 @@ cudaError_t dispatch_fmt(int fmt, const GemmOperand &a, const GemmOperand *a2, c
 
 }  // namespace
 
+// Token tile width: narrow tiles for small batches (decode-like calls stay
+// weight-bandwidth bound and need no padding to 256 tokens); quantised weights
+// take 256-token tiles in SwiGLU mode too, halving the decode work per MMA.
+int gemm_token_tile(int n_tok, bool dual, bool quant) {
+    if (n_tok <= 32) return 32;
+    if (n_tok <= 64) return 64;
+    if (n_tok <= 128) return 128;
+    return (dual && !quant) ? 128 : 256;
+}
+
 cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, const GemmOperand &b, GemmParams p,
                         int num_sms, cudaStream_t stream) {
     const bool dual = (p.flags & kEpiSwiglu) != 0;
     if (dual && !a2) return cudaErrorInvalidValue;
-    const int bn = p.bn ? p.bn : gemm_token_tile(p.n_tok, dual);
+    const int bn = p.bn ? p.bn : gemm_token_tile(p.n_tok, dual, fmt != kFmtBf16);
     if (dual) {
         if (bn == 32) return dispatch_fmt<32, true>(fmt, a, a2, b, p, num_sms, stream);
         if (bn == 64) return dispatch_fmt<64, true>(fmt, a, a2, b, p, num_sms, stream);
         if (bn == 128) return dispatch_fmt<128, true>(fmt, a, a2, b, p, num_sms, stream);
+        if (bn == 256 && fmt != kFmtBf16) return dispatch_fmt<256, true>(fmt, a, a2, b, p, num_sms, stream);
         return cudaErrorInvalidValue;
     }
     if (bn == 32) return dispatch_fmt<32, false>(fmt, a, a2, b, p, num_sms, stream);
@@ -552,15 +584,6 @@ cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, co
     if (bn == 128) return dispatch_fmt<128, false>(fmt, a, a2, b, p, num_sms, stream);
     if (bn == 256) return dispatch_fmt<256, false>(fmt, a, a2, b, p, num_sms, stream);
     return cudaErrorInvalidValue;
-}
-
-// Narrow token tiles for small batches (decode-like calls stay weight-
-// bandwidth bound and need no padding to 256 tokens).
-int gemm_token_tile(int n_tok, bool dual) {
-    if (n_tok <= 32) return 32;
-    if (n_tok <= 64) return 64;
-    if (dual || n_tok <= 128) return 128;
-    return 256;
 }
 
 }  // namespace ditch

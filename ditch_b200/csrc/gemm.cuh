@@ -73,8 +73,9 @@ struct GemmParams {
     int bn;               // token tile (32, 64, 128, 256); 0 = chosen from n_tok
 };
 
-// Token tile width the GEMM uses for n_tok tokens (dual = SwiGLU mode).
-int gemm_token_tile(int n_tok, bool dual);
+// Token tile width the GEMM uses for n_tok tokens (dual = SwiGLU mode,
+// quant = a weight format decoded inside the GEMM).
+int gemm_token_tile(int n_tok, bool dual, bool quant);
 
 // Host side: launches one GEMM on `stream`. Returns a CUDA error code.
 struct GemmOperand {

@@ -229,14 +229,32 @@ int build_mat(ditch_cuda_model *m, const std::vector<Seg> &segs, int slabs, Mat 
             r += t->rows;
         }
     } else {
+        // bf16 rows, zero-padded to a multiple of 8 columns (TMA row strides
+        // are multiples of 16 bytes); the padding multiplies zero activations.
+        const size_t kp = (cols + 7) / 8 * 8;
         out.fmt = kFmtBf16;
-        out.row_bytes = (long long)cols * 2;
-        REQUIRE(cols % 8 == 0, "%s: width %zu is not a multiple of 8", what, cols);
-        DITCH_CUDA(out.data.reserve(rows * cols * 2));
+        out.cols = (int)kp;
+        out.row_bytes = (long long)kp * 2;
+        DITCH_CUDA(out.data.reserve(rows * kp * 2));
+        DevBuf tmp;
+        if (kp != cols) {
+            DITCH_CUDA(cudaMemsetAsync(out.data.ptr, 0, rows * kp * 2, dev->stream));
+            size_t mx = 0;
+            for (const Seg &s : segs) mx = std::max(mx, s.t->rows);
+            DITCH_CUDA(tmp.reserve(mx * cols * 2));
+        }
         size_t r = 0;
         for (const Seg &s : segs) {
-            int st = decode_seg_bf16(m, s, out.data.as<uint16_t>() + r * cols);
-            if (st) return st;
+            if (kp == cols) {
+                int st = decode_seg_bf16(m, s, out.data.as<uint16_t>() + r * cols);
+                if (st) return st;
+            } else {
+                int st = decode_seg_bf16(m, s, tmp.as<uint16_t>());
+                if (st) return st;
+                DITCH_CUDA(cudaMemcpy2DAsync(out.data.as<uint16_t>() + r * kp, kp * 2, tmp.ptr, cols * 2, cols * 2,
+                                             s.t->rows, cudaMemcpyDeviceToDevice, dev->stream));
+                DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+            }
             r += s.t->rows;
         }
     }
@@ -318,6 +336,7 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
     REQUIRE(cfg->heads % cfg->kv_heads == 0, "heads must be a multiple of kv heads");
     REQUIRE(cfg->head_dim % 2 == 0, "head_dim must be even");
     REQUIRE(cfg->hidden % 8 == 0, "hidden must be a multiple of 8");
+    REQUIRE((cfg->heads * cfg->head_dim) % 8 == 0, "heads * head_dim must be a multiple of 8");
     std::unique_ptr<ditch_cuda_model> m(new ditch_cuda_model());
     m->dev = dev;
     Config &c = m->cfg;
@@ -448,7 +467,7 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
             if ((st = build_mat(m.get(), gu, E, L.e_gate_up, "e_gate_up"))) return st;
             if ((st = build_mat(m.get(), dn, E, L.e_down, "e_down"))) return st;
             L.e_edit.assign(E, 0);
-            DITCH_CUDA(L.e_a.reserve((size_t)E * mi * 4));
+            DITCH_CUDA(L.e_a.reserve((size_t)E * L.e_down.cols * 4));
             DITCH_CUDA(L.e_b.reserve((size_t)E * H * 4));
             DITCH_CUDA(L.e_edit_dev.reserve((size_t)E * 4));
             DITCH_CUDA(cudaMemset(L.e_edit_dev.ptr, 0, (size_t)E * 4));
@@ -460,7 +479,7 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
                     "layer %d: MLP shapes", i);
             if ((st = build_mat(m.get(), {Seg{g, 0}, Seg{u, 0}}, 1, L.gate_up, "gate_up"))) return st;
             if ((st = build_mat(m.get(), {Seg{d, 0}}, 1, L.down, "down"))) return st;
-            DITCH_CUDA(L.down_a.reserve((size_t)c.inter * 4));
+            DITCH_CUDA(L.down_a.reserve((size_t)L.down.cols * 4));
             DITCH_CUDA(L.down_b.reserve((size_t)H * 4));
         }
         DITCH_CUDA(L.o_a.reserve((size_t)qd * 4));

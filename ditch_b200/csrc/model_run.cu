@@ -105,7 +105,7 @@ namespace ditch {
 int ensure_workspace(ditch_cuda_model *m, int n, int nc, int nl) {
     const Config &c = m->cfg;
     const size_t N = (size_t)std::max(n, 1), H = c.hidden;
-    const size_t inter = std::max(c.inter, 1);
+    const size_t inter = (std::max(c.inter, 1) + 7) / 8 * 8;
     DITCH_CUDA(m->x.reserve(N * H * 4));
     DITCH_CUDA(m->h.reserve(N * H * 2));
     DITCH_CUDA(m->qkv.reserve(N * c.qkv_width() * 4));
@@ -253,11 +253,12 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
             if ((s = moe_mlp(m, L, li, n))) return s;
         } else {
             DITCH_LAUNCH(dev, rmsnorm_rows_bf16(x, L.post_norm.as<float>(), n, H, c.eps, h, nullptr, nullptr, nullptr, st));
-            const int I = c.inter;
-            if ((s = gemm_weight(m, L.gate_up, 0, I, h, n, m->act.ptr, I, kEpiSwiglu, nullptr, nullptr, nullptr, I)))
+            const int I = c.inter, Ip = L.down.cols;  // Ip: the stored (8-aligned) width
+            if (Ip != I) DITCH_CUDA(cudaMemsetAsync(m->act.ptr, 0, (size_t)n * Ip * 2, st));
+            if ((s = gemm_weight(m, L.gate_up, 0, I, h, n, m->act.ptr, Ip, kEpiSwiglu, nullptr, nullptr, nullptr, I)))
                 return s;
             if (L.down_edit)
-                DITCH_LAUNCH(dev, rowdot_bf16(m->act.as<uint16_t>(), L.down_a.as<float>(), n, I, m->xa.as<float>(), st));
+                DITCH_LAUNCH(dev, rowdot_bf16(m->act.as<uint16_t>(), L.down_a.as<float>(), n, Ip, m->xa.as<float>(), st));
             if ((s = gemm_weight(m, L.down, 0, H, m->act.as<uint16_t>(), n, x, H, kEpiResidual, nullptr,
                                  L.down_edit ? m->xa.as<float>() : nullptr, L.down_edit ? L.down_b.as<float>() : nullptr,
                                  0)))
@@ -302,7 +303,7 @@ int apply_component_edit(ditch_cuda_model *m, int li, bool is_o, const float *v,
 int apply_expert_delta(ditch_cuda_model *m, int li, int e, const float *v, float lambda) {
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
-    const int H = m->cfg.hidden, mi = m->cfg.moe_inter;
+    const int H = m->cfg.hidden, mi = L.e_down.cols;  // the stored (8-aligned) width
     int s;
     if ((s = gemv_t_mat(m, L.e_down, e * H, H, v, L.e_a.as<float>() + (size_t)e * mi))) return s;
     DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.e_b.as<float>() + (size_t)e * H, dev->stream));
@@ -346,7 +347,7 @@ int prepare_direction(ditch_cuda_model *m, float di, bool use_di) {
 int expert_scores(ditch_cuda_model *m, int li, const float *v, std::vector<float> &scores) {
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
-    const int E = m->cfg.n_experts, H = m->cfg.hidden, mi = m->cfg.moe_inter;
+    const int E = m->cfg.n_experts, H = m->cfg.hidden, mi = L.e_down.cols;  // the stored (8-aligned) width
     DevBuf proj, norms;
     DITCH_CUDA(proj.reserve((size_t)E * mi * 4));
     DITCH_CUDA(norms.reserve((size_t)E * H * 4));

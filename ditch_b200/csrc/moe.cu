@@ -271,10 +271,11 @@ __global__ void k_combine(const float *eo, const int *sel, const float *wts, con
     }
 }
 
-int tile_for(int avg, bool dual) {
+// Token tile of a grouped GEMM from the mean rows per expert.
+int tile_for(int avg, bool dual, bool quant) {
     if (avg <= 32) return 32;
     if (avg <= 64) return 64;
-    if (dual || avg <= 160) return 128;
+    if ((dual && !quant) || avg <= 160) return 128;
     return 256;
 }
 
@@ -305,9 +306,11 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
         return DITCH_CUDA_UNSUPPORTED;
     }
     const int nk = n * k;
+    const int mip = L.e_down.cols;  // stored (8-aligned) expert width: the act row stride
     const int cp = (H + 63) / 64 * 64;
     const int avg = (nk + E - 1) / E;
-    const int bn_gu = tile_for(avg, true), bn_d = tile_for(avg, false);
+    const int bn_gu = tile_for(avg, true, L.e_gate_up.fmt != kFmtBf16);
+    const int bn_d = tile_for(avg, false, L.e_down.fmt != kFmtBf16);
     const int wt_gu = (mi + 127) / 128, wt_d = (H + 127) / 128;
     const int max_gu = (nk / bn_gu + E) * wt_gu, max_d = (nk / bn_d + E) * wt_d;
     DITCH_CUDA(m->moe_h3.reserve((size_t)n * 3 * cp * 2));
@@ -321,7 +324,7 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     DITCH_CUDA(m->moe_pexp.reserve((size_t)nk * 4));
     DITCH_CUDA(m->moe_slot.reserve((size_t)nk * 4));
     DITCH_CUDA(m->moe_xg.reserve((size_t)nk * H * 2));
-    DITCH_CUDA(m->moe_act.reserve((size_t)nk * mi * 2));
+    DITCH_CUDA(m->moe_act.reserve((size_t)nk * mip * 2));
     DITCH_CUDA(m->moe_eo.reserve((size_t)nk * H * 4));
     DITCH_CUDA(m->moe_xa.reserve((size_t)nk * 4));
     DITCH_CUDA(m->moe_sched_gu.reserve((size_t)max_gu * 16));
@@ -357,14 +360,15 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     gu.n_sched = n_gu;
     gu.slab_rows = 2 * mi;
     gu.bn = bn_gu;
-    if ((s = gemm_mat(dev, L.e_gate_up, 0, mi, m->moe_xg.as<uint16_t>(), nk, m->moe_act.ptr, mi, kEpiSwiglu, nullptr,
+    if (mip != mi) DITCH_CUDA(cudaMemsetAsync(m->moe_act.ptr, 0, (size_t)nk * mip * 2, st));
+    if ((s = gemm_mat(dev, L.e_gate_up, 0, mi, m->moe_xg.as<uint16_t>(), nk, m->moe_act.ptr, mip, kEpiSwiglu, nullptr,
                       nullptr, nullptr, mi, &gu)))
         return s;
     bool any_edit = false;
     for (uint8_t f : L.e_edit) any_edit |= f != 0;
     if (any_edit) {
         k_rowdot_grouped<<<(nk + 7) / 8, 256, 0, st>>>(m->moe_act.as<uint16_t>(), L.e_a.as<float>(),
-                                                       m->moe_pexp.as<int>(), L.e_edit_dev.as<int>(), nk, mi,
+                                                       m->moe_pexp.as<int>(), L.e_edit_dev.as<int>(), nk, mip,
                                                        m->moe_xa.as<float>());
         DITCH_LAUNCH(dev, cudaGetLastError());
     }
