@@ -110,6 +110,7 @@ SIGNATURES = {
     "ditch_cuda_kl_score": (C.c_int, [vp, f64p]),
     "ditch_cuda_kl_score_prompts": (C.c_int, [vp, u32p, C.POINTER(sz), sz, f64p]),
     "ditch_cuda_edit_weight_bf16": (C.c_int, [vp, vp, sz, sz, vp, C.c_float]),
+    "ditch_cuda_edit_weight_bf16_noalloc": (C.c_int, [vp, sz, sz, vp, C.c_float, vp]),
     "ditch_cuda_weight_load": (C.c_int, [vp, C.POINTER(TensorDesc), C.POINTER(vp)]),
     "ditch_cuda_weight_free": (None, [vp]),
     "ditch_cuda_weight_format": (C.c_int, [vp]),

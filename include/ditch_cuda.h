@@ -243,6 +243,24 @@ int ditch_cuda_kl_score_prompts(ditch_cuda_model *m, const uint32_t *tokens, con
 int ditch_cuda_edit_weight_bf16(ditch_cuda_device *dev, void *w, size_t rows, size_t cols, const float *r,
                                 float alpha);
 
+/* The same edit for callers that cannot allocate device memory: a host
+ * whose own pool owns HBM, code that must not synchronise the device (as
+ * cudaMalloc / cudaFree can), or a caller without a ditch_cuda_device handle.
+ * No counterpart in the reference: ditch's CPU engine has no device memory.
+ *
+ * The scratch (a = r^T W and b = -alpha r) is a fixed 512 KiB array inside
+ * the library, held by every GPU that loads it until the process exits; the
+ * call itself allocates nothing. Limit: rows <= 65536 and cols <= 65536
+ * (larger sizes return DITCH_CUDA_INVALID). w and r are device pointers of
+ * the current device; the work is queued on `stream` (a cudaStream_t, NULL
+ * for the default stream) and the call returns without waiting. The first
+ * call on a device looks the array's device address up (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture.
+ * All calls share the array and it keeps the last call's contents (the call
+ * clears what must start at zero), so calls that overlap on the GPU race. */
+int ditch_cuda_edit_weight_bf16_noalloc(void *w, size_t rows, size_t cols, const float *r, float alpha,
+                                        void *stream);
+
 /* ---- one resident weight and its dequant-fused GEMM ----
  * The product behind `matmulT` (src/tensor.zig:1023-1045) for one weight
  * kept in HBM in its stored format: FP8 blocks, MXFP4 and INT4 groups of 64k
