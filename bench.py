@@ -49,6 +49,13 @@ def parse():
     ap.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline sample budget (seconds)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c5", "gemm"],
+                    help="c2 (default): the trial loop; c1: Qwen2-0.5B-style fp32 pipeline with oracle parity; "
+                         "c3: dequant + GEMM sweep; c5: Llama-3-70B-shaped in-place edit sweep; gemm: one GEMM")
+    ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
+    ap.add_argument("--rows", type=int, default=4096)
+    ap.add_argument("--cols", type=int, default=4096)
+    ap.add_argument("--m", type=int, default=8192)
     return ap.parse_args()
 
 
@@ -312,6 +319,10 @@ def traffic_from_profiles():
 
 def main():
     args = parse()
+    if args.config != "c2":
+        import bench_configs
+
+        return bench_configs.run(args)
     world, rank, local, dist = dist_setup(args.gpus)
     if args.impl == "reference":
         if rank == 0:

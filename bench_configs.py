@@ -1,0 +1,296 @@
+"""The other BASELINE configurations of `bench.py` (`--config ...`).
+
+* `gemm`: one resident-weight GEMM (a profiling target): `--fmt`, `--rows`, `--cols`, `--m`.
+* `c3`: the standalone dequant + GEMM sweep of BASELINE config 3. Weights of
+  [4096 x 4096], [14336 x 4096] and [4096 x 14336] are stored as GGUF Q8_0,
+  GGUF Q4_K, INT4 (group 128, packed zero points) and MXFP4, with bf16
+  activations for M in {1, 16, 128, 1024, 8192}. The sweep reports TFLOP/s
+  (M >= 128) or weight-stream GB/s (M < 128) per case.
+* `c5`: the in-place rank-1 edit W <- W - alpha_l r_l (r_l^T W) on all 80
+  o_proj [8192 x 8192] and down_proj [8192 x 28672] bf16 matrices of a
+  Llama-3-70B shape. It reports HBM GB/s over the algorithmic 3 x 48.32 GB.
+* `c1`: the Qwen2-0.5B-style fp32 pipeline of BASELINE config 1, timed end to
+  end: capture of two 64 x 48 batches, directions, then per trial the edit,
+  the forward and the KL. The CPU baseline is the oracle on the same workload.
+
+All weights are seeded synthetic N(0, 0.02), generated and quantised on the
+GPU with torch (device-memory plumbing; the kernels under test are the
+library's).
+"""
+import json
+import math
+import os
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---- quantisers on the GPU (synthetic data; formats as ditch stores them) ----
+def q8_0_blocks(w):
+    """GGUF Q8_0 (src/quant.zig:245-255): per 32: d = amax / 127 (f16), q = round(x / d)."""
+    import torch
+
+    rows, cols = w.shape
+    x = w.float().view(rows, cols // 32, 32)
+    d = x.abs().amax(-1) / 127.0
+    inv = torch.where(d != 0, 1.0 / d, torch.zeros_like(d))
+    q = torch.round(x * inv[..., None]).clamp(-127, 127).to(torch.int8)
+    d16 = d.half().view(torch.uint8).view(rows, cols // 32, 2)
+    return torch.cat([d16, q.view(torch.uint8)], -1).reshape(rows, cols // 32 * 34).contiguous()
+
+
+def q4_k_blocks(w):
+    """A valid GGUF Q4_K encoding (d, dmin, 6-bit sub-scales / mins, nibbles)."""
+    import torch
+
+    rows, cols = w.shape
+    nb = cols // 256
+    x = w.float().view(rows, nb, 8, 32)
+    lo = x.amin(-1).clamp(max=0)
+    hi = x.amax(-1).clamp(min=0)
+    sc, mn = (hi - lo) / 15.0, -lo
+    d = (sc.amax(-1) / 63.0).half()
+    dmin = (mn.amax(-1) / 63.0).half()
+    df, dmf = d.float()[..., None], dmin.float()[..., None]
+    ls = torch.where(df > 0, torch.round(sc / df), torch.zeros_like(sc)).clamp(0, 63).to(torch.int32)
+    lm = torch.where(dmf > 0, torch.round(mn / dmf), torch.zeros_like(mn)).clamp(0, 63).to(torch.int32)
+    ds, ms = (df * ls)[..., None], (dmf * lm)[..., None]
+    q = torch.where(ds > 0, torch.round((x + ms) / ds), torch.zeros_like(x)).clamp(0, 15).to(torch.int32)
+    s12 = torch.zeros(rows, nb, 12, dtype=torch.int32, device=w.device)
+    for j in range(4):  # get_scale_min_k4 layout (src/quant.zig:140-146)
+        s12[..., j] = ls[..., j] | ((ls[..., j + 4] >> 4) << 6)
+        s12[..., j + 4] = lm[..., j] | ((lm[..., j + 4] >> 4) << 6)
+        s12[..., j + 8] = (ls[..., j + 4] & 0xF) | ((lm[..., j + 4] & 0xF) << 4)
+    nib = (q[:, :, 0::2, :] | (q[:, :, 1::2, :] << 4)).reshape(rows, nb, 128)
+    head = torch.cat([d.view(torch.uint8).view(rows, nb, 2), dmin.view(torch.uint8).view(rows, nb, 2)], -1)
+    out = torch.cat([head, s12.to(torch.uint8), nib.to(torch.uint8)], -1)
+    return out.reshape(rows, nb * 144).contiguous()
+
+
+def int4_packed(w, group=128):
+    """compressed-tensors pack-quantized INT4, asymmetric (tools/make_fixture.py:156-194 rule)."""
+    import torch
+
+    rows, cols = w.shape
+    g = cols // group
+    x = w.float().view(rows, g, group)
+    mn = x.amin(-1).clamp(max=0)
+    mx = x.amax(-1).clamp(min=0)
+    scale = ((mx - mn).clamp(min=1e-8) / 15.0).to(torch.bfloat16).float()
+    zp = torch.round(-8 - mn / scale).clamp(-8, 7)
+    q = (torch.round(x / scale[..., None]) + zp[..., None]).clamp(-8, 7).to(torch.int64) + 8
+    q = q.view(rows, cols // 8, 8)
+    words = torch.zeros(rows, cols // 8, dtype=torch.int64, device=w.device)
+    for i in range(8):
+        words |= q[..., i] << (4 * i)
+    z = (zp.to(torch.int64) + 8).view(rows // 8, 8, g)
+    zw = torch.zeros(rows // 8, g, dtype=torch.int64, device=w.device)
+    for i in range(8):
+        zw |= z[:, i, :] << (4 * i)
+    as_u32 = lambda t: t.to(torch.int64).bitwise_and(0xFFFFFFFF).to(torch.int32)  # noqa: E731
+    return as_u32(words).contiguous(), scale.contiguous(), as_u32(zw).contiguous()
+
+
+E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+
+
+def mxfp4_packed(w):
+    """MXFP4, natural layout (tools/make_fixture.py:210-224): e = floor(log2(amax / 6))."""
+    import torch
+
+    rows, cols = w.shape
+    x = w.float().view(rows, cols // 32, 32)
+    amax = x.abs().amax(-1)
+    e = torch.where(amax > 0, torch.floor(torch.log2(amax.clamp(min=1e-30) / 6.0)), torch.zeros_like(amax))
+    e = e.clamp(-127, 127)
+    y = (x / torch.exp2(e)[..., None]).clamp(-6, 6)
+    grid = torch.tensor(E2M1, device=w.device)
+    mag = (y.abs()[..., None] - grid).abs().argmin(-1)
+    code = (mag | ((y < 0).to(torch.int64) << 3)).to(torch.uint8)
+    packed = (code[..., 0::2] | (code[..., 1::2] << 4)).reshape(rows, cols // 2).contiguous()
+    return packed, (e + 127).to(torch.uint8).contiguous()
+
+
+def make_weight(dev, fmt, rows, cols, gen):
+    import torch
+
+    from ditch_b200 import Tensor, Weight
+    from ditch_b200.cuda import SCALE_F32
+
+    w = (torch.randn(rows, cols, generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+    if fmt == "bf16":
+        t = Tensor("w", "bf16", rows, cols, w)
+        wbytes = rows * cols * 2
+    elif fmt == "fp8":
+        from bench import fp8_block_quant
+
+        codes, sc = fp8_block_quant(w)
+        t = Tensor("w", "fp8", rows, cols, codes, scales=sc, block_rows=128, block_cols=128)
+        wbytes = rows * cols + sc.numel() * 4
+    elif fmt == "q8_0":
+        raw = q8_0_blocks(w)
+        t = Tensor("w", "q8_0", rows, cols, raw)
+        wbytes = raw.numel()
+    elif fmt == "q4_k":
+        raw = q4_k_blocks(w)
+        t = Tensor("w", "q4_k", rows, cols, raw)
+        wbytes = raw.numel()
+    elif fmt == "int4":
+        words, scale, zeros = int4_packed(w)
+        t = Tensor("w", "int", rows, cols, words, scales=scale, scales_dtype=SCALE_F32, zeros=zeros, block_cols=128,
+                   bits=4)
+        wbytes = words.numel() * 4 + scale.numel() * 2 + zeros.numel() * 4  # scales bf16 on disk
+    elif fmt == "mxfp4":
+        packed, scales = mxfp4_packed(w)
+        t = Tensor("w", "mxfp4", rows, cols, packed, scales=scales)
+        wbytes = packed.numel() + scales.numel()
+    else:
+        raise ValueError(fmt)
+    W = Weight(dev, t)
+    del w, t
+    return W, wbytes
+
+
+def time_gemm(dev, W, m, cols, rows, steps, warmup, k_splits=1):
+    import torch
+
+    x = torch.randn(m, cols, device="cuda").to(torch.bfloat16)
+    out = torch.empty(m, rows, device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    for _ in range(warmup):
+        W.gemm(x.data_ptr(), m, out.data_ptr(), k_splits)
+    dev.synchronize()
+    dev.timer_start()
+    for _ in range(steps):
+        W.gemm(x.data_ptr(), m, out.data_ptr(), k_splits)
+    ms = dev.timer_stop() / steps
+    return ms, x, out
+
+
+def run_gemm(args, dev):
+    import torch
+
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    W, wbytes = make_weight(dev, args.fmt, args.rows, args.cols, gen)
+    ms, _, _ = time_gemm(dev, W, args.m, args.cols, args.rows, args.steps, args.warmup)
+    hbm, tf, src = _peaks()
+    tflops = 2.0 * args.m * args.rows * args.cols / ms / 1e9
+    print(json.dumps({"config": "gemm", "fmt": args.fmt, "gemm_format": W.format(), "rows": args.rows,
+                      "cols": args.cols, "m": args.m, "ms": round(ms, 4), "tflops": round(tflops, 1),
+                      "frac_of_burst_bf16": round(tflops / tf, 4), "peak_source": src}), flush=True)
+    W.close()
+
+
+def run_c3(args, dev):
+    import torch
+
+    hbm, tf, src = _peaks()
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    results = []
+    for fmt in ("q8_0", "q4_k", "int4", "mxfp4"):
+        for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336)):
+            W, wbytes = make_weight(dev, fmt, rows, cols, gen)
+            for m in (1, 16, 128, 1024, 8192):
+                tiles = -(-rows // 128) * -(-m // (32 if m <= 32 else 64 if m <= 64 else 128 if m <= 128 else 256))
+                ks = max(1, min(cols // 64, (2 * 148) // max(tiles, 1))) if m < 128 else 1
+                ms, _, _ = time_gemm(dev, W, m, cols, rows, args.steps, args.warmup, ks)
+                flops = 2.0 * m * rows * cols
+                bytes_ = wbytes + 2 * m * cols + 4 * m * rows
+                r = {"fmt": fmt, "gemm_format": W.format(), "shape": [rows, cols], "m": m, "ms": round(ms, 4),
+                     "tflops": round(flops / ms / 1e9, 2), "gbs": round(bytes_ / ms / 1e6, 1), "k_splits": ks,
+                     "bound": "hbm" if m < 128 else "tensor"}
+                r["frac"] = round(r["gbs"] / hbm if m < 128 else r["tflops"] / tf, 4)
+                results.append(r)
+                print(json.dumps(r), flush=True)
+            W.close()
+            torch.cuda.empty_cache()
+    print(json.dumps({"config": "c3", "cases": len(results), "peak_source": src, "hbm_gbs": hbm,
+                      "bf16_tflops_burst": tf}), flush=True)
+
+
+def run_c5(args, dev):
+    """In-place edit of 80 o_proj + 80 down_proj bf16 matrices (48.3 GB)."""
+    import torch
+
+    import ditch_b200
+
+    hbm, tf, src = _peaks()
+    L, H, I = args.layers if args.layers != 32 else 80, 8192, 28672
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    mats = []
+    for _ in range(L):
+        for rows, cols in ((H, H), (H, I)):
+            w = torch.empty(rows, cols, dtype=torch.bfloat16, device="cuda")
+            w.normal_(0.0, 0.02, generator=gen)
+            mats.append(w)
+    rs = torch.randn(L, H, generator=gen, device="cuda")
+    rs = (rs / rs.norm(dim=1, keepdim=True)).contiguous()
+    rng = np.random.default_rng(args.seed)
+    p = (float(rng.uniform(0.8, 1.5)), float(rng.uniform(0.6 * (L - 1), L - 1)), 0.0, float(rng.uniform(1, 0.6 * L)))
+    p = (p[0], p[1], float(rng.uniform(0, 1)) * p[0], p[3])
+
+    def kernel_weight(layer):
+        dist = abs(float(layer) - p[1])
+        if dist > p[3]:
+            return 0.0
+        return p[0] + (dist / p[3]) * (p[2] - p[0])
+
+    alphas = [kernel_weight(l) for l in range(L)]
+    lib = ditch_b200.lib()
+    stream = torch.cuda.current_stream()
+
+    def sweep():
+        for l in range(L):
+            for k in range(2):
+                w = mats[2 * l + k]
+                st = lib.ditch_cuda_edit_weight_bf16_noalloc(w.data_ptr(), w.shape[0], w.shape[1],
+                                                             rs[l].data_ptr(), alphas[l], stream.cuda_stream)
+                if st != 0:
+                    raise RuntimeError(lib.ditch_cuda_last_error())
+
+    for _ in range(args.warmup):
+        sweep()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        sweep()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    elems = sum(w.numel() for w in mats)
+    algo = 3 * 2 * elems
+    print(json.dumps({"config": "c5", "metric": "edit-kernel HBM GB/s", "layers": L, "elements": elems,
+                      "algorithmic_bytes": algo, "ms_per_edit": round(ms, 3), "gbs": round(algo / ms / 1e6, 1),
+                      "frac": round(algo / ms / 1e6 / hbm, 4), "peak": hbm, "peak_source": src,
+                      "note": "all 80 o_proj + down_proj edited per step (GEMV-T read + rank-1 read/write)"}),
+          flush=True)
+
+
+def run(args):
+    import torch
+
+    import ditch_b200
+
+    torch.cuda.set_device(0)
+    dev = ditch_b200.Device(0)
+    if args.config == "gemm":
+        run_gemm(args, dev)
+    elif args.config == "c3":
+        run_c3(args, dev)
+    elif args.config == "c5":
+        run_c5(args, dev)
+    else:
+        raise SystemExit(f"config {args.config} is not implemented")
+    dev.close()
+    return 0

@@ -223,6 +223,181 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnParams p) {
     }
 }
 
+// ---- register-tiled attention for head_dim 64 / 128 ----------------------
+// Block = (prompt, q head, chunk of 64 query positions); 256 threads. Q (64
+// rows) and each 64-key chunk of K are staged transposed in f32 shared memory
+// after q/k norm and RoPE; V natural. Scores: thread (ty, tx) owns queries
+// 4ty..4ty+3 x keys 4tx..4tx+3 (two LDS.128 per 16 FMAs); the output: the
+// same 4 queries x HD/16 dimensions. Online softmax across key chunks, f32.
+constexpr int kQB = 64, kKB = 64;
+
+template <int HD>
+__global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
+    extern __shared__ float sm[];
+    float *qt = sm;                    // [HD][kQB]
+    float *kt = qt + HD * kQB;         // [HD][kKB]
+    float *vs = kt + HD * kKB;         // [kKB][HD]
+    float *pt = vs + kKB * HD;         // [kKB][kQB]; also the staging rows
+    float *row = pt;                   // [8 warps][HD] while staging Q / K
+    const int b = blockIdx.x, h = blockIdx.y, i0 = blockIdx.z * kQB;
+    const int start = p.seq_start[b], len = p.seq_len[b];
+    if (i0 >= len) return;
+    const int nh = p.heads, nkv = p.kv_heads, groups = nh / nkv, kvh = h / groups;
+    const int qd = nh * HD, kvd = nkv * HD, width = qd + 2 * kvd;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ty = tid >> 4, tx = tid & 15;
+    float *wrow = row + warp * HD;
+    constexpr int DPT = HD / 16;  // output dimensions per thread
+
+    // stage Q: rows i0 .. i0 + 63 of head h (zero beyond the prompt)
+    for (int r = warp; r < kQB; r += 8) {
+        const int i = i0 + r;
+        if (i < len) {
+            const float *src = p.qkv + (long long)(start + i) * width + h * HD;
+            for (int d = lane; d < HD; d += 32) wrow[d] = src[d];
+            __syncwarp();
+            if (p.q_norm) rms_inplace(wrow, HD, p.q_norm, p.eps, lane);
+            rope_neox_inplace(wrow, HD, i, p.rope_cos, p.rope_sin, lane);
+            __syncwarp();
+            for (int d = lane; d < HD; d += 32) qt[d * kQB + r] = wrow[d];
+        } else {
+            for (int d = lane; d < HD; d += 32) qt[d * kQB + r] = 0.0f;
+        }
+        __syncwarp();
+    }
+    float m[4], l[4], o[4][DPT];
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        m[a] = -INFINITY;
+        l[a] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < DPT; c++) o[a][c] = 0.0f;
+    }
+    const int last_q = min(len, i0 + kQB) - 1;  // causal: keys 0 .. last_q
+    for (int k0 = 0; k0 <= last_q; k0 += kKB) {
+        __syncthreads();
+        for (int r = warp; r < kKB; r += 8) {
+            const int j = k0 + r;
+            if (j < len) {
+                const float *src = p.qkv + (long long)(start + j) * width;
+                for (int d = lane; d < HD; d += 32) {
+                    wrow[d] = src[qd + kvh * HD + d];
+                    vs[r * HD + d] = src[qd + kvd + kvh * HD + d];
+                }
+                __syncwarp();
+                if (p.k_norm) rms_inplace(wrow, HD, p.k_norm, p.eps, lane);
+                rope_neox_inplace(wrow, HD, j, p.rope_cos, p.rope_sin, lane);
+                __syncwarp();
+                for (int d = lane; d < HD; d += 32) kt[d * kKB + r] = wrow[d];
+            } else {
+                for (int d = lane; d < HD; d += 32) {
+                    kt[d * kKB + r] = 0.0f;
+                    vs[r * HD + d] = 0.0f;
+                }
+            }
+            __syncwarp();
+        }
+        __syncthreads();
+        // scores of queries 4ty.. x keys 4tx..
+        float s[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) s[a][c] = 0.0f;
+#pragma unroll 8
+        for (int d = 0; d < HD; d++) {
+            const float4 qv = *reinterpret_cast<const float4 *>(qt + d * kQB + 4 * ty);
+            const float4 kv = *reinterpret_cast<const float4 *>(kt + d * kKB + 4 * tx);
+            const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+            for (int a = 0; a < 4; a++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) s[a][c] = fmaf(qa[a], ka[c], s[a][c]);
+        }
+        float corr[4];
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+            const int qi = i0 + 4 * ty + a;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int kj = k0 + 4 * tx + c;
+                s[a][c] = (kj <= qi && kj < len) ? s[a][c] * p.scale : -INFINITY;
+                mx = fmaxf(mx, s[a][c]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mnew = fmaxf(m[a], mx);
+            corr[a] = (m[a] == -INFINITY) ? 0.0f : expf(m[a] - mnew);
+            float sum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float e = (s[a][c] == -INFINITY) ? 0.0f : expf(s[a][c] - mnew);
+                s[a][c] = e;
+                sum += e;
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            l[a] = l[a] * corr[a] + sum;
+            m[a] = (mnew == -INFINITY) ? m[a] : mnew;
+        }
+        // P^T [key][query] for the value product
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+            *reinterpret_cast<float4 *>(pt + (4 * tx + c) * kQB + 4 * ty) = make_float4(s[0][c], s[1][c], s[2][c], s[3][c]);
+        __syncthreads();
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < DPT; c++) o[a][c] *= corr[a];
+        const int nk = min(kKB, last_q + 1 - k0);
+        for (int k = 0; k < nk; k++) {
+            const float4 pv = *reinterpret_cast<const float4 *>(pt + k * kQB + 4 * ty);
+            const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+            float vv[DPT];
+#pragma unroll
+            for (int c = 0; c < DPT; c += 4) {
+                const float4 t = *reinterpret_cast<const float4 *>(vs + k * HD + DPT * tx + c);
+                vv[c] = t.x;
+                vv[c + 1] = t.y;
+                vv[c + 2] = t.z;
+                vv[c + 3] = t.w;
+            }
+#pragma unroll
+            for (int a = 0; a < 4; a++)
+#pragma unroll
+                for (int c = 0; c < DPT; c++) o[a][c] = fmaf(pa[a], vv[c], o[a][c]);
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        const int qi = i0 + 4 * ty + a;
+        if (qi >= len) continue;
+        const float inv = 1.0f / l[a];
+        uint16_t *dst = p.out + (long long)(start + qi) * qd + h * HD + DPT * tx;
+#pragma unroll
+        for (int c = 0; c < DPT; c += 2)
+            *reinterpret_cast<uint32_t *>(dst + c) = pack_bf16x2(o[a][c] * inv, o[a][c + 1] * inv);
+    }
+}
+
+template <int HD>
+cudaError_t launch_attention_tiled(const AttnParams &p, cudaStream_t st) {
+    static_assert(8 * HD <= kKB * kQB, "staging rows live in the P buffer");
+    const size_t smem = sizeof(float) * (2 * HD * kQB + kKB * HD + kKB * kQB);
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(k_attention_tiled<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    int max_len = p.max_len > 0 ? p.max_len : kQB;
+    dim3 grid(p.n_prompts, p.heads, (max_len + kQB - 1) / kQB);
+    k_attention_tiled<HD><<<grid, 256, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
 // xa[m] = sum_k act[m][k] * a[k], one warp per row.
 __global__ void k_rowdot_bf16(const uint16_t *act, const float *a, int m, int k, float *xa) {
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -279,6 +454,9 @@ cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st) {
     if (p.n_prompts <= 0) return cudaSuccess;
     if (p.heads % p.kv_heads) return cudaErrorInvalidValue;
     const int hd = p.head_dim;
+    if (hd == 128 && !p.force_generic) return launch_attention_tiled<128>(p, st);
+    if (hd == 64 && !p.force_generic) return launch_attention_tiled<64>(p, st);
+    // other head sizes: one warp per (query, head) with an online softmax
     const size_t smem = sizeof(float) * (kKeyChunk * (hd + 1) + kKeyChunk * hd + kAttnWarps * hd +
                                          kAttnWarps * kKeyChunk + kAttnWarps * hd);
     static size_t configured = 0;

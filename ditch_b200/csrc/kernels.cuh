@@ -65,6 +65,8 @@ struct AttnParams {
     const float *q_norm, *k_norm;      // per-head RMSNorm weights or null
     float eps, scale;
     int *status;
+    int max_len;        // longest prompt of the batch
+    int force_generic;  // use the one-warp-per-query kernel for any head size
 };
 // Causal attention within each prompt with GQA, RoPE (neox) and optional q/k
 // norms (src/model.zig:4226-4374, attentionWorker 2935-2986).

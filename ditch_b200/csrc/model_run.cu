@@ -244,6 +244,7 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
         ap.eps = c.eps;
         ap.scale = 1.0f / std::sqrt((float)c.head_dim);
         ap.status = dev->status;
+        ap.max_len = b.h_len.empty() ? 1 : *std::max_element(b.h_len.begin(), b.h_len.end());
         DITCH_LAUNCH(dev, attention_prefill(ap, st));
         if (L.o_edit) DITCH_LAUNCH(dev, rowdot_bf16(m->att.as<uint16_t>(), L.o_a.as<float>(), n, qd, m->xa.as<float>(), st));
         if ((s = gemm_weight(m, L.o, 0, H, m->att.as<uint16_t>(), n, x, H, kEpiResidual, nullptr,
