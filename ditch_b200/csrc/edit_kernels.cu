@@ -58,25 +58,49 @@ __device__ float block_max(float v, float *sh) {
 
 constexpr int kGemvThreads = 256;
 
+// Row splits of a GEMV-T: about two blocks per SM in all, at least 64 rows
+// each (every split adds its partial sums atomically).
 inline int row_splits(int rows, int col_blocks) {
-    const int target = 4 * 148;
+    const int target = 2 * 148;
     int s = (target + col_blocks - 1) / col_blocks;
     s = s < 1 ? 1 : s;
-    const int max_s = (rows + 15) / 16;  // at least 16 rows per split
+    const int max_s = (rows + 63) / 64;
     return s > max_s ? (max_s < 1 ? 1 : max_s) : s;
 }
 
 // out[c] += sum_{r in split} v[r] W[r][c]; thread = 8 consecutive bf16 columns.
+// (The reference skips rows with v[r] == 0, src/tensor.zig:1065-1068; for
+// finite weights those rows add exactly zero, so the stream reads every row
+// without a data-dependent branch and keeps four loads in flight.)
 __global__ void k_gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, int rows_per) {
     const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
     if (c0 >= cols) return;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (c0 + 8 <= cols && (cols & 7) == 0) {
-        for (int r = r0; r < r1; r++) {
-            const float vr = v[r];
-            if (vr == 0.0f) continue;  // rows with y == 0 are skipped (src/tensor.zig:1065-1068)
-            uint4 q = __ldg(reinterpret_cast<const uint4 *>(w + (long long)r * cols + c0));
+        const uint16_t *base = w + c0;
+        int r = r0;
+        for (; r + 4 <= r1; r += 4) {
+            uint4 q[4];
+            float vr[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                q[u] = __ldg(reinterpret_cast<const uint4 *>(base + (long long)(r + u) * cols));
+                vr[u] = __ldg(v + r + u);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    acc[2 * j] = fmaf(vr[u], __uint_as_float(wd[j] << 16), acc[2 * j]);
+                    acc[2 * j + 1] = fmaf(vr[u], __uint_as_float(wd[j] & 0xffff0000u), acc[2 * j + 1]);
+                }
+            }
+        }
+        for (; r < r1; r++) {
+            const float vr = __ldg(v + r);
+            uint4 q = __ldg(reinterpret_cast<const uint4 *>(base + (long long)r * cols));
             const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -233,23 +257,49 @@ struct LoadMxfp4 {
     }
 };
 
-__global__ void k_rank1_bf16(uint16_t *w, int rows, int cols, const float *b, const float *a) {
-    const long long total8 = (long long)rows * cols / 8;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total8;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long e0 = i * 8;
-        const int r = (int)(e0 / cols), c0 = (int)(e0 % cols);
-        const float br = b[r];
-        uint4 *p = reinterpret_cast<uint4 *>(w + e0);
-        uint4 q = *p;
+// Block = a strip of 8 * blockDim columns over a range of rows: the strip's
+// a values stay in registers, each row is one 16-byte read and write per
+// thread, four rows in flight.
+__global__ void k_rank1_bf16(uint16_t *w, int rows, int cols, const float *b, const float *a, int rows_per) {
+    const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
+    if (c0 >= cols) return;
+    float av[8];
+    {
+        const float4 a0 = *reinterpret_cast<const float4 *>(a + c0), a1 = *reinterpret_cast<const float4 *>(a + c0 + 4);
+        av[0] = a0.x, av[1] = a0.y, av[2] = a0.z, av[3] = a0.w, av[4] = a1.x, av[5] = a1.y, av[6] = a1.z, av[7] = a1.w;
+    }
+    uint16_t *base = w + c0;
+    int r = r0;
+    for (; r + 4 <= r1; r += 4) {
+        uint4 q[4];
+        float br[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            q[u] = *reinterpret_cast<const uint4 *>(base + (long long)(r + u) * cols);
+            br[u] = __ldg(b + r + u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float lo = fmaf(br[u], av[2 * j], __uint_as_float(wd[j] << 16));
+                const float hi = fmaf(br[u], av[2 * j + 1], __uint_as_float(wd[j] & 0xffff0000u));
+                wd[j] = pack_bf16x2(lo, hi);
+            }
+            *reinterpret_cast<uint4 *>(base + (long long)(r + u) * cols) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
+    }
+    for (; r < r1; r++) {
+        uint4 q = *reinterpret_cast<const uint4 *>(base + (long long)r * cols);
+        const float br = __ldg(b + r);
         uint32_t wd[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const float lo = fmaf(br, a[c0 + 2 * j], __uint_as_float(wd[j] << 16));
-            const float hi = fmaf(br, a[c0 + 2 * j + 1], __uint_as_float(wd[j] & 0xffff0000u));
-            wd[j] = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
-        }
-        *p = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        for (int j = 0; j < 4; j++)
+            wd[j] = pack_bf16x2(fmaf(br, av[2 * j], __uint_as_float(wd[j] << 16)),
+                                fmaf(br, av[2 * j + 1], __uint_as_float(wd[j] & 0xffff0000u)));
+        *reinterpret_cast<uint4 *>(base + (long long)r * cols) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
     }
 }
 
@@ -456,10 +506,12 @@ cudaError_t row_norms_mxfp4(const uint8_t *blocks, const uint8_t *scales, int ro
 
 cudaError_t rank1_update_bf16(uint16_t *w, int rows, int cols, const float *b, const float *a, cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return cudaSuccess;
-    if ((cols & 7) == 0) {
-        const long long n8 = (long long)rows * cols / 8;
-        const int blocks = (int)std::min<long long>((n8 + 255) / 256, 148LL * 16);
-        k_rank1_bf16<<<blocks, 256, 0, st>>>(w, rows, cols, b, a);
+    if ((cols & 7) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+        const int cb = (cols + 2047) / 2048;
+        int sp = std::max(1, (8 * 148 + cb - 1) / cb);
+        sp = std::min(sp, std::max(1, rows / 16));
+        const int per = (rows + sp - 1) / sp;
+        k_rank1_bf16<<<dim3(cb, (rows + per - 1) / per), 256, 0, st>>>(w, rows, cols, b, a, per);
     } else {
         const long long n = (long long)rows * cols;
         const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);

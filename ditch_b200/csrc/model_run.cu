@@ -181,6 +181,25 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         p.db_stride = ex->db_stride;
         p.bn = ex->bn;
     }
+    // Split K when the output tiles leave SMs idle (few tokens or few weight
+    // rows) and the epilogue is linear: partial sums are added atomically, the
+    // residual add being itself such a sum; bias and delta come with split 0.
+    const bool dual = (flags & kEpiSwiglu) != 0;
+    if (!p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16)) {
+        const int bn = gemm_token_tile(n_tok, false, w.fmt != kFmtBf16);
+        const long long tiles = (long long)((m_rows + 127) / 128) * ((n_tok + bn - 1) / bn);
+        const int k_tiles = (w.cols + 63) / 64;
+        if (tiles < dev->sms && k_tiles >= 8) {
+            int ks = (int)((dev->sms + tiles - 1) / tiles);
+            ks = std::min(ks, k_tiles / 4);
+            if (ks > 1) {
+                p.k_splits = ks;
+                if (!(flags & kEpiResidual))
+                    DITCH_CUDA(cudaMemset2DAsync(out, (size_t)ldo * 4, 0, (size_t)m_rows * 4, n_tok, dev->stream));
+                flags = (flags & ~kEpiResidual) | kEpiAtomic;
+            }
+        }
+    }
     p.a2_row_offset = a2_row_offset;
     p.a_row0 = slab_row0;
     p.out = out;
