@@ -159,15 +159,13 @@ __device__ __forceinline__ uint32_t scale_pack(float2 v, float s) {
 
 // FP8 E4M3 with f32 block scales: bf16(code * scale[row / br][col / bc]).
 // Raw tile: 128 rows x 64 bytes, TMA 64B swizzle (chunk c at c ^ ((r >> 1) & 3)).
-__device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *atile, int r, int h, int grow, int k0,
-                                          const GemmParams &p) {
+// srow: the scale row of this weight row; s_tile: the k-tile's scale when the
+// block columns are a multiple of 64 (one_scale), loaded by the caller ahead
+// of the stage's barrier wait.
+__device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *atile, int r, int h, const float *srow,
+                                          bool one_scale, float s_tile, int k0, const GemmParams &p) {
     uint8_t *arow = atile + r * 128;
     const int rs = (r >> 1) & 3;
-    const float *srow = p.scales + (long long)(grow / p.blk_rows) * p.scale_cols;
-    // Block columns that are a multiple of the 64-wide k-tile share one scale
-    // per tile (the 128 x 128 blocks of the BASELINE checkpoints).
-    const bool one_scale = (p.blk_cols & 63) == 0;
-    const float s_tile = one_scale ? __ldg(srow + k0 / p.blk_cols) : 0.0f;
 #pragma unroll
     for (int cc = 0; cc < 2; cc++) {
         const int c = 2 * h + cc;  // raw 16-byte chunk: output chunks 2c, 2c + 1
@@ -423,26 +421,37 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         // ---------------- weight transform ----------------
         const int t = threadIdx.x - (2 + kEpiWarps) * 32;  // 0..255
         const int r = t & 127, h = t >> 7;
+        const bool one_scale = FMT == kFmtFp8 && (p.blk_cols & 63) == 0;
         int it = 0;
         for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
             const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
+            int vrow[C::kNA];
+            const float *srow[C::kNA];
+#pragma unroll
+            for (int i = 0; i < C::kNA; i++) {
+                const int off = i ? p.a2_row_offset : 0;
+                const int grow = ti.a_row0 + ti.wt * BM + r + off;
+                vrow[i] = min(grow, ti.a_row0 + off + p.m_w - 1);  // clamp side-data reads
+                srow[i] = FMT == kFmtFp8 ? p.scales + (long long)(vrow[i] / p.blk_rows) * p.scale_cols : nullptr;
+            }
             bool ok = true;
             for (int kt = ti.kt0; kt < ti.kt1; kt++, it++) {
                 const int s = it % C::kStages;
                 const int rs = it % C::kRawStages;
                 const uint32_t rph = (it / C::kRawStages) & 1;
+                float s_tile[C::kNA];
+#pragma unroll
+                for (int i = 0; i < C::kNA; i++)  // issued before the wait: its latency hides behind it
+                    s_tile[i] = one_scale ? __ldg(srow[i] + (kt * BK) / p.blk_cols) : 0.0f;
                 if (!mbar_wait(&L.rawfull[rs], rph, abort, p.status)) {
                     ok = false;
                     break;
                 }
 #pragma unroll
                 for (int i = 0; i < C::kNA; i++) {
-                    const int off = i ? p.a2_row_offset : 0;
-                    const int grow = ti.a_row0 + ti.wt * BM + r + off;
-                    const int vrow = min(grow, ti.a_row0 + off + p.m_w - 1);  // clamp side-data reads
-                    if (FMT == kFmtFp8) xform_fp8(L.raw(rs, i), L.a(s, i), r, h, vrow, kt * BK, p);
-                    if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(rs, i), L.a(s, i), r, h, vrow, kt * BK, p);
-                    if (FMT == kFmtInt4) xform_int4(L.raw(rs, i), L.a(s, i), r, h, vrow, kt * BK, p);
+                    if (FMT == kFmtFp8) xform_fp8(L.raw(rs, i), L.a(s, i), r, h, srow[i], one_scale, s_tile[i], kt * BK, p);
+                    if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(rs, i), L.a(s, i), r, h, vrow[i], kt * BK, p);
+                    if (FMT == kFmtInt4) xform_int4(L.raw(rs, i), L.a(s, i), r, h, vrow[i], kt * BK, p);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
