@@ -185,7 +185,10 @@ def run_gemm(args, dev):
     ms, _, _ = time_gemm(dev, W, args.m, args.cols, args.rows, args.steps, args.warmup)
     hbm, tf, src = _peaks()
     tflops = 2.0 * args.m * args.rows * args.cols / ms / 1e9
-    print(json.dumps({"config": "gemm", "fmt": args.fmt, "gemm_format": W.format(), "rows": args.rows,
+    stage = 1024 if args.stage_min_tokens is None else args.stage_min_tokens
+    plan = "staged" if W.format() != "bf16" and 0 < stage <= args.m else "in-gemm"
+    print(json.dumps({"config": "gemm", "fmt": args.fmt, "gemm_format": W.format(), "decode_plan": plan,
+                      "rows": args.rows,
                       "cols": args.cols, "m": args.m, "ms": round(ms, 4), "tflops": round(tflops, 1),
                       "frac_of_burst_bf16": round(tflops / tf, 4), "peak_source": src}), flush=True)
     W.close()
@@ -284,6 +287,8 @@ def run(args):
 
     torch.cuda.set_device(0)
     dev = ditch_b200.Device(0)
+    if args.stage_min_tokens is not None:
+        dev.set_decode_staging(args.stage_min_tokens)
     if args.config == "gemm":
         run_gemm(args, dev)
     elif args.config == "c3":

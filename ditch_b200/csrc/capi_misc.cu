@@ -262,6 +262,14 @@ int ditch_cuda_edit_weight_bf16(ditch_cuda_device *dev, void *w, size_t rows, si
 }
 
 // ---- timing ----
+int ditch_cuda_set_decode_staging(ditch_cuda_device *dev, int min_tokens) {
+    REQUIRE(dev, "null device");
+    REQUIRE(min_tokens >= 0, "min_tokens must be >= 0");
+    std::lock_guard<std::mutex> lk(dev->mu);
+    dev->stage_min_tokens = min_tokens;
+    return DITCH_CUDA_OK;
+}
+
 int ditch_cuda_set_profiling(ditch_cuda_device *dev, int enabled) {
     REQUIRE(dev, "null device");
     std::lock_guard<std::mutex> lk(dev->mu);

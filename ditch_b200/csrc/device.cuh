@@ -90,6 +90,10 @@ struct ditch_cuda_device {
     uint64_t used_bytes = 0, clock = 0;
     // per-op scratch
     ditch::DevBuf bx, bw, bo, by, braw;
+    // staged decode: quantised weights of GEMMs with at least this many tokens
+    // are decoded once to bf16 here and multiplied by the bf16 GEMM (0 = never)
+    ditch::DevBuf stage;
+    int stage_min_tokens = 1024;
     // profiling of GEMMs
     bool profiling = false;
     std::vector<ditch::GemmEvent> events;

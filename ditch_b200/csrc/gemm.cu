@@ -42,6 +42,7 @@ struct Cfg {
     static constexpr int kStageBytes = kNA * kABytes + kBBytes;
     static constexpr int kRawStageBytes = kNA * kRawBytes;
     static constexpr int kRawStages = kQuant ? 3 : 0;
+    static constexpr int kRawRing = kRawStages > 0 ? kRawStages : 1;  // modulus (unused without raw tiles)
     static constexpr int kStagesFit = (kSmemBudget - kRawStages * kRawStageBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
     static constexpr int kAccCols = kNA * BN;
@@ -251,6 +252,72 @@ __device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *atile, i
     }
 }
 
+// ---- staged decode ----------------------------------------------------------
+// Rows [row0, row0 + rows) of a quantised weight decoded once to bf16
+// [rows][cols] with the transforms' own arithmetic, so that the bf16 GEMM over
+// the staged copy equals the fused GEMM bit for bit. One thread decodes one
+// 16-byte chunk of codes: 16 FP8 elements, or 32 MXFP4 / INT4 elements.
+__global__ void __launch_bounds__(256) k_stage_decode(const StageArgs a) {
+    const int epc = a.fmt == kFmtFp8 ? 16 : 32;  // elements per chunk
+    const int chunks = a.cols / epc;
+    const long long total = (long long)a.rows * chunks;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / chunks), ch = (int)(i % chunks);
+        const int grow = a.row0 + r, c0 = ch * epc;
+        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(a.data + (long long)grow * a.row_bytes + ch * 16));
+        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+        uint4 *dst = reinterpret_cast<uint4 *>(a.out + (long long)r * a.cols + c0);
+        if (a.fmt == kFmtFp8) {
+            const float *srow = a.scales + (long long)(grow / a.blk_rows) * a.scale_cols;
+            const bool one = (a.blk_cols & 15) == 0;
+            const float s0 = __ldg(srow + c0 / a.blk_cols);
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                uint32_t o[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int c = c0 + 8 * half + 2 * e;
+                    const uint32_t two = words[2 * half + (e >> 1)] >> (16 * (e & 1));
+                    const float2 v = e4m3x2_f32(two & 0xffff);
+                    if (one) {
+                        o[e] = scale_pack(v, s0);
+                    } else {  // block columns not a multiple of 16: a scale per element
+                        const float sl = __ldg(srow + c / a.blk_cols), sh = __ldg(srow + (c + 1) / a.blk_cols);
+                        o[e] = pack_bf16x2(v.x * sl, v.y * sh);
+                    }
+                }
+                dst[half] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        } else if (a.fmt == kFmtMxfp4) {
+            const float s = e8m0_scale(__ldg(a.scales_u8 + (long long)grow * (a.cols / 32) + ch));
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                const uint32_t w = words[jj];
+                dst[jj] = make_uint4(scale_pack(e2m1x2_f32(w & 0xff), s), scale_pack(e2m1x2_f32((w >> 8) & 0xff), s),
+                                     scale_pack(e2m1x2_f32((w >> 16) & 0xff), s), scale_pack(e2m1x2_f32(w >> 24), s));
+            }
+        } else {  // kFmtInt4
+            const int g = c0 / a.blk_cols;
+            const float s = __ldg(a.scales + (long long)grow * a.scale_cols + g);
+            int zq = 8;
+            if (a.zeros) zq = (__ldg(a.zeros + (long long)(grow >> 3) * a.scale_cols + g) >> ((grow & 7) * 4)) & 0xf;
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                const uint32_t w = words[jj];
+                uint32_t o[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int lo = (int)((w >> (8 * e)) & 0xf) - zq;
+                    const int hi = (int)((w >> (8 * e + 4)) & 0xf) - zq;
+                    o[e] = scale_pack(make_float2((float)lo, (float)hi), s);
+                }
+                dst[jj] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        }
+    }
+}
+
 template <int BN, bool DUAL, int FMT>
 __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
@@ -307,8 +374,8 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                     const uint32_t ph = (it / C::kStages) & 1;
                     if (!mbar_wait(&L.empty[s], ph ^ 1, abort, p.status)) break;
                     if (C::kQuant) {
-                        const int rs = it % C::kRawStages;
-                        const uint32_t rph = (it / C::kRawStages) & 1;
+                        const int rs = it % C::kRawRing;
+                        const uint32_t rph = (it / C::kRawRing) & 1;
                         if (!mbar_wait(&L.rawempty[rs], rph ^ 1, abort, p.status)) break;
                         mbar_arrive_expect_tx(&L.rawfull[rs], C::kRawStageBytes);
                         const int xb = kt * (FMT == kFmtFp8 ? BK : BK / 2);  // raw bytes along K
@@ -437,8 +504,8 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
             bool ok = true;
             for (int kt = ti.kt0; kt < ti.kt1; kt++, it++) {
                 const int s = it % C::kStages;
-                const int rs = it % C::kRawStages;
-                const uint32_t rph = (it / C::kRawStages) & 1;
+                const int rs = it % C::kRawRing;
+                const uint32_t rph = (it / C::kRawRing) & 1;
                 float s_tile[C::kNA];
 #pragma unroll
                 for (int i = 0; i < C::kNA; i++)  // issued before the wait: its latency hides behind it
@@ -574,6 +641,19 @@ int gemm_token_tile(int n_tok, bool dual, bool quant) {
     if (n_tok <= 64) return 64;
     if (n_tok <= 128) return 128;
     return (dual && !quant) ? 128 : 256;
+}
+
+cudaError_t launch_stage_decode(const StageArgs &a, int num_sms, cudaStream_t stream) {
+    const int epc = a.fmt == kFmtFp8 ? 16 : 32;
+    if (a.rows <= 0) return cudaSuccess;
+    if ((a.fmt != kFmtFp8 && a.fmt != kFmtMxfp4 && a.fmt != kFmtInt4) || a.cols % epc != 0)
+        return cudaErrorInvalidValue;
+    if (a.fmt == kFmtInt4 && a.blk_cols % 32 != 0) return cudaErrorInvalidValue;
+    const long long chunks = (long long)a.rows * (a.cols / epc);
+    const long long want = (chunks + 255) / 256;
+    const int grid = (int)std::min<long long>(want, (long long)num_sms * 8);
+    k_stage_decode<<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, const GemmOperand &b, GemmParams p,

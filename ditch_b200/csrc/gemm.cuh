@@ -88,4 +88,22 @@ struct GemmOperand {
 cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, const GemmOperand &b,
                         GemmParams p, int num_sms, cudaStream_t stream);
 
+// Staged decode of rows [row0, row0 + rows) of a quantised weight (FP8 block,
+// MXFP4 or INT4 in the GEMM's storage) to bf16 [rows][cols], bit-identical to
+// the operand the fused GEMM builds in shared memory. cols must be a multiple
+// of 16 (FP8) or 32 (MXFP4, INT4); INT4 groups a multiple of 32.
+struct StageArgs {
+    int fmt;
+    const uint8_t *data;
+    long long row_bytes;
+    int row0, rows, cols;
+    const float *scales;       // FP8 [rows / blk_rows][scale_cols]; INT4 [rows][scale_cols]
+    const uint8_t *scales_u8;  // MXFP4 E8M0 [rows][cols / 32]
+    const uint32_t *zeros;     // INT4 packed zero points or null
+    int blk_rows, blk_cols, scale_cols;
+    uint16_t *out;
+};
+
+cudaError_t launch_stage_decode(const StageArgs &a, int num_sms, cudaStream_t stream);
+
 }  // namespace ditch

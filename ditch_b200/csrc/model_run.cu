@@ -167,6 +167,41 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     if (n_tok <= 0 || m_rows <= 0) return DITCH_CUDA_OK;
     GemmOperand A{w.data.ptr, w.rows * w.slabs, w.cols, w.row_bytes};
     GemmOperand B{act, n_tok, w.cols, (long long)w.cols * 2};
+    int fmt = w.fmt;
+    const bool dual = (flags & kEpiSwiglu) != 0;
+    // Staged decode. The fused transform decodes every weight element once per
+    // token tile; past a few tiles, decoding the rows once to bf16 scratch (one
+    // more pass over the weight: codes in, 2 bytes out, 2 bytes back in) and
+    // running the bf16 GEMM costs less. Both build the same bf16 operand.
+    if (fmt != kFmtBf16 && !(ex && ex->sched) && dev->stage_min_tokens > 0 && n_tok >= dev->stage_min_tokens) {
+        const int rows = (dual ? a2_row_offset : 0) + m_rows;
+        DITCH_CUDA(dev->stage.reserve((size_t)rows * w.cols * 2));
+        StageArgs sa{};
+        sa.fmt = fmt;
+        sa.data = w.data.as<uint8_t>();
+        sa.row_bytes = w.row_bytes;
+        sa.row0 = slab_row0;
+        sa.rows = rows;
+        sa.cols = w.cols;
+        sa.out = dev->stage.as<uint16_t>();
+        if (fmt == kFmtFp8) {
+            sa.scales = w.scales.as<float>();
+            sa.blk_rows = w.br;
+            sa.blk_cols = w.bc;
+            sa.scale_cols = w.scols;
+        } else if (fmt == kFmtMxfp4) {
+            sa.scales_u8 = w.scales.as<uint8_t>();
+        } else {
+            sa.scales = w.scales.as<float>();
+            sa.zeros = w.zeros.as<uint32_t>();
+            sa.blk_cols = w.group;
+            sa.scale_cols = w.groups;
+        }
+        DITCH_LAUNCH(dev, launch_stage_decode(sa, dev->sms, dev->stream));
+        A = GemmOperand{dev->stage.ptr, rows, w.cols, (long long)w.cols * 2};
+        fmt = kFmtBf16;
+        slab_row0 = 0;
+    }
     GemmParams p{};
     p.m_w = m_rows;
     p.n_tok = n_tok;
@@ -184,9 +219,8 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     // Split K when the output tiles leave SMs idle (few tokens or few weight
     // rows) and the epilogue is linear: partial sums are added atomically, the
     // residual add being itself such a sum; bias and delta come with split 0.
-    const bool dual = (flags & kEpiSwiglu) != 0;
     if (!p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16)) {
-        const int bn = gemm_token_tile(n_tok, false, w.fmt != kFmtBf16);
+        const int bn = gemm_token_tile(n_tok, false, fmt != kFmtBf16);
         const long long tiles = (long long)((m_rows + 127) / 128) * ((n_tok + bn - 1) / bn);
         const int k_tiles = (w.cols + 63) / 64;
         if (tiles < dev->sms && k_tiles >= 8) {
@@ -208,20 +242,20 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     p.bias = bias;
     p.xa = xa;
     p.db = db;
-    if (w.fmt == kFmtFp8) {
+    if (fmt == kFmtFp8) {
         p.scales = w.scales.as<float>();
         p.blk_rows = w.br;
         p.blk_cols = w.bc;
         p.scale_cols = w.scols;
-    } else if (w.fmt == kFmtMxfp4) {
+    } else if (fmt == kFmtMxfp4) {
         p.scales_u8 = w.scales.as<uint8_t>();
-    } else if (w.fmt == kFmtInt4) {
+    } else if (fmt == kFmtInt4) {
         p.scales = w.scales.as<float>();
         p.zeros = w.zeros.as<uint32_t>();
         p.blk_cols = w.group;
         p.scale_cols = w.groups;
     }
-    cudaError_t e = run_gemm(dev, w.fmt, A, (flags & kEpiSwiglu) ? &A : nullptr, B, p);
+    cudaError_t e = run_gemm(dev, fmt, A, (flags & kEpiSwiglu) ? &A : nullptr, B, p);
     if (e != cudaSuccess) return cuda_status(e, "gemm");
     return DITCH_CUDA_OK;
 }

@@ -116,6 +116,7 @@ SIGNATURES = {
     "ditch_cuda_weight_format": (C.c_int, [vp]),
     "ditch_cuda_weight_gemm": (C.c_int, [vp, vp, sz, vp, C.c_int]),
     "ditch_cuda_weight_decode": (C.c_int, [vp, vp]),
+    "ditch_cuda_set_decode_staging": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_profiling": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_gemm_stats": (C.c_int, [vp, f64p, u64p, f64p]),
     "ditch_cuda_reset_stats": (C.c_int, [vp]),
@@ -308,6 +309,11 @@ class Device:
         check(lib().ditch_cuda_edit_weight_bf16(self.h, w_ptr, rows, cols, r_ptr, alpha))
 
     # ---- timing ----
+    def set_decode_staging(self, min_tokens):
+        """Dense GEMMs over quantised weights with at least `min_tokens` tokens
+        decode the weight once to bf16 scratch; 0 keeps every decode in the GEMM."""
+        check(lib().ditch_cuda_set_decode_staging(self.h, int(min_tokens)))
+
     def set_profiling(self, on):
         check(lib().ditch_cuda_set_profiling(self.h, int(on)))
 

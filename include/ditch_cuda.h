@@ -277,6 +277,14 @@ int ditch_cuda_weight_format(const ditch_cuda_weight *w);
 int ditch_cuda_weight_gemm(ditch_cuda_weight *w, const void *x_bf16, size_t m, float *out, int k_splits);
 /* The decoded weight [rows][cols] bf16 into device memory (asynchronous). */
 int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out_bf16);
+/* GEMM plan for FP8 / MXFP4 / INT4 weights (dense products; the routed-expert
+ * grouped GEMM always decodes in the GEMM). A product over at least
+ * `min_tokens` tokens decodes the weight once into device scratch as bf16 and
+ * runs the bf16 GEMM; smaller ones decode tile by tile inside the GEMM. Both
+ * plans build the same bf16 operand, so results are identical. 0 = always in
+ * the GEMM. Default 1024. No counterpart in the reference (a tuning knob of
+ * this backend). */
+int ditch_cuda_set_decode_staging(ditch_cuda_device *dev, int min_tokens);
 
 /* ---- timing support (CUDA events on the device's stream) ---- */
 /* Accumulated device time and launch count of the weight GEMMs since the

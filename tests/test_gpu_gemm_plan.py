@@ -1,0 +1,56 @@
+"""The two plans of the quantised-weight GEMM: decode inside the GEMM (each
+128 x 64 weight tile decoded into shared memory per token tile) and staged
+decode (the weight decoded once to bf16 scratch, then the bf16 GEMM).
+
+Both build the operand with the reference's arithmetic (FP8 block
+src/dequant.zig:477-514, INT4 pack-quantized 518-597, MXFP4 natural layout
+643-673: the f32 product rounded to bf16), so each equals x . W^T over the
+standalone decoder's bf16 weight up to f32 accumulation order, and the two are
+bit-identical where neither splits K (no atomics, same order of k-steps)."""
+import pytest
+import torch
+
+from bench_configs import make_weight
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    (3200, 1024, 1500),  # 25 x 6 tiles of 256 tokens: no split-K in either plan
+    (384, 512, 1100),    # few tiles: split-K with atomics
+    (640, 2048, 100),    # a narrow token tile
+]
+
+
+def _bound(x, w):
+    # |sum - ref| <= 2^-18 * sum_k |x_k| |w_k| + tiny: f32 accumulation over K
+    return (x.float().abs() @ w.float().abs().T) * 2.0 ** -18 + 1e-6
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "mxfp4", "int4"])
+@pytest.mark.parametrize("shape", range(len(SHAPES)))
+def test_staged_and_fused_plans(device, fmt, shape):
+    rows, cols, m = SHAPES[shape]
+    torch.backends.cuda.matmul.allow_tf32 = False
+    gen = torch.Generator(device="cuda").manual_seed(17 + shape)
+    W, _ = make_weight(device, fmt, rows, cols, gen)
+    x = torch.randn(m, cols, device="cuda", generator=gen).to(torch.bfloat16)
+    dec = torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16)
+    W.decode(dec.data_ptr())
+    device.synchronize()
+    ref = x.float() @ dec.float().T
+    bound = _bound(x, dec)
+    outs = []
+    try:
+        for plan in (0, 1):  # 0: always in the GEMM; 1: staged from one token on
+            device.set_decode_staging(plan)
+            out = torch.full((m, rows), float("nan"), device="cuda", dtype=torch.float32)
+            W.gemm(x.data_ptr(), m, out.data_ptr())
+            device.synchronize()
+            err = (out - ref).abs()
+            assert bool((err <= bound).all()), (plan, float(err.max()), float(bound.min()))
+            outs.append(out)
+    finally:
+        device.set_decode_staging(1024)
+        W.close()
+    if shape == 0:
+        assert torch.equal(outs[0], outs[1])

@@ -60,3 +60,17 @@ def test_synthetic_moe_forward(device, fmt):
                                     moe=dict(experts=16, top_k=4, inter=128))
     ps = prompts(31, [40, 17, 64, 3, 70], spec["vocab"])
     check_forward(device, spec, f32, tensors, ps, max_bad_rows=0.2)
+
+
+@pytest.mark.parametrize("case", [2, 3])
+def test_synthetic_dense_forward_staged(device, case):
+    """The staged-decode plan (weights decoded once to bf16, then the bf16
+    GEMM, SwiGLU pair included) forced on for every GEMM of the FP8 models."""
+    kw = dict(CASES[case])
+    spec, f32, tensors = make_model(100 + case, **kw)
+    ps = prompts(7 + case, [1, 5, 64, 65, 150, 33], spec["vocab"])
+    device.set_decode_staging(1)
+    try:
+        check_forward(device, spec, f32, tensors, ps)
+    finally:
+        device.set_decode_staging(1024)
