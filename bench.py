@@ -43,15 +43,16 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ditch_b200", choices=["ditch_b200", "reference"])
-    ap.add_argument("--prompts", type=int, default=128)
+    ap.add_argument("--prompts", type=int, default=None, help="prompts per GPU (default: the config's)")
     ap.add_argument("--seq", type=int, default=64)
-    ap.add_argument("--layers", type=int, default=C2["n_layers"])
+    ap.add_argument("--layers", type=int, default=None, help="decoder layers (default: the config's)")
     ap.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline sample budget (seconds)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c5", "gemm"],
-                    help="c2 (default): the trial loop; c1: Qwen2-0.5B-style fp32 pipeline with oracle parity; "
-                         "c3: dequant + GEMM sweep; c5: Llama-3-70B-shaped in-place edit sweep; gemm: one GEMM")
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5", "gemm"],
+                    help="c2 (default): the FP8 dense trial loop; c3: dequant + GEMM sweep; c4: the Qwen3-MoE MXFP4 "
+                         "trial loop (expert-selective edit); c5: Llama-3-70B-shaped in-place edit sweep; gemm: one "
+                         "GEMM")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=4096)
@@ -59,7 +60,11 @@ def parse():
     ap.add_argument("--stage-min-tokens", type=int, default=None,
                     help="GEMMs over quantised weights with at least this many tokens decode the weight once to "
                          "bf16 first (0 = decode inside the GEMM always; default: the library's 1024)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.config == "c2":
+        args.layers = args.layers or C2["n_layers"]
+        args.prompts = args.prompts or 128
+    return args
 
 
 def dist_setup(gpus):

@@ -9,9 +9,13 @@
 * `c5`: the in-place rank-1 edit W <- W - alpha_l r_l (r_l^T W) on all 80
   o_proj [8192 x 8192] and down_proj [8192 x 28672] bf16 matrices of a
   Llama-3-70B shape. It reports HBM GB/s over the algorithmic 3 x 48.32 GB.
-* `c1`: the Qwen2-0.5B-style fp32 pipeline of BASELINE config 1, timed end to
-  end: capture of two 64 x 48 batches, directions, then per trial the edit,
-  the forward and the KL. The CPU baseline is the oracle on the same workload.
+* `c4`: the Qwen3-MoE-shaped trial loop of BASELINE config 4 on one GPU: 48
+  layers, hidden 2048, 32/4 heads of 128 with q/k norms, 128 routed experts
+  (top-8 softmax, renormalised) of intermediate 768 stored as MXFP4, bf16
+  attention, vocab 151936; 256 prompts x 64 tokens. A trial is the
+  expert-selective edit (o_proj plus the down projections of the 8 experts per
+  layer best aligned with the direction, src/moe.zig:1373-1477), the edited
+  forward and the first-token KL.
 
 All weights are seeded synthetic N(0, 0.02), generated and quantised on the
 GPU with torch (device-memory plumbing; the kernels under test are the
@@ -228,7 +232,7 @@ def run_c5(args, dev):
     import ditch_b200
 
     hbm, tf, src = _peaks()
-    L, H, I = args.layers if args.layers != 32 else 80, 8192, 28672
+    L, H, I = args.layers or 80, 8192, 28672
     gen = torch.Generator(device="cuda").manual_seed(args.seed)
     mats = []
     for _ in range(L):
@@ -280,6 +284,164 @@ def run_c5(args, dev):
           flush=True)
 
 
+C4 = dict(n_layers=48, hidden=2048, heads=32, kv_heads=4, head_dim=128, inter=768, vocab=151936, eps=1e-6,
+          rope_theta=1e6, qk_norm=1, n_experts=128, top_k=8, moe_inter=768, norm_topk=1)
+
+
+def build_c4_model(dev, spec, seed, max_seq):
+    """Seeded N(0, 0.02) weights: attention, router, embedding and LM head in
+    bf16, routed experts quantised to MXFP4 (natural layout) on the GPU."""
+    import torch
+
+    import ditch_b200
+    from ditch_b200 import Tensor
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    H, V, L, E, mi = spec["hidden"], spec["vocab"], spec["n_layers"], spec["n_experts"], spec["moe_inter"]
+    hd = spec["head_dim"]
+    qd, kvd = spec["heads"] * hd, spec["kv_heads"] * hd
+    keep, tensors = [], []
+
+    def bf16(shape):
+        return (torch.randn(shape, generator=g, device="cuda", dtype=torch.float32) * 0.02).to(torch.bfloat16)
+
+    def add_bf16(name, rows, cols):
+        w = bf16((rows, cols))
+        keep.append(w)
+        tensors.append(Tensor(name, "bf16", rows, cols, w))
+
+    def add_experts(name, rows, cols):
+        packed, scales = [], []
+        for e0 in range(0, E, 32):  # bounded temporaries
+            w = bf16((32 * rows, cols))
+            p_, s_ = mxfp4_packed(w)
+            packed.append(p_)
+            scales.append(s_)
+            del w
+        p_, s_ = torch.cat(packed), torch.cat(scales)
+        keep.extend([p_, s_])
+        tensors.append(Tensor(name, "mxfp4", rows, cols, p_, slabs=E, scales=s_))
+
+    ones = torch.ones(max(H, hd), dtype=torch.bfloat16, device="cuda")
+    keep.append(ones)
+    add_bf16("embed", V, H)
+    add_bf16("lm_head", V, H)
+    tensors.append(Tensor("final_norm", "bf16", H, 1, ones[:H]))
+    for i in range(L):
+        tensors += [Tensor(f"L{i}.input_norm", "bf16", H, 1, ones[:H]),
+                    Tensor(f"L{i}.post_norm", "bf16", H, 1, ones[:H]),
+                    Tensor(f"L{i}.q_norm", "bf16", hd, 1, ones[:hd]), Tensor(f"L{i}.k_norm", "bf16", hd, 1, ones[:hd])]
+        add_bf16(f"L{i}.q", qd, H)
+        add_bf16(f"L{i}.k", kvd, H)
+        add_bf16(f"L{i}.v", kvd, H)
+        add_bf16(f"L{i}.o", H, qd)
+        add_bf16(f"L{i}.router", E, H)
+        add_experts(f"L{i}.e_gate", mi, H)
+        add_experts(f"L{i}.e_up", mi, H)
+        add_experts(f"L{i}.e_down", H, mi)
+    torch.cuda.synchronize()
+    model = ditch_b200.Model(dev, spec, tensors, max_seq=max_seq)
+    del keep, tensors
+    torch.cuda.empty_cache()
+    return model
+
+
+def c4_flops(spec, tokens):
+    """Algorithmic FLOPs of one forward (SURVEY-style count: linear layers of
+    the attention, the router, top-k experts' SwiGLU, attention scores/values
+    over causal prompts, the LM head on the last rows)."""
+    H, L, E, k, mi = spec["hidden"], spec["n_layers"], spec["n_experts"], spec["top_k"], spec["moe_inter"]
+    qd, kvd = spec["heads"] * spec["head_dim"], spec["kv_heads"] * spec["head_dim"]
+    per_tok = 2 * (H * (qd + 2 * kvd) + qd * H + E * H + k * 3 * mi * H)
+    return L * per_tok * tokens
+
+
+def run_c4(args, dev):
+    import torch
+
+    from bench import Clocks, measured_peaks, trial_params
+
+    spec = dict(C4, n_layers=args.layers or C4["n_layers"], moe_layers=[True] * (args.layers or C4["n_layers"]))
+    L, V, S = spec["n_layers"], spec["vocab"], args.seq
+    P = args.prompts or 256
+    t0 = time.time()
+    model = build_c4_model(dev, spec, args.seed, max_seq=S)
+    load_s = time.time() - t0
+    rng = np.random.default_rng(args.seed + 1000)
+    good = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
+    bad = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
+    kl_prompts = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
+    dev.synchronize()
+    dev.timer_start()
+    gs, gc = model.residual_sums(good, window=1, batch_size=P)
+    bs, bc = model.residual_sums(bad, window=1, batch_size=P)
+    model.directions(gs, gc, bs, bc, True)
+    capture_ms = dev.timer_stop()
+    model.kl_init(kl_prompts)
+    tokens_flat = np.concatenate(kl_prompts).astype(np.uint32)
+    offs = np.zeros(P + 1, np.uintp)
+    offs[1:] = np.cumsum([len(p) for p in kl_prompts])
+    trial_rng = np.random.default_rng(args.seed + 7)
+    kls = []
+
+    def step(e2e):
+        po, pd, di = trial_params(trial_rng, L)
+        model.apply_expert_edit(po, pd, di, n_experts=spec["top_k"], strength=1.0)
+        kls.append(model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score())
+
+    def timed(e2e, steps):
+        torch.cuda.synchronize()
+        dev.synchronize()
+        dev.timer_start()
+        for _ in range(steps):
+            step(e2e)
+        return dev.timer_stop()
+
+    for _ in range(args.warmup):
+        step(False)
+    dev.set_profiling(True)
+    dev.reset_stats()
+    clocks = Clocks(0)
+    ms = timed(False, args.steps)
+    clk = clocks.stop()
+    gemm_ms, gemm_launches, gemm_flops = dev.gemm_stats()
+    launches = dev.launches()
+    dev.set_profiling(False)
+    for _ in range(max(1, args.warmup // 2)):
+        step(True)
+    ms_e2e = timed(True, args.steps)
+    hbm, tf_burst, tf_sust, src = measured_peaks()
+    tokens = P * S
+    fl = c4_flops(spec, tokens)
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
+    line = {
+        "metric": "trial-eval forward tokens/s", "value": round(tokens * args.steps / (ms / 1000.0), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3), "s_per_trial": round(ms / args.steps / 1000.0, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 experts + bf16 attention, bf16 MMA, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "C4: Qwen3-MoE-shaped, 128 MXFP4 experts top-8, trial = expert-selective rank-1 edit "
+                               "(o_proj + top-8 expert down per layer) + edited forward + first-token KL",
+                   "layers": L, "prompts_per_gpu": P, "seq_len": S, "vocab": V, "parallelism": "dp1",
+                   "l2": "inputs larger than L2 (15.4 GB of MXFP4 experts per forward)"},
+        "e2e": {"value": round(tokens * args.steps / (ms_e2e / 1000.0), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(tokens * 4 + (P + 1) * 8), "d2h_bytes_per_step": 8,
+                "ms_per_step": round(ms_e2e / args.steps, 3)},
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel: tcgen05 grouped GEMM, MXFP4 decoded per tile",
+                     "achieved": round(achieved, 1), "peak": tf_sust, "unit": "TFLOP/s",
+                     "frac": round(achieved / tf_sust, 4), "peak_source": f"{src} bf16 sustained", "traffic": None,
+                     "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
+                     "gemm_share_of_step": round(gemm_ms / ms, 4) if ms > 0 else None,
+                     "forward_tflop": round(fl / 1e12, 2),
+                     "forward_tflops_per_s": round(fl * args.steps / (ms / 1000.0) / 1e12, 1)},
+        "gpu_launches": int(launches), "clocks": clk,
+        "one_off": {"load_s": round(load_s, 2), "capture_and_directions_ms": round(capture_ms, 2)},
+        "kl_last": kls[-1] if kls else None,
+    }
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
 def run(args):
     import torch
 
@@ -293,6 +455,8 @@ def run(args):
         run_gemm(args, dev)
     elif args.config == "c3":
         run_c3(args, dev)
+    elif args.config == "c4":
+        run_c4(args, dev)
     elif args.config == "c5":
         run_c5(args, dev)
     else:

@@ -58,13 +58,13 @@ __device__ float block_max(float v, float *sh) {
 
 constexpr int kGemvThreads = 256;
 
-// Row splits of a GEMV-T: about two blocks per SM in all, at least 64 rows
-// each (every split adds its partial sums atomically).
-inline int row_splits(int rows, int col_blocks) {
+// Row splits of a GEMV-T: about two blocks per SM in all, at least
+// `min_rows` rows each (every split adds its partial sums atomically).
+inline int row_splits(int rows, int col_blocks, int min_rows = 64) {
     const int target = 2 * 148;
     int s = (target + col_blocks - 1) / col_blocks;
     s = s < 1 ? 1 : s;
-    const int max_s = (rows + 63) / 64;
+    const int max_s = (rows + min_rows - 1) / min_rows;
     return s > max_s ? (max_s < 1 ? 1 : max_s) : s;
 }
 
@@ -165,13 +165,37 @@ __global__ void k_gemv_t_fp8(const uint8_t *codes, const float *scales, int rows
 #pragma unroll
     for (int j = 0; j < 16; j++) acc[j] = 0.0f;
     const bool vec = (cols & 15) == 0 && (bc & 15) == 0;
-    for (int r = r0; r < r1; r++) {
-        const float vr = v[r];
-        if (vr == 0.0f) continue;
-        const float *srow = scales + (long long)(r / br) * scols;
-        if (vec) {
-            const float s = srow[c0 / bc];
-            uint4 q = __ldg(reinterpret_cast<const uint4 *>(codes + (long long)r * cols + c0));
+    if (vec) {
+        // Rows four at a time, all loads of a group issued before the math
+        // (no skip of v[r] == 0 rows: they add exactly zero for finite weights).
+        const int sc = c0 / bc;
+        int r = r0;
+        for (; r + 4 <= r1; r += 4) {
+            uint4 q[4];
+            float vr[4], s[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                q[u] = __ldg(reinterpret_cast<const uint4 *>(codes + (long long)(r + u) * cols + c0));
+                vr[u] = __ldg(v + r + u);
+                s[u] = __ldg(scales + (long long)((r + u) / br) * scols + sc);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float f[4];
+                    e4m3x4(wd[j], f);
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        acc[4 * j + e] =
+                            fmaf(vr[u], bf16_bits_to_f32(f32_to_bf16_bits(f[e] * s[u])), acc[4 * j + e]);
+                }
+            }
+        }
+        for (; r < r1; r++) {
+            const float vr = __ldg(v + r), s = __ldg(scales + (long long)(r / br) * scols + sc);
+            const uint4 q = __ldg(reinterpret_cast<const uint4 *>(codes + (long long)r * cols + c0));
             const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -181,7 +205,11 @@ __global__ void k_gemv_t_fp8(const uint8_t *codes, const float *scales, int rows
                 for (int e = 0; e < 4; e++)
                     acc[4 * j + e] = fmaf(vr, bf16_bits_to_f32(f32_to_bf16_bits(f[e] * s)), acc[4 * j + e]);
             }
-        } else {
+        }
+    } else {
+        for (int r = r0; r < r1; r++) {
+            const float vr = v[r];
+            const float *srow = scales + (long long)(r / br) * scols;
             for (int j = 0; j < 16 && c0 + j < cols; j++) {
                 float f[4];
                 e4m3x4(codes[(long long)r * cols + c0 + j], f);
@@ -466,7 +494,7 @@ cudaError_t gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int 
                        const float *v, float *out, cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return cudaSuccess;
     const int cb = (cols + kGemvThreads * 16 - 1) / (kGemvThreads * 16);
-    const int sp = row_splits(rows, cb);
+    const int sp = row_splits(rows, cb, 16);
     const int per = (rows + sp - 1) / sp;
     k_gemv_t_fp8<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(codes, scales, rows, cols, br, bc,
                                                                           (cols + bc - 1) / bc, v, out, per);

@@ -116,11 +116,18 @@ __device__ __forceinline__ TileInfo tile_info(const GemmParams &p, int tile, int
         t.first_split = true;
         return t;
     }
+    // Output tiles run in bands of kBand token tiles, weight tile by weight
+    // tile within a band: the tiles the persistent CTAs hold at one time share
+    // a few weight tiles and a few token tiles, which then stay in L2.
+    constexpr int kBand = 8;
     const int split = tile % p.k_splits;
     const int rest = tile / p.k_splits;
+    const int band = rest / (kBand * p.w_tiles);
+    const int idx = rest - band * kBand * p.w_tiles;
+    const int g = min(kBand, p.t_tiles - band * kBand);
     t.e = -1;
-    t.wt = rest / p.t_tiles;
-    t.tok0 = (rest % p.t_tiles) * BN;
+    t.wt = idx / g;
+    t.tok0 = (band * kBand + idx % g) * BN;
     t.tok_cnt = min(BN, p.n_tok - t.tok0);
     t.a_row0 = p.a_row0;
     t.kt0 = split * kt_per_split;
@@ -458,26 +465,54 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                 float u[32];
                 if (DUAL) tmem_ld32(tbase + BN + c0, u);
                 const int m0 = ti.tok0 + c0;
+                const int mv = min(32, m_end - m0);  // valid tokens of this chunk (>= 1)
+                // Every load of a chunk is issued before its first store: as far
+                // as the compiler knows the stores may alias the loads, and
+                // interleaving them serialises one memory round trip per token.
+                float r[32];
+                if (p.xa && dbn != 0.0f) {
+                    float xa[32];
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const int m = m0 + j;
-                    if (!n_ok || m >= m_end) continue;
-                    float r = v[j];
-                    if (p.xa && dbn != 0.0f) r += p.xa[m] * dbn;
-                    r += bias;
-                    const long long o = (long long)m * p.ldo + n;
-                    if (DUAL) {
-                        reinterpret_cast<uint16_t *>(p.out)[o] = f32_to_bf16_bits(silu_f(r) * u[j]);
-                    } else if (p.flags & kEpiAtomic) {
-                        atomicAdd(reinterpret_cast<float *>(p.out) + o, r);
-                    } else if (p.flags & kEpiResidual) {
-                        float *po = reinterpret_cast<float *>(p.out) + o;
-                        *po = *po + r;
-                    } else if (p.flags & kEpiOutBf16) {
-                        reinterpret_cast<uint16_t *>(p.out)[o] = f32_to_bf16_bits(r);
-                    } else {
-                        reinterpret_cast<float *>(p.out)[o] = r;
-                    }
+                    for (int j = 0; j < 32; j++) xa[j] = j < mv ? __ldg(p.xa + m0 + j) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) r[j] = v[j] + xa[j] * dbn;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) r[j] = v[j];
+                }
+#pragma unroll
+                for (int j = 0; j < 32; j++) r[j] += bias;
+                const long long o0 = (long long)m0 * p.ldo + n;
+                if (!n_ok) {
+                    // weight row past the matrix: nothing to store
+                } else if (DUAL) {
+                    uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + o0;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (j < mv) ob[(long long)j * p.ldo] = f32_to_bf16_bits(silu_f(r[j]) * u[j]);
+                } else if (p.flags & kEpiAtomic) {
+                    float *of = reinterpret_cast<float *>(p.out) + o0;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (j < mv) atomicAdd(of + (long long)j * p.ldo, r[j]);
+                } else if (p.flags & kEpiResidual) {
+                    float *of = reinterpret_cast<float *>(p.out) + o0;
+                    float old[32];
+#pragma unroll
+                    for (int j = 0; j < 32; j++) old[j] = j < mv ? of[(long long)j * p.ldo] : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (j < mv) of[(long long)j * p.ldo] = old[j] + r[j];
+                } else if (p.flags & kEpiOutBf16) {
+                    uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + o0;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (j < mv) ob[(long long)j * p.ldo] = f32_to_bf16_bits(r[j]);
+                } else {
+                    float *of = reinterpret_cast<float *>(p.out) + o0;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (j < mv) of[(long long)j * p.ldo] = r[j];
                 }
             }
             tc_fence_before();

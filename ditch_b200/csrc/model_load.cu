@@ -336,6 +336,12 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
     REQUIRE(cfg->heads % cfg->kv_heads == 0, "heads must be a multiple of kv heads");
     REQUIRE(cfg->head_dim % 2 == 0, "head_dim must be even");
     REQUIRE(cfg->hidden % 8 == 0, "hidden must be a multiple of 8");
+    // device-resident inputs may still be in flight on their producers' streams
+    for (size_t i = 0; i < n_tensors; i++)
+        if (tensors[i].on_device) {
+            DITCH_CUDA(cudaDeviceSynchronize());
+            break;
+        }
     REQUIRE((cfg->heads * cfg->head_dim) % 8 == 0, "heads * head_dim must be a multiple of 8");
     std::unique_ptr<ditch_cuda_model> m(new ditch_cuda_model());
     m->dev = dev;
@@ -536,6 +542,8 @@ int ditch_cuda_weight_load(ditch_cuda_device *dev, const ditch_cuda_tensor *t, d
     *out = nullptr;
     std::lock_guard<std::mutex> lk(dev->mu);
     DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    // device-resident input may still be in flight on the producer's stream
+    if (t->on_device) DITCH_CUDA(cudaDeviceSynchronize());
     std::unique_ptr<ditch_cuda_weight> w(new ditch_cuda_weight());
     w->dev = dev;
     int st = build_weight(dev, t, w->mat);

@@ -154,7 +154,9 @@ typedef struct {
  * "L<i>.qb|kb|vb", "L<i>.q_norm|k_norm", "L<i>.gate|up|down" (dense MLP),
  * "L<i>.router" and the expert stacks "L<i>.e_gate|e_up|e_down" ([slabs =
  * experts][rows][cols]). Host memory (or device memory when on_device is
- * set), read during the call only. */
+ * set), read during the call only. With device memory the loader first waits
+ * for all work queued on the GPU, so data still being produced on another
+ * stream is complete before it is read. */
 typedef struct {
     const char *name;
     int format;
@@ -272,8 +274,10 @@ void ditch_cuda_weight_free(ditch_cuda_weight *w);
 /* 0 bf16, 1 FP8 block, 2 MXFP4, 3 INT4 (how the GEMM reads the weight). */
 int ditch_cuda_weight_format(const ditch_cuda_weight *w);
 /* out[m][rows] f32 = x[m][cols] . W^T with x bf16; x and out are device
- * pointers on the device's stream (asynchronous). k_splits > 1 splits K
- * (partial sums added atomically; out is zeroed first). */
+ * pointers, used in order on the device's own stream (asynchronous; that
+ * stream does not wait for other streams, so x must be complete when the call
+ * is made). k_splits > 1 splits K (partial sums added atomically; out is
+ * zeroed first). */
 int ditch_cuda_weight_gemm(ditch_cuda_weight *w, const void *x_bf16, size_t m, float *out, int k_splits);
 /* The decoded weight [rows][cols] bf16 into device memory (asynchronous). */
 int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out_bf16);

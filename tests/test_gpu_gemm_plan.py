@@ -35,6 +35,7 @@ def test_staged_and_fused_plans(device, fmt, shape):
     W, _ = make_weight(device, fmt, rows, cols, gen)
     x = torch.randn(m, cols, device="cuda", generator=gen).to(torch.bfloat16)
     dec = torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()  # the library's stream does not wait for torch's
     W.decode(dec.data_ptr())
     device.synchronize()
     ref = x.float() @ dec.float().T
@@ -44,6 +45,7 @@ def test_staged_and_fused_plans(device, fmt, shape):
         for plan in (0, 1):  # 0: always in the GEMM; 1: staged from one token on
             device.set_decode_staging(plan)
             out = torch.full((m, rows), float("nan"), device="cuda", dtype=torch.float32)
+            torch.cuda.synchronize()
             W.gemm(x.data_ptr(), m, out.data_ptr())
             device.synchronize()
             err = (out - ref).abs()
