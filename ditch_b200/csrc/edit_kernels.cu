@@ -1,6 +1,8 @@
 // Bandwidth-bound kernels of the edit, the scorers and the residual
 // reduction: GEMV-T (A = v^T W), row norms, the in-place rank-1 update, the
 // fused log-softmax / KL, and the f64 residual sums and directions.
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace ditch {
@@ -225,31 +227,83 @@ __device__ __constant__ float kE2M1e[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f,
 
 __device__ __forceinline__ float mx_scale(uint32_t b) { return __uint_as_float(b == 0 ? 0x00400000u : (b << 23)); }
 
-// MXFP4 (natural layout); a thread covers one 32-element block of a row.
-__global__ void k_gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, const float *v,
-                               float *out, int rows_per) {
-    const int blk = blockIdx.x * blockDim.x + threadIdx.x;
+// Two E2M1 nibbles (one byte, low nibble first) to two f32, exactly.
+__device__ __forceinline__ float2 e2m1x2(uint32_t byte) {
+    uint32_t h;
+    asm("{\n\t.reg .b8 b;\n\tcvt.u8.u32 b, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b;\n\t}" : "=r"(h) : "r"(byte));
+    return __half22float2(*reinterpret_cast<__half2 *>(&h));
+}
+
+// MXFP4 (natural layout) over a stack of `slabs` matrices [rows][cols]:
+// out[e][c] = sum_r v[r] W_e[r][c] (the decoded value e2m1 * 2^(b - 127) is
+// exact in bf16, src/dequant.zig:643-673). Block = 32 column blocks (x) by 8
+// row lanes (y); grid = (column-block groups, row chunks, slabs). Each thread
+// streams one 32-element block of its rows, four rows of loads in flight, and
+// the 8 row lanes are summed in shared memory before one atomic per column.
+constexpr int kMxLanes = 8;
+__global__ void __launch_bounds__(32 * kMxLanes) k_gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales,
+                                                                int rows, int cols, const float *v, float *out,
+                                                                int rows_per) {
+    __shared__ float part[kMxLanes][32][33];
     const int nblk = cols / 32;
+    const int blk = blockIdx.x * 32 + threadIdx.x;
+    const int e = blockIdx.z;
     const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
-    if (blk >= nblk) return;
+    const uint8_t *bl = blocks + (long long)e * rows * (cols / 2);
+    const uint8_t *sc = scales + (long long)e * rows * nblk;
     float acc[32];
 #pragma unroll
     for (int j = 0; j < 32; j++) acc[j] = 0.0f;
-    for (int r = r0; r < r1; r++) {
-        const float vr = v[r];
-        if (vr == 0.0f) continue;
-        const float s = mx_scale(scales[(long long)r * nblk + blk]);
-        uint4 q = __ldg(reinterpret_cast<const uint4 *>(blocks + (long long)r * (cols / 2) + blk * 16));
-        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+    if (blk < nblk) {
+        int r = r0 + threadIdx.y;
+        for (; r + 3 * kMxLanes < r1; r += 4 * kMxLanes) {
+            uint4 q[4];
+            float vr[4], s[4];
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            const uint32_t byte = (wd[j / 4] >> (8 * (j & 3))) & 0xff;
-            acc[2 * j] = fmaf(vr, kE2M1e[byte & 0xf] * s, acc[2 * j]);
-            acc[2 * j + 1] = fmaf(vr, kE2M1e[byte >> 4] * s, acc[2 * j + 1]);
+            for (int u = 0; u < 4; u++) {
+                const int rr = r + u * kMxLanes;
+                q[u] = __ldg(reinterpret_cast<const uint4 *>(bl + (long long)rr * (cols / 2) + blk * 16));
+                vr[u] = __ldg(v + rr);
+                s[u] = mx_scale(__ldg(sc + (long long)rr * nblk + blk));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+                const float vs = vr[u];
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float2 f = e2m1x2((wd[j / 4] >> (8 * (j & 3))) & 0xff);
+                    acc[2 * j] = fmaf(vs, f.x * s[u], acc[2 * j]);
+                    acc[2 * j + 1] = fmaf(vs, f.y * s[u], acc[2 * j + 1]);
+                }
+            }
+        }
+        for (; r < r1; r += kMxLanes) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4 *>(bl + (long long)r * (cols / 2) + blk * 16));
+            const float vs = __ldg(v + r), s = mx_scale(__ldg(sc + (long long)r * nblk + blk));
+            const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const float2 f = e2m1x2((wd[j / 4] >> (8 * (j & 3))) & 0xff);
+                acc[2 * j] = fmaf(vs, f.x * s, acc[2 * j]);
+                acc[2 * j + 1] = fmaf(vs, f.y * s, acc[2 * j + 1]);
+            }
         }
     }
 #pragma unroll
-    for (int j = 0; j < 32; j++) atomicAdd(out + blk * 32 + j, acc[j]);
+    for (int j = 0; j < 32; j++) part[threadIdx.y][threadIdx.x][j] = acc[j];
+    __syncthreads();
+    // thread (x, y) sums columns y, y + 8, y + 16, y + 24 of column block x
+    if (blk < nblk) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int j = threadIdx.y + kMxLanes * k;
+            float t = 0.0f;
+#pragma unroll
+            for (int l = 0; l < kMxLanes; l++) t += part[l][threadIdx.x][j];
+            atomicAdd(out + (long long)e * cols + blk * 32 + j, t);
+        }
+    }
 }
 
 template <typename LOAD>
@@ -503,13 +557,20 @@ cudaError_t gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int 
 
 cudaError_t gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, const float *v,
                          float *out, cudaStream_t st) {
-    if (rows <= 0 || cols <= 0) return cudaSuccess;
-    if (cols % 32) return cudaErrorInvalidValue;
-    const int nblk = cols / 32;
-    const int cb = (nblk + 127) / 128;
-    const int sp = row_splits(rows, cb);
-    const int per = (rows + sp - 1) / sp;
-    k_gemv_t_mxfp4<<<dim3(cb, (rows + per - 1) / per), 128, 0, st>>>(blocks, scales, rows, cols, v, out, per);
+    return gemv_t_mxfp4_stack(blocks, scales, 1, rows, cols, v, out, st);
+}
+
+cudaError_t gemv_t_mxfp4_stack(const uint8_t *blocks, const uint8_t *scales, int slabs, int rows, int cols,
+                               const float *v, float *out, cudaStream_t st) {
+    if (rows <= 0 || cols <= 0 || slabs <= 0) return cudaSuccess;
+    if (cols % 32 || slabs > 65535) return cudaErrorInvalidValue;
+    const int gx = (cols / 32 + 31) / 32;
+    // about four blocks per SM in all, at least 4 rows per row lane
+    int chunks = (4 * 148 + gx * slabs - 1) / (gx * slabs);
+    chunks = std::max(1, std::min(chunks, (rows + 4 * kMxLanes - 1) / (4 * kMxLanes)));
+    const int per = (rows + chunks - 1) / chunks;
+    k_gemv_t_mxfp4<<<dim3(gx, (rows + per - 1) / per, slabs), dim3(32, kMxLanes), 0, st>>>(blocks, scales, rows,
+                                                                                         cols, v, out, per);
     return cudaGetLastError();
 }
 

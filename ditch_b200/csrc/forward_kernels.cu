@@ -67,6 +67,18 @@ __global__ void k_rmsnorm_bf16(const float *x, const float *w, int n, int hidden
     uint16_t *hr = h + (long long)row * hidden;
     const int slot = cap_slot ? cap_slot[src] : -1;
     float *cr = slot >= 0 ? res + (long long)slot * hidden : nullptr;
+    if ((hidden & 3) == 0) {  // four elements per lane and access
+        for (int i = lane * 4; i < hidden; i += 128) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + i);
+            const float4 g = *reinterpret_cast<const float4 *>(w + i);
+            uint2 o;
+            o.x = pack_bf16x2(v.x * inv * g.x, v.y * inv * g.y);
+            o.y = pack_bf16x2(v.z * inv * g.z, v.w * inv * g.w);
+            *reinterpret_cast<uint2 *>(hr + i) = o;
+            if (cr) *reinterpret_cast<float4 *>(cr + i) = v;
+        }
+        return;
+    }
     for (int i = lane; i < hidden; i += 32) {
         const float v = xr[i];
         hr[i] = f32_to_bf16_bits(v * inv * w[i]);
@@ -223,12 +235,65 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnParams p) {
     }
 }
 
+// ---- q/k norm and RoPE, once per (token, head) ---------------------------
+// Warp per (token, head slot) with the head's values in registers: lane l
+// holds elements l, l + 32, ... (the order rms_inplace and rope_neox_inplace
+// use), so the arithmetic is theirs. Applied in place to the q and k columns
+// of the QKV rows before the tiled attention reads them.
+template <int HD>
+__global__ void __launch_bounds__(256) k_qk_prep(float *qkv, AttnParams p) {
+    constexpr int V = HD / 32, H2 = V / 2;  // values per lane; pair (k, k + H2) = (i, i + HD / 2)
+    const int b = blockIdx.x;
+    const int start = p.seq_start[b], len = p.seq_len[b];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos = blockIdx.y * 8 + warp;
+    if (pos >= len) return;
+    const int nh = p.heads, nkv = p.kv_heads;
+    const int width = (nh + 2 * nkv) * HD;
+    float *row = qkv + (long long)(start + pos) * width;
+    const float *c = p.rope_cos + (long long)pos * (HD / 2);
+    const float *sn = p.rope_sin + (long long)pos * (HD / 2);
+    float cs[H2], ss[H2];
+#pragma unroll
+    for (int k = 0; k < H2; k++) {
+        cs[k] = __ldg(c + lane + 32 * k);
+        ss[k] = __ldg(sn + lane + 32 * k);
+    }
+    for (int slot = 0; slot < nh + nkv; slot++) {  // q heads, then k heads
+        float *v = row + slot * HD;
+        const float *nw = slot < nh ? p.q_norm : p.k_norm;
+        float x[V];
+#pragma unroll
+        for (int k = 0; k < V; k++) x[k] = v[lane + 32 * k];
+        if (nw) {
+            float sq = 0.0f;
+#pragma unroll
+            for (int k = 0; k < V; k++) sq += x[k] * x[k];
+            sq = warp_sum(sq);
+            const float inv = 1.0f / sqrtf(sq / (float)HD + p.eps);
+#pragma unroll
+            for (int k = 0; k < V; k++) x[k] = x[k] * inv * __ldg(nw + lane + 32 * k);
+        }
+#pragma unroll
+        for (int k = 0; k < H2; k++) {
+            const float x1 = x[k], x2 = x[k + H2];
+            x[k] = x1 * cs[k] - x2 * ss[k];
+            x[k + H2] = x2 * cs[k] + x1 * ss[k];
+        }
+#pragma unroll
+        for (int k = 0; k < V; k++) v[lane + 32 * k] = x[k];
+    }
+}
+
 // ---- register-tiled attention for head_dim 64 / 128 ----------------------
-// Block = (prompt, q head, chunk of 64 query positions); 256 threads. Q (64
-// rows) and each 64-key chunk of K are staged transposed in f32 shared memory
-// after q/k norm and RoPE; V natural. Scores: thread (ty, tx) owns queries
-// 4ty..4ty+3 x keys 4tx..4tx+3 (two LDS.128 per 16 FMAs); the output: the
-// same 4 queries x HD/16 dimensions. Online softmax across key chunks, f32.
+// Block = (prompt, kv head, chunk of 64 query positions); 256 threads; the
+// group's query heads one after another, so a prompt whose keys fit one
+// 64-key chunk stages K and V once for the whole group. Q (64 rows) and each
+// 64-key chunk of K are staged transposed in f32 shared memory (rows across
+// lanes: conflict-free), V natural, from rows already normed and roped.
+// Scores: thread (ty, tx) owns queries 4ty..4ty+3 x keys 4tx..4tx+3 (two
+// LDS.128 per 16 FMAs); the output: the same 4 queries x HD/16 dimensions.
+// Online softmax across key chunks, f32.
 constexpr int kQB = 64, kKB = 64;
 
 template <int HD>
@@ -237,153 +302,148 @@ __global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
     float *qt = sm;                    // [HD][kQB]
     float *kt = qt + HD * kQB;         // [HD][kKB]
     float *vs = kt + HD * kKB;         // [kKB][HD]
-    float *pt = vs + kKB * HD;         // [kKB][kQB]; also the staging rows
-    float *row = pt;                   // [8 warps][HD] while staging Q / K
-    const int b = blockIdx.x, h = blockIdx.y, i0 = blockIdx.z * kQB;
+    float *pt = vs + kKB * HD;         // [kKB][kQB]
+    const int b = blockIdx.x, kvh = blockIdx.y, i0 = blockIdx.z * kQB;
     const int start = p.seq_start[b], len = p.seq_len[b];
     if (i0 >= len) return;
-    const int nh = p.heads, nkv = p.kv_heads, groups = nh / nkv, kvh = h / groups;
+    const int nh = p.heads, nkv = p.kv_heads, groups = nh / nkv;
     const int qd = nh * HD, kvd = nkv * HD, width = qd + 2 * kvd;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x;
     const int ty = tid >> 4, tx = tid & 15;
-    float *wrow = row + warp * HD;
     constexpr int DPT = HD / 16;  // output dimensions per thread
-
-    // stage Q: rows i0 .. i0 + 63 of head h (zero beyond the prompt)
-    for (int r = warp; r < kQB; r += 8) {
-        const int i = i0 + r;
-        if (i < len) {
-            const float *src = p.qkv + (long long)(start + i) * width + h * HD;
-            for (int d = lane; d < HD; d += 32) wrow[d] = src[d];
-            __syncwarp();
-            if (p.q_norm) rms_inplace(wrow, HD, p.q_norm, p.eps, lane);
-            rope_neox_inplace(wrow, HD, i, p.rope_cos, p.rope_sin, lane);
-            __syncwarp();
-            for (int d = lane; d < HD; d += 32) qt[d * kQB + r] = wrow[d];
-        } else {
-            for (int d = lane; d < HD; d += 32) qt[d * kQB + r] = 0.0f;
-        }
-        __syncwarp();
-    }
-    float m[4], l[4], o[4][DPT];
-#pragma unroll
-    for (int a = 0; a < 4; a++) {
-        m[a] = -INFINITY;
-        l[a] = 0.0f;
-#pragma unroll
-        for (int c = 0; c < DPT; c++) o[a][c] = 0.0f;
-    }
+    constexpr int C4 = HD / 4;    // float4 per row
     const int last_q = min(len, i0 + kQB) - 1;  // causal: keys 0 .. last_q
-    for (int k0 = 0; k0 <= last_q; k0 += kKB) {
-        __syncthreads();
-        for (int r = warp; r < kKB; r += 8) {
-            const int j = k0 + r;
-            if (j < len) {
-                const float *src = p.qkv + (long long)(start + j) * width;
-                for (int d = lane; d < HD; d += 32) {
-                    wrow[d] = src[qd + kvh * HD + d];
-                    vs[r * HD + d] = src[qd + kvd + kvh * HD + d];
+    const bool one_chunk = last_q < kKB;
+
+    for (int g = 0; g < groups; g++) {
+        const int h = kvh * groups + g;
+        __syncthreads();  // the previous head's reads of the buffers are done
+        for (int idx = tid; idx < kQB * C4; idx += 256) {
+            const int r = idx % kQB, c4 = idx / kQB, i = i0 + r;
+            float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (i < len) q = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + i) * width + h * HD + 4 * c4);
+            qt[(4 * c4 + 0) * kQB + r] = q.x;
+            qt[(4 * c4 + 1) * kQB + r] = q.y;
+            qt[(4 * c4 + 2) * kQB + r] = q.z;
+            qt[(4 * c4 + 3) * kQB + r] = q.w;
+        }
+        float m[4], l[4], o[4][DPT];
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+            m[a] = -INFINITY;
+            l[a] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < DPT; c++) o[a][c] = 0.0f;
+        }
+        for (int k0 = 0; k0 <= last_q; k0 += kKB) {
+            if (!one_chunk || g == 0) {
+                if (k0 > 0) __syncthreads();  // the previous chunk's reads of kt / vs / pt are done
+                for (int idx = tid; idx < kKB * C4; idx += 256) {
+                    const int r = idx % kKB, c4 = idx / kKB, j = k0 + r;
+                    float4 k = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (j < len) k = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd +
+                                                                       kvh * HD + 4 * c4);
+                    kt[(4 * c4 + 0) * kKB + r] = k.x;
+                    kt[(4 * c4 + 1) * kKB + r] = k.y;
+                    kt[(4 * c4 + 2) * kKB + r] = k.z;
+                    kt[(4 * c4 + 3) * kKB + r] = k.w;
                 }
-                __syncwarp();
-                if (p.k_norm) rms_inplace(wrow, HD, p.k_norm, p.eps, lane);
-                rope_neox_inplace(wrow, HD, j, p.rope_cos, p.rope_sin, lane);
-                __syncwarp();
-                for (int d = lane; d < HD; d += 32) kt[d * kKB + r] = wrow[d];
-            } else {
-                for (int d = lane; d < HD; d += 32) {
-                    kt[d * kKB + r] = 0.0f;
-                    vs[r * HD + d] = 0.0f;
+                for (int idx = tid; idx < kKB * C4; idx += 256) {
+                    const int r = idx / C4, c4 = idx % C4, j = k0 + r;
+                    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (j < len) v = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd +
+                                                                       kvd + kvh * HD + 4 * c4);
+                    *reinterpret_cast<float4 *>(vs + r * HD + 4 * c4) = v;
                 }
             }
-            __syncwarp();
-        }
-        __syncthreads();
-        // scores of queries 4ty.. x keys 4tx..
-        float s[4][4];
-#pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int c = 0; c < 4; c++) s[a][c] = 0.0f;
-#pragma unroll 8
-        for (int d = 0; d < HD; d++) {
-            const float4 qv = *reinterpret_cast<const float4 *>(qt + d * kQB + 4 * ty);
-            const float4 kv = *reinterpret_cast<const float4 *>(kt + d * kKB + 4 * tx);
-            const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+            __syncthreads();
+            // scores of queries 4ty.. x keys 4tx..
+            float s[4][4];
 #pragma unroll
             for (int a = 0; a < 4; a++)
 #pragma unroll
-                for (int c = 0; c < 4; c++) s[a][c] = fmaf(qa[a], ka[c], s[a][c]);
+                for (int c = 0; c < 4; c++) s[a][c] = 0.0f;
+#pragma unroll 8
+            for (int d = 0; d < HD; d++) {
+                const float4 qv = *reinterpret_cast<const float4 *>(qt + d * kQB + 4 * ty);
+                const float4 kv = *reinterpret_cast<const float4 *>(kt + d * kKB + 4 * tx);
+                const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                for (int a = 0; a < 4; a++)
+#pragma unroll
+                    for (int c = 0; c < 4; c++) s[a][c] = fmaf(qa[a], ka[c], s[a][c]);
+            }
+            float corr[4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) {
+                const int qi = i0 + 4 * ty + a;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const int kj = k0 + 4 * tx + c;
+                    s[a][c] = (kj <= qi && kj < len) ? s[a][c] * p.scale : -INFINITY;
+                    mx = fmaxf(mx, s[a][c]);
+                }
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                const float mnew = fmaxf(m[a], mx);
+                corr[a] = (m[a] == -INFINITY) ? 0.0f : expf(m[a] - mnew);
+                float sum = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const float e = (s[a][c] == -INFINITY) ? 0.0f : expf(s[a][c] - mnew);
+                    s[a][c] = e;
+                    sum += e;
+                }
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                l[a] = l[a] * corr[a] + sum;
+                m[a] = (mnew == -INFINITY) ? m[a] : mnew;
+            }
+            // P^T [key][query] for the value product
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                *reinterpret_cast<float4 *>(pt + (4 * tx + c) * kQB + 4 * ty) =
+                    make_float4(s[0][c], s[1][c], s[2][c], s[3][c]);
+            __syncthreads();
+#pragma unroll
+            for (int a = 0; a < 4; a++)
+#pragma unroll
+                for (int c = 0; c < DPT; c++) o[a][c] *= corr[a];
+            const int nk = min(kKB, last_q + 1 - k0);
+            for (int k = 0; k < nk; k++) {
+                const float4 pv = *reinterpret_cast<const float4 *>(pt + k * kQB + 4 * ty);
+                const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+                float vv[DPT];
+#pragma unroll
+                for (int c = 0; c < DPT; c += 4) {
+                    const float4 t = *reinterpret_cast<const float4 *>(vs + k * HD + DPT * tx + c);
+                    vv[c] = t.x;
+                    vv[c + 1] = t.y;
+                    vv[c + 2] = t.z;
+                    vv[c + 3] = t.w;
+                }
+#pragma unroll
+                for (int a = 0; a < 4; a++)
+#pragma unroll
+                    for (int c = 0; c < DPT; c++) o[a][c] = fmaf(pa[a], vv[c], o[a][c]);
+            }
         }
-        float corr[4];
 #pragma unroll
         for (int a = 0; a < 4; a++) {
             const int qi = i0 + 4 * ty + a;
-            float mx = -INFINITY;
+            if (qi >= len) continue;
+            const float inv = 1.0f / l[a];
+            uint16_t *dst = p.out + (long long)(start + qi) * qd + h * HD + DPT * tx;
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const int kj = k0 + 4 * tx + c;
-                s[a][c] = (kj <= qi && kj < len) ? s[a][c] * p.scale : -INFINITY;
-                mx = fmaxf(mx, s[a][c]);
-            }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float mnew = fmaxf(m[a], mx);
-            corr[a] = (m[a] == -INFINITY) ? 0.0f : expf(m[a] - mnew);
-            float sum = 0.0f;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const float e = (s[a][c] == -INFINITY) ? 0.0f : expf(s[a][c] - mnew);
-                s[a][c] = e;
-                sum += e;
-            }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            l[a] = l[a] * corr[a] + sum;
-            m[a] = (mnew == -INFINITY) ? m[a] : mnew;
+            for (int c = 0; c < DPT; c += 2)
+                *reinterpret_cast<uint32_t *>(dst + c) = pack_bf16x2(o[a][c] * inv, o[a][c + 1] * inv);
         }
-        // P^T [key][query] for the value product
-#pragma unroll
-        for (int c = 0; c < 4; c++)
-            *reinterpret_cast<float4 *>(pt + (4 * tx + c) * kQB + 4 * ty) = make_float4(s[0][c], s[1][c], s[2][c], s[3][c]);
-        __syncthreads();
-#pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int c = 0; c < DPT; c++) o[a][c] *= corr[a];
-        const int nk = min(kKB, last_q + 1 - k0);
-        for (int k = 0; k < nk; k++) {
-            const float4 pv = *reinterpret_cast<const float4 *>(pt + k * kQB + 4 * ty);
-            const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
-            float vv[DPT];
-#pragma unroll
-            for (int c = 0; c < DPT; c += 4) {
-                const float4 t = *reinterpret_cast<const float4 *>(vs + k * HD + DPT * tx + c);
-                vv[c] = t.x;
-                vv[c + 1] = t.y;
-                vv[c + 2] = t.z;
-                vv[c + 3] = t.w;
-            }
-#pragma unroll
-            for (int a = 0; a < 4; a++)
-#pragma unroll
-                for (int c = 0; c < DPT; c++) o[a][c] = fmaf(pa[a], vv[c], o[a][c]);
-        }
-    }
-#pragma unroll
-    for (int a = 0; a < 4; a++) {
-        const int qi = i0 + 4 * ty + a;
-        if (qi >= len) continue;
-        const float inv = 1.0f / l[a];
-        uint16_t *dst = p.out + (long long)(start + qi) * qd + h * HD + DPT * tx;
-#pragma unroll
-        for (int c = 0; c < DPT; c += 2)
-            *reinterpret_cast<uint32_t *>(dst + c) = pack_bf16x2(o[a][c] * inv, o[a][c + 1] * inv);
     }
 }
 
 template <int HD>
 cudaError_t launch_attention_tiled(const AttnParams &p, cudaStream_t st) {
-    static_assert(8 * HD <= kKB * kQB, "staging rows live in the P buffer");
     const size_t smem = sizeof(float) * (2 * HD * kQB + kKB * HD + kKB * kQB);
     static bool configured = false;
     if (!configured) {
@@ -393,7 +453,12 @@ cudaError_t launch_attention_tiled(const AttnParams &p, cudaStream_t st) {
         configured = true;
     }
     int max_len = p.max_len > 0 ? p.max_len : kQB;
-    dim3 grid(p.n_prompts, p.heads, (max_len + kQB - 1) / kQB);
+    // q / k norm and RoPE in place on the workspace rows (the buffer is the
+    // forward's own QKV output, read only by this attention)
+    k_qk_prep<HD><<<dim3(p.n_prompts, (max_len + 7) / 8), 256, 0, st>>>(const_cast<float *>(p.qkv), p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    dim3 grid(p.n_prompts, p.kv_heads, (max_len + kQB - 1) / kQB);
     k_attention_tiled<HD><<<grid, 256, smem, st>>>(p);
     return cudaGetLastError();
 }
@@ -405,16 +470,37 @@ __global__ void k_rowdot_bf16(const uint16_t *act, const float *a, int m, int k,
     if (row >= m) return;
     const uint16_t *r = act + (long long)row * k;
     float s = 0.0f;
-    if ((k & 7) == 0) {
-        for (int i = lane * 8; i < k; i += 256) {
-            uint4 v = *reinterpret_cast<const uint4 *>(r + i);
+    if ((k & 7) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && (reinterpret_cast<uintptr_t>(act) & 15) == 0) {
+        // four 16-byte loads in flight per lane, four independent sums
+        float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        int i = lane * 8;
+        for (; i + 3 * 256 < k; i += 4 * 256) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) v[u] = __ldg(reinterpret_cast<const uint4 *>(r + i + u * 256));
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                const float4 a0 = __ldg(reinterpret_cast<const float4 *>(a + i + u * 256));
+                const float4 a1 = __ldg(reinterpret_cast<const float4 *>(a + i + u * 256 + 4));
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    t[u] = fmaf(__uint_as_float(w[j] << 16), av[2 * j], t[u]);
+                    t[u] = fmaf(__uint_as_float(w[j] & 0xffff0000u), av[2 * j + 1], t[u]);
+                }
+            }
+        }
+        for (; i < k; i += 256) {
+            uint4 v = __ldg(reinterpret_cast<const uint4 *>(r + i));
             const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                s = fmaf(__uint_as_float(w[j] << 16), a[i + 2 * j], s);
-                s = fmaf(__uint_as_float(w[j] & 0xffff0000u), a[i + 2 * j + 1], s);
+                t[0] = fmaf(__uint_as_float(w[j] << 16), a[i + 2 * j], t[0]);
+                t[0] = fmaf(__uint_as_float(w[j] & 0xffff0000u), a[i + 2 * j + 1], t[0]);
             }
         }
+        s = (t[0] + t[1]) + (t[2] + t[3]);
     } else {
         for (int i = lane; i < k; i += 32) s = fmaf(bf16_bits_to_f32(r[i]), a[i], s);
     }

@@ -41,6 +41,8 @@ struct Layer {
     bool o_edit = false, down_edit = false;
     DevBuf o_a, o_b, down_a, down_b;               // f32 [qd], [H], [I], [H]
     std::vector<uint8_t> e_edit;                   // per expert
+    std::vector<float> e_fro;                      // ||W_down_e||_F per expert (computed once)
+    DevBuf e_proj;                                 // f32 [E][mi]: v^T W_down_e of the last scoring
     DevBuf e_a, e_b;                               // f32 [E][mi], [E][H]
     DevBuf e_edit_dev;                             // int [E]
 };

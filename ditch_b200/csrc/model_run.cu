@@ -354,17 +354,6 @@ int apply_component_edit(ditch_cuda_model *m, int li, bool is_o, const float *v,
     return DITCH_CUDA_OK;
 }
 
-int apply_expert_delta(ditch_cuda_model *m, int li, int e, const float *v, float lambda) {
-    ditch_cuda_device *dev = m->dev;
-    Layer &L = m->layers[li];
-    const int H = m->cfg.hidden, mi = L.e_down.cols;  // the stored (8-aligned) width
-    int s;
-    if ((s = gemv_t_mat(m, L.e_down, e * H, H, v, L.e_a.as<float>() + (size_t)e * mi))) return s;
-    DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.e_b.as<float>() + (size_t)e * H, dev->stream));
-    L.e_edit[e] = 1;
-    return DITCH_CUDA_OK;
-}
-
 int upload_expert_flags(ditch_cuda_model *m) {
     for (Layer &L : m->layers) {
         if (!L.moe) continue;
@@ -397,17 +386,35 @@ int prepare_direction(ditch_cuda_model *m, float di, bool use_di) {
     return DITCH_CUDA_OK;
 }
 
-// Scores of every routed expert of `li` against v (device f32 [H]).
-int expert_scores(ditch_cuda_model *m, int li, const float *v, std::vector<float> &scores) {
+// A_e = v^T W_down_e for every routed expert of `li` into L.e_proj [E][mi]
+// (v device f32 [H]); one launch over the whole MXFP4 stack.
+int expert_projections(ditch_cuda_model *m, int li, const float *v) {
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
     const int E = m->cfg.n_experts, H = m->cfg.hidden, mi = L.e_down.cols;  // the stored (8-aligned) width
-    DevBuf proj, norms;
-    DITCH_CUDA(proj.reserve((size_t)E * mi * 4));
-    DITCH_CUDA(norms.reserve((size_t)E * H * 4));
+    DITCH_CUDA(L.e_proj.reserve((size_t)E * mi * 4));
+    float *proj = L.e_proj.as<float>();
+    if (L.e_down.fmt == kFmtMxfp4) {
+        DITCH_CUDA(cudaMemsetAsync(proj, 0, (size_t)E * mi * 4, dev->stream));
+        DITCH_LAUNCH(dev, gemv_t_mxfp4_stack(L.e_down.data.as<uint8_t>(), L.e_down.scales.as<uint8_t>(), E, H, mi, v,
+                                             proj, dev->stream));
+        return DITCH_CUDA_OK;
+    }
     int s;
     for (int e = 0; e < E; e++)
-        if ((s = gemv_t_mat(m, L.e_down, e * H, H, v, proj.as<float>() + (size_t)e * mi))) return s;
+        if ((s = gemv_t_mat(m, L.e_down, e * H, H, v, proj + (size_t)e * mi))) return s;
+    return DITCH_CUDA_OK;
+}
+
+// ||W_down_e||_F of every routed expert of `li`, once per model (the base
+// weights never change; edits are kept as separate deltas).
+int expert_frobenius(ditch_cuda_model *m, int li) {
+    ditch_cuda_device *dev = m->dev;
+    Layer &L = m->layers[li];
+    const int E = m->cfg.n_experts, H = m->cfg.hidden, mi = L.e_down.cols;
+    if ((int)L.e_fro.size() == E) return DITCH_CUDA_OK;
+    DevBuf norms;
+    DITCH_CUDA(norms.reserve((size_t)E * H * 4));
     const Mat &w = L.e_down;
     if (w.fmt == kFmtBf16) {
         DITCH_LAUNCH(dev, row_norms_bf16(w.data.as<uint16_t>(), E * H, mi, norms.as<float>(), dev->stream));
@@ -431,18 +438,51 @@ int expert_scores(ditch_cuda_model *m, int li, const float *v, std::vector<float
             DITCH_LAUNCH(dev, row_norms_bf16(tmp.as<uint16_t>(), H, mi, norms.as<float>() + (size_t)e * H, dev->stream));
         }
     }
-    std::vector<float> hp((size_t)E * mi), hn((size_t)E * H);
-    DITCH_CUDA(cudaMemcpyAsync(hp.data(), proj.ptr, hp.size() * 4, cudaMemcpyDeviceToHost, dev->stream));
+    std::vector<float> hn((size_t)E * H);
     DITCH_CUDA(cudaMemcpyAsync(hn.data(), norms.ptr, hn.size() * 4, cudaMemcpyDeviceToHost, dev->stream));
+    DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+    L.e_fro.assign(E, 0.0f);
+    for (int e = 0; e < E; e++) {
+        float fro = 0.0f;
+        for (int r = 0; r < H; r++) fro = std::fma(hn[(size_t)e * H + r], hn[(size_t)e * H + r], fro);
+        L.e_fro[e] = std::sqrt(fro);
+    }
+    return DITCH_CUDA_OK;
+}
+
+// Scores of every routed expert of `li` against v (device f32 [H]):
+// ||v^T W_down_e|| / ||W_down_e||_F (src/moe.zig:1239-1283). Leaves the
+// projections in L.e_proj for the edit of the selected experts.
+int expert_scores(ditch_cuda_model *m, int li, const float *v, std::vector<float> &scores) {
+    ditch_cuda_device *dev = m->dev;
+    Layer &L = m->layers[li];
+    const int E = m->cfg.n_experts, mi = L.e_down.cols;
+    int s;
+    if ((s = expert_frobenius(m, li))) return s;
+    if ((s = expert_projections(m, li, v))) return s;
+    std::vector<float> hp((size_t)E * mi);
+    DITCH_CUDA(cudaMemcpyAsync(hp.data(), L.e_proj.ptr, hp.size() * 4, cudaMemcpyDeviceToHost, dev->stream));
     DITCH_CUDA(cudaStreamSynchronize(dev->stream));
     scores.assign(E, 0.0f);
     for (int e = 0; e < E; e++) {
-        float fro = 0.0f, pn = 0.0f;
-        for (int r = 0; r < H; r++) fro = std::fma(hn[(size_t)e * H + r], hn[(size_t)e * H + r], fro);
+        float pn = 0.0f;
         for (int j = 0; j < mi; j++) pn = std::fma(hp[(size_t)e * mi + j], hp[(size_t)e * mi + j], pn);
-        fro = std::sqrt(fro);
+        const float fro = L.e_fro[e];
         scores[e] = fro > 0 ? std::sqrt(pn) / fro : 0.0f;
     }
+    return DITCH_CUDA_OK;
+}
+
+// The none-mode delta of expert e from its projection in L.e_proj:
+// a = v^T W_down_e, b = -lambda v, stored as (a, lambda v) for the epilogue.
+int expert_delta_from_proj(ditch_cuda_model *m, int li, int e, const float *v, float lambda) {
+    ditch_cuda_device *dev = m->dev;
+    Layer &L = m->layers[li];
+    const int H = m->cfg.hidden, mi = L.e_down.cols;
+    DITCH_CUDA(cudaMemcpyAsync(L.e_a.as<float>() + (size_t)e * mi, L.e_proj.as<float>() + (size_t)e * mi,
+                               (size_t)mi * 4, cudaMemcpyDeviceToDevice, dev->stream));
+    DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.e_b.as<float>() + (size_t)e * H, dev->stream));
+    L.e_edit[e] = 1;
     return DITCH_CUDA_OK;
 }
 
@@ -475,8 +515,9 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
         }
         const int E = c.n_experts;
         if (!selective || n_experts == 0) {
+            if ((s = expert_projections(m, li, v))) return s;
             for (int e = 0; e < E; e++)
-                if ((s = apply_expert_delta(m, li, e, v, lambda))) return s;
+                if ((s = expert_delta_from_proj(m, li, e, v, lambda))) return s;
             continue;
         }
         const float weight = std::max(0.0f, lambda * strength);
@@ -486,7 +527,7 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
         if ((s = expert_scores(m, li, v, scores))) return s;
         std::vector<uint32_t> order = rank(scores);
         for (size_t j = 0; j < n; j++)
-            if ((s = apply_expert_delta(m, li, (int)order[j], v, weight))) return s;
+            if ((s = expert_delta_from_proj(m, li, (int)order[j], v, weight))) return s;
     }
     if ((s = upload_expert_flags(m))) return s;
     return check_status(m->dev, "apply_edit");
