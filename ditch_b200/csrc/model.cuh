@@ -87,7 +87,7 @@ struct ditch_cuda_model {
     ditch::DevBuf res, hl, logits;
     // MoE workspace
     ditch::DevBuf moe_h3, moe_logits, moe_sel, moe_w, moe_counts, moe_offsets, moe_perm, moe_pw, moe_pexp, moe_slot,
-        moe_xg, moe_act, moe_eo, moe_xa, moe_sched_gu, moe_sched_d, moe_nsched;
+        moe_xg, moe_act, moe_eo, moe_xa, moe_sched_gu, moe_sched_d, moe_nsched, moe_cc;
     // directions
     ditch::DevBuf dirs;
     std::vector<float> h_dirs;

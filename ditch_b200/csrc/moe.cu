@@ -123,8 +123,33 @@ __global__ void k_route(const float *logits, int n, int E, int k, int norm_topk,
     }
 }
 
-__global__ void k_count(const int *sel, int nk, int *counts) {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nk; i += gridDim.x * blockDim.x) atomicAdd(counts + sel[i], 1);
+// Selections are bucketed by expert in chunks of kChunk (token-major order):
+// per-chunk histograms, then per expert an exclusive prefix over chunks, so
+// the scatter places every selection with one pass and the order within an
+// expert stays the selection order (tokens ascending, as src/moe.zig gathers).
+constexpr int kChunk = 256;
+
+__global__ void k_chunk_counts(const int *sel, int nk, int E, int *cc) {
+    extern __shared__ int hist[];  // [E]
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
+    const int i = blockIdx.x * kChunk + threadIdx.x;
+    if (i < nk) atomicAdd(&hist[sel[i]], 1);
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cc[(long long)blockIdx.x * E + e] = hist[e];
+}
+
+// In place: cc[c][e] <- sum of cc[c'][e] for c' < c; counts[e] = the total.
+__global__ void k_chunk_prefix(int *cc, int chunks, int E, int *counts) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= E) return;
+    int run = 0;
+    for (int c = 0; c < chunks; c++) {
+        const int t = cc[(long long)c * E + e];
+        cc[(long long)c * E + e] = run;
+        run += t;
+    }
+    counts[e] = run;
 }
 
 // One block: expert offsets and the two grouped-GEMM tile schedules
@@ -166,36 +191,39 @@ __global__ void k_schedule(const int *counts, int E, int bn_gu, int wt_gu, int b
 
 // Stable scatter: block e walks all (token, slot) pairs in order and places
 // those routed to expert e at offsets[e] + rank.
-__global__ void k_scatter(const int *sel, const float *wts, int nk, int k, const int *offsets, int *perm, float *pw,
-                          int *pexp, int *slot) {
-    __shared__ int warp_tot[32];
-    __shared__ int base;
-    const int e = blockIdx.x;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    if (threadIdx.x == 0) base = offsets[e];
+// One block of kChunk threads per chunk: thread i's rank among the equal
+// experts of its warp (match_any), plus the counts of the earlier warps of the
+// chunk, plus the chunk's base in the expert's segment.
+__global__ void __launch_bounds__(kChunk) k_scatter(const int *sel, const float *wts, int nk, int k, int E,
+                                                    const int *cc, const int *offsets, int *perm, float *pw,
+                                                    int *pexp, int *slot) {
+    extern __shared__ int cnt[];  // [kChunk / 32][E]
+    constexpr int kW = kChunk / 32;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int j = threadIdx.x; j < kW * E; j += kChunk) cnt[j] = 0;
     __syncthreads();
-    for (int i0 = 0; i0 < nk; i0 += blockDim.x) {
-        const int i = i0 + threadIdx.x;
-        const bool hit = i < nk && sel[i] == e;
-        const unsigned ball = __ballot_sync(0xffffffffu, hit);
-        const int within = __popc(ball & ((1u << lane) - 1));
-        if (lane == 0) warp_tot[w] = __popc(ball);
-        __syncthreads();
-        int before = 0, total = 0;
-        for (int j = 0; j < nw; j++) {
-            if (j < w) before += warp_tot[j];
-            total += warp_tot[j];
+    const int i = blockIdx.x * kChunk + threadIdx.x;
+    const bool valid = i < nk;
+    const int e = valid ? sel[i] : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(same & ((1u << lane) - 1));
+    if (valid && rank == 0) cnt[w * E + e] = __popc(same);
+    __syncthreads();
+    for (int x = threadIdx.x; x < E; x += kChunk) {  // exclusive prefix over the warps
+        int run = 0;
+        for (int ww = 0; ww < kW; ww++) {
+            const int t = cnt[ww * E + x];
+            cnt[ww * E + x] = run;
+            run += t;
         }
-        if (hit) {
-            const int pos = base + before + within;
-            perm[pos] = i / k;
-            pw[pos] = wts[i];
-            pexp[pos] = e;
-            slot[i] = pos;
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) base += total;
-        __syncthreads();
+    }
+    __syncthreads();
+    if (valid) {
+        const int pos = offsets[e] + cc[(long long)blockIdx.x * E + e] + cnt[w * E + e] + rank;
+        perm[pos] = i / k;
+        pw[pos] = wts[i];
+        pexp[pos] = e;
+        slot[i] = pos;
     }
 }
 
@@ -239,9 +267,10 @@ __global__ void k_rowdot_grouped(const uint16_t *act, const float *e_a, const in
 __global__ void k_combine(const float *eo, const int *sel, const float *wts, const int *slot, int n, int k, int hidden,
                           float *x) {
     const int t = blockIdx.x;
-    __shared__ int order[16];
+    __shared__ int s_slot[16];
+    __shared__ float s_w[16];
     if (threadIdx.x == 0) {
-        int e[16];
+        int order[16], e[16];
         for (int q = 0; q < k; q++) {
             order[q] = q;
             e[q] = sel[(long long)t * k + q];
@@ -257,16 +286,36 @@ __global__ void k_combine(const float *eo, const int *sel, const float *wts, con
             e[b] = ev;
             order[b] = oq;
         }
+        for (int q = 0; q < k; q++) {
+            s_slot[q] = slot[(long long)t * k + order[q]];
+            s_w[q] = wts[(long long)t * k + order[q]];
+        }
     }
     __syncthreads();
     float *xr = x + (long long)t * hidden;
+    if ((hidden & 3) == 0) {
+        for (int i = threadIdx.x * 4; i < hidden; i += blockDim.x * 4) {
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int q = 0; q < k; q++) {
+                const float wq = s_w[q];
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(eo + (long long)s_slot[q] * hidden + i));
+                acc.x = acc.x + wq * v.x;
+                acc.y = acc.y + wq * v.y;
+                acc.z = acc.z + wq * v.z;
+                acc.w = acc.w + wq * v.w;
+            }
+            float4 xv = *reinterpret_cast<const float4 *>(xr + i);
+            xv.x = xv.x + acc.x;
+            xv.y = xv.y + acc.y;
+            xv.z = xv.z + acc.z;
+            xv.w = xv.w + acc.w;
+            *reinterpret_cast<float4 *>(xr + i) = xv;
+        }
+        return;
+    }
     for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
         float acc = 0.0f;
-        for (int q = 0; q < k; q++) {
-            const int j = order[q];
-            const long long idx = (long long)t * k + j;
-            acc = acc + wts[idx] * eo[(long long)slot[idx] * hidden + i];
-        }
+        for (int q = 0; q < k; q++) acc = acc + s_w[q] * eo[(long long)s_slot[q] * hidden + i];
         xr[i] = xr[i] + acc;
     }
 }
@@ -318,6 +367,7 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     DITCH_CUDA(m->moe_sel.reserve((size_t)nk * 4));
     DITCH_CUDA(m->moe_w.reserve((size_t)nk * 4));
     DITCH_CUDA(m->moe_counts.reserve((size_t)E * 4));
+    DITCH_CUDA(m->moe_cc.reserve((size_t)((nk + kChunk - 1) / kChunk) * E * 4));
     DITCH_CUDA(m->moe_offsets.reserve((size_t)(E + 1) * 4 + 8));
     DITCH_CUDA(m->moe_perm.reserve((size_t)nk * 4));
     DITCH_CUDA(m->moe_pw.reserve((size_t)nk * 4));
@@ -342,15 +392,17 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     k_route<<<(n + 7) / 8, 256, 0, st>>>(m->moe_logits.as<float>(), n, E, k, c.norm_topk, m->moe_sel.as<int>(),
                                          m->moe_w.as<float>());
     DITCH_LAUNCH(dev, cudaGetLastError());
-    DITCH_CUDA(cudaMemsetAsync(m->moe_counts.ptr, 0, (size_t)E * 4, st));
-    k_count<<<std::min((nk + 255) / 256, 1024), 256, 0, st>>>(m->moe_sel.as<int>(), nk, m->moe_counts.as<int>());
+    const int chunks = (nk + kChunk - 1) / kChunk;
+    k_chunk_counts<<<chunks, kChunk, (size_t)E * 4, st>>>(m->moe_sel.as<int>(), nk, E, m->moe_cc.as<int>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    k_chunk_prefix<<<(E + 127) / 128, 128, 0, st>>>(m->moe_cc.as<int>(), chunks, E, m->moe_counts.as<int>());
     DITCH_LAUNCH(dev, cudaGetLastError());
     k_schedule<<<1, 1024, 0, st>>>(m->moe_counts.as<int>(), E, bn_gu, wt_gu, bn_d, wt_d, m->moe_offsets.as<int>(),
                                    m->moe_sched_gu.as<int4>(), n_gu, m->moe_sched_d.as<int4>(), n_d);
     DITCH_LAUNCH(dev, cudaGetLastError());
-    k_scatter<<<E, 512, 0, st>>>(m->moe_sel.as<int>(), m->moe_w.as<float>(), nk, k, m->moe_offsets.as<int>(),
-                                 m->moe_perm.as<int>(), m->moe_pw.as<float>(), m->moe_pexp.as<int>(),
-                                 m->moe_slot.as<int>());
+    k_scatter<<<chunks, kChunk, (size_t)(kChunk / 32) * E * 4, st>>>(
+        m->moe_sel.as<int>(), m->moe_w.as<float>(), nk, k, E, m->moe_cc.as<int>(), m->moe_offsets.as<int>(),
+        m->moe_perm.as<int>(), m->moe_pw.as<float>(), m->moe_pexp.as<int>(), m->moe_slot.as<int>());
     DITCH_LAUNCH(dev, cudaGetLastError());
     k_gather_rows<<<(nk + 7) / 8, 256, 0, st>>>(m->moe_h3.as<uint16_t>(), 3LL * cp, m->moe_perm.as<int>(), nk, H,
                                                 m->moe_xg.as<uint16_t>());
