@@ -49,8 +49,9 @@ def parse():
     ap.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline sample budget (seconds)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5", "gemm"],
-                    help="c2 (default): the FP8 dense trial loop; c3: dequant + GEMM sweep; c4: the Qwen3-MoE MXFP4 "
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4", "c5", "gemm"],
+                    help="c2 (default): the FP8 dense trial loop; c1: the Qwen2-0.5B fp32 trial loop with the "
+                         "whole-trial CPU baseline; c3: dequant + GEMM sweep; c4: the Qwen3-MoE MXFP4 "
                          "trial loop (expert-selective edit); c5: Llama-3-70B-shaped in-place edit sweep; gemm: one "
                          "GEMM")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
@@ -91,7 +92,7 @@ def trial_params(rng, n_layers):
         max_w = float(rng.uniform(0.8, 1.5))
         max_pos = float(rng.uniform(0.6 * (n_layers - 1), n_layers - 1))
         min_frac = float(rng.uniform(0.0, 1.0))
-        min_dist = float(rng.uniform(1.0, 0.6 * (n_layers - 1)))
+        min_dist = float(rng.uniform(1.0, max(1.0, 0.6 * (n_layers - 1))))
         out.append((max_w, max_pos, min_frac * max_w, min_dist))
     scope_global = rng.random() < 0.5
     di = float(rng.uniform(0.4, 0.9) * (n_layers - 1)) if scope_global else None

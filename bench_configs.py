@@ -9,6 +9,13 @@
 * `c5`: the in-place rank-1 edit W <- W - alpha_l r_l (r_l^T W) on all 80
   o_proj [8192 x 8192] and down_proj [8192 x 28672] bf16 matrices of a
   Llama-3-70B shape. It reports HBM GB/s over the algorithmic 3 x 48.32 GB.
+* `c1`: BASELINE config 1, the Qwen2-0.5B-shaped fp32 model (24 layers,
+  hidden 896, 14/2 heads of 64, SwiGLU 4864, vocab 151936, q/k/v biases, tied
+  embedding, seeded N(0, 0.02) f32 weights) with two batches of 64 prompts x
+  48 tokens: capture, directions, then per trial the none-mode edit of
+  o_proj / down_proj and the KL forward of the first batch. The CPU baseline
+  is ditch's engine restated in C (the oracle) timed on one whole trial of
+  the same workload (the edit GEMVs, the forward with the deltas, the KL).
 * `c4`: the Qwen3-MoE-shaped trial loop of BASELINE config 4 on one GPU: 48
   layers, hidden 2048, 32/4 heads of 128 with q/k norms, 128 routed experts
   (top-8 softmax, renormalised) of intermediate 768 stored as MXFP4, bf16
@@ -284,6 +291,150 @@ def run_c5(args, dev):
           flush=True)
 
 
+C1 = dict(n_layers=24, hidden=896, heads=14, kv_heads=2, head_dim=64, inter=4864, vocab=151936, eps=1e-6,
+          rope_theta=1e6, tied=True)
+
+
+def c1_weights(seed, n_layers):
+    rng = np.random.default_rng(seed)
+    s = C1
+    H, I, qd, kvd = s["hidden"], s["inter"], s["heads"] * s["head_dim"], s["kv_heads"] * s["head_dim"]
+
+    def w(*shape):
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+
+    out = {"embed": w(s["vocab"], H), "final_norm": np.ones(H, np.float32)}
+    out["lm_head"] = out["embed"]
+    for i in range(n_layers):
+        out.update({f"L{i}.input_norm": np.ones(H, np.float32), f"L{i}.post_norm": np.ones(H, np.float32),
+                    f"L{i}.q": w(qd, H), f"L{i}.k": w(kvd, H), f"L{i}.v": w(kvd, H), f"L{i}.o": w(H, qd),
+                    f"L{i}.qb": w(qd), f"L{i}.kb": w(kvd), f"L{i}.vb": w(kvd), f"L{i}.gate": w(I, H),
+                    f"L{i}.up": w(I, H), f"L{i}.down": w(H, I)})
+    return out
+
+
+def c1_cpu_trial(spec, w, dirs, good, po, pd, reps):
+    """One C1 trial on ditch's CPU engine restated (oracle): the none-mode
+    delta of every o_proj / down_proj with a kernel weight (A = v^T W on the
+    CPU), the forward of the KL batch with the deltas, log-softmax and KL."""
+    import oracle
+    from oracle.model import OracleModel, flatten_batch
+
+    m = OracleModel(spec, w)
+    toks, rb, rp, cap, first, take, last = flatten_batch(good, 1)
+    _, base = m.forward(toks, rb, rp, (), last)
+    lb = oracle.log_softmax(base)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        m.reset_deltas()
+        for li in range(spec["n_layers"]):
+            for comp, p, name in (("o", po, f"L{li}.o"), ("down", pd, f"L{li}.down")):
+                lam = oracle.kernel_weight(p, li)
+                if lam is not None:
+                    a, b = oracle.compute_delta_none(w[name], dirs[li + 1], lam)
+                    m.set_delta(li, comp, a, b)
+        _, logits = m.forward(toks, rb, rp, (), last)
+        kl, _ = oracle.kl_first_token(lb, logits)
+    return (time.perf_counter() - t0) / reps, kl, oracle.lib().or_get_threads()
+
+
+def run_c1(args, dev):
+    import torch
+
+    import ditch_b200
+    from bench import Clocks, measured_peaks, trial_params
+
+    L = args.layers or C1["n_layers"]
+    spec = dict(C1, n_layers=L)
+    P, S = args.prompts or 64, 48
+    t0 = time.time()
+    w = c1_weights(args.seed, L)
+    tensors = []
+    for name, a in w.items():
+        rows, cols = (a.shape[0], 1) if a.ndim == 1 else a.shape
+        tensors.append(ditch_b200.Tensor(name, "f32", rows, cols, a))
+    model = ditch_b200.Model(dev, spec, tensors, max_seq=S)
+    load_s = time.time() - t0
+    rng = np.random.default_rng(args.seed + 1)
+    good = [rng.integers(0, spec["vocab"], S).astype(np.uint32) for _ in range(P)]
+    bad = [rng.integers(0, spec["vocab"], S).astype(np.uint32) for _ in range(P)]
+    dev.synchronize()
+    dev.timer_start()
+    gs, gc = model.residual_sums(good, window=1, batch_size=P)
+    bs, bc = model.residual_sums(bad, window=1, batch_size=P)
+    dirs = model.directions(gs, gc, bs, bc, True)
+    capture_ms = dev.timer_stop()
+    model.kl_init(good)
+    tokens_flat = np.concatenate(good).astype(np.uint32)
+    offs = np.zeros(P + 1, np.uintp)
+    offs[1:] = np.cumsum([len(p) for p in good])
+    trial_rng = np.random.default_rng(args.seed + 7)
+    kls, trials = [], []
+
+    def step(e2e):
+        po, pd, di = trial_params(trial_rng, L)
+        trials.append((po, pd))
+        model.apply_edit(po, pd, None)
+        kls.append(model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score())
+
+    def timed(e2e, steps):
+        torch.cuda.synchronize()
+        dev.synchronize()
+        dev.timer_start()
+        for _ in range(steps):
+            step(e2e)
+        return dev.timer_stop()
+
+    for _ in range(args.warmup):
+        step(False)
+    dev.set_profiling(True)
+    dev.reset_stats()
+    clocks = Clocks(0)
+    ms = timed(False, args.steps)
+    clk = clocks.stop()
+    gemm_ms, gemm_launches, gemm_flops = dev.gemm_stats()
+    launches = dev.launches()
+    dev.set_profiling(False)
+    for _ in range(max(1, args.warmup // 2)):
+        step(True)
+    ms_e2e = timed(True, args.steps)
+    hbm, tf_burst, tf_sust, src = measured_peaks()
+    tokens = P * S
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
+    line = {
+        "metric": "trial-eval forward tokens/s", "value": round(tokens * args.steps / (ms / 1000.0), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3), "s_per_trial": round(ms / args.steps / 1000.0, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 weights run as bf16 MMA with f32 accumulate", "data": "synthetic",
+        "config": {"workload": "C1: Qwen2-0.5B-shaped fp32, trial = none-mode rank-1 edit of o_proj/down_proj + "
+                               "edited forward + first-token KL over 151936 logits",
+                   "layers": L, "prompts_per_gpu": P, "seq_len": S, "vocab": spec["vocab"], "parallelism": "dp1",
+                   "l2": "weights 0.7 GB bf16 + logits; the working set exceeds L2"},
+        "e2e": {"value": round(tokens * args.steps / (ms_e2e / 1000.0), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(tokens * 4 + (P + 1) * 8), "d2h_bytes_per_step": 8,
+                "ms_per_step": round(ms_e2e / args.steps, 3)},
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel: tcgen05 bf16 MMA", "achieved": round(achieved, 1),
+                     "peak": tf_sust, "unit": "TFLOP/s", "frac": round(achieved / tf_sust, 4),
+                     "peak_source": f"{src} bf16 sustained", "traffic": None,
+                     "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
+                     "gemm_share_of_step": round(gemm_ms / ms, 4) if ms > 0 else None},
+        "gpu_launches": int(launches), "clocks": clk,
+        "one_off": {"load_s": round(load_s, 2), "capture_and_directions_ms": round(capture_ms, 2)},
+        "kl_last": kls[-1] if kls else None,
+    }
+    if not args.no_cpu_baseline:
+        po, pd = trials[-1]
+        cpu_s, cpu_kl, cores = c1_cpu_trial(spec, w, dirs, good, po, pd, 1)
+        line["cpu_baseline"] = {"value": round(tokens / cpu_s, 2), "unit": "tokens/s", "cores": cores,
+                                "kind": "port", "s_per_trial": round(cpu_s, 3),
+                                "sample": f"one whole C1 trial (edit GEMVs, forward of {P} x {S} tokens with "
+                                          f"the deltas, KL over {spec['vocab']} logits) on the oracle",
+                                "kl": cpu_kl, "kl_device_same_trial": kls[-1]}
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
 C4 = dict(n_layers=48, hidden=2048, heads=32, kv_heads=4, head_dim=128, inter=768, vocab=151936, eps=1e-6,
           rope_theta=1e6, qk_norm=1, n_experts=128, top_k=8, moe_inter=768, norm_topk=1)
 
@@ -453,6 +604,8 @@ def run(args):
         dev.set_decode_staging(args.stage_min_tokens)
     if args.config == "gemm":
         run_gemm(args, dev)
+    elif args.config == "c1":
+        run_c1(args, dev)
     elif args.config == "c3":
         run_c3(args, dev)
     elif args.config == "c4":

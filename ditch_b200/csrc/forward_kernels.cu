@@ -286,15 +286,17 @@ __global__ void __launch_bounds__(256) k_qk_prep(float *qkv, AttnParams p) {
 }
 
 // ---- register-tiled attention for head_dim 64 / 128 ----------------------
-// Block = (prompt, kv head, chunk of 64 query positions); 256 threads; the
-// group's query heads one after another, so a prompt whose keys fit one
-// 64-key chunk stages K and V once for the whole group. Q (64 rows) and each
+// Block = (prompt, kv head and part of its group, chunk of 64 query
+// positions); 256 threads; up to kMaxHeads query heads of the group one after
+// another, so a prompt whose keys fit one 64-key chunk stages K and V once
+// for them. Q (64 rows) and each
 // 64-key chunk of K are staged transposed in f32 shared memory (rows across
 // lanes: conflict-free), V natural, from rows already normed and roped.
 // Scores: thread (ty, tx) owns queries 4ty..4ty+3 x keys 4tx..4tx+3 (two
 // LDS.128 per 16 FMAs); the output: the same 4 queries x HD/16 dimensions.
 // Online softmax across key chunks, f32.
 constexpr int kQB = 64, kKB = 64;
+constexpr int kMaxHeads = 4;  // query heads per block
 
 template <int HD>
 __global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
@@ -303,10 +305,15 @@ __global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
     float *kt = qt + HD * kQB;         // [HD][kKB]
     float *vs = kt + HD * kKB;         // [kKB][HD]
     float *pt = vs + kKB * HD;         // [kKB][kQB]
-    const int b = blockIdx.x, kvh = blockIdx.y, i0 = blockIdx.z * kQB;
+    const int nh = p.heads, nkv = p.kv_heads, groups = nh / nkv;
+    // blockIdx.y = (kv head, part): a group wider than kMaxHeads query heads
+    // is split over several blocks (each stages its own K / V)
+    const int parts = (groups + kMaxHeads - 1) / kMaxHeads;
+    const int kvh = blockIdx.y / parts, part = blockIdx.y % parts;
+    const int g0 = part * kMaxHeads, g1 = min(groups, g0 + kMaxHeads);
+    const int b = blockIdx.x, i0 = blockIdx.z * kQB;
     const int start = p.seq_start[b], len = p.seq_len[b];
     if (i0 >= len) return;
-    const int nh = p.heads, nkv = p.kv_heads, groups = nh / nkv;
     const int qd = nh * HD, kvd = nkv * HD, width = qd + 2 * kvd;
     const int tid = threadIdx.x;
     const int ty = tid >> 4, tx = tid & 15;
@@ -315,7 +322,7 @@ __global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
     const int last_q = min(len, i0 + kQB) - 1;  // causal: keys 0 .. last_q
     const bool one_chunk = last_q < kKB;
 
-    for (int g = 0; g < groups; g++) {
+    for (int g = g0; g < g1; g++) {
         const int h = kvh * groups + g;
         __syncthreads();  // the previous head's reads of the buffers are done
         for (int idx = tid; idx < kQB * C4; idx += 256) {
@@ -336,7 +343,7 @@ __global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
             for (int c = 0; c < DPT; c++) o[a][c] = 0.0f;
         }
         for (int k0 = 0; k0 <= last_q; k0 += kKB) {
-            if (!one_chunk || g == 0) {
+            if (!one_chunk || g == g0) {
                 if (k0 > 0) __syncthreads();  // the previous chunk's reads of kt / vs / pt are done
                 for (int idx = tid; idx < kKB * C4; idx += 256) {
                     const int r = idx % kKB, c4 = idx / kKB, j = k0 + r;
@@ -458,7 +465,8 @@ cudaError_t launch_attention_tiled(const AttnParams &p, cudaStream_t st) {
     k_qk_prep<HD><<<dim3(p.n_prompts, (max_len + 7) / 8), 256, 0, st>>>(const_cast<float *>(p.qkv), p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    dim3 grid(p.n_prompts, p.kv_heads, (max_len + kQB - 1) / kQB);
+    const int groups = p.heads / p.kv_heads, parts = (groups + kMaxHeads - 1) / kMaxHeads;
+    dim3 grid(p.n_prompts, p.kv_heads * parts, (max_len + kQB - 1) / kQB);
     k_attention_tiled<HD><<<grid, 256, smem, st>>>(p);
     return cudaGetLastError();
 }

@@ -140,16 +140,37 @@ __global__ void k_chunk_counts(const int *sel, int nk, int E, int *cc) {
 }
 
 // In place: cc[c][e] <- sum of cc[c'][e] for c' < c; counts[e] = the total.
-__global__ void k_chunk_prefix(int *cc, int chunks, int E, int *counts) {
-    const int e = blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= E) return;
+// One block per expert: each thread sums a run of consecutive chunks, a block
+// scan turns the run sums into run bases, and the runs are rewritten.
+__global__ void __launch_bounds__(256) k_chunk_prefix(int *cc, int chunks, int E, int *counts) {
+    __shared__ int warp_tot[8];
+    const int e = blockIdx.x;
+    const int per = (chunks + 255) / 256;
+    const int c0 = threadIdx.x * per, c1 = min(chunks, c0 + per);
     int run = 0;
-    for (int c = 0; c < chunks; c++) {
-        const int t = cc[(long long)c * E + e];
-        cc[(long long)c * E + e] = run;
-        run += t;
+    for (int c = c0; c < c1; c++) run += cc[(long long)c * E + e];
+    // exclusive scan of the run sums across the block
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
     }
-    counts[e] = run;
+    if (lane == 31) warp_tot[w] = incl;
+    __syncthreads();
+    int base = 0, total = 0;
+    for (int j = 0; j < 8; j++) {
+        if (j < w) base += warp_tot[j];
+        total += warp_tot[j];
+    }
+    int acc = base + incl - run;
+    for (int c = c0; c < c1; c++) {
+        const int t = cc[(long long)c * E + e];
+        cc[(long long)c * E + e] = acc;
+        acc += t;
+    }
+    if (threadIdx.x == 0) counts[e] = total;
 }
 
 // One block: expert offsets and the two grouped-GEMM tile schedules
@@ -395,7 +416,7 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     const int chunks = (nk + kChunk - 1) / kChunk;
     k_chunk_counts<<<chunks, kChunk, (size_t)E * 4, st>>>(m->moe_sel.as<int>(), nk, E, m->moe_cc.as<int>());
     DITCH_LAUNCH(dev, cudaGetLastError());
-    k_chunk_prefix<<<(E + 127) / 128, 128, 0, st>>>(m->moe_cc.as<int>(), chunks, E, m->moe_counts.as<int>());
+    k_chunk_prefix<<<E, 256, 0, st>>>(m->moe_cc.as<int>(), chunks, E, m->moe_counts.as<int>());
     DITCH_LAUNCH(dev, cudaGetLastError());
     k_schedule<<<1, 1024, 0, st>>>(m->moe_counts.as<int>(), E, bn_gu, wt_gu, bn_d, wt_d, m->moe_offsets.as<int>(),
                                    m->moe_sched_gu.as<int4>(), n_gu, m->moe_sched_d.as<int4>(), n_d);
