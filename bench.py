@@ -215,7 +215,16 @@ def measured_peaks():
 
 
 # ---- CPU baseline: the oracle (a C restatement of ditch's CPU engine) ----
-def cpu_baseline(args, prompts=None):
+def host_threads():
+    """Host threads this process may run on (torchrun sets OMP_NUM_THREADS=1
+    for its workers; the CPU baseline uses every core it is allowed)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(args, reps=None, warmup=0):
     """Times ditch's CPU engine restated in C (oracle/, f32, VL=16 FMA, all
     host threads) on a bounded sample: one decoder layer of the C2 shape over
     a few prompts, the LM head rows, the per-layer edit GEMVs and the KL rows,
@@ -226,6 +235,7 @@ def cpu_baseline(args, prompts=None):
     from oracle.model import OracleModel, flatten_batch
 
     L = oracle.lib()
+    L.or_set_threads(host_threads())
     cores = L.or_get_threads()
     spec = dict(C2, n_layers=1)
     H, I, V = spec["hidden"], spec["inter"], spec["vocab"]
@@ -244,13 +254,17 @@ def cpu_baseline(args, prompts=None):
     p_cpu = 2
     sample = [rng.integers(0, V, args.seq).astype(np.uint32) for _ in range(p_cpu)]
     toks, rb, rp, cap, first, take, last = flatten_batch(sample)
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
+    for _ in range(warmup):
         m.forward(toks, rb, rp, (), ())
-        reps += 1
-        if time.perf_counter() - t0 > args.cpu_sample_s * 0.5 or reps >= 8:
+    t0 = time.perf_counter()
+    n = 0
+    while True:  # `reps` timed samples, or as many as fit half the sample budget (at most 8)
+        m.forward(toks, rb, rp, (), ())
+        n += 1
+        if (reps is not None and n >= reps) or (reps is None and (time.perf_counter() - t0 > args.cpu_sample_s * 0.5
+                                                                  or n >= 8)):
             break
+    reps = n
     t_layer = (time.perf_counter() - t0) / reps
     hl = rng.standard_normal((p_cpu, H), dtype=np.float32)
     t0 = time.perf_counter()
@@ -279,7 +293,9 @@ def cpu_baseline(args, prompts=None):
 
 
 def reference_arm(args):
-    cb = cpu_baseline(args)
+    # one step = one timed sample (a C2 decoder layer over 2 prompts, the LM
+    # head and KL rows, the edit GEMVs), after `warmup` untimed ones
+    cb = cpu_baseline(args, reps=max(1, args.steps), warmup=args.warmup)
     tokens = args.prompts * args.seq
     v = cb["value"]
     line = {

@@ -318,8 +318,10 @@ def c1_cpu_trial(spec, w, dirs, good, po, pd, reps):
     delta of every o_proj / down_proj with a kernel weight (A = v^T W on the
     CPU), the forward of the KL batch with the deltas, log-softmax and KL."""
     import oracle
+    from bench import host_threads
     from oracle.model import OracleModel, flatten_batch
 
+    oracle.lib().or_set_threads(host_threads())
     m = OracleModel(spec, w)
     toks, rb, rp, cap, first, take, last = flatten_batch(good, 1)
     _, base = m.forward(toks, rb, rp, (), last)
