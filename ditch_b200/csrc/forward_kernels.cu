@@ -293,8 +293,9 @@ __global__ void __launch_bounds__(256) k_qk_prep(float *qkv, AttnParams p) {
 // 64-key chunk of K are staged transposed in f32 shared memory (rows across
 // lanes: conflict-free), V natural, from rows already normed and roped.
 // Scores: thread (ty, tx) owns queries 4ty..4ty+3 x keys 4tx..4tx+3 (two
-// LDS.128 per 16 FMAs); the output: the same 4 queries x HD/16 dimensions.
-// Online softmax across key chunks, f32.
+// LDS.128 per 16 FMAs); the output: the same 4 queries x HD/16 dimensions
+// (float4 groups tx, tx + 16, ..., so a quarter-warp's value loads are
+// conflict-free). Online softmax across key chunks, f32.
 constexpr int kQB = 64, kKB = 64;
 constexpr int kMaxHeads = 4;  // query heads per block
 
@@ -423,8 +424,8 @@ __global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
                 const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
                 float vv[DPT];
 #pragma unroll
-                for (int c = 0; c < DPT; c += 4) {
-                    const float4 t = *reinterpret_cast<const float4 *>(vs + k * HD + DPT * tx + c);
+                for (int c = 0; c < DPT; c += 4) {  // dimensions 4 (tx + 16 c/4) ..: a quarter-warp reads 128 B
+                    const float4 t = *reinterpret_cast<const float4 *>(vs + k * HD + 4 * tx + 16 * c);
                     vv[c] = t.x;
                     vv[c + 1] = t.y;
                     vv[c + 2] = t.z;
@@ -441,10 +442,14 @@ __global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
             const int qi = i0 + 4 * ty + a;
             if (qi >= len) continue;
             const float inv = 1.0f / l[a];
-            uint16_t *dst = p.out + (long long)(start + qi) * qd + h * HD + DPT * tx;
+            uint16_t *dst = p.out + (long long)(start + qi) * qd + h * HD + 4 * tx;
 #pragma unroll
-            for (int c = 0; c < DPT; c += 2)
-                *reinterpret_cast<uint32_t *>(dst + c) = pack_bf16x2(o[a][c] * inv, o[a][c + 1] * inv);
+            for (int c = 0; c < DPT; c += 4) {
+                uint2 w;
+                w.x = pack_bf16x2(o[a][c] * inv, o[a][c + 1] * inv);
+                w.y = pack_bf16x2(o[a][c + 2] * inv, o[a][c + 3] * inv);
+                *reinterpret_cast<uint2 *>(dst + 16 * c) = w;
+            }
         }
     }
 }
