@@ -237,14 +237,18 @@ __device__ __forceinline__ float2 e2m1x2(uint32_t byte) {
 // MXFP4 (natural layout) over a stack of `slabs` matrices [rows][cols]:
 // out[e][c] = sum_r v[r] W_e[r][c] (the decoded value e2m1 * 2^(b - 127) is
 // exact in bf16, src/dequant.zig:643-673). Block = 32 column blocks (x) by 8
-// row lanes (y); grid = (column-block groups, row chunks, slabs). Each thread
-// streams one 32-element block of its rows, four rows of loads in flight, and
-// the 8 row lanes are summed in shared memory before one atomic per column.
+// row lanes (y); grid = (column-block groups, row chunks of kMxChunk rows,
+// slabs). Each thread streams one 32-element block of its rows, four rows of
+// loads in flight; the 8 row lanes are summed in shared memory and each
+// chunk's partial sums are stored, then k_sum_parts adds the chunks in order.
+// The chunking depends only on the matrix shape, so every matrix of a stack
+// gets the same sums whatever the stack size (no atomics, deterministic).
 constexpr int kMxLanes = 8;
+constexpr int kMxChunk = 256;
 __global__ void __launch_bounds__(32 * kMxLanes) k_gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales,
-                                                                int rows, int cols, const float *v, float *out,
+                                                                int rows, int cols, const float *v, float *part,
                                                                 int rows_per) {
-    __shared__ float part[kMxLanes][32][33];
+    __shared__ float lanes[kMxLanes][32][33];
     const int nblk = cols / 32;
     const int blk = blockIdx.x * 32 + threadIdx.x;
     const int e = blockIdx.z;
@@ -291,7 +295,7 @@ __global__ void __launch_bounds__(32 * kMxLanes) k_gemv_t_mxfp4(const uint8_t *b
         }
     }
 #pragma unroll
-    for (int j = 0; j < 32; j++) part[threadIdx.y][threadIdx.x][j] = acc[j];
+    for (int j = 0; j < 32; j++) lanes[threadIdx.y][threadIdx.x][j] = acc[j];
     __syncthreads();
     // thread (x, y) sums columns y, y + 8, y + 16, y + 24 of column block x
     if (blk < nblk) {
@@ -300,9 +304,20 @@ __global__ void __launch_bounds__(32 * kMxLanes) k_gemv_t_mxfp4(const uint8_t *b
             const int j = threadIdx.y + kMxLanes * k;
             float t = 0.0f;
 #pragma unroll
-            for (int l = 0; l < kMxLanes; l++) t += part[l][threadIdx.x][j];
-            atomicAdd(out + (long long)e * cols + blk * 32 + j, t);
+            for (int l = 0; l < kMxLanes; l++) t += lanes[l][threadIdx.x][j];
+            part[((long long)e * gridDim.y + blockIdx.y) * cols + blk * 32 + j] = t;
         }
+    }
+}
+
+// out[e][c] = sum over chunks q (in order) of part[e][q][c].
+__global__ void k_sum_parts(const float *part, int chunks, int slabs, int cols, float *out) {
+    const long long n = (long long)slabs * cols;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long e = i / cols, c = i % cols;
+        float t = 0.0f;
+        for (int q = 0; q < chunks; q++) t += part[(e * chunks + q) * cols + c];
+        out[i] = t;
     }
 }
 
@@ -555,22 +570,27 @@ cudaError_t gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int 
     return cudaGetLastError();
 }
 
+size_t gemv_t_mxfp4_scratch(int slabs, int rows, int cols) {
+    return (size_t)slabs * ((rows + kMxChunk - 1) / kMxChunk) * cols;
+}
+
 cudaError_t gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, const float *v,
-                         float *out, cudaStream_t st) {
-    return gemv_t_mxfp4_stack(blocks, scales, 1, rows, cols, v, out, st);
+                         float *out, float *scratch, cudaStream_t st) {
+    return gemv_t_mxfp4_stack(blocks, scales, 1, rows, cols, v, out, scratch, st);
 }
 
 cudaError_t gemv_t_mxfp4_stack(const uint8_t *blocks, const uint8_t *scales, int slabs, int rows, int cols,
-                               const float *v, float *out, cudaStream_t st) {
+                               const float *v, float *out, float *scratch, cudaStream_t st) {
     if (rows <= 0 || cols <= 0 || slabs <= 0) return cudaSuccess;
-    if (cols % 32 || slabs > 65535) return cudaErrorInvalidValue;
+    if (cols % 32 || slabs > 65535 || !scratch) return cudaErrorInvalidValue;
     const int gx = (cols / 32 + 31) / 32;
-    // about four blocks per SM in all, at least 4 rows per row lane
-    int chunks = (4 * 148 + gx * slabs - 1) / (gx * slabs);
-    chunks = std::max(1, std::min(chunks, (rows + 4 * kMxLanes - 1) / (4 * kMxLanes)));
-    const int per = (rows + chunks - 1) / chunks;
-    k_gemv_t_mxfp4<<<dim3(gx, (rows + per - 1) / per, slabs), dim3(32, kMxLanes), 0, st>>>(blocks, scales, rows,
-                                                                                         cols, v, out, per);
+    const int chunks = (rows + kMxChunk - 1) / kMxChunk;
+    k_gemv_t_mxfp4<<<dim3(gx, chunks, slabs), dim3(32, kMxLanes), 0, st>>>(blocks, scales, rows, cols, v, scratch,
+                                                                         kMxChunk);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const long long n = (long long)slabs * cols;
+    k_sum_parts<<<(int)std::min<long long>((n + 255) / 256, 4096), 256, 0, st>>>(scratch, chunks, slabs, cols, out);
     return cudaGetLastError();
 }
 

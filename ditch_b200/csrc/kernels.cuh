@@ -83,12 +83,15 @@ cudaError_t gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, f
 cudaError_t gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int cols, int br, int bc,
                        const float *v, float *out, cudaStream_t st);
 cudaError_t gemv_t_f32(const float *w, int rows, int cols, const float *v, float *out, cudaStream_t st);
+// MXFP4: deterministic (fixed row chunks, partial sums added in order), out
+// overwritten; `scratch` holds gemv_t_mxfp4_scratch(slabs, rows, cols) floats.
+size_t gemv_t_mxfp4_scratch(int slabs, int rows, int cols);
 cudaError_t gemv_t_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, const float *v,
-                         float *out, cudaStream_t st);
+                         float *out, float *scratch, cudaStream_t st);
 // The same for each matrix of a stack of `slabs` [rows][cols] MXFP4 matrices
-// (one direction v [rows] for all): out[e][c] for e < slabs, one launch.
+// (one direction v [rows] for all): out[e][c] for e < slabs.
 cudaError_t gemv_t_mxfp4_stack(const uint8_t *blocks, const uint8_t *scales, int slabs, int rows, int cols,
-                               const float *v, float *out, cudaStream_t st);
+                               const float *v, float *out, float *scratch, cudaStream_t st);
 // out[r] = ||W_r||_2
 cudaError_t row_norms_bf16(const uint16_t *w, int rows, int cols, float *out, cudaStream_t st);
 cudaError_t row_norms_f32(const float *w, int rows, int cols, float *out, cudaStream_t st);

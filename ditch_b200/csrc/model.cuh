@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "device.cuh"
+#include "peer.cuh"
 
 namespace ditch {
 
@@ -57,6 +58,8 @@ struct Config {
     int n_experts, top_k, moe_inter, norm_topk;
     std::vector<uint8_t> moe_layers;
     int max_seq;
+    int ep_rank = 0, ep_world = 1;  // expert parallelism: this rank's routed experts are [e0, e0 + e_loc)
+    int e_loc = 0, e0 = 0;
     int qd() const { return heads * head_dim; }
     int kvd() const { return kv_heads * head_dim; }
     int qkv_width() const { return qd() + 2 * kvd(); }
@@ -93,12 +96,19 @@ struct ditch_cuda_model {
     std::vector<float> h_dirs;
     int dir_entries = 0;
     ditch::DevBuf vtmp;  // interpolated direction
+    ditch::DevBuf gemv_part;  // partial sums of the deterministic GEMV-T
     // KL prompts
     ditch::Batch kl;
     ditch::DevBuf kl_base, kl_vals;
     bool kl_ready = false;
     std::vector<size_t> kl_offsets;
     std::vector<uint32_t> kl_tokens_host;
+    // expert parallelism: the peer group and this rank's receive-side scratch
+    ditch_cuda_group *group = nullptr;
+    size_t group_tokens = 0;  // most tokens per rank per forward
+    ditch::DevBuf ep_dst, ep_rcnt, ep_roff, ep_pexp, ep_act, ep_eo, ep_xa, ep_sched_gu, ep_sched_d, ep_nsched,
+        ep_scores;
+    int ep_score_parity = 0;
     ditch::Batch work;   // scratch batch for forward / residual passes
     ditch::DevBuf sums;  // f64 residual sums
     uint64_t bytes = 0;
@@ -120,6 +130,10 @@ int ensure_workspace(ditch_cuda_model *m, int n_tokens, int nc, int nl);
 
 // MoE MLP of layer `li`: post-norm of x, routing, experts, combine into x.
 int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n);
+
+// Expert scores of this rank's routed experts (`local` [e_loc]) gathered from
+// every rank of the model's peer group into `all` [n_experts].
+int ep_allgather_scores(ditch_cuda_model *m, const std::vector<float> &local, std::vector<float> &all);
 
 // The split-bf16 router operand from f32 router weights [E][hidden] (device).
 int build_router_split(ditch_cuda_device *dev, const float *router_f32, int E, int hidden, Mat &out);

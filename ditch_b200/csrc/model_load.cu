@@ -366,6 +366,13 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
     c.moe_inter = cfg->moe_inter;
     c.norm_topk = cfg->norm_topk;
     c.max_seq = cfg->max_seq > 0 ? cfg->max_seq : 4096;
+    c.ep_world = cfg->ep_world > 1 ? cfg->ep_world : 1;
+    c.ep_rank = c.ep_world > 1 ? cfg->ep_rank : 0;
+    REQUIRE(c.ep_rank >= 0 && c.ep_rank < c.ep_world, "ep_rank out of range");
+    REQUIRE(c.ep_world == 1 || (c.n_experts > 0 && c.n_experts % c.ep_world == 0),
+            "expert parallelism needs the experts to split evenly over ep_world");
+    c.e_loc = c.ep_world > 1 ? c.n_experts / c.ep_world : c.n_experts;
+    c.e0 = c.ep_rank * c.e_loc;
     c.moe_layers.assign(c.n_layers, 0);
     if (cfg->moe_layers)
         for (int i = 0; i < c.n_layers; i++) c.moe_layers[i] = cfg->moe_layers[i] ? 1 : 0;
@@ -464,19 +471,21 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
                 }
                 if ((st = build_router_split(dev, rf.as<float>(), E, H, L.router3))) return st;
             }
+            // this rank's experts only (all of them without expert parallelism)
+            const int El = c.e_loc;
             std::vector<Seg> gu, dn;
-            for (int e = 0; e < E; e++) {
+            for (int e = c.e0; e < c.e0 + El; e++) {
                 gu.push_back(Seg{eg, e});
                 gu.push_back(Seg{eu, e});
                 dn.push_back(Seg{ed, e});
             }
-            if ((st = build_mat(m.get(), gu, E, L.e_gate_up, "e_gate_up"))) return st;
-            if ((st = build_mat(m.get(), dn, E, L.e_down, "e_down"))) return st;
-            L.e_edit.assign(E, 0);
-            DITCH_CUDA(L.e_a.reserve((size_t)E * L.e_down.cols * 4));
-            DITCH_CUDA(L.e_b.reserve((size_t)E * H * 4));
-            DITCH_CUDA(L.e_edit_dev.reserve((size_t)E * 4));
-            DITCH_CUDA(cudaMemset(L.e_edit_dev.ptr, 0, (size_t)E * 4));
+            if ((st = build_mat(m.get(), gu, El, L.e_gate_up, "e_gate_up"))) return st;
+            if ((st = build_mat(m.get(), dn, El, L.e_down, "e_down"))) return st;
+            L.e_edit.assign(El, 0);
+            DITCH_CUDA(L.e_a.reserve((size_t)El * L.e_down.cols * 4));
+            DITCH_CUDA(L.e_b.reserve((size_t)El * H * 4));
+            DITCH_CUDA(L.e_edit_dev.reserve((size_t)El * 4));
+            DITCH_CUDA(cudaMemset(L.e_edit_dev.ptr, 0, (size_t)El * 4));
         } else {
             const ditch_cuda_tensor *g = t("gate"), *u = t("up"), *d = t("down");
             REQUIRE(g && u && d, "layer %d: MLP projections missing", i);

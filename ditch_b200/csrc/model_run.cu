@@ -60,9 +60,10 @@ int gemv_t_mat(ditch_cuda_model *m, const Mat &w, int row0, int rows, const floa
                                      v, out, dev->stream));
         break;
     case kFmtMxfp4:
+        DITCH_CUDA(m->gemv_part.reserve(gemv_t_mxfp4_scratch(1, rows, w.cols) * 4));
         DITCH_LAUNCH(dev, gemv_t_mxfp4(w.data.as<uint8_t>() + (size_t)row0 * w.cols / 2,
                                        w.scales.as<uint8_t>() + (size_t)row0 * w.cols / 32, rows, w.cols, v, out,
-                                       dev->stream));
+                                       m->gemv_part.as<float>(), dev->stream));
         break;
     case kFmtInt4: {
         DevBuf tmp;
@@ -391,13 +392,14 @@ int prepare_direction(ditch_cuda_model *m, float di, bool use_di) {
 int expert_projections(ditch_cuda_model *m, int li, const float *v) {
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
-    const int E = m->cfg.n_experts, H = m->cfg.hidden, mi = L.e_down.cols;  // the stored (8-aligned) width
+    const int E = m->cfg.e_loc, H = m->cfg.hidden, mi = L.e_down.cols;  // this rank's experts; stored width
     DITCH_CUDA(L.e_proj.reserve((size_t)E * mi * 4));
     float *proj = L.e_proj.as<float>();
     if (L.e_down.fmt == kFmtMxfp4) {
         DITCH_CUDA(cudaMemsetAsync(proj, 0, (size_t)E * mi * 4, dev->stream));
+        DITCH_CUDA(m->gemv_part.reserve(gemv_t_mxfp4_scratch(E, H, mi) * 4));
         DITCH_LAUNCH(dev, gemv_t_mxfp4_stack(L.e_down.data.as<uint8_t>(), L.e_down.scales.as<uint8_t>(), E, H, mi, v,
-                                             proj, dev->stream));
+                                             proj, m->gemv_part.as<float>(), dev->stream));
         return DITCH_CUDA_OK;
     }
     int s;
@@ -411,7 +413,7 @@ int expert_projections(ditch_cuda_model *m, int li, const float *v) {
 int expert_frobenius(ditch_cuda_model *m, int li) {
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
-    const int E = m->cfg.n_experts, H = m->cfg.hidden, mi = L.e_down.cols;
+    const int E = m->cfg.e_loc, H = m->cfg.hidden, mi = L.e_down.cols;  // this rank's experts
     if ((int)L.e_fro.size() == E) return DITCH_CUDA_OK;
     DevBuf norms;
     DITCH_CUDA(norms.reserve((size_t)E * H * 4));
@@ -452,11 +454,12 @@ int expert_frobenius(ditch_cuda_model *m, int li) {
 
 // Scores of every routed expert of `li` against v (device f32 [H]):
 // ||v^T W_down_e|| / ||W_down_e||_F (src/moe.zig:1239-1283). Leaves the
-// projections in L.e_proj for the edit of the selected experts.
+// projections in L.e_proj for the edit of the selected experts. With expert
+// parallelism each rank scores its own experts and the group gathers them.
 int expert_scores(ditch_cuda_model *m, int li, const float *v, std::vector<float> &scores) {
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
-    const int E = m->cfg.n_experts, mi = L.e_down.cols;
+    const int E = m->cfg.e_loc, mi = L.e_down.cols;
     int s;
     if ((s = expert_frobenius(m, li))) return s;
     if ((s = expert_projections(m, li, v))) return s;
@@ -469,6 +472,11 @@ int expert_scores(ditch_cuda_model *m, int li, const float *v, std::vector<float
         for (int j = 0; j < mi; j++) pn = std::fma(hp[(size_t)e * mi + j], hp[(size_t)e * mi + j], pn);
         const float fro = L.e_fro[e];
         scores[e] = fro > 0 ? std::sqrt(pn) / fro : 0.0f;
+    }
+    if (m->group) {
+        std::vector<float> all;
+        if ((s = ep_allgather_scores(m, scores, all))) return s;
+        scores.swap(all);
     }
     return DITCH_CUDA_OK;
 }
@@ -516,7 +524,7 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
         const int E = c.n_experts;
         if (!selective || n_experts == 0) {
             if ((s = expert_projections(m, li, v))) return s;
-            for (int e = 0; e < E; e++)
+            for (int e = 0; e < c.e_loc; e++)  // this rank's experts
                 if ((s = expert_delta_from_proj(m, li, e, v, lambda))) return s;
             continue;
         }
@@ -526,8 +534,11 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
         std::vector<float> scores;
         if ((s = expert_scores(m, li, v, scores))) return s;
         std::vector<uint32_t> order = rank(scores);
-        for (size_t j = 0; j < n; j++)
-            if ((s = expert_delta_from_proj(m, li, (int)order[j], v, weight))) return s;
+        for (size_t j = 0; j < n; j++) {
+            const int e = (int)order[j] - c.e0;  // edited by the rank that owns it
+            if (e >= 0 && e < c.e_loc)
+                if ((s = expert_delta_from_proj(m, li, e, v, weight))) return s;
+        }
     }
     if ((s = upload_expert_flags(m))) return s;
     return check_status(m->dev, "apply_edit");

@@ -341,6 +341,148 @@ __global__ void k_combine(const float *eo, const int *sel, const float *wts, con
     }
 }
 
+// ---- expert parallelism over a peer group ---------------------------------
+// Layout of the group region's data part (offsets from peer_data), per rank.
+struct EpLayout {
+    size_t cnt, scores, eo, xg, meta, end;
+    size_t cap;  // receive rows: every rank's pairs could land on one rank
+};
+
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+EpLayout ep_layout(const Config &c, size_t max_tokens) {
+    EpLayout l{};
+    const size_t W = c.ep_world, E = c.n_experts, H = c.hidden, nk = max_tokens * c.top_k;
+    l.cap = W * nk;
+    l.cnt = 0;
+    l.scores = align256(l.cnt + W * E * 4);
+    l.eo = align256(l.scores + 2 * E * 4);
+    l.xg = align256(l.eo + nk * H * 4);
+    l.meta = align256(l.xg + l.cap * H * 2);
+    l.end = align256(l.meta + l.cap * 8);
+    return l;
+}
+
+template <class T>
+__device__ __forceinline__ T *region(const PeerPtrs &pp, int r, size_t off) {
+    return reinterpret_cast<T *>(pp.p[r] + kPeerFlagBytes + off);
+}
+
+// This rank's per-expert pair counts into every rank's [world][E] table.
+__global__ void k_ep_put_counts(const int *counts, int E, PeerPtrs pp, size_t off, int rank) {
+    int *dst = region<int>(pp, blockIdx.x, off) + (size_t)rank * E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) dst[e] = counts[e];
+    __threadfence_system();
+}
+
+// From the gathered counts: where this rank's pairs of expert e land in the
+// owner's receive rows (dst_base[e] + local sorted position), and how many
+// rows each of this rank's own experts receives. Receive rows are ordered by
+// local expert, then source rank, then the source's order.
+__global__ void k_ep_plan(const int *cnt_all, const int *offsets_local, int E, int El, int world, int rank,
+                          int *dst_base, int *rcnt) {
+    __shared__ int tot[1024];
+    const int e = threadIdx.x;
+    int before = 0;
+    if (e < E) {
+        int t = 0;
+        for (int s = 0; s < world; s++) {
+            const int c = cnt_all[(size_t)s * E + e];
+            if (s < rank) before += c;
+            t += c;
+        }
+        tot[e] = t;
+    }
+    __syncthreads();
+    if (e >= E) return;
+    const int d = e / El;
+    int base = 0;
+    for (int x = d * El; x < e; x++) base += tot[x];
+    dst_base[e] = base + before - offsets_local[e];
+    if (d == rank) rcnt[e - d * El] = tot[e];
+}
+
+// One warp per local (token, expert) pair in expert-sorted order: the pair's
+// normalised row (bf16, the hi part of the split rows) and (source rank,
+// position) into the owner's receive region.
+__global__ void k_ep_dispatch(const uint16_t *h3, long long ss, const int *perm, const int *pexp, int nk,
+                              const int *dst_base, int El, PeerPtrs pp, size_t xg_off, size_t meta_off, int H,
+                              int rank) {
+    const int pos = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (pos < nk) {
+        const int e = pexp[pos], d = e / El;
+        const long long row = (long long)dst_base[e] + pos;
+        const uint16_t *src = h3 + (long long)perm[pos] * ss;
+        uint16_t *dst = region<uint16_t>(pp, d, xg_off) + row * H;
+        for (int i = lane * 8; i < H; i += 256)
+            *reinterpret_cast<uint4 *>(dst + i) = *reinterpret_cast<const uint4 *>(src + i);
+        if (lane == 0) region<int2>(pp, d, meta_off)[row] = make_int2(rank, pos);
+    }
+    __threadfence_system();
+}
+
+// Local expert of every receive row (rows past the total get -1).
+__global__ void k_ep_fill_pexp(const int *offsets, int El, int cap, int *pexp) {
+    const int total = offsets[El];
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < cap; r += gridDim.x * blockDim.x) {
+        if (r >= total) {
+            pexp[r] = -1;
+            continue;
+        }
+        int lo = 0, hi = El - 1;  // last expert whose offset <= r
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) / 2;
+            if (offsets[mid] <= r) lo = mid;
+            else hi = mid - 1;
+        }
+        pexp[r] = lo;
+    }
+}
+
+// xa of receive rows of edited local experts (rows with pexp < 0 skipped).
+__global__ void k_ep_rowdot(const uint16_t *act, const float *e_a, const int *pexp, const int *e_flags, int cap,
+                            int mi, float *xa) {
+    const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= cap) return;
+    const int e = pexp[r];
+    if (e < 0) return;
+    if (!e_flags[e]) {
+        if (lane == 0) xa[r] = 0.0f;
+        return;
+    }
+    const uint16_t *ar = act + (long long)r * mi;
+    const float *a = e_a + (long long)e * mi;
+    float s = 0.0f;
+    for (int i = lane; i < mi; i += 32) s = fmaf(bf16_bits_to_f32(ar[i]), a[i], s);
+    s = warp_sum(s);
+    if (lane == 0) xa[r] = s;
+}
+
+// One warp per receive row: its expert output back to the source rank's eo
+// rows at the pair's position there.
+__global__ void k_ep_return(const float *eo, const int2 *meta, const int *offsets, int El, PeerPtrs pp,
+                            size_t eo_off, int H) {
+    const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r < offsets[El]) {
+        const int2 sp = meta[r];
+        const float *src = eo + (long long)r * H;
+        float *dst = region<float>(pp, sp.x, eo_off) + (long long)sp.y * H;
+        for (int i = lane * 4; i < H; i += 128)
+            *reinterpret_cast<float4 *>(dst + i) = *reinterpret_cast<const float4 *>(src + i);
+    }
+    __threadfence_system();
+}
+
+// This rank's expert scores into every rank's score buffer (double-buffered).
+__global__ void k_ep_put_scores(const float *local, int El, int rank, PeerPtrs pp, size_t off) {
+    float *dst = region<float>(pp, blockIdx.x, off) + (size_t)rank * El;
+    for (int e = threadIdx.x; e < El; e += blockDim.x) dst[e] = local[e];
+    __threadfence_system();
+}
+
 // Token tile of a grouped GEMM from the mean rows per expert.
 int tile_for(int avg, bool dual, bool quant) {
     if (avg <= 32) return 32;
@@ -365,8 +507,11 @@ int build_router_split(ditch_cuda_device *dev, const float *router_f32, int E, i
     return DITCH_CUDA_OK;
 }
 
+int moe_mlp_ep(ditch_cuda_model *m, Layer &L, int n);
+
 int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     (void)li;
+    if (m->group) return moe_mlp_ep(m, L, n);
     ditch_cuda_device *dev = m->dev;
     cudaStream_t st = dev->stream;
     const Config &c = m->cfg;
@@ -461,4 +606,215 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     return DITCH_CUDA_OK;
 }
 
+namespace {
+
+#define EP_REQUIRE(cond, ...)          \
+    do {                               \
+        if (!(cond)) {                 \
+            set_error(__VA_ARGS__);    \
+            return DITCH_CUDA_INVALID; \
+        }                              \
+    } while (0)
+
+// One exchange of the model's peer group: signal this rank's epoch to every
+// peer, then wait (bounded) until every peer has signalled it.
+int ep_exchange(ditch_cuda_model *m) {
+    ditch_cuda_device *dev = m->dev;
+    ditch_cuda_group *g = m->group;
+    const uint64_t ep = ++g->epoch;
+    DITCH_LAUNCH(dev, peer_signal(g->peers, g->rank, g->world, ep, dev->stream));
+    DITCH_LAUNCH(dev, peer_wait(g->base, g->world, ep, dev->status, 30.0, dev->stream));
+    return DITCH_CUDA_OK;
+}
+
+}  // namespace
+
+// Expert-parallel MoE MLP: routing on this rank's tokens, the pairs sent to
+// their experts' owners, the owners' grouped GEMMs over every rank's rows,
+// the outputs returned to the pairs' positions, then the same ordered combine
+// as one GPU (so the result equals the single-GPU forward bit for bit).
+// Exchange order per layer: counts, rows, outputs.
+int moe_mlp_ep(ditch_cuda_model *m, Layer &L, int n) {
+    ditch_cuda_device *dev = m->dev;
+    cudaStream_t st = dev->stream;
+    const Config &c = m->cfg;
+    ditch_cuda_group *g = m->group;
+    const int H = c.hidden, E = c.n_experts, El = c.e_loc, k = c.top_k, mi = c.moe_inter;
+    const int W = g->world, rank = g->rank;
+    EP_REQUIRE(E <= 1024 && k <= 16, "MoE with %d experts / top-%d is not supported (<= 1024 / 16)", E, k);
+    EP_REQUIRE((size_t)n <= m->group_tokens, "%d tokens exceed the %zu the peer group was sized for", n,
+               m->group_tokens);
+    const EpLayout lay = ep_layout(c, m->group_tokens);
+    const int nk = n * k;
+    const int cap = (int)lay.cap;
+    const int mip = L.e_down.cols;
+    const int cp = (H + 63) / 64 * 64;
+    const int avg = (int)(((long long)W * nk + E - 1) / E);  // rows per expert with balanced routing
+    const int bn_gu = tile_for(avg, true, L.e_gate_up.fmt != kFmtBf16);
+    const int bn_d = tile_for(avg, false, L.e_down.fmt != kFmtBf16);
+    const int wt_gu = (mi + 127) / 128, wt_d = (H + 127) / 128;
+    const int src_gu = (nk / bn_gu + E) * wt_gu, src_d = (nk / bn_d + E) * wt_d;
+    const int max_gu = (cap / bn_gu + El) * wt_gu, max_d = (cap / bn_d + El) * wt_d;
+    DITCH_CUDA(m->moe_h3.reserve((size_t)n * 3 * cp * 2));
+    DITCH_CUDA(m->moe_logits.reserve((size_t)n * E * 4));
+    DITCH_CUDA(m->moe_sel.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_w.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_counts.reserve((size_t)E * 4));
+    DITCH_CUDA(m->moe_cc.reserve((size_t)((nk + kChunk - 1) / kChunk) * E * 4));
+    DITCH_CUDA(m->moe_offsets.reserve((size_t)(E + 1) * 4 + 8));
+    DITCH_CUDA(m->moe_perm.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_pw.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_pexp.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_slot.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_sched_gu.reserve((size_t)src_gu * 16));
+    DITCH_CUDA(m->moe_sched_d.reserve((size_t)src_d * 16));
+    DITCH_CUDA(m->moe_nsched.reserve(16));
+    DITCH_CUDA(m->ep_dst.reserve((size_t)E * 4));
+    DITCH_CUDA(m->ep_rcnt.reserve((size_t)El * 4));
+    DITCH_CUDA(m->ep_roff.reserve((size_t)(El + 1) * 4 + 8));
+    DITCH_CUDA(m->ep_pexp.reserve((size_t)cap * 4));
+    DITCH_CUDA(m->ep_act.reserve((size_t)cap * mip * 2));
+    DITCH_CUDA(m->ep_eo.reserve((size_t)cap * H * 4));
+    DITCH_CUDA(m->ep_xa.reserve((size_t)cap * 4));
+    DITCH_CUDA(m->ep_sched_gu.reserve((size_t)max_gu * 16));
+    DITCH_CUDA(m->ep_sched_d.reserve((size_t)max_d * 16));
+    DITCH_CUDA(m->ep_nsched.reserve(16));
+    uint8_t *own = peer_data(g->base);
+
+    // routing of this rank's tokens, pairs sorted by expert (as one GPU)
+    k_rmsnorm_split3<<<(n + 7) / 8, 256, 0, st>>>(m->x.as<float>(), L.post_norm.as<float>(), n, H, cp, c.eps,
+                                                   m->moe_h3.as<uint16_t>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    int s;
+    if ((s = gemm_mat(dev, L.router3, 0, E, m->moe_h3.as<uint16_t>(), n, m->moe_logits.ptr, E, 0, nullptr, nullptr,
+                      nullptr, 0, nullptr)))
+        return s;
+    k_route<<<(n + 7) / 8, 256, 0, st>>>(m->moe_logits.as<float>(), n, E, k, c.norm_topk, m->moe_sel.as<int>(),
+                                         m->moe_w.as<float>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    const int chunks = (nk + kChunk - 1) / kChunk;
+    k_chunk_counts<<<chunks, kChunk, (size_t)E * 4, st>>>(m->moe_sel.as<int>(), nk, E, m->moe_cc.as<int>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    k_chunk_prefix<<<E, 256, 0, st>>>(m->moe_cc.as<int>(), chunks, E, m->moe_counts.as<int>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    int *src_n = m->moe_nsched.as<int>();
+    k_schedule<<<1, 1024, 0, st>>>(m->moe_counts.as<int>(), E, bn_gu, wt_gu, bn_d, wt_d, m->moe_offsets.as<int>(),
+                                   m->moe_sched_gu.as<int4>(), src_n, m->moe_sched_d.as<int4>(), src_n + 1);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    k_scatter<<<chunks, kChunk, (size_t)(kChunk / 32) * E * 4, st>>>(
+        m->moe_sel.as<int>(), m->moe_w.as<float>(), nk, k, E, m->moe_cc.as<int>(), m->moe_offsets.as<int>(),
+        m->moe_perm.as<int>(), m->moe_pw.as<float>(), m->moe_pexp.as<int>(), m->moe_slot.as<int>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+
+    // exchange 1: every rank's per-expert pair counts
+    k_ep_put_counts<<<W, 256, 0, st>>>(m->moe_counts.as<int>(), E, g->peers, lay.cnt, rank);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    if ((s = ep_exchange(m))) return s;
+    k_ep_plan<<<1, 1024, 0, st>>>(reinterpret_cast<const int *>(own + lay.cnt), m->moe_offsets.as<int>(), E, El, W,
+                                  rank, m->ep_dst.as<int>(), m->ep_rcnt.as<int>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    int *n_gu = m->ep_nsched.as<int>(), *n_d = n_gu + 1;
+    k_schedule<<<1, 1024, 0, st>>>(m->ep_rcnt.as<int>(), El, bn_gu, wt_gu, bn_d, wt_d, m->ep_roff.as<int>(),
+                                   m->ep_sched_gu.as<int4>(), n_gu, m->ep_sched_d.as<int4>(), n_d);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+
+    // exchange 2: the rows to their experts' owners
+    k_ep_dispatch<<<(nk + 7) / 8, 256, 0, st>>>(m->moe_h3.as<uint16_t>(), 3LL * cp, m->moe_perm.as<int>(),
+                                                m->moe_pexp.as<int>(), nk, m->ep_dst.as<int>(), El, g->peers, lay.xg,
+                                                lay.meta, H, rank);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    if ((s = ep_exchange(m))) return s;
+
+    // this rank's experts over every rank's rows
+    k_ep_fill_pexp<<<std::min((cap + 255) / 256, 4096), 256, 0, st>>>(m->ep_roff.as<int>(), El, cap,
+                                                                      m->ep_pexp.as<int>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    const uint16_t *xg = reinterpret_cast<const uint16_t *>(own + lay.xg);
+    GemmExtra gu;
+    gu.sched = m->ep_sched_gu.as<int4>();
+    gu.n_sched = n_gu;
+    gu.slab_rows = 2 * mi;
+    gu.bn = bn_gu;
+    if (mip != mi) DITCH_CUDA(cudaMemsetAsync(m->ep_act.ptr, 0, (size_t)cap * mip * 2, st));
+    if ((s = gemm_mat(dev, L.e_gate_up, 0, mi, xg, cap, m->ep_act.ptr, mip, kEpiSwiglu, nullptr, nullptr, nullptr, mi,
+                      &gu)))
+        return s;
+    bool any_edit = false;
+    for (uint8_t f : L.e_edit) any_edit |= f != 0;
+    if (any_edit) {
+        k_ep_rowdot<<<(cap + 7) / 8, 256, 0, st>>>(m->ep_act.as<uint16_t>(), L.e_a.as<float>(), m->ep_pexp.as<int>(),
+                                                   L.e_edit_dev.as<int>(), cap, mip, m->ep_xa.as<float>());
+        DITCH_LAUNCH(dev, cudaGetLastError());
+    }
+    GemmExtra dn;
+    dn.sched = m->ep_sched_d.as<int4>();
+    dn.n_sched = n_d;
+    dn.slab_rows = H;
+    dn.bn = bn_d;
+    dn.e_flags = L.e_edit_dev.as<int>();
+    dn.db_stride = H;
+    if ((s = gemm_mat(dev, L.e_down, 0, H, m->ep_act.as<uint16_t>(), cap, m->ep_eo.ptr, H, 0, nullptr,
+                      any_edit ? m->ep_xa.as<float>() : nullptr, any_edit ? L.e_b.as<float>() : nullptr, 0, &dn)))
+        return s;
+
+    // exchange 3: the outputs back to the pairs' positions on their source ranks
+    k_ep_return<<<(cap + 7) / 8, 256, 0, st>>>(m->ep_eo.as<float>(), reinterpret_cast<const int2 *>(own + lay.meta),
+                                               m->ep_roff.as<int>(), El, g->peers, lay.eo, H);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    if ((s = ep_exchange(m))) return s;
+    k_combine<<<n, 256, 0, st>>>(reinterpret_cast<const float *>(own + lay.eo), m->moe_sel.as<int>(),
+                                 m->moe_w.as<float>(), m->moe_slot.as<int>(), n, k, H, m->x.as<float>());
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    return DITCH_CUDA_OK;
+}
+
+int ep_allgather_scores(ditch_cuda_model *m, const std::vector<float> &local, std::vector<float> &all) {
+    ditch_cuda_device *dev = m->dev;
+    cudaStream_t st = dev->stream;
+    const Config &c = m->cfg;
+    ditch_cuda_group *g = m->group;
+    const int E = c.n_experts, El = c.e_loc;
+    EP_REQUIRE((int)local.size() == El, "local scores size");
+    const EpLayout lay = ep_layout(c, m->group_tokens);
+    const size_t off = lay.scores + (size_t)m->ep_score_parity * E * 4;
+    m->ep_score_parity ^= 1;
+    DITCH_CUDA(m->ep_scores.reserve((size_t)El * 4));
+    DITCH_CUDA(cudaMemcpyAsync(m->ep_scores.ptr, local.data(), (size_t)El * 4, cudaMemcpyHostToDevice, st));
+    k_ep_put_scores<<<g->world, 256, 0, st>>>(m->ep_scores.as<float>(), El, g->rank, g->peers, off);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    int s;
+    if ((s = ep_exchange(m))) return s;
+    all.assign(E, 0.0f);
+    DITCH_CUDA(cudaMemcpyAsync(all.data(), peer_data(g->base) + off, (size_t)E * 4, cudaMemcpyDeviceToHost, st));
+    return check_status(dev, "expert score exchange");
+}
+
 }  // namespace ditch
+
+extern "C" {
+
+size_t ditch_cuda_model_group_bytes(const ditch_cuda_model *m, size_t max_tokens) {
+    if (!m || m->cfg.ep_world <= 1) return 0;
+    return ditch::ep_layout(m->cfg, max_tokens).end;
+}
+
+int ditch_cuda_model_set_group(ditch_cuda_model *m, ditch_cuda_group *g, size_t max_tokens) {
+    using namespace ditch;
+    clear_error();
+    EP_REQUIRE(m && g, "null argument");
+    EP_REQUIRE(m->cfg.ep_world > 1, "the model was loaded without expert parallelism (ep_world <= 1)");
+    EP_REQUIRE(g->opened, "the group is not opened");
+    EP_REQUIRE(g->dev == m->dev, "the group lives on another device");
+    EP_REQUIRE(g->world == m->cfg.ep_world && g->rank == m->cfg.ep_rank,
+               "group rank %d / world %d differ from the model's ep_rank %d / ep_world %d", g->rank, g->world,
+               m->cfg.ep_rank, m->cfg.ep_world);
+    EP_REQUIRE(max_tokens > 0, "max_tokens must be positive");
+    EP_REQUIRE(ep_layout(m->cfg, max_tokens).end <= g->bytes, "the group region holds %zu bytes; %zu needed", g->bytes,
+               (size_t)ep_layout(m->cfg, max_tokens).end);
+    std::lock_guard<std::mutex> lk(m->dev->mu);
+    m->group = g;
+    m->group_tokens = max_tokens;
+    return DITCH_CUDA_OK;
+}
+
+}  // extern "C"

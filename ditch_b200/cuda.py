@@ -46,6 +46,7 @@ class ModelConfig(C.Structure):
         ("rope_low_ff", C.c_double), ("rope_high_ff", C.c_double), ("rope_orig_max", C.c_double),
         ("qk_norm", C.c_int), ("n_experts", C.c_int), ("top_k", C.c_int), ("moe_inter", C.c_int),
         ("norm_topk", C.c_int), ("moe_layers", C.POINTER(C.c_uint8)), ("max_seq", C.c_int),
+        ("ep_rank", C.c_int), ("ep_world", C.c_int),
     ]
 
 
@@ -117,6 +118,13 @@ SIGNATURES = {
     "ditch_cuda_weight_gemm": (C.c_int, [vp, vp, sz, vp, C.c_int]),
     "ditch_cuda_weight_decode": (C.c_int, [vp, vp]),
     "ditch_cuda_set_decode_staging": (C.c_int, [vp, C.c_int]),
+    "ditch_cuda_peer_handle_bytes": (sz, []),
+    "ditch_cuda_group_create": (C.c_int, [vp, C.c_int, C.c_int, sz, C.POINTER(vp), vp]),
+    "ditch_cuda_group_open": (C.c_int, [vp, vp]),
+    "ditch_cuda_group_free": (None, [vp]),
+    "ditch_cuda_group_barrier": (C.c_int, [vp]),
+    "ditch_cuda_model_group_bytes": (sz, [vp, sz]),
+    "ditch_cuda_model_set_group": (C.c_int, [vp, vp, sz]),
     "ditch_cuda_set_profiling": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_gemm_stats": (C.c_int, [vp, f64p, u64p, f64p]),
     "ditch_cuda_reset_stats": (C.c_int, [vp]),
@@ -409,10 +417,42 @@ class Weight:
             pass
 
 
+class Group:
+    """One rank's share of a peer group (GPUs of one node over NVLink).
+
+    `exchange(handle_bytes) -> list of every rank's handle bytes` is the host
+    transport (e.g. torch.distributed.all_gather_object)."""
+
+    def __init__(self, device, rank, world, nbytes, exchange):
+        self.dev = device
+        n = int(lib().ditch_cuda_peer_handle_bytes())
+        buf = (C.c_uint8 * n)()
+        h = vp()
+        check(lib().ditch_cuda_group_create(device.h, rank, world, nbytes, C.byref(h), C.cast(buf, vp)))
+        self.h = h
+        handles = exchange(bytes(buf))
+        allh = (C.c_uint8 * (n * world)).from_buffer_copy(b"".join(handles))
+        check(lib().ditch_cuda_group_open(self.h, C.cast(allh, vp)))
+
+    def barrier(self):
+        check(lib().ditch_cuda_group_barrier(self.h))
+
+    def close(self):
+        if self.h:
+            lib().ditch_cuda_group_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Model:
     """A model resident in HBM (the coarse C-ABI entries)."""
 
-    def __init__(self, device, spec, tensors, max_seq=4096):
+    def __init__(self, device, spec, tensors, max_seq=4096, ep_rank=0, ep_world=1):
         self.dev = device
         self.spec = spec
         cfg = ModelConfig(
@@ -422,7 +462,8 @@ class Model:
             rope_factor=spec.get("rope_factor", 1.0), rope_low_ff=spec.get("rope_low_ff", 1.0),
             rope_high_ff=spec.get("rope_high_ff", 1.0), rope_orig_max=spec.get("rope_orig_max", 1.0),
             qk_norm=int(spec.get("qk_norm", 0)), n_experts=spec.get("n_experts", 0), top_k=spec.get("top_k", 0),
-            moe_inter=spec.get("moe_inter", 0), norm_topk=int(spec.get("norm_topk", 1)), max_seq=max_seq)
+            moe_inter=spec.get("moe_inter", 0), norm_topk=int(spec.get("norm_topk", 1)), max_seq=max_seq,
+            ep_rank=ep_rank, ep_world=ep_world)
         self._moe = None
         if spec.get("moe_layers"):
             self._moe = np.array([1 if x else 0 for x in spec["moe_layers"]], np.uint8)
@@ -446,6 +487,15 @@ class Model:
 
     def bytes(self):
         return int(lib().ditch_cuda_model_bytes(self.h))
+
+    def group_bytes(self, max_tokens):
+        """Peer-group region bytes this expert-parallel model needs."""
+        return int(lib().ditch_cuda_model_group_bytes(self.h, max_tokens))
+
+    def set_group(self, group, max_tokens):
+        """Runs the routed-expert layers expert-parallel over `group`."""
+        check(lib().ditch_cuda_model_set_group(self.h, group.h, max_tokens))
+        self._group = group  # the group outlives the model's use of it
 
     def forward(self, tokens, row_b, row_pos, capture_rows=(), logit_rows=()):
         s = self.spec

@@ -134,6 +134,11 @@ typedef struct {
     int n_experts, top_k, moe_inter, norm_topk;
     const uint8_t *moe_layers; /* [n_layers]: 1 = routed-expert MLP; NULL = dense model */
     int max_seq;               /* longest prompt (RoPE table rows) */
+    /* Expert parallelism over ep_world ranks (0 or 1: this model holds every
+     * expert): this rank keeps routed experts [ep_rank E / ep_world,
+     * (ep_rank + 1) E / ep_world) of the stacks it is given and runs MoE
+     * layers through a peer group (ditch_cuda_model_set_group). */
+    int ep_rank, ep_world;
 } ditch_cuda_model_config;
 
 /* Storage formats of a resident tensor. */
@@ -289,6 +294,34 @@ int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out_bf16);
  * the GEMM. Default 1024. No counterpart in the reference (a tuning knob of
  * this backend). */
 int ditch_cuda_set_decode_staging(ditch_cuda_device *dev, int min_tokens);
+
+/* ---- peer groups and expert parallelism (one process per GPU of one node;
+ * no counterpart in ditch, which runs on one host) ---- */
+typedef struct ditch_cuda_group ditch_cuda_group;
+/* Bytes of one rank's IPC handle; the host gathers `world` of them in rank
+ * order and gives the array to ditch_cuda_group_open on every rank. */
+size_t ditch_cuda_peer_handle_bytes(void);
+/* Allocates this rank's region of a peer group (`bytes` of data after a flag
+ * block) on the device and writes its IPC handle to `handle`. world <= 8. */
+int ditch_cuda_group_create(ditch_cuda_device *dev, int rank, int world, size_t bytes, ditch_cuda_group **out,
+                            void *handle);
+/* Maps every peer's region (handles: world x handle bytes, rank order). */
+int ditch_cuda_group_open(ditch_cuda_group *g, const void *handles);
+void ditch_cuda_group_free(ditch_cuda_group *g);
+/* A device-side barrier over the group (bounded: returns
+ * DITCH_CUDA_DEVICE_FAILED when a peer does not arrive within 20 s). */
+int ditch_cuda_group_barrier(ditch_cuda_group *g);
+/* Region bytes that a model loaded with ep_world > 1 needs for forwards of
+ * at most max_tokens tokens per rank (0 without expert parallelism). */
+size_t ditch_cuda_model_group_bytes(const ditch_cuda_model *m, size_t max_tokens);
+/* Runs the model's routed-expert layers expert-parallel over the group: each
+ * rank routes its own tokens, sends every (token, expert) row to the expert's
+ * owner over NVLink, runs its experts' grouped GEMMs on every rank's rows and
+ * returns the outputs; the combine then equals the single-GPU one bit for
+ * bit. Expert scoring gathers every rank's scores, so the selective edit picks
+ * the same experts on all ranks. Every rank must make the same calls in the
+ * same order (forward, residual sums, edits, KL). */
+int ditch_cuda_model_set_group(ditch_cuda_model *m, ditch_cuda_group *g, size_t max_tokens);
 
 /* ---- timing support (CUDA events on the device's stream) ---- */
 /* Accumulated device time and launch count of the weight GEMMs since the
