@@ -391,7 +391,7 @@ def run_c1(args, dev):
         step(False)
     dev.set_profiling(True)
     dev.reset_stats()
-    clocks = Clocks(0)
+    clocks = Clocks(torch.cuda.current_device())
     ms = timed(False, args.steps)
     clk = clocks.stop()
     gemm_ms, gemm_launches, gemm_flops = dev.gemm_stats()
@@ -404,8 +404,8 @@ def run_c1(args, dev):
     tokens = P * S
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
     line = {
-        "metric": "trial-eval forward tokens/s", "value": round(tokens * args.steps / (ms / 1000.0), 1),
-        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "metric": "trial-eval forward tokens/s", "value": round(tokens * world * args.steps / (ms / 1000.0), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3), "s_per_trial": round(ms / args.steps / 1000.0, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 weights run as bf16 MMA with f32 accumulate", "data": "synthetic",
@@ -441,7 +441,7 @@ C4 = dict(n_layers=48, hidden=2048, heads=32, kv_heads=4, head_dim=128, inter=76
           rope_theta=1e6, qk_norm=1, n_experts=128, top_k=8, moe_inter=768, norm_topk=1)
 
 
-def build_c4_model(dev, spec, seed, max_seq):
+def build_c4_model(dev, spec, seed, max_seq, ep_rank=0, ep_world=1):
     """Seeded N(0, 0.02) weights: attention, router, embedding and LM head in
     bf16, routed experts quantised to MXFP4 (natural layout) on the GPU."""
     import torch
@@ -493,7 +493,7 @@ def build_c4_model(dev, spec, seed, max_seq):
         add_experts(f"L{i}.e_up", mi, H)
         add_experts(f"L{i}.e_down", H, mi)
     torch.cuda.synchronize()
-    model = ditch_b200.Model(dev, spec, tensors, max_seq=max_seq)
+    model = ditch_b200.Model(dev, spec, tensors, max_seq=max_seq, ep_rank=ep_rank, ep_world=ep_world)
     del keep, tensors
     torch.cuda.empty_cache()
     return model
@@ -509,18 +509,32 @@ def c4_flops(spec, tokens):
     return L * per_tok * tokens
 
 
-def run_c4(args, dev):
+def run_c4(args, dev, world=1, rank=0, dist=None):
+    """C4 on `world` GPUs: expert-parallel (each rank owns 128 / world experts,
+    rows exchanged over NVLink peer memory) and data-parallel over prompts
+    (each rank routes its own 256 prompts; residual sums and KL all-reduced)."""
     import torch
 
-    from bench import Clocks, measured_peaks, trial_params
+    import ditch_b200
+    from bench import Clocks, all_reduce, measured_peaks, trial_params
 
     spec = dict(C4, n_layers=args.layers or C4["n_layers"], moe_layers=[True] * (args.layers or C4["n_layers"]))
     L, V, S = spec["n_layers"], spec["vocab"], args.seq
     P = args.prompts or 256
     t0 = time.time()
-    model = build_c4_model(dev, spec, args.seed, max_seq=S)
+    model = build_c4_model(dev, spec, args.seed, max_seq=S, ep_rank=rank, ep_world=world)
+    group = None
+    if world > 1:
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+
+        group = ditch_b200.Group(dev, rank, world, model.group_bytes(P * S), exchange)
+        model.set_group(group, P * S)
+        dist.barrier()
     load_s = time.time() - t0
-    rng = np.random.default_rng(args.seed + 1000)
+    rng = np.random.default_rng(args.seed + 1000 * (rank + 1))
     good = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
     bad = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
     kl_prompts = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
@@ -528,7 +542,9 @@ def run_c4(args, dev):
     dev.timer_start()
     gs, gc = model.residual_sums(good, window=1, batch_size=P)
     bs, bc = model.residual_sums(bad, window=1, batch_size=P)
-    model.directions(gs, gc, bs, bc, True)
+    gs, bs = all_reduce(dist, gs), all_reduce(dist, bs)
+    counts = all_reduce(dist, np.array([gc, bc], np.float64))
+    model.directions(gs, int(counts[0]), bs, int(counts[1]), True)
     capture_ms = dev.timer_stop()
     model.kl_init(kl_prompts)
     tokens_flat = np.concatenate(kl_prompts).astype(np.uint32)
@@ -540,21 +556,26 @@ def run_c4(args, dev):
     def step(e2e):
         po, pd, di = trial_params(trial_rng, L)
         model.apply_expert_edit(po, pd, di, n_experts=spec["top_k"], strength=1.0)
-        kls.append(model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score())
+        kl = model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score()
+        tot = all_reduce(dist, np.array([kl * P, P], np.float64))
+        kls.append(tot[0] / tot[1])
 
     def timed(e2e, steps):
+        if dist:
+            dist.barrier()
         torch.cuda.synchronize()
         dev.synchronize()
         dev.timer_start()
         for _ in range(steps):
             step(e2e)
-        return dev.timer_stop()
+        ms = dev.timer_stop()
+        return float(all_reduce(dist, np.array([ms], np.float64), op="max")[0])
 
     for _ in range(args.warmup):
         step(False)
     dev.set_profiling(True)
     dev.reset_stats()
-    clocks = Clocks(0)
+    clocks = Clocks(torch.cuda.current_device())
     ms = timed(False, args.steps)
     clk = clocks.stop()
     gemm_ms, gemm_launches, gemm_flops = dev.gemm_stats()
@@ -568,16 +589,18 @@ def run_c4(args, dev):
     fl = c4_flops(spec, tokens)
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
     line = {
-        "metric": "trial-eval forward tokens/s", "value": round(tokens * args.steps / (ms / 1000.0), 1),
-        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "metric": "trial-eval forward tokens/s", "value": round(tokens * world * args.steps / (ms / 1000.0), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3), "s_per_trial": round(ms / args.steps / 1000.0, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "mxfp4 experts + bf16 attention, bf16 MMA, f32 accumulate", "data": "synthetic",
         "config": {"workload": "C4: Qwen3-MoE-shaped, 128 MXFP4 experts top-8, trial = expert-selective rank-1 edit "
                                "(o_proj + top-8 expert down per layer) + edited forward + first-token KL",
-                   "layers": L, "prompts_per_gpu": P, "seq_len": S, "vocab": V, "parallelism": "dp1",
+                   "layers": L, "prompts_per_gpu": P, "seq_len": S, "vocab": V,
+                   "parallelism": (f"ep{world} (experts {spec['n_experts'] // world} per GPU, rows exchanged over "
+                                   f"NVLink peer memory) x dp{world} (prompts)" if world > 1 else "dp1"),
                    "l2": "inputs larger than L2 (15.4 GB of MXFP4 experts per forward)"},
-        "e2e": {"value": round(tokens * args.steps / (ms_e2e / 1000.0), 1), "unit": "tokens/s",
+        "e2e": {"value": round(tokens * world * args.steps / (ms_e2e / 1000.0), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(tokens * 4 + (P + 1) * 8), "d2h_bytes_per_step": 8,
                 "ms_per_step": round(ms_e2e / args.steps, 3)},
         "roofline": {"bound": "tensor", "kernel": "gemm_kernel: tcgen05 grouped GEMM, MXFP4 decoded per tile",
@@ -586,35 +609,55 @@ def run_c4(args, dev):
                      "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
                      "gemm_share_of_step": round(gemm_ms / ms, 4) if ms > 0 else None,
                      "forward_tflop": round(fl / 1e12, 2),
-                     "forward_tflops_per_s": round(fl * args.steps / (ms / 1000.0) / 1e12, 1)},
+                     "forward_tflops_per_s": round(fl * world * args.steps / (ms / 1000.0) / 1e12, 1)},
         "gpu_launches": int(launches), "clocks": clk,
         "one_off": {"load_s": round(load_s, 2), "capture_and_directions_ms": round(capture_ms, 2)},
         "kl_last": kls[-1] if kls else None,
     }
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     model.close()
+    if group is not None:
+        dist.barrier()
+        group.close()
 
 
 def run(args):
     import torch
 
     import ditch_b200
+    from bench import dist_setup
 
-    torch.cuda.set_device(0)
-    dev = ditch_b200.Device(0)
+    world, rank, local, dist = dist_setup(args.gpus)
+    if world > 1 and args.config != "c4":
+        # only C4 shards (expert parallel); the others run on rank 0
+        if rank != 0:
+            dist.barrier()
+            dist.destroy_process_group()
+            return 0
+    torch.cuda.set_device(local)
+    dev = ditch_b200.Device(local)
     if args.stage_min_tokens is not None:
         dev.set_decode_staging(args.stage_min_tokens)
+    if args.config == "c4":
+        run_c4(args, dev, world, rank, dist)
+        dev.close()
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     if args.config == "gemm":
         run_gemm(args, dev)
     elif args.config == "c1":
         run_c1(args, dev)
     elif args.config == "c3":
         run_c3(args, dev)
-    elif args.config == "c4":
-        run_c4(args, dev)
     elif args.config == "c5":
         run_c5(args, dev)
     else:
         raise SystemExit(f"config {args.config} is not implemented")
     dev.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
