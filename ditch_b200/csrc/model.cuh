@@ -60,6 +60,7 @@ struct Config {
     int max_seq;
     int ep_rank = 0, ep_world = 1;  // expert parallelism: this rank's routed experts are [e0, e0 + e_loc)
     int e_loc = 0, e0 = 0;
+    int tp_rank = 0, tp_world = 1;  // tensor parallelism: heads, kv_heads and inter above are this rank's
     int qd() const { return heads * head_dim; }
     int kvd() const { return kv_heads * head_dim; }
     int qkv_width() const { return qd() + 2 * kvd(); }
@@ -130,6 +131,13 @@ int ensure_workspace(ditch_cuda_model *m, int n_tokens, int nc, int nl);
 
 // MoE MLP of layer `li`: post-norm of x, routing, experts, combine into x.
 int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n);
+
+// Tensor parallelism: region bytes per rank, this rank's send rows (where the
+// row-parallel GEMMs write their partial sums) and the all-reduce that adds
+// the summed partials of the first n rows into x.
+size_t tp_group_bytes(const Config &c, size_t max_tokens);
+float *tp_send_rows(ditch_cuda_model *m);
+int tp_allreduce_add(ditch_cuda_model *m, int n, float *x);
 
 // Expert scores of this rank's routed experts (`local` [e_loc]) gathered from
 // every rank of the model's peer group into `all` [n_experts].

@@ -376,6 +376,22 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
     c.moe_layers.assign(c.n_layers, 0);
     if (cfg->moe_layers)
         for (int i = 0; i < c.n_layers; i++) c.moe_layers[i] = cfg->moe_layers[i] ? 1 : 0;
+    c.tp_world = cfg->tp_world > 1 ? cfg->tp_world : 1;
+    c.tp_rank = c.tp_world > 1 ? cfg->tp_rank : 0;
+    REQUIRE(c.tp_rank >= 0 && c.tp_rank < c.tp_world, "tp_rank out of range");
+    if (c.tp_world > 1) {
+        bool any_moe = false;
+        for (uint8_t f : c.moe_layers) any_moe |= f != 0;
+        REQUIRE(!any_moe && c.ep_world == 1, "tensor parallelism is for dense models");
+        REQUIRE(c.heads % c.tp_world == 0 && c.kv_heads % c.tp_world == 0 && c.inter % (8 * c.tp_world) == 0,
+                "tensor parallelism needs heads, kv heads and inter / 8 divisible by tp_world");
+    }
+    // full (as stored) dimensions; the config keeps this rank's share
+    const int W_tp = c.tp_world, r_tp = c.tp_rank;
+    const int qd_full = c.qd(), kvd_full = c.kvd(), inter_full = c.inter;
+    c.heads /= W_tp;
+    c.kv_heads /= W_tp;
+    c.inter /= W_tp;
 
     std::map<std::string, const ditch_cuda_tensor *> byname;
     for (size_t i = 0; i < n_tensors; i++) {
@@ -386,8 +402,45 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
         auto it = byname.find(name);
         return it == byname.end() ? nullptr : it->second;
     };
-    const int H = c.hidden, qd = c.qd(), kvd = c.kvd();
+    const int H = c.hidden, qd = c.qd(), kvd = c.kvd();  // this rank's widths
     int st;
+    // Tensor-parallel shards: a tensor given whole is sliced (rows: a view;
+    // columns: a device copy of the window), one given at the shard's shape is
+    // taken as is. Views and copies live until the load returns.
+    std::vector<std::unique_ptr<ditch_cuda_tensor>> views;
+    std::vector<DevBuf> windows;
+    auto esz = [](const ditch_cuda_tensor *t) -> size_t {
+        return t->format == DITCH_FMT_F32 ? 4 : (t->format == DITCH_FMT_BF16 || t->format == DITCH_FMT_F16) ? 2 : 0;
+    };
+    auto shard_rows = [&](const ditch_cuda_tensor *t, size_t full, size_t part) -> const ditch_cuda_tensor * {
+        if (!t || W_tp == 1 || t->rows == part) return t;
+        if (t->rows != full || !esz(t) || t->slabs > 1) return nullptr;
+        const size_t e = esz(t);
+        views.emplace_back(new ditch_cuda_tensor(*t));
+        ditch_cuda_tensor *v = views.back().get();
+        v->data = static_cast<const uint8_t *>(t->data) + (size_t)r_tp * part * t->cols * e;
+        v->rows = part;
+        v->data_bytes = part * t->cols * e;
+        return v;
+    };
+    auto shard_cols = [&](const ditch_cuda_tensor *t, size_t full, size_t part) -> const ditch_cuda_tensor * {
+        if (!t || W_tp == 1 || t->cols == part) return t;
+        if (t->cols != full || !esz(t) || t->slabs > 1) return nullptr;
+        const size_t e = esz(t);
+        windows.emplace_back();
+        DevBuf &w = windows.back();
+        if (w.reserve(t->rows * part * e) != cudaSuccess) return nullptr;
+        if (cudaMemcpy2D(w.ptr, part * e, static_cast<const uint8_t *>(t->data) + (size_t)r_tp * part * e, full * e,
+                         part * e, t->rows, kind_of(t)) != cudaSuccess)
+            return nullptr;
+        views.emplace_back(new ditch_cuda_tensor(*t));
+        ditch_cuda_tensor *v = views.back().get();
+        v->data = w.ptr;
+        v->cols = part;
+        v->data_bytes = t->rows * part * e;
+        v->on_device = 1;
+        return v;
+    };
     // embedding table: bf16 or f32 as stored
     const ditch_cuda_tensor *emb = get("embed");
     REQUIRE(emb && emb->rows == (size_t)c.vocab && emb->cols == (size_t)H, "embed [vocab][hidden] missing");
@@ -429,12 +482,20 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
         }
         const ditch_cuda_tensor *q = t("q"), *k = t("k"), *v = t("v"), *o = t("o");
         REQUIRE(q && k && v && o, "layer %d: attention projections missing", i);
+        if (W_tp > 1) {
+            q = shard_rows(q, qd_full, qd);
+            k = shard_rows(k, kvd_full, kvd);
+            v = shard_rows(v, kvd_full, kvd);
+            o = shard_cols(o, qd_full, qd);
+            REQUIRE(q && k && v && o, "layer %d: tensor-parallel shards need f32 / f16 / bf16 q, k, v, o", i);
+        }
         REQUIRE(q->rows == (size_t)qd && k->rows == (size_t)kvd && v->rows == (size_t)kvd && q->cols == (size_t)H,
                 "layer %d: q/k/v shapes", i);
         REQUIRE(o->rows == (size_t)H && o->cols == (size_t)qd, "layer %d: o shape", i);
         if ((st = build_mat(m.get(), {Seg{q, 0}, Seg{k, 0}, Seg{v, 0}}, 1, L.qkv, "qkv"))) return st;
         if ((st = build_mat(m.get(), {Seg{o, 0}}, 1, L.o, "o"))) return st;
-        const ditch_cuda_tensor *qb = t("qb"), *kb = t("kb"), *vb = t("vb");
+        const ditch_cuda_tensor *qb = shard_rows(t("qb"), qd_full, qd), *kb = shard_rows(t("kb"), kvd_full, kvd),
+                                *vb = shard_rows(t("vb"), kvd_full, kvd);
         if (qb || kb || vb) {
             std::vector<float> zeros(c.qkv_width(), 0.0f);
             DITCH_CUDA(L.qkv_bias.reserve(c.qkv_width() * 4));
@@ -489,6 +550,12 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
         } else {
             const ditch_cuda_tensor *g = t("gate"), *u = t("up"), *d = t("down");
             REQUIRE(g && u && d, "layer %d: MLP projections missing", i);
+            if (W_tp > 1) {
+                g = shard_rows(g, inter_full, c.inter);
+                u = shard_rows(u, inter_full, c.inter);
+                d = shard_cols(d, inter_full, c.inter);
+                REQUIRE(g && u && d, "layer %d: tensor-parallel shards need f32 / f16 / bf16 gate, up, down", i);
+            }
             REQUIRE(g->rows == (size_t)c.inter && u->rows == (size_t)c.inter && g->cols == (size_t)H &&
                         d->rows == (size_t)H && d->cols == (size_t)c.inter,
                     "layer %d: MLP shapes", i);

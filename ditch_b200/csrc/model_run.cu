@@ -267,6 +267,10 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
     cudaStream_t st = dev->stream;
     const int n = b.n, H = c.hidden, qd = c.qd(), W = c.qkv_width();
     int s;
+    if (m->group && c.tp_world > 1 && (size_t)n > m->group_tokens) {
+        set_error("%d tokens exceed the %zu the peer group was sized for", n, m->group_tokens);
+        return DITCH_CUDA_INVALID;
+    }
     if ((s = ensure_workspace(m, n, nc, nl))) return s;
     float *x = m->x.as<float>();
     uint16_t *h = m->h.as<uint16_t>();
@@ -301,9 +305,12 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
         ap.max_len = b.h_len.empty() ? 1 : *std::max_element(b.h_len.begin(), b.h_len.end());
         DITCH_LAUNCH(dev, attention_prefill(ap, st));
         if (L.o_edit) DITCH_LAUNCH(dev, rowdot_bf16(m->att.as<uint16_t>(), L.o_a.as<float>(), n, qd, m->xa.as<float>(), st));
-        if ((s = gemm_weight(m, L.o, 0, H, m->att.as<uint16_t>(), n, x, H, kEpiResidual, nullptr,
-                             L.o_edit ? m->xa.as<float>() : nullptr, L.o_edit ? L.o_b.as<float>() : nullptr, 0)))
+        // tensor parallel: the partial sum goes to the group's send rows, then the all-reduce adds it to x
+        const bool tp = m->group && c.tp_world > 1;
+        if ((s = gemm_weight(m, L.o, 0, H, m->att.as<uint16_t>(), n, tp ? tp_send_rows(m) : x, H, tp ? 0 : kEpiResidual,
+                             nullptr, L.o_edit ? m->xa.as<float>() : nullptr, L.o_edit ? L.o_b.as<float>() : nullptr, 0)))
             return s;
+        if (tp && (s = tp_allreduce_add(m, n, x))) return s;
         if (L.moe) {
             if ((s = moe_mlp(m, L, li, n))) return s;
         } else {
@@ -314,10 +321,11 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
                 return s;
             if (L.down_edit)
                 DITCH_LAUNCH(dev, rowdot_bf16(m->act.as<uint16_t>(), L.down_a.as<float>(), n, Ip, m->xa.as<float>(), st));
-            if ((s = gemm_weight(m, L.down, 0, H, m->act.as<uint16_t>(), n, x, H, kEpiResidual, nullptr,
-                                 L.down_edit ? m->xa.as<float>() : nullptr, L.down_edit ? L.down_b.as<float>() : nullptr,
-                                 0)))
+            if ((s = gemm_weight(m, L.down, 0, H, m->act.as<uint16_t>(), n, tp ? tp_send_rows(m) : x, H,
+                                 tp ? 0 : kEpiResidual, nullptr, L.down_edit ? m->xa.as<float>() : nullptr,
+                                 L.down_edit ? L.down_b.as<float>() : nullptr, 0)))
                 return s;
+            if (tp && (s = tp_allreduce_add(m, n, x))) return s;
         }
     }
     if (res) {

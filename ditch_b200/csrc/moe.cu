@@ -618,14 +618,7 @@ namespace {
 
 // One exchange of the model's peer group: signal this rank's epoch to every
 // peer, then wait (bounded) until every peer has signalled it.
-int ep_exchange(ditch_cuda_model *m) {
-    ditch_cuda_device *dev = m->dev;
-    ditch_cuda_group *g = m->group;
-    const uint64_t ep = ++g->epoch;
-    DITCH_LAUNCH(dev, peer_signal(g->peers, g->rank, g->world, ep, dev->stream));
-    DITCH_LAUNCH(dev, peer_wait(g->base, g->world, ep, dev->status, 30.0, dev->stream));
-    return DITCH_CUDA_OK;
-}
+int ep_exchange(ditch_cuda_model *m) { return group_exchange(m->dev, m->group, 30.0); }
 
 }  // namespace
 
@@ -794,23 +787,26 @@ int ep_allgather_scores(ditch_cuda_model *m, const std::vector<float> &local, st
 extern "C" {
 
 size_t ditch_cuda_model_group_bytes(const ditch_cuda_model *m, size_t max_tokens) {
-    if (!m || m->cfg.ep_world <= 1) return 0;
-    return ditch::ep_layout(m->cfg, max_tokens).end;
+    if (!m) return 0;
+    if (m->cfg.ep_world > 1) return ditch::ep_layout(m->cfg, max_tokens).end;
+    if (m->cfg.tp_world > 1) return ditch::tp_group_bytes(m->cfg, max_tokens);
+    return 0;
 }
 
 int ditch_cuda_model_set_group(ditch_cuda_model *m, ditch_cuda_group *g, size_t max_tokens) {
     using namespace ditch;
     clear_error();
     EP_REQUIRE(m && g, "null argument");
-    EP_REQUIRE(m->cfg.ep_world > 1, "the model was loaded without expert parallelism (ep_world <= 1)");
+    const Config &c = m->cfg;
+    const bool ep = c.ep_world > 1, tp = c.tp_world > 1;
+    EP_REQUIRE(ep || tp, "the model was loaded without expert or tensor parallelism");
     EP_REQUIRE(g->opened, "the group is not opened");
     EP_REQUIRE(g->dev == m->dev, "the group lives on another device");
-    EP_REQUIRE(g->world == m->cfg.ep_world && g->rank == m->cfg.ep_rank,
-               "group rank %d / world %d differ from the model's ep_rank %d / ep_world %d", g->rank, g->world,
-               m->cfg.ep_rank, m->cfg.ep_world);
+    EP_REQUIRE(g->world == (ep ? c.ep_world : c.tp_world) && g->rank == (ep ? c.ep_rank : c.tp_rank),
+               "group rank %d / world %d differ from the model's", g->rank, g->world);
     EP_REQUIRE(max_tokens > 0, "max_tokens must be positive");
-    EP_REQUIRE(ep_layout(m->cfg, max_tokens).end <= g->bytes, "the group region holds %zu bytes; %zu needed", g->bytes,
-               (size_t)ep_layout(m->cfg, max_tokens).end);
+    const size_t need = ep ? ep_layout(c, max_tokens).end : tp_group_bytes(c, max_tokens);
+    EP_REQUIRE(need <= g->bytes, "the group region holds %zu bytes; %zu needed", g->bytes, need);
     std::lock_guard<std::mutex> lk(m->dev->mu);
     m->group = g;
     m->group_tokens = max_tokens;

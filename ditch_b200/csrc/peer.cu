@@ -61,6 +61,13 @@ cudaError_t peer_wait(uint8_t *own, int world, uint64_t epoch, int *status, doub
     return cudaGetLastError();
 }
 
+int group_exchange(ditch_cuda_device *dev, ditch_cuda_group *g, double budget_s) {
+    const uint64_t ep = ++g->epoch;
+    DITCH_LAUNCH(dev, peer_signal(g->peers, g->rank, g->world, ep, dev->stream));
+    DITCH_LAUNCH(dev, peer_wait(g->base, g->world, ep, dev->status, budget_s, dev->stream));
+    return DITCH_CUDA_OK;
+}
+
 }  // namespace ditch
 
 extern "C" {

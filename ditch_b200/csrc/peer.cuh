@@ -60,4 +60,9 @@ namespace ditch {
 // Flag block at the head of every region: [kMaxPeers] u64, slot s written by rank s.
 constexpr size_t kPeerFlagBytes = 256;
 inline uint8_t *peer_data(uint8_t *region) { return region + kPeerFlagBytes; }
+
+// One exchange on the device's stream: signal the next epoch to every peer,
+// then wait (bounded by budget_s; then the status word reports a timeout)
+// until every peer has signalled it.
+int group_exchange(ditch_cuda_device *dev, ditch_cuda_group *g, double budget_s);
 }  // namespace ditch

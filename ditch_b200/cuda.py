@@ -46,7 +46,7 @@ class ModelConfig(C.Structure):
         ("rope_low_ff", C.c_double), ("rope_high_ff", C.c_double), ("rope_orig_max", C.c_double),
         ("qk_norm", C.c_int), ("n_experts", C.c_int), ("top_k", C.c_int), ("moe_inter", C.c_int),
         ("norm_topk", C.c_int), ("moe_layers", C.POINTER(C.c_uint8)), ("max_seq", C.c_int),
-        ("ep_rank", C.c_int), ("ep_world", C.c_int),
+        ("ep_rank", C.c_int), ("ep_world", C.c_int), ("tp_rank", C.c_int), ("tp_world", C.c_int),
     ]
 
 
@@ -452,7 +452,7 @@ class Group:
 class Model:
     """A model resident in HBM (the coarse C-ABI entries)."""
 
-    def __init__(self, device, spec, tensors, max_seq=4096, ep_rank=0, ep_world=1):
+    def __init__(self, device, spec, tensors, max_seq=4096, ep_rank=0, ep_world=1, tp_rank=0, tp_world=1):
         self.dev = device
         self.spec = spec
         cfg = ModelConfig(
@@ -463,7 +463,7 @@ class Model:
             rope_high_ff=spec.get("rope_high_ff", 1.0), rope_orig_max=spec.get("rope_orig_max", 1.0),
             qk_norm=int(spec.get("qk_norm", 0)), n_experts=spec.get("n_experts", 0), top_k=spec.get("top_k", 0),
             moe_inter=spec.get("moe_inter", 0), norm_topk=int(spec.get("norm_topk", 1)), max_seq=max_seq,
-            ep_rank=ep_rank, ep_world=ep_world)
+            ep_rank=ep_rank, ep_world=ep_world, tp_rank=tp_rank, tp_world=tp_world)
         self._moe = None
         if spec.get("moe_layers"):
             self._moe = np.array([1 if x else 0 for x in spec["moe_layers"]], np.uint8)
@@ -489,11 +489,11 @@ class Model:
         return int(lib().ditch_cuda_model_bytes(self.h))
 
     def group_bytes(self, max_tokens):
-        """Peer-group region bytes this expert-parallel model needs."""
+        """Peer-group region bytes this expert- or tensor-parallel model needs."""
         return int(lib().ditch_cuda_model_group_bytes(self.h, max_tokens))
 
     def set_group(self, group, max_tokens):
-        """Runs the routed-expert layers expert-parallel over `group`."""
+        """Runs the model expert- or tensor-parallel (as loaded) over `group`."""
         check(lib().ditch_cuda_model_set_group(self.h, group.h, max_tokens))
         self._group = group  # the group outlives the model's use of it
 

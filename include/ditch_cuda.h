@@ -139,6 +139,13 @@ typedef struct {
      * (ep_rank + 1) E / ep_world) of the stacks it is given and runs MoE
      * layers through a peer group (ditch_cuda_model_set_group). */
     int ep_rank, ep_world;
+    /* Tensor parallelism over tp_world ranks (0 or 1: none; dense models,
+     * f32 / f16 / bf16 weights): this rank keeps query heads [tp_rank H_q /
+     * tp_world, ...), the matching kv heads and MLP columns; q / k / v / gate /
+     * up are split by rows and o / down by columns. Tensors may be given whole
+     * (the loader takes this rank's slice) or already sharded. o / down
+     * partial sums are all-reduced over the peer group after each layer. */
+    int tp_rank, tp_world;
 } ditch_cuda_model_config;
 
 /* Storage formats of a resident tensor. */
@@ -311,10 +318,14 @@ void ditch_cuda_group_free(ditch_cuda_group *g);
 /* A device-side barrier over the group (bounded: returns
  * DITCH_CUDA_DEVICE_FAILED when a peer does not arrive within 20 s). */
 int ditch_cuda_group_barrier(ditch_cuda_group *g);
-/* Region bytes that a model loaded with ep_world > 1 needs for forwards of
- * at most max_tokens tokens per rank (0 without expert parallelism). */
+/* Region bytes that a model loaded with ep_world > 1 or tp_world > 1 needs
+ * for forwards of at most max_tokens tokens per rank (0 without either). */
 size_t ditch_cuda_model_group_bytes(const ditch_cuda_model *m, size_t max_tokens);
-/* Runs the model's routed-expert layers expert-parallel over the group: each
+/* Tensor parallel (tp_world > 1): every rank runs the same tokens on its
+ * shard of the attention heads and MLP columns, and the o_proj / down_proj
+ * partial sums are all-reduced over the group (rank-ordered sums read over
+ * NVLink), so every rank holds the same residual stream and logits.
+ * Expert parallel (ep_world > 1): runs the model's routed-expert layers over the group: each
  * rank routes its own tokens, sends every (token, expert) row to the expert's
  * owner over NVLink, runs its experts' grouped GEMMs on every rank's rows and
  * returns the outputs; the combine then equals the single-GPU one bit for

@@ -1,0 +1,107 @@
+"""Tensor parallelism over a peer group on two GPUs (one process each).
+
+Each rank loads the whole tensors and keeps its shard: half the query and kv
+heads (q / k / v rows, o columns) and half the MLP columns (gate / up rows,
+down columns). The o_proj and down_proj partial sums are all-reduced over
+NVLink peer memory after every layer. Both ranks run the same prompts and
+must hold identical residual streams and logits (every element is one sum in
+rank order); against the single-GPU model the products are split over K, so
+the results agree to rounding: within the forward bound of
+`test_gpu_model.py`, max |err| <= 2e-3 + 2e-2 max |ref|, and in practice far
+closer. The none-mode edit of o_proj / down_proj is local to each shard
+(src/abliterate.zig:264-280: A = v^T W splits by columns with W), so the
+edited forward must agree the same way.
+
+Needs two GPUs; skipped otherwise."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, out_dir):
+    import sys
+
+    for p in (ROOT, os.path.join(ROOT, "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ditch_b200
+    from oracle.model import flatten_batch
+    from synth import make_model, prompts
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    dev = ditch_b200.Device(rank)
+    spec, f32, tensors = make_model(500, n_layers=3, hidden=256, head_dim=64, heads=4, kv_heads=2, inter=512,
+                                    qkv_bias=True)
+    ps = prompts(77, [40, 17, 64, 3, 70], spec["vocab"])  # the same prompts on every rank
+    toks, rb, rp, cap, first, take, last = flatten_batch(ps, 2)
+    max_tokens = 256
+
+    def exchange(h):
+        out = [None] * world
+        dist.all_gather_object(out, h)
+        return out
+
+    one = ditch_b200.Model(dev, spec, tensors, max_seq=128)
+    tp = ditch_b200.Model(dev, spec, tensors, max_seq=128, tp_rank=rank, tp_world=world)
+    group = ditch_b200.Group(dev, rank, world, tp.group_bytes(max_tokens), exchange)
+    tp.set_group(group, max_tokens)
+    dist.barrier()
+    res1, log1 = one.forward(toks, rb, rp, cap, last)
+    res2, log2 = tp.forward(toks, rb, rp, cap, last)
+    rng = np.random.default_rng(3)
+    dirs = rng.standard_normal((spec["n_layers"] + 1, spec["hidden"])).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    for m in (one, tp):
+        m.set_directions(dirs)
+        m.apply_edit((1.2, 1.5, 0.5, 2.0), (1.1, 1.0, 0.4, 2.0), None)
+    res3, log3 = one.forward(toks, rb, rp, cap, last)
+    res4, log4 = tp.forward(toks, rb, rp, cap, last)
+    group.barrier()
+    np.savez(os.path.join(out_dir, f"r{rank}.npz"), res1=res1, log1=log1, res2=res2, log2=log2, res3=res3, log3=log3,
+             res4=res4, log4=log4)
+    tp.close()
+    one.close()
+    dist.barrier()
+    group.close()
+    dev.close()
+    dist.destroy_process_group()
+
+
+def test_tensor_parallel_forward_matches_one_gpu(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    z0, z1 = np.load(tmp_path / "r0.npz"), np.load(tmp_path / "r1.npz")
+    for key in ("res2", "log2", "res4", "log4"):
+        assert np.array_equal(z0[key], z1[key]), key  # replicated streams are identical
+    for a, b in (("res1", "res2"), ("log1", "log2"), ("res3", "res4"), ("log3", "log4")):
+        ref, got = z0[a], z0[b]
+        err = float(np.abs(got - ref).max())
+        bound = 2e-3 + 2e-2 * float(np.abs(ref).max())
+        assert err <= bound, (a, b, err, bound)
+        print(f"{a} vs {b}: max |err| {err:.3e} (bound {bound:.3e})")
+    assert not np.array_equal(z0["log1"], z0["log3"]), "the edit changed nothing"
