@@ -6,9 +6,13 @@
   GGUF Q4_K, INT4 (group 128, packed zero points) and MXFP4, with bf16
   activations for M in {1, 16, 128, 1024, 8192}. The sweep reports TFLOP/s
   (M >= 128) or weight-stream GB/s (M < 128) per case.
-* `c5`: the in-place rank-1 edit W <- W - alpha_l r_l (r_l^T W) on all 80
-  o_proj [8192 x 8192] and down_proj [8192 x 28672] bf16 matrices of a
-  Llama-3-70B shape. It reports HBM GB/s over the algorithmic 3 x 48.32 GB.
+* `c5`: on one GPU, the in-place rank-1 edit W <- W - alpha_l r_l (r_l^T W)
+  on all 80 o_proj [8192 x 8192] and down_proj [8192 x 28672] bf16 matrices
+  of a Llama-3-70B shape (HBM GB/s over the algorithmic 3 x 48.32 GB). Under
+  torchrun with 2 or more GPUs, the C5 trial tensor-parallel: the 141 GB
+  model split by heads and MLP columns, 64 prompts x 32 tokens, the none-mode
+  edit of every o_proj / down_proj shard, the forward with the o / down
+  partial sums all-reduced over NVLink peer memory, and the first-token KL.
 * `c1`: BASELINE config 1, the Qwen2-0.5B-shaped fp32 model (24 layers,
   hidden 896, 14/2 heads of 64, SwiGLU 4864, vocab 151936, q/k/v biases, tied
   embedding, seeded N(0, 0.02) f32 weights) with two batches of 64 prompts x
@@ -622,6 +626,154 @@ def run_c4(args, dev, world=1, rank=0, dist=None):
         group.close()
 
 
+C5 = dict(n_layers=80, hidden=8192, heads=64, kv_heads=8, head_dim=128, inter=28672, vocab=128256, eps=1e-5,
+          rope_theta=5e5)
+
+
+def build_c5_shards(dev, spec, seed, rank, world, max_seq):
+    """The Llama-3-70B-shaped bf16 model as this rank's tensor-parallel shards:
+    q / k / v / gate / up rows and o / down columns of the rank, each drawn
+    N(0, 0.02) from a seed of (layer, tensor, rank), so the ranks together hold
+    one consistent random model. Embedding, LM head and norms are replicated
+    (same seed on every rank)."""
+    import torch
+
+    import ditch_b200
+    from ditch_b200 import Tensor
+
+    H, I, V, L = spec["hidden"], spec["inter"], spec["vocab"], spec["n_layers"]
+    qd, kvd = spec["heads"] * spec["head_dim"], spec["kv_heads"] * spec["head_dim"]
+    qs, ks, isz = qd // world, kvd // world, I // world
+    keep, tensors = [], []
+
+    def gen(tag, shape):
+        g = torch.Generator(device="cuda").manual_seed(seed * 1000003 + tag)
+        w = torch.empty(shape, dtype=torch.bfloat16, device="cuda")
+        w.normal_(0.0, 0.02, generator=g)
+        keep.append(w)
+        return w
+
+    ones = torch.ones(H, dtype=torch.bfloat16, device="cuda")
+    keep.append(ones)
+    tensors += [Tensor("embed", "bf16", V, H, gen(1, (V, H))), Tensor("lm_head", "bf16", V, H, gen(2, (V, H))),
+                Tensor("final_norm", "bf16", H, 1, ones)]
+    for i in range(L):
+        base = 16 + (i * 8 + 0) * 64 + rank * 8
+        tensors += [Tensor(f"L{i}.input_norm", "bf16", H, 1, ones), Tensor(f"L{i}.post_norm", "bf16", H, 1, ones),
+                    Tensor(f"L{i}.q", "bf16", qs, H, gen(base + 0, (qs, H))),
+                    Tensor(f"L{i}.k", "bf16", ks, H, gen(base + 1, (ks, H))),
+                    Tensor(f"L{i}.v", "bf16", ks, H, gen(base + 2, (ks, H))),
+                    Tensor(f"L{i}.o", "bf16", H, qs, gen(base + 3, (H, qs))),
+                    Tensor(f"L{i}.gate", "bf16", isz, H, gen(base + 4, (isz, H))),
+                    Tensor(f"L{i}.up", "bf16", isz, H, gen(base + 5, (isz, H))),
+                    Tensor(f"L{i}.down", "bf16", H, isz, gen(base + 6, (H, isz)))]
+    torch.cuda.synchronize()
+    model = ditch_b200.Model(dev, spec, tensors, max_seq=max_seq, tp_rank=rank, tp_world=world)
+    del keep, tensors
+    torch.cuda.empty_cache()
+    return model
+
+
+def run_c5_tp(args, dev, world, rank, dist):
+    """The C5 trial tensor-parallel over `world` GPUs (strong scaling: every
+    rank works on the same 64 x 32 tokens with its shard of the weights): the
+    none-mode edit of all o_proj / down_proj shards (A = v^T W per shard, no
+    exchange), the edited forward with the o / down partial sums all-reduced
+    over NVLink peer memory, and the first-token KL."""
+    import torch
+
+    import ditch_b200
+    from bench import Clocks, all_reduce, measured_peaks, trial_params
+
+    L = args.layers or C5["n_layers"]
+    spec = dict(C5, n_layers=L)
+    P, S = args.prompts or 64, 32
+    H = spec["hidden"]
+    t0 = time.time()
+    model = build_c5_shards(dev, spec, args.seed, rank, world, max_seq=S)
+
+    def exchange(h):
+        out = [None] * world
+        dist.all_gather_object(out, h)
+        return out
+
+    group = ditch_b200.Group(dev, rank, world, model.group_bytes(P * S), exchange)
+    model.set_group(group, P * S)
+    dist.barrier()
+    load_s = time.time() - t0
+    rng = np.random.default_rng(args.seed + 5)
+    kl_prompts = [rng.integers(0, spec["vocab"], S).astype(np.uint32) for _ in range(P)]  # same on every rank
+    dirs = rng.standard_normal((L + 1, H)).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)  # r_l = normalise(N(0, 1))
+    model.set_directions(dirs)
+    model.kl_init(kl_prompts)
+    tokens_flat = np.concatenate(kl_prompts).astype(np.uint32)
+    offs = np.zeros(P + 1, np.uintp)
+    offs[1:] = np.cumsum([len(p) for p in kl_prompts])
+    trial_rng = np.random.default_rng(args.seed + 7)
+    kls = []
+
+    def step(e2e):
+        po, pd, di = trial_params(trial_rng, L)
+        model.apply_edit(po, pd, None)
+        kls.append(model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score())
+
+    def timed(e2e, steps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        dev.synchronize()
+        dev.timer_start()
+        for _ in range(steps):
+            step(e2e)
+        ms = dev.timer_stop()
+        return float(all_reduce(dist, np.array([ms], np.float64), op="max")[0])
+
+    for _ in range(args.warmup):
+        step(False)
+    dev.set_profiling(True)
+    dev.reset_stats()
+    clocks = Clocks(torch.cuda.current_device())
+    ms = timed(False, args.steps)
+    clk = clocks.stop()
+    gemm_ms, gemm_launches, gemm_flops = dev.gemm_stats()
+    launches = dev.launches()
+    dev.set_profiling(False)
+    for _ in range(max(1, args.warmup // 2)):
+        step(True)
+    ms_e2e = timed(True, args.steps)
+    hbm, tf_burst, tf_sust, src = measured_peaks()
+    tokens = P * S
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
+    line = {
+        "metric": "trial-eval forward tokens/s", "value": round(tokens * args.steps / (ms / 1000.0), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3), "s_per_trial": round(ms / args.steps / 1000.0, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16 weights, f32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": "C5: Llama-3-70B-shaped bf16, trial = none-mode rank-1 edit of every o_proj/down_proj "
+                               "shard + edited forward + first-token KL",
+                   "layers": L, "prompts": P, "seq_len": S, "vocab": spec["vocab"],
+                   "parallelism": f"tp{world} (heads and MLP columns; o/down partials all-reduced over NVLink peer "
+                                  f"memory)",
+                   "l2": f"weights {141.1 / world:.1f} GB per GPU, read once per forward"},
+        "e2e": {"value": round(tokens * args.steps / (ms_e2e / 1000.0), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(tokens * 4 + (P + 1) * 8), "d2h_bytes_per_step": 8,
+                "ms_per_step": round(ms_e2e / args.steps, 3)},
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel: tcgen05 bf16 MMA (this rank's shards)",
+                     "achieved": round(achieved, 1), "peak": tf_sust, "unit": "TFLOP/s",
+                     "frac": round(achieved / tf_sust, 4), "peak_source": f"{src} bf16 sustained", "traffic": None,
+                     "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
+                     "gemm_share_of_step": round(gemm_ms / ms, 4) if ms > 0 else None},
+        "gpu_launches": int(launches), "clocks": clk, "one_off": {"load_s": round(load_s, 2)},
+        "kl_last": kls[-1] if kls else None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    dist.barrier()
+    group.close()
+
+
 def run(args):
     import torch
 
@@ -629,7 +781,7 @@ def run(args):
     from bench import dist_setup
 
     world, rank, local, dist = dist_setup(args.gpus)
-    if world > 1 and args.config != "c4":
+    if world > 1 and args.config not in ("c4", "c5"):
         # only C4 shards (expert parallel); the others run on rank 0
         if rank != 0:
             dist.barrier()
@@ -639,8 +791,11 @@ def run(args):
     dev = ditch_b200.Device(local)
     if args.stage_min_tokens is not None:
         dev.set_decode_staging(args.stage_min_tokens)
-    if args.config == "c4":
-        run_c4(args, dev, world, rank, dist)
+    if args.config == "c4" or (args.config == "c5" and world > 1):
+        if args.config == "c4":
+            run_c4(args, dev, world, rank, dist)
+        else:
+            run_c5_tp(args, dev, world, rank, dist)
         dev.close()
         if dist:
             dist.barrier()
