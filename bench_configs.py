@@ -408,8 +408,8 @@ def run_c1(args, dev):
     tokens = P * S
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
     line = {
-        "metric": "trial-eval forward tokens/s", "value": round(tokens * world * args.steps / (ms / 1000.0), 1),
-        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "metric": "trial-eval forward tokens/s", "value": round(tokens * args.steps / (ms / 1000.0), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3), "s_per_trial": round(ms / args.steps / 1000.0, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 weights run as bf16 MMA with f32 accumulate", "data": "synthetic",

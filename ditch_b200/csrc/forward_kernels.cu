@@ -285,181 +285,226 @@ __global__ void __launch_bounds__(256) k_qk_prep(float *qkv, AttnParams p) {
     }
 }
 
-// ---- register-tiled attention for head_dim 64 / 128 ----------------------
+// ---- tensor-core attention for head_dim 64 / 128 -------------------------
 // Block = (prompt, kv head and part of its group, chunk of 64 query
-// positions); 256 threads; up to kMaxHeads query heads of the group one after
-// another, so a prompt whose keys fit one 64-key chunk stages K and V once
-// for them. Q (64 rows) and each
-// 64-key chunk of K are staged transposed in f32 shared memory (rows across
-// lanes: conflict-free), V natural, from rows already normed and roped.
-// Scores: thread (ty, tx) owns queries 4ty..4ty+3 x keys 4tx..4tx+3 (two
-// LDS.128 per 16 FMAs); the output: the same 4 queries x HD/16 dimensions
-// (float4 groups tx, tx + 16, ..., so a quarter-warp's value loads are
-// conflict-free). Online softmax across key chunks, f32.
+// positions); 4 warps, warp w owns query rows 16w .. 16w + 15 of the chunk.
+// Up to kMaxHeads query heads of the group run one after another, so a prompt
+// whose keys fit one 64-key chunk stages K and V once for them. Q, K and V
+// (already normed and roped by k_qk_prep) are staged in shared memory as
+// bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi)); every product is
+// hi*hi + hi*lo + lo*hi on mma.sync m16n8k16 with f32 accumulation, which
+// keeps the scores and the P.V sums to about 2^-16 relative (f32-like). The
+// scores never leave registers: the S accumulator fragments are the A
+// operand of the P.V product. Online softmax in f32 across key chunks; the
+// causal limit skips the 8-key tiles and 16-key steps above each warp's rows.
 constexpr int kQB = 64, kKB = 64;
 constexpr int kMaxHeads = 4;  // query heads per block
 
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// (a, b) -> bf16x2 hi and the bf16x2 of the remainders (low half = a).
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    hi = pack_bf16x2(a, b);
+    const float ah = __uint_as_float(hi << 16), bh = __uint_as_float(hi & 0xffff0000u);
+    lo = pack_bf16x2(a - ah, b - bh);
+}
+
 template <int HD>
-__global__ void __launch_bounds__(256) k_attention_tiled(AttnParams p) {
-    extern __shared__ float sm[];
-    float *qt = sm;                    // [HD][kQB]
-    float *kt = qt + HD * kQB;         // [HD][kKB]
-    float *vs = kt + HD * kKB;         // [kKB][HD]
-    float *pt = vs + kKB * HD;         // [kKB][kQB]
+__global__ void __launch_bounds__(128) k_attention_mma(AttnParams p) {
+    constexpr int QS = HD + 8;   // row stride (bf16) of the Q and K tiles: conflict-free fragment loads
+    constexpr int VS = kKB + 8;  // row stride of the transposed V tile
+    constexpr int C4 = HD / 4;
+    extern __shared__ __align__(16) uint16_t smb[];
+    uint16_t *qh = smb, *ql = qh + kQB * QS;
+    uint16_t *kh = ql + kQB * QS, *kl = kh + kKB * QS;
+    uint16_t *vh = kl + kKB * QS, *vl = vh + HD * VS;  // [dim][key]
     const int nh = p.heads, nkv = p.kv_heads, groups = nh / nkv;
-    // blockIdx.y = (kv head, part): a group wider than kMaxHeads query heads
-    // is split over several blocks (each stages its own K / V)
     const int parts = (groups + kMaxHeads - 1) / kMaxHeads;
     const int kvh = blockIdx.y / parts, part = blockIdx.y % parts;
-    const int g0 = part * kMaxHeads, g1 = min(groups, g0 + kMaxHeads);
+    const int gh0 = part * kMaxHeads, gh1 = min(groups, gh0 + kMaxHeads);
     const int b = blockIdx.x, i0 = blockIdx.z * kQB;
     const int start = p.seq_start[b], len = p.seq_len[b];
     if (i0 >= len) return;
     const int qd = nh * HD, kvd = nkv * HD, width = qd + 2 * kvd;
-    const int tid = threadIdx.x;
-    const int ty = tid >> 4, tx = tid & 15;
-    constexpr int DPT = HD / 16;  // output dimensions per thread
-    constexpr int C4 = HD / 4;    // float4 per row
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+    const int r0 = 16 * w;                      // this warp's first row in the chunk
     const int last_q = min(len, i0 + kQB) - 1;  // causal: keys 0 .. last_q
     const bool one_chunk = last_q < kKB;
+    const int row_a = i0 + r0 + g, row_b = row_a + 8;            // this thread's two query positions
+    const int warp_last = min(i0 + r0 + 15, len - 1);            // last query position of the warp
 
-    for (int g = g0; g < g1; g++) {
-        const int h = kvh * groups + g;
+    auto ld32 = [](const uint16_t *p_) { return *reinterpret_cast<const uint32_t *>(p_); };
+
+    for (int gh = gh0; gh < gh1; gh++) {
+        const int h = kvh * groups + gh;
         __syncthreads();  // the previous head's reads of the buffers are done
-        for (int idx = tid; idx < kQB * C4; idx += 256) {
-            const int r = idx % kQB, c4 = idx / kQB, i = i0 + r;
+        for (int idx = tid; idx < kQB * C4; idx += 128) {
+            const int r = idx / C4, c4 = idx % C4, i = i0 + r;
             float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             if (i < len) q = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + i) * width + h * HD + 4 * c4);
-            qt[(4 * c4 + 0) * kQB + r] = q.x;
-            qt[(4 * c4 + 1) * kQB + r] = q.y;
-            qt[(4 * c4 + 2) * kQB + r] = q.z;
-            qt[(4 * c4 + 3) * kQB + r] = q.w;
+            uint2 hi, lo;
+            split_bf16x2(q.x, q.y, hi.x, lo.x);
+            split_bf16x2(q.z, q.w, hi.y, lo.y);
+            *reinterpret_cast<uint2 *>(qh + r * QS + 4 * c4) = hi;
+            *reinterpret_cast<uint2 *>(ql + r * QS + 4 * c4) = lo;
         }
-        float m[4], l[4], o[4][DPT];
+        float o[HD / 8][4];
 #pragma unroll
-        for (int a = 0; a < 4; a++) {
-            m[a] = -INFINITY;
-            l[a] = 0.0f;
-#pragma unroll
-            for (int c = 0; c < DPT; c++) o[a][c] = 0.0f;
-        }
+        for (int d = 0; d < HD / 8; d++) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
+        float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+
         for (int k0 = 0; k0 <= last_q; k0 += kKB) {
-            if (!one_chunk || g == g0) {
-                if (k0 > 0) __syncthreads();  // the previous chunk's reads of kt / vs / pt are done
-                for (int idx = tid; idx < kKB * C4; idx += 256) {
-                    const int r = idx % kKB, c4 = idx / kKB, j = k0 + r;
-                    float4 k = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (j < len) k = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd +
-                                                                       kvh * HD + 4 * c4);
-                    kt[(4 * c4 + 0) * kKB + r] = k.x;
-                    kt[(4 * c4 + 1) * kKB + r] = k.y;
-                    kt[(4 * c4 + 2) * kKB + r] = k.z;
-                    kt[(4 * c4 + 3) * kKB + r] = k.w;
-                }
-                for (int idx = tid; idx < kKB * C4; idx += 256) {
+            if (!one_chunk || gh == gh0) {
+                if (k0 > 0) __syncthreads();  // the previous chunk's reads of the K / V tiles are done
+                for (int idx = tid; idx < kKB * C4; idx += 128) {
                     const int r = idx / C4, c4 = idx % C4, j = k0 + r;
+                    float4 k = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (j < len)
+                        k = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd + kvh * HD +
+                                                              4 * c4);
+                    uint2 hi, lo;
+                    split_bf16x2(k.x, k.y, hi.x, lo.x);
+                    split_bf16x2(k.z, k.w, hi.y, lo.y);
+                    *reinterpret_cast<uint2 *>(kh + r * QS + 4 * c4) = hi;
+                    *reinterpret_cast<uint2 *>(kl + r * QS + 4 * c4) = lo;
+                }
+                for (int idx = tid; idx < kKB * C4; idx += 128) {  // keys across lanes: conflict-free transposed stores
+                    const int r = idx % kKB, c4 = idx / kKB, j = k0 + r;
                     float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (j < len) v = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd +
-                                                                       kvd + kvh * HD + 4 * c4);
-                    *reinterpret_cast<float4 *>(vs + r * HD + 4 * c4) = v;
+                    if (j < len)
+                        v = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd + kvd +
+                                                              kvh * HD + 4 * c4);
+                    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const uint16_t hb = f32_to_bf16_bits(vv[e]);
+                        vh[(4 * c4 + e) * VS + r] = hb;
+                        vl[(4 * c4 + e) * VS + r] = f32_to_bf16_bits(vv[e] - bf16_bits_to_f32(hb));
+                    }
                 }
             }
             __syncthreads();
-            // scores of queries 4ty.. x keys 4tx..
-            float s[4][4];
+            // 8-key tiles this warp needs (causal limit) and the 16-key steps of P . V
+            const int nt = max(0, min(8, (warp_last - k0) / 8 + 1));
+            float s[8][4];
 #pragma unroll
-            for (int a = 0; a < 4; a++)
+            for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 4; c++) s[a][c] = 0.0f;
-#pragma unroll 8
-            for (int d = 0; d < HD; d++) {
-                const float4 qv = *reinterpret_cast<const float4 *>(qt + d * kQB + 4 * ty);
-                const float4 kv = *reinterpret_cast<const float4 *>(kt + d * kKB + 4 * tx);
-                const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+            for (int kk = 0; kk < HD / 16; kk++) {
+                const int c = 16 * kk + 2 * t;
+                const uint32_t ah0 = ld32(qh + (r0 + g) * QS + c), ah1 = ld32(qh + (r0 + g + 8) * QS + c);
+                const uint32_t ah2 = ld32(qh + (r0 + g) * QS + c + 8), ah3 = ld32(qh + (r0 + g + 8) * QS + c + 8);
+                const uint32_t al0 = ld32(ql + (r0 + g) * QS + c), al1 = ld32(ql + (r0 + g + 8) * QS + c);
+                const uint32_t al2 = ld32(ql + (r0 + g) * QS + c + 8), al3 = ld32(ql + (r0 + g + 8) * QS + c + 8);
 #pragma unroll
-                for (int a = 0; a < 4; a++)
-#pragma unroll
-                    for (int c = 0; c < 4; c++) s[a][c] = fmaf(qa[a], ka[c], s[a][c]);
+                for (int j = 0; j < 8; j++) {
+                    if (j < nt) {
+                        const uint32_t bh0 = ld32(kh + (8 * j + g) * QS + c), bh1 = ld32(kh + (8 * j + g) * QS + c + 8);
+                        const uint32_t bl0 = ld32(kl + (8 * j + g) * QS + c), bl1 = ld32(kl + (8 * j + g) * QS + c + 8);
+                        mma_bf16_16816(s[j], ah0, ah1, ah2, ah3, bh0, bh1);
+                        mma_bf16_16816(s[j], ah0, ah1, ah2, ah3, bl0, bl1);
+                        mma_bf16_16816(s[j], al0, al1, al2, al3, bh0, bh1);
+                    }
+                }
             }
-            float corr[4];
+            // scale, causal mask, online softmax (rows row_a: s[j][0..1], row_b: s[j][2..3])
+            float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
-            for (int a = 0; a < 4; a++) {
-                const int qi = i0 + 4 * ty + a;
-                float mx = -INFINITY;
+            for (int j = 0; j < 8; j++) {
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const int kj = k0 + 4 * tx + c;
-                    s[a][c] = (kj <= qi && kj < len) ? s[a][c] * p.scale : -INFINITY;
-                    mx = fmaxf(mx, s[a][c]);
+                for (int e = 0; e < 4; e++) {
+                    const int key = k0 + 8 * j + 2 * t + (e & 1);
+                    const int row = (e < 2) ? row_a : row_b;
+                    const bool ok = j < nt && key <= row && key < len;
+                    s[j][e] = ok ? s[j][e] * p.scale : -INFINITY;
                 }
-#pragma unroll
-                for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-                const float mnew = fmaxf(m[a], mx);
-                corr[a] = (m[a] == -INFINITY) ? 0.0f : expf(m[a] - mnew);
-                float sum = 0.0f;
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const float e = (s[a][c] == -INFINITY) ? 0.0f : expf(s[a][c] - mnew);
-                    s[a][c] = e;
-                    sum += e;
-                }
-#pragma unroll
-                for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                l[a] = l[a] * corr[a] + sum;
-                m[a] = (mnew == -INFINITY) ? m[a] : mnew;
+                mx_a = fmaxf(mx_a, fmaxf(s[j][0], s[j][1]));
+                mx_b = fmaxf(mx_b, fmaxf(s[j][2], s[j][3]));
             }
-            // P^T [key][query] for the value product
 #pragma unroll
-            for (int c = 0; c < 4; c++)
-                *reinterpret_cast<float4 *>(pt + (4 * tx + c) * kQB + 4 * ty) =
-                    make_float4(s[0][c], s[1][c], s[2][c], s[3][c]);
-            __syncthreads();
+            for (int off = 1; off < 4; off <<= 1) {
+                mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+                mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+            }
+            const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+            const float corr_a = (m_a == -INFINITY) ? 0.0f : expf(m_a - mn_a);
+            const float corr_b = (m_b == -INFINITY) ? 0.0f : expf(m_b - mn_b);
+            float sum_a = 0.0f, sum_b = 0.0f;
 #pragma unroll
-            for (int a = 0; a < 4; a++)
+            for (int j = 0; j < 8; j++) {
 #pragma unroll
-                for (int c = 0; c < DPT; c++) o[a][c] *= corr[a];
-            const int nk = min(kKB, last_q + 1 - k0);
-            for (int k = 0; k < nk; k++) {
-                const float4 pv = *reinterpret_cast<const float4 *>(pt + k * kQB + 4 * ty);
-                const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
-                float vv[DPT];
-#pragma unroll
-                for (int c = 0; c < DPT; c += 4) {  // dimensions 4 (tx + 16 c/4) ..: a quarter-warp reads 128 B
-                    const float4 t = *reinterpret_cast<const float4 *>(vs + k * HD + 4 * tx + 16 * c);
-                    vv[c] = t.x;
-                    vv[c + 1] = t.y;
-                    vv[c + 2] = t.z;
-                    vv[c + 3] = t.w;
+                for (int e = 0; e < 4; e++) {
+                    const float mref = e < 2 ? mn_a : mn_b;
+                    const float pe = (s[j][e] == -INFINITY) ? 0.0f : expf(s[j][e] - mref);
+                    s[j][e] = pe;
+                    if (e < 2) sum_a += pe;
+                    else sum_b += pe;
                 }
+            }
 #pragma unroll
-                for (int a = 0; a < 4; a++)
+            for (int off = 1; off < 4; off <<= 1) {
+                sum_a += __shfl_xor_sync(0xffffffffu, sum_a, off);
+                sum_b += __shfl_xor_sync(0xffffffffu, sum_b, off);
+            }
+            l_a = l_a * corr_a + sum_a;
+            l_b = l_b * corr_b + sum_b;
+            m_a = (mn_a == -INFINITY) ? m_a : mn_a;
+            m_b = (mn_b == -INFINITY) ? m_b : mn_b;
 #pragma unroll
-                    for (int c = 0; c < DPT; c++) o[a][c] = fmaf(pa[a], vv[c], o[a][c]);
+            for (int d = 0; d < HD / 8; d++) {
+                o[d][0] *= corr_a;
+                o[d][1] *= corr_a;
+                o[d][2] *= corr_b;
+                o[d][3] *= corr_b;
+            }
+            // O += P . V over the 16-key steps this warp needs
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                if (2 * kk >= nt) break;
+                uint32_t ph0, ph1, ph2, ph3, pl0, pl1, pl2, pl3;
+                split_bf16x2(s[2 * kk][0], s[2 * kk][1], ph0, pl0);
+                split_bf16x2(s[2 * kk][2], s[2 * kk][3], ph1, pl1);
+                split_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1], ph2, pl2);
+                split_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3], ph3, pl3);
+                const int c = 16 * kk + 2 * t;
+#pragma unroll
+                for (int d = 0; d < HD / 8; d++) {
+                    const uint16_t *vrh = vh + (8 * d + g) * VS, *vrl = vl + (8 * d + g) * VS;
+                    const uint32_t bh0 = ld32(vrh + c), bh1 = ld32(vrh + c + 8);
+                    const uint32_t bl0 = ld32(vrl + c), bl1 = ld32(vrl + c + 8);
+                    mma_bf16_16816(o[d], ph0, ph1, ph2, ph3, bh0, bh1);
+                    mma_bf16_16816(o[d], ph0, ph1, ph2, ph3, bl0, bl1);
+                    mma_bf16_16816(o[d], pl0, pl1, pl2, pl3, bh0, bh1);
+                }
             }
         }
+        const float inv_a = 1.0f / l_a, inv_b = 1.0f / l_b;
 #pragma unroll
-        for (int a = 0; a < 4; a++) {
-            const int qi = i0 + 4 * ty + a;
-            if (qi >= len) continue;
-            const float inv = 1.0f / l[a];
-            uint16_t *dst = p.out + (long long)(start + qi) * qd + h * HD + 4 * tx;
-#pragma unroll
-            for (int c = 0; c < DPT; c += 4) {
-                uint2 w;
-                w.x = pack_bf16x2(o[a][c] * inv, o[a][c + 1] * inv);
-                w.y = pack_bf16x2(o[a][c + 2] * inv, o[a][c + 3] * inv);
-                *reinterpret_cast<uint2 *>(dst + 16 * c) = w;
-            }
+        for (int d = 0; d < HD / 8; d++) {
+            const int dim = h * HD + 8 * d + 2 * t;
+            if (row_a < len)
+                *reinterpret_cast<uint32_t *>(p.out + (long long)(start + row_a) * qd + dim) =
+                    pack_bf16x2(o[d][0] * inv_a, o[d][1] * inv_a);
+            if (row_b < len)
+                *reinterpret_cast<uint32_t *>(p.out + (long long)(start + row_b) * qd + dim) =
+                    pack_bf16x2(o[d][2] * inv_b, o[d][3] * inv_b);
         }
     }
 }
 
 template <int HD>
 cudaError_t launch_attention_tiled(const AttnParams &p, cudaStream_t st) {
-    const size_t smem = sizeof(float) * (2 * HD * kQB + kKB * HD + kKB * kQB);
+    const size_t smem = sizeof(uint16_t) * (2 * kQB * (HD + 8) + 2 * kKB * (HD + 8) + 2 * HD * (kKB + 8));
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention_tiled<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(k_attention_mma<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
         configured = true;
@@ -472,7 +517,7 @@ cudaError_t launch_attention_tiled(const AttnParams &p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const int groups = p.heads / p.kv_heads, parts = (groups + kMaxHeads - 1) / kMaxHeads;
     dim3 grid(p.n_prompts, p.kv_heads * parts, (max_len + kQB - 1) / kQB);
-    k_attention_tiled<HD><<<grid, 256, smem, st>>>(p);
+    k_attention_mma<HD><<<grid, 128, smem, st>>>(p);
     return cudaGetLastError();
 }
 
