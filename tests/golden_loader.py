@@ -18,6 +18,9 @@ class Golden:
         self.config = json.loads(bytes(z["config_json"]).decode())
         self.dtypes = json.loads(bytes(z["dtypes_json"]).decode())
         self.raw = {k[2:]: z[k] for k in z.files if k.startswith("t/")}
+        self.shapes = json.loads(bytes(z["shapes_json"]).decode()) if "shapes_json" in z.files else {}
+        self.gguf = bool(self.config.get("gguf"))
+        self._canonical_experts()
         self.cases = []
         for i in range(int(z["n_cases"][0])):
             self.cases.append({
@@ -34,6 +37,39 @@ class Golden:
         if q and q.get("quant_method") == "compressed-tensors":
             w = q["config_groups"]["group_0"]["weights"]
             self.int_bits, self.int_group = w["num_bits"], w["group_size"]
+
+    def _canonical_experts(self):
+        """Routed experts as one tensor per expert and projection, the
+        "separate" layout of src/moe.zig:83-92, the host-side step a caller of
+        the C ABI performs: mixtral's w1 / w3 / w2 are gate / up / down; the
+        fused `experts.gate_up_proj` [E, 2I, hidden] splits into gate rows
+        then up rows, and its transposed form [E, hidden, 2I] (with `down_proj`
+        [E, I, hidden]) is transposed per expert, as src/moe.zig:728-770."""
+        c, raw, dt = self.config, self.raw, self.dtypes
+        if c["model_type"] == "mixtral":
+            for name in list(raw):
+                if ".block_sparse_moe." not in name:
+                    continue
+                new = name.replace(".block_sparse_moe.", ".mlp.")
+                for a, b in ((".w1.", ".gate_proj."), (".w3.", ".up_proj."), (".w2.", ".down_proj.")):
+                    new = new.replace(a, b)
+                raw[new], dt[new] = raw.pop(name), dt.pop(name)
+        H = c["hidden_size"]
+        for name in list(raw):
+            if not name.endswith(".mlp.experts.gate_up_proj"):
+                continue
+            p = name[: -len("gate_up_proj")]
+            gu, dn = raw.pop(name), raw.pop(p + "down_proj")
+            t_gu, t_dn = dt.pop(name), dt.pop(p + "down_proj")
+            transposed = gu.shape[1] == H and gu.shape[2] != H
+            if transposed:
+                gu, dn = np.swapaxes(gu, 1, 2), np.swapaxes(dn, 1, 2)
+            inter = gu.shape[1] // 2
+            for e in range(gu.shape[0]):
+                for proj, arr, t in (("gate_proj", gu[e, :inter], t_gu), ("up_proj", gu[e, inter:], t_gu),
+                                     ("down_proj", dn[e], t_dn)):
+                    key = f"{p}{e}.{proj}.weight"
+                    raw[key], dt[key] = np.ascontiguousarray(arr), t
 
     def _spec(self):
         c = self.config
@@ -53,6 +89,9 @@ class Golden:
             mlp_only = set(c.get("mlp_only_layers", []))
             step = c.get("decoder_sparse_step", 1)
             s["moe_layers"] = [(i not in mlp_only) and (i + 1) % step == 0 for i in range(s["n_layers"])]
+        if c["model_type"] == "mixtral":  # every layer routed; top-k weights renormalised
+            s.update(n_experts=c["num_local_experts"], top_k=c["num_experts_per_tok"], moe_inter=c["intermediate_size"],
+                     norm_topk=1, moe_layers=[True] * s["n_layers"])
         return s
 
     # ---- decoding to f32 (the oracle's view of every weight) ----
@@ -69,6 +108,12 @@ class Golden:
                 br, bc = self.block
                 bits = oracle.dequant_fp8(a, self.raw[name + "_scale_inv"], br, bc)
                 return oracle.bf16_bits_to_f32(bits)
+            if dt == "F16":
+                return a.view(np.float16).astype(np.float32)
+            if dt.startswith("GGML_"):  # ggml blocks decoded to f32 as src/quant.zig:57-79
+                rows, cols = self.shapes[name]
+                code = {"GGML_Q8_0": 5, "GGML_Q4_K": 10, "GGML_Q6_K": 11}[dt]
+                return oracle.dequant_ggml(code, a, rows * cols).reshape(rows, cols)
             raise ValueError(f"unsupported dtype {dt} for {name}")
         base = name[: -len(".weight")]
         if base + ".weight_packed" in self.raw:
@@ -81,8 +126,20 @@ class Golden:
         raise KeyError(name)
 
     def hf_names(self):
-        """canonical name -> HF tensor name."""
+        """canonical name -> HF tensor name (GGUF names for GGUF fixtures)."""
         s = self.spec
+        if self.gguf:
+            m = {"embed": "token_embd.weight", "final_norm": "output_norm.weight",
+                 "lm_head": "token_embd.weight" if s["tied"] else "output.weight"}
+            for i in range(s["n_layers"]):
+                p = f"blk.{i}."
+                m.update({f"L{i}.input_norm": p + "attn_norm.weight", f"L{i}.post_norm": p + "ffn_norm.weight",
+                          f"L{i}.q": p + "attn_q.weight", f"L{i}.k": p + "attn_k.weight",
+                          f"L{i}.v": p + "attn_v.weight", f"L{i}.o": p + "attn_output.weight",
+                          f"L{i}.qb": p + "attn_q.bias", f"L{i}.kb": p + "attn_k.bias", f"L{i}.vb": p + "attn_v.bias",
+                          f"L{i}.gate": p + "ffn_gate.weight", f"L{i}.up": p + "ffn_up.weight",
+                          f"L{i}.down": p + "ffn_down.weight"})
+            return m
         m = {"embed": "model.embed_tokens.weight", "final_norm": "model.norm.weight",
              "lm_head": "model.embed_tokens.weight" if s["tied"] else "lm_head.weight"}
         for i in range(s["n_layers"]):
@@ -145,6 +202,11 @@ class Golden:
                 sc = np.stack([self.raw[n + "_scale_inv"] for n in names]) if stack else self.raw[first + "_scale_inv"]
                 return Tensor(canon, "fp8", rows, cols, a, slabs=slabs, scales=sc.astype(np.float32),
                               scales_dtype=SCALE_F32, block_rows=br, block_cols=bc)
+            if dt == "F16":
+                return Tensor(canon, "f16", rows, cols, a, slabs=slabs)
+            if dt.startswith("GGML_"):  # raw blocks, as stored
+                rows, cols = self.shapes[first]
+                return Tensor(canon, {"GGML_Q8_0": "q8_0", "GGML_Q4_K": "q4_k"}[dt], rows, cols, a, slabs=slabs)
             raise ValueError(dt)
         if base + ".weight_packed" in self.raw:
             rows, cols = (int(v) for v in self.raw[base + ".weight_shape"])

@@ -19,11 +19,44 @@ from oracle.model import OracleModel, flatten_batch
 pytestmark = pytest.mark.gpu
 
 FWD_ATOL, FWD_RTOL = 2e-3, 2e-2
-DENSE = ["qwen2", "llama", "qwen3", "qwen2_fp8", "qwen2_int4", "qwen3_moe"]
+DENSE = ["qwen2", "llama", "qwen3", "qwen2_fp8", "qwen2_int4", "qwen3_moe", "qwen3_moe_big", "qwen3_moe_fused",
+         "qwen3_moe_fused_t", "mixtral", "qwen2_gguf"]
 
 
 def bound(want):
     return FWD_ATOL + FWD_RTOL * float(np.abs(want).max())
+
+
+ROUTER_TIE = 2e-2  # router logit gap below which bf16 activations may pick the other expert
+
+
+def near_tied_tokens(g, toks, rb, rp, cap, last):
+    """Token rows whose top-k boundary in some routed layer is a near-tie in
+    the oracle: the gap between the k-th and (k+1)-th router logit is below
+    ROUTER_TIE. ditch picks the first maximum of f32 scores
+    (src/moe.zig:971-985); the device computes the router input from
+    activations rounded to bf16 at every GEMM, so such a token can take the
+    other expert, which changes its row and, through attention, the later rows
+    of its prompt. The router input of layer l is x + attn(x): the oracle's
+    layer-l output with that layer's experts set to zero."""
+    s = g.spec
+    if not s.get("moe_layers"):
+        return set()
+    w = g.f32_weights()
+    k = s["top_k"]
+    tied = set()
+    for li in range(s["n_layers"]):
+        if not s["moe_layers"][li]:
+            continue
+        w0 = dict(w)
+        for a in ("gate", "up", "down"):
+            w0[f"L{li}.e_{a}"] = np.zeros_like(w[f"L{li}.e_{a}"])
+        res, _ = OracleModel(s, w0).forward(toks, rb, rp, cap, last)
+        x = res[li + 1]
+        h = x / np.sqrt((x * x).mean(axis=1, keepdims=True) + s["eps"]) * w[f"L{li}.post_norm"]
+        top = np.sort(h @ w[f"L{li}.router"].T, axis=1)[:, ::-1]
+        tied |= set(np.nonzero(top[:, k - 1] - top[:, k] < ROUTER_TIE)[0].tolist())
+    return tied
 
 
 def load(device, family):
@@ -33,16 +66,38 @@ def load(device, family):
 
 @pytest.mark.parametrize("family", DENSE)
 def test_fixture_forward(device, family):
+    """Every prompt's last logits and last-token residual entries against the
+    reference and the oracle (the reference's own check). With routed
+    experts, a prompt with a near-tied routing choice (see near_tied_tokens)
+    is checked on its rows before that token instead, every entry: causal
+    attention keeps them independent of the choice."""
     g, m = load(device, family)
-    toks, rb, rp, cap, first, take, last = flatten_batch(g.prompts())
+    toks, rb, rp, cap, first, take, last = flatten_batch(g.prompts(), 10 ** 6)  # capture every row
     res, logits = m.forward(toks, rb, rp, cap, last)
     om = OracleModel(g.spec, g.f32_weights())
     ores, ologits = om.forward(toks, rb, rp, cap, last)
+    tied = near_tied_tokens(g, toks, rb, rp, cap, last)
+    checked = 0
+    start = 0
     for i, c in enumerate(g.cases):
+        n = len(c["ids"])
+        assert np.isfinite(logits[i]).all()
+        stop = min([t - start for t in tied if start <= t < start + n] + [n])
+        if stop < n:  # near-tied routing: the rows before the tie, every entry
+            for pos in range(stop):
+                for l in range(res.shape[0]):
+                    got, want = res[l, start + pos], ores[l, start + pos]
+                    assert np.abs(got - want).max() <= bound(want), (i, pos, l)
+                checked += 1
+            start += n
+            continue
+        start += n
+        checked += 1
         assert np.abs(logits[i] - c["last_logits"]).max() <= bound(c["last_logits"])
-        assert np.abs(res[:, i] - c["last_hidden"]).max() <= bound(c["last_hidden"])
+        assert np.abs(res[:, start - 1] - c["last_hidden"]).max() <= bound(c["last_hidden"])
         assert np.abs(logits[i] - ologits[i]).max() <= bound(ologits[i])
         assert int(np.argmax(logits[i])) == c["argmax"]
+    assert checked > 0
     m.close()
 
 
