@@ -242,6 +242,31 @@ __global__ void k_dequant_ggml(int dt, const uint8_t *src, long long n, void *ou
     }
 }
 
+// Q8_0 blocks (f16 d, 32 x int8; src/quant.zig:81-85) of `rows` rows to the
+// GEMM's layout: int8 codes [rows][cols] and f32 scales [rows][cols / 32].
+__global__ void k_repack_q8_0(const uint8_t *src, long long blocks, int8_t *codes, float *scales) {
+    for (long long b = blockIdx.x * (long long)blockDim.x + threadIdx.x; b < blocks;
+         b += (long long)gridDim.x * blockDim.x) {
+        const uint8_t *blk = src + b * 34;
+        const uint16_t dbits = (uint16_t)blk[0] | ((uint16_t)blk[1] << 8);
+        scales[b] = __half2float(__ushort_as_half(dbits));
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            w[i] = (uint32_t)blk[2 + 4 * i] | ((uint32_t)blk[3 + 4 * i] << 8) | ((uint32_t)blk[4 + 4 * i] << 16) |
+                   ((uint32_t)blk[5 + 4 * i] << 24);
+        uint4 *dst = reinterpret_cast<uint4 *>(codes + b * 32);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+
+// The repacked Q8_0 values as f32 (d * q, exact as src/quant.zig:81-85).
+__global__ void k_q8_0_f32(const int8_t *codes, const float *scales, long long n, float *out) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = scales[i / 32] * (float)codes[i];
+}
+
 __global__ void k_split(const float *src, int rows, int cols, int cp, int nseg, int pattern, uint16_t *dst) {
     const long long total = (long long)rows * cp;
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
@@ -274,6 +299,18 @@ __global__ void k_f16_to_f32(const uint16_t *src, float *dst, long long n) {
 }
 
 }  // namespace
+
+cudaError_t repack_q8_0(const uint8_t *src, long long blocks, int8_t *codes, float *scales, cudaStream_t st) {
+    if (blocks <= 0) return cudaSuccess;
+    k_repack_q8_0<<<blocks_for(blocks, 1), kThreads, 0, st>>>(src, blocks, codes, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t q8_0_f32(const int8_t *codes, const float *scales, long long n, float *out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_q8_0_f32<<<blocks_for(n, 4), kThreads, 0, st>>>(codes, scales, n, out);
+    return cudaGetLastError();
+}
 
 cudaError_t dequant_fp8_bf16(const uint8_t *codes, const float *scales, int rows, int cols, int br, int bc,
                              uint16_t *out, cudaStream_t st) {

@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <unordered_map>
 
 namespace ditch {
 
@@ -38,10 +39,14 @@ struct Cfg {
     static constexpr int kNA = DUAL ? 2 : 1;
     static constexpr int kABytes = BM * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
-    static constexpr int kRawBytes = FMT == kFmtFp8 ? BM * BK : (FMT == kFmtMxfp4 || FMT == kFmtInt4) ? BM * BK / 2 : 0;
+    static constexpr int kRawBytes = (FMT == kFmtFp8 || FMT == kFmtQ8_0)  ? BM * BK
+                                     : (FMT == kFmtMxfp4 || FMT == kFmtInt4) ? BM * BK / 2
+                                                                             : 0;
     static constexpr int kStageBytes = kNA * kABytes + kBBytes;
     static constexpr int kRawStageBytes = kNA * kRawBytes;
-    static constexpr int kRawStages = kQuant ? 3 : 0;
+    // raw-tile stages in flight: narrow token tiles (decode-like products,
+    // bound by streaming the weight) keep more of the weight in flight
+    static constexpr int kRawStages = !kQuant ? 0 : BN <= 64 ? (DUAL ? 4 : 8) : 3;
     static constexpr int kRawRing = kRawStages > 0 ? kRawStages : 1;  // modulus (unused without raw tiles)
     static constexpr int kStagesFit = (kSmemBudget - kRawStages * kRawStageBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
@@ -259,13 +264,50 @@ __device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *atile, i
     }
 }
 
+// Eight int8 codes (two words) to four bf16x2 of bf16(f32(code) * d): the
+// ggml Q8_0 value d * q in f32 (src/quant.zig:81-85), rounded to bf16.
+__device__ __forceinline__ uint4 q8x8_bf16(uint32_t w0, uint32_t w1, float d) {
+    uint32_t o[4];
+    const uint32_t w[2] = {w0, w1};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t word = w[k >> 1];
+        const int sh = 16 * (k & 1);
+        const float lo = (float)(int8_t)((word >> sh) & 0xff), hi = (float)(int8_t)((word >> (sh + 8)) & 0xff);
+        o[k] = scale_pack(make_float2(lo, hi), d);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// GGUF Q8_0 repacked at load: int8 codes [rows][cols] and the block scales d
+// as f32 [rows][cols / 32]. Raw tile: 128 rows x 64 codes, TMA 64B swizzle
+// (chunk c at c ^ ((r >> 1) & 3), as FP8); half h is one 32-code block.
+__device__ __forceinline__ void xform_q8_0(const uint8_t *raw, uint8_t *atile, int r, int h, int grow, int k0,
+                                           const GemmParams &p) {
+    uint8_t *arow = atile + r * 128;
+    const int rs = (r >> 1) & 3;
+    const int blk = (k0 >> 5) + h;
+    const float d = (blk * 32 < p.k) ? __ldg(p.scales + (long long)grow * p.scale_cols + blk) : 0.0f;
+#pragma unroll
+    for (int cc = 0; cc < 2; cc++) {
+        const int c = 2 * h + cc;  // raw 16-byte chunk: output chunks 2c, 2c + 1
+        const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ rs) << 4));
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            const int j = 2 * c + half;
+            const uint4 o = half ? q8x8_bf16(q.z, q.w, d) : q8x8_bf16(q.x, q.y, d);
+            *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
+        }
+    }
+}
+
 // ---- staged decode ----------------------------------------------------------
 // Rows [row0, row0 + rows) of a quantised weight decoded once to bf16
 // [rows][cols] with the transforms' own arithmetic, so that the bf16 GEMM over
 // the staged copy equals the fused GEMM bit for bit. One thread decodes one
 // 16-byte chunk of codes: 16 FP8 elements, or 32 MXFP4 / INT4 elements.
 __global__ void __launch_bounds__(256) k_stage_decode(const StageArgs a) {
-    const int epc = a.fmt == kFmtFp8 ? 16 : 32;  // elements per chunk
+    const int epc = (a.fmt == kFmtFp8 || a.fmt == kFmtQ8_0) ? 16 : 32;  // elements per chunk
     const int chunks = a.cols / epc;
     const long long total = (long long)a.rows * chunks;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -296,6 +338,10 @@ __global__ void __launch_bounds__(256) k_stage_decode(const StageArgs a) {
                 }
                 dst[half] = make_uint4(o[0], o[1], o[2], o[3]);
             }
+        } else if (a.fmt == kFmtQ8_0) {
+            const float d = __ldg(a.scales + (long long)grow * a.scale_cols + c0 / 32);
+            dst[0] = q8x8_bf16(words[0], words[1], d);
+            dst[1] = q8x8_bf16(words[2], words[3], d);
         } else if (a.fmt == kFmtMxfp4) {
             const float s = e8m0_scale(__ldg(a.scales_u8 + (long long)grow * (a.cols / 32) + ch));
 #pragma unroll
@@ -385,7 +431,7 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                         const uint32_t rph = (it / C::kRawRing) & 1;
                         if (!mbar_wait(&L.rawempty[rs], rph ^ 1, abort, p.status)) break;
                         mbar_arrive_expect_tx(&L.rawfull[rs], C::kRawStageBytes);
-                        const int xb = kt * (FMT == kFmtFp8 ? BK : BK / 2);  // raw bytes along K
+                        const int xb = kt * ((FMT == kFmtFp8 || FMT == kFmtQ8_0) ? BK : BK / 2);  // raw bytes along K
                         tma_load_2d(&tmA, &L.rawfull[rs], L.raw(rs, 0), xb, arow);
                         if (DUAL) tma_load_2d(&tmA2, &L.rawfull[rs], L.raw(rs, 1), xb, arow + p.a2_row_offset);
                         mbar_arrive_expect_tx(&L.full[s], C::kBBytes);
@@ -554,6 +600,7 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                     if (FMT == kFmtFp8) xform_fp8(L.raw(rs, i), L.a(s, i), r, h, srow[i], one_scale, s_tile[i], kt * BK, p);
                     if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(rs, i), L.a(s, i), r, h, vrow[i], kt * BK, p);
                     if (FMT == kFmtInt4) xform_int4(L.raw(rs, i), L.a(s, i), r, h, vrow[i], kt * BK, p);
+                    if (FMT == kFmtQ8_0) xform_q8_0(L.raw(rs, i), L.a(s, i), r, h, vrow[i], kt * BK, p);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -594,9 +641,54 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// A 2D map over a row-major [rows][inner] tensor.
+// A 2D map over a row-major [rows][inner] tensor. Encodings are cached by
+// their full parameter tuple (a map depends on nothing else), which takes the
+// driver call off the host path of repeated launches.
+struct MapKey {
+    const void *ptr;
+    uint64_t inner, rows, row_bytes;
+    uint32_t box_inner, box_rows;
+    int dt, sw;
+    bool operator==(const MapKey &o) const {
+        return ptr == o.ptr && inner == o.inner && rows == o.rows && row_bytes == o.row_bytes &&
+               box_inner == o.box_inner && box_rows == o.box_rows && dt == o.dt && sw == o.sw;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        size_t h = std::hash<const void *>()(k.ptr);
+        for (uint64_t v : {k.inner, k.rows, k.row_bytes, (uint64_t)k.box_inner << 32 | k.box_rows,
+                           (uint64_t)k.dt << 8 | (uint64_t)k.sw})
+            h = h * 1000003u ^ std::hash<uint64_t>()(v);
+        return h;
+    }
+};
+
+bool encode_map(CUtensorMap *map, const void *ptr, CUtensorMapDataType dt, uint64_t inner, uint64_t rows,
+                uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw);
+
 bool make_map(CUtensorMap *map, const void *ptr, CUtensorMapDataType dt, uint64_t inner, uint64_t rows,
               uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+    static std::mutex mu;
+    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{ptr, inner, rows, row_bytes, box_inner, box_rows, (int)dt, (int)sw};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *map = it->second;
+            return true;
+        }
+    }
+    if (!encode_map(map, ptr, dt, inner, rows, row_bytes, box_inner, box_rows, sw)) return false;
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, *map);
+    return true;
+}
+
+bool encode_map(CUtensorMap *map, const void *ptr, CUtensorMapDataType dt, uint64_t inner, uint64_t rows,
+                uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {inner, rows};
@@ -621,8 +713,9 @@ cudaError_t launch_t(const GemmOperand &a, const GemmOperand *a2, const GemmOper
             ok = make_map(&ma2, a2->ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a2->cols, a2->rows, a2->row_bytes, BK, BM,
                           CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
-        const uint32_t raw_inner = FMT == kFmtFp8 ? BK : BK / 2;  // bytes per row per k-tile
-        const CUtensorMapSwizzle sw = FMT == kFmtFp8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
+        const bool bytes8 = FMT == kFmtFp8 || FMT == kFmtQ8_0;  // one byte per element
+        const uint32_t raw_inner = bytes8 ? BK : BK / 2;        // bytes per row per k-tile
+        const CUtensorMapSwizzle sw = bytes8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
         ok = make_map(&ma, a.ptr, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.row_bytes, a.rows, a.row_bytes, raw_inner, BM, sw);
         if (ok && DUAL)
             ok = make_map(&ma2, a2->ptr, CU_TENSOR_MAP_DATA_TYPE_UINT8, a2->row_bytes, a2->rows, a2->row_bytes,
@@ -662,6 +755,7 @@ cudaError_t dispatch_fmt(int fmt, const GemmOperand &a, const GemmOperand *a2, c
     case kFmtFp8: return launch_t<BN, DUAL, kFmtFp8>(a, a2, b, p, sms, st);
     case kFmtMxfp4: return launch_t<BN, DUAL, kFmtMxfp4>(a, a2, b, p, sms, st);
     case kFmtInt4: return launch_t<BN, DUAL, kFmtInt4>(a, a2, b, p, sms, st);
+    case kFmtQ8_0: return launch_t<BN, DUAL, kFmtQ8_0>(a, a2, b, p, sms, st);
     default: return cudaErrorNotSupported;
     }
 }
@@ -679,9 +773,9 @@ int gemm_token_tile(int n_tok, bool dual, bool quant) {
 }
 
 cudaError_t launch_stage_decode(const StageArgs &a, int num_sms, cudaStream_t stream) {
-    const int epc = a.fmt == kFmtFp8 ? 16 : 32;
+    const int epc = (a.fmt == kFmtFp8 || a.fmt == kFmtQ8_0) ? 16 : 32;
     if (a.rows <= 0) return cudaSuccess;
-    if ((a.fmt != kFmtFp8 && a.fmt != kFmtMxfp4 && a.fmt != kFmtInt4) || a.cols % epc != 0)
+    if ((a.fmt != kFmtFp8 && a.fmt != kFmtMxfp4 && a.fmt != kFmtInt4 && a.fmt != kFmtQ8_0) || a.cols % epc != 0)
         return cudaErrorInvalidValue;
     if (a.fmt == kFmtInt4 && a.blk_cols % 32 != 0) return cudaErrorInvalidValue;
     const long long chunks = (long long)a.rows * (a.cols / epc);

@@ -23,6 +23,10 @@ cudaError_t dequant_mxfp4t_bf16(const uint8_t *blocks, const uint8_t *scales, in
                                 uint16_t *out, cudaStream_t st);
 // ggml blocks to f32 (dtype codes of src/tensor.zig:11-32)  quant.zig:57-209
 cudaError_t dequant_ggml_f32(int dtype, const uint8_t *src, long long n, float *out, cudaStream_t st);
+// Q8_0 blocks to the GEMM's layout (int8 codes [n] and f32 scales [n / 32]),
+// and that layout back to the f32 values d * q.
+cudaError_t repack_q8_0(const uint8_t *src, long long blocks, int8_t *codes, float *scales, cudaStream_t st);
+cudaError_t q8_0_f32(const int8_t *codes, const float *scales, long long n, float *out, cudaStream_t st);
 // ggml blocks to bf16 (the GEMM operand of a GGUF weight)
 cudaError_t dequant_ggml_bf16(int dtype, const uint8_t *src, long long n, uint16_t *out, cudaStream_t st);
 

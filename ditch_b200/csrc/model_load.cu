@@ -134,6 +134,10 @@ int native_format(const std::vector<Seg> &segs) {
     }
     case DITCH_FMT_MXFP4:
         return cols % 32 ? -1 : kFmtMxfp4;
+    case DITCH_FMT_Q8_0:  // repacked for the GEMM; single matrices (expert stacks decode to bf16)
+        for (const Seg &s : segs)
+            if (std::max<size_t>(s.t->slabs, 1) > 1) return -1;
+        return cols % 32 ? -1 : kFmtQ8_0;
     case DITCH_FMT_INT_PACKED: {
         if (t0->bits != 4 || t0->block_cols % 64 || cols % 32 || !t0->zeros) return -1;
         for (size_t i = 0; i < segs.size(); i++) {
@@ -183,6 +187,25 @@ int build_mat(ditch_cuda_model *m, const std::vector<Seg> &segs, int slabs, Mat 
             DITCH_CUDA(copy_in(m, out.scales.as<float>() + sr * out.scols, s.t->scales, sb * s.slab, ns * 4, s.t));
             r += s.t->rows;
             sr += (s.t->rows + out.br - 1) / out.br;
+        }
+    } else if (fmt == kFmtQ8_0) {
+        out.fmt = kFmtQ8_0;
+        out.row_bytes = (long long)cols;
+        out.scols = (int)(cols / 32);
+        DITCH_CUDA(out.data.reserve(rows * cols));
+        DITCH_CUDA(out.scales.reserve(rows * (cols / 32) * 4));
+        size_t r = 0;
+        for (const Seg &s : segs) {
+            const size_t bytes = s.t->rows * (cols / 32) * 34;
+            REQUIRE(s.t->data_bytes >= bytes, "%s: Q8_0 data too short", what);
+            DevBuf raw;
+            DITCH_CUDA(raw.reserve(bytes));
+            DITCH_CUDA(copy_in(m, raw.ptr, s.t->data, 0, bytes, s.t));
+            DITCH_LAUNCH(dev, repack_q8_0(raw.as<uint8_t>(), (long long)s.t->rows * (cols / 32),
+                                          out.data.as<int8_t>() + r * cols, out.scales.as<float>() + r * (cols / 32),
+                                          dev->stream));
+            DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+            r += s.t->rows;
         }
     } else if (fmt == kFmtMxfp4) {
         out.fmt = kFmtMxfp4;
@@ -683,6 +706,19 @@ int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out) {
                                            mt.zeros.as<uint32_t>(), nullptr, mt.groups, rows, mt.cols, 4, mt.group, out,
                                            dev->stream));
         break;
+    case kFmtQ8_0: {  // the GEMM operand itself: bf16(d * q)
+        StageArgs sa{};
+        sa.fmt = kFmtQ8_0;
+        sa.data = mt.data.as<uint8_t>();
+        sa.row_bytes = mt.row_bytes;
+        sa.rows = rows;
+        sa.cols = mt.cols;
+        sa.scales = mt.scales.as<float>();
+        sa.scale_cols = mt.scols;
+        sa.out = out;
+        DITCH_LAUNCH(dev, launch_stage_decode(sa, dev->sms, dev->stream));
+        break;
+    }
     default:
         set_error("weight format %d cannot be decoded", mt.fmt);
         return DITCH_CUDA_UNSUPPORTED;

@@ -76,6 +76,15 @@ int gemv_t_mat(ditch_cuda_model *m, const Mat &w, int row0, int rows, const floa
         DITCH_CUDA(cudaStreamSynchronize(dev->stream));
         break;
     }
+    case kFmtQ8_0: {  // the f32 values d * q, as ditch's A = v^T W reads them
+        DevBuf tmp;
+        DITCH_CUDA(tmp.reserve((size_t)rows * w.cols * 4));
+        DITCH_LAUNCH(dev, q8_0_f32(w.data.as<int8_t>() + (size_t)row0 * w.cols, w.scales.as<float>() + (size_t)row0 * w.scols,
+                                   (long long)rows * w.cols, tmp.as<float>(), dev->stream));
+        DITCH_LAUNCH(dev, gemv_t_f32(tmp.as<float>(), rows, w.cols, v, out, dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+        break;
+    }
     default:
         set_error("edit: weight format %d not supported", w.fmt);
         return DITCH_CUDA_UNSUPPORTED;
@@ -192,6 +201,9 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
             sa.scale_cols = w.scols;
         } else if (fmt == kFmtMxfp4) {
             sa.scales_u8 = w.scales.as<uint8_t>();
+        } else if (fmt == kFmtQ8_0) {
+            sa.scales = w.scales.as<float>();
+            sa.scale_cols = w.scols;
         } else {
             sa.scales = w.scales.as<float>();
             sa.zeros = w.zeros.as<uint32_t>();
@@ -225,7 +237,9 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         const long long tiles = (long long)((m_rows + 127) / 128) * ((n_tok + bn - 1) / bn);
         const int k_tiles = (w.cols + 63) / 64;
         if (tiles < dev->sms && k_tiles >= 8) {
-            int ks = (int)((dev->sms + tiles - 1) / tiles);
+            // as many splits as still fit one wave: a second, nearly empty
+            // wave would double the time of the streaming-bound product
+            int ks = (int)(dev->sms / tiles);
             ks = std::min(ks, k_tiles / 4);
             if (ks > 1) {
                 p.k_splits = ks;
@@ -250,6 +264,9 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         p.scale_cols = w.scols;
     } else if (fmt == kFmtMxfp4) {
         p.scales_u8 = w.scales.as<uint8_t>();
+    } else if (fmt == kFmtQ8_0) {
+        p.scales = w.scales.as<float>();
+        p.scale_cols = w.scols;
     } else if (fmt == kFmtInt4) {
         p.scales = w.scales.as<float>();
         p.zeros = w.zeros.as<uint32_t>();

@@ -283,7 +283,7 @@ int ditch_cuda_edit_weight_bf16_noalloc(void *w, size_t rows, size_t cols, const
 typedef struct ditch_cuda_weight ditch_cuda_weight;
 int ditch_cuda_weight_load(ditch_cuda_device *dev, const ditch_cuda_tensor *t, ditch_cuda_weight **out);
 void ditch_cuda_weight_free(ditch_cuda_weight *w);
-/* 0 bf16, 1 FP8 block, 2 MXFP4, 3 INT4 (how the GEMM reads the weight). */
+/* 0 bf16, 1 FP8 block, 2 MXFP4, 3 INT4, 4 Q8_0 (how the GEMM reads the weight). */
 int ditch_cuda_weight_format(const ditch_cuda_weight *w);
 /* out[m][rows] f32 = x[m][cols] . W^T with x bf16; x and out are device
  * pointers, used in order on the device's own stream (asynchronous; that

@@ -26,7 +26,7 @@ def _bound(x, w):
     return (x.float().abs() @ w.float().abs().T) * 2.0 ** -18 + 1e-6
 
 
-@pytest.mark.parametrize("fmt", ["fp8", "mxfp4", "int4"])
+@pytest.mark.parametrize("fmt", ["fp8", "mxfp4", "int4", "q8_0"])
 @pytest.mark.parametrize("shape", range(len(SHAPES)))
 def test_staged_and_fused_plans(device, fmt, shape):
     rows, cols, m = SHAPES[shape]
@@ -56,3 +56,27 @@ def test_staged_and_fused_plans(device, fmt, shape):
         W.close()
     if shape == 0:
         assert torch.equal(outs[0], outs[1])
+
+
+def test_q8_0_operand_is_ditchs_decode(device):
+    """The Q8_0 GEMM operand (repacked codes and f32 scales, decoded in the
+    GEMM or staged) equals ditch's f32 decode d * q (src/quant.zig:81-85)
+    rounded to bf16, bit for bit, across mixed-sign and zero blocks."""
+    import numpy as np
+
+    import oracle
+    from ditch_b200 import Tensor, Weight
+
+    rng = np.random.default_rng(8)
+    rows, cols = 96, 256
+    w = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float32)
+    w[3, :32] = 0.0  # an all-zero block (d = 0)
+    raw = oracle.quant_q8_0(w).reshape(rows, -1)
+    W = Weight(device, Tensor("w", "q8_0", rows, cols, raw))
+    assert W.format() == "q8_0"
+    got = torch.empty(rows, cols, device="cuda", dtype=torch.int16)
+    W.decode(got.data_ptr())
+    device.synchronize()
+    want = oracle.f32_to_bf16_bits(oracle.dequant_ggml(5, raw, rows * cols).reshape(rows, cols))
+    assert np.array_equal(got.cpu().numpy().view(np.uint16), want)
+    W.close()
