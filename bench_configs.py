@@ -4,8 +4,10 @@
 * `c3`: the standalone dequant + GEMM sweep of BASELINE config 3. Weights of
   [4096 x 4096], [14336 x 4096] and [4096 x 14336] are stored as GGUF Q8_0,
   GGUF Q4_K, INT4 (group 128, packed zero points) and MXFP4, with bf16
-  activations for M in {1, 16, 128, 1024, 8192}. The sweep reports TFLOP/s
-  (M >= 128) or weight-stream GB/s (M < 128) per case.
+  activations for M in {1, 16, 128, 1024, 8192}. Per case: `ms` per call of
+  back-to-back calls (host launch costs included), `kernel_ms` the device
+  time of the product's kernels, and from it TFLOP/s (M >= 128) or GB/s over
+  weight + activation + output bytes (M < 128).
 * `c5`: on one GPU, the in-place rank-1 edit W <- W - alpha_l r_l (r_l^T W)
   on all 80 o_proj [8192 x 8192] and down_proj [8192 x 28672] bf16 matrices
   of a Llama-3-70B shape (HBM GB/s over the algorithmic 3 x 48.32 GB). Under
@@ -176,7 +178,11 @@ def make_weight(dev, fmt, rows, cols, gen):
     return W, wbytes
 
 
-def time_gemm(dev, W, m, cols, rows, steps, warmup, k_splits=1):
+def time_gemm(dev, W, m, cols, rows, steps, warmup, k_splits=1, kernel_time=False):
+    """ms per call of back-to-back calls (CUDA events around the loop: host
+    launch costs included when the device outruns the host); with
+    `kernel_time`, also the device time of the product's own kernels (CUDA
+    events around each launch, summed by the library)."""
     import torch
 
     x = torch.randn(m, cols, device="cuda").to(torch.bfloat16)
@@ -189,7 +195,15 @@ def time_gemm(dev, W, m, cols, rows, steps, warmup, k_splits=1):
     for _ in range(steps):
         W.gemm(x.data_ptr(), m, out.data_ptr(), k_splits)
     ms = dev.timer_stop() / steps
-    return ms, x, out
+    if not kernel_time:
+        return ms, x, out
+    dev.set_profiling(True)
+    dev.reset_stats()
+    for _ in range(steps):
+        W.gemm(x.data_ptr(), m, out.data_ptr(), k_splits)
+    kms, n, _ = dev.gemm_stats()
+    dev.set_profiling(False)
+    return ms, kms / max(n, 1), x, out
 
 
 def run_gemm(args, dev):
@@ -197,15 +211,18 @@ def run_gemm(args, dev):
 
     gen = torch.Generator(device="cuda").manual_seed(args.seed)
     W, wbytes = make_weight(dev, args.fmt, args.rows, args.cols, gen)
-    ms, _, _ = time_gemm(dev, W, args.m, args.cols, args.rows, args.steps, args.warmup)
+    ms, kms, _, _ = time_gemm(dev, W, args.m, args.cols, args.rows, args.steps, args.warmup, kernel_time=True)
     hbm, tf, src = _peaks()
     tflops = 2.0 * args.m * args.rows * args.cols / ms / 1e9
     stage = 1024 if args.stage_min_tokens is None else args.stage_min_tokens
-    plan = "staged" if W.format() != "bf16" and 0 < stage <= args.m else "in-gemm"
+    plan = ("streaming" if args.m <= 16 else "staged" if W.format() != "bf16" and 0 < stage <= args.m
+            else "in-gemm")
+    bytes_ = wbytes + 2 * args.m * args.cols + 4 * args.m * args.rows
     print(json.dumps({"config": "gemm", "fmt": args.fmt, "gemm_format": W.format(), "decode_plan": plan,
-                      "rows": args.rows,
-                      "cols": args.cols, "m": args.m, "ms": round(ms, 4), "tflops": round(tflops, 1),
-                      "frac_of_burst_bf16": round(tflops / tf, 4), "peak_source": src}), flush=True)
+                      "rows": args.rows, "cols": args.cols, "m": args.m, "ms": round(ms, 4),
+                      "kernel_ms": round(kms, 4), "tflops": round(tflops, 1),
+                      "kernel_gbs": round(bytes_ / kms / 1e6, 1), "frac_of_burst_bf16": round(tflops / tf, 4),
+                      "kernel_frac_of_hbm": round(bytes_ / kms / 1e6 / hbm, 4), "peak_source": src}), flush=True)
     W.close()
 
 
@@ -219,14 +236,14 @@ def run_c3(args, dev):
         for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336)):
             W, wbytes = make_weight(dev, fmt, rows, cols, gen)
             for m in (1, 16, 128, 1024, 8192):
-                tiles = -(-rows // 128) * -(-m // (32 if m <= 32 else 64 if m <= 64 else 128 if m <= 128 else 256))
-                ks = max(1, min(cols // 64, (2 * 148) // max(tiles, 1))) if m < 128 else 1
-                ms, _, _ = time_gemm(dev, W, m, cols, rows, args.steps, args.warmup, ks)
+                # the library picks the plan: weight streaming (m <= 16),
+                # decode in the GEMM with one-wave split-K, or staged decode
+                ms, kms, _, _ = time_gemm(dev, W, m, cols, rows, args.steps, args.warmup, kernel_time=True)
                 flops = 2.0 * m * rows * cols
                 bytes_ = wbytes + 2 * m * cols + 4 * m * rows
                 r = {"fmt": fmt, "gemm_format": W.format(), "shape": [rows, cols], "m": m, "ms": round(ms, 4),
-                     "tflops": round(flops / ms / 1e9, 2), "gbs": round(bytes_ / ms / 1e6, 1), "k_splits": ks,
-                     "bound": "hbm" if m < 128 else "tensor"}
+                     "kernel_ms": round(kms, 4), "tflops": round(flops / kms / 1e9, 2),
+                     "gbs": round(bytes_ / kms / 1e6, 1), "bound": "hbm" if m < 128 else "tensor"}
                 r["frac"] = round(r["gbs"] / hbm if m < 128 else r["tflops"] / tf, 4)
                 results.append(r)
                 print(json.dumps(r), flush=True)

@@ -51,6 +51,28 @@ int check_status(ditch_cuda_device *dev, const char *what) {
     return DITCH_CUDA_OK;
 }
 
+cudaError_t run_skinny(ditch_cuda_device *dev, int fmt, const GemmOperand &a, const GemmOperand &b,
+                       const GemmParams &p0, int k_splits) {
+    GemmParams p = p0;
+    p.status = dev->status;
+    GemmEvent *ev = nullptr;
+    if (dev->profiling) {
+        if (dev->n_events == dev->events.size()) {
+            GemmEvent g;
+            cudaEventCreate(&g.start);
+            cudaEventCreate(&g.stop);
+            dev->events.push_back(g);
+        }
+        ev = &dev->events[dev->n_events++];
+        ev->flops = 2.0 * p.m_w * (double)p.n_tok * p.k;
+        cudaEventRecord(ev->start, dev->stream);
+    }
+    cudaError_t e = launch_skinny(fmt, a, b, p, k_splits, dev->stream);
+    dev->launches.fetch_add(1, std::memory_order_relaxed);
+    if (ev) cudaEventRecord(ev->stop, dev->stream);
+    return e;
+}
+
 cudaError_t run_gemm(ditch_cuda_device *dev, int fmt, const GemmOperand &a, const GemmOperand *a2,
                      const GemmOperand &b, const GemmParams &p0) {
     GemmParams p = p0;

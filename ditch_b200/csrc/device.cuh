@@ -126,6 +126,9 @@ int cuda_status(cudaError_t e, const char *what);
 // device profiles. flops = 2 * m * n * k (algorithmic).
 cudaError_t run_gemm(ditch_cuda_device *dev, int fmt, const GemmOperand &a, const GemmOperand *a2,
                      const GemmOperand &b, const GemmParams &p);
+// The weight-streaming product for 1..16 tokens (same bookkeeping).
+cudaError_t run_skinny(ditch_cuda_device *dev, int fmt, const GemmOperand &a, const GemmOperand &b,
+                       const GemmParams &p, int k_splits);
 
 // Reads and clears the device status word; returns DITCH_CUDA_OK or a failure.
 int check_status(ditch_cuda_device *dev, const char *what);

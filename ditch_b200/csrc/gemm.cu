@@ -371,6 +371,144 @@ __global__ void __launch_bounds__(256) k_stage_decode(const StageArgs a) {
     }
 }
 
+// ---- weight-streaming product for at most 16 tokens ----------------------
+// out[m][n] = x[m] . W[n] for m < M <= 16, the weight read once in its
+// stored format. Block = 8 warps over 16 weight rows (two n8 tiles); the
+// warps share the block's K range chunk by chunk and their partial sums are
+// added in shared memory (then atomically across grid.y K splits). Lane
+// (g, t) streams 16 bytes of row g (and g + 8) per chunk with plain loads,
+// decodes them to bf16 pairs with the in-GEMM arithmetic, and feeds
+// mma.sync m16n8k16 with the tokens as A (rows g, g + 8) and the weight as B.
+// K is permuted consistently for A and B: the lane's EPL consecutive weight
+// elements fill k-positions {2t, 2t + 1, 2t + 8, 2t + 9} of EPL / 4 steps,
+// and its A fragments read the same x elements (one 8-byte load per row and
+// step). A dot product does not depend on the order of its K terms.
+template <int FMT>
+struct Skinny {
+    static constexpr int kEPL = FMT == kFmtBf16 ? 8 : (FMT == kFmtFp8 || FMT == kFmtQ8_0) ? 16 : 32;
+    static constexpr int kChunk = 4 * kEPL;  // K per chunk (four lanes per row)
+};
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The EPL / 2 bf16 pairs of one lane's 16 raw bytes of weight row `row` at
+// element k0 (a multiple of EPL).
+template <int FMT>
+__device__ __forceinline__ void skinny_decode(const uint4 q, int row, int k0, const GemmParams &p, uint32_t *pr) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    if (FMT == kFmtBf16) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) pr[i] = w[i];
+    } else if (FMT == kFmtFp8) {
+        const float s = __ldg(p.scales + (long long)(row / p.blk_rows) * p.scale_cols + k0 / p.blk_cols);
+#pragma unroll
+        for (int i = 0; i < 8; i++) pr[i] = scale_pack(e4m3x2_f32((w[i >> 1] >> (16 * (i & 1))) & 0xffff), s);
+    } else if (FMT == kFmtQ8_0) {
+        const float d = __ldg(p.scales + (long long)row * p.scale_cols + k0 / 32);
+        const uint4 a = q8x8_bf16(w[0], w[1], d), b = q8x8_bf16(w[2], w[3], d);
+        pr[0] = a.x; pr[1] = a.y; pr[2] = a.z; pr[3] = a.w;
+        pr[4] = b.x; pr[5] = b.y; pr[6] = b.z; pr[7] = b.w;
+    } else if (FMT == kFmtMxfp4) {
+        const float s = e8m0_scale(__ldg(p.scales_u8 + (long long)row * (p.k / 32) + k0 / 32));
+#pragma unroll
+        for (int i = 0; i < 16; i++) pr[i] = scale_pack(e2m1x2_f32((w[i >> 2] >> (8 * (i & 3))) & 0xff), s);
+    } else {  // kFmtInt4
+        const int g = k0 / p.blk_cols;
+        const float s = __ldg(p.scales + (long long)row * p.scale_cols + g);
+        int zq = 8;
+        if (p.zeros) zq = (__ldg(p.zeros + (long long)(row >> 3) * p.scale_cols + g) >> ((row & 7) * 4)) & 0xf;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xff;
+            pr[i] = scale_pack(make_float2((float)((int)(byte & 0xf) - zq), (float)((int)(byte >> 4) - zq)), s);
+        }
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) k_skinny(const uint8_t *wdata, long long row_bytes, const uint16_t *x,
+                                                long long ldx, const GemmParams p, int chunks_per_split) {
+    using S = Skinny<FMT>;
+    constexpr int EPL = S::kEPL, STEPS = EPL / 4;
+    constexpr int kNum = EPL == 8 ? 2 : 1, kDen = EPL == 32 ? 2 : 1;  // bytes per element = kNum / kDen
+    __shared__ float red[8][16][17];  // [warp][row of 16][token]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int n0 = blockIdx.x * 16;
+    const int c_lo = blockIdx.y * chunks_per_split;
+    const int c_hi = min((p.k + S::kChunk - 1) / S::kChunk, c_lo + chunks_per_split);
+    const int M = p.n_tok;
+    float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+    const int rows[2] = {min(n0 + g, p.m_w - 1), min(n0 + 8 + g, p.m_w - 1)};  // clamped: stores are masked
+    const uint16_t *xa = x + (long long)min(g, M - 1) * ldx, *xb = x + (long long)min(g + 8, M - 1) * ldx;
+    const bool va = g < M, vb = g + 8 < M;
+    // kU chunks per round: all their weight loads are issued before any is
+    // decoded, so each lane keeps 2 kU 16-byte loads in flight
+    constexpr int kU = 4;
+    const uint8_t *wrow[2] = {wdata + (long long)(p.a_row0 + rows[0]) * row_bytes,
+                              wdata + (long long)(p.a_row0 + rows[1]) * row_bytes};
+    for (int c0 = c_lo + warp; c0 < c_hi; c0 += 8 * kU) {
+        uint4 q[kU][2];
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int c = c0 + 8 * u;
+            const long long off = (long long)(c * S::kChunk + t * EPL) * kNum / kDen;
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+                q[u][j] = c < c_hi ? __ldg(reinterpret_cast<const uint4 *>(wrow[j] + off)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int c = c0 + 8 * u;
+            if (c >= c_hi) break;
+            const int k0 = c * S::kChunk + t * EPL;  // this lane's first element
+            uint2 ax[STEPS], bx[STEPS];
+#pragma unroll
+            for (int s2 = 0; s2 < STEPS; s2++) {
+                ax[s2] = va ? *reinterpret_cast<const uint2 *>(xa + k0 + 4 * s2) : make_uint2(0, 0);
+                bx[s2] = vb ? *reinterpret_cast<const uint2 *>(xb + k0 + 4 * s2) : make_uint2(0, 0);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                uint32_t pr[EPL / 2];
+                skinny_decode<FMT>(q[u][j], p.a_row0 + rows[j], k0, p, pr);
+#pragma unroll
+                for (int s2 = 0; s2 < STEPS; s2++)
+                    mma_16816(acc[j], ax[s2].x, bx[s2].x, ax[s2].y, bx[s2].y, pr[2 * s2], pr[2 * s2 + 1]);
+            }
+        }
+    }
+    // acc[j]: tokens (g, g + 8) x weight rows 8 j + 2 t, + 1 -> red[warp][row][token]
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        red[warp][8 * j + 2 * t][g] = acc[j][0];
+        red[warp][8 * j + 2 * t + 1][g] = acc[j][1];
+        red[warp][8 * j + 2 * t][g + 8] = acc[j][2];
+        red[warp][8 * j + 2 * t + 1][g + 8] = acc[j][3];
+    }
+    __syncthreads();
+    // thread (row, token): warps added in order, then the epilogue
+    const int row = threadIdx.x >> 4, m = threadIdx.x & 15, n = n0 + row;
+    if (m >= M || n >= p.m_w) return;
+    float r = 0.0f;
+#pragma unroll
+    for (int w2 = 0; w2 < 8; w2++) r += red[w2][row][m];
+    if (blockIdx.y == 0) {
+        if (p.xa && p.db) r += p.xa[m] * p.db[n];
+        if (p.bias) r += p.bias[n];
+    }
+    float *o = reinterpret_cast<float *>(p.out) + (long long)m * p.ldo + n;
+    if (p.flags & kEpiAtomic) atomicAdd(o, r);
+    else if (p.flags & kEpiResidual) *o = *o + r;
+    else *o = r;
+}
+
 template <int BN, bool DUAL, int FMT>
 __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
@@ -782,6 +920,41 @@ cudaError_t launch_stage_decode(const StageArgs &a, int num_sms, cudaStream_t st
     const long long want = (chunks + 255) / 256;
     const int grid = (int)std::min<long long>(want, (long long)num_sms * 8);
     k_stage_decode<<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+int skinny_chunk(int fmt) {
+    switch (fmt) {
+    case kFmtBf16: return Skinny<kFmtBf16>::kChunk;
+    case kFmtFp8: return Skinny<kFmtFp8>::kChunk;
+    case kFmtQ8_0: return Skinny<kFmtQ8_0>::kChunk;
+    case kFmtMxfp4: return Skinny<kFmtMxfp4>::kChunk;
+    case kFmtInt4: return Skinny<kFmtInt4>::kChunk;
+    default: return 0;
+    }
+}
+
+cudaError_t launch_skinny(int fmt, const GemmOperand &a, const GemmOperand &b, const GemmParams &p, int k_splits,
+                          cudaStream_t stream) {
+    const int chunk = skinny_chunk(fmt);
+    if (!chunk || p.n_tok < 1 || p.n_tok > 16 || p.k % chunk) return cudaErrorInvalidValue;
+    if (fmt == kFmtFp8 && p.blk_cols % 16) return cudaErrorInvalidValue;
+    if (fmt == kFmtInt4 && p.blk_cols % 32) return cudaErrorInvalidValue;
+    const int chunks = p.k / chunk;
+    k_splits = std::max(1, std::min(k_splits, chunks));
+    const int per = (chunks + k_splits - 1) / k_splits;
+    dim3 grid((p.m_w + 15) / 16, (chunks + per - 1) / per);
+    const uint8_t *w = static_cast<const uint8_t *>(a.ptr);
+    const uint16_t *x = static_cast<const uint16_t *>(b.ptr);
+    const long long ldx = b.row_bytes / 2;
+    switch (fmt) {
+    case kFmtBf16: k_skinny<kFmtBf16><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtFp8: k_skinny<kFmtFp8><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtQ8_0: k_skinny<kFmtQ8_0><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtMxfp4: k_skinny<kFmtMxfp4><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtInt4: k_skinny<kFmtInt4><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 

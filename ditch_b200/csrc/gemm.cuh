@@ -106,4 +106,13 @@ struct StageArgs {
 
 cudaError_t launch_stage_decode(const StageArgs &a, int num_sms, cudaStream_t stream);
 
+// Weight-streaming product for 1..16 tokens (decode-like calls): the weight
+// read once in its stored format (bf16, FP8, Q8_0, MXFP4, INT4), tensor-core
+// mma.sync with the tokens as the 16-row operand. Plain f32 output, residual
+// add or atomic add (p.flags), bias and rank-1 delta (split 0). K must be a
+// multiple of skinny_chunk(fmt); 0 = format not supported.
+int skinny_chunk(int fmt);
+cudaError_t launch_skinny(int fmt, const GemmOperand &a, const GemmOperand &b, const GemmParams &p, int k_splits,
+                          cudaStream_t stream);
+
 }  // namespace ditch

@@ -229,6 +229,45 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         p.db_stride = ex->db_stride;
         p.bn = ex->bn;
     }
+    // 1..16 tokens: the weight-streaming product (K split over the grid, the
+    // partial sums added atomically, bias and delta with split 0)
+    const int sk = skinny_chunk(fmt);
+    if (!p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16) && n_tok <= 16 && sk && w.cols % sk == 0 &&
+        !(fmt == kFmtFp8 && w.bc % 16) && !(fmt == kFmtInt4 && w.group % 32)) {
+        const int bx = (m_rows + 15) / 16, chunks = w.cols / sk;
+        const int ks = std::max(1, std::min(chunks, (2 * dev->sms + bx - 1) / bx));  // about one wave
+        if (ks > 1) {
+            if (!(flags & kEpiResidual))
+                DITCH_CUDA(cudaMemset2DAsync(out, (size_t)ldo * 4, 0, (size_t)m_rows * 4, n_tok, dev->stream));
+            flags = (flags & ~kEpiResidual) | kEpiAtomic;
+        }
+        p.a_row0 = slab_row0;
+        p.out = out;
+        p.ldo = ldo;
+        p.flags = flags;
+        p.bias = bias;
+        p.xa = xa;
+        p.db = db;
+        if (fmt == kFmtFp8) {
+            p.scales = w.scales.as<float>();
+            p.blk_rows = w.br;
+            p.blk_cols = w.bc;
+            p.scale_cols = w.scols;
+        } else if (fmt == kFmtMxfp4) {
+            p.scales_u8 = w.scales.as<uint8_t>();
+        } else if (fmt == kFmtQ8_0) {
+            p.scales = w.scales.as<float>();
+            p.scale_cols = w.scols;
+        } else if (fmt == kFmtInt4) {
+            p.scales = w.scales.as<float>();
+            p.zeros = w.zeros.as<uint32_t>();
+            p.blk_cols = w.group;
+            p.scale_cols = w.groups;
+        }
+        cudaError_t e = run_skinny(dev, fmt, A, B, p, ks);
+        if (e != cudaSuccess) return cuda_status(e, "skinny product");
+        return DITCH_CUDA_OK;
+    }
     // Split K when the output tiles leave SMs idle (few tokens or few weight
     // rows) and the epilogue is linear: partial sums are added atomically, the
     // residual add being itself such a sum; bias and delta come with split 0.

@@ -80,3 +80,28 @@ def test_q8_0_operand_is_ditchs_decode(device):
     want = oracle.f32_to_bf16_bits(oracle.dequant_ggml(5, raw, rows * cols).reshape(rows, cols))
     assert np.array_equal(got.cpu().numpy().view(np.uint16), want)
     W.close()
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4", "int4", "q8_0"])
+@pytest.mark.parametrize("m", [1, 5, 16])
+def test_weight_streaming_small_m(device, fmt, m):
+    """1..16 tokens take the weight-streaming product (mma.sync over the
+    decoded stored format, K split across the grid): equal to x . W^T over
+    the decoded weight up to f32 accumulation order."""
+    rows, cols = 1000, 1024
+    torch.backends.cuda.matmul.allow_tf32 = False
+    gen = torch.Generator(device="cuda").manual_seed(31 + m)
+    W, _ = make_weight(device, fmt, rows, cols, gen)
+    x = torch.randn(m, cols, device="cuda", generator=gen).to(torch.bfloat16)
+    dec = torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    W.decode(dec.data_ptr())
+    device.synchronize()
+    ref = x.float() @ dec.float().T
+    out = torch.full((m, rows), float("nan"), device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    W.gemm(x.data_ptr(), m, out.data_ptr())
+    device.synchronize()
+    err = (out - ref).abs()
+    assert bool((err <= _bound(x, dec)).all()), float(err.max())
+    W.close()
