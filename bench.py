@@ -49,11 +49,12 @@ def parse():
     ap.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline sample budget (seconds)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4", "c5", "gemm"],
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4", "c5", "gemm", "gen"],
                     help="c2 (default): the FP8 dense trial loop; c1: the Qwen2-0.5B fp32 trial loop with the "
                          "whole-trial CPU baseline; c3: dequant + GEMM sweep; c4: the Qwen3-MoE MXFP4 "
                          "trial loop (expert-selective edit); c5: Llama-3-70B-shaped in-place edit sweep; gemm: one "
                          "GEMM")
+    ap.add_argument("--max-new", type=int, default=100, help="gen: tokens generated per prompt")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=4096)

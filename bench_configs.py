@@ -30,6 +30,13 @@
   layer best aligned with the direction, src/moe.zig:1373-1477), the edited
   forward and the first-token KL.
 
+* `gen`: greedy generation (the device half of ditch's KeywordRate scorer,
+  src/scorers.zig:95-155) on the C2 model: `--prompts` (default 128) prompts
+  x `--seq` tokens, `--max-new` (default 100, ditch's max_response_length)
+  tokens each, no EOS so every prompt runs to the limit. A step is one
+  ditch_cuda_generate call: the prefill into the KV cache and the decode
+  steps, with the per-step host round trip of the tokens included.
+
 All weights are seeded synthetic N(0, 0.02), generated and quantised on the
 GPU with torch (device-memory plumbing; the kernels under test are the
 library's).
@@ -791,6 +798,63 @@ def run_c5_tp(args, dev, world, rank, dist):
     group.close()
 
 
+def run_gen(args, dev):
+    """Greedy generation on the C2 model (see the module docstring)."""
+    from bench import C2, Clocks, build_c2_model, measured_peaks
+
+    spec = dict(C2, n_layers=args.layers or C2["n_layers"])
+    P, S, N = args.prompts or 128, args.seq, args.max_new
+    t0 = time.time()
+    model = build_c2_model(dev, spec, args.seed, max_seq=S + N)
+    load_s = time.time() - t0
+    rng = np.random.default_rng(args.seed + 5)
+    ps = [rng.integers(0, spec["vocab"], S).astype(np.uint32) for _ in range(P)]
+    for _ in range(args.warmup):
+        out = model.generate(ps, N)
+    dev.set_profiling(True)
+    dev.reset_stats()
+    clocks = Clocks(dev.ordinal)
+    dev.synchronize()
+    dev.timer_start()
+    n_gen = 0
+    for _ in range(args.steps):
+        out = model.generate(ps, N)
+        n_gen += sum(len(o) for o in out)
+    ms = dev.timer_stop()
+    clk = clocks.stop()
+    gemm_ms, gemm_launches, gemm_flops = dev.gemm_stats()
+    launches = dev.launches()
+    dev.set_profiling(False)
+    hbm, tf_burst, tf_sust, src = measured_peaks()
+    # weight bytes streamed per decode step: the FP8 linear weights (1 B per
+    # element plus 4 B per 128 x 128 block) and the bf16 LM head
+    H, I, V, L = spec["hidden"], spec["inter"], spec["vocab"], spec["n_layers"]
+    qd, kvd = spec["heads"] * spec["head_dim"], spec["kv_heads"] * spec["head_dim"]
+    per_layer = (qd + 2 * kvd) * H + H * qd + 2 * I * H + H * I
+    w_bytes = L * per_layer * (1 + 4 / (128 * 128)) + V * H * 2
+    steps_per_call = N - 1
+    line = {
+        "metric": "greedy generation tokens/s", "value": round(n_gen / (ms / 1000.0), 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8-e4m3 weights, bf16 MMA, f32 accumulate, f32 KV cache", "data": "synthetic",
+        "config": {"workload": "gen", "model": "llama-3-8b-shape fp8", "prompts": P, "seq_len": S, "max_new": N,
+                   "layers": L, "l2": "weights and KV cache larger than L2"},
+        "tokens_per_call": n_gen // max(args.steps, 1),
+        "roofline": {"bound": "hbm", "kernel": "decode step: every weight read once per step",
+                     "weight_gb_per_decode_step": round(w_bytes / 1e9, 3),
+                     "achieved_weight_gbs": round(w_bytes * steps_per_call * args.steps / (ms / 1000.0) / 1e9, 1),
+                     "peak": hbm, "unit": "GB/s", "peak_source": f"{src} HBM",
+                     "gemm_ms_per_step": round(gemm_ms / args.steps, 3),
+                     "gemm_share_of_step": round(gemm_ms / ms, 4) if ms > 0 else None},
+        "gpu_launches": int(launches), "clocks": clk, "one_off": {"load_s": round(load_s, 2)},
+        "first_tokens": out[0][:8],
+    }
+    line["roofline"]["frac"] = round(line["roofline"]["achieved_weight_gbs"] / hbm, 4)
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
 def run(args):
     import torch
 
@@ -826,6 +890,8 @@ def run(args):
         run_c3(args, dev)
     elif args.config == "c5":
         run_c5(args, dev)
+    elif args.config == "gen":
+        run_gen(args, dev)
     else:
         raise SystemExit(f"config {args.config} is not implemented")
     dev.close()

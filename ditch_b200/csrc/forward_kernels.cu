@@ -1,23 +1,17 @@
 // Forward-pass kernels around the GEMMs: embedding gather, RMSNorm with the
 // residual capture fused in, causal GQA attention with RoPE and q/k norms,
 // and the x . A row dot of a rank-1 delta.
+#include "attn_common.cuh"
 #include "kernels.cuh"
 
 namespace ditch {
 
 namespace {
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
+using attn::warp_max;
+using attn::warp_sum;
+using attn::rope_neox_inplace;
+using attn::rms_inplace;
 
 // One warp per row. Token ids past the table set status (the reference's
 // embedRowIndex error, src/model.zig:2547) and leave the row zero.
@@ -110,29 +104,6 @@ __global__ void k_rmsnorm_f32(const float *x, const float *w, int n, int len, fl
 // the causal key range.
 constexpr int kKeyChunk = 64;
 constexpr int kAttnWarps = 8;
-
-__device__ __forceinline__ void rope_neox_inplace(float *v, int hd, int pos, const float *cos_t, const float *sin_t,
-                                                  int lane) {
-    const int half = hd / 2;
-    const float *c = cos_t + (long long)pos * half;
-    const float *s = sin_t + (long long)pos * half;
-    // lanes split the half; x1 = v[i], x2 = v[i + half]
-    for (int i = lane; i < half; i += 32) {
-        const float x1 = v[i], x2 = v[i + half];
-        v[i] = x1 * c[i] - x2 * s[i];
-        v[i + half] = x2 * c[i] + x1 * s[i];
-    }
-}
-
-__device__ __forceinline__ void rms_inplace(float *v, int hd, const float *w, float eps, int lane) {
-    float ss = 0.0f;
-    for (int i = lane; i < hd; i += 32) ss += v[i] * v[i];
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
-    __syncwarp();
-    for (int i = lane; i < hd; i += 32) v[i] = v[i] * inv * w[i];
-    __syncwarp();
-}
 
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnParams p) {
     extern __shared__ float sm[];
@@ -592,6 +563,10 @@ cudaError_t rmsnorm_rows_f32(const float *x, const float *w, int n, int len, flo
 cudaError_t gather_rmsnorm_bf16(const float *x, const int *rows, int n, int hidden, float eps, const float *w,
                                 uint16_t *h, cudaStream_t st) {
     return rmsnorm_rows_bf16(x, w, n, hidden, eps, h, nullptr, nullptr, rows, st);
+}
+
+bool attention_prefill_preps_in_place(int head_dim, int force_generic) {
+    return !force_generic && (head_dim == 128 || head_dim == 64);
 }
 
 cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st) {

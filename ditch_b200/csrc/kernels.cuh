@@ -75,6 +75,46 @@ struct AttnParams {
 // Causal attention within each prompt with GQA, RoPE (neox) and optional q/k
 // norms (src/model.zig:4226-4374, attentionWorker 2935-2986).
 cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st);
+// True when attention_prefill leaves the q and k columns of the QKV rows
+// normed and roped in place (the tensor-core path, head sizes 64 and 128).
+bool attention_prefill_preps_in_place(int head_dim, int force_generic);
+
+// ---- greedy decode with a KV cache (src/model.zig:5378-5444) ---------------
+// One layer's cache: keys (normed and roped) and values, f32
+// [slots][max_len][kvd] each, the reference's KvCache layout
+// (src/model.zig:2586-2724) with a slot per prompt.
+struct KvParams {
+    float *qkv;                  // [n][qd + 2 kvd]
+    const int *row_b, *row_pos;  // per row: cache slot and position
+    int n, slots, max_len;
+    int heads, kv_heads, head_dim;
+    const float *rope_cos, *rope_sin;
+    const float *q_norm, *k_norm;
+    float eps;
+    float *cache_k, *cache_v;
+    int prep_k;  // 1: norm and rope the keys while storing them (0: the attention already did, in place)
+    int prep_q;  // 1: norm and rope the queries in place (decode rows)
+    int *status;
+};
+// Stores every row's keys and values at (slot, position) of the cache.
+cudaError_t kv_store(const KvParams &p, cudaStream_t st);
+
+struct DecodeAttnParams {
+    const float *qkv;            // [n][qd + 2 kvd], queries normed and roped
+    uint16_t *out;               // [n][qd] bf16
+    const int *row_b, *row_pos;  // per row: cache slot and position
+    int n, max_len;
+    int heads, kv_heads, head_dim;
+    const float *cache_k, *cache_v;
+    float scale;
+};
+// Row r attends to keys 0..row_pos[r] of its slot (its own key included:
+// kv_store runs first).
+cudaError_t attention_decode(const DecodeAttnParams &p, cudaStream_t st);
+
+// out[r] = argmax of row r of x [n][len]: the first maximum wins and NaN
+// never does; a row with nothing above -inf gives 0 (src/model.zig:5194-5204).
+cudaError_t argmax_rows(const float *x, int n, int len, uint32_t *out, cudaStream_t st);
 
 // xa[m] = sum_k act[m][k] * a[k] (act bf16, a f32): the x . A term of a rank-1
 // delta (src/tensor.zig:1036-1042).

@@ -70,8 +70,14 @@ struct Config {
 struct Batch {
     int n = 0, prompts = 0;
     DevBuf tokens, seq_start, seq_len, cap_slot, logit_rows;
+    DevBuf row_b, row_pos;  // per row: KV-cache slot and position (generation only)
     std::vector<int> h_start, h_len;
 };
+
+// What a forward does with the KV cache: nothing (prompts attend within the
+// call), store the prompts' keys and values (a generation's prefill), or run
+// single-token rows against the cache (a decode step).
+enum FwdMode { kFwdPrompts = 0, kFwdPromptsCache = 1, kFwdDecode = 2 };
 
 }  // namespace ditch
 
@@ -110,6 +116,9 @@ struct ditch_cuda_model {
     ditch::DevBuf ep_dst, ep_rcnt, ep_roff, ep_pexp, ep_act, ep_eo, ep_xa, ep_sched_gu, ep_sched_d, ep_nsched,
         ep_scores;
     int ep_score_parity = 0;
+    // greedy generation: KV cache f32 [layers][slots][kv_len][kvd] for keys and for values
+    ditch::DevBuf kv_k, kv_v, gen_next;
+    int kv_slots = 0, kv_len = 0;
     ditch::Batch work;   // scratch batch for forward / residual passes
     ditch::DevBuf sums;  // f64 residual sums
     uint64_t bytes = 0;
@@ -125,7 +134,9 @@ int make_batch(ditch_cuda_model *m, Batch &b, const uint32_t *tokens, const size
 
 // The forward over a device batch: residual capture into m->res ([L+1][nc][H])
 // when nc > 0, logits of the batch's logit rows into m->logits when nl > 0.
-int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl);
+// `mode` (FwdMode) says how attention uses the KV cache (b.row_b / b.row_pos
+// and m->kv_* must be set for the cache modes).
+int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode = kFwdPrompts);
 
 int ensure_workspace(ditch_cuda_model *m, int n_tokens, int nc, int nl);
 

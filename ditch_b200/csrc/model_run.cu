@@ -317,7 +317,7 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     return DITCH_CUDA_OK;
 }
 
-int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
+int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
     const Config &c = m->cfg;
     ditch_cuda_device *dev = m->dev;
     cudaStream_t st = dev->stream;
@@ -359,7 +359,53 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl) {
         ap.scale = 1.0f / std::sqrt((float)c.head_dim);
         ap.status = dev->status;
         ap.max_len = b.h_len.empty() ? 1 : *std::max_element(b.h_len.begin(), b.h_len.end());
-        DITCH_LAUNCH(dev, attention_prefill(ap, st));
+        if (mode == kFwdPrompts) {
+            DITCH_LAUNCH(dev, attention_prefill(ap, st));
+        } else {
+            // the cache of this layer; decode rows store their key and value
+            // first, so each attends to its own key as well
+            const size_t per_layer = (size_t)m->kv_slots * m->kv_len * c.kvd();
+            KvParams kp{};
+            kp.qkv = m->qkv.as<float>();
+            kp.row_b = b.row_b.as<int>();
+            kp.row_pos = b.row_pos.as<int>();
+            kp.n = n;
+            kp.slots = m->kv_slots;
+            kp.max_len = m->kv_len;
+            kp.heads = c.heads;
+            kp.kv_heads = c.kv_heads;
+            kp.head_dim = c.head_dim;
+            kp.rope_cos = ap.rope_cos;
+            kp.rope_sin = ap.rope_sin;
+            kp.q_norm = ap.q_norm;
+            kp.k_norm = ap.k_norm;
+            kp.eps = c.eps;
+            kp.cache_k = m->kv_k.as<float>() + li * per_layer;
+            kp.cache_v = m->kv_v.as<float>() + li * per_layer;
+            kp.status = dev->status;
+            if (mode == kFwdDecode) {
+                kp.prep_k = kp.prep_q = 1;
+                DITCH_LAUNCH(dev, kv_store(kp, st));
+                DecodeAttnParams dp{};
+                dp.qkv = m->qkv.as<float>();
+                dp.out = m->att.as<uint16_t>();
+                dp.row_b = kp.row_b;
+                dp.row_pos = kp.row_pos;
+                dp.n = n;
+                dp.max_len = m->kv_len;
+                dp.heads = c.heads;
+                dp.kv_heads = c.kv_heads;
+                dp.head_dim = c.head_dim;
+                dp.cache_k = kp.cache_k;
+                dp.cache_v = kp.cache_v;
+                dp.scale = ap.scale;
+                DITCH_LAUNCH(dev, attention_decode(dp, st));
+            } else {
+                DITCH_LAUNCH(dev, attention_prefill(ap, st));
+                kp.prep_k = attention_prefill_preps_in_place(c.head_dim, 0) ? 0 : 1;
+                DITCH_LAUNCH(dev, kv_store(kp, st));
+            }
+        }
         if (L.o_edit) DITCH_LAUNCH(dev, rowdot_bf16(m->att.as<uint16_t>(), L.o_a.as<float>(), n, qd, m->xa.as<float>(), st));
         // tensor parallel: the partial sum goes to the group's send rows, then the all-reduce adds it to x
         const bool tp = m->group && c.tp_world > 1;
@@ -863,6 +909,124 @@ int ditch_cuda_kl_score_prompts(ditch_cuda_model *m, const uint32_t *tokens, con
     DITCH_CUDA(cudaMemcpyAsync(m->kl.tokens.ptr, tokens + prompt_offsets[0], n * 4, cudaMemcpyHostToDevice,
                                m->dev->stream));
     return kl_score_impl(m, kl);
+}
+
+int ditch_cuda_generate(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets, size_t n_prompts,
+                        size_t max_new_tokens, const uint32_t *eos_ids, size_t n_eos, uint32_t *out_tokens,
+                        size_t *out_counts) {
+    clear_error();
+    REQUIRE(m && tokens && prompt_offsets && out_tokens && out_counts, "null argument");
+    REQUIRE(n_prompts > 0 && n_prompts < (1u << 20), "bad prompt count %zu", n_prompts);
+    REQUIRE(!n_eos || eos_ids, "null eos ids");
+    ditch_cuda_device *dev = m->dev;
+    std::lock_guard<std::mutex> lk(dev->mu);
+    DITCH_CUDA(cudaSetDevice(dev->ordinal));
+    const Config &c = m->cfg;
+    if (c.ep_world > 1) {
+        // ranks would leave the per-layer exchanges at different steps
+        set_error("generation under expert parallelism is not supported");
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    const size_t P = n_prompts;
+    size_t longest = 0;
+    for (size_t p = 0; p < P; p++) {
+        REQUIRE(prompt_offsets[p + 1] > prompt_offsets[p], "prompt %zu is empty", p);
+        longest = std::max(longest, prompt_offsets[p + 1] - prompt_offsets[p]);
+    }
+    REQUIRE(longest + max_new_tokens <= (size_t)m->rope_len,
+            "%zu prompt tokens plus %zu new ones exceed the %d positions the model was loaded for", longest,
+            max_new_tokens, m->rope_len);
+    // KvCache.initFor(model, prompts, longest + max_new + 1) (src/engine.zig:254-260)
+    const size_t max_len = longest + max_new_tokens + 1;
+    const size_t cache_bytes = (size_t)c.n_layers * P * max_len * c.kvd() * 4;
+    DITCH_CUDA(m->kv_k.reserve(cache_bytes));
+    DITCH_CUDA(m->kv_v.reserve(cache_bytes));
+    DITCH_CUDA(m->gen_next.reserve(P * 4));
+    m->kv_slots = (int)P;
+    m->kv_len = (int)max_len;
+    cudaStream_t st = dev->stream;
+    const int V = c.vocab;
+    int s;
+
+    // prefill: the prompts' keys and values go to their slots, the last row
+    // of every prompt gives the first token (src/model.zig:5292-5357)
+    Batch &b = m->work;
+    if ((s = make_batch(m, b, tokens, prompt_offsets, P, 0, true, nullptr, nullptr))) return s;
+    std::vector<int> rb, rp;
+    rb.reserve(b.n);
+    rp.reserve(b.n);
+    for (size_t p = 0; p < P; p++)
+        for (int pos = 0; pos < b.h_len[p]; pos++) {
+            rb.push_back((int)p);
+            rp.push_back(pos);
+        }
+    DITCH_CUDA(upload_vec(b.row_b, rb, st));
+    DITCH_CUDA(upload_vec(b.row_pos, rp, st));
+    if ((s = forward_batch(m, b, 0, (int)P, kFwdPromptsCache))) return s;
+    std::vector<uint32_t> next(P);
+    DITCH_LAUNCH(dev, argmax_rows(m->logits.as<float>(), (int)P, V, m->gen_next.as<uint32_t>(), st));
+    DITCH_CUDA(cudaMemcpyAsync(next.data(), m->gen_next.ptr, P * 4, cudaMemcpyDeviceToHost, st));
+    DITCH_CUDA(cudaStreamSynchronize(st));
+
+    auto is_eos = [&](uint32_t t) {
+        for (size_t e = 0; e < n_eos; e++)
+            if (eos_ids[e] == t) return true;
+        return false;
+    };
+    const size_t stride = std::max<size_t>(max_new_tokens, 1);
+    std::vector<size_t> pos(P), count(P, 1);
+    std::vector<char> active(P, 0);
+    size_t n_active = 0;
+    for (size_t i = 0; i < P; i++) {
+        out_tokens[i * stride] = next[i];
+        pos[i] = (size_t)b.h_len[i];
+        if (!(is_eos(next[i]) || max_new_tokens <= 1 || pos[i] >= max_len)) {
+            active[i] = 1;
+            n_active++;
+        }
+    }
+    // decode steps over the active prompts, one row each at its next position
+    std::vector<uint32_t> toks;
+    std::vector<int> lr;
+    for (size_t step = 1; step < max_new_tokens && n_active > 0; step++) {
+        toks.clear();
+        rb.clear();
+        rp.clear();
+        lr.clear();
+        for (size_t i = 0; i < P; i++) {
+            if (!active[i]) continue;
+            lr.push_back((int)toks.size());
+            toks.push_back(out_tokens[i * stride + count[i] - 1]);
+            rb.push_back((int)i);
+            rp.push_back((int)pos[i]);
+        }
+        const int n = (int)toks.size();
+        b.n = n;
+        b.prompts = n;
+        b.h_start.clear();
+        b.h_len.clear();
+        DITCH_CUDA(upload_vec(b.tokens, toks, st));
+        DITCH_CUDA(upload_vec(b.row_b, rb, st));
+        DITCH_CUDA(upload_vec(b.row_pos, rp, st));
+        DITCH_CUDA(upload_vec(b.logit_rows, lr, st));
+        if ((s = forward_batch(m, b, 0, n, kFwdDecode))) return s;
+        DITCH_LAUNCH(dev, argmax_rows(m->logits.as<float>(), n, V, m->gen_next.as<uint32_t>(), st));
+        DITCH_CUDA(cudaMemcpyAsync(next.data(), m->gen_next.ptr, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+        DITCH_CUDA(cudaStreamSynchronize(st));
+        int j = 0;
+        for (size_t i = 0; i < P; i++) {
+            if (!active[i]) continue;
+            const uint32_t t = next[j++];
+            pos[i]++;
+            out_tokens[i * stride + count[i]++] = t;
+            if (is_eos(t) || pos[i] >= max_len) {
+                active[i] = 0;
+                n_active--;
+            }
+        }
+    }
+    for (size_t i = 0; i < P; i++) out_counts[i] = count[i];
+    return check_status(dev, "generate");
 }
 
 }  // extern "C"

@@ -99,6 +99,7 @@ SIGNATURES = {
     "ditch_cuda_model_free": (None, [vp]),
     "ditch_cuda_model_bytes": (C.c_uint64, [vp]),
     "ditch_cuda_forward": (C.c_int, [vp, u32p, u32p, u32p, sz, C.POINTER(sz), sz, f32p, C.POINTER(sz), sz, f32p]),
+    "ditch_cuda_generate": (C.c_int, [vp, u32p, C.POINTER(sz), sz, sz, u32p, sz, u32p, C.POINTER(sz)]),
     "ditch_cuda_residual_sums": (C.c_int, [vp, u32p, C.POINTER(sz), sz, sz, sz, f64p, u64p]),
     "ditch_cuda_directions": (C.c_int, [vp, f64p, C.c_uint64, f64p, C.c_uint64, C.c_int, f32p]),
     "ditch_cuda_set_directions": (C.c_int, [vp, f32p, sz]),
@@ -181,6 +182,7 @@ class Device:
         h = vp()
         check(lib().ditch_cuda_open(ordinal, memory_budget, C.byref(h)))
         self.h = h
+        self.ordinal = ordinal
 
     def close(self):
         if self.h:
@@ -519,6 +521,20 @@ class Model:
         offs = np.zeros(len(prompts) + 1, np.uintp)
         offs[1:] = np.cumsum([len(p) for p in prompts])
         return tokens, offs
+
+    def generate(self, prompts, max_new_tokens, eos_ids=()):
+        """Greedy generation (model.generate, src/model.zig:5359-5444): a list
+        of token lists, one per prompt, each ending at its first EOS token
+        (kept) or after max_new_tokens tokens (at least one)."""
+        tokens, offs = self._flat(prompts)
+        eos = np.ascontiguousarray(eos_ids, np.uint32)
+        stride = max(int(max_new_tokens), 1)
+        out = np.zeros((len(prompts), stride), np.uint32)
+        counts = np.zeros(len(prompts), np.uintp)
+        check(lib().ditch_cuda_generate(self.h, _p(tokens, u32p), _p(offs, C.POINTER(sz)), len(prompts),
+                                        int(max_new_tokens), _p(eos, u32p) if len(eos) else None, len(eos),
+                                        _p(out, u32p), _p(counts, C.POINTER(sz))))
+        return [out[i, :counts[i]].tolist() for i in range(len(prompts))]
 
     def residual_sums(self, prompts, window=1, batch_size=0):
         s = self.spec

@@ -199,6 +199,23 @@ int ditch_cuda_forward(ditch_cuda_model *m, const uint32_t *tokens, const uint32
                        size_t n, const size_t *capture_rows, size_t nc, float *residuals, const size_t *logit_rows,
                        size_t nl, float *logits);
 
+/* Greedy generation, model.generate (src/model.zig:5359-5444) with the cache
+ * Engine.generateBatch sizes (src/engine.zig:254-260): one prefill of the
+ * prompts (concatenated tokens, prompt_offsets[n_prompts + 1]) filling a
+ * device KV cache, the first token from its logits, then one-row decode
+ * steps over the prompts still active. A prompt stops after a token in
+ * eos_ids (which is kept) or after max_new_tokens tokens; at least one token
+ * is produced. Tokens go to out_tokens [n_prompts][max(max_new_tokens, 1)]
+ * (row-major), their number per prompt to out_counts [n_prompts]. The
+ * argmax keeps the first maximum (src/model.zig:5194-5204). The longest
+ * prompt plus max_new_tokens must fit the positions the model was loaded
+ * for. Under expert parallelism it returns DITCH_CUDA_UNSUPPORTED. This is
+ * the device half of KeywordRate (src/scorers.zig:95-155); detokenising and
+ * the keyword match stay on the host. */
+int ditch_cuda_generate(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets, size_t n_prompts,
+                        size_t max_new_tokens, const uint32_t *eos_ids, size_t n_eos, uint32_t *out_tokens,
+                        size_t *out_counts);
+
 /* engine.getResidualMeanObserved (src/engine.zig:314-438) without winsorising:
  * prompts given as concatenated tokens with prompt_offsets[n_prompts + 1];
  * the last `window` tokens of every prompt are averaged and summed in f64

@@ -92,6 +92,54 @@ class OracleModel:
         return res, logits
 
 
+    def generate(self, prompts, max_new_tokens, eos_ids=()):
+        """Greedy generation restated from model.generate
+        (src/model.zig:5378-5444): the first token from each prompt's last
+        logits, then one token per step for every prompt still active; a
+        prompt stops after an EOS token (kept) or after max_new_tokens tokens
+        (at least one is produced). Each step re-runs the forward over the
+        whole sequences: the reference's cached decode step computes the same
+        per-query arithmetic over the same keys.
+
+        Returns (tokens, margins): per prompt the token list and, per token,
+        the gap between the two largest logits of the row it was picked from
+        (a tie-closeness measure for comparisons at float tolerance)."""
+        eos = set(int(e) for e in eos_ids)
+        seqs = [list(map(int, p)) for p in prompts]
+        out = [[] for _ in prompts]
+        gaps = [[] for _ in prompts]
+        active = list(range(len(prompts)))
+        steps = max(int(max_new_tokens), 1)
+        for step in range(steps):
+            toks, rb, rp, _, _, _, last = flatten_batch([seqs[i] for i in active])
+            _, logits = self.forward(toks, rb, rp, logit_rows=last)
+            still = []
+            for j, i in enumerate(active):
+                t, gap = argmax_first(logits[j])
+                out[i].append(t)
+                gaps[i].append(gap)
+                seqs[i].append(t)
+                if t not in eos and step + 1 < steps:
+                    still.append(i)
+            active = still
+            if not active:
+                break
+        return out, gaps
+
+
+def argmax_first(x):
+    """argmax of src/model.zig:5194-5204: a scan from -inf at index 0 with a
+    strict `>`, so the first maximum wins and NaN never does. Also returns
+    the gap between the two largest values (inf with one candidate)."""
+    v = np.where(np.isnan(x), -np.inf, x).astype(np.float64)
+    i = int(np.argmax(v))
+    if not np.isfinite(v[i]) and v[i] < 0:
+        return 0, np.inf
+    rest = np.delete(v, i)
+    second = rest.max() if rest.size else -np.inf
+    return i, float(v[i] - second)
+
+
 def flatten_batch(prompts, window=1):
     """Flattens prompts into (tokens, row_b, row_pos, capture, first_capture,
     take, last_rows) as src/engine.zig:392-410 does."""

@@ -31,6 +31,45 @@ def test_fixture_forward(family):
         assert int(np.argmax(logits[i])) == c["argmax"]
 
 
+@pytest.mark.parametrize("family", FAMILIES)
+def test_fixture_generation(family):
+    """src/model_test.zig:76-83: greedy generation of 4 tokens starts with
+    the reference's argmax; each step's token is the first maximum of that
+    step's logits over the extended sequence (src/model.zig:5378-5444)."""
+    g = Golden(family)
+    m = OracleModel(g.spec, g.f32_weights())
+    toks, gaps = m.generate(g.prompts(), 4)
+    assert [t[0] for t in toks] == [c["argmax"] for c in g.cases]
+    assert all(len(t) == 4 for t in toks)
+    seq = [np.concatenate([p, np.asarray(t[:3], np.uint32)]) for p, t in zip(g.prompts(), toks)]
+    ft, rb, rp, cap, first, take, last = flatten_batch(seq)
+    _, logits = m.forward(ft, rb, rp, cap, last)
+    assert [int(np.argmax(r)) for r in logits] == [t[3] for t in toks]
+
+
+def test_generation_stop_rules():
+    """EOS is kept and ends the prompt; max_new_tokens 0 and 1 give one
+    token (src/model.zig:5404-5440)."""
+    g = Golden("qwen2")
+    m = OracleModel(g.spec, g.f32_weights())
+    free, _ = m.generate(g.prompts(), 6)
+    stop, _ = m.generate(g.prompts(), 6, eos_ids=[free[0][2]])
+    assert stop[0] == free[0][:free[0].index(free[0][2]) + 1]
+    for n in (0, 1):
+        one, _ = m.generate(g.prompts(), n)
+        assert [len(t) for t in one] == [1] * len(free)
+
+
+def test_argmax_first_rule():
+    """src/model.zig:5194-5204: the first maximum wins, NaN never does, a row
+    with nothing above -inf gives 0."""
+    from oracle.model import argmax_first
+    assert argmax_first(np.array([1, 3, 3], np.float32))[0] == 1
+    assert argmax_first(np.array([np.nan, 2, np.nan, 2], np.float32))[0] == 1
+    assert argmax_first(np.array([-np.inf, -np.inf], np.float32))[0] == 0
+    assert argmax_first(np.array([np.nan, -np.inf], np.float32))[0] == 0
+
+
 def test_fixture_forward_unbatched_matches_batched():
     """One prompt per call gives the same rows as the batched call (engine batching)."""
     g = Golden("qwen2")
