@@ -107,6 +107,7 @@ struct DecodeAttnParams {
     int heads, kv_heads, head_dim;
     const float *cache_k, *cache_v;
     float scale;
+    int force_generic;  // the shared-memory kernel for any head size (tests)
 };
 // Row r attends to keys 0..row_pos[r] of its slot (its own key included:
 // kv_store runs first).

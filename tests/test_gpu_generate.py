@@ -77,6 +77,9 @@ CASES = {
     "qknorm_hd32_gqa4": dict(n_layers=2, hidden=256, heads=8, kv_heads=2, head_dim=32, inter=384, qk_norm=True),
     "fp8_hd128": dict(n_layers=2, hidden=256, heads=2, kv_heads=1, head_dim=128, inter=512, fmt="fp8",
                       block=(128, 128)),
+    # 7 query heads per kv head (padded to 8 in the register decode path), and plain multi-head attention
+    "gqa7_hd64": dict(n_layers=2, hidden=256, heads=14, kv_heads=2, head_dim=64, inter=512, qkv_bias=True),
+    "mha_hd128": dict(n_layers=2, hidden=256, heads=2, kv_heads=2, head_dim=128, inter=512),
     "moe_mxfp4": dict(n_layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, inter=256, fmt="mxfp4",
                       moe=dict(experts=8, top_k=2, inter=128)),
 }
