@@ -55,6 +55,8 @@ def parse():
                          "trial loop (expert-selective edit); c5: Llama-3-70B-shaped in-place edit sweep; gemm: one "
                          "GEMM")
     ap.add_argument("--max-new", type=int, default=100, help="gen: tokens generated per prompt")
+    ap.add_argument("--deterministic", type=int, default=0,
+                    help="1: K splits summed in a fixed order (stream-K) instead of atomically")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=4096)
@@ -370,6 +372,7 @@ def main():
     dev = ditch_b200.Device(local)
     if args.stage_min_tokens is not None:
         dev.set_decode_staging(args.stage_min_tokens)
+    dev.set_deterministic(args.deterministic)
     spec = dict(C2, n_layers=args.layers)
     L, V, P, S = spec["n_layers"], spec["vocab"], args.prompts, args.seq
     t0 = time.time()

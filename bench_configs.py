@@ -872,6 +872,7 @@ def run(args):
     dev = ditch_b200.Device(local)
     if args.stage_min_tokens is not None:
         dev.set_decode_staging(args.stage_min_tokens)
+    dev.set_deterministic(args.deterministic)
     if args.config == "c4" or (args.config == "c5" and world > 1):
         if args.config == "c4":
             run_c4(args, dev, world, rank, dist)

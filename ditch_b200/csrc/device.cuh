@@ -93,7 +93,10 @@ struct ditch_cuda_device {
     // staged decode: quantised weights of GEMMs with at least this many tokens
     // are decoded once to bf16 here and multiplied by the bf16 GEMM (0 = never)
     ditch::DevBuf stage;
+    ditch::DevBuf sk_ws, sk_cnt;  // stream-K partial sums and per-tile arrival counters
+    long long sk_tiles = 0;      // counters zeroed so far
     int stage_min_tokens = 1024;
+    bool deterministic = false;  // K splits summed in a fixed order (no atomics)
     // profiling of GEMMs
     bool profiling = false;
     std::vector<ditch::GemmEvent> events;

@@ -39,13 +39,19 @@ struct Cfg {
     static constexpr int kNA = DUAL ? 2 : 1;
     static constexpr int kABytes = BM * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
+    // raw weight tile of one k-tile: 128 rows x 64 bytes (8-bit codes, TMA
+    // 64-byte swizzle) or x 32 bytes (4-bit codes, no swizzle)
     static constexpr int kRawBytes = (FMT == kFmtFp8 || FMT == kFmtQ8_0)  ? BM * BK
                                      : (FMT == kFmtMxfp4 || FMT == kFmtInt4) ? BM * BK / 2
                                                                              : 0;
     static constexpr int kStageBytes = kNA * kABytes + kBBytes;
     static constexpr int kRawStageBytes = kNA * kRawBytes;
     // raw-tile stages in flight: narrow token tiles (decode-like products,
-    // bound by streaming the weight) keep more of the weight in flight
+    // bound by streaming the weight) keep more of the weight in flight. A raw
+    // tile is loaded together with its stage's token tile, so at most
+    // min(kStages, kRawStages) raw tiles are in flight. (Measured on B200: a
+    // separate raw-tile producer running up to 16 tiles ahead, with fewer
+    // operand stages, and 128-byte raw rows were both slower at 128 tokens.)
     static constexpr int kRawStages = !kQuant ? 0 : BN <= 64 ? (DUAL ? 4 : 8) : 3;
     static constexpr int kRawRing = kRawStages > 0 ? kRawStages : 1;  // modulus (unused without raw tiles)
     static constexpr int kStagesFit = (kSmemBudget - kRawStages * kRawStageBytes) / kStageBytes;
@@ -54,9 +60,14 @@ struct Cfg {
     static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
     static constexpr int kTmemColsRaw = kAccBufs * kAccCols;
     static constexpr int kTmemCols = kTmemColsRaw < 32 ? 32 : kTmemColsRaw;
+    // producer, MMA, epilogue, then (quantised) the decode warps
     static constexpr int kWarps = 2 + kEpiWarps + (kQuant ? kXformWarps : 0);
     static constexpr int kThreads = kWarps * 32;
-    static constexpr int kSmemBytes = kStages * kStageBytes + kRawStages * kRawStageBytes + 1024 + 256;
+    // mbarriers (full, empty, raw full, raw empty, 2 + 2 accumulator, 2 stream-K), then the
+    // TMEM base, the abort word and the stream-K flag
+    static constexpr int kBarBytes = (8 * (2 * kStages + 2 * kRawStages + 6) + 16 + 63) / 64 * 64;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kRawStages * kRawStageBytes + 1024 + kBarBytes;
+    static_assert(kSmemBytes <= 232448, "over the 227 KB of shared memory per block");
     static_assert(kStages >= 2, "shared memory too small for two stages");
     static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
     static_assert((kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation must be a power of two");
@@ -66,8 +77,10 @@ template <class C>
 struct SmemLayout {
     uint8_t *base;
     uint64_t *full, *empty, *rawfull, *rawempty, *tfull, *tempty;
+    uint64_t *skbar;  // stream-K: [0] parts stored (one arrival per epilogue warp), [1] flag set
     uint32_t *tmem_base;
     int *abort;
+    int *sk_flag;  // stream-K: this CTA finishes the current split tile
     __device__ __forceinline__ uint8_t *a(int s, int i) const { return base + s * C::kStageBytes + i * C::kABytes; }
     __device__ __forceinline__ uint8_t *b(int s) const { return base + s * C::kStageBytes + C::kNA * C::kABytes; }
     __device__ __forceinline__ uint8_t *raw(int s, int i) const {
@@ -88,8 +101,10 @@ __device__ __forceinline__ SmemLayout<C> carve(uint8_t *smem_raw) {
     L.rawempty = L.rawfull + C::kRawStages;
     L.tfull = L.rawempty + C::kRawStages;
     L.tempty = L.tfull + 2;
-    L.tmem_base = reinterpret_cast<uint32_t *>(L.tempty + 2);
+    L.skbar = L.tempty + 2;
+    L.tmem_base = reinterpret_cast<uint32_t *>(L.skbar + 2);
     L.abort = reinterpret_cast<int *>(L.tmem_base + 1);
+    L.sk_flag = L.abort + 1;
     return L;
 }
 
@@ -104,7 +119,44 @@ struct TileInfo {
     int e;         // expert (grouped mode), else -1
     int kt0, kt1;  // k-tiles of this tile's split
     bool first_split;
+    bool sk_partial;  // stream-K: the tile is split between CTAs
+    int sk_tile;      // stream-K: the tile's index
 };
+
+// k-units: runs of p.kt_unit k-tiles (the k-tiles one raw weight tile holds),
+// the grain of K splits and stream-K ranges.
+__device__ __forceinline__ int k_units(const GemmParams &p) { return (p.k_tiles + p.kt_unit - 1) / p.kt_unit; }
+
+// Stream-K range of CTA `cta` of `grid`: units [u0, u1) of tiles x k-units.
+__device__ __forceinline__ void sk_range(const GemmParams &p, int cta, int grid, long long &u0, long long &u1) {
+    const long long U = (long long)p.w_tiles * p.t_tiles * k_units(p);
+    u0 = U * cta / grid;
+    u1 = U * (cta + 1) / grid;
+}
+
+// The CTA whose stream-K range holds unit u: the largest c with u0(c) <= u.
+__device__ __forceinline__ int sk_owner(const GemmParams &p, long long u, int grid) {
+    const long long U = (long long)p.w_tiles * p.t_tiles * k_units(p);
+    return (int)(((u + 1) * grid - 1) / U);
+}
+
+// This CTA's work: tiles first, first + step, ... below end (whole tiles or
+// k-splits), or under stream-K its segments 0, 1, ... (one per tile its
+// range touches).
+__device__ __forceinline__ void work_range(const GemmParams &p, int tiles, int &first, int &end, int &step) {
+    if (!p.stream_k) {
+        first = blockIdx.x;
+        end = tiles;
+        step = gridDim.x;
+        return;
+    }
+    long long u0, u1;
+    sk_range(p, blockIdx.x, gridDim.x, u0, u1);
+    first = 0;
+    step = 1;
+    const int ku = k_units(p);
+    end = u1 > u0 ? (int)((u1 - 1) / ku - u0 / ku + 1) : 0;
+}
 
 template <int BN>
 __device__ __forceinline__ TileInfo tile_info(const GemmParams &p, int tile, int kt_per_split) {
@@ -119,14 +171,36 @@ __device__ __forceinline__ TileInfo tile_info(const GemmParams &p, int tile, int
         t.kt0 = 0;
         t.kt1 = p.k_tiles;
         t.first_split = true;
+        t.sk_partial = false;
+        t.sk_tile = -1;
         return t;
     }
     // Output tiles run in bands of kBand token tiles, weight tile by weight
     // tile within a band: the tiles the persistent CTAs hold at one time share
     // a few weight tiles and a few token tiles, which then stay in L2.
     constexpr int kBand = 8;
-    const int split = tile % p.k_splits;
-    const int rest = tile / p.k_splits;
+    int split, rest;
+    if (p.stream_k) {  // `tile` is the segment index within this CTA's range
+        long long u0, u1;
+        sk_range(p, blockIdx.x, gridDim.x, u0, u1);
+        const int ku = k_units(p);
+        rest = (int)(u0 / ku) + tile;
+        const long long k0 = (long long)rest * ku;
+        t.kt0 = (int)max(u0 - k0, 0LL) * p.kt_unit;
+        t.kt1 = (int)min((long long)p.k_tiles, min(u1 - k0, (long long)ku) * p.kt_unit);
+        t.first_split = true;  // the epilogue runs once, on the whole sum
+        t.sk_partial = !(t.kt0 == 0 && t.kt1 == p.k_tiles);
+        t.sk_tile = rest;
+        split = 0;
+    } else {
+        split = tile % p.k_splits;
+        rest = tile / p.k_splits;
+        t.kt0 = split * kt_per_split;
+        t.kt1 = min(p.k_tiles, t.kt0 + kt_per_split);
+        t.first_split = split == 0;
+        t.sk_partial = false;
+        t.sk_tile = -1;
+    }
     const int band = rest / (kBand * p.w_tiles);
     const int idx = rest - band * kBand * p.w_tiles;
     const int g = min(kBand, p.t_tiles - band * kBand);
@@ -135,9 +209,7 @@ __device__ __forceinline__ TileInfo tile_info(const GemmParams &p, int tile, int
     t.tok0 = (band * kBand + idx % g) * BN;
     t.tok_cnt = min(BN, p.n_tok - t.tok0);
     t.a_row0 = p.a_row0;
-    t.kt0 = split * kt_per_split;
-    t.kt1 = min(p.k_tiles, t.kt0 + kt_per_split);
-    t.first_split = split == 0;
+    (void)split;
     return t;
 }
 
@@ -170,14 +242,20 @@ __device__ __forceinline__ uint32_t scale_pack(float2 v, float s) {
     return pack_bf16x2(r.x, r.y);
 }
 
+// The decoded operand tile is bf16 K-major with the 128-byte swizzle: output
+// chunk j (eight elements) of row r at j ^ (r & 7). Half h of a row's k-tile
+// is elements [32 h, 32 h + 32), output chunks 4 h .. 4 h + 3.
+__device__ __forceinline__ void put_chunk(uint8_t *atile, int r, int j, uint4 o) {
+    *reinterpret_cast<uint4 *>(atile + r * 128 + ((j ^ (r & 7)) << 4)) = o;
+}
+
 // FP8 E4M3 with f32 block scales: bf16(code * scale[row / br][col / bc]).
 // Raw tile: 128 rows x 64 bytes, TMA 64B swizzle (chunk c at c ^ ((r >> 1) & 3)).
 // srow: the scale row of this weight row; s_tile: the k-tile's scale when the
 // block columns are a multiple of 64 (one_scale), loaded by the caller ahead
-// of the stage's barrier wait.
+// of the barrier wait.
 __device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *atile, int r, int h, const float *srow,
                                           bool one_scale, float s_tile, int k0, const GemmParams &p) {
-    uint8_t *arow = atile + r * 128;
     const int rs = (r >> 1) & 3;
 #pragma unroll
     for (int cc = 0; cc < 2; cc++) {
@@ -195,7 +273,7 @@ __device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *atile, in
             o.y = scale_pack(e4m3x2_f32(w0 >> 16), s);
             o.z = scale_pack(e4m3x2_f32(w1 & 0xffff), s);
             o.w = scale_pack(e4m3x2_f32(w1 >> 16), s);
-            *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
+            put_chunk(atile, r, j, o);
         }
     }
 }
@@ -212,46 +290,31 @@ __device__ __forceinline__ float2 e2m1x2_f32(uint32_t byte) {
 }
 
 // MXFP4 (natural layout): bf16(e2m1[nibble] * 2^(e - 127)), low nibble first.
-// Raw tile: 128 rows x 32 bytes (no swizzle); half h reads 16 bytes = 32 elements.
-__device__ __forceinline__ void xform_mxfp4(const uint8_t *raw, uint8_t *atile, int r, int h, int grow, int k0,
-                                            const GemmParams &p) {
-    uint8_t *arow = atile + r * 128;
-    const uint8_t *srow = p.scales_u8 + (long long)grow * (p.k / 32);
+// Raw tile: 128 rows x 32 bytes (no swizzle); half h reads 16 bytes = one
+// 32-element block with scale s (loaded by the caller ahead of the wait).
+__device__ __forceinline__ void xform_mxfp4(const uint8_t *raw, uint8_t *atile, int r, int h, float s) {
     const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
     const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-    const int blk = (k0 >> 5) + h;
-    const float s = (blk * 32 < p.k) ? e8m0_scale(__ldg(srow + blk)) : 0.0f;
 #pragma unroll
     for (int jj = 0; jj < 4; jj++) {  // one word = 8 elements = one output chunk
-        const int j = 4 * h + jj;
         const uint32_t w = words[jj];
         uint4 o;
         o.x = scale_pack(e2m1x2_f32(w & 0xff), s);
         o.y = scale_pack(e2m1x2_f32((w >> 8) & 0xff), s);
         o.z = scale_pack(e2m1x2_f32((w >> 16) & 0xff), s);
         o.w = scale_pack(e2m1x2_f32(w >> 24), s);
-        *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
+        put_chunk(atile, r, 4 * h + jj, o);
     }
 }
 
 // INT4 pack-quantized, contiguous groups (a multiple of 64):
-// bf16(f32(q - zp) * scale[row][g]).
-__device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *atile, int r, int h, int grow, int k0,
-                                           const GemmParams &p) {
-    uint8_t *arow = atile + r * 128;
-    const int groups = p.scale_cols;
-    const int g = k0 / p.blk_cols;
-    const float s = (k0 < p.k) ? __ldg(p.scales + (long long)grow * groups + g) : 0.0f;
-    int zq = 8;
-    if (p.zeros) {
-        const uint32_t zw = __ldg(p.zeros + (long long)(grow >> 3) * groups + g);
-        zq = (zw >> ((grow & 7) * 4)) & 0xf;
-    }
+// bf16(f32(q - zp) * scale[row][g]); s and the zero point zq of the k-tile's
+// group are loaded by the caller. Raw tile as MXFP4.
+__device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *atile, int r, int h, float s, int zq) {
     const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
     const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int jj = 0; jj < 4; jj++) {
-        const int j = 4 * h + jj;
         const uint32_t w = words[jj];
         uint32_t o[4];
 #pragma unroll
@@ -260,7 +323,7 @@ __device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *atile, i
             const int hi = (int)((w >> (8 * e + 4)) & 0xf) - zq;
             o[e] = scale_pack(make_float2((float)lo, (float)hi), s);
         }
-        *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        put_chunk(atile, r, 4 * h + jj, make_uint4(o[0], o[1], o[2], o[3]));
     }
 }
 
@@ -280,24 +343,39 @@ __device__ __forceinline__ uint4 q8x8_bf16(uint32_t w0, uint32_t w1, float d) {
 }
 
 // GGUF Q8_0 repacked at load: int8 codes [rows][cols] and the block scales d
-// as f32 [rows][cols / 32]. Raw tile: 128 rows x 64 codes, TMA 64B swizzle
-// (chunk c at c ^ ((r >> 1) & 3), as FP8); half h is one 32-code block.
-__device__ __forceinline__ void xform_q8_0(const uint8_t *raw, uint8_t *atile, int r, int h, int grow, int k0,
-                                           const GemmParams &p) {
-    uint8_t *arow = atile + r * 128;
+// as f32 [rows][cols / 32]. Raw tile as FP8; half h is one 32-code block
+// with scale d (loaded by the caller).
+__device__ __forceinline__ void xform_q8_0(const uint8_t *raw, uint8_t *atile, int r, int h, float d) {
     const int rs = (r >> 1) & 3;
-    const int blk = (k0 >> 5) + h;
-    const float d = (blk * 32 < p.k) ? __ldg(p.scales + (long long)grow * p.scale_cols + blk) : 0.0f;
 #pragma unroll
     for (int cc = 0; cc < 2; cc++) {
         const int c = 2 * h + cc;  // raw 16-byte chunk: output chunks 2c, 2c + 1
         const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ rs) << 4));
-#pragma unroll
-        for (int half = 0; half < 2; half++) {
-            const int j = 2 * c + half;
-            const uint4 o = half ? q8x8_bf16(q.z, q.w, d) : q8x8_bf16(q.x, q.y, d);
-            *reinterpret_cast<uint4 *>(arow + ((j ^ (r & 7)) << 4)) = o;
-        }
+        put_chunk(atile, r, 2 * c, q8x8_bf16(q.x, q.y, d));
+        put_chunk(atile, r, 2 * c + 1, q8x8_bf16(q.z, q.w, d));
+    }
+}
+
+// The side data of half h of one row's k-tile at k0, loaded ahead of the
+// barrier waits: the scale (FP8 one_scale, MXFP4, Q8_0, INT4) and the INT4
+// zero point.
+template <int FMT>
+__device__ __forceinline__ void load_side(const GemmParams &p, int vrow, const float *srow, bool one_scale, int k0,
+                                          int h, float &s, int &zq) {
+    s = 0.0f;
+    zq = 8;
+    if (FMT == kFmtFp8) {
+        if (one_scale) s = __ldg(srow + k0 / p.blk_cols);
+    } else if (FMT == kFmtMxfp4) {
+        const int blk = (k0 >> 5) + h;
+        if (blk * 32 < p.k) s = e8m0_scale(__ldg(p.scales_u8 + (long long)vrow * (p.k / 32) + blk));
+    } else if (FMT == kFmtQ8_0) {
+        const int blk = (k0 >> 5) + h;
+        if (blk * 32 < p.k) s = __ldg(p.scales + (long long)vrow * p.scale_cols + blk);
+    } else if (FMT == kFmtInt4) {
+        const int groups = p.scale_cols, g = k0 / p.blk_cols;
+        if (k0 < p.k) s = __ldg(p.scales + (long long)vrow * groups + g);
+        if (p.zeros) zq = (__ldg(p.zeros + (long long)(vrow >> 3) * groups + g) >> ((vrow & 7) * 4)) & 0xf;
     }
 }
 
@@ -493,13 +571,35 @@ __global__ void __launch_bounds__(256) k_skinny(const uint8_t *wdata, long long 
         red[warp][8 * j + 2 * t + 1][g + 8] = acc[j][3];
     }
     __syncthreads();
-    // thread (row, token): warps added in order, then the epilogue
+    // thread (row, token): warps added in order
     const int row = threadIdx.x >> 4, m = threadIdx.x & 15, n = n0 + row;
-    if (m >= M || n >= p.m_w) return;
     float r = 0.0f;
 #pragma unroll
     for (int w2 = 0; w2 < 8; w2++) r += red[w2][row][m];
-    if (blockIdx.y == 0) {
+    if (gridDim.y > 1 && p.sk_ws) {
+        // K split over the grid, deterministic mode: each block leaves its
+        // partial sums in sk_ws; the block that arrives last adds them in
+        // split order (the result does not depend on timing) and runs the
+        // epilogue. Otherwise every split adds its sum atomically.
+        __shared__ int s_last;
+        float *ws = p.sk_ws + (size_t)blockIdx.x * 256;
+        const size_t split_stride = (size_t)gridDim.x * 256;
+        __stcg(ws + blockIdx.y * split_stride + threadIdx.x, r);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const int old = atomicAdd(p.sk_cnt + blockIdx.x, 1);
+            s_last = old == (int)gridDim.y - 1;
+            if (s_last) p.sk_cnt[blockIdx.x] = 0;  // every split has arrived: ready for the next launch
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        r = 0.0f;
+        for (int y = 0; y < (int)gridDim.y; y++) r += __ldcg(ws + y * split_stride + threadIdx.x);
+    }
+    if (m >= M || n >= p.m_w) return;
+    if (blockIdx.y == 0 || p.sk_ws) {  // bias and delta once per output
         if (p.xa && p.db) r += p.xa[m] * p.db[n];
         if (p.bias) r += p.bias[n];
     }
@@ -533,6 +633,8 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
             mbar_init(&L.tfull[b], 1);
             mbar_init(&L.tempty[b], kEpiWarps);
         }
+        mbar_init(&L.skbar[0], kEpiWarps);
+        mbar_init(&L.skbar[1], 1);
         *L.abort = 0;
         fence_barrier_init();
     }
@@ -551,13 +653,15 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
     const uint32_t tmem = *L.tmem_base;
 
     const int tiles = p.sched ? *p.n_sched : p.w_tiles * p.t_tiles * p.k_splits;
-    const int kt_per_split = (p.k_tiles + p.k_splits - 1) / p.k_splits;
+    const int kt_per_split = (k_units(p) + p.k_splits - 1) / p.k_splits * p.kt_unit;
+    int w_first, w_end, w_step;
+    work_range(p, tiles, w_first, w_end, w_step);
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             int it = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+            for (int tile = w_first; tile < w_end && !*abort; tile += w_step) {
                 const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
                 const int arow = ti.a_row0 + ti.wt * BM;
                 for (int kt = ti.kt0; kt < ti.kt1; kt++, it++) {
@@ -587,7 +691,7 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
             int it = 0, local = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, local++) {
+            for (int tile = w_first; tile < w_end && !*abort; tile += w_step, local++) {
                 const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
                 const int buf = local % C::kAccBufs;
                 const uint32_t use_ph = (local / C::kAccBufs) & 1;
@@ -621,15 +725,16 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
     } else if (warp < 2 + kEpiWarps) {
         // ---------------- epilogue ----------------
         const int q = warp & 3;  // TMEM lane quarter this warp may access
-        int local = 0;
-        for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, local++) {
+        const int trow = q * 32 + lane;  // row of the tile (weight row) this thread owns
+        int local = 0, sk_uses = 0;
+        for (int tile = w_first; tile < w_end && !*abort; tile += w_step, local++) {
             const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
             const bool first_split = ti.first_split;  // bias and delta once per output
             const int buf = local % C::kAccBufs;
             const uint32_t use_ph = (local / C::kAccBufs) & 1;
             if (!mbar_wait(&L.tfull[buf], use_ph, abort, p.status)) break;
             tc_fence_after();
-            const int n = ti.wt * BM + q * 32 + lane;  // weight row = output feature
+            const int n = ti.wt * BM + trow;  // weight row = output feature
             const bool n_ok = n < p.m_w;
             const float bias = (p.bias && n_ok && first_split) ? p.bias[n] : 0.0f;
             bool delta = p.db && n_ok && first_split;
@@ -641,61 +746,143 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
             const float dbn = delta ? dbp[n] : 0.0f;
             const uint32_t tbase = tmem + buf * C::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
             const int m_end = ti.tok0 + ti.tok_cnt;
+            // stream-K: a part of a split tile goes to this CTA's slot; the CTA
+            // that brings the last part sums them all in k order and finishes
+            constexpr int EC = 32;  // accumulator columns (tokens) per step
+            bool finish = true;
+            int c_lo = 0, c_hi = -1;
+            long long t_u0 = 0;
+            if (ti.sk_partial) {
+                t_u0 = (long long)ti.sk_tile * k_units(p);
+                c_lo = sk_owner(p, t_u0, gridDim.x);
+                c_hi = sk_owner(p, t_u0 + k_units(p) - 1, gridDim.x);
+                float *mine = p.sk_ws + ((size_t)(blockIdx.x * 2 + (tile == 0 ? 0 : 1)) * C::kNA * BM + trow) * BN;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+                for (int c0 = 0; c0 < BN; c0 += EC) {
+                    if (ti.tok0 + c0 >= m_end) break;
+#pragma unroll
+                    for (int i = 0; i < C::kNA; i++)
+#pragma unroll
+                        for (int hc = 0; hc < EC; hc += 16) {
+                            float v[16];
+                            tmem_ld16(tbase + i * BN + c0 + hc, v);
+                            float4 *dst = reinterpret_cast<float4 *>(mine + (size_t)i * BM * BN + c0 + hc);
+#pragma unroll
+                            for (int j = 0; j < 4; j++)
+                                __stcg(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+                        }
+                }
+                // all epilogue warps' stores, then one thread counts this part in
+                const uint32_t sk_ph = sk_uses++ & 1;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&L.skbar[0]);
+                bool ok = true;
+                if (threadIdx.x == 64) {  // first epilogue thread
+                    ok = mbar_wait(&L.skbar[0], sk_ph, abort, p.status);
+                    if (ok) {
+                        __threadfence();
+                        const int old = atomicAdd(p.sk_cnt + ti.sk_tile, 1);
+                        const int last = old == c_hi - c_lo;
+                        if (last) p.sk_cnt[ti.sk_tile] = 0;  // every part has arrived: ready for the next launch
+                        *reinterpret_cast<volatile int *>(L.sk_flag) = last;
+                        mbar_arrive(&L.skbar[1]);
+                    }
+                }
+                if (ok) ok = mbar_wait(&L.skbar[1], sk_ph, abort, p.status);
+                finish = ok && *reinterpret_cast<volatile int *>(L.sk_flag) != 0;
+                if (finish) {
+                    // the whole sum, parts in k order (this CTA's from TMEM),
+                    // back into TMEM, where the epilogue below reads it
+                    __threadfence();
+#pragma unroll 1
+                    for (int c0 = 0; c0 < BN; c0 += 16) {
+                        if (ti.tok0 + c0 >= m_end) break;
+#pragma unroll
+                        for (int i = 0; i < C::kNA; i++) {
+                            float acc[16];
+#pragma unroll
+                            for (int j = 0; j < 16; j++) acc[j] = 0.0f;
+                            for (int c = c_lo; c <= c_hi; c++) {
+                                float part[16];
+                                if (c == (int)blockIdx.x) {
+                                    tmem_ld16(tbase + i * BN + c0, part);
+                                } else {
+                                    long long cu0, cu1;
+                                    sk_range(p, c, gridDim.x, cu0, cu1);
+                                    const float4 *src = reinterpret_cast<const float4 *>(
+                                        p.sk_ws + ((size_t)((c * 2 + (cu0 >= t_u0 ? 0 : 1)) * C::kNA + i) * BM + trow) * BN +
+                                        c0);
+#pragma unroll
+                                    for (int j = 0; j < 4; j++) {
+                                        const float4 a4 = __ldcg(src + j);
+                                        part[4 * j] = a4.x;
+                                        part[4 * j + 1] = a4.y;
+                                        part[4 * j + 2] = a4.z;
+                                        part[4 * j + 3] = a4.w;
+                                    }
+                                }
+#pragma unroll
+                                for (int j = 0; j < 16; j++) acc[j] += part[j];
+                            }
+                            tmem_st16(tbase + i * BN + c0, acc);
+                        }
+                    }
+                }
+            }
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN && finish; c0 += EC) {
                 if (ti.tok0 + c0 >= m_end) break;  // warp-uniform: no valid token left
-                float v[32];
+                float v[EC], u[EC];
                 tmem_ld32(tbase + c0, v);
-                float u[32];
                 if (DUAL) tmem_ld32(tbase + BN + c0, u);
                 const int m0 = ti.tok0 + c0;
-                const int mv = min(32, m_end - m0);  // valid tokens of this chunk (>= 1)
+                const int mv = min(EC, m_end - m0);  // valid tokens of this chunk (>= 1)
                 // Every load of a chunk is issued before its first store: as far
                 // as the compiler knows the stores may alias the loads, and
                 // interleaving them serialises one memory round trip per token.
-                float r[32];
+                float r[EC];
                 if (p.xa && dbn != 0.0f) {
-                    float xa[32];
+                    float xa[EC];
 #pragma unroll
-                    for (int j = 0; j < 32; j++) xa[j] = j < mv ? __ldg(p.xa + m0 + j) : 0.0f;
+                    for (int j = 0; j < EC; j++) xa[j] = j < mv ? __ldg(p.xa + m0 + j) : 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 32; j++) r[j] = v[j] + xa[j] * dbn;
+                    for (int j = 0; j < EC; j++) r[j] = v[j] + xa[j] * dbn;
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; j++) r[j] = v[j];
+                    for (int j = 0; j < EC; j++) r[j] = v[j];
                 }
 #pragma unroll
-                for (int j = 0; j < 32; j++) r[j] += bias;
+                for (int j = 0; j < EC; j++) r[j] += bias;
                 const long long o0 = (long long)m0 * p.ldo + n;
                 if (!n_ok) {
                     // weight row past the matrix: nothing to store
                 } else if (DUAL) {
                     uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + o0;
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
+                    for (int j = 0; j < EC; j++)
                         if (j < mv) ob[(long long)j * p.ldo] = f32_to_bf16_bits(silu_f(r[j]) * u[j]);
                 } else if (p.flags & kEpiAtomic) {
                     float *of = reinterpret_cast<float *>(p.out) + o0;
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
+                    for (int j = 0; j < EC; j++)
                         if (j < mv) atomicAdd(of + (long long)j * p.ldo, r[j]);
                 } else if (p.flags & kEpiResidual) {
                     float *of = reinterpret_cast<float *>(p.out) + o0;
-                    float old[32];
+                    float old[EC];
 #pragma unroll
-                    for (int j = 0; j < 32; j++) old[j] = j < mv ? of[(long long)j * p.ldo] : 0.0f;
+                    for (int j = 0; j < EC; j++) old[j] = j < mv ? of[(long long)j * p.ldo] : 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
+                    for (int j = 0; j < EC; j++)
                         if (j < mv) of[(long long)j * p.ldo] = old[j] + r[j];
                 } else if (p.flags & kEpiOutBf16) {
                     uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + o0;
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
+                    for (int j = 0; j < EC; j++)
                         if (j < mv) ob[(long long)j * p.ldo] = f32_to_bf16_bits(r[j]);
                 } else {
                     float *of = reinterpret_cast<float *>(p.out) + o0;
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
+                    for (int j = 0; j < EC; j++)
                         if (j < mv) of[(long long)j * p.ldo] = r[j];
                 }
             }
@@ -709,7 +896,7 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         const int r = t & 127, h = t >> 7;
         const bool one_scale = FMT == kFmtFp8 && (p.blk_cols & 63) == 0;
         int it = 0;
-        for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+        for (int tile = w_first; tile < w_end && !*abort; tile += w_step) {
             const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
             int vrow[C::kNA];
             const float *srow[C::kNA];
@@ -725,20 +912,22 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                 const int s = it % C::kStages;
                 const int rs = it % C::kRawRing;
                 const uint32_t rph = (it / C::kRawRing) & 1;
-                float s_tile[C::kNA];
+                float sd[C::kNA];
+                int zd[C::kNA];
 #pragma unroll
-                for (int i = 0; i < C::kNA; i++)  // issued before the wait: its latency hides behind it
-                    s_tile[i] = one_scale ? __ldg(srow[i] + (kt * BK) / p.blk_cols) : 0.0f;
+                for (int i = 0; i < C::kNA; i++)  // issued before the wait: their latency hides behind it
+                    load_side<FMT>(p, vrow[i], srow[i], one_scale, kt * BK, h, sd[i], zd[i]);
+                // the raw tile has landed (the producer loaded it after operand stage s was free)
                 if (!mbar_wait(&L.rawfull[rs], rph, abort, p.status)) {
                     ok = false;
                     break;
                 }
 #pragma unroll
                 for (int i = 0; i < C::kNA; i++) {
-                    if (FMT == kFmtFp8) xform_fp8(L.raw(rs, i), L.a(s, i), r, h, srow[i], one_scale, s_tile[i], kt * BK, p);
-                    if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(rs, i), L.a(s, i), r, h, vrow[i], kt * BK, p);
-                    if (FMT == kFmtInt4) xform_int4(L.raw(rs, i), L.a(s, i), r, h, vrow[i], kt * BK, p);
-                    if (FMT == kFmtQ8_0) xform_q8_0(L.raw(rs, i), L.a(s, i), r, h, vrow[i], kt * BK, p);
+                    if (FMT == kFmtFp8) xform_fp8(L.raw(rs, i), L.a(s, i), r, h, srow[i], one_scale, sd[i], kt * BK, p);
+                    if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(rs, i), L.a(s, i), r, h, sd[i]);
+                    if (FMT == kFmtInt4) xform_int4(L.raw(rs, i), L.a(s, i), r, h, sd[i], zd[i]);
+                    if (FMT == kFmtQ8_0) xform_q8_0(L.raw(rs, i), L.a(s, i), r, h, sd[i]);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -872,14 +1061,24 @@ cudaError_t launch_t(const GemmOperand &a, const GemmOperand *a2, const GemmOper
         attr_set = true;
     }
     p.k_tiles = (p.k + BK - 1) / BK;
+    p.kt_unit = 1;
     p.w_tiles = (p.m_w + BM - 1) / BM;
     p.t_tiles = (p.n_tok + BN - 1) / BN;
+    const int ku = (p.k_tiles + p.kt_unit - 1) / p.kt_unit;
     if (p.k_splits < 1) p.k_splits = 1;
-    if (p.k_splits > p.k_tiles) p.k_splits = p.k_tiles;
     if (p.sched) p.k_splits = 1;  // grouped tiles are whole-K
+    if (p.k_splits > 1) {  // splits of whole k-units, none empty
+        const int per = (ku + p.k_splits - 1) / p.k_splits;
+        p.k_splits = (ku + per - 1) / per;
+    }
     const int tiles = p.w_tiles * p.t_tiles * p.k_splits;
     // grouped mode: the tile count is on the device; the grid is persistent
-    const int grid = p.sched ? num_sms : std::min(tiles, num_sms);
+    // stream-K: every CTA gets at least 4 k-units (so none is empty)
+    const long long units = (long long)tiles * ku;
+    const int grid = p.sched ? num_sms
+                     : p.stream_k ? (int)std::max(1LL, std::min<long long>(num_sms, units / 4))
+                                  : std::min(tiles, num_sms);
+    if (p.stream_k && (p.sched || p.k_splits != 1 || !p.sk_ws || !p.sk_cnt)) return cudaErrorInvalidValue;
     if (grid <= 0) return cudaSuccess;
     gemm_kernel<BN, DUAL, FMT><<<grid, C::kThreads, C::kSmemBytes, stream>>>(ma, ma2, mb, p);
     return cudaGetLastError();
@@ -899,6 +1098,19 @@ cudaError_t dispatch_fmt(int fmt, const GemmOperand &a, const GemmOperand *a2, c
 }
 
 }  // namespace
+
+size_t skinny_split_bytes(int rows, int splits) { return (size_t)((rows + 15) / 16) * splits * 256 * sizeof(float); }
+
+size_t gemm_stream_k_bytes(int grid, int bn, bool dual) {
+    return (size_t)grid * 2 * (dual ? 2 : 1) * BM * bn * sizeof(float);
+}
+
+bool gemm_wants_stream_k(long long tiles, int k_tiles, int sms) {
+    // Only where whole tiles would leave over half the SMs idle: measured on
+    // B200, the split tiles' extra partial-sum traffic and fix-up cost more
+    // than a ragged last wave of wider occupancy.
+    return tiles > 0 && sms > 0 && k_tiles >= 8 && 2 * tiles <= sms;
+}
 
 // Token tile width: narrow tiles for small batches (decode-like calls stay
 // weight-bandwidth bound and need no padding to 256 tokens); quantised weights
@@ -944,6 +1156,7 @@ cudaError_t launch_skinny(int fmt, const GemmOperand &a, const GemmOperand &b, c
     k_splits = std::max(1, std::min(k_splits, chunks));
     const int per = (chunks + k_splits - 1) / k_splits;
     dim3 grid((p.m_w + 15) / 16, (chunks + per - 1) / per);
+    if (grid.y > 1 && (p.sk_ws ? !p.sk_cnt : !(p.flags & kEpiAtomic))) return cudaErrorInvalidValue;
     const uint8_t *w = static_cast<const uint8_t *>(a.ptr);
     const uint16_t *x = static_cast<const uint16_t *>(b.ptr);
     const long long ldx = b.row_bytes / 2;

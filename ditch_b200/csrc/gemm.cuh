@@ -46,6 +46,7 @@ struct GemmParams {
     int n_tok;     // valid tokens
     int k;         // reduction length
     int w_tiles, t_tiles, k_tiles, k_splits;
+    int kt_unit;        // k-tiles per raw weight tile: the grain of K splits (set by the launcher)
     int a2_row_offset;  // dual mode: row offset of the up weight in the A2 map
     int a_row0;         // first weight row (a slab of a stacked tensor)
     void *out;
@@ -71,7 +72,24 @@ struct GemmParams {
     const int *e_flags;   // per expert: apply the rank-1 delta (xa, db) only when set
     long long db_stride;  // db of expert e at db + e * db_stride
     int bn;               // token tile (32, 64, 128, 256); 0 = chosen from n_tok
+    // Stream-K (dense mode, k_splits 1): the grid's CTAs take equal contiguous
+    // ranges of the (tile, k-tile) units. A tile split between CTAs is summed
+    // in k order by the CTA that finishes the last of its parts (the others
+    // leave their partial sums in sk_ws and count themselves in sk_cnt), which
+    // then runs the epilogue once: results do not depend on timing.
+    int stream_k;
+    float *sk_ws;  // [grid][2][accumulators][128][bn] f32 partial sums
+    int *sk_cnt;   // [tiles] arrival counters, zero between launches
 };
+
+// Device bytes of the weight-streaming product's split partial sums (in
+// sk_ws; the per-row-block counters are the first (rows + 15) / 16 of sk_cnt).
+size_t skinny_split_bytes(int rows, int splits);
+// Device bytes of the stream-K partial sums for a grid of `grid` CTAs.
+size_t gemm_stream_k_bytes(int grid, int bn, bool dual);
+// Whether a dense GEMM of `tiles` whole output tiles runs stream-K on `sms`
+// SMs (when the whole tiles would leave over half of them idle).
+bool gemm_wants_stream_k(long long tiles, int k_tiles, int sms);
 
 // Token tile width the GEMM uses for n_tok tokens (dual = SwiGLU mode,
 // quant = a weight format decoded inside the GEMM).

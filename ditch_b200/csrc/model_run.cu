@@ -229,17 +229,28 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         p.db_stride = ex->db_stride;
         p.bn = ex->bn;
     }
-    // 1..16 tokens: the weight-streaming product (K split over the grid, the
-    // partial sums added atomically, bias and delta with split 0)
+    // 1..16 tokens: the weight-streaming product, K split over the grid: the
+    // partial sums are added atomically, or in deterministic mode left in
+    // sk_ws and added in split order by the last block of each row block
     const int sk = skinny_chunk(fmt);
     if (!p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16) && n_tok <= 16 && sk && w.cols % sk == 0 &&
         !(fmt == kFmtFp8 && w.bc % 16) && !(fmt == kFmtInt4 && w.group % 32)) {
         const int bx = (m_rows + 15) / 16, chunks = w.cols / sk;
         const int ks = std::max(1, std::min(chunks, (2 * dev->sms + bx - 1) / bx));  // about one wave
-        if (ks > 1) {
+        if (ks > 1 && !dev->deterministic) {
             if (!(flags & kEpiResidual))
                 DITCH_CUDA(cudaMemset2DAsync(out, (size_t)ldo * 4, 0, (size_t)m_rows * 4, n_tok, dev->stream));
             flags = (flags & ~kEpiResidual) | kEpiAtomic;
+        } else if (ks > 1) {
+            const int per = (chunks + ks - 1) / ks, splits = (chunks + per - 1) / per;
+            DITCH_CUDA(dev->sk_ws.reserve(skinny_split_bytes(m_rows, splits)));
+            if (dev->sk_tiles < bx) {
+                DITCH_CUDA(dev->sk_cnt.reserve((size_t)bx * sizeof(int)));
+                DITCH_CUDA(cudaMemsetAsync(dev->sk_cnt.ptr, 0, (size_t)bx * sizeof(int), dev->stream));
+                dev->sk_tiles = bx;
+            }
+            p.sk_ws = dev->sk_ws.as<float>();
+            p.sk_cnt = dev->sk_cnt.as<int>();
         }
         p.a_row0 = slab_row0;
         p.out = out;
@@ -268,24 +279,37 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         if (e != cudaSuccess) return cuda_status(e, "skinny product");
         return DITCH_CUDA_OK;
     }
-    // Split K when the output tiles leave SMs idle (few tokens or few weight
-    // rows) and the epilogue is linear: partial sums are added atomically, the
-    // residual add being itself such a sum; bias and delta come with split 0.
-    if (!p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16)) {
-        const int bn = gemm_token_tile(n_tok, false, fmt != kFmtBf16);
-        const long long tiles = (long long)((m_rows + 127) / 128) * ((n_tok + bn - 1) / bn);
-        const int k_tiles = (w.cols + 63) / 64;
-        if (tiles < dev->sms && k_tiles >= 8) {
-            // as many splits as still fit one wave: a second, nearly empty
-            // wave would double the time of the streaming-bound product
-            int ks = (int)(dev->sms / tiles);
-            ks = std::min(ks, k_tiles / 4);
-            if (ks > 1) {
-                p.k_splits = ks;
-                if (!(flags & kEpiResidual))
-                    DITCH_CUDA(cudaMemset2DAsync(out, (size_t)ldo * 4, 0, (size_t)m_rows * 4, n_tok, dev->stream));
-                flags = (flags & ~kEpiResidual) | kEpiAtomic;
+    // Few output tiles (few weight rows and few tokens) leave SMs idle: split
+    // K. By default the splits are fixed and add their partial sums
+    // atomically (linear epilogues only); in deterministic mode the GEMM runs
+    // stream-K, where a tile split between CTAs is summed in k order by the
+    // CTA that brings its last part, for any epilogue.
+    const int bn = gemm_token_tile(n_tok, dual, fmt != kFmtBf16);
+    const long long tiles = (long long)((m_rows + 127) / 128) * ((n_tok + bn - 1) / bn);
+    const int k_tiles = (w.cols + 63) / 64;
+    if (!dev->deterministic && !p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16) &&
+        tiles < dev->sms && k_tiles >= 8) {
+        // as many splits as still fit one wave: a second, nearly empty wave
+        // would double the time of the streaming-bound product
+        const int ks = std::min((int)(dev->sms / tiles), k_tiles / 4);
+        if (ks > 1) {
+            p.k_splits = ks;
+            if (!(flags & kEpiResidual))
+                DITCH_CUDA(cudaMemset2DAsync(out, (size_t)ldo * 4, 0, (size_t)m_rows * 4, n_tok, dev->stream));
+            flags = (flags & ~kEpiResidual) | kEpiAtomic;
+        }
+    }
+    if (dev->deterministic && !p.sched && p.k_splits == 1) {
+        if (gemm_wants_stream_k(tiles, k_tiles, dev->sms)) {
+            DITCH_CUDA(dev->sk_ws.reserve(gemm_stream_k_bytes(dev->sms, bn, dual)));
+            if (dev->sk_tiles < tiles) {
+                DITCH_CUDA(dev->sk_cnt.reserve((size_t)tiles * sizeof(int)));
+                DITCH_CUDA(cudaMemsetAsync(dev->sk_cnt.ptr, 0, (size_t)tiles * sizeof(int), dev->stream));
+                dev->sk_tiles = tiles;
             }
+            p.stream_k = 1;
+            p.sk_ws = dev->sk_ws.as<float>();
+            p.sk_cnt = dev->sk_cnt.as<int>();
         }
     }
     p.a2_row_offset = a2_row_offset;

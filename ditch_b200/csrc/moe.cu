@@ -810,6 +810,9 @@ int ditch_cuda_model_set_group(ditch_cuda_model *m, ditch_cuda_group *g, size_t 
     std::lock_guard<std::mutex> lk(m->dev->mu);
     m->group = g;
     m->group_tokens = max_tokens;
+    // tensor parallel ranks recompute the replicated parts (norms, the LM
+    // head) and must agree bit for bit: products summed in a fixed order
+    if (tp) m->dev->deterministic = true;
     return DITCH_CUDA_OK;
 }
 

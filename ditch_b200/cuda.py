@@ -119,6 +119,7 @@ SIGNATURES = {
     "ditch_cuda_weight_gemm": (C.c_int, [vp, vp, sz, vp, C.c_int]),
     "ditch_cuda_weight_decode": (C.c_int, [vp, vp]),
     "ditch_cuda_set_decode_staging": (C.c_int, [vp, C.c_int]),
+    "ditch_cuda_set_deterministic": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_peer_handle_bytes": (sz, []),
     "ditch_cuda_group_create": (C.c_int, [vp, C.c_int, C.c_int, sz, C.POINTER(vp), vp]),
     "ditch_cuda_group_open": (C.c_int, [vp, vp]),
@@ -323,6 +324,10 @@ class Device:
         """Dense GEMMs over quantised weights with at least `min_tokens` tokens
         decode the weight once to bf16 scratch; 0 keeps every decode in the GEMM."""
         check(lib().ditch_cuda_set_decode_staging(self.h, int(min_tokens)))
+
+    def set_deterministic(self, on):
+        """K splits summed in a fixed order instead of atomically (default off)."""
+        check(lib().ditch_cuda_set_deterministic(self.h, int(bool(on))))
 
     def set_profiling(self, on):
         check(lib().ditch_cuda_set_profiling(self.h, int(on)))

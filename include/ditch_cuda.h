@@ -318,6 +318,17 @@ int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out_bf16);
  * the GEMM. Default 1024. No counterpart in the reference (a tuning knob of
  * this backend). */
 int ditch_cuda_set_decode_staging(ditch_cuda_device *dev, int min_tokens);
+/* Deterministic products. GEMMs with few output tiles split K over the SMs;
+ * by default the splits add their partial sums with atomics, whose order
+ * (and so the last bits of the result) varies from run to run. With
+ * deterministic mode on, they run stream-K instead (each CTA takes an equal
+ * share of the tile x k-tile work and a tile split between CTAs is summed in
+ * k order by the CTA that brings its last part), and the 1..16-token product
+ * adds its splits in order: the same inputs give the same bits on every run
+ * and every GPU, at some cost in speed. A model joined to a tensor-parallel
+ * group turns it on for its device (the ranks' replicated results must
+ * agree bit for bit). Default off. No counterpart in the reference. */
+int ditch_cuda_set_deterministic(ditch_cuda_device *dev, int enabled);
 
 /* ---- peer groups and expert parallelism (one process per GPU of one node;
  * no counterpart in ditch, which runs on one host) ---- */

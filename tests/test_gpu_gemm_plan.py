@@ -58,6 +58,39 @@ def test_staged_and_fused_plans(device, fmt, shape):
         assert torch.equal(outs[0], outs[1])
 
 
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4"])
+@pytest.mark.parametrize("rows,cols,m", [(1408, 2048, 128), (1408, 2048, 5), (384, 512, 1100), (640, 4096, 300)])
+def test_split_products_are_deterministic(device, fmt, rows, cols, m):
+    """In deterministic mode, stream-K tiles (split between CTAs) and the
+    split weight-streaming product are summed in a fixed order: repeated
+    calls give the same bits, within the f32 bound of the decoded operand's
+    product. The default (atomic) splits stay within the same bound."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    gen = torch.Generator(device="cuda").manual_seed(rows + m)
+    W, _ = make_weight(device, fmt, rows, cols, gen)
+    x = torch.randn(m, cols, device="cuda", generator=gen).to(torch.bfloat16)
+    dec = torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    W.decode(dec.data_ptr())
+    device.synchronize()
+    ref = x.float() @ dec.float().T
+    bound = _bound(x, dec)
+    outs = []
+    try:
+        for det in (0, 1, 1, 1):
+            device.set_deterministic(det)
+            out = torch.full((m, rows), float("nan"), device="cuda", dtype=torch.float32)
+            torch.cuda.synchronize()
+            W.gemm(x.data_ptr(), m, out.data_ptr())
+            device.synchronize()
+            assert bool(((out - ref).abs() <= bound).all()), (det, float((out - ref).abs().max()))
+            outs.append(out)
+    finally:
+        device.set_deterministic(0)
+        W.close()
+    assert torch.equal(outs[1], outs[2]) and torch.equal(outs[1], outs[3])
+
+
 def test_q8_0_operand_is_ditchs_decode(device):
     """The Q8_0 GEMM operand (repacked codes and f32 scales, decoded in the
     GEMM or staged) equals ditch's f32 decode d * q (src/quant.zig:81-85)
