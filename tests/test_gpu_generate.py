@@ -154,3 +154,32 @@ def test_fixture_generation(device, family):
     routed = (g.spec, g.f32_weights()) if g.spec.get("moe_layers") else None
     check_generation(OracleModel(g.spec, g.f32_weights()), ps, got, 4, routed=routed)
     m.close()
+
+
+def test_keyword_rate_on_device(device):
+    """KeywordRate (src/scorers.zig:97-155) with the device generating and a
+    toy tokenizer on the host: the rate is the share of responses with a
+    marker, batch by batch; deterministic mode makes the repeated generation
+    bit-identical so the two counts must agree exactly."""
+    from ditch_b200.scorers import is_match, keyword_rate
+
+    spec, f32, tensors = make_model(960, n_layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, inter=512)
+    ps = prompts(33, [6, 9, 12, 4, 20, 7], spec["vocab"])
+    m = ditch_b200.Model(device, spec, tensors, max_seq=64)
+    words = ["sorry", "a", "b", "c", "d", "e", "f"]
+
+    def detok(toks):
+        return " ".join(words[t % 7] for t in toks)
+
+    device.set_deterministic(True)
+    try:
+        first = []
+        r = keyword_rate(m, ps, detok, max_new_tokens=8, batch_size=4, first_tokens=first)
+        outs = m.generate(ps[:4], 8) + m.generate(ps[4:], 8)
+    finally:
+        device.set_deterministic(False)
+    want = [is_match(detok(o)) for o in outs]
+    assert r["value"] == sum(want) / len(ps) and r["pruned"] is None
+    assert first == [(o[0], w) for o, w in zip(outs, want)]
+    check_generation(OracleModel(spec, f32), ps, outs, 8)
+    m.close()
