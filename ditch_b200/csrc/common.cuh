@@ -115,6 +115,30 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap *map, uint64_t *ba
         : "memory");
 }
 
+// The same with an L2 eviction-priority hint (a policy from l2_policy_*).
+__device__ __forceinline__ void tma_load_2d_hint(const CUtensorMap *map, uint64_t *bar, void *dst, int x, int y,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
+// L2 policies: data read once (evicted first) and data many CTAs reread
+// (kept longest).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 // Makes this thread's generic-proxy shared-memory writes visible to the async
 // proxy (the tensor cores read operands through it).
 __device__ __forceinline__ void fence_proxy_async_smem() {

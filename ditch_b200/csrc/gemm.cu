@@ -242,6 +242,15 @@ __device__ __forceinline__ uint32_t scale_pack(float2 v, float s) {
     return pack_bf16x2(r.x, r.y);
 }
 
+// Four E4M3 codes (one word, low byte first) times one block scale s, as two
+// bf16x2 words (codes 0, 1 and 2, 3). (Measured on B200: building the f32
+// values with integer shifts and one multiply by s * 2^120, exact but with
+// twice the instructions, made the decode-bound GEMMs slower.)
+__device__ __forceinline__ void e4m3x4_scaled(uint32_t w, float s, uint32_t &lo, uint32_t &hi) {
+    lo = scale_pack(e4m3x2_f32(w & 0xffff), s);
+    hi = scale_pack(e4m3x2_f32(w >> 16), s);
+}
+
 // The decoded operand tile is bf16 K-major with the 128-byte swizzle: output
 // chunk j (eight elements) of row r at j ^ (r & 7). Half h of a row's k-tile
 // is elements [32 h, 32 h + 32), output chunks 4 h .. 4 h + 3.
@@ -267,12 +276,9 @@ __device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *atile, in
             const int j = 2 * c + half;
             const int col = k0 + 8 * j;
             const float s = one_scale ? s_tile : ((col < p.k) ? __ldg(srow + col / p.blk_cols) : 0.0f);
-            const uint32_t w0 = words[2 * half], w1 = words[2 * half + 1];
             uint4 o;
-            o.x = scale_pack(e4m3x2_f32(w0 & 0xffff), s);
-            o.y = scale_pack(e4m3x2_f32(w0 >> 16), s);
-            o.z = scale_pack(e4m3x2_f32(w1 & 0xffff), s);
-            o.w = scale_pack(e4m3x2_f32(w1 >> 16), s);
+            e4m3x4_scaled(words[2 * half], s, o.x, o.y);
+            e4m3x4_scaled(words[2 * half + 1], s, o.z, o.w);
             put_chunk(atile, r, j, o);
         }
     }
@@ -402,14 +408,15 @@ __global__ void __launch_bounds__(256) k_stage_decode(const StageArgs a) {
 #pragma unroll
             for (int half = 0; half < 2; half++) {
                 uint32_t o[4];
+                if (one) {
+                    e4m3x4_scaled(words[2 * half], s0, o[0], o[1]);
+                    e4m3x4_scaled(words[2 * half + 1], s0, o[2], o[3]);
+                } else {  // block columns not a multiple of 16: a scale per element
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int c = c0 + 8 * half + 2 * e;
-                    const uint32_t two = words[2 * half + (e >> 1)] >> (16 * (e & 1));
-                    const float2 v = e4m3x2_f32(two & 0xffff);
-                    if (one) {
-                        o[e] = scale_pack(v, s0);
-                    } else {  // block columns not a multiple of 16: a scale per element
+                    for (int e = 0; e < 4; e++) {
+                        const int c = c0 + 8 * half + 2 * e;
+                        const uint32_t two = words[2 * half + (e >> 1)] >> (16 * (e & 1));
+                        const float2 v = e4m3x2_f32(two & 0xffff);
                         const float sl = __ldg(srow + c / a.blk_cols), sh = __ldg(srow + (c + 1) / a.blk_cols);
                         o[e] = pack_bf16x2(v.x * sl, v.y * sh);
                     }
@@ -453,7 +460,8 @@ __global__ void __launch_bounds__(256) k_stage_decode(const StageArgs a) {
 // out[m][n] = x[m] . W[n] for m < M <= 16, the weight read once in its
 // stored format. Block = 8 warps over 16 weight rows (two n8 tiles); the
 // warps share the block's K range chunk by chunk and their partial sums are
-// added in shared memory (then atomically across grid.y K splits). Lane
+// added in shared memory (then across grid.y K splits: atomically, or in
+// split order in deterministic mode). Lane
 // (g, t) streams 16 bytes of row g (and g + 8) per chunk with plain loads,
 // decodes them to bf16 pairs with the in-GEMM arithmetic, and feeds
 // mma.sync m16n8k16 with the tokens as A (rows g, g + 8) and the weight as B.
@@ -487,7 +495,7 @@ __device__ __forceinline__ void skinny_decode(const uint4 q, int row, int k0, co
     } else if (FMT == kFmtFp8) {
         const float s = __ldg(p.scales + (long long)(row / p.blk_rows) * p.scale_cols + k0 / p.blk_cols);
 #pragma unroll
-        for (int i = 0; i < 8; i++) pr[i] = scale_pack(e4m3x2_f32((w[i >> 1] >> (16 * (i & 1))) & 0xffff), s);
+        for (int i = 0; i < 4; i++) e4m3x4_scaled(w[i], s, pr[2 * i], pr[2 * i + 1]);
     } else if (FMT == kFmtQ8_0) {
         const float d = __ldg(p.scales + (long long)row * p.scale_cols + k0 / 32);
         const uint4 a = q8x8_bf16(w[0], w[1], d), b = q8x8_bf16(w[2], w[3], d);
@@ -660,6 +668,11 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
+            // one or two token tiles (decode-sized products): every weight tile
+            // is read once and every token tile by all CTAs, so the weight
+            // stream goes first out of L2 and the token tiles stay
+            const bool hint = !p.sched && p.t_tiles <= 2;
+            const uint64_t pol_w = l2_policy_evict_first(), pol_t = l2_policy_evict_last();
             int it = 0;
             for (int tile = w_first; tile < w_end && !*abort; tile += w_step) {
                 const TileInfo ti = tile_info<BN>(p, tile, kt_per_split);
@@ -674,15 +687,28 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                         if (!mbar_wait(&L.rawempty[rs], rph ^ 1, abort, p.status)) break;
                         mbar_arrive_expect_tx(&L.rawfull[rs], C::kRawStageBytes);
                         const int xb = kt * ((FMT == kFmtFp8 || FMT == kFmtQ8_0) ? BK : BK / 2);  // raw bytes along K
-                        tma_load_2d(&tmA, &L.rawfull[rs], L.raw(rs, 0), xb, arow);
-                        if (DUAL) tma_load_2d(&tmA2, &L.rawfull[rs], L.raw(rs, 1), xb, arow + p.a2_row_offset);
+                        if (hint) {
+                            tma_load_2d_hint(&tmA, &L.rawfull[rs], L.raw(rs, 0), xb, arow, pol_w);
+                            if (DUAL)
+                                tma_load_2d_hint(&tmA2, &L.rawfull[rs], L.raw(rs, 1), xb, arow + p.a2_row_offset, pol_w);
+                        } else {
+                            tma_load_2d(&tmA, &L.rawfull[rs], L.raw(rs, 0), xb, arow);
+                            if (DUAL) tma_load_2d(&tmA2, &L.rawfull[rs], L.raw(rs, 1), xb, arow + p.a2_row_offset);
+                        }
                         mbar_arrive_expect_tx(&L.full[s], C::kBBytes);
                     } else {
                         mbar_arrive_expect_tx(&L.full[s], C::kNA * C::kABytes + C::kBBytes);
-                        tma_load_2d(&tmA, &L.full[s], L.a(s, 0), kt * BK, arow);
-                        if (DUAL) tma_load_2d(&tmA2, &L.full[s], L.a(s, 1), kt * BK, arow + p.a2_row_offset);
+                        if (hint) {
+                            tma_load_2d_hint(&tmA, &L.full[s], L.a(s, 0), kt * BK, arow, pol_w);
+                            if (DUAL)
+                                tma_load_2d_hint(&tmA2, &L.full[s], L.a(s, 1), kt * BK, arow + p.a2_row_offset, pol_w);
+                        } else {
+                            tma_load_2d(&tmA, &L.full[s], L.a(s, 0), kt * BK, arow);
+                            if (DUAL) tma_load_2d(&tmA2, &L.full[s], L.a(s, 1), kt * BK, arow + p.a2_row_offset);
+                        }
                     }
-                    tma_load_2d(&tmB, &L.full[s], L.b(s), kt * BK, ti.tok0);
+                    if (hint) tma_load_2d_hint(&tmB, &L.full[s], L.b(s), kt * BK, ti.tok0, pol_t);
+                    else tma_load_2d(&tmB, &L.full[s], L.b(s), kt * BK, ti.tok0);
                 }
             }
         }

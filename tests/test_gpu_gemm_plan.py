@@ -115,6 +115,54 @@ def test_q8_0_operand_is_ditchs_decode(device):
     W.close()
 
 
+def test_fp8_operand_is_ditchs_decode(device):
+    """Every E4M3 code (subnormals, both zeros, NaN) under block scales from
+    1e-30 to 300 (past 2^8 the decoders take their conversion path): the
+    staged operand equals ditch's bf16(f32(code) * scale) bit for bit (NaN as
+    NaN), and the GEMM decoding in the tile and the staged GEMM give the same
+    bits."""
+    import numpy as np
+
+    import oracle
+    from ditch_b200 import Tensor, Weight
+
+    rows, cols = 256, 512
+    codes = np.tile(np.arange(256, dtype=np.uint8), rows * cols // 256).reshape(rows, cols)
+    codes = np.ascontiguousarray(np.roll(codes, 37, axis=1))
+    scales = np.array([[1e-30, 0.5, 3e-4, 300.0], [2.0 ** -7, 1.0, 255.9, 7e-3]], np.float32)
+    W = Weight(device, Tensor("w", "fp8", rows, cols, codes, scales=scales, block_rows=128, block_cols=128))
+    got = torch.empty(rows, cols, device="cuda", dtype=torch.int16)
+    W.decode(got.data_ptr())
+    device.synchronize()
+    got = got.cpu().numpy().view(np.uint16)
+    want = oracle.dequant_fp8(codes, scales, 128, 128)
+    nan_g = ((got & 0x7F80) == 0x7F80) & ((got & 0x7F) != 0)
+    nan_w = ((want & 0x7F80) == 0x7F80) & ((want & 0x7F) != 0)
+    assert np.array_equal(nan_g, nan_w)
+    assert np.array_equal(got[~nan_g], want[~nan_w])
+    # the fused and staged GEMMs over the same operand (rows without NaN codes)
+    finite = codes.copy()
+    finite[(finite & 0x7F) == 0x7F] = 0x01
+    W2 = Weight(device, Tensor("w", "fp8", rows, cols, finite, scales=scales, block_rows=128, block_cols=128))
+    x = (torch.randn(600, cols, device="cuda") * 0.01).to(torch.bfloat16)
+    outs = []
+    device.set_deterministic(True)  # both plans split K the same way, summed in order
+    try:
+        for plan in (0, 1):
+            device.set_decode_staging(plan)
+            out = torch.empty(600, rows, device="cuda", dtype=torch.float32)
+            torch.cuda.synchronize()
+            W2.gemm(x.data_ptr(), 600, out.data_ptr())
+            device.synchronize()
+            outs.append(out)
+    finally:
+        device.set_decode_staging(1024)
+        device.set_deterministic(False)
+        W.close()
+        W2.close()
+    assert torch.equal(outs[0], outs[1])
+
+
 @pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4", "int4", "q8_0"])
 @pytest.mark.parametrize("m", [1, 5, 16])
 def test_weight_streaming_small_m(device, fmt, m):
