@@ -629,6 +629,20 @@ cudaError_t rank1_update_bf16(uint16_t *w, int rows, int cols, const float *b, c
     return cudaGetLastError();
 }
 
+__global__ void k_prenorm_vec(const float *v, const float *n, float lambda, int len, float *vn, float *b) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= len) return;
+    const float ni = n[i];
+    vn[i] = ni > 0.0f ? v[i] / ni : 0.0f;
+    b[i] = -lambda * v[i] * ni;
+}
+
+cudaError_t prenorm_vec(const float *v, const float *n, float lambda, int len, float *vn, float *b, cudaStream_t st) {
+    if (len <= 0) return cudaSuccess;
+    k_prenorm_vec<<<(len + 255) / 256, 256, 0, st>>>(v, n, lambda, len, vn, b);
+    return cudaGetLastError();
+}
+
 cudaError_t scale_vec(const float *v, float lambda, int n, float *b, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
     k_scale_vec<<<(n + 255) / 256, 256, 0, st>>>(v, lambda, n, b);

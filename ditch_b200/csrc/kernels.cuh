@@ -146,6 +146,9 @@ cudaError_t row_norms_mxfp4(const uint8_t *blocks, const uint8_t *scales, int ro
 // W <- W - alpha r (r^T W) with b = -alpha r, a = r^T W).
 cudaError_t rank1_update_bf16(uint16_t *w, int rows, int cols, const float *b, const float *a, cudaStream_t st);
 // b[i] = -lambda * v[i]
+// Pre-normalised edit (src/abliterate.zig:305-323): vn = v / n (0 where the
+// row norm n is 0) and b = -lambda v n.
+cudaError_t prenorm_vec(const float *v, const float *n, float lambda, int len, float *vn, float *b, cudaStream_t st);
 cudaError_t scale_vec(const float *v, float lambda, int n, float *b, cudaStream_t st);
 
 // ---- scoring ----------------------------------------------------------------

@@ -46,6 +46,8 @@ struct Layer {
     DevBuf e_proj;                                 // f32 [E][mi]: v^T W_down_e of the last scoring
     DevBuf e_a, e_b;                               // f32 [E][mi], [E][H]
     DevBuf e_edit_dev;                             // int [E]
+    // row norms ||W_i|| for the pre-normalised edit (computed once; the base weights never change)
+    DevBuf o_rn, down_rn, e_rn;                    // f32 [H], [H], [E][H]
 };
 
 struct Config {
@@ -119,6 +121,8 @@ struct ditch_cuda_model {
     // greedy generation: KV cache f32 [layers][slots][kv_len][kvd] for keys and for values
     ditch::DevBuf kv_k, kv_v, gen_next;
     int kv_slots = 0, kv_len = 0;
+    int row_norm = 0;    // edit row normalisation: 0 none, 1 pre (src/abliterate.zig:295-330)
+    ditch::DevBuf vn;    // f32 [H]: v / ||W_i|| of the pre-normalised edit
     ditch::Batch work;   // scratch batch for forward / residual passes
     ditch::DevBuf sums;  // f64 residual sums
     uint64_t bytes = 0;
@@ -139,6 +143,11 @@ int make_batch(ditch_cuda_model *m, Batch &b, const uint32_t *tokens, const size
 int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode = kFwdPrompts);
 
 int ensure_workspace(ditch_cuda_model *m, int n_tokens, int nc, int nl);
+
+// Rows [row0, row0 + rows) of a weight decoded to the bf16 operand the GEMM
+// sees (quantised formats), and their row norms ||W_i|| in f32.
+cudaError_t decode_rows_bf16(ditch_cuda_device *dev, const Mat &w, int row0, int rows, uint16_t *out);
+int mat_row_norms(ditch_cuda_device *dev, const Mat &w, int row0, int rows, float *out);
 
 // MoE MLP of layer `li`: post-norm of x, routing, experts, combine into x.
 int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n);

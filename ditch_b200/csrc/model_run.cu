@@ -165,6 +165,54 @@ int make_batch(ditch_cuda_model *m, Batch &b, const uint32_t *tokens, const size
     return DITCH_CUDA_OK;
 }
 
+cudaError_t decode_rows_bf16(ditch_cuda_device *dev, const Mat &w, int row0, int rows, uint16_t *out) {
+    StageArgs sa{};
+    sa.fmt = w.fmt;
+    sa.data = w.data.as<uint8_t>();
+    sa.row_bytes = w.row_bytes;
+    sa.row0 = row0;
+    sa.rows = rows;
+    sa.cols = w.cols;
+    sa.out = out;
+    if (w.fmt == kFmtFp8) {
+        sa.scales = w.scales.as<float>();
+        sa.blk_rows = w.br;
+        sa.blk_cols = w.bc;
+        sa.scale_cols = w.scols;
+    } else if (w.fmt == kFmtMxfp4) {
+        sa.scales_u8 = w.scales.as<uint8_t>();
+    } else if (w.fmt == kFmtQ8_0) {
+        sa.scales = w.scales.as<float>();
+        sa.scale_cols = w.scols;
+    } else {
+        sa.scales = w.scales.as<float>();
+        sa.zeros = w.zeros.as<uint32_t>();
+        sa.blk_cols = w.group;
+        sa.scale_cols = w.groups;
+    }
+    return launch_stage_decode(sa, dev->sms, dev->stream);
+}
+
+int mat_row_norms(ditch_cuda_device *dev, const Mat &w, int row0, int rows, float *out) {
+    if (w.fmt == kFmtBf16) {
+        DITCH_LAUNCH(dev, row_norms_bf16(w.data.as<uint16_t>() + (size_t)row0 * w.cols, rows, w.cols, out, dev->stream));
+        return DITCH_CUDA_OK;
+    }
+    if (w.fmt == kFmtMxfp4) {
+        DITCH_LAUNCH(dev, row_norms_mxfp4(w.data.as<uint8_t>() + (size_t)row0 * w.row_bytes,
+                                          w.scales.as<uint8_t>() + (size_t)row0 * (w.cols / 32), rows, w.cols, out,
+                                          dev->stream));
+        return DITCH_CUDA_OK;
+    }
+    // other formats: the bf16 operand the GEMM sees, then its norms
+    DevBuf tmp;
+    DITCH_CUDA(tmp.reserve((size_t)rows * w.cols * 2));
+    DITCH_LAUNCH(dev, decode_rows_bf16(dev, w, row0, rows, tmp.as<uint16_t>()));
+    DITCH_LAUNCH(dev, row_norms_bf16(tmp.as<uint16_t>(), rows, w.cols, out, dev->stream));
+    DITCH_CUDA(cudaStreamSynchronize(dev->stream));  // tmp is freed on return
+    return DITCH_CUDA_OK;
+}
+
 int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
                 void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
                 int a2_row_offset) {
@@ -186,31 +234,7 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     if (fmt != kFmtBf16 && !(ex && ex->sched) && dev->stage_min_tokens > 0 && n_tok >= dev->stage_min_tokens) {
         const int rows = (dual ? a2_row_offset : 0) + m_rows;
         DITCH_CUDA(dev->stage.reserve((size_t)rows * w.cols * 2));
-        StageArgs sa{};
-        sa.fmt = fmt;
-        sa.data = w.data.as<uint8_t>();
-        sa.row_bytes = w.row_bytes;
-        sa.row0 = slab_row0;
-        sa.rows = rows;
-        sa.cols = w.cols;
-        sa.out = dev->stage.as<uint16_t>();
-        if (fmt == kFmtFp8) {
-            sa.scales = w.scales.as<float>();
-            sa.blk_rows = w.br;
-            sa.blk_cols = w.bc;
-            sa.scale_cols = w.scols;
-        } else if (fmt == kFmtMxfp4) {
-            sa.scales_u8 = w.scales.as<uint8_t>();
-        } else if (fmt == kFmtQ8_0) {
-            sa.scales = w.scales.as<float>();
-            sa.scale_cols = w.scols;
-        } else {
-            sa.scales = w.scales.as<float>();
-            sa.zeros = w.zeros.as<uint32_t>();
-            sa.blk_cols = w.group;
-            sa.scale_cols = w.groups;
-        }
-        DITCH_LAUNCH(dev, launch_stage_decode(sa, dev->sms, dev->stream));
+        DITCH_LAUNCH(dev, decode_rows_bf16(dev, w, slab_row0, rows, dev->stage.as<uint16_t>()));
         A = GemmOperand{dev->stage.ptr, rows, w.cols, (long long)w.cols * 2};
         fmt = kFmtBf16;
         slab_row0 = 0;
@@ -472,18 +496,56 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
 
 namespace {
 
-int apply_component_edit(ditch_cuda_model *m, int li, bool is_o, const float *v, float lambda) {
+// The rank-1 delta (a, b) of one matrix whose rows are the H outputs:
+// none mode a = v^T W, b = -lambda v; pre mode a = (v / n)^T W, b = -lambda v n
+// with n the row norms (src/abliterate.zig:264-323).
+int rank1_delta(ditch_cuda_model *m, const Mat &w, int row0, DevBuf &rn_cache, size_t rn_off, const float *v,
+                float lambda, float *a, float *b) {
     ditch_cuda_device *dev = m->dev;
-    Layer &L = m->layers[li];
+    const int H = m->cfg.hidden;
+    if (m->row_norm == 0) {
+        int s;
+        if ((s = gemv_t_mat(m, w, row0, H, v, a))) return s;
+        DITCH_LAUNCH(dev, scale_vec(v, lambda, H, b, dev->stream));
+        return DITCH_CUDA_OK;
+    }
+    DITCH_CUDA(m->vn.reserve((size_t)H * 4));
+    DITCH_LAUNCH(dev, prenorm_vec(v, rn_cache.as<float>() + rn_off, lambda, H, m->vn.as<float>(), b, dev->stream));
+    return gemv_t_mat(m, w, row0, H, m->vn.as<float>(), a);
+}
+
+// Row norms of o_proj, down_proj and the routed experts' down projections of
+// layer li, computed on first use.
+int ensure_row_norms(ditch_cuda_model *m, Layer &L) {
+    ditch_cuda_device *dev = m->dev;
     const int H = m->cfg.hidden;
     int s;
+    if (!L.o_rn.ptr) {
+        DITCH_CUDA(L.o_rn.reserve((size_t)H * 4));
+        if ((s = mat_row_norms(dev, L.o, 0, H, L.o_rn.as<float>()))) return s;
+    }
+    if (!L.moe && !L.down_rn.ptr) {
+        DITCH_CUDA(L.down_rn.reserve((size_t)H * 4));
+        if ((s = mat_row_norms(dev, L.down, 0, H, L.down_rn.as<float>()))) return s;
+    }
+    if (L.moe && !L.e_rn.ptr) {
+        const int E = m->cfg.e_loc;
+        DITCH_CUDA(L.e_rn.reserve((size_t)E * H * 4));
+        if ((s = mat_row_norms(dev, L.e_down, 0, E * H, L.e_rn.as<float>()))) return s;
+    }
+    return DITCH_CUDA_OK;
+}
+
+int apply_component_edit(ditch_cuda_model *m, int li, bool is_o, const float *v, float lambda) {
+    Layer &L = m->layers[li];
+    int s;
+    if (m->row_norm && (s = ensure_row_norms(m, L))) return s;
     if (is_o) {
-        if ((s = gemv_t_mat(m, L.o, 0, H, v, L.o_a.as<float>()))) return s;
-        DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.o_b.as<float>(), dev->stream));
+        if ((s = rank1_delta(m, L.o, 0, L.o_rn, 0, v, lambda, L.o_a.as<float>(), L.o_b.as<float>()))) return s;
         L.o_edit = true;
     } else {
-        if ((s = gemv_t_mat(m, L.down, 0, H, v, L.down_a.as<float>()))) return s;
-        DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.down_b.as<float>(), dev->stream));
+        if ((s = rank1_delta(m, L.down, 0, L.down_rn, 0, v, lambda, L.down_a.as<float>(), L.down_b.as<float>())))
+            return s;
         L.down_edit = true;
     }
     return DITCH_CUDA_OK;
@@ -621,6 +683,15 @@ int expert_delta_from_proj(ditch_cuda_model *m, int li, int e, const float *v, f
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
     const int H = m->cfg.hidden, mi = L.e_down.cols;
+    if (m->row_norm) {  // pre-normalised: the projection of v / n_e, not of v
+        int s;
+        if ((s = ensure_row_norms(m, L))) return s;
+        if ((s = rank1_delta(m, L.e_down, e * H, L.e_rn, (size_t)e * H, v, lambda, L.e_a.as<float>() + (size_t)e * mi,
+                             L.e_b.as<float>() + (size_t)e * H)))
+            return s;
+        L.e_edit[e] = 1;
+        return DITCH_CUDA_OK;
+    }
     DITCH_CUDA(cudaMemcpyAsync(L.e_a.as<float>() + (size_t)e * mi, L.e_proj.as<float>() + (size_t)e * mi,
                                (size_t)mi * 4, cudaMemcpyDeviceToDevice, dev->stream));
     DITCH_LAUNCH(dev, scale_vec(v, lambda, H, L.e_b.as<float>() + (size_t)e * H, dev->stream));
@@ -657,7 +728,7 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
         }
         const int E = c.n_experts;
         if (!selective || n_experts == 0) {
-            if ((s = expert_projections(m, li, v))) return s;
+            if (!m->row_norm && (s = expert_projections(m, li, v))) return s;
             for (int e = 0; e < c.e_loc; e++)  // this rank's experts
                 if ((s = expert_delta_from_proj(m, li, e, v, lambda))) return s;
             continue;
@@ -933,6 +1004,24 @@ int ditch_cuda_kl_score_prompts(ditch_cuda_model *m, const uint32_t *tokens, con
     DITCH_CUDA(cudaMemcpyAsync(m->kl.tokens.ptr, tokens + prompt_offsets[0], n * 4, cudaMemcpyHostToDevice,
                                m->dev->stream));
     return kl_score_impl(m, kl);
+}
+
+int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode) {
+    clear_error();
+    REQUIRE(m, "null model");
+    REQUIRE(mode >= 0 && mode <= 2, "row normalisation %d is not none (0), pre (1) or full (2)", mode);
+    if (mode == 2) {
+        set_error("row_normalization = full (randomised SVD of the normalised edit) is not implemented on the device");
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    if (mode == 1 && m->cfg.tp_world > 1) {
+        // a rank holds column shards of o_proj / down_proj: its row norms are partial
+        set_error("row_normalization = pre under tensor parallelism is not supported");
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    std::lock_guard<std::mutex> lk(m->dev->mu);
+    m->row_norm = mode;
+    return DITCH_CUDA_OK;
 }
 
 int ditch_cuda_generate(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets, size_t n_prompts,

@@ -100,6 +100,7 @@ SIGNATURES = {
     "ditch_cuda_model_bytes": (C.c_uint64, [vp]),
     "ditch_cuda_forward": (C.c_int, [vp, u32p, u32p, u32p, sz, C.POINTER(sz), sz, f32p, C.POINTER(sz), sz, f32p]),
     "ditch_cuda_generate": (C.c_int, [vp, u32p, C.POINTER(sz), sz, sz, u32p, sz, u32p, C.POINTER(sz)]),
+    "ditch_cuda_set_row_normalization": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_residual_sums": (C.c_int, [vp, u32p, C.POINTER(sz), sz, sz, sz, f64p, u64p]),
     "ditch_cuda_directions": (C.c_int, [vp, f64p, C.c_uint64, f64p, C.c_uint64, C.c_int, f32p]),
     "ditch_cuda_set_directions": (C.c_int, [vp, f32p, sz]),
@@ -526,6 +527,12 @@ class Model:
         offs = np.zeros(len(prompts) + 1, np.uintp)
         offs[1:] = np.cumsum([len(p) for p in prompts])
         return tokens, offs
+
+    def set_row_normalization(self, mode):
+        """Options.row_normalization of the following edits: "none" or "pre"
+        ("full" raises Unsupported)."""
+        code = {"none": 0, "pre": 1, "full": 2}[mode]
+        check(lib().ditch_cuda_set_row_normalization(self.h, code))
 
     def generate(self, prompts, max_new_tokens, eos_ids=()):
         """Greedy generation (model.generate, src/model.zig:5359-5444): a list

@@ -275,6 +275,19 @@ def compute_delta_none(w, v, lam):
     return a, b
 
 
+def compute_delta_pre(w, v, lam):
+    """computeOutputDelta with row_normalization = pre, K = 1
+    (src/abliterate.zig:305-323): n = rowNorms(W), vn = v / n (0 where n is
+    0), a = vn^T W, b = -lam v n, in ditch's f32 order."""
+    w, v = f32(w), f32(v)
+    n = row_norms(w)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        vn = np.where(n > 0, v / n, np.float32(0)).astype(np.float32)
+    a = matvec_t_multi(w, vn[None, :])[0].astype(np.float32)
+    b = ((np.float32(-lam) * v) * n).astype(np.float32)
+    return a, b
+
+
 def materialize(w, a, b):
     w = f32(w)
     a, b = f32(a).reshape(-1, w.shape[1]), f32(b).reshape(w.shape[0], -1)

@@ -244,3 +244,62 @@ def test_residual_sums_and_directions(device):
         cos = np.sum(dirs * odirs, axis=1)
         assert cos.min() > 0.99, cos
     m.close()
+
+
+@pytest.mark.parametrize("family", ["qwen2", "qwen2_fp8", "qwen2_int4", "qwen3_moe"])
+def test_pre_normalised_edit(device, family):
+    """row_normalization = pre (src/abliterate.zig:295-323): the device's
+    edited KL against the oracle with a = (v / n)^T W, b = -lambda v n (n the
+    row norms of the decoded weights), for o_proj, down_proj and (MoE) every
+    expert's down projection; then the selective expert edit in the same
+    mode. "full" is refused as unsupported."""
+    g, m = load(device, family)
+    s = g.spec
+    w = g.f32_weights()
+    rng = np.random.default_rng(11)
+    dirs = rng.standard_normal((s["n_layers"] + 1, s["hidden"])).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    m.set_directions(dirs)
+    prompts = g.prompts()
+    toks, rb, rp, cap, first, take, last = flatten_batch(prompts)
+    m.kl_init(prompts)
+    po, pd = (1.1, 0.0, 0.5, 3.0), (0.9, 1.0, 0.3, 2.0)
+    moe = s.get("moe_layers") or [False] * s["n_layers"]
+
+    def oracle_kl(expert_weights):
+        om = OracleModel(s, w)
+        for li in range(s["n_layers"]):
+            v = dirs[li + 1]
+            lam = oracle.kernel_weight(po, li)
+            if lam is not None:
+                om.set_delta(li, "o", *oracle.compute_delta_pre(w[f"L{li}.o"], v, lam))
+            lam = oracle.kernel_weight(pd, li)
+            if lam is None:
+                continue
+            if not moe[li]:
+                om.set_delta(li, "down", *oracle.compute_delta_pre(w[f"L{li}.down"], v, lam))
+                continue
+            for e, weight in expert_weights(li, v, lam):
+                om.set_delta(li, ("e", e), *oracle.compute_delta_pre(w[f"L{li}.e_down"][e], v, weight))
+        _, base = OracleModel(s, w).forward(toks, rb, rp, (), last)
+        _, ed = om.forward(toks, rb, rp, (), last)
+        return oracle.kl_first_token(oracle.log_softmax(base), ed)[0]
+
+    with pytest.raises(ditch_b200.Unsupported):
+        m.set_row_normalization("full")
+    m.set_row_normalization("pre")
+    m.apply_edit(po, pd)
+    got = m.kl_score()
+    want = oracle_kl(lambda li, v, lam: [(e, lam) for e in range(s["n_experts"])])
+    assert got > 0 and abs(got - want) <= 2e-3 + 0.05 * abs(want), (got, want)
+    if s.get("moe_layers"):
+        m.apply_expert_edit(po, pd, n_experts=2, strength=0.7)
+
+        def top2(li, v, lam):
+            sc = np.array([oracle.score_down(w[f"L{li}.e_down"][e], v) for e in range(s["n_experts"])], np.float32)
+            return [(int(e), lam * 0.7) for e in oracle.rank_scores(sc)[:2]]
+
+        got, want = m.kl_score(), oracle_kl(top2)
+        assert abs(got - want) <= 2e-3 + 0.05 * abs(want), (got, want)
+    m.set_row_normalization("none")
+    m.close()

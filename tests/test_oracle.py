@@ -60,6 +60,25 @@ def test_generation_stop_rules():
         assert [len(t) for t in one] == [1] * len(free)
 
 
+def test_pre_normalised_edit_removes_direction():
+    """src/abliterate.zig:554-592, row_normalization = pre, K = 1: the
+    direction vanishes from the row-normalised edited matrix,
+    sum_i (v_i / n_i) W'_ij ~ 0, and the delta stays rank 1."""
+    rng = np.random.default_rng(7)
+    w = rng.standard_normal((6, 5)).astype(np.float32)
+    v = rng.standard_normal(6).astype(np.float32)
+    v /= np.linalg.norm(v)
+    a, b = oracle.compute_delta_pre(w, v, 1.0)
+    assert a.shape == (5,) and b.shape == (6,)
+    wp = oracle.materialize(w, a, b)
+    n = oracle.row_norms(w)
+    assert np.abs((v / n) @ wp).max() < 1e-4
+    # a zero row keeps its zero norm out of the division (vn = 0 there)
+    w[2] = 0.0
+    a, b = oracle.compute_delta_pre(w, v, 0.5)
+    assert np.isfinite(a).all() and b[2] == 0.0
+
+
 def test_argmax_first_rule():
     """src/model.zig:5194-5204: the first maximum wins, NaN never does, a row
     with nothing above -inf gives 0."""
