@@ -493,7 +493,7 @@ cudaError_t launch_attention_tiled(const AttnParams &p, cudaStream_t st) {
 }
 
 // xa[m] = sum_k act[m][k] * a[k], one warp per row.
-__global__ void k_rowdot_bf16(const uint16_t *act, const float *a, int m, int k, float *xa) {
+__global__ void k_rowdot_bf16(const uint16_t *act, const float *a, int m, int k, float *xa, int stride) {
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= m) return;
@@ -534,7 +534,7 @@ __global__ void k_rowdot_bf16(const uint16_t *act, const float *a, int m, int k,
         for (int i = lane; i < k; i += 32) s = fmaf(bf16_bits_to_f32(r[i]), a[i], s);
     }
     s = warp_sum(s);
-    if (lane == 0) xa[row] = s;
+    if (lane == 0) xa[(long long)row * stride] = s;
 }
 
 }  // namespace
@@ -591,7 +591,14 @@ cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st) {
 
 cudaError_t rowdot_bf16(const uint16_t *act, const float *a, int m, int k, float *xa, cudaStream_t st) {
     if (m <= 0) return cudaSuccess;
-    k_rowdot_bf16<<<(m + 7) / 8, 256, 0, st>>>(act, a, m, k, xa);
+    k_rowdot_bf16<<<(m + 7) / 8, 256, 0, st>>>(act, a, m, k, xa, 1);
+    return cudaGetLastError();
+}
+
+cudaError_t rowdot_bf16_strided(const uint16_t *act, const float *a, int m, int k, float *xa, int stride,
+                                cudaStream_t st) {
+    if (m <= 0) return cudaSuccess;
+    k_rowdot_bf16<<<(m + 7) / 8, 256, 0, st>>>(act, a, m, k, xa, stride);
     return cudaGetLastError();
 }
 

@@ -608,7 +608,10 @@ __global__ void __launch_bounds__(256) k_skinny(const uint8_t *wdata, long long 
     }
     if (m >= M || n >= p.m_w) return;
     if (blockIdx.y == 0 || p.sk_ws) {  // bias and delta once per output
-        if (p.xa && p.db) r += p.xa[m] * p.db[n];
+        if (p.xa && p.db) {
+            const int drank = p.delta_rank > 1 ? p.delta_rank : 1;
+            for (int t = 0; t < drank; t++) r += p.xa[m * drank + t] * p.db[(long long)n * drank + t];
+        }
         if (p.bias) r += p.bias[n];
     }
     float *o = reinterpret_cast<float *>(p.out) + (long long)m * p.ldo + n;
@@ -769,7 +772,14 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                 delta = p.e_flags == nullptr || p.e_flags[ti.e] != 0;
                 dbp = p.db + ti.e * p.db_stride;
             }
-            const float dbn = delta ? dbp[n] : 0.0f;
+            const int drank = p.delta_rank > 1 ? p.delta_rank : 1;
+            float dbn[kMaxDeltaRank];
+            bool any_delta = false;
+#pragma unroll
+            for (int t = 0; t < kMaxDeltaRank; t++) {
+                dbn[t] = (delta && t < drank) ? dbp[(long long)n * drank + t] : 0.0f;
+                any_delta |= dbn[t] != 0.0f;
+            }
             const uint32_t tbase = tmem + buf * C::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
             const int m_end = ti.tok0 + ti.tok_cnt;
             // stream-K: a part of a split tile goes to this CTA's slot; the CTA
@@ -867,15 +877,17 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                 // as the compiler knows the stores may alias the loads, and
                 // interleaving them serialises one memory round trip per token.
                 float r[EC];
-                if (p.xa && dbn != 0.0f) {
-                    float xa[EC];
 #pragma unroll
-                    for (int j = 0; j < EC; j++) xa[j] = j < mv ? __ldg(p.xa + m0 + j) : 0.0f;
+                for (int j = 0; j < EC; j++) r[j] = v[j];
+                if (p.xa && any_delta) {
+#pragma unroll 1
+                    for (int t = 0; t < drank; t++) {  // r += (x . a_t) b_t, term by term
+                        float xa[EC];
 #pragma unroll
-                    for (int j = 0; j < EC; j++) r[j] = v[j] + xa[j] * dbn;
-                } else {
+                        for (int j = 0; j < EC; j++) xa[j] = j < mv ? __ldg(p.xa + (long long)(m0 + j) * drank + t) : 0.0f;
 #pragma unroll
-                    for (int j = 0; j < EC; j++) r[j] = v[j];
+                        for (int j = 0; j < EC; j++) r[j] += xa[j] * dbn[t];
+                    }
                 }
 #pragma unroll
                 for (int j = 0; j < EC; j++) r[j] += bias;

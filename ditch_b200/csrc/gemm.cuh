@@ -53,8 +53,9 @@ struct GemmParams {
     long long ldo;      // row stride of out, in elements
     int flags;
     const float *bias;  // [m_w] or null
-    const float *xa;    // [n_tok]: x . a of a rank-1 delta, or null
-    const float *db;    // [m_w]:  B of the delta (-lambda v)
+    const float *xa;    // [n_tok][delta_rank]: x . a_t of the delta's rank terms, or null
+    const float *db;    // [m_w][delta_rank]: B of the delta (-lambda v for rank 1)
+    int delta_rank;     // terms of the delta (0 or 1: rank 1; at most kMaxDeltaRank)
     // quantised weights: per-format side data
     const float *scales;     // fp8 block scales [rows/br][scols]; int4 [rows][groups]
     const uint8_t *scales_u8;  // mxfp4 E8M0 scales [rows][k/32]
@@ -90,6 +91,8 @@ size_t gemm_stream_k_bytes(int grid, int bn, bool dual);
 // Whether a dense GEMM of `tiles` whole output tiles runs stream-K on `sms`
 // SMs (when the whole tiles would leave over half of them idle).
 bool gemm_wants_stream_k(long long tiles, int k_tiles, int sms);
+
+constexpr int kMaxDeltaRank = 4;
 
 // Token tile width the GEMM uses for n_tok tokens (dual = SwiGLU mode,
 // quant = a weight format decoded inside the GEMM).

@@ -120,6 +120,9 @@ cudaError_t argmax_rows(const float *x, int n, int len, uint32_t *out, cudaStrea
 // xa[m] = sum_k act[m][k] * a[k] (act bf16, a f32): the x . A term of a rank-1
 // delta (src/tensor.zig:1036-1042).
 cudaError_t rowdot_bf16(const uint16_t *act, const float *a, int m, int k, float *xa, cudaStream_t st);
+// The same into xa[row * stride] (one term of a rank-r delta).
+cudaError_t rowdot_bf16_strided(const uint16_t *act, const float *a, int m, int k, float *xa, int stride,
+                                cudaStream_t st);
 
 // ---- edit (src/abliterate.zig:264-280) and ranking (src/moe.zig:1239-1306) --
 // out[c] = sum_r v[r] W[r][c] over a weight in its stored format (bf16 or

@@ -40,7 +40,8 @@ struct Layer {
     Mat e_down;                                    // [E][H][mi]
     // none-mode deltas (src/abliterate.zig:270-280): out += (x . a) b
     bool o_edit = false, down_edit = false;
-    DevBuf o_a, o_b, down_a, down_b;               // f32 [qd], [H], [I], [H]
+    int o_rank = 1, down_rank = 1;                 // terms of the delta (full row normalisation: up to kMaxDeltaRank)
+    DevBuf o_a, o_b, down_a, down_b;               // f32 [rank][qd], [H][rank], [rank][I], [H][rank]
     std::vector<uint8_t> e_edit;                   // per expert
     std::vector<float> e_fro;                      // ||W_down_e||_F per expert (computed once)
     DevBuf e_proj;                                 // f32 [E][mi]: v^T W_down_e of the last scoring
@@ -121,7 +122,9 @@ struct ditch_cuda_model {
     // greedy generation: KV cache f32 [layers][slots][kv_len][kvd] for keys and for values
     ditch::DevBuf kv_k, kv_v, gen_next;
     int kv_slots = 0, kv_len = 0;
-    int row_norm = 0;    // edit row normalisation: 0 none, 1 pre (src/abliterate.zig:295-330)
+    int row_norm = 0;    // edit row normalisation: 0 none, 1 pre, 2 full (src/abliterate.zig:283-350)
+    int lora_rank = 3;   // full: rank of the delta (Options.lora_rank)
+    uint64_t edit_seed = 0, seed_counter = 0;  // full: the sketch seed of each matrix is seed + its index
     ditch::DevBuf vn;    // f32 [H]: v / ||W_i|| of the pre-normalised edit
     ditch::Batch work;   // scratch batch for forward / residual passes
     ditch::DevBuf sums;  // f64 residual sums
@@ -143,6 +146,16 @@ int make_batch(ditch_cuda_model *m, Batch &b, const uint32_t *tokens, const size
 int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode = kFwdPrompts);
 
 int ensure_workspace(ditch_cuda_model *m, int n_tokens, int nc, int nl);
+
+// out[cols] = v^T W over rows [row0, row0 + rows) of a resident weight in its
+// stored format (v device f32 [rows]); out is overwritten.
+int gemv_t_mat(ditch_cuda_model *m, const Mat &w, int row0, int rows, const float *v, float *out);
+
+// row_normalization = full (src/abliterate.zig:324-350): the rank-`*rank_out`
+// delta (a_out [rank][cols], b_out [rows][rank], device) of the H-row weight
+// at row0 for direction v (device f32 [H]) with row norms rn (device).
+int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn, const float *v_dev, float lambda,
+                    int lora_rank, uint64_t seed, float *a_out, float *b_out, int *rank_out);
 
 // Rows [row0, row0 + rows) of a weight decoded to the bf16 operand the GEMM
 // sees (quantised formats), and their row norms ||W_i|| in f32.
@@ -169,7 +182,7 @@ int build_router_split(ditch_cuda_device *dev, const float *router_f32, int E, i
 // GEMM with a resident weight as the A operand.
 int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
                 void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
-                int a2_row_offset);
+                int a2_row_offset, int delta_rank = 1);
 
 // Options beyond the dense single-matrix product: split-K, or the grouped
 // (per-expert) tile schedule of the routed-expert path.
@@ -185,7 +198,7 @@ struct GemmExtra {
 
 int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
              void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
-             int a2_row_offset, const GemmExtra *ex);
+             int a2_row_offset, const GemmExtra *ex, int delta_rank = 1);
 
 // Builds a GEMM operand from one tensor of the C ABI (quantised formats the
 // GEMM decodes stay quantised; others are decoded to bf16 once).

@@ -584,11 +584,11 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
                     "layer %d: MLP shapes", i);
             if ((st = build_mat(m.get(), {Seg{g, 0}, Seg{u, 0}}, 1, L.gate_up, "gate_up"))) return st;
             if ((st = build_mat(m.get(), {Seg{d, 0}}, 1, L.down, "down"))) return st;
-            DITCH_CUDA(L.down_a.reserve((size_t)L.down.cols * 4));
-            DITCH_CUDA(L.down_b.reserve((size_t)H * 4));
+            DITCH_CUDA(L.down_a.reserve((size_t)L.down.cols * 4 * kMaxDeltaRank));
+            DITCH_CUDA(L.down_b.reserve((size_t)H * 4 * kMaxDeltaRank));
         }
-        DITCH_CUDA(L.o_a.reserve((size_t)qd * 4));
-        DITCH_CUDA(L.o_b.reserve((size_t)H * 4));
+        DITCH_CUDA(L.o_a.reserve((size_t)qd * 4 * kMaxDeltaRank));
+        DITCH_CUDA(L.o_b.reserve((size_t)H * 4 * kMaxDeltaRank));
     }
     if ((st = build_rope(m.get()))) return st;
     DITCH_CUDA(m->dirs.reserve((size_t)(c.n_layers + 1) * H * 4));

@@ -47,6 +47,27 @@ bool kernel_weight(const ditch_cuda_params &p, size_t layer, float *out) {
 }
 
 // GEMV-T over one slab of a resident weight: out[cols] = v^T W (out zeroed here).
+
+// interpolateBasis with k = 1 (src/abliterate.zig:119-131, orthonormalize 409-423).
+std::vector<float> interpolate(const std::vector<float> &dirs, int entries, int hidden, float di) {
+    const float shifted = di + 1.0f;
+    const int idx = (int)std::floor(shifted);
+    const float frac = shifted - std::floor(shifted);
+    const float *a = dirs.data() + (size_t)std::min(idx, entries - 1) * hidden;
+    const float *b = dirs.data() + (size_t)std::min(idx + 1, entries - 1) * hidden;
+    std::vector<float> out(hidden);
+    for (int i = 0; i < hidden; i++) out[i] = a[i] + frac * (b[i] - a[i]);
+    double s = 0;
+    for (float x : out) s += (double)x * x;
+    const float nrm = (float)std::sqrt(s);
+    for (float &x : out) x = nrm > 1e-20f ? x * (1.0f / nrm) : 0.0f;
+    return out;
+}
+
+}  // namespace
+
+namespace ditch {
+
 int gemv_t_mat(ditch_cuda_model *m, const Mat &w, int row0, int rows, const float *v, float *out) {
     ditch_cuda_device *dev = m->dev;
     DITCH_CUDA(cudaMemsetAsync(out, 0, (size_t)w.cols * 4, dev->stream));
@@ -92,26 +113,6 @@ int gemv_t_mat(ditch_cuda_model *m, const Mat &w, int row0, int rows, const floa
     return DITCH_CUDA_OK;
 }
 
-// interpolateBasis with k = 1 (src/abliterate.zig:119-131, orthonormalize 409-423).
-std::vector<float> interpolate(const std::vector<float> &dirs, int entries, int hidden, float di) {
-    const float shifted = di + 1.0f;
-    const int idx = (int)std::floor(shifted);
-    const float frac = shifted - std::floor(shifted);
-    const float *a = dirs.data() + (size_t)std::min(idx, entries - 1) * hidden;
-    const float *b = dirs.data() + (size_t)std::min(idx + 1, entries - 1) * hidden;
-    std::vector<float> out(hidden);
-    for (int i = 0; i < hidden; i++) out[i] = a[i] + frac * (b[i] - a[i]);
-    double s = 0;
-    for (float x : out) s += (double)x * x;
-    const float nrm = (float)std::sqrt(s);
-    for (float &x : out) x = nrm > 1e-20f ? x * (1.0f / nrm) : 0.0f;
-    return out;
-}
-
-}  // namespace
-
-namespace ditch {
-
 int ensure_workspace(ditch_cuda_model *m, int n, int nc, int nl) {
     const Config &c = m->cfg;
     const size_t N = (size_t)std::max(n, 1), H = c.hidden;
@@ -121,7 +122,7 @@ int ensure_workspace(ditch_cuda_model *m, int n, int nc, int nl) {
     DITCH_CUDA(m->qkv.reserve(N * c.qkv_width() * 4));
     DITCH_CUDA(m->att.reserve(N * c.qd() * 2));
     DITCH_CUDA(m->act.reserve(N * inter * 2));
-    DITCH_CUDA(m->xa.reserve(N * 4));
+    DITCH_CUDA(m->xa.reserve(N * 4 * kMaxDeltaRank));
     if (nc > 0) DITCH_CUDA(m->res.reserve((size_t)(c.n_layers + 1) * nc * H * 4));
     if (nl > 0) {
         DITCH_CUDA(m->hl.reserve((size_t)nl * H * 2));
@@ -215,14 +216,19 @@ int mat_row_norms(ditch_cuda_device *dev, const Mat &w, int row0, int rows, floa
 
 int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
                 void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
-                int a2_row_offset) {
-    return gemm_mat(m->dev, w, slab_row0, m_rows, act, n_tok, out, ldo, flags, bias, xa, db, a2_row_offset, nullptr);
+                int a2_row_offset, int delta_rank) {
+    return gemm_mat(m->dev, w, slab_row0, m_rows, act, n_tok, out, ldo, flags, bias, xa, db, a2_row_offset, nullptr,
+                    delta_rank);
 }
 
 int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
              void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
-             int a2_row_offset, const GemmExtra *ex) {
+             int a2_row_offset, const GemmExtra *ex, int delta_rank) {
     if (n_tok <= 0 || m_rows <= 0) return DITCH_CUDA_OK;
+    if (delta_rank < 1 || delta_rank > kMaxDeltaRank) {
+        set_error("delta rank %d is not within 1..%d", delta_rank, kMaxDeltaRank);
+        return DITCH_CUDA_INVALID;
+    }
     GemmOperand A{w.data.ptr, w.rows * w.slabs, w.cols, w.row_bytes};
     GemmOperand B{act, n_tok, w.cols, (long long)w.cols * 2};
     int fmt = w.fmt;
@@ -283,6 +289,7 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         p.bias = bias;
         p.xa = xa;
         p.db = db;
+        p.delta_rank = delta_rank;
         if (fmt == kFmtFp8) {
             p.scales = w.scales.as<float>();
             p.blk_rows = w.br;
@@ -344,6 +351,7 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     p.bias = bias;
     p.xa = xa;
     p.db = db;
+    p.delta_rank = delta_rank;
     if (fmt == kFmtFp8) {
         p.scales = w.scales.as<float>();
         p.blk_rows = w.br;
@@ -454,11 +462,15 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
                 DITCH_LAUNCH(dev, kv_store(kp, st));
             }
         }
-        if (L.o_edit) DITCH_LAUNCH(dev, rowdot_bf16(m->att.as<uint16_t>(), L.o_a.as<float>(), n, qd, m->xa.as<float>(), st));
+        if (L.o_edit)
+            for (int t = 0; t < L.o_rank; t++)
+                DITCH_LAUNCH(dev, rowdot_bf16_strided(m->att.as<uint16_t>(), L.o_a.as<float>() + (size_t)t * qd, n, qd,
+                                                      m->xa.as<float>() + t, L.o_rank, st));
         // tensor parallel: the partial sum goes to the group's send rows, then the all-reduce adds it to x
         const bool tp = m->group && c.tp_world > 1;
         if ((s = gemm_weight(m, L.o, 0, H, m->att.as<uint16_t>(), n, tp ? tp_send_rows(m) : x, H, tp ? 0 : kEpiResidual,
-                             nullptr, L.o_edit ? m->xa.as<float>() : nullptr, L.o_edit ? L.o_b.as<float>() : nullptr, 0)))
+                             nullptr, L.o_edit ? m->xa.as<float>() : nullptr, L.o_edit ? L.o_b.as<float>() : nullptr, 0,
+                             L.o_edit ? L.o_rank : 1)))
             return s;
         if (tp && (s = tp_allreduce_add(m, n, x))) return s;
         if (L.moe) {
@@ -470,10 +482,12 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
             if ((s = gemm_weight(m, L.gate_up, 0, I, h, n, m->act.ptr, Ip, kEpiSwiglu, nullptr, nullptr, nullptr, I)))
                 return s;
             if (L.down_edit)
-                DITCH_LAUNCH(dev, rowdot_bf16(m->act.as<uint16_t>(), L.down_a.as<float>(), n, Ip, m->xa.as<float>(), st));
+                for (int t = 0; t < L.down_rank; t++)
+                    DITCH_LAUNCH(dev, rowdot_bf16_strided(m->act.as<uint16_t>(), L.down_a.as<float>() + (size_t)t * Ip, n,
+                                                          Ip, m->xa.as<float>() + t, L.down_rank, st));
             if ((s = gemm_weight(m, L.down, 0, H, m->act.as<uint16_t>(), n, tp ? tp_send_rows(m) : x, H,
                                  tp ? 0 : kEpiResidual, nullptr, L.down_edit ? m->xa.as<float>() : nullptr,
-                                 L.down_edit ? L.down_b.as<float>() : nullptr, 0)))
+                                 L.down_edit ? L.down_b.as<float>() : nullptr, 0, L.down_edit ? L.down_rank : 1)))
                 return s;
             if (tp && (s = tp_allreduce_add(m, n, x))) return s;
         }
@@ -540,6 +554,22 @@ int apply_component_edit(ditch_cuda_model *m, int li, bool is_o, const float *v,
     Layer &L = m->layers[li];
     int s;
     if (m->row_norm && (s = ensure_row_norms(m, L))) return s;
+    if (m->row_norm == 2) {  // full: a rank-r delta from a randomised SVD
+        const Mat &w = is_o ? L.o : L.down;
+        int rank = 1;
+        if ((s = full_norm_delta(m, w, 0, (is_o ? L.o_rn : L.down_rn).as<float>(), v, lambda, m->lora_rank,
+                                 m->edit_seed + m->seed_counter++, (is_o ? L.o_a : L.down_a).as<float>(),
+                                 (is_o ? L.o_b : L.down_b).as<float>(), &rank)))
+            return s;
+        if (is_o) {
+            L.o_rank = rank;
+            L.o_edit = true;
+        } else {
+            L.down_rank = rank;
+            L.down_edit = true;
+        }
+        return DITCH_CUDA_OK;
+    }
     if (is_o) {
         if ((s = rank1_delta(m, L.o, 0, L.o_rn, 0, v, lambda, L.o_a.as<float>(), L.o_b.as<float>()))) return s;
         L.o_edit = true;
@@ -564,6 +594,7 @@ int upload_expert_flags(ditch_cuda_model *m) {
 void clear_edits(ditch_cuda_model *m) {
     for (Layer &L : m->layers) {
         L.o_edit = L.down_edit = false;
+        L.o_rank = L.down_rank = 1;
         std::fill(L.e_edit.begin(), L.e_edit.end(), 0);
     }
 }
@@ -713,6 +744,7 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
                 int use_di, bool selective, size_t n_experts, float strength) {
     const Config &c = m->cfg;
     clear_edits(m);
+    m->seed_counter = 0;
     int s;
     if ((s = prepare_direction(m, di, use_di != 0))) return s;
     for (int li = 0; li < c.n_layers; li++) {
@@ -1006,21 +1038,30 @@ int ditch_cuda_kl_score_prompts(ditch_cuda_model *m, const uint32_t *tokens, con
     return kl_score_impl(m, kl);
 }
 
-int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode) {
+int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_rank, uint64_t seed) {
     clear_error();
     REQUIRE(m, "null model");
     REQUIRE(mode >= 0 && mode <= 2, "row normalisation %d is not none (0), pre (1) or full (2)", mode);
-    if (mode == 2) {
-        set_error("row_normalization = full (randomised SVD of the normalised edit) is not implemented on the device");
+    if (mode != 0 && m->cfg.tp_world > 1) {
+        // a rank holds column shards of o_proj / down_proj: its row norms are partial
+        set_error("row normalisation under tensor parallelism is not supported");
         return DITCH_CUDA_UNSUPPORTED;
     }
-    if (mode == 1 && m->cfg.tp_world > 1) {
-        // a rank holds column shards of o_proj / down_proj: its row norms are partial
-        set_error("row_normalization = pre under tensor parallelism is not supported");
-        return DITCH_CUDA_UNSUPPORTED;
+    if (mode == 2) {
+        REQUIRE(lora_rank >= 1 && lora_rank <= (size_t)kMaxDeltaRank, "lora_rank %zu is not within 1..%d", lora_rank,
+                kMaxDeltaRank);
+        for (const Layer &L : m->layers)
+            if (L.moe) {
+                set_error("row_normalization = full on routed experts is not implemented on the device");
+                return DITCH_CUDA_UNSUPPORTED;
+            }
     }
     std::lock_guard<std::mutex> lk(m->dev->mu);
     m->row_norm = mode;
+    if (mode == 2) {
+        m->lora_rank = (int)lora_rank;
+        m->edit_seed = seed;
+    }
     return DITCH_CUDA_OK;
 }
 

@@ -12,6 +12,7 @@ and a status other than OK raises. `Unsupported` is the seam's
 """
 import ctypes as C
 import os
+import weakref
 
 import numpy as np
 
@@ -100,7 +101,7 @@ SIGNATURES = {
     "ditch_cuda_model_bytes": (C.c_uint64, [vp]),
     "ditch_cuda_forward": (C.c_int, [vp, u32p, u32p, u32p, sz, C.POINTER(sz), sz, f32p, C.POINTER(sz), sz, f32p]),
     "ditch_cuda_generate": (C.c_int, [vp, u32p, C.POINTER(sz), sz, sz, u32p, sz, u32p, C.POINTER(sz)]),
-    "ditch_cuda_set_row_normalization": (C.c_int, [vp, C.c_int]),
+    "ditch_cuda_set_row_normalization": (C.c_int, [vp, C.c_int, sz, C.c_uint64]),
     "ditch_cuda_residual_sums": (C.c_int, [vp, u32p, C.POINTER(sz), sz, sz, sz, f64p, u64p]),
     "ditch_cuda_directions": (C.c_int, [vp, f64p, C.c_uint64, f64p, C.c_uint64, C.c_int, f32p]),
     "ditch_cuda_set_directions": (C.c_int, [vp, f32p, sz]),
@@ -185,9 +186,17 @@ class Device:
         check(lib().ditch_cuda_open(ordinal, memory_budget, C.byref(h)))
         self.h = h
         self.ordinal = ordinal
+        self._children = weakref.WeakSet()  # models, weights and groups living on this device
+
+    def _adopt(self, child):
+        self._children.add(child)
 
     def close(self):
+        """Closes the models, weights and groups still open on this device
+        (their handles point into it), then the device."""
         if self.h:
+            for child in list(self._children):
+                child.close()
             lib().ditch_cuda_close(self.h)
             self.h = None
 
@@ -402,6 +411,7 @@ class Weight:
         check(lib().ditch_cuda_weight_load(device.h, C.byref(d), C.byref(h)))
         self.h = h
         self.rows, self.cols = tensor.rows, tensor.cols
+        device._adopt(self)
 
     def format(self):
         return self.FORMATS.get(lib().ditch_cuda_weight_format(self.h), "?")
@@ -441,6 +451,7 @@ class Group:
         handles = exchange(bytes(buf))
         allh = (C.c_uint8 * (n * world)).from_buffer_copy(b"".join(handles))
         check(lib().ditch_cuda_group_open(self.h, C.cast(allh, vp)))
+        device._adopt(self)
 
     def barrier(self):
         check(lib().ditch_cuda_group_barrier(self.h))
@@ -481,6 +492,7 @@ class Model:
         h = vp()
         check(lib().ditch_cuda_model_load(device.h, C.byref(cfg), descs, len(tensors), C.byref(h)))
         self.h = h
+        device._adopt(self)
 
     def close(self):
         if self.h:
@@ -528,11 +540,12 @@ class Model:
         offs[1:] = np.cumsum([len(p) for p in prompts])
         return tokens, offs
 
-    def set_row_normalization(self, mode):
-        """Options.row_normalization of the following edits: "none" or "pre"
-        ("full" raises Unsupported)."""
+    def set_row_normalization(self, mode, lora_rank=3, seed=0):
+        """Options.row_normalization of the following edits: "none", "pre" or
+        "full" (a rank-`lora_rank` delta from a randomised SVD seeded with
+        `seed` + the matrix's index)."""
         code = {"none": 0, "pre": 1, "full": 2}[mode]
-        check(lib().ditch_cuda_set_row_normalization(self.h, code))
+        check(lib().ditch_cuda_set_row_normalization(self.h, code, int(lora_rank), int(seed)))
 
     def generate(self, prompts, max_new_tokens, eos_ids=()):
         """Greedy generation (model.generate, src/model.zig:5359-5444): a list

@@ -247,12 +247,16 @@ typedef struct {
 int ditch_cuda_apply_edit(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down,
                           float direction_index, int use_direction_index);
 /* Options.row_normalization for the edits that follow (src/abliterate.zig:
- * 283-330): 0 none (the default), 1 pre, where a = (v / n)^T W and
+ * 283-350): 0 none (the default); 1 pre, where a = (v / n)^T W and
  * b = -lambda v n with n the row norms ||W_i|| of the decoded weight (the
- * delta stays rank 1). 2 (full: a randomised SVD of the row-renormalised
- * edit) returns DITCH_CUDA_UNSUPPORTED, and so does pre on a tensor-parallel
- * rank (column shards hold partial row norms). */
-int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode);
+ * delta stays rank 1); 2 full, W' = diag(n) rownorm(Wn + B A^T), applied as a
+ * rank-lora_rank delta (1..4, Options.lora_rank, default 3 in ditch) from a
+ * randomised SVD of W' - W with 2 r + 4 sketch vectors and 6 power
+ * iterations; the sketch of the k-th edited matrix is seeded with seed + k
+ * (Options.seed) from this library's own generator, not ditch's, so the two
+ * agree to the SVD's accuracy. Tensor-parallel ranks (partial row norms) and,
+ * for full, models with routed experts return DITCH_CUDA_UNSUPPORTED. */
+int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_rank, uint64_t seed);
 /* moe.applyExpertSelective, ranked selection (src/moe.zig:1373-1477): the
  * o_proj edit as above, then per MoE layer the top n_experts experts by
  * ||v^T W_down|| / ||W_down||_F get lambda * strength. */

@@ -331,3 +331,139 @@ def residual_sums(res, first_capture, take):
     sums = np.zeros((entries, hidden), np.float64)
     lib().or_residual_sums(ptr(res), entries, nc, hidden, ptr(fc, szp), ptr(tk, szp), len(tk), ptr(sums, f64p))
     return sums
+
+
+# ---- row_normalization = full (src/abliterate.zig:324-350, 409-538) -------
+
+def orthonormalize_rows(vecs):
+    """abliterate.orthonormalize (src/abliterate.zig:409-423): modified
+    Gram-Schmidt, two passes, zero for a vanishing vector."""
+    v = f32(vecs).copy()
+    for i in range(v.shape[0]):
+        for _ in range(2):
+            for j in range(i):
+                v[i] -= np.float32(np.dot(v[i], v[j])) * v[j]
+        nrm = np.float32(np.sqrt(np.dot(v[i], v[i])))
+        v[i] = v[i] / nrm if nrm > 1e-20 else 0.0
+    return v
+
+
+def jacobi_eigen(m):
+    """abliterate.jacobiEigen (src/abliterate.zig:427-470): cyclic Jacobi in
+    f32; returns (matrix with the eigenvalues on its diagonal, vectors in
+    columns)."""
+    m = f32(m).copy()
+    n = m.shape[0]
+    vecs = np.eye(n, dtype=np.float32)
+    for _ in range(50):
+        off = float(np.sum(m.astype(np.float64) ** 2) - np.sum(np.diag(m).astype(np.float64) ** 2))
+        if off < 1e-18:
+            break
+        for p in range(n):
+            for q in range(p + 1, n):
+                apq = m[p, q]
+                if abs(apq) < 1e-20:
+                    continue
+                theta = np.float32((m[q, q] - m[p, p]) / (np.float32(2) * apq))
+                with np.errstate(over="ignore"):  # theta^2 may overflow to inf, then t = 0, as in f32
+                    t = np.float32(np.sign(theta) / (abs(theta) + np.sqrt(theta * theta + np.float32(1))))
+                t = np.float32(1) if theta == 0 else t
+                cs = np.float32(1) / np.float32(np.sqrt(t * t + np.float32(1)))
+                sn = t * cs
+                cp, cq = m[:, p].copy(), m[:, q].copy()
+                m[:, p], m[:, q] = cs * cp - sn * cq, sn * cp + cs * cq
+                rp, rq = m[p, :].copy(), m[q, :].copy()
+                m[p, :], m[q, :] = cs * rp - sn * rq, sn * rp + cs * rq
+                vp, vq = vecs[:, p].copy(), vecs[:, q].copy()
+                vecs[:, p], vecs[:, q] = cs * vp - sn * vq, sn * vp + cs * vq
+    return m, vecs
+
+
+def sketch_normals(seed, count):
+    """The sketch of ditch_b200's full-mode edit: SplitMix64 then Box-Muller
+    (the library's generator, not ditch's; both only seed the randomised
+    SVD's test matrix)."""
+    mask = (1 << 64) - 1
+    s = seed & mask
+    out = np.zeros(count, np.float32)
+    i = 0
+
+    def nxt():
+        nonlocal s
+        s = (s + 0x9E3779B97F4A7C15) & mask
+        z = s
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & mask
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & mask
+        return z ^ (z >> 31)
+
+    while i < count:
+        u1 = ((nxt() >> 11) + 1.0) * 2.0 ** -53
+        u2 = (nxt() >> 11) * 2.0 ** -53
+        r, th = np.sqrt(-2.0 * np.log(u1)), 6.283185307179586 * u2
+        out[i] = np.float32(r * np.cos(th))
+        if i + 1 < count:
+            out[i + 1] = np.float32(r * np.sin(th))
+        i += 2
+    return out
+
+
+def compute_delta_full(w, v, lam, lora_rank=3, seed=0, omega=None):
+    """computeOutputDelta with row_normalization = full, K = 1
+    (src/abliterate.zig:324-350) and randomizedSvd (473-538): the rank-r
+    delta (a [r][cols], b [rows][r]) of W' = diag(n) rownorm(Wn + B A^T), from
+    the implicit operator D = diag(c) W + d a^T, 2 r + 4 sketch vectors and 6
+    power iterations. `omega` overrides the seeded sketch [q][cols]."""
+    w, v = f32(w), f32(v)
+    rows, cols = w.shape
+    lam = np.float32(lam)
+    n = row_norms(w)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        vn = np.where(n > 0, v / n, np.float32(0)).astype(np.float32)
+    a = matvec_t_multi(w, vn[None, :])[0]
+    wa = matmul_t(a[None, :], w)[0]
+    gram = np.float32(np.dot(a, a))
+    bij = -lam * v
+    with np.errstate(divide="ignore", invalid="ignore"):
+        wn_dot_a = np.where(n > 0, wa / n, np.float32(0)).astype(np.float32)
+    s2 = np.float32(1) + np.float32(2) * bij * wn_dot_a + bij * (-lam * v) * gram
+    s = np.sqrt(np.maximum(s2, np.float32(1e-12))).astype(np.float32)
+    c = (np.float32(1) / s - np.float32(1)).astype(np.float32)
+    d = (n * (-lam * v) / s).astype(np.float32)
+
+    def apply(x):  # (D X^T)^T for x [q][cols]
+        y = matmul_t(x, w) * c
+        return (y + np.outer(x @ a, d)).astype(np.float32)
+
+    def apply_t(y):  # (D^T Y^T)^T for y [q][rows]
+        x = matvec_t_multi(w, y * c)
+        return (x + np.outer(y @ d, a)).astype(np.float32)
+
+    r = max(int(lora_rank), 1)
+    q = min(2 * r + 4, min(rows, cols))
+    if omega is None:
+        omega = sketch_normals(seed, q * cols).reshape(q, cols)
+    qy = orthonormalize_rows(apply(omega))
+    for _ in range(6):
+        qx = orthonormalize_rows(apply_t(qy))
+        qy = orthonormalize_rows(apply(qx))
+    bt = apply_t(qy)
+    m, vecs = jacobi_eigen(bt @ bt.T)
+    order = sorted(range(q), key=lambda i: -float(m[i, i]))
+    rank = min(r, q)
+    la = np.zeros((rank, cols), np.float32)
+    lb = np.zeros((rows, rank), np.float32)
+    for k in range(rank):
+        src = order[k]
+        sk = np.float32(np.sqrt(max(float(m[src, src]), 0.0)))
+        uk = (vecs[:, src] @ qy).astype(np.float32)
+        vk = (vecs[:, src] @ bt).astype(np.float32)
+        vk = vk / sk if sk > 1e-12 else np.zeros(cols, np.float32)
+        sq = np.float32(np.sqrt(max(float(sk), 0.0)))
+        la[k] = sq * vk
+        lb[:, k] = uk * sq
+    return la, lb
+
+
+def materialize_rank(w, a, b):
+    """W + b a (a [r][cols], b [rows][r]) in f32."""
+    return (f32(w) + f32(b) @ f32(a)).astype(np.float32)

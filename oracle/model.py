@@ -51,12 +51,12 @@ class OracleModel:
             for f in ("input_norm", "post_norm", "q", "k", "v", "o", "qb", "kb", "vb", "q_norm",
                       "k_norm", "gate", "up", "down", "router", "e_gate", "e_up", "e_down"):
                 setattr(L, f, g(f"L{i}.{f}"))
-            if (i, "o") in self.deltas:
+            if (i, "o") in self.deltas:  # a [rank][cols] (or [cols]), b [rows][rank] (or [rows])
                 a, b = self.deltas[(i, "o")]
-                L.o_da, L.o_db, L.o_rank = ptr(a), ptr(b), 1
+                L.o_da, L.o_db, L.o_rank = ptr(a), ptr(b), a.shape[0] if a.ndim == 2 else 1
             if (i, "down") in self.deltas:
                 a, b = self.deltas[(i, "down")]
-                L.down_da, L.down_db, L.down_rank = ptr(a), ptr(b), 1
+                L.down_da, L.down_db, L.down_rank = ptr(a), ptr(b), a.shape[0] if a.ndim == 2 else 1
             E = s.get("n_experts", 0)
             if E and f"L{i}.router" in self.w:
                 da = (f32p * E)()

@@ -252,7 +252,7 @@ def test_pre_normalised_edit(device, family):
     edited KL against the oracle with a = (v / n)^T W, b = -lambda v n (n the
     row norms of the decoded weights), for o_proj, down_proj and (MoE) every
     expert's down projection; then the selective expert edit in the same
-    mode. "full" is refused as unsupported."""
+    mode."""
     g, m = load(device, family)
     s = g.spec
     w = g.f32_weights()
@@ -285,8 +285,6 @@ def test_pre_normalised_edit(device, family):
         _, ed = om.forward(toks, rb, rp, (), last)
         return oracle.kl_first_token(oracle.log_softmax(base), ed)[0]
 
-    with pytest.raises(ditch_b200.Unsupported):
-        m.set_row_normalization("full")
     m.set_row_normalization("pre")
     m.apply_edit(po, pd)
     got = m.kl_score()
@@ -303,3 +301,48 @@ def test_pre_normalised_edit(device, family):
         assert abs(got - want) <= 2e-3 + 0.05 * abs(want), (got, want)
     m.set_row_normalization("none")
     m.close()
+
+
+@pytest.mark.parametrize("family", ["qwen2", "qwen2_fp8", "llama"])
+def test_full_normalised_edit(device, family):
+    """row_normalization = full (src/abliterate.zig:324-350, randomized SVD
+    473-538): the device's rank-3 deltas against the oracle's restatement
+    run with the same seeded sketch (matrix k of the edit takes seed + k, in
+    the order layer by layer, o_proj then down_proj), compared through the
+    edited KL. Models with routed experts refuse full."""
+    g, m = load(device, family)
+    s = g.spec
+    w = g.f32_weights()
+    rng = np.random.default_rng(13)
+    dirs = rng.standard_normal((s["n_layers"] + 1, s["hidden"])).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    m.set_directions(dirs)
+    prompts = g.prompts()
+    toks, rb, rp, cap, first, take, last = flatten_batch(prompts)
+    m.kl_init(prompts)
+    po, pd = (1.1, 0.0, 0.5, 3.0), (0.9, 1.0, 0.3, 2.0)
+    seed = 77
+    m.set_row_normalization("full", lora_rank=3, seed=seed)
+    m.apply_edit(po, pd)
+    got = m.kl_score()
+    om = OracleModel(s, w)
+    k = 0
+    for li in range(s["n_layers"]):
+        v = dirs[li + 1]
+        for comp, p in (("o", po), ("down", pd)):
+            lam = oracle.kernel_weight(p, li)
+            if lam is None:
+                continue
+            a, b = oracle.compute_delta_full(w[f"L{li}.{comp}"], v, lam, lora_rank=3, seed=seed + k)
+            k += 1
+            om.set_delta(li, comp, a, b)
+    _, base = OracleModel(s, w).forward(toks, rb, rp, (), last)
+    _, ed = om.forward(toks, rb, rp, (), last)
+    want = oracle.kl_first_token(oracle.log_softmax(base), ed)[0]
+    assert got > 0 and abs(got - want) <= 2e-3 + 0.05 * abs(want), (got, want)
+    m.set_row_normalization("none")
+    m.close()
+    g2, m2 = load(device, "qwen3_moe")
+    with pytest.raises(ditch_b200.Unsupported):
+        m2.set_row_normalization("full")
+    m2.close()

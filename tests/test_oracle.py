@@ -79,6 +79,29 @@ def test_pre_normalised_edit_removes_direction():
     assert np.isfinite(a).all() and b[2] == 0.0
 
 
+def test_full_normalised_edit_reconstructs_the_renormalised_matrix():
+    """src/abliterate.zig:554-620, row_normalization = full, K = 1, lora_rank
+    5 on a 6 x 5 matrix: the rank-5 randomised SVD reproduces
+    W' = diag(n) rownorm(Wn - v a^T), a = v^T Wn, within 1e-3."""
+    rng = np.random.default_rng(7)
+    w = rng.standard_normal((6, 5)).astype(np.float32)
+    v = rng.standard_normal(6).astype(np.float32)
+    v /= np.linalg.norm(v)
+    la, lb = oracle.compute_delta_full(w, v, 1.0, lora_rank=5, seed=1)
+    assert la.shape == (5, 5) and lb.shape == (6, 5)
+    wp = oracle.materialize_rank(w, la, lb)
+    n = np.linalg.norm(w, axis=1)
+    wn = w / n[:, None]
+    a = v @ wn
+    rows = wn - np.outer(v, a)
+    want = rows / np.linalg.norm(rows, axis=1, keepdims=True) * n[:, None]
+    assert np.abs(wp - want).max() < 1e-3
+    # rank 3 (ditch's default) of the same: close, not exact
+    la3, lb3 = oracle.compute_delta_full(w, v, 1.0, lora_rank=3, seed=1)
+    assert la3.shape == (3, 5)
+    assert np.abs(oracle.materialize_rank(w, la3, lb3) - want).max() < 0.5
+
+
 def test_argmax_first_rule():
     """src/model.zig:5194-5204: the first maximum wins, NaN never does, a row
     with nothing above -inf gives 0."""
