@@ -55,6 +55,8 @@ def parse():
                          "trial loop (expert-selective edit); c5: Llama-3-70B-shaped in-place edit sweep; gemm: one "
                          "GEMM")
     ap.add_argument("--max-new", type=int, default=100, help="gen: tokens generated per prompt")
+    ap.add_argument("--row-normalization", default="none", choices=["none", "pre", "full"],
+                    help="c1 / c2: the edit's row normalisation (full: rank-3 delta from the randomised SVD)")
     ap.add_argument("--deterministic", type=int, default=0,
                     help="1: K splits summed in a fixed order (stream-K) instead of atomically")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
@@ -316,8 +318,9 @@ def reference_arm(args):
 
 
 def config_block(args):
-    return {"workload": "C2: Llama-3-8B-shaped, FP8 E4M3 128x128 block-scaled weights, trial = none-mode rank-1 "
-                        "edit of o_proj/down_proj + edited forward + first-token KL",
+    return {"workload": "C2: Llama-3-8B-shaped, FP8 E4M3 128x128 block-scaled weights, trial = %s-mode edit of "
+                        "o_proj/down_proj + edited forward + first-token KL" % args.row_normalization,
+            "row_normalization": args.row_normalization,
             "layers": args.layers, "prompts_per_gpu": args.prompts, "seq_len": args.seq, "vocab": C2["vocab"],
             "parallelism": f"dp{args.gpus} (prompt batches)",
             "l2": "inputs larger than L2 (7 GB of FP8 weights read per trial)",
@@ -394,6 +397,8 @@ def main():
     model.directions(gs, int(counts[0]), bs, int(counts[1]), True)
     capture_ms = dev.timer_stop()
     model.kl_init(kl_prompts)
+    if args.row_normalization != "none":
+        model.set_row_normalization(args.row_normalization, lora_rank=3, seed=args.seed)
 
     tokens_flat = np.concatenate(kl_prompts).astype(np.uint32)
     offs = np.zeros(P + 1, np.uintp)

@@ -30,14 +30,22 @@ uint16_t f32_to_bf16_host(float x) {
     return (uint16_t)((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
 }
 
+// f32 dot product in eight interleaved partial sums (the shape of ditch's
+// vector-lane dot, src/tensor.zig:550-558, and one the host compiler
+// vectorises), then the partials in order and the tail.
 float dotf(const float *a, const float *b, size_t n) {
+    float p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    size_t i = 0;
+    for (; i + 8 <= n; i += 8)
+        for (int l = 0; l < 8; l++) p[l] += a[i + l] * b[i + l];
     float s = 0.0f;
-    for (size_t i = 0; i < n; i++) s = std::fma(a[i], b[i], s);
+    for (int l = 0; l < 8; l++) s += p[l];
+    for (; i < n; i++) s += a[i] * b[i];
     return s;
 }
 
 void axpyf(float *y, float a, const float *x, size_t n) {
-    for (size_t i = 0; i < n; i++) y[i] = std::fma(a, x[i], y[i]);
+    for (size_t i = 0; i < n; i++) y[i] += a * x[i];
 }
 
 // Modified Gram-Schmidt with two passes, rows of `vecs` (orthonormalize,
@@ -132,7 +140,7 @@ struct Operator {
     const Mat &w;
     int row0, rows, cols;
     const std::vector<float> &a, &c, &d;
-    DevBuf act, out, ybuf, xbuf;
+    DevBuf &act, &out, &ybuf, &xbuf;  // the model's scratch (kept between matrices)
 
     // out[q][rows] = (D X)^T for x[q][cols]
     int apply(const std::vector<float> &x, int q, std::vector<float> &y) {
@@ -197,7 +205,7 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
     int s;
     // a = (v / n)^T W on the device, then n, v, a on the host
     DITCH_CUDA(m->vn.reserve((size_t)rows * 4));
-    DevBuf scratch, adev;
+    DevBuf &scratch = m->fn_s, &adev = m->fn_a;
     DITCH_CUDA(scratch.reserve((size_t)rows * 4));
     DITCH_CUDA(adev.reserve((size_t)cols * 4));
     DITCH_LAUNCH(dev, prenorm_vec(v_dev, rn, lambda, rows, m->vn.as<float>(), scratch.as<float>(), dev->stream));
@@ -211,7 +219,7 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
     std::vector<float> ones(rows, 1.0f), zeros(rows, 0.0f), c(rows), d(rows);
     std::vector<float> wa;
     {
-        Operator plain{m, w, row0, rows, cols, a, ones, zeros, {}, {}, {}, {}};
+        Operator plain{m, w, row0, rows, cols, a, ones, zeros, m->fn_act, m->fn_out, m->fn_y, m->fn_x};
         if ((s = plain.apply(a, 1, wa))) return s;
     }
     const float gram = dotf(a.data(), a.data(), cols);
@@ -228,7 +236,7 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
     // randomised SVD of D (q sketch vectors, 6 power iterations)
     const int r = std::max(lora_rank, 1);
     const int q = std::min(2 * r + 4, std::min(rows, cols));
-    Operator op{m, w, row0, rows, cols, a, c, d, {}, {}, {}, {}};
+    Operator op{m, w, row0, rows, cols, a, c, d, m->fn_act, m->fn_out, m->fn_y, m->fn_x};
     Normal rng{seed};
     std::vector<float> omega((size_t)q * cols), qy, qx, bt;
     for (float &x : omega) x = rng();

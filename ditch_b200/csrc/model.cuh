@@ -126,6 +126,7 @@ struct ditch_cuda_model {
     int lora_rank = 3;   // full: rank of the delta (Options.lora_rank)
     uint64_t edit_seed = 0, seed_counter = 0;  // full: the sketch seed of each matrix is seed + its index
     ditch::DevBuf vn;    // f32 [H]: v / ||W_i|| of the pre-normalised edit
+    ditch::DevBuf fn_act, fn_out, fn_y, fn_x, fn_a, fn_s;  // full-mode scratch
     ditch::Batch work;   // scratch batch for forward / residual passes
     ditch::DevBuf sums;  // f64 residual sums
     uint64_t bytes = 0;
