@@ -31,6 +31,11 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kEpiWarps = 4;
 constexpr int kXformWarps = 8;
+// Each decode thread owns one row part of a k-tile: 64 / kParts elements of
+// one of the 128 rows. (Measured on B200: 16 decode warps, a quarter row
+// each, were 4-9 % faster for FP8 at 128-512 tokens but 10-18 % slower for
+// MXFP4 and INT4, and the MoE trial lost 3 %.)
+constexpr int kParts = kXformWarps / 4;
 constexpr int kSmemBudget = 224 * 1024;
 
 template <int BN, bool DUAL, int FMT>
@@ -267,8 +272,8 @@ __device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *atile, in
                                           bool one_scale, float s_tile, int k0, const GemmParams &p) {
     const int rs = (r >> 1) & 3;
 #pragma unroll
-    for (int cc = 0; cc < 2; cc++) {
-        const int c = 2 * h + cc;  // raw 16-byte chunk: output chunks 2c, 2c + 1
+    for (int cc = 0; cc < 4 / kParts; cc++) {
+        const int c = (4 / kParts) * h + cc;  // raw 16-byte chunk: output chunks 2c, 2c + 1
         const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ rs) << 4));
         const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -299,17 +304,24 @@ __device__ __forceinline__ float2 e2m1x2_f32(uint32_t byte) {
 // Raw tile: 128 rows x 32 bytes (no swizzle); half h reads 16 bytes = one
 // 32-element block with scale s (loaded by the caller ahead of the wait).
 __device__ __forceinline__ void xform_mxfp4(const uint8_t *raw, uint8_t *atile, int r, int h, float s) {
-    const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    // part h: 32 / kParts bytes = 64 / kParts elements, output chunks (8 / kParts) h ...
+    uint32_t words[8 / kParts];
+    if constexpr (kParts == 2) {
+        const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
+        words[0] = q.x, words[1] = q.y, words[2] = q.z, words[3] = q.w;
+    } else {
+        const uint2 q = *reinterpret_cast<const uint2 *>(raw + r * 32 + h * 8);
+        words[0] = q.x, words[1] = q.y;
+    }
 #pragma unroll
-    for (int jj = 0; jj < 4; jj++) {  // one word = 8 elements = one output chunk
+    for (int jj = 0; jj < 8 / kParts; jj++) {  // one word = 8 elements = one output chunk
         const uint32_t w = words[jj];
         uint4 o;
         o.x = scale_pack(e2m1x2_f32(w & 0xff), s);
         o.y = scale_pack(e2m1x2_f32((w >> 8) & 0xff), s);
         o.z = scale_pack(e2m1x2_f32((w >> 16) & 0xff), s);
         o.w = scale_pack(e2m1x2_f32(w >> 24), s);
-        put_chunk(atile, r, 4 * h + jj, o);
+        put_chunk(atile, r, (8 / kParts) * h + jj, o);
     }
 }
 
@@ -317,10 +329,16 @@ __device__ __forceinline__ void xform_mxfp4(const uint8_t *raw, uint8_t *atile, 
 // bf16(f32(q - zp) * scale[row][g]); s and the zero point zq of the k-tile's
 // group are loaded by the caller. Raw tile as MXFP4.
 __device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *atile, int r, int h, float s, int zq) {
-    const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    uint32_t words[8 / kParts];
+    if constexpr (kParts == 2) {
+        const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
+        words[0] = q.x, words[1] = q.y, words[2] = q.z, words[3] = q.w;
+    } else {
+        const uint2 q = *reinterpret_cast<const uint2 *>(raw + r * 32 + h * 8);
+        words[0] = q.x, words[1] = q.y;
+    }
 #pragma unroll
-    for (int jj = 0; jj < 4; jj++) {
+    for (int jj = 0; jj < 8 / kParts; jj++) {
         const uint32_t w = words[jj];
         uint32_t o[4];
 #pragma unroll
@@ -329,7 +347,7 @@ __device__ __forceinline__ void xform_int4(const uint8_t *raw, uint8_t *atile, i
             const int hi = (int)((w >> (8 * e + 4)) & 0xf) - zq;
             o[e] = scale_pack(make_float2((float)lo, (float)hi), s);
         }
-        put_chunk(atile, r, 4 * h + jj, make_uint4(o[0], o[1], o[2], o[3]));
+        put_chunk(atile, r, (8 / kParts) * h + jj, make_uint4(o[0], o[1], o[2], o[3]));
     }
 }
 
@@ -354,8 +372,8 @@ __device__ __forceinline__ uint4 q8x8_bf16(uint32_t w0, uint32_t w1, float d) {
 __device__ __forceinline__ void xform_q8_0(const uint8_t *raw, uint8_t *atile, int r, int h, float d) {
     const int rs = (r >> 1) & 3;
 #pragma unroll
-    for (int cc = 0; cc < 2; cc++) {
-        const int c = 2 * h + cc;  // raw 16-byte chunk: output chunks 2c, 2c + 1
+    for (int cc = 0; cc < 4 / kParts; cc++) {
+        const int c = (4 / kParts) * h + cc;  // raw 16-byte chunk: output chunks 2c, 2c + 1
         const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ rs) << 4));
         put_chunk(atile, r, 2 * c, q8x8_bf16(q.x, q.y, d));
         put_chunk(atile, r, 2 * c + 1, q8x8_bf16(q.z, q.w, d));
@@ -373,10 +391,10 @@ __device__ __forceinline__ void load_side(const GemmParams &p, int vrow, const f
     if (FMT == kFmtFp8) {
         if (one_scale) s = __ldg(srow + k0 / p.blk_cols);
     } else if (FMT == kFmtMxfp4) {
-        const int blk = (k0 >> 5) + h;
+        const int blk = (k0 >> 5) + h * 2 / kParts;  // the 32-element block of part h
         if (blk * 32 < p.k) s = e8m0_scale(__ldg(p.scales_u8 + (long long)vrow * (p.k / 32) + blk));
     } else if (FMT == kFmtQ8_0) {
-        const int blk = (k0 >> 5) + h;
+        const int blk = (k0 >> 5) + h * 2 / kParts;  // the 32-element block of part h
         if (blk * 32 < p.k) s = __ldg(p.scales + (long long)vrow * p.scale_cols + blk);
     } else if (FMT == kFmtInt4) {
         const int groups = p.scale_cols, g = k0 / p.blk_cols;
@@ -784,7 +802,9 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
             const int m_end = ti.tok0 + ti.tok_cnt;
             // stream-K: a part of a split tile goes to this CTA's slot; the CTA
             // that brings the last part sums them all in k order and finishes
-            constexpr int EC = 32;  // accumulator columns (tokens) per step
+            // accumulator columns (tokens) per step: 16 where the decode warps
+            // leave each thread fewer registers
+            constexpr int EC = (C::kQuant && kXformWarps > 8) ? 16 : 32;
             bool finish = true;
             int c_lo = 0, c_hi = -1;
             long long t_u0 = 0;
@@ -869,8 +889,13 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
             for (int c0 = 0; c0 < BN && finish; c0 += EC) {
                 if (ti.tok0 + c0 >= m_end) break;  // warp-uniform: no valid token left
                 float v[EC], u[EC];
-                tmem_ld32(tbase + c0, v);
-                if (DUAL) tmem_ld32(tbase + BN + c0, u);
+                if constexpr (EC == 32) {
+                    tmem_ld32(tbase + c0, v);
+                    if (DUAL) tmem_ld32(tbase + BN + c0, u);
+                } else {
+                    tmem_ld16(tbase + c0, v);
+                    if (DUAL) tmem_ld16(tbase + BN + c0, u);
+                }
                 const int m0 = ti.tok0 + c0;
                 const int mv = min(EC, m_end - m0);  // valid tokens of this chunk (>= 1)
                 // Every load of a chunk is issued before its first store: as far
@@ -930,8 +955,8 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
         }
     } else if (C::kQuant) {
         // ---------------- weight transform ----------------
-        const int t = threadIdx.x - (2 + kEpiWarps) * 32;  // 0..255
-        const int r = t & 127, h = t >> 7;
+        const int t = threadIdx.x - (2 + kEpiWarps) * 32;  // 0 .. 32 kXformWarps - 1
+        const int r = t & 127, h = t >> 7;                  // row, part of the row
         const bool one_scale = FMT == kFmtFp8 && (p.blk_cols & 63) == 0;
         int it = 0;
         for (int tile = w_first; tile < w_end && !*abort; tile += w_step) {
