@@ -324,7 +324,9 @@ def config_block(args):
             "layers": args.layers, "prompts_per_gpu": args.prompts, "seq_len": args.seq, "vocab": C2["vocab"],
             "parallelism": f"dp{args.gpus} (prompt batches)",
             "l2": "inputs larger than L2 (7 GB of FP8 weights read per trial)",
-            "fp8_decode": ("staged: each GEMM with >= %d tokens decodes its FP8 weight once to bf16, then bf16 GEMM"
+            "fp8_decode": ("staged: each GEMM with >= %d tokens runs the bf16 GEMM over its FP8 weight decoded once "
+                           "to bf16 (decoded on first use, the copy kept across trials: the weights never change, "
+                           "edits are separate deltas)"
                            % (1024 if args.stage_min_tokens is None else args.stage_min_tokens)
                            if args.stage_min_tokens != 0 else "inside the GEMM (tile by tile)")}
 
@@ -446,8 +448,8 @@ def main():
     tpg, tsrc = traffic_from_profiles()
     traffic = tpg * gemm_flops / 1e9 / max(gemm_launches, 1) if tpg else None
     staged = args.stage_min_tokens != 0 and P * S >= (args.stage_min_tokens or 1024)
-    kernel_name = ("gemm_kernel: tcgen05 bf16 MMA over the FP8 weights decoded once per GEMM to bf16 (staged plan)"
-                   if staged else "gemm_kernel: tcgen05 bf16 MMA, FP8 decoded per tile inside the GEMM")
+    kernel_name = ("gemm_kernel: tcgen05 bf16 MMA over bf16 copies of the FP8 weights (decoded on first use and "
+                   "kept; staged plan)" if staged else "gemm_kernel: tcgen05 bf16 MMA, FP8 decoded per tile inside the GEMM")
     line = {
         "metric": "trial-eval forward tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),

@@ -270,6 +270,13 @@ int ditch_cuda_set_decode_staging(ditch_cuda_device *dev, int min_tokens) {
     return DITCH_CUDA_OK;
 }
 
+int ditch_cuda_set_decode_cache(ditch_cuda_device *dev, int enabled) {
+    REQUIRE(dev, "null device");
+    std::lock_guard<std::mutex> lk(dev->mu);
+    dev->decode_cache = enabled != 0;
+    return DITCH_CUDA_OK;
+}
+
 int ditch_cuda_set_deterministic(ditch_cuda_device *dev, int enabled) {
     REQUIRE(dev, "null device");
     std::lock_guard<std::mutex> lk(dev->mu);

@@ -97,6 +97,7 @@ struct ditch_cuda_device {
     long long sk_tiles = 0;      // counters zeroed so far
     int stage_min_tokens = 1024;
     bool deterministic = false;  // K splits summed in a fixed order (no atomics)
+    bool decode_cache = true;    // staged GEMMs keep their weight's bf16 copy
     // profiling of GEMMs
     bool profiling = false;
     std::vector<ditch::GemmEvent> events;

@@ -22,6 +22,10 @@ struct Mat {
     DevBuf scales;  // FP8 f32 [slabs*srows][scols] | MXFP4 u8 [slabs*rows][cols/32] | INT4 f32 [slabs*rows][groups]
     DevBuf zeros;   // INT4 packed zero points [slabs*rows/8][groups]
     int br = 0, bc = 0, scols = 0, groups = 0, group = 0;
+    // Rows [decoded_row0, decoded_row0 + decoded_rows) decoded to bf16 by a
+    // staged GEMM and kept (the weights never change: edits are deltas).
+    mutable DevBuf decoded;
+    mutable int decoded_row0 = -1, decoded_rows = 0;
     bool empty() const { return data.ptr == nullptr; }
     size_t bytes() const { return data.bytes + scales.bytes + zeros.bytes; }
 };

@@ -239,9 +239,27 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     // running the bf16 GEMM costs less. Both build the same bf16 operand.
     if (fmt != kFmtBf16 && !(ex && ex->sched) && dev->stage_min_tokens > 0 && n_tok >= dev->stage_min_tokens) {
         const int rows = (dual ? a2_row_offset : 0) + m_rows;
-        DITCH_CUDA(dev->stage.reserve((size_t)rows * w.cols * 2));
-        DITCH_LAUNCH(dev, decode_rows_bf16(dev, w, slab_row0, rows, dev->stage.as<uint16_t>()));
-        A = GemmOperand{dev->stage.ptr, rows, w.cols, (long long)w.cols * 2};
+        const size_t bytes = (size_t)rows * w.cols * 2;
+        const void *dec = nullptr;
+        if (w.decoded.ptr && w.decoded_row0 == slab_row0 && w.decoded_rows == rows) {
+            dec = w.decoded.ptr;  // decoded by an earlier call
+        } else if (dev->decode_cache && !w.decoded.ptr) {
+            // keep the bf16 copy when memory allows (4 GiB left for everything else)
+            size_t free_b = 0, total_b = 0;
+            if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && free_b > bytes + (4ull << 30) &&
+                w.decoded.reserve(bytes) == cudaSuccess) {
+                DITCH_LAUNCH(dev, decode_rows_bf16(dev, w, slab_row0, rows, w.decoded.as<uint16_t>()));
+                w.decoded_row0 = slab_row0;
+                w.decoded_rows = rows;
+                dec = w.decoded.ptr;
+            }
+        }
+        if (!dec) {
+            DITCH_CUDA(dev->stage.reserve(bytes));
+            DITCH_LAUNCH(dev, decode_rows_bf16(dev, w, slab_row0, rows, dev->stage.as<uint16_t>()));
+            dec = dev->stage.ptr;
+        }
+        A = GemmOperand{dec, rows, w.cols, (long long)w.cols * 2};
         fmt = kFmtBf16;
         slab_row0 = 0;
     }

@@ -329,6 +329,13 @@ int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out_bf16);
  * the GEMM. Default 1024. No counterpart in the reference (a tuning knob of
  * this backend). */
 int ditch_cuda_set_decode_staging(ditch_cuda_device *dev, int min_tokens);
+/* A staged GEMM keeps the bf16 copy of the weight it decoded and reuses it on
+ * later calls (the resident weights never change; edits are separate deltas):
+ * a trial loop then decodes each FP8 / MXFP4 / INT4 / Q8_0 weight once, like
+ * ditch's own bf16 copies in mapped mode, at 2 bytes per element of device
+ * memory (copies are made only while more than 4 GiB stays free). 0 decodes
+ * into scratch on every call. Default on. Results are the same either way. */
+int ditch_cuda_set_decode_cache(ditch_cuda_device *dev, int enabled);
 /* Deterministic products. GEMMs with few output tiles split K over the SMs;
  * by default the splits add their partial sums with atomics, whose order
  * (and so the last bits of the result) varies from run to run. With
