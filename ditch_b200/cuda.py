@@ -98,6 +98,9 @@ SIGNATURES = {
     "ditch_cuda_dequant_ggml": (C.c_int, [vp, C.c_int, u8p, sz, sz, f32p]),
     "ditch_cuda_model_load": (C.c_int, [vp, C.POINTER(ModelConfig), C.POINTER(TensorDesc), sz, C.POINTER(vp)]),
     "ditch_cuda_model_free": (None, [vp]),
+    "ditch_cuda_model_load_checkpoint": (C.c_int, [vp, C.c_char_p, C.c_int, C.POINTER(vp)]),
+    "ditch_cuda_checkpoint_inspect": (C.c_int, [C.c_char_p, C.POINTER(ModelConfig), C.POINTER(sz),
+                                                C.POINTER(C.c_uint8), sz]),
     "ditch_cuda_model_bytes": (C.c_uint64, [vp]),
     "ditch_cuda_forward": (C.c_int, [vp, u32p, u32p, u32p, sz, C.POINTER(sz), sz, f32p, C.POINTER(sz), sz, f32p]),
     "ditch_cuda_generate": (C.c_int, [vp, u32p, C.POINTER(sz), sz, sz, u32p, sz, u32p, C.POINTER(sz)]),
@@ -473,8 +476,38 @@ class Group:
             pass
 
 
+def inspect_checkpoint(path):
+    """The model spec and tensor count ditch_cuda_model_load_checkpoint would
+    use for a Hugging Face directory or a GGUF file (no device needed)."""
+    cfg = ModelConfig()
+    n = sz(0)
+    flags = (C.c_uint8 * 4096)()
+    check(lib().ditch_cuda_checkpoint_inspect(str(path).encode(), C.byref(cfg), C.byref(n), flags, 4096))
+    spec = dict(n_layers=cfg.n_layers, hidden=cfg.hidden, heads=cfg.heads, kv_heads=cfg.kv_heads,
+                head_dim=cfg.head_dim, inter=cfg.inter, vocab=cfg.vocab, eps=cfg.eps, rope_theta=cfg.rope_theta,
+                rope_scaling=cfg.rope_scaling, rope_factor=cfg.rope_factor, rope_low_ff=cfg.rope_low_ff,
+                rope_high_ff=cfg.rope_high_ff, rope_orig_max=cfg.rope_orig_max, qk_norm=cfg.qk_norm)
+    if cfg.n_experts:
+        spec.update(n_experts=cfg.n_experts, top_k=cfg.top_k, moe_inter=cfg.moe_inter, norm_topk=cfg.norm_topk,
+                    moe_layers=[bool(flags[i]) for i in range(cfg.n_layers)])
+    return spec, n.value
+
+
 class Model:
     """A model resident in HBM (the coarse C-ABI entries)."""
+
+    @classmethod
+    def from_checkpoint(cls, device, path, max_seq=4096):
+        """Loads a Hugging Face directory or a GGUF file
+        (ditch_cuda_model_load_checkpoint)."""
+        spec, _ = inspect_checkpoint(path)
+        self = cls.__new__(cls)
+        self.dev, self.spec, self._moe = device, spec, None
+        h = vp()
+        check(lib().ditch_cuda_model_load_checkpoint(device.h, str(path).encode(), int(max_seq), C.byref(h)))
+        self.h = h
+        device._adopt(self)
+        return self
 
     def __init__(self, device, spec, tensors, max_seq=4096, ep_rank=0, ep_world=1, tp_rank=0, tp_world=1):
         self.dev = device

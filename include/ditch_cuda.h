@@ -188,6 +188,24 @@ typedef struct {
 int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config *cfg, const ditch_cuda_tensor *tensors,
                           size_t n_tensors, ditch_cuda_model **out);
 void ditch_cuda_model_free(ditch_cuda_model *m);
+
+/* A checkpoint from disk (src/safetensors.zig, src/gguf_model.zig,
+ * src/dequant.zig:783-1187): a Hugging Face directory (config.json and
+ * *.safetensors; model_type llama, mistral, qwen2, qwen3, qwen3_moe or
+ * mixtral; bf16 / f16 / f32, FP8 block-scaled with weight_block_size, or
+ * compressed-tensors pack-quantized INT without g_idx; routed experts one
+ * tensor per expert, mixtral's w1 / w3 / w2, or fused gate_up_proj /
+ * down_proj in either orientation) or a GGUF file (qwen2 or llama; F32, F16,
+ * BF16, Q8_0, Q4_K; llama's permuted q / k rows restored). Quantised groups
+ * reach the device raw. The files are memory-mapped during the call.
+ * max_seq: the RoPE table rows (0 = 4096). Anything else returns
+ * DITCH_CUDA_UNSUPPORTED with the reason in ditch_cuda_last_error(). */
+int ditch_cuda_model_load_checkpoint(ditch_cuda_device *dev, const char *path, int max_seq, ditch_cuda_model **out);
+/* The config and tensor count the loader would use, without a device
+ * (moe_layers, when given, receives up to moe_layers_len flags; cfg's own
+ * moe_layers pointer is left NULL). */
+int ditch_cuda_checkpoint_inspect(const char *path, ditch_cuda_model_config *cfg, size_t *n_tensors,
+                                  uint8_t *moe_layers, size_t moe_layers_len);
 /* Device bytes the resident model holds. */
 uint64_t ditch_cuda_model_bytes(const ditch_cuda_model *m);
 

@@ -1,0 +1,190 @@
+"""The checkpoint loader (ditch_cuda_checkpoint_inspect /
+ditch_cuda_model_load_checkpoint): a Hugging Face directory (config.json +
+*.safetensors) or a GGUF file read in place, its tensors handed to the device
+loader as stored, the way src/model.zig's load resolves names, layouts and
+quantised formats (src/safetensors.zig, src/gguf.zig, src/moe.zig:83-92,
+728-770). The files are written from the committed golden fixtures by
+tests/checkpoint_files.py.
+
+CPU: the config each file yields against the fixture's own spec, the tensor
+count, and the refusals. GPU: a model loaded from the file against the model
+built from the fixture's tensors through ditch_cuda_model_load, bit for bit
+(deterministic K splits)."""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import ditch_b200
+from checkpoint_files import fixture, write_gguf, write_gguf_fixture, write_hf_dir, write_llama_gguf
+from golden_loader import Golden
+from oracle.model import flatten_batch
+
+HF_FAMILIES = ["qwen2", "qwen2_fp8", "qwen2_int4", "qwen3", "llama", "mixtral", "qwen3_moe", "qwen3_moe_fused",
+               "qwen3_moe_fused_t"]
+
+SPEC_KEYS = ["n_layers", "hidden", "heads", "kv_heads", "head_dim", "vocab", "qk_norm", "n_experts", "top_k",
+             "moe_inter", "norm_topk", "moe_layers", "rope_scaling", "rope_factor", "rope_low_ff", "rope_high_ff",
+             "rope_orig_max"]
+
+
+def checkpoint(tmp_path, family):
+    if family == "qwen2_gguf":
+        return write_gguf_fixture(str(tmp_path / "model.gguf"), family)
+    if family == "llama_gguf":
+        return write_llama_gguf(str(tmp_path / "model.gguf"))
+    return write_hf_dir(str(tmp_path / family), family)
+
+
+def golden_spec(family):
+    g = Golden("llama" if family == "llama_gguf" else family)
+    s = dict(g.spec)
+    if family == "llama_gguf":  # GGUF carries no llama3 rope factors
+        for k in ("rope_scaling", "rope_factor", "rope_low_ff", "rope_high_ff", "rope_orig_max"):
+            s.pop(k, None)
+    return g, s
+
+
+def check_spec(got, want):
+    for k in SPEC_KEYS:
+        if k in want:
+            assert got.get(k) == (int(want[k]) if isinstance(want[k], bool) else want[k]), k
+    assert got.get("rope_scaling", 0) == int(want.get("rope_scaling", 0))
+    if got.get("inter"):
+        assert got["inter"] == want["inter"]
+    assert got["eps"] == pytest.approx(want["eps"], rel=1e-6)
+    assert got["rope_theta"] == pytest.approx(want["rope_theta"], rel=1e-6)
+
+
+@pytest.mark.parametrize("family", HF_FAMILIES + ["qwen2_gguf", "llama_gguf"])
+def test_inspect_matches_fixture_spec(tmp_path, family):
+    path = checkpoint(tmp_path, family)
+    spec, n = ditch_b200.inspect_checkpoint(path)
+    g, want = golden_spec(family)
+    check_spec(spec, want)
+    # one table entry per canonical weight, stacked experts counted once
+    n_want = sum(1 for c, hf in g.hf_names().items() if g.has(hf))
+    n_want += 3 * sum(1 for x in (want.get("moe_layers") or []) if x)
+    assert n == n_want
+
+
+def test_hf_dir_with_shards(tmp_path):
+    """A checkpoint split over several safetensors files, as large models are."""
+    config, dtypes, _, raw = fixture("qwen2")
+    from checkpoint_files import write_safetensors
+    d = tmp_path / "sharded"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(config))
+    names = sorted(raw)
+    for i, part in enumerate((names[: len(names) // 2], names[len(names) // 2:])):
+        write_safetensors(str(d / f"model-0000{i + 1}-of-00002.safetensors"), {n: (dtypes[n], raw[n]) for n in part})
+    spec, n = ditch_b200.inspect_checkpoint(str(d))
+    check_spec(spec, Golden("qwen2").spec)
+
+
+def test_refusals(tmp_path):
+    with pytest.raises(ditch_b200.DitchCudaError):
+        ditch_b200.inspect_checkpoint(str(tmp_path / "missing"))
+    # a model_type the device path does not take
+    config, dtypes, _, raw = fixture("qwen2")
+    d = write_hf_dir(str(tmp_path / "other"), "qwen2")
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(dict(config, model_type="gpt2"), f)
+    with pytest.raises(ditch_b200.Unsupported):
+        ditch_b200.inspect_checkpoint(d)
+    # a required tensor missing
+    d = write_hf_dir(str(tmp_path / "short"), "qwen2")
+    from checkpoint_files import write_safetensors
+    keep = {n: (dtypes[n], raw[n]) for n in sorted(raw) if "layers.1.mlp.up_proj" not in n}
+    write_safetensors(os.path.join(d, "model.safetensors"), keep)
+    with pytest.raises(ditch_b200.DitchCudaError, match="up_proj"):
+        ditch_b200.inspect_checkpoint(d)
+    # a safetensors header that points past the end of its file
+    d = write_hf_dir(str(tmp_path / "trunc"), "qwen2")
+    p = os.path.join(d, "model.safetensors")
+    size = os.path.getsize(p)
+    with open(p, "r+b") as f:
+        f.truncate(size - 64)
+    with pytest.raises(ditch_b200.DitchCudaError):
+        ditch_b200.inspect_checkpoint(d)
+    # not a GGUF file
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGUX" + bytes(60))
+    with pytest.raises(ditch_b200.DitchCudaError):
+        ditch_b200.inspect_checkpoint(str(bad))
+    # a ggml type the device path has no decoder for (Q5_0 = 6)
+    q = tmp_path / "q5.gguf"
+    blob = np.zeros(22 * 2, np.uint8)
+    from checkpoint_files import GGML_TYPE
+    GGML_TYPE["Q5_0"] = 6
+    try:
+        write_gguf(str(q), "qwen2", [("qwen2.block_count", 4, 1)], {"token_embd.weight": ("Q5_0", blob, [2, 32])})
+    finally:
+        del GGML_TYPE["Q5_0"]
+    with pytest.raises(ditch_b200.Unsupported):
+        ditch_b200.inspect_checkpoint(str(q))
+
+
+def test_gguf_rope_freqs_refused(tmp_path):
+    """llama3-style rope factors in a GGUF file (rope_freqs.weight) are refused
+    rather than silently dropped."""
+    config, _, _, _ = fixture("llama")
+    half = config["hidden_size"] // config["num_attention_heads"] // 2
+    path = write_llama_gguf(str(tmp_path / "f.gguf"),
+                            extra={"rope_freqs.weight": ("F32", np.ones(half, np.float32), [half])})
+    with pytest.raises(ditch_b200.Unsupported, match="rope_freqs"):
+        ditch_b200.inspect_checkpoint(path)
+
+
+def test_safetensors_header_is_parsed_not_trusted(tmp_path):
+    """A header length larger than the file and a tensor whose byte range
+    disagrees with its dtype x shape are errors, not reads out of bounds."""
+    d = tmp_path / "h"
+    d.mkdir()
+    config, _, _, _ = fixture("qwen2")
+    (d / "config.json").write_text(json.dumps(config))
+    with open(d / "model.safetensors", "wb") as f:
+        f.write(struct.pack("<Q", 1 << 40) + b"{}")
+    with pytest.raises(ditch_b200.DitchCudaError):
+        ditch_b200.inspect_checkpoint(str(d))
+    hdr = json.dumps({"model.embed_tokens.weight": {"dtype": "BF16", "shape": [4, 4], "data_offsets": [0, 30]}}).encode()
+    with open(d / "model.safetensors", "wb") as f:
+        f.write(struct.pack("<Q", len(hdr)) + hdr + bytes(30))
+    with pytest.raises(ditch_b200.DitchCudaError):
+        ditch_b200.inspect_checkpoint(str(d))
+
+
+# ---- on the device -----------------------------------------------------------
+
+def _logits(m, prompts):
+    toks, rb, rp, cap, first, take, last = flatten_batch(prompts)
+    return m.forward(toks, rb, rp, (), last)[1]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("family", HF_FAMILIES + ["qwen2_gguf", "llama_gguf"])
+def test_load_checkpoint_matches_tensor_table(device, tmp_path, family):
+    """The model loaded from the file computes bit-identical logits to the one
+    built from the fixture's own tensor table (which test_gpu_model checks
+    against the reference's logits)."""
+    path = checkpoint(tmp_path, family)
+    g, spec = golden_spec(family)
+    prompts = g.prompts()
+    device.set_deterministic(True)
+    try:
+        a = ditch_b200.Model.from_checkpoint(device, path, max_seq=64)
+        try:
+            got = _logits(a, prompts)
+        finally:
+            a.close()
+        b = ditch_b200.Model(device, spec, g.cuda_tensors(), max_seq=64)
+        try:
+            want = _logits(b, prompts)
+        finally:
+            b.close()
+    finally:
+        device.set_deterministic(False)
+    assert got.shape == want.shape
+    assert np.array_equal(got, want), float(np.abs(got - want).max())
