@@ -248,7 +248,8 @@ int ditch_cuda_open(int ordinal, uint64_t memory_budget, ditch_cuda_device **out
     dev->budget = memory_budget;
     cudaError_t e = cudaStreamCreateWithFlags(&dev->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&dev->status, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(dev->status, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemsetAsync(dev->status, 0, sizeof(int), dev->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(dev->stream);
     if (e == cudaSuccess) e = cudaEventCreate(&dev->t0);
     if (e == cudaSuccess) e = cudaEventCreate(&dev->t1);
     if (e != cudaSuccess) {

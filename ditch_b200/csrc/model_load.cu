@@ -336,8 +336,11 @@ int build_rope(ditch_cuda_model *m) {
         }
     DITCH_CUDA(m->rope_cos.reserve(cs.size() * 4));
     DITCH_CUDA(m->rope_sin.reserve(sn.size() * 4));
-    DITCH_CUDA(cudaMemcpy(m->rope_cos.ptr, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
-    DITCH_CUDA(cudaMemcpy(m->rope_sin.ptr, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    // on the model's stream (non-blocking: the legacy stream would not order
+    // these copies before its kernels), done before the host tables go
+    DITCH_CUDA(cudaMemcpyAsync(m->rope_cos.ptr, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, m->dev->stream));
+    DITCH_CUDA(cudaMemcpyAsync(m->rope_sin.ptr, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, m->dev->stream));
+    DITCH_CUDA(cudaStreamSynchronize(m->dev->stream));
     m->rope_len = len;
     return DITCH_CUDA_OK;
 }
@@ -453,8 +456,8 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
         windows.emplace_back();
         DevBuf &w = windows.back();
         if (w.reserve(t->rows * part * e) != cudaSuccess) return nullptr;
-        if (cudaMemcpy2D(w.ptr, part * e, static_cast<const uint8_t *>(t->data) + (size_t)r_tp * part * e, full * e,
-                         part * e, t->rows, kind_of(t)) != cudaSuccess)
+        if (cudaMemcpy2DAsync(w.ptr, part * e, static_cast<const uint8_t *>(t->data) + (size_t)r_tp * part * e,
+                              full * e, part * e, t->rows, kind_of(t), m->dev->stream) != cudaSuccess)
             return nullptr;
         views.emplace_back(new ditch_cuda_tensor(*t));
         ditch_cuda_tensor *v = views.back().get();
@@ -522,14 +525,19 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
         if (qb || kb || vb) {
             std::vector<float> zeros(c.qkv_width(), 0.0f);
             DITCH_CUDA(L.qkv_bias.reserve(c.qkv_width() * 4));
-            DITCH_CUDA(cudaMemcpy(L.qkv_bias.ptr, zeros.data(), zeros.size() * 4, cudaMemcpyHostToDevice));
+            // every copy on the model's stream: load_vec's upload of an f32
+            // vector is asynchronous there, and the legacy stream does not
+            // wait for it
+            DITCH_CUDA(cudaMemsetAsync(L.qkv_bias.ptr, 0, c.qkv_width() * 4, dev->stream));
             DevBuf tmp;
             const ditch_cuda_tensor *bs[3] = {qb, kb, vb};
             const int off[3] = {0, qd, qd + kvd}, len[3] = {qd, kvd, kvd};
             for (int j = 0; j < 3; j++) {
                 if (!bs[j]) continue;
                 if ((st = load_vec(m.get(), bs[j], len[j], tmp, "qkv bias"))) return st;
-                DITCH_CUDA(cudaMemcpy(L.qkv_bias.as<float>() + off[j], tmp.ptr, len[j] * 4, cudaMemcpyDeviceToDevice));
+                DITCH_CUDA(cudaMemcpyAsync(L.qkv_bias.as<float>() + off[j], tmp.ptr, len[j] * 4, cudaMemcpyDeviceToDevice,
+                                           dev->stream));
+                DITCH_CUDA(cudaStreamSynchronize(dev->stream));  // before tmp is reused or freed
             }
         }
         if (c.moe_layers[i]) {
@@ -569,7 +577,7 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
             DITCH_CUDA(L.e_a.reserve((size_t)El * L.e_down.cols * 4));
             DITCH_CUDA(L.e_b.reserve((size_t)El * H * 4));
             DITCH_CUDA(L.e_edit_dev.reserve((size_t)El * 4));
-            DITCH_CUDA(cudaMemset(L.e_edit_dev.ptr, 0, (size_t)El * 4));
+            DITCH_CUDA(cudaMemsetAsync(L.e_edit_dev.ptr, 0, (size_t)El * 4, dev->stream));
         } else {
             const ditch_cuda_tensor *g = t("gate"), *u = t("up"), *d = t("down");
             REQUIRE(g && u && d, "layer %d: MLP projections missing", i);

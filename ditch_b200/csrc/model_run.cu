@@ -948,7 +948,8 @@ int ditch_cuda_set_directions(ditch_cuda_model *m, const float *dirs, size_t ent
     DITCH_CUDA(cudaSetDevice(dev->ordinal));
     const size_t H = m->cfg.hidden;
     DITCH_CUDA(m->dirs.reserve(entries * H * 4));
-    DITCH_CUDA(cudaMemcpy(m->dirs.ptr, dirs, entries * H * 4, cudaMemcpyHostToDevice));
+    DITCH_CUDA(cudaMemcpyAsync(m->dirs.ptr, dirs, entries * H * 4, cudaMemcpyHostToDevice, dev->stream));
+    DITCH_CUDA(cudaStreamSynchronize(dev->stream));
     m->h_dirs.assign(dirs, dirs + entries * H);
     m->dir_entries = (int)entries;
     return DITCH_CUDA_OK;
@@ -987,7 +988,8 @@ int ditch_cuda_rank_experts(ditch_cuda_model *m, size_t layer, const float *v, u
     REQUIRE(layer < (size_t)m->cfg.n_layers && m->layers[layer].moe, "layer %zu is not an MoE layer", layer);
     std::lock_guard<std::mutex> lk(m->dev->mu);
     DITCH_CUDA(cudaSetDevice(m->dev->ordinal));
-    DITCH_CUDA(cudaMemcpy(m->vtmp.ptr, v, (size_t)m->cfg.hidden * 4, cudaMemcpyHostToDevice));
+    DITCH_CUDA(cudaMemcpyAsync(m->vtmp.ptr, v, (size_t)m->cfg.hidden * 4, cudaMemcpyHostToDevice, m->dev->stream));
+    DITCH_CUDA(cudaStreamSynchronize(m->dev->stream));
     std::vector<float> s;
     int st = expert_scores(m, (int)layer, m->vtmp.as<float>(), s);
     if (st) return st;

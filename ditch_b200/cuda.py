@@ -386,20 +386,23 @@ class Tensor:
         self.scales_dtype, self.block_rows, self.block_cols, self.bits = scales_dtype, block_rows, block_cols, bits
 
     @staticmethod
-    def _ref(a):
-        """(pointer, bytes, on_device) of a numpy array or a CUDA torch tensor."""
+    def _ref(a, keep):
+        """(pointer, bytes, on_device) of a numpy array or a CUDA torch tensor;
+        the array whose memory the pointer names (a contiguous copy when `a`
+        is not contiguous) goes into `keep`, which outlives the C call."""
         if a is None:
             return None, 0, 0
         if hasattr(a, "data_ptr"):  # torch tensor on the device
+            keep.append(a)
             return a.data_ptr(), a.numel() * a.element_size(), 1 if a.is_cuda else 0
         a = np.ascontiguousarray(a)
+        keep.append(a)
         return a.ctypes.data, a.nbytes, 0
 
     def desc(self, keep):
-        d, db, dev = self._ref(self.data)
-        s, sb, _ = self._ref(self.scales)
-        z, zb, _ = self._ref(self.zeros)
-        keep += [self.data, self.scales, self.zeros]
+        d, db, dev = self._ref(self.data, keep)
+        s, sb, _ = self._ref(self.scales, keep)
+        z, zb, _ = self._ref(self.zeros, keep)
         name = self.name.encode()
         keep.append(name)
         return TensorDesc(name, FMT[self.fmt], self.slabs, self.rows, self.cols, d, db, s, sb, self.scales_dtype, z,
