@@ -13,6 +13,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -254,7 +255,8 @@ struct RawTensor {
 struct Checkpoint {
     std::vector<std::unique_ptr<Mapping>> maps;
     std::map<std::string, RawTensor> t;
-    JVal config;                        // config.json, or built from GGUF metadata
+    JVal config;                        // config.json, or the GGUF metadata
+    JVal embedded;                      // a GGUF file's embedded Hugging Face config, if any
     bool gguf = false;
     std::vector<std::vector<uint8_t>> owned;  // stacked experts, split or un-permuted rows
 
@@ -302,6 +304,15 @@ int read_safetensors(const std::string &path, Checkpoint &ck) {
         CK_REQUIRE(b <= en && data0 + en <= m->size, "%s: tensor %s outside the file", path.c_str(), kv.first.c_str());
         r.data = base + data0 + b;
         r.bytes = en - b;
+        if (const size_t es = dtype_size(r.dtype)) {
+            size_t elems = 1;
+            for (int64_t d : r.shape) {
+                CK_REQUIRE(d >= 0, "%s: tensor %s has a negative dimension", path.c_str(), kv.first.c_str());
+                elems *= (size_t)d;
+            }
+            CK_REQUIRE(elems * es == r.bytes, "%s: tensor %s holds %zu bytes, its %s shape needs %zu", path.c_str(),
+                       kv.first.c_str(), r.bytes, r.dtype.c_str(), elems * es);
+        }
         ck.t[kv.first] = r;
     }
     ck.maps.push_back(std::move(m));
@@ -473,6 +484,7 @@ struct Built {
     std::vector<ditch_cuda_tensor> tensors;
     std::vector<std::unique_ptr<std::string>> names;
     bool tied = false;
+    std::string family;          // model_type of the device path
     int br = 0, bc = 0;          // FP8 weight blocks
     int int_bits = 0, int_group = 0;
 };
@@ -486,97 +498,190 @@ const JVal *path_get(const JVal &v, std::initializer_list<const char *> keys) {
     return cur;
 }
 
-// Fields of src/model.zig's config for the families of the device path: HF
-// config.json (llama, mistral, qwen2, qwen3, qwen3_moe, mixtral) or GGUF
-// metadata (qwen2, llama).
-int build_config(const Checkpoint &ck, Built &b) {
+// The Hugging Face config.json fields of src/model.zig's parseConfig for the
+// families of the device path (llama, mistral, qwen2, qwen3, qwen3_moe,
+// mixtral), with the fp8 / compressed-tensors quantization_config of
+// src/dequant.zig:108-233.
+int hf_config(const JVal &j, Built &b) {
     ditch_cuda_model_config &c = b.cfg;
-    const JVal &j = ck.config;
-    if (ck.gguf) {
-        const std::string arch = j.string("general.architecture");
-        if (arch != "qwen2" && arch != "llama") {
-            set_error("GGUF architecture '%s' is not taken (qwen2 and llama are)", arch.c_str());
-            return DITCH_CUDA_UNSUPPORTED;
-        }
-        if (ck.find("rope_freqs.weight")) {
-            set_error("GGUF rope frequency factors (rope_freqs.weight) are not taken");
-            return DITCH_CUDA_UNSUPPORTED;
-        }
-        const std::string a = arch + ".";
-        c.n_layers = (int)j.number(a + "block_count", 0);
-        c.hidden = (int)j.number(a + "embedding_length", 0);
-        c.heads = (int)j.number(a + "attention.head_count", 0);
-        c.kv_heads = (int)j.number(a + "attention.head_count_kv", c.heads);
-        c.head_dim = c.heads ? (int)j.number(a + "attention.key_length", c.hidden / c.heads) : 0;
-        c.inter = (int)j.number(a + "feed_forward_length", 0);
-        c.eps = (float)j.number(a + "attention.layer_norm_rms_epsilon", 1e-6);
-        c.rope_theta = j.number(a + "rope.freq_base", 10000.0);
-        const RawTensor *emb = ck.find("token_embd.weight");
-        CK_REQUIRE(emb && emb->shape.size() == 2, "GGUF without token_embd.weight");
-        c.vocab = (int)emb->shape[0];
-        b.tied = ck.find("output.weight") == nullptr;
-    } else {
-        const std::string mt = j.string("model_type");
-        if (mt != "llama" && mt != "mistral" && mt != "qwen2" && mt != "qwen3" && mt != "qwen3_moe" && mt != "mixtral") {
-            set_error("model_type '%s' is not taken by the device path", mt.c_str());
-            return DITCH_CUDA_UNSUPPORTED;
-        }
-        c.n_layers = (int)j.number("num_hidden_layers", 0);
-        c.hidden = (int)j.number("hidden_size", 0);
-        c.heads = (int)j.number("num_attention_heads", 0);
-        c.kv_heads = (int)j.number("num_key_value_heads", c.heads);
-        const JVal *hd = j.get("head_dim");
-        c.head_dim = hd && hd->kind == JVal::Num ? (int)hd->num : (c.heads ? c.hidden / c.heads : 0);
-        c.inter = (int)j.number("intermediate_size", 0);
-        c.vocab = (int)j.number("vocab_size", 0);
-        c.eps = (float)j.number("rms_norm_eps", 1e-6);
-        c.rope_theta = j.number("rope_theta", 10000.0);
-        c.qk_norm = mt == "qwen3" || mt == "qwen3_moe";
-        b.tied = j.number("tie_word_embeddings", 0) != 0;
-        if (const JVal *rs = j.get("rope_scaling"))
-            if (rs->kind == JVal::Obj && (rs->string("rope_type") == "llama3" || rs->string("type") == "llama3")) {
+    const std::string mt = j.string("model_type");
+    if (mt != "llama" && mt != "mistral" && mt != "qwen2" && mt != "qwen3" && mt != "qwen3_moe" && mt != "mixtral") {
+        set_error("model_type '%s' is not taken by the device path", mt.c_str());
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    b.family = mt;
+    c.n_layers = (int)j.number("num_hidden_layers", 0);
+    c.hidden = (int)j.number("hidden_size", 0);
+    c.heads = (int)j.number("num_attention_heads", 0);
+    c.kv_heads = (int)j.number("num_key_value_heads", c.heads);
+    const JVal *hd = j.get("head_dim");
+    c.head_dim = hd && hd->kind == JVal::Num ? (int)hd->num : (c.heads ? c.hidden / c.heads : 0);
+    c.inter = (int)j.number("intermediate_size", 0);
+    c.vocab = (int)j.number("vocab_size", 0);
+    c.eps = (float)j.number("rms_norm_eps", 1e-6);
+    c.rope_theta = j.number("rope_theta", 10000.0);
+    c.qk_norm = mt == "qwen3" || mt == "qwen3_moe";
+    b.tied = j.number("tie_word_embeddings", 0) != 0;
+    if (const JVal *rs = j.get("rope_scaling"))
+        if (rs->kind == JVal::Obj) {
+            const std::string ty = rs->string("rope_type", rs->string("type"));
+            if (ty == "llama3") {
                 c.rope_scaling = 1;
                 c.rope_factor = rs->number("factor", 1.0);
                 c.rope_low_ff = rs->number("low_freq_factor", 1.0);
                 c.rope_high_ff = rs->number("high_freq_factor", 1.0);
                 c.rope_orig_max = rs->number("original_max_position_embeddings", 8192);
-            }
-        if (mt == "qwen3_moe") {
-            c.n_experts = (int)j.number("num_experts", 0);
-            c.top_k = (int)j.number("num_experts_per_tok", 0);
-            c.moe_inter = (int)j.number("moe_intermediate_size", 0);
-            c.norm_topk = j.number("norm_topk_prob", 1) != 0;
-            const int step = std::max(1, (int)j.number("decoder_sparse_step", 1));
-            std::vector<int> only;
-            if (const JVal *o = j.get("mlp_only_layers"))
-                for (const JVal &e : o->arr) only.push_back((int)e.num);
-            b.moe_layers.assign(c.n_layers, 0);
-            for (int i = 0; i < c.n_layers; i++)
-                b.moe_layers[i] = std::find(only.begin(), only.end(), i) == only.end() && (i + 1) % step == 0;
-        } else if (mt == "mixtral") {
-            c.n_experts = (int)j.number("num_local_experts", 0);
-            c.top_k = (int)j.number("num_experts_per_tok", 0);
-            c.moe_inter = c.inter;
-            c.norm_topk = 1;
-            b.moe_layers.assign(c.n_layers, 1);
-        }
-        if (const JVal *q = j.get("quantization_config")) {
-            const std::string qm = q->string("quant_method");
-            if (qm == "fp8") {
-                const JVal *bs = q->get("weight_block_size");
-                CK_REQUIRE(bs && bs->arr.size() == 2, "fp8 quantization_config without weight_block_size");
-                b.br = (int)bs->arr[0].num;
-                b.bc = (int)bs->arr[1].num;
-            } else if (qm == "compressed-tensors") {
-                const JVal *w = path_get(*q, {"config_groups", "group_0", "weights"});
-                CK_REQUIRE(w, "compressed-tensors config without config_groups.group_0.weights");
-                b.int_bits = (int)w->number("num_bits", 4);
-                b.int_group = (int)w->number("group_size", 128);
-            } else {
-                set_error("quant_method '%s' is not taken", qm.c_str());
+            } else if (!ty.empty() && ty != "default") {
+                set_error("rope_scaling type '%s' is not taken by the device path (llama3 is)", ty.c_str());
                 return DITCH_CUDA_UNSUPPORTED;
             }
         }
+    if (mt == "qwen3_moe") {
+        c.n_experts = (int)j.number("num_experts", 0);
+        c.top_k = (int)j.number("num_experts_per_tok", 0);
+        c.moe_inter = (int)j.number("moe_intermediate_size", 0);
+        c.norm_topk = j.number("norm_topk_prob", 1) != 0;
+        const int step = std::max(1, (int)j.number("decoder_sparse_step", 1));
+        std::vector<int> only;
+        if (const JVal *o = j.get("mlp_only_layers"))
+            for (const JVal &e : o->arr) only.push_back((int)e.num);
+        b.moe_layers.assign(std::max(c.n_layers, 0), 0);
+        for (int i = 0; i < c.n_layers; i++)
+            b.moe_layers[i] = std::find(only.begin(), only.end(), i) == only.end() && (i + 1) % step == 0;
+    } else if (mt == "mixtral") {
+        c.n_experts = (int)j.number("num_local_experts", 0);
+        c.top_k = (int)j.number("num_experts_per_tok", 0);
+        c.moe_inter = c.inter;
+        c.norm_topk = 1;
+        b.moe_layers.assign(std::max(c.n_layers, 0), 1);
+    }
+    if (const JVal *q = j.get("quantization_config")) {
+        const std::string qm = q->string("quant_method");
+        if (qm == "fp8") {
+            const JVal *bs = q->get("weight_block_size");
+            CK_REQUIRE(bs && bs->arr.size() == 2, "fp8 quantization_config without weight_block_size");
+            b.br = (int)bs->arr[0].num;
+            b.bc = (int)bs->arr[1].num;
+        } else if (qm == "compressed-tensors") {
+            const JVal *w = path_get(*q, {"config_groups", "group_0", "weights"});
+            CK_REQUIRE(w, "compressed-tensors config without config_groups.group_0.weights");
+            b.int_bits = (int)w->number("num_bits", 4);
+            b.int_group = (int)w->number("group_size", 128);
+        } else {
+            set_error("quant_method '%s' is not taken", qm.c_str());
+            return DITCH_CUDA_UNSUPPORTED;
+        }
+    }
+    return DITCH_CUDA_OK;
+}
+
+// The config ditch builds from GGUF metadata (src/gguf_model.zig:114-129
+// for the family, 282-372 for the fields): general.architecture as llama.cpp
+// names it, `llama` with experts being Mixtral; layers with no
+// ffn_gate_exps tensor are the dense ones.
+int gguf_config(const Checkpoint &ck, Built &b) {
+    ditch_cuda_model_config &c = b.cfg;
+    const JVal &j = ck.config;
+    const std::string arch = j.string("general.architecture");
+    const std::string a = arch + ".";
+    const int n_exp = (int)j.number(a + "expert_count", 0);
+    if (arch == "llama") b.family = n_exp > 0 ? "mixtral" : "llama";
+    else if (arch == "qwen2" || arch == "qwen3") b.family = arch;
+    else if (arch == "qwen3moe") b.family = "qwen3_moe";
+    else {
+        set_error("GGUF architecture '%s' is not taken (llama, qwen2, qwen3 and qwen3moe are)", arch.c_str());
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    CK_REQUIRE(n_exp == 0 || b.family == "mixtral" || b.family == "qwen3_moe", "GGUF %s with %d experts", arch.c_str(),
+               n_exp);
+    c.n_layers = (int)j.number(a + "block_count", 0);
+    c.hidden = (int)j.number(a + "embedding_length", 0);
+    c.heads = (int)j.number(a + "attention.head_count", 0);
+    c.kv_heads = (int)j.number(a + "attention.head_count_kv", c.heads);
+    c.head_dim = c.heads ? (int)j.number(a + "attention.key_length", c.hidden / c.heads) : 0;
+    c.inter = (int)j.number(a + "feed_forward_length", 4.0 * c.hidden);
+    c.eps = (float)j.number(a + "attention.layer_norm_rms_epsilon", 1e-6);
+    c.rope_theta = j.number(a + "rope.freq_base", 10000.0);
+    c.qk_norm = b.family == "qwen3" || b.family == "qwen3_moe";
+    const std::string scaling = j.string(a + "rope.scaling.type");
+    if (scaling == "linear") {
+        set_error("GGUF linear rope scaling is not taken by the device path");
+        return DITCH_CUDA_UNSUPPORTED;
+    }
+    const RawTensor *emb = ck.find("token_embd.weight");
+    CK_REQUIRE(emb && emb->shape.size() == 2, "GGUF without a 2-D token_embd.weight");
+    c.vocab = (int)emb->shape[0];
+    b.tied = ck.find("output.weight") == nullptr;
+    if (n_exp > 0) {
+        c.n_experts = n_exp;
+        c.top_k = (int)j.number(a + "expert_used_count", 2);
+        c.moe_inter = (int)j.number(a + "expert_feed_forward_length", c.inter);
+        c.norm_topk = 1;  // qwen3_moe and mixtral
+        b.moe_layers.assign(std::max(c.n_layers, 0), 0);
+        for (int i = 0; i < c.n_layers; i++)
+            b.moe_layers[i] = ck.find("blk." + std::to_string(i) + ".ffn_gate_exps.weight") != nullptr;
+    }
+    return DITCH_CUDA_OK;
+}
+
+// llama.cpp's per-frequency factors of a llama3 rope scaling, recomputed the
+// way ditch does to recognise the standard Llama 3 settings in a GGUF file's
+// rope_freqs.weight (src/gguf_model.zig:150-170, 301-325): low_freq_factor 1,
+// high_freq_factor 4, 8192 original positions, factor = the largest factor.
+bool llama3_factors_match(const float *f, size_t n, float theta, int head_dim, float factor) {
+    if ((size_t)head_dim / 2 != n) return false;
+    const float orig = 8192.f, low_ff = 1.f, high_ff = 4.f;
+    const float low_wavelen = orig / low_ff, high_wavelen = orig / high_ff;
+    for (size_t i = 0; i < n; i++) {
+        const double exponent = (double)(2 * i) / (double)head_dim;
+        const double freq = 1.0 / std::pow((double)theta, exponent);
+        const float wavelen = (float)(2.0 * M_PI / freq);
+        float e;
+        if (wavelen < high_wavelen) e = 1.f;
+        else if (wavelen > low_wavelen) e = factor;
+        else {
+            const float smooth = (orig / wavelen - low_ff) / (high_ff - low_ff);
+            e = 1.f / ((1.f - smooth) / factor + smooth);
+        }
+        if (std::fabs(e - f[i]) > 1e-4f * std::max(1.f, std::fabs(e))) return false;
+    }
+    return true;
+}
+
+int build_config(Checkpoint &ck, Built &b) {
+    ditch_cuda_model_config &c = b.cfg;
+    int s;
+    if (ck.gguf) {
+        // a GGUF file written by ditch's export carries the Hugging Face
+        // config itself (src/gguf_model.zig:25, 222-227)
+        const JVal *e = ck.config.get("ditch.hf.config_json");
+        if (e && e->kind == JVal::Str) {
+            CK_REQUIRE(parse_json(e->str.data(), e->str.size(), ck.embedded) && ck.embedded.kind == JVal::Obj,
+                       "GGUF: bad ditch.hf.config_json");
+            s = hf_config(ck.embedded, b);
+        } else {
+            s = gguf_config(ck, b);
+        }
+        if (s) return s;
+        if (const RawTensor *rf = ck.find("rope_freqs.weight"); rf && !c.rope_scaling) {
+            CK_REQUIRE(rf->dtype == "F32", "GGUF rope_freqs.weight of type %s", rf->dtype.c_str());
+            const float *f = reinterpret_cast<const float *>(rf->data);
+            const size_t n = rf->bytes / 4;
+            float factor = 1.f;
+            for (size_t i = 0; i < n; i++) factor = std::max(factor, f[i]);
+            if (!llama3_factors_match(f, n, (float)c.rope_theta, c.head_dim, factor)) {
+                set_error("GGUF rope frequency factors (rope_freqs.weight) other than Llama 3's standard scaling "
+                          "are not taken");
+                return DITCH_CUDA_UNSUPPORTED;
+            }
+            c.rope_scaling = 1;
+            c.rope_factor = factor;
+            c.rope_low_ff = 1.0;
+            c.rope_high_ff = 4.0;
+            c.rope_orig_max = 8192.0;
+        }
+    } else if ((s = hf_config(ck.config, b))) {
+        return s;
     }
     CK_REQUIRE(c.n_layers > 0 && c.hidden > 0 && c.heads > 0 && c.kv_heads > 0 && c.vocab > 0,
                "incomplete model config (layers %d, hidden %d, heads %d / %d, vocab %d)", c.n_layers, c.hidden, c.heads,
@@ -820,30 +925,47 @@ int build_tensors(Checkpoint &ck, Built &b) {
     Table tb{ck, b};
     int s;
     if (ck.gguf) {
-        const bool llama = ck.config.string("general.architecture") == "llama";
+        // llama.cpp names; q / k rows (and biases) of the llama family stored
+        // permuted (src/gguf_model.zig:141-143, 700-800)
+        const bool permuted = b.family == "llama" || b.family == "mistral" || b.family == "mixtral";
         if ((s = tb.dense("embed", "token_embd.weight", true))) return s;
         if ((s = tb.dense("final_norm", "output_norm.weight", true))) return s;
         if ((s = tb.dense("lm_head", b.tied ? "token_embd.weight" : "output.weight", true))) return s;
         for (int i = 0; i < c.n_layers; i++) {
             const std::string p = "blk." + std::to_string(i) + ".", L = "L" + std::to_string(i) + ".";
             const char *map[][2] = {{"input_norm", "attn_norm.weight"}, {"post_norm", "ffn_norm.weight"},
-                                    {"v", "attn_v.weight"},          {"o", "attn_output.weight"},
-                                    {"gate", "ffn_gate.weight"},     {"up", "ffn_up.weight"},
-                                    {"down", "ffn_down.weight"}};
+                                    {"v", "attn_v.weight"}, {"o", "attn_output.weight"}};
             for (auto &m : map)
                 if ((s = tb.dense(L + m[0], p + m[1], true))) return s;
-            for (const char *qk : {"q", "k"}) {
-                const std::string hf = p + "attn_" + qk + ".weight";
-                const RawTensor *r = ck.find(hf);
-                CK_REQUIRE(r, "tensor %s is missing", hf.c_str());
-                if (llama) {
-                    const RawTensor u = unpermute_rows(ck, *r, qk[0] == 'q' ? c.heads : c.kv_heads);
-                    ck.t[hf] = u;
+            for (const char *qk : {"q", "k"})
+                for (const char *kind : {"weight", "bias"}) {
+                    const std::string hf = p + "attn_" + qk + "." + kind;
+                    const RawTensor *r = ck.find(hf);
+                    const bool weight = kind[0] == 'w';
+                    CK_REQUIRE(r || !weight, "tensor %s is missing", hf.c_str());
+                    if (!r) continue;
+                    if (permuted) ck.t[hf] = unpermute_rows(ck, *r, qk[0] == 'q' ? c.heads : c.kv_heads);
+                    if ((s = tb.dense(L + qk + (weight ? "" : "b"), hf, true))) return s;
                 }
-                if ((s = tb.dense(L + qk, hf, true))) return s;
+            if ((s = tb.dense(L + "vb", p + "attn_v.bias", false))) return s;
+            if (c.qk_norm) {
+                if ((s = tb.dense(L + "q_norm", p + "attn_q_norm.weight", true))) return s;
+                if ((s = tb.dense(L + "k_norm", p + "attn_k_norm.weight", true))) return s;
             }
-            for (const char *bn : {"q", "k", "v"})
-                if ((s = tb.dense(L + bn + "b", p + "attn_" + bn + ".bias", false))) return s;
+            if (!b.moe_layers.empty() && b.moe_layers[i]) {
+                // experts stacked [E][rows][cols] in one tensor, the device's slab layout
+                if ((s = tb.dense(L + "router", p + "ffn_gate_inp.weight", true))) return s;
+                for (const char *e : {"gate", "up", "down"}) {
+                    const std::string hf = p + "ffn_" + e + "_exps.weight";
+                    const RawTensor *r = ck.find(hf);
+                    CK_REQUIRE(r && r->shape.size() == 3 && r->shape[0] == c.n_experts,
+                               "%s: 3-D [%d experts][rows][cols] expected", hf.c_str(), c.n_experts);
+                    if ((s = tb.entry(L + "e_" + e, hf, *r, (size_t)c.n_experts, nullptr))) return s;
+                }
+                continue;
+            }
+            for (const char *m : {"gate", "up", "down"})
+                if ((s = tb.dense(L + m, p + "ffn_" + m + ".weight", true))) return s;
         }
         return DITCH_CUDA_OK;
     }

@@ -18,12 +18,23 @@ import numpy as np
 import pytest
 
 import ditch_b200
-from checkpoint_files import fixture, write_gguf, write_gguf_fixture, write_hf_dir, write_llama_gguf
+from checkpoint_files import (fixture, llama3_factors, write_gguf, write_gguf_fixture, write_gguf_from_hf,
+                              write_gguf_with_package, write_hf_dir, write_llama_gguf)
 from golden_loader import Golden
 from oracle.model import flatten_batch
 
 HF_FAMILIES = ["qwen2", "qwen2_fp8", "qwen2_int4", "qwen3", "llama", "mixtral", "qwen3_moe", "qwen3_moe_fused",
                "qwen3_moe_fused_t"]
+
+# GGUF files converted from the bf16 Hugging Face fixtures (llama.cpp names,
+# permuted llama q / k, stacked experts)
+GGUF_FROM_HF = {"qwen2_bf16_gguf": "qwen2", "llama_gguf": "llama", "qwen3_gguf": "qwen3",
+                "qwen3_moe_gguf": "qwen3_moe", "mixtral_gguf": "mixtral"}
+FILES = HF_FAMILIES + ["qwen2_gguf", "qwen2_gguf_pkg", "llama_gguf_embedded", "llama_gguf_rope_freqs"] + list(GGUF_FROM_HF)
+# Llama 3's theta: with head_dim 8 its longest wavelength passes 8192 positions,
+# so the largest factor is the scaling factor itself (how ditch recognises it)
+LLAMA3_THETA = 500000.0
+ROPE_KEYS = ("rope_scaling", "rope_factor", "rope_low_ff", "rope_high_ff", "rope_orig_max")
 
 SPEC_KEYS = ["n_layers", "hidden", "heads", "kv_heads", "head_dim", "vocab", "qk_norm", "n_experts", "top_k",
              "moe_inter", "norm_topk", "moe_layers", "rope_scaling", "rope_factor", "rope_low_ff", "rope_high_ff",
@@ -31,19 +42,32 @@ SPEC_KEYS = ["n_layers", "hidden", "heads", "kv_heads", "head_dim", "vocab", "qk
 
 
 def checkpoint(tmp_path, family):
+    path = str(tmp_path / "model.gguf")
     if family == "qwen2_gguf":
-        return write_gguf_fixture(str(tmp_path / "model.gguf"), family)
-    if family == "llama_gguf":
-        return write_llama_gguf(str(tmp_path / "model.gguf"))
+        return write_gguf_fixture(path, family)
+    if family == "qwen2_gguf_pkg":
+        return write_gguf_with_package(path)
+    if family == "llama_gguf_embedded":  # the HF config (llama3 rope included) inside the file
+        return write_gguf_from_hf(path, "llama", embed_config=True, drop_rope_scaling=False)
+    if family == "llama_gguf_rope_freqs":  # Llama 3's standard scaling as llama.cpp's factors
+        c, _, _, _ = fixture("llama")
+        f = llama3_factors(LLAMA3_THETA, c["head_dim"], 8.0)
+        return write_llama_gguf(path, extra={"rope_freqs.weight": ("F32", f, [len(f)])}, rope_theta=LLAMA3_THETA)
+    if family in GGUF_FROM_HF:
+        return write_gguf_from_hf(path, GGUF_FROM_HF[family])
     return write_hf_dir(str(tmp_path / family), family)
 
 
 def golden_spec(family):
-    g = Golden("llama" if family == "llama_gguf" else family)
+    base = {"qwen2_gguf_pkg": "qwen2_gguf", "llama_gguf_embedded": "llama", "llama_gguf_rope_freqs": "llama"}
+    g = Golden(base.get(family) or GGUF_FROM_HF.get(family) or family)
     s = dict(g.spec)
-    if family == "llama_gguf":  # GGUF carries no llama3 rope factors
-        for k in ("rope_scaling", "rope_factor", "rope_low_ff", "rope_high_ff", "rope_orig_max"):
+    if family in GGUF_FROM_HF:  # GGUF metadata carries no llama3 rope keys
+        for k in ROPE_KEYS:
             s.pop(k, None)
+    if family == "llama_gguf_rope_freqs":
+        s.update(rope_scaling=1, rope_factor=8.0, rope_low_ff=1.0, rope_high_ff=4.0, rope_orig_max=8192.0,
+                 rope_theta=LLAMA3_THETA)
     return g, s
 
 
@@ -58,7 +82,7 @@ def check_spec(got, want):
     assert got["rope_theta"] == pytest.approx(want["rope_theta"], rel=1e-6)
 
 
-@pytest.mark.parametrize("family", HF_FAMILIES + ["qwen2_gguf", "llama_gguf"])
+@pytest.mark.parametrize("family", FILES)
 def test_inspect_matches_fixture_spec(tmp_path, family):
     path = checkpoint(tmp_path, family)
     spec, n = ditch_b200.inspect_checkpoint(path)
@@ -68,6 +92,24 @@ def test_inspect_matches_fixture_spec(tmp_path, family):
     n_want = sum(1 for c, hf in g.hf_names().items() if g.has(hf))
     n_want += 3 * sum(1 for x in (want.get("moe_layers") or []) if x)
     assert n == n_want
+
+
+def test_own_gguf_writer_reads_back_with_the_package(tmp_path):
+    """The test's GGUF writer checked by the `gguf` package's reader: names,
+    ggml types, logical shapes and bytes."""
+    gguf = pytest.importorskip("gguf")
+    path = write_gguf_fixture(str(tmp_path / "m.gguf"), "qwen2_gguf")
+    _, dtypes, shapes, raw = fixture("qwen2_gguf")
+    r = gguf.GGUFReader(path)
+    assert str(bytes(r.fields["general.architecture"].parts[-1]), "utf8") == "qwen2"
+    seen = {}
+    for t in r.tensors:
+        seen[t.name] = t
+        assert t.tensor_type.name == {"F16": "F16", "F32": "F32", "GGML_Q8_0": "Q8_0"}[dtypes[t.name]]
+        want = shapes.get(t.name) or list(raw[t.name].shape)
+        assert list(reversed([int(x) for x in t.shape])) == list(want)
+        assert np.asarray(t.data).tobytes() == raw[t.name].tobytes()
+    assert set(seen) == set(raw)
 
 
 def test_hf_dir_with_shards(tmp_path):
@@ -127,15 +169,35 @@ def test_refusals(tmp_path):
         ditch_b200.inspect_checkpoint(str(q))
 
 
-def test_gguf_rope_freqs_refused(tmp_path):
-    """llama3-style rope factors in a GGUF file (rope_freqs.weight) are refused
-    rather than silently dropped."""
-    config, _, _, _ = fixture("llama")
-    half = config["hidden_size"] // config["num_attention_heads"] // 2
-    path = write_llama_gguf(str(tmp_path / "f.gguf"),
+def test_gguf_rope_freqs(tmp_path):
+    """rope_freqs.weight equal to Llama 3's standard scaling (low 1, high 4,
+    8192 positions, any factor) becomes that scaling, as ditch recognises it;
+    any other factors are refused rather than dropped."""
+    c, _, _, _ = fixture("llama")
+    half = c["head_dim"] // 2
+    ones = write_llama_gguf(str(tmp_path / "ones.gguf"),
                             extra={"rope_freqs.weight": ("F32", np.ones(half, np.float32), [half])})
+    spec, _ = ditch_b200.inspect_checkpoint(ones)
+    assert spec["rope_scaling"] == 1 and spec["rope_factor"] == 1.0  # factor 1: plain rope
+    f = llama3_factors(LLAMA3_THETA, c["head_dim"], 32.0)
+    std = write_llama_gguf(str(tmp_path / "std.gguf"), extra={"rope_freqs.weight": ("F32", f, [half])},
+                           rope_theta=LLAMA3_THETA)
+    spec, _ = ditch_b200.inspect_checkpoint(std)
+    assert (spec["rope_scaling"], spec["rope_factor"], spec["rope_low_ff"], spec["rope_high_ff"],
+            spec["rope_orig_max"]) == (1, 32.0, 1.0, 4.0, 8192.0)
+    odd = np.arange(1, half + 1, dtype=np.float32)
+    path = write_llama_gguf(str(tmp_path / "f.gguf"), extra={"rope_freqs.weight": ("F32", odd, [half])})
     with pytest.raises(ditch_b200.Unsupported, match="rope_freqs"):
         ditch_b200.inspect_checkpoint(path)
+
+
+def test_unsupported_rope_scaling_refused(tmp_path):
+    config, _, _, _ = fixture("qwen2")
+    d = write_hf_dir(str(tmp_path / "dyn"), "qwen2")
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(dict(config, rope_scaling={"rope_type": "dynamic", "factor": 2.0}), f)
+    with pytest.raises(ditch_b200.Unsupported, match="dynamic"):
+        ditch_b200.inspect_checkpoint(d)
 
 
 def test_safetensors_header_is_parsed_not_trusted(tmp_path):
@@ -152,7 +214,7 @@ def test_safetensors_header_is_parsed_not_trusted(tmp_path):
     hdr = json.dumps({"model.embed_tokens.weight": {"dtype": "BF16", "shape": [4, 4], "data_offsets": [0, 30]}}).encode()
     with open(d / "model.safetensors", "wb") as f:
         f.write(struct.pack("<Q", len(hdr)) + hdr + bytes(30))
-    with pytest.raises(ditch_b200.DitchCudaError):
+    with pytest.raises(ditch_b200.DitchCudaError, match="holds 30 bytes"):
         ditch_b200.inspect_checkpoint(str(d))
 
 
@@ -164,7 +226,7 @@ def _logits(m, prompts):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("family", HF_FAMILIES + ["qwen2_gguf", "llama_gguf"])
+@pytest.mark.parametrize("family", FILES)
 def test_load_checkpoint_matches_tensor_table(device, tmp_path, family):
     """The model loaded from the file computes bit-identical logits to the one
     built from the fixture's own tensor table (which test_gpu_model checks
