@@ -5,6 +5,6 @@ path, exposed through the C ABI in include/ditch_cuda.h (libditch_cuda.so).
 ABI. Importing it requires the built library; there is no CPU fallback.
 """
 from .cuda import (DTYPE, FMT, DitchCudaError, Device, Group, Model, Params, Tensor, Unsupported,  # noqa: F401
-                   Weight, inspect_checkpoint, lib)
+                   Weight, export_config, inspect_checkpoint, lib)
 
 __version__ = "0.1.0"

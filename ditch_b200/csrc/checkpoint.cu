@@ -21,44 +21,12 @@
 #include <string>
 #include <vector>
 
-#include "model.cuh"
+#include "checkpoint.cuh"
 
-namespace {
+namespace ditch {
+namespace ckpt {
 
 using namespace ditch;
-
-#define CK_REQUIRE(cond, ...)          \
-    do {                               \
-        if (!(cond)) {                 \
-            set_error(__VA_ARGS__);    \
-            return DITCH_CUDA_INVALID; \
-        }                              \
-    } while (0)
-
-// ---- a small JSON reader (config.json, safetensors headers) ----------------
-struct JVal {
-    enum Kind { Null, Bool, Num, Str, Arr, Obj } kind = Null;
-    bool b = false;
-    double num = 0.0;
-    std::string str;
-    std::vector<JVal> arr;
-    std::vector<std::pair<std::string, JVal>> obj;
-
-    const JVal *get(const std::string &k) const {
-        if (kind != Obj) return nullptr;
-        for (const auto &kv : obj)
-            if (kv.first == k) return &kv.second;
-        return nullptr;
-    }
-    double number(const std::string &k, double dflt) const {
-        const JVal *v = get(k);
-        return v && v->kind == Num ? v->num : v && v->kind == Bool ? (v->b ? 1.0 : 0.0) : dflt;
-    }
-    std::string string(const std::string &k, const std::string &dflt = "") const {
-        const JVal *v = get(k);
-        return v && v->kind == Str ? v->str : dflt;
-    }
-};
 
 struct JParser {
     const char *p, *end;
@@ -203,14 +171,6 @@ bool parse_json(const char *s, size_t n, JVal &out) {
 }
 
 // ---- read-only file mappings -----------------------------------------------
-struct Mapping {
-    void *base = nullptr;
-    size_t size = 0;
-    ~Mapping() {
-        if (base && base != MAP_FAILED) munmap(base, size);
-    }
-};
-
 int map_file(const std::string &path, std::unique_ptr<Mapping> &out) {
     const int fd = open(path.c_str(), O_RDONLY);
     CK_REQUIRE(fd >= 0, "cannot open %s", path.c_str());
@@ -240,36 +200,13 @@ bool read_text(const std::string &path, std::string &out) {
     return true;
 }
 
-}  // namespace
+}  // namespace ckpt
+}  // namespace ditch
 
-namespace {
+namespace ditch {
+namespace ckpt {
 
 // ---- the tensors of a checkpoint, as stored -------------------------------
-struct RawTensor {
-    std::string dtype;            // safetensors dtype ("BF16", "F8_E4M3", ...) or "GGML_Q8_0" / "GGML_Q4_K"
-    std::vector<int64_t> shape;   // rows first (GGUF dims reversed)
-    const uint8_t *data = nullptr;
-    size_t bytes = 0;
-};
-
-struct Checkpoint {
-    std::vector<std::unique_ptr<Mapping>> maps;
-    std::map<std::string, RawTensor> t;
-    JVal config;                        // config.json, or the GGUF metadata
-    JVal embedded;                      // a GGUF file's embedded Hugging Face config, if any
-    bool gguf = false;
-    std::vector<std::vector<uint8_t>> owned;  // stacked experts, split or un-permuted rows
-
-    const RawTensor *find(const std::string &n) const {
-        auto it = t.find(n);
-        return it == t.end() ? nullptr : &it->second;
-    }
-    uint8_t *alloc(size_t n) {
-        owned.emplace_back(n);
-        return owned.back().data();
-    }
-};
-
 size_t dtype_size(const std::string &d) {
     if (d == "BF16" || d == "F16" || d == "I16" || d == "U16") return 2;
     if (d == "F32" || d == "I32" || d == "U32") return 4;
@@ -320,6 +257,9 @@ int read_safetensors(const std::string &path, Checkpoint &ck) {
 }
 
 int read_hf_dir(const std::string &dir, Checkpoint &ck) {
+    // an export that did not finish leaves its marker (src/model.zig:866-869)
+    CK_REQUIRE(access((dir + "/.incomplete").c_str(), F_OK) != 0,
+               "%s contains .incomplete: the export did not finish; refusing to load it", dir.c_str());
     std::string text;
     CK_REQUIRE(read_text(dir + "/config.json", text), "%s: no config.json", dir.c_str());
     CK_REQUIRE(parse_json(text.data(), text.size(), ck.config) && ck.config.kind == JVal::Obj,
@@ -473,22 +413,13 @@ int read_gguf(const std::string &path, Checkpoint &ck) {
     return DITCH_CUDA_OK;
 }
 
-}  // namespace
+}  // namespace ckpt
+}  // namespace ditch
 
-namespace {
+namespace ditch {
+namespace ckpt {
 
 // ---- the model config ------------------------------------------------------
-struct Built {
-    ditch_cuda_model_config cfg{};
-    std::vector<uint8_t> moe_layers;
-    std::vector<ditch_cuda_tensor> tensors;
-    std::vector<std::unique_ptr<std::string>> names;
-    bool tied = false;
-    std::string family;          // model_type of the device path
-    int br = 0, bc = 0;          // FP8 weight blocks
-    int int_bits = 0, int_group = 0;
-};
-
 const JVal *path_get(const JVal &v, std::initializer_list<const char *> keys) {
     const JVal *cur = &v;
     for (const char *k : keys) {
@@ -690,9 +621,11 @@ int build_config(Checkpoint &ck, Built &b) {
     return DITCH_CUDA_OK;
 }
 
-}  // namespace
+}  // namespace ckpt
+}  // namespace ditch
 
-namespace {
+namespace ditch {
+namespace ckpt {
 
 // ---- the tensor table --------------------------------------------------------
 struct Table {
@@ -870,9 +803,11 @@ struct Table {
     }
 };
 
-}  // namespace
+}  // namespace ckpt
+}  // namespace ditch
 
-namespace {
+namespace ditch {
+namespace ckpt {
 
 // Rows of a llama GGUF q / k weight back in the Hugging Face order: the
 // converter stores head h's rows as (i, half) pairs, ditch's model reads
@@ -1036,7 +971,10 @@ int open_checkpoint(const char *path, Checkpoint &ck, Built &b) {
     return build_tensors(ck, b);
 }
 
-}  // namespace
+}  // namespace ckpt
+}  // namespace ditch
+
+using namespace ditch::ckpt;
 
 extern "C" {
 

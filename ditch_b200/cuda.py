@@ -102,6 +102,10 @@ SIGNATURES = {
     "ditch_cuda_checkpoint_inspect": (C.c_int, [C.c_char_p, C.POINTER(ModelConfig), C.POINTER(sz),
                                                 C.POINTER(C.c_uint8), sz]),
     "ditch_cuda_model_bytes": (C.c_uint64, [vp]),
+    "ditch_cuda_export_checkpoint": (C.c_int, [vp, C.c_char_p, C.c_char_p, C.c_int, C.c_uint64]),
+    "ditch_cuda_export_config": (C.c_int, [C.c_char_p, sz, C.c_int, C.c_int, C.c_char_p, sz, C.POINTER(sz)]),
+    "ditch_cuda_model_delta": (C.c_int, [vp, sz, C.c_int, sz, f32p, f32p, sz, C.POINTER(sz)]),
+    "ditch_cuda_round_f32": (C.c_int, [vp, f32p, sz, C.c_int, u16p]),
     "ditch_cuda_forward": (C.c_int, [vp, u32p, u32p, u32p, sz, C.POINTER(sz), sz, f32p, C.POINTER(sz), sz, f32p]),
     "ditch_cuda_generate": (C.c_int, [vp, u32p, C.POINTER(sz), sz, sz, u32p, sz, u32p, C.POINTER(sz)]),
     "ditch_cuda_set_row_normalization": (C.c_int, [vp, C.c_int, sz, C.c_uint64]),
@@ -343,6 +347,13 @@ class Device:
         """Staged GEMMs keep their weight's decoded bf16 copy (default on)."""
         check(lib().ditch_cuda_set_decode_cache(self.h, int(bool(on))))
 
+    def round_f32(self, values, dtype):
+        """The export's rounding of f32 values to "bf16" or "f16" bits."""
+        v = np.ascontiguousarray(values, np.float32).reshape(-1)
+        out = np.zeros(v.size, np.uint16)
+        check(lib().ditch_cuda_round_f32(self.h, _p(v, f32p), v.size, DTYPE[dtype], _p(out, u16p)))
+        return out.reshape(np.shape(values))
+
     def set_deterministic(self, on):
         """K splits summed in a fixed order instead of atomically (default off)."""
         check(lib().ditch_cuda_set_deterministic(self.h, int(bool(on))))
@@ -496,6 +507,20 @@ def inspect_checkpoint(path):
     return spec, n.value
 
 
+def export_config(text, dtype=None, strip_quantization_config=False):
+    """The config.json text an export writes (ditch_cuda_export_config)."""
+    raw = text.encode()
+    n = sz(0)
+    code = -1 if dtype is None else DTYPE[dtype]
+    check(lib().ditch_cuda_export_config(raw, len(raw), code, int(strip_quantization_config), None, 0, C.byref(n)))
+    buf = C.create_string_buffer(n.value + 1)
+    check(lib().ditch_cuda_export_config(raw, len(raw), code, int(strip_quantization_config), buf, n.value, C.byref(n)))
+    return buf.raw[: n.value].decode()
+
+
+COMPONENTS = {"attn_o_proj": 0, "mlp_down_proj": 1, "expert_down_proj": 2}
+
+
 class Model:
     """A model resident in HBM (the coarse C-ABI entries)."""
 
@@ -509,8 +534,36 @@ class Model:
         h = vp()
         check(lib().ditch_cuda_model_load_checkpoint(device.h, str(path).encode(), int(max_seq), C.byref(h)))
         self.h = h
+        self.source = str(path)
         device._adopt(self)
         return self
+
+    def export(self, out_dir, source=None, dtype=None, max_shard_bytes=0):
+        """Writes the checkpoint with this model's deltas merged
+        (ditch_cuda_export_checkpoint); `source` defaults to the directory
+        the model was loaded from, `dtype` ("f32", "f16", "bf16") to each
+        tensor's own."""
+        src = source or getattr(self, "source", None)
+        if src is None:
+            raise ValueError("no source checkpoint: pass source=")
+        check(lib().ditch_cuda_export_checkpoint(self.h, str(src).encode(), str(out_dir).encode(),
+                                                 -1 if dtype is None else DTYPE[dtype], int(max_shard_bytes)))
+
+    def delta(self, layer, component, expert=0):
+        """(a [rank][cols], b [rows][rank]) of an edited weight, or None."""
+        s = self.spec
+        comp = COMPONENTS[component]
+        cols = {0: s["heads"] * s["head_dim"], 1: s.get("inter", 0), 2: s.get("moe_inter", 0)}[comp]
+        a = np.zeros((4, max(cols, 1)), np.float32)
+        b = np.zeros((s["hidden"], 4), np.float32)
+        r = sz(0)
+        check(lib().ditch_cuda_model_delta(self.h, layer, comp, expert, _p(a, f32p), _p(b, f32p), 4, C.byref(r)))
+        if r.value == 0:
+            return None
+        k = r.value
+        a = np.ascontiguousarray(a.reshape(-1)[: k * cols].reshape(k, cols))
+        b = np.ascontiguousarray(b.reshape(-1)[: s["hidden"] * k].reshape(s["hidden"], k))
+        return a, b
 
     def __init__(self, device, spec, tensors, max_seq=4096, ep_rank=0, ep_world=1, tp_rank=0, tp_world=1):
         self.dev = device

@@ -195,9 +195,13 @@ void ditch_cuda_model_free(ditch_cuda_model *m);
  * mixtral; bf16 / f16 / f32, FP8 block-scaled with weight_block_size, or
  * compressed-tensors pack-quantized INT without g_idx; routed experts one
  * tensor per expert, mixtral's w1 / w3 / w2, or fused gate_up_proj /
- * down_proj in either orientation) or a GGUF file (qwen2 or llama; F32, F16,
- * BF16, Q8_0, Q4_K; llama's permuted q / k rows restored). Quantised groups
- * reach the device raw. The files are memory-mapped during the call.
+ * down_proj in either orientation) or a GGUF file (general.architecture
+ * llama, with experts mixtral, qwen2, qwen3 or qwen3moe; F32, F16, BF16, Q8_0,
+ * Q4_K; llama's permuted q / k rows and biases restored; stacked ffn_*_exps
+ * experts; an embedded ditch.hf.config_json; rope_freqs.weight only as Llama
+ * 3's standard scaling). Quantised groups reach the device raw. The files
+ * are memory-mapped during the call. A directory holding an export's
+ * .incomplete marker is refused.
  * max_seq: the RoPE table rows (0 = 4096). Anything else returns
  * DITCH_CUDA_UNSUPPORTED with the reason in ditch_cuda_last_error(). */
 int ditch_cuda_model_load_checkpoint(ditch_cuda_device *dev, const char *path, int max_seq, ditch_cuda_model **out);
@@ -208,6 +212,36 @@ int ditch_cuda_checkpoint_inspect(const char *path, ditch_cuda_model_config *cfg
                                   uint8_t *moe_layers, size_t moe_layers_len);
 /* Device bytes the resident model holds. */
 uint64_t ditch_cuda_model_bytes(const ditch_cuda_model *m);
+
+/* Export (src/export.zig saveModel): the Hugging Face directory src_dir the
+ * model was loaded from, written to out_dir with the model's deltas merged on
+ * the device (W' = W + B A, rank terms added in order; fused expert tensors
+ * per expert slice, src/moe.zig:368-390). FP8 and pack-quantized groups are
+ * written decoded (bf16, config.json without quantization_config); float
+ * tensors keep their dtype. export_dtype: DITCH_DTYPE_F32 / F16 / BF16 for
+ * every float tensor (config.json's dtype / torch_dtype then name it), or -1.
+ * Shards of at most max_shard_bytes (0 = 5 GiB) with
+ * model.safetensors.index.json when there are several; tokenizer and side
+ * files copied; a .incomplete marker exists until everything is written.
+ * Tensor- or expert-parallel models and GGUF sources return
+ * DITCH_CUDA_UNSUPPORTED. */
+int ditch_cuda_export_checkpoint(ditch_cuda_model *m, const char *src_dir, const char *out_dir, int export_dtype,
+                                 uint64_t max_shard_bytes);
+/* The config.json text an export writes (no device): quantization_config and
+ * expert_dtype removed when strip_quantization_config (dequant.zig:1195-1219),
+ * float dtype names replaced by export_dtype's when it is not -1
+ * (export.zig:239-283). out receives min(cap, *out_len) bytes. */
+int ditch_cuda_export_config(const char *json, size_t len, int export_dtype, int strip_quantization_config, char *out,
+                             size_t cap, size_t *out_len);
+/* The delta the last edit left on a weight: component 0 = attention output,
+ * 1 = MLP down, 2 = routed expert `expert`'s down projection. *rank = 0 when
+ * the weight is not edited; else a [rank][cols] and b [rows][rank] (f32) are
+ * filled (max_rank at least *rank). */
+int ditch_cuda_model_delta(ditch_cuda_model *m, size_t layer, int component, size_t expert, float *a, float *b,
+                           size_t max_rank, size_t *rank);
+/* The export's rounding of f32 values (host buffers) to bf16
+ * (src/tensor.zig:423-430) or IEEE f16 (round to nearest even). */
+int ditch_cuda_round_f32(ditch_cuda_device *dev, const float *src, size_t n, int dtype, uint16_t *dst);
 
 /* model.forward (src/model.zig:4619) with ForwardOptions (3136-3144): rows
  * {b, pos} per token (every prompt's rows contiguous, positions 0..len-1);

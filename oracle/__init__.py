@@ -467,3 +467,32 @@ def compute_delta_full(w, v, lam, lora_rank=3, seed=0, omega=None):
 def materialize_rank(w, a, b):
     """W + b a (a [r][cols], b [rows][r]) in f32."""
     return (f32(w) + f32(b) @ f32(a)).astype(np.float32)
+
+
+def export_merge_rows(w, a, b):
+    """src/export.zig:108-112 (tensor.axpy per rank term, src/tensor.zig:561-570):
+    every row of W (f32 [rows][cols]) gets b[row][k] * a[k] added for k in
+    order, each product rounded to f32 before the add."""
+    y = np.array(w, np.float32, copy=True)
+    a, b = f32(a).reshape(-1, y.shape[1]), f32(b).reshape(y.shape[0], -1)
+    for k in range(a.shape[0]):
+        y = y + b[:, k:k + 1] * a[k][None, :]
+    return y
+
+
+def export_merge_cols(w, a, b):
+    """The transposed merge (src/export.zig:114-122, src/moe.zig:380-387):
+    W [in][out] gets, at (j, i), the rank terms b[i][k] * a[k][j] summed
+    first (in k order, rounded per step) and then added."""
+    y = np.array(w, np.float32, copy=True)
+    a, b = f32(a).reshape(-1, y.shape[0]), f32(b).reshape(y.shape[1], -1)
+    acc = np.zeros_like(y)
+    for k in range(a.shape[0]):
+        acc = acc + a[k][:, None] * b[:, k][None, :]
+    return y + acc
+
+
+def f32_to_f16_bits(x):
+    """IEEE binary16 round to nearest even (Zig's @floatCast, src/tensor.zig:437-440)."""
+    with np.errstate(over="ignore"):  # overflow to infinity is the rule
+        return np.ascontiguousarray(x, np.float32).astype(np.float16).view(np.uint16)
