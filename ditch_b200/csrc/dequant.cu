@@ -261,6 +261,46 @@ __global__ void k_repack_q8_0(const uint8_t *src, long long blocks, int8_t *code
     }
 }
 
+// Q4_K super-blocks (f16 d, f16 dmin, 12 bytes of 6-bit scales / mins, 128
+// bytes of nibbles; src/quant.zig:140-173) to the GEMM's layout: 4-bit codes
+// in element order (byte i: elements 2i, 2i + 1, low nibble first) and per
+// 32-element sub-block the f32 pair (d * scale, dmin * min), both products
+// exact. One thread per output byte; sub-block is = e / 32 of the super-block.
+__global__ void k_repack_q4_k(const uint8_t *src, long long n_bytes, uint8_t *codes, float2 *dm) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_bytes;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long b = i / 128;
+        const int e = (int)(i % 128) * 2;  // first element of the pair in the super-block
+        const uint8_t *blk = src + b * 144, *sc = blk + 4, *qs = blk + 16;
+        const int grp = e / 64, l = e % 32;
+        const bool high = (e % 64) >= 32;
+        const uint8_t b0 = qs[grp * 32 + l], b1 = qs[grp * 32 + l + 1];
+        codes[i] = high ? (uint8_t)((b0 >> 4) | (b1 & 0xf0)) : (uint8_t)((b0 & 0xf) | ((b1 & 0xf) << 4));
+        if ((e & 31) == 0) {
+            const int is = e / 32;
+            uint32_t s, m;
+            if (is < 4) {
+                s = sc[is] & 63;
+                m = sc[is + 4] & 63;
+            } else {
+                s = (sc[is + 4] & 0xf) | ((sc[is - 4] >> 6) << 4);
+                m = (sc[is + 4] >> 4) | ((sc[is] >> 6) << 4);
+            }
+            const float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+            dm[b * 8 + is] = make_float2(__fmul_rn(d, (float)s), __fmul_rn(dmin, (float)m));
+        }
+    }
+}
+
+// The repacked Q4_K values as f32 (d1 * q - m1, src/quant.zig:148-173).
+__global__ void k_q4_k_f32(const uint8_t *codes, const float2 *dm, long long n, float *out) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const uint32_t q = (codes[i / 2] >> (4 * (i & 1))) & 0xf;
+        const float2 v = dm[i / 32];
+        out[i] = __fsub_rn(__fmul_rn(v.x, (float)q), v.y);
+    }
+}
+
 // The repacked Q8_0 values as f32 (d * q, exact as src/quant.zig:81-85).
 __global__ void k_q8_0_f32(const int8_t *codes, const float *scales, long long n, float *out) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
@@ -303,6 +343,19 @@ __global__ void k_f16_to_f32(const uint16_t *src, float *dst, long long n) {
 cudaError_t repack_q8_0(const uint8_t *src, long long blocks, int8_t *codes, float *scales, cudaStream_t st) {
     if (blocks <= 0) return cudaSuccess;
     k_repack_q8_0<<<blocks_for(blocks, 1), kThreads, 0, st>>>(src, blocks, codes, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t repack_q4_k(const uint8_t *src, long long super_blocks, uint8_t *codes, float *dm, cudaStream_t st) {
+    if (super_blocks <= 0) return cudaSuccess;
+    k_repack_q4_k<<<blocks_for(super_blocks * 128, 1), kThreads, 0, st>>>(src, super_blocks * 128, codes,
+                                                                         reinterpret_cast<float2 *>(dm));
+    return cudaGetLastError();
+}
+
+cudaError_t q4_k_f32(const uint8_t *codes, const float *dm, long long n, float *out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_q4_k_f32<<<blocks_for(n, 4), kThreads, 0, st>>>(codes, reinterpret_cast<const float2 *>(dm), n, out);
     return cudaGetLastError();
 }
 

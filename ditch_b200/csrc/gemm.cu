@@ -47,7 +47,7 @@ struct Cfg {
     // raw weight tile of one k-tile: 128 rows x 64 bytes (8-bit codes, TMA
     // 64-byte swizzle) or x 32 bytes (4-bit codes, no swizzle)
     static constexpr int kRawBytes = (FMT == kFmtFp8 || FMT == kFmtQ8_0)  ? BM * BK
-                                     : (FMT == kFmtMxfp4 || FMT == kFmtInt4) ? BM * BK / 2
+                                     : (FMT == kFmtMxfp4 || FMT == kFmtInt4 || FMT == kFmtQ4K) ? BM * BK / 2
                                                                              : 0;
     static constexpr int kStageBytes = kNA * kABytes + kBBytes;
     static constexpr int kRawStageBytes = kNA * kRawBytes;
@@ -380,14 +380,44 @@ __device__ __forceinline__ void xform_q8_0(const uint8_t *raw, uint8_t *atile, i
     }
 }
 
+// A pair of Q4_K codes to bf16x2 of bf16(d1 * q - m1): the ggml value in f32
+// (src/quant.zig:148-173; d1 = d * scale and m1 = dmin * min were formed at
+// repack, every product here is exact), rounded to bf16.
+__device__ __forceinline__ uint32_t q4k_pair(uint32_t lo, uint32_t hi, float d1, float m1) {
+    return pack_bf16x2(__fsub_rn(__fmul_rn(d1, (float)lo), m1), __fsub_rn(__fmul_rn(d1, (float)hi), m1));
+}
+
+// GGUF Q4_K repacked at load: 4-bit codes [rows][cols / 2] in element order
+// (low nibble first) and (d1, m1) f32 pairs per 32-element sub-block
+// [rows][cols / 32]. Raw tile as MXFP4; half h is one sub-block.
+__device__ __forceinline__ void xform_q4k(const uint8_t *raw, uint8_t *atile, int r, int h, float d1, float m1) {
+    uint32_t words[8 / kParts];
+    if constexpr (kParts == 2) {
+        const uint4 q = *reinterpret_cast<const uint4 *>(raw + r * 32 + h * 16);
+        words[0] = q.x, words[1] = q.y, words[2] = q.z, words[3] = q.w;
+    } else {
+        const uint2 q = *reinterpret_cast<const uint2 *>(raw + r * 32 + h * 8);
+        words[0] = q.x, words[1] = q.y;
+    }
+#pragma unroll
+    for (int jj = 0; jj < 8 / kParts; jj++) {
+        const uint32_t w = words[jj];
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[e] = q4k_pair((w >> (8 * e)) & 0xf, (w >> (8 * e + 4)) & 0xf, d1, m1);
+        put_chunk(atile, r, (8 / kParts) * h + jj, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+}
+
 // The side data of half h of one row's k-tile at k0, loaded ahead of the
 // barrier waits: the scale (FP8 one_scale, MXFP4, Q8_0, INT4) and the INT4
 // zero point.
 template <int FMT>
 __device__ __forceinline__ void load_side(const GemmParams &p, int vrow, const float *srow, bool one_scale, int k0,
-                                          int h, float &s, int &zq) {
+                                          int h, float &s, int &zq, float &mn) {
     s = 0.0f;
     zq = 8;
+    mn = 0.0f;
     if (FMT == kFmtFp8) {
         if (one_scale) s = __ldg(srow + k0 / p.blk_cols);
     } else if (FMT == kFmtMxfp4) {
@@ -400,6 +430,12 @@ __device__ __forceinline__ void load_side(const GemmParams &p, int vrow, const f
         const int groups = p.scale_cols, g = k0 / p.blk_cols;
         if (k0 < p.k) s = __ldg(p.scales + (long long)vrow * groups + g);
         if (p.zeros) zq = (__ldg(p.zeros + (long long)(vrow >> 3) * groups + g) >> ((vrow & 7) * 4)) & 0xf;
+    } else if (FMT == kFmtQ4K) {
+        const int blk = (k0 >> 5) + h * 2 / kParts;  // the 32-element sub-block of part h
+        if (blk * 32 < p.k) {
+            const float2 dm = __ldg(reinterpret_cast<const float2 *>(p.scales) + (long long)vrow * p.scale_cols + blk);
+            s = dm.x, mn = dm.y;
+        }
     }
 }
 
@@ -452,6 +488,16 @@ __global__ void __launch_bounds__(256) k_stage_decode(const StageArgs a) {
                 const uint32_t w = words[jj];
                 dst[jj] = make_uint4(scale_pack(e2m1x2_f32(w & 0xff), s), scale_pack(e2m1x2_f32((w >> 8) & 0xff), s),
                                      scale_pack(e2m1x2_f32((w >> 16) & 0xff), s), scale_pack(e2m1x2_f32(w >> 24), s));
+            }
+        } else if (a.fmt == kFmtQ4K) {
+            const float2 dm = __ldg(reinterpret_cast<const float2 *>(a.scales) + (long long)grow * a.scale_cols + c0 / 32);
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                const uint32_t w = words[jj];
+                dst[jj] = make_uint4(q4k_pair(w & 0xf, (w >> 4) & 0xf, dm.x, dm.y),
+                                     q4k_pair((w >> 8) & 0xf, (w >> 12) & 0xf, dm.x, dm.y),
+                                     q4k_pair((w >> 16) & 0xf, (w >> 20) & 0xf, dm.x, dm.y),
+                                     q4k_pair((w >> 24) & 0xf, w >> 28, dm.x, dm.y));
             }
         } else {  // kFmtInt4
             const int g = c0 / a.blk_cols;
@@ -523,6 +569,13 @@ __device__ __forceinline__ void skinny_decode(const uint4 q, int row, int k0, co
         const float s = e8m0_scale(__ldg(p.scales_u8 + (long long)row * (p.k / 32) + k0 / 32));
 #pragma unroll
         for (int i = 0; i < 16; i++) pr[i] = scale_pack(e2m1x2_f32((w[i >> 2] >> (8 * (i & 3))) & 0xff), s);
+    } else if (FMT == kFmtQ4K) {
+        const float2 dm = __ldg(reinterpret_cast<const float2 *>(p.scales) + (long long)row * p.scale_cols + k0 / 32);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xff;
+            pr[i] = q4k_pair(byte & 0xf, byte >> 4, dm.x, dm.y);
+        }
     } else {  // kFmtInt4
         const int g = k0 / p.blk_cols;
         const float s = __ldg(p.scales + (long long)row * p.scale_cols + g);
@@ -975,11 +1028,11 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                 const int s = it % C::kStages;
                 const int rs = it % C::kRawRing;
                 const uint32_t rph = (it / C::kRawRing) & 1;
-                float sd[C::kNA];
+                float sd[C::kNA], md[C::kNA];
                 int zd[C::kNA];
 #pragma unroll
                 for (int i = 0; i < C::kNA; i++)  // issued before the wait: their latency hides behind it
-                    load_side<FMT>(p, vrow[i], srow[i], one_scale, kt * BK, h, sd[i], zd[i]);
+                    load_side<FMT>(p, vrow[i], srow[i], one_scale, kt * BK, h, sd[i], zd[i], md[i]);
                 // the raw tile has landed (the producer loaded it after operand stage s was free)
                 if (!mbar_wait(&L.rawfull[rs], rph, abort, p.status)) {
                     ok = false;
@@ -991,6 +1044,7 @@ __global__ void __launch_bounds__(Cfg<BN, DUAL, FMT>::kThreads, 1)
                     if (FMT == kFmtMxfp4) xform_mxfp4(L.raw(rs, i), L.a(s, i), r, h, sd[i]);
                     if (FMT == kFmtInt4) xform_int4(L.raw(rs, i), L.a(s, i), r, h, sd[i], zd[i]);
                     if (FMT == kFmtQ8_0) xform_q8_0(L.raw(rs, i), L.a(s, i), r, h, sd[i]);
+                    if (FMT == kFmtQ4K) xform_q4k(L.raw(rs, i), L.a(s, i), r, h, sd[i], md[i]);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -1156,6 +1210,7 @@ cudaError_t dispatch_fmt(int fmt, const GemmOperand &a, const GemmOperand *a2, c
     case kFmtMxfp4: return launch_t<BN, DUAL, kFmtMxfp4>(a, a2, b, p, sms, st);
     case kFmtInt4: return launch_t<BN, DUAL, kFmtInt4>(a, a2, b, p, sms, st);
     case kFmtQ8_0: return launch_t<BN, DUAL, kFmtQ8_0>(a, a2, b, p, sms, st);
+    case kFmtQ4K: return launch_t<BN, DUAL, kFmtQ4K>(a, a2, b, p, sms, st);
     default: return cudaErrorNotSupported;
     }
 }
@@ -1188,7 +1243,8 @@ int gemm_token_tile(int n_tok, bool dual, bool quant) {
 cudaError_t launch_stage_decode(const StageArgs &a, int num_sms, cudaStream_t stream) {
     const int epc = (a.fmt == kFmtFp8 || a.fmt == kFmtQ8_0) ? 16 : 32;
     if (a.rows <= 0) return cudaSuccess;
-    if ((a.fmt != kFmtFp8 && a.fmt != kFmtMxfp4 && a.fmt != kFmtInt4 && a.fmt != kFmtQ8_0) || a.cols % epc != 0)
+    if ((a.fmt != kFmtFp8 && a.fmt != kFmtMxfp4 && a.fmt != kFmtInt4 && a.fmt != kFmtQ8_0 && a.fmt != kFmtQ4K) ||
+        a.cols % epc != 0)
         return cudaErrorInvalidValue;
     if (a.fmt == kFmtInt4 && a.blk_cols % 32 != 0) return cudaErrorInvalidValue;
     const long long chunks = (long long)a.rows * (a.cols / epc);
@@ -1205,6 +1261,7 @@ int skinny_chunk(int fmt) {
     case kFmtQ8_0: return Skinny<kFmtQ8_0>::kChunk;
     case kFmtMxfp4: return Skinny<kFmtMxfp4>::kChunk;
     case kFmtInt4: return Skinny<kFmtInt4>::kChunk;
+    case kFmtQ4K: return Skinny<kFmtQ4K>::kChunk;
     default: return 0;
     }
 }
@@ -1229,6 +1286,7 @@ cudaError_t launch_skinny(int fmt, const GemmOperand &a, const GemmOperand &b, c
     case kFmtQ8_0: k_skinny<kFmtQ8_0><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
     case kFmtMxfp4: k_skinny<kFmtMxfp4><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
     case kFmtInt4: k_skinny<kFmtInt4><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtQ4K: k_skinny<kFmtQ4K><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

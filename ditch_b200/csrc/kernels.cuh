@@ -27,6 +27,11 @@ cudaError_t dequant_ggml_f32(int dtype, const uint8_t *src, long long n, float *
 // and that layout back to the f32 values d * q.
 cudaError_t repack_q8_0(const uint8_t *src, long long blocks, int8_t *codes, float *scales, cudaStream_t st);
 cudaError_t q8_0_f32(const int8_t *codes, const float *scales, long long n, float *out, cudaStream_t st);
+// Q4_K super-blocks to the GEMM's layout (4-bit codes [n / 2] in element
+// order and (d * scale, dmin * min) f32 pairs [n / 32]), and that layout back
+// to the f32 values d1 * q - m1.
+cudaError_t repack_q4_k(const uint8_t *src, long long super_blocks, uint8_t *codes, float *dm, cudaStream_t st);
+cudaError_t q4_k_f32(const uint8_t *codes, const float *dm, long long n, float *out, cudaStream_t st);
 // ggml blocks to bf16 (the GEMM operand of a GGUF weight)
 cudaError_t dequant_ggml_bf16(int dtype, const uint8_t *src, long long n, uint16_t *out, cudaStream_t st);
 

@@ -138,6 +138,10 @@ int native_format(const std::vector<Seg> &segs) {
         for (const Seg &s : segs)
             if (std::max<size_t>(s.t->slabs, 1) > 1) return -1;
         return cols % 32 ? -1 : kFmtQ8_0;
+    case DITCH_FMT_Q4_K:  // likewise, in 256-element super-blocks
+        for (const Seg &s : segs)
+            if (std::max<size_t>(s.t->slabs, 1) > 1) return -1;
+        return cols % 256 ? -1 : kFmtQ4K;
     case DITCH_FMT_INT_PACKED: {
         if (t0->bits != 4 || t0->block_cols % 64 || cols % 32 || !t0->zeros) return -1;
         for (size_t i = 0; i < segs.size(); i++) {
@@ -203,6 +207,25 @@ int build_mat(ditch_cuda_model *m, const std::vector<Seg> &segs, int slabs, Mat 
             DITCH_CUDA(copy_in(m, raw.ptr, s.t->data, 0, bytes, s.t));
             DITCH_LAUNCH(dev, repack_q8_0(raw.as<uint8_t>(), (long long)s.t->rows * (cols / 32),
                                           out.data.as<int8_t>() + r * cols, out.scales.as<float>() + r * (cols / 32),
+                                          dev->stream));
+            DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+            r += s.t->rows;
+        }
+    } else if (fmt == kFmtQ4K) {
+        out.fmt = kFmtQ4K;
+        out.row_bytes = (long long)cols / 2;
+        out.scols = (int)(cols / 32);
+        DITCH_CUDA(out.data.reserve(rows * cols / 2));
+        DITCH_CUDA(out.scales.reserve(rows * (cols / 32) * 8));  // (d1, m1) pairs
+        size_t r = 0;
+        for (const Seg &s : segs) {
+            const size_t bytes = s.t->rows * (cols / 256) * 144;
+            REQUIRE(s.t->data_bytes >= bytes, "%s: Q4_K data too short", what);
+            DevBuf raw;
+            DITCH_CUDA(raw.reserve(bytes));
+            DITCH_CUDA(copy_in(m, raw.ptr, s.t->data, 0, bytes, s.t));
+            DITCH_LAUNCH(dev, repack_q4_k(raw.as<uint8_t>(), (long long)s.t->rows * (cols / 256),
+                                          out.data.as<uint8_t>() + r * cols / 2, out.scales.as<float>() + r * (cols / 32) * 2,
                                           dev->stream));
             DITCH_CUDA(cudaStreamSynchronize(dev->stream));
             r += s.t->rows;
@@ -714,9 +737,10 @@ int ditch_cuda_weight_decode(ditch_cuda_weight *w, uint16_t *out) {
                                            mt.zeros.as<uint32_t>(), nullptr, mt.groups, rows, mt.cols, 4, mt.group, out,
                                            dev->stream));
         break;
-    case kFmtQ8_0: {  // the GEMM operand itself: bf16(d * q)
+    case kFmtQ8_0:    // the GEMM operand itself: bf16(d * q)
+    case kFmtQ4K: {   // bf16(d1 * q - m1)
         StageArgs sa{};
-        sa.fmt = kFmtQ8_0;
+        sa.fmt = mt.fmt;
         sa.data = mt.data.as<uint8_t>();
         sa.row_bytes = mt.row_bytes;
         sa.rows = rows;

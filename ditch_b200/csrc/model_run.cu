@@ -106,6 +106,16 @@ int gemv_t_mat(ditch_cuda_model *m, const Mat &w, int row0, int rows, const floa
         DITCH_CUDA(cudaStreamSynchronize(dev->stream));
         break;
     }
+    case kFmtQ4K: {  // the f32 values d1 * q - m1
+        DevBuf tmp;
+        DITCH_CUDA(tmp.reserve((size_t)rows * w.cols * 4));
+        DITCH_LAUNCH(dev, q4_k_f32(w.data.as<uint8_t>() + (size_t)row0 * w.cols / 2,
+                                   w.scales.as<float>() + (size_t)row0 * w.scols * 2, (long long)rows * w.cols,
+                                   tmp.as<float>(), dev->stream));
+        DITCH_LAUNCH(dev, gemv_t_f32(tmp.as<float>(), rows, w.cols, v, out, dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+        break;
+    }
     default:
         set_error("edit: weight format %d not supported", w.fmt);
         return DITCH_CUDA_UNSUPPORTED;
@@ -182,7 +192,7 @@ cudaError_t decode_rows_bf16(ditch_cuda_device *dev, const Mat &w, int row0, int
         sa.scale_cols = w.scols;
     } else if (w.fmt == kFmtMxfp4) {
         sa.scales_u8 = w.scales.as<uint8_t>();
-    } else if (w.fmt == kFmtQ8_0) {
+    } else if (w.fmt == kFmtQ8_0 || w.fmt == kFmtQ4K) {
         sa.scales = w.scales.as<float>();
         sa.scale_cols = w.scols;
     } else {
@@ -315,7 +325,7 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
             p.scale_cols = w.scols;
         } else if (fmt == kFmtMxfp4) {
             p.scales_u8 = w.scales.as<uint8_t>();
-        } else if (fmt == kFmtQ8_0) {
+        } else if (fmt == kFmtQ8_0 || fmt == kFmtQ4K) {
             p.scales = w.scales.as<float>();
             p.scale_cols = w.scols;
         } else if (fmt == kFmtInt4) {
@@ -377,7 +387,7 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         p.scale_cols = w.scols;
     } else if (fmt == kFmtMxfp4) {
         p.scales_u8 = w.scales.as<uint8_t>();
-    } else if (fmt == kFmtQ8_0) {
+    } else if (fmt == kFmtQ8_0 || fmt == kFmtQ4K) {
         p.scales = w.scales.as<float>();
         p.scale_cols = w.scols;
     } else if (fmt == kFmtInt4) {

@@ -423,7 +423,7 @@ class Tensor:
 class Weight:
     """One resident weight and its dequant-fused GEMM (device pointers in/out)."""
 
-    FORMATS = {0: "bf16", 1: "fp8", 2: "mxfp4", 3: "int4", 4: "q8_0"}
+    FORMATS = {0: "bf16", 1: "fp8", 2: "mxfp4", 3: "int4", 4: "q8_0", 5: "q4_k"}
 
     def __init__(self, device, tensor):
         self.dev = device

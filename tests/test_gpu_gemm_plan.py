@@ -26,7 +26,7 @@ def _bound(x, w):
     return (x.float().abs() @ w.float().abs().T) * 2.0 ** -18 + 1e-6
 
 
-@pytest.mark.parametrize("fmt", ["fp8", "mxfp4", "int4", "q8_0"])
+@pytest.mark.parametrize("fmt", ["fp8", "mxfp4", "int4", "q8_0", "q4_k"])
 @pytest.mark.parametrize("shape", range(len(SHAPES)))
 def test_staged_and_fused_plans(device, fmt, shape):
     rows, cols, m = SHAPES[shape]
@@ -115,6 +115,64 @@ def test_q8_0_operand_is_ditchs_decode(device):
     W.close()
 
 
+def test_q4_k_operand_is_ditchs_decode(device):
+    """The Q4_K GEMM operand (codes in element order and (d * scale, dmin *
+    min) pairs, decoded in the GEMM, in the weight-streaming product or
+    staged) equals ditch's f32 decode d1 * q - m1 (src/quant.zig:148-173)
+    rounded to bf16, bit for bit: sub-scales and mins from 0 to 63 (the
+    high-bit packing of sub-blocks 4-7), zero and negative super-block
+    scales; the fused and staged GEMMs give the same bits."""
+    import numpy as np
+
+    import oracle
+    from ditch_b200 import Tensor, Weight
+
+    rng = np.random.default_rng(12)
+    rows, cols = 256, 1024
+    n_blk = rows * cols // 256
+    raw = rng.integers(0, 256, (n_blk, 144), dtype=np.uint8)  # every scale / min / nibble pattern
+    d = (rng.standard_normal(n_blk) * 0.01).astype(np.float16)
+    dmin = (rng.standard_normal(n_blk) * 0.01).astype(np.float16)
+    d[::17] = 0
+    dmin[::13] = 0
+    raw[:, 0:2] = d.view(np.uint8).reshape(-1, 2)
+    raw[:, 2:4] = dmin.view(np.uint8).reshape(-1, 2)
+    raw = np.ascontiguousarray(raw.reshape(rows, -1))
+    W = Weight(device, Tensor("w", "q4_k", rows, cols, raw))
+    assert W.format() == "q4_k"
+    got = torch.empty(rows, cols, device="cuda", dtype=torch.int16)
+    W.decode(got.data_ptr())
+    device.synchronize()
+    want = oracle.f32_to_bf16_bits(oracle.dequant_ggml(10, raw, rows * cols).reshape(rows, cols))
+    assert np.array_equal(got.cpu().numpy().view(np.uint16), want)
+    x = (torch.randn(600, cols, device="cuda") * 0.1).to(torch.bfloat16)
+    dec = torch.from_numpy(want.view(np.int16)).cuda().view(torch.bfloat16)
+    outs = []
+    device.set_deterministic(True)
+    try:
+        for plan in (0, 1):
+            device.set_decode_staging(plan)
+            out = torch.empty(600, rows, device="cuda", dtype=torch.float32)
+            torch.cuda.synchronize()
+            W.gemm(x.data_ptr(), 600, out.data_ptr())
+            device.synchronize()
+            outs.append(out)
+        for m in (1, 7, 16):  # the weight-streaming product decodes the same operand
+            out = torch.empty(m, rows, device="cuda", dtype=torch.float32)
+            torch.cuda.synchronize()
+            W.gemm(x.data_ptr(), m, out.data_ptr())
+            device.synchronize()
+            ref = x[:m].float() @ dec.float().T
+            assert bool(((out - ref).abs() <= _bound(x[:m], dec)).all()), m
+    finally:
+        device.set_decode_staging(1024)
+        device.set_deterministic(False)
+        W.close()
+    assert torch.equal(outs[0], outs[1])
+    ref = x.float() @ dec.float().T
+    assert bool(((outs[0] - ref).abs() <= _bound(x, dec)).all())
+
+
 def test_fp8_operand_is_ditchs_decode(device):
     """Every E4M3 code (subnormals, both zeros, NaN) under block scales from
     1e-30 to 300 (past 2^8 the decoders take their conversion path): the
@@ -163,7 +221,7 @@ def test_fp8_operand_is_ditchs_decode(device):
     assert torch.equal(outs[0], outs[1])
 
 
-@pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4", "int4", "q8_0"])
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4", "int4", "q8_0", "q4_k"])
 @pytest.mark.parametrize("m", [1, 5, 16])
 def test_weight_streaming_small_m(device, fmt, m):
     """1..16 tokens take the weight-streaming product (mma.sync over the
