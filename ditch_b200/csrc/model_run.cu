@@ -247,8 +247,19 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     // token tile; past a few tiles, decoding the rows once to bf16 scratch (one
     // more pass over the weight: codes in, 2 bytes out, 2 bytes back in) and
     // running the bf16 GEMM costs less. Both build the same bf16 operand.
-    if (fmt != kFmtBf16 && !(ex && ex->sched) && dev->stage_min_tokens > 0 && n_tok >= dev->stage_min_tokens) {
-        const int rows = (dual ? a2_row_offset : 0) + m_rows;
+    // A bf16 copy kept by an earlier staged call also serves the products
+    // below the staging threshold (the decode steps of generation after the
+    // prefill): past 16 tokens the bf16 GEMM over it runs faster than
+    // decoding the stored format tile by tile (same operand bits).
+    const int st_rows = (dual ? a2_row_offset : 0) + m_rows;
+    const bool cached = fmt != kFmtBf16 && !(ex && ex->sched) && w.decoded.ptr && w.decoded_row0 == slab_row0 &&
+                        w.decoded_rows == st_rows;
+    if (cached && n_tok > 16 && n_tok < dev->stage_min_tokens) {
+        A = GemmOperand{w.decoded.ptr, st_rows, w.cols, (long long)w.cols * 2};
+        fmt = kFmtBf16;
+        slab_row0 = 0;
+    } else if (fmt != kFmtBf16 && !(ex && ex->sched) && dev->stage_min_tokens > 0 && n_tok >= dev->stage_min_tokens) {
+        const int rows = st_rows;
         const size_t bytes = (size_t)rows * w.cols * 2;
         const void *dec = nullptr;
         if (w.decoded.ptr && w.decoded_row0 == slab_row0 && w.decoded_rows == rows) {
