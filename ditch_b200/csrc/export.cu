@@ -422,7 +422,8 @@ int merge(Work &w, const OutTensor &o) {
         CK_REQUIRE(o.rows == (size_t)H && o.cols == (size_t)mi, "%s: [%zu][%zu] is not the model's [%d][%d]",
                    o.name.c_str(), o.rows, o.cols, H, mi);
         k_merge_rows<<<export_blocks(n), kExportThreads, 0, dev->stream>>>(
-            v, H, mi, L.e_a.as<float>() + (size_t)o.expert * mi, L.e_b.as<float>() + (size_t)o.expert * H, 1);
+            v, H, mi, L.e_a.as<float>() + (size_t)o.expert * L.e_rank * mi,
+            L.e_b.as<float>() + (size_t)o.expert * H * L.e_rank, L.e_rank);
         DITCH_LAUNCH(dev, cudaGetLastError());
         break;
     case OutTensor::Fused: {
@@ -432,9 +433,10 @@ int merge(Work &w, const OutTensor &o) {
         for (int e = 0; e < E; e++) {
             if (!L.e_edit[e]) continue;
             float *blk = v + (size_t)e * H * mi;
-            const float *a = L.e_a.as<float>() + (size_t)e * mi, *b = L.e_b.as<float>() + (size_t)e * H;
-            if (o.fused_t) k_merge_cols<<<export_blocks((long long)H * mi), kExportThreads, 0, dev->stream>>>(blk, mi, H, a, b, 1);
-            else k_merge_rows<<<export_blocks((long long)H * mi), kExportThreads, 0, dev->stream>>>(blk, H, mi, a, b, 1);
+            const int r = L.e_rank;
+            const float *a = L.e_a.as<float>() + (size_t)e * r * mi, *b = L.e_b.as<float>() + (size_t)e * H * r;
+            if (o.fused_t) k_merge_cols<<<export_blocks((long long)H * mi), kExportThreads, 0, dev->stream>>>(blk, mi, H, a, b, r);
+            else k_merge_rows<<<export_blocks((long long)H * mi), kExportThreads, 0, dev->stream>>>(blk, H, mi, a, b, r);
             DITCH_LAUNCH(dev, cudaGetLastError());
         }
         break;
@@ -724,8 +726,8 @@ int ditch_cuda_model_delta(ditch_cuda_model *m, size_t layer, int which, size_t 
     else if (which == 2) {
         CK_REQUIRE(L.moe && expert < L.e_edit.size(), "layer %zu has no routed expert %zu", layer, expert);
         if (L.e_edit[expert]) {
-            da = L.e_a.as<float>() + expert * c.moe_inter, db = L.e_b.as<float>() + expert * c.hidden;
-            r = 1, cols = c.moe_inter;
+            r = (size_t)L.e_rank, cols = c.moe_inter;
+            da = L.e_a.as<float>() + expert * r * c.moe_inter, db = L.e_b.as<float>() + expert * c.hidden * r;
         }
     } else CK_REQUIRE(which >= 0 && which <= 2, "component %d: 0 attention output, 1 MLP down, 2 expert down", which);
     *rank = r;

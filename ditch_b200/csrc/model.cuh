@@ -49,7 +49,8 @@ struct Layer {
     std::vector<uint8_t> e_edit;                   // per expert
     std::vector<float> e_fro;                      // ||W_down_e||_F per expert (computed once)
     DevBuf e_proj;                                 // f32 [E][mi]: v^T W_down_e of the last scoring
-    DevBuf e_a, e_b;                               // f32 [E][mi], [E][H]
+    int e_rank = 1;                                // terms of the expert deltas (full row normalisation: up to kMaxDeltaRank)
+    DevBuf e_a, e_b;                               // f32 [E][e_rank][mi], [E][H][e_rank]
     DevBuf e_edit_dev;                             // int [E]
     // row norms ||W_i|| for the pre-normalised edit (computed once; the base weights never change)
     DevBuf o_rn, down_rn, e_rn;                    // f32 [H], [H], [E][H]

@@ -597,8 +597,8 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
             if ((st = build_mat(m.get(), gu, El, L.e_gate_up, "e_gate_up"))) return st;
             if ((st = build_mat(m.get(), dn, El, L.e_down, "e_down"))) return st;
             L.e_edit.assign(El, 0);
-            DITCH_CUDA(L.e_a.reserve((size_t)El * L.e_down.cols * 4));
-            DITCH_CUDA(L.e_b.reserve((size_t)El * H * 4));
+            DITCH_CUDA(L.e_a.reserve((size_t)El * L.e_down.cols * 4 * kMaxDeltaRank));
+            DITCH_CUDA(L.e_b.reserve((size_t)El * H * 4 * kMaxDeltaRank));
             DITCH_CUDA(L.e_edit_dev.reserve((size_t)El * 4));
             DITCH_CUDA(cudaMemsetAsync(L.e_edit_dev.ptr, 0, (size_t)El * 4, dev->stream));
         } else {

@@ -633,7 +633,7 @@ int upload_expert_flags(ditch_cuda_model *m) {
 void clear_edits(ditch_cuda_model *m) {
     for (Layer &L : m->layers) {
         L.o_edit = L.down_edit = false;
-        L.o_rank = L.down_rank = 1;
+        L.o_rank = L.down_rank = L.e_rank = 1;
         std::fill(L.e_edit.begin(), L.e_edit.end(), 0);
     }
 }
@@ -753,6 +753,20 @@ int expert_delta_from_proj(ditch_cuda_model *m, int li, int e, const float *v, f
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
     const int H = m->cfg.hidden, mi = L.e_down.cols;
+    if (m->row_norm == 2) {  // full: expert e's rank-r delta, [E][r][mi] and [E][H][r]
+        int s;
+        if ((s = ensure_row_norms(m, L))) return s;
+        const int r = m->lora_rank;
+        int got = 0;
+        if ((s = full_norm_delta(m, L.e_down, e * H, L.e_rn.as<float>() + (size_t)e * H, v, lambda, r,
+                                 m->edit_seed + m->seed_counter++, L.e_a.as<float>() + (size_t)e * r * mi,
+                                 L.e_b.as<float>() + (size_t)e * H * r, &got)))
+            return s;
+        REQUIRE(got == r, "expert %d: a rank-%d delta where the layer's experts take rank %d", e, got, r);
+        L.e_rank = r;
+        L.e_edit[e] = 1;
+        return DITCH_CUDA_OK;
+    }
     if (m->row_norm) {  // pre-normalised: the projection of v / n_e, not of v
         int s;
         if ((s = ensure_row_norms(m, L))) return s;
@@ -799,7 +813,7 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
         }
         const int E = c.n_experts;
         if (!selective || n_experts == 0) {
-            if (!m->row_norm && (s = expert_projections(m, li, v))) return s;
+            if (!m->row_norm && (s = expert_projections(m, li, v))) return s;  // every expert's v^T W_e at once
             for (int e = 0; e < c.e_loc; e++)  // this rank's experts
                 if ((s = expert_delta_from_proj(m, li, e, v, lambda))) return s;
             continue;
@@ -1091,11 +1105,10 @@ int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_
     if (mode == 2) {
         REQUIRE(lora_rank >= 1 && lora_rank <= (size_t)kMaxDeltaRank, "lora_rank %zu is not within 1..%d", lora_rank,
                 kMaxDeltaRank);
-        for (const Layer &L : m->layers)
-            if (L.moe) {
-                set_error("row_normalization = full on routed experts is not implemented on the device");
-                return DITCH_CUDA_UNSUPPORTED;
-            }
+        if (m->cfg.ep_world > 1) {
+            set_error("row_normalization = full under expert parallelism is not implemented on the device");
+            return DITCH_CUDA_UNSUPPORTED;
+        }
     }
     std::lock_guard<std::mutex> lk(m->dev->mu);
     m->row_norm = mode;

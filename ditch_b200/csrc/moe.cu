@@ -263,24 +263,26 @@ __global__ void k_gather_rows(const uint16_t *src, long long ss, const int *perm
     }
 }
 
-// xa[pos] = act[pos] . a[e(pos)] for experts with an edit (the x . A term of
-// the per-expert rank-1 delta), 0 otherwise.
+// xa[pos][t] = act[pos] . a_t[e(pos)] for experts with an edit (the x . A
+// terms of the per-expert rank-`rank` delta, a [E][rank][mi]), 0 otherwise.
 __global__ void k_rowdot_grouped(const uint16_t *act, const float *e_a, const int *pexp, const int *e_flags, int rows,
-                                 int mi, float *xa) {
+                                 int mi, int rank, float *xa) {
     const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (r >= rows) return;
     const int e = pexp[r];
     if (!e_flags[e]) {
-        if (lane == 0) xa[r] = 0.0f;
+        if (lane < rank) xa[(long long)r * rank + lane] = 0.0f;
         return;
     }
     const uint16_t *ar = act + (long long)r * mi;
-    const float *a = e_a + (long long)e * mi;
-    float s = 0.0f;
-    for (int i = lane; i < mi; i += 32) s = fmaf(bf16_bits_to_f32(ar[i]), a[i], s);
-    s = warp_sum(s);
-    if (lane == 0) xa[r] = s;
+    for (int t = 0; t < rank; t++) {
+        const float *a = e_a + ((long long)e * rank + t) * mi;
+        float s = 0.0f;
+        for (int i = lane; i < mi; i += 32) s = fmaf(bf16_bits_to_f32(ar[i]), a[i], s);
+        s = warp_sum(s);
+        if (lane == 0) xa[(long long)r * rank + t] = s;
+    }
 }
 
 // x[t] += sum over t's experts in index order of w * eo[slot], accumulated
@@ -542,7 +544,7 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     DITCH_CUDA(m->moe_xg.reserve((size_t)nk * H * 2));
     DITCH_CUDA(m->moe_act.reserve((size_t)nk * mip * 2));
     DITCH_CUDA(m->moe_eo.reserve((size_t)nk * H * 4));
-    DITCH_CUDA(m->moe_xa.reserve((size_t)nk * 4));
+    DITCH_CUDA(m->moe_xa.reserve((size_t)nk * 4 * kMaxDeltaRank));
     DITCH_CUDA(m->moe_sched_gu.reserve((size_t)max_gu * 16));
     DITCH_CUDA(m->moe_sched_d.reserve((size_t)max_d * 16));
     DITCH_CUDA(m->moe_nsched.reserve(16));
@@ -587,7 +589,7 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     if (any_edit) {
         k_rowdot_grouped<<<(nk + 7) / 8, 256, 0, st>>>(m->moe_act.as<uint16_t>(), L.e_a.as<float>(),
                                                        m->moe_pexp.as<int>(), L.e_edit_dev.as<int>(), nk, mip,
-                                                       m->moe_xa.as<float>());
+                                                       L.e_rank, m->moe_xa.as<float>());
         DITCH_LAUNCH(dev, cudaGetLastError());
     }
     GemmExtra dn;
@@ -596,9 +598,10 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     dn.slab_rows = H;
     dn.bn = bn_d;
     dn.e_flags = L.e_edit_dev.as<int>();
-    dn.db_stride = H;
+    dn.db_stride = H * L.e_rank;
     if ((s = gemm_mat(dev, L.e_down, 0, H, m->moe_act.as<uint16_t>(), nk, m->moe_eo.ptr, H, 0, nullptr,
-                      any_edit ? m->moe_xa.as<float>() : nullptr, any_edit ? L.e_b.as<float>() : nullptr, 0, &dn)))
+                      any_edit ? m->moe_xa.as<float>() : nullptr, any_edit ? L.e_b.as<float>() : nullptr, 0, &dn,
+                      L.e_rank)))
         return s;
     k_combine<<<n, 256, 0, st>>>(m->moe_eo.as<float>(), m->moe_sel.as<int>(), m->moe_w.as<float>(),
                                  m->moe_slot.as<int>(), n, k, H, m->x.as<float>());

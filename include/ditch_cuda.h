@@ -306,8 +306,9 @@ int ditch_cuda_apply_edit(ditch_cuda_model *m, const ditch_cuda_params *attn_o, 
  * randomised SVD of W' - W with 2 r + 4 sketch vectors and 6 power
  * iterations; the sketch of the k-th edited matrix is seeded with seed + k
  * (Options.seed) from this library's own generator, not ditch's, so the two
- * agree to the SVD's accuracy. Tensor-parallel ranks (partial row norms) and,
- * for full, models with routed experts return DITCH_CUDA_UNSUPPORTED. */
+ * agree to the SVD's accuracy. Routed experts get one such delta per edited
+ * expert. Tensor-parallel ranks (partial row norms) and, for full,
+ * expert-parallel ranks return DITCH_CUDA_UNSUPPORTED. */
 int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_rank, uint64_t seed);
 /* moe.applyExpertSelective, ranked selection (src/moe.zig:1373-1477): the
  * o_proj edit as above, then per MoE layer the top n_experts experts by

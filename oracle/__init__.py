@@ -42,6 +42,7 @@ class Layer(C.Structure):
         ("o_da", f32p), ("o_db", f32p), ("o_rank", C.c_size_t),
         ("down_da", f32p), ("down_db", f32p), ("down_rank", C.c_size_t),
         ("e_down_da", C.POINTER(f32p)), ("e_down_db", C.POINTER(f32p)),
+        ("e_down_rank", szp),
     ]
 
 

@@ -122,6 +122,7 @@ typedef struct {
     const float *o_da, *o_db; size_t o_rank;       /* o_proj delta */
     const float *down_da, *down_db; size_t down_rank;
     const float *const *e_down_da; const float *const *e_down_db; /* per expert, may be NULL */
+    const size_t *e_down_rank;        /* per expert terms of its delta (NULL: 1) */
 } or_layer;
 
 typedef struct {

@@ -99,7 +99,8 @@ static void moe_forward(const or_model *m, const or_layer *L, const float *h, si
         or_gated_silu(g, g, u, ne, mi, mi, mi);
         const float *da = L->e_down_da ? L->e_down_da[e] : NULL;
         const float *db = L->e_down_db ? L->e_down_db[e] : NULL;
-        or_matmul_t(eo, g, ne, L->e_down + e * H * mi, H, mi, da, db, da && db ? 1 : 0);
+        const size_t dr = L->e_down_rank ? L->e_down_rank[e] : 1;
+        or_matmul_t(eo, g, ne, L->e_down + e * H * mi, H, mi, da, db, da && db ? dr : 0);
         for (size_t j = 0; j < ne; j++) axpy(out + tok[j] * H, w[j], eo + j * H, H);
     }
     free(logits); free(sel); free(selw); free(choice); free(xg); free(g); free(u); free(eo);

@@ -61,13 +61,16 @@ class OracleModel:
             if E and f"L{i}.router" in self.w:
                 da = (f32p * E)()
                 db = (f32p * E)()
+                dr = (C.c_size_t * E)()
                 for e in range(E):
                     if (i, ("e", e)) in self.deltas:
                         a, b = self.deltas[(i, ("e", e))]
                         da[e], db[e] = ptr(a), ptr(b)
+                        dr[e] = a.shape[0] if a.ndim == 2 else 1
                 L.e_down_da = C.cast(da, C.POINTER(f32p))
                 L.e_down_db = C.cast(db, C.POINTER(f32p))
-                keep += [da, db]
+                L.e_down_rank = C.cast(dr, szp)
+                keep += [da, db, dr]
         m = Model(c=cfg, embed=g("embed"), final_norm=g("final_norm"), lm_head=g("lm_head"),
                   layers=C.cast(layers, C.POINTER(Layer)))
         self._keep = [layers, keep]

@@ -309,7 +309,7 @@ def test_full_normalised_edit(device, family):
     473-538): the device's rank-3 deltas against the oracle's restatement
     run with the same seeded sketch (matrix k of the edit takes seed + k, in
     the order layer by layer, o_proj then down_proj), compared through the
-    edited KL. Models with routed experts refuse full."""
+    edited KL."""
     g, m = load(device, family)
     s = g.spec
     w = g.f32_weights()
@@ -342,7 +342,63 @@ def test_full_normalised_edit(device, family):
     assert got > 0 and abs(got - want) <= 2e-3 + 0.05 * abs(want), (got, want)
     m.set_row_normalization("none")
     m.close()
-    g2, m2 = load(device, "qwen3_moe")
-    with pytest.raises(ditch_b200.Unsupported):
-        m2.set_row_normalization("full")
-    m2.close()
+
+
+@pytest.mark.parametrize("selective", [False, True])
+def test_full_normalised_expert_edit(device, selective):
+    """row_normalization = full on routed experts (src/moe.zig:1648, 1751: the
+    reference's own full-mode expert tests): every edited expert's down
+    projection gets a rank-3 delta from the randomised SVD, seeded in the
+    device's order (layer by layer: o_proj, then the experts in the order they
+    are edited, or the dense down_proj), against the oracle through the
+    edited KL; broad (every expert) and selective (top 2 by alignment)."""
+    g, m = load(device, "qwen3_moe")
+    s = g.spec
+    w = g.f32_weights()
+    rng = np.random.default_rng(21)
+    dirs = rng.standard_normal((s["n_layers"] + 1, s["hidden"])).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    m.set_directions(dirs)
+    prompts = g.prompts()
+    toks, rb, rp, cap, first, take, last = flatten_batch(prompts)
+    m.kl_init(prompts)
+    po, pd = (1.1, 0.0, 0.5, 3.0), (0.9, 1.0, 0.3, 2.0)
+    seed = 41
+    m.set_row_normalization("full", lora_rank=3, seed=seed)
+    if selective:
+        m.apply_expert_edit(po, pd, n_experts=2, strength=0.8)
+    else:
+        m.apply_edit(po, pd)
+    got = m.kl_score()
+    om = OracleModel(s, w)
+    k = 0
+    for li in range(s["n_layers"]):
+        v = dirs[li + 1]
+        lam = oracle.kernel_weight(po, li)
+        if lam is not None:
+            om.set_delta(li, "o", *oracle.compute_delta_full(w[f"L{li}.o"], v, lam, lora_rank=3, seed=seed + k))
+            k += 1
+        lam = oracle.kernel_weight(pd, li)
+        if lam is None:
+            continue
+        if not s["moe_layers"][li]:
+            om.set_delta(li, "down", *oracle.compute_delta_full(w[f"L{li}.down"], v, lam, lora_rank=3, seed=seed + k))
+            k += 1
+            continue
+        if selective:
+            sc = np.array([oracle.score_down(w[f"L{li}.e_down"][e], v) for e in range(s["n_experts"])], np.float32)
+            chosen = [(int(e), lam * 0.8) for e in oracle.rank_scores(sc)[:2]]
+        else:
+            chosen = [(e, lam) for e in range(s["n_experts"])]
+        for e, weight in chosen:
+            a, b = oracle.compute_delta_full(w[f"L{li}.e_down"][e], v, weight, lora_rank=3, seed=seed + k)
+            k += 1
+            om.set_delta(li, ("e", e), a, b)
+            got_d = m.delta(li, "expert_down_proj", e)
+            assert got_d is not None and got_d[0].shape[0] == 3
+    _, base = OracleModel(s, w).forward(toks, rb, rp, (), last)
+    _, ed = om.forward(toks, rb, rp, (), last)
+    want = oracle.kl_first_token(oracle.log_softmax(base), ed)[0]
+    assert got > 0 and abs(got - want) <= 2e-3 + 0.05 * abs(want), (got, want)
+    m.set_row_normalization("none")
+    m.close()
