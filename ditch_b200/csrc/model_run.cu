@@ -749,7 +749,10 @@ int expert_scores(ditch_cuda_model *m, int li, const float *v, std::vector<float
 
 // The none-mode delta of expert e from its projection in L.e_proj:
 // a = v^T W_down_e, b = -lambda v, stored as (a, lambda v) for the epilogue.
-int expert_delta_from_proj(ditch_cuda_model *m, int li, int e, const float *v, float lambda) {
+// seed_index: this matrix's running index in the edit as one device would
+// count it (full mode seeds its sketch with edit_seed plus it, so every rank
+// of an expert-parallel model draws the same sketch for the same expert).
+int expert_delta_from_proj(ditch_cuda_model *m, int li, int e, const float *v, float lambda, uint64_t seed_index) {
     ditch_cuda_device *dev = m->dev;
     Layer &L = m->layers[li];
     const int H = m->cfg.hidden, mi = L.e_down.cols;
@@ -759,7 +762,7 @@ int expert_delta_from_proj(ditch_cuda_model *m, int li, int e, const float *v, f
         const int r = m->lora_rank;
         int got = 0;
         if ((s = full_norm_delta(m, L.e_down, e * H, L.e_rn.as<float>() + (size_t)e * H, v, lambda, r,
-                                 m->edit_seed + m->seed_counter++, L.e_a.as<float>() + (size_t)e * r * mi,
+                                 m->edit_seed + seed_index, L.e_a.as<float>() + (size_t)e * r * mi,
                                  L.e_b.as<float>() + (size_t)e * H * r, &got)))
             return s;
         REQUIRE(got == r, "expert %d: a rank-%d delta where the layer's experts take rank %d", e, got, r);
@@ -815,7 +818,8 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
         if (!selective || n_experts == 0) {
             if (!m->row_norm && (s = expert_projections(m, li, v))) return s;  // every expert's v^T W_e at once
             for (int e = 0; e < c.e_loc; e++)  // this rank's experts
-                if ((s = expert_delta_from_proj(m, li, e, v, lambda))) return s;
+                if ((s = expert_delta_from_proj(m, li, e, v, lambda, m->seed_counter + c.e0 + e))) return s;
+            m->seed_counter += E;  // every expert of the layer counts, wherever it lives
             continue;
         }
         const float weight = std::max(0.0f, lambda * strength);
@@ -827,8 +831,9 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
         for (size_t j = 0; j < n; j++) {
             const int e = (int)order[j] - c.e0;  // edited by the rank that owns it
             if (e >= 0 && e < c.e_loc)
-                if ((s = expert_delta_from_proj(m, li, e, v, weight))) return s;
+                if ((s = expert_delta_from_proj(m, li, e, v, weight, m->seed_counter + j))) return s;
         }
+        m->seed_counter += n;
     }
     if ((s = upload_expert_flags(m))) return s;
     return check_status(m->dev, "apply_edit");
@@ -1105,10 +1110,6 @@ int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_
     if (mode == 2) {
         REQUIRE(lora_rank >= 1 && lora_rank <= (size_t)kMaxDeltaRank, "lora_rank %zu is not within 1..%d", lora_rank,
                 kMaxDeltaRank);
-        if (m->cfg.ep_world > 1) {
-            set_error("row_normalization = full under expert parallelism is not implemented on the device");
-            return DITCH_CUDA_UNSUPPORTED;
-        }
     }
     std::lock_guard<std::mutex> lk(m->dev->mu);
     m->row_norm = mode;

@@ -442,24 +442,27 @@ __global__ void k_ep_fill_pexp(const int *offsets, int El, int cap, int *pexp) {
     }
 }
 
-// xa of receive rows of edited local experts (rows with pexp < 0 skipped).
+// xa of receive rows of edited local experts (rows with pexp < 0 skipped),
+// `rank` terms per row as k_rowdot_grouped.
 __global__ void k_ep_rowdot(const uint16_t *act, const float *e_a, const int *pexp, const int *e_flags, int cap,
-                            int mi, float *xa) {
+                            int mi, int rank, float *xa) {
     const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (r >= cap) return;
     const int e = pexp[r];
     if (e < 0) return;
     if (!e_flags[e]) {
-        if (lane == 0) xa[r] = 0.0f;
+        if (lane < rank) xa[(long long)r * rank + lane] = 0.0f;
         return;
     }
     const uint16_t *ar = act + (long long)r * mi;
-    const float *a = e_a + (long long)e * mi;
-    float s = 0.0f;
-    for (int i = lane; i < mi; i += 32) s = fmaf(bf16_bits_to_f32(ar[i]), a[i], s);
-    s = warp_sum(s);
-    if (lane == 0) xa[r] = s;
+    for (int t = 0; t < rank; t++) {
+        const float *a = e_a + ((long long)e * rank + t) * mi;
+        float s = 0.0f;
+        for (int i = lane; i < mi; i += 32) s = fmaf(bf16_bits_to_f32(ar[i]), a[i], s);
+        s = warp_sum(s);
+        if (lane == 0) xa[(long long)r * rank + t] = s;
+    }
 }
 
 // One warp per receive row: its expert output back to the source rank's eo
@@ -671,7 +674,7 @@ int moe_mlp_ep(ditch_cuda_model *m, Layer &L, int n) {
     DITCH_CUDA(m->ep_pexp.reserve((size_t)cap * 4));
     DITCH_CUDA(m->ep_act.reserve((size_t)cap * mip * 2));
     DITCH_CUDA(m->ep_eo.reserve((size_t)cap * H * 4));
-    DITCH_CUDA(m->ep_xa.reserve((size_t)cap * 4));
+    DITCH_CUDA(m->ep_xa.reserve((size_t)cap * 4 * kMaxDeltaRank));
     DITCH_CUDA(m->ep_sched_gu.reserve((size_t)max_gu * 16));
     DITCH_CUDA(m->ep_sched_d.reserve((size_t)max_d * 16));
     DITCH_CUDA(m->ep_nsched.reserve(16));
@@ -739,7 +742,7 @@ int moe_mlp_ep(ditch_cuda_model *m, Layer &L, int n) {
     for (uint8_t f : L.e_edit) any_edit |= f != 0;
     if (any_edit) {
         k_ep_rowdot<<<(cap + 7) / 8, 256, 0, st>>>(m->ep_act.as<uint16_t>(), L.e_a.as<float>(), m->ep_pexp.as<int>(),
-                                                   L.e_edit_dev.as<int>(), cap, mip, m->ep_xa.as<float>());
+                                                   L.e_edit_dev.as<int>(), cap, mip, L.e_rank, m->ep_xa.as<float>());
         DITCH_LAUNCH(dev, cudaGetLastError());
     }
     GemmExtra dn;
@@ -748,9 +751,10 @@ int moe_mlp_ep(ditch_cuda_model *m, Layer &L, int n) {
     dn.slab_rows = H;
     dn.bn = bn_d;
     dn.e_flags = L.e_edit_dev.as<int>();
-    dn.db_stride = H;
+    dn.db_stride = H * L.e_rank;
     if ((s = gemm_mat(dev, L.e_down, 0, H, m->ep_act.as<uint16_t>(), cap, m->ep_eo.ptr, H, 0, nullptr,
-                      any_edit ? m->ep_xa.as<float>() : nullptr, any_edit ? L.e_b.as<float>() : nullptr, 0, &dn)))
+                      any_edit ? m->ep_xa.as<float>() : nullptr, any_edit ? L.e_b.as<float>() : nullptr, 0, &dn,
+                      L.e_rank)))
         return s;
 
     // exchange 3: the outputs back to the pairs' positions on their source ranks

@@ -79,11 +79,21 @@ def _worker(rank, world, port, out_dir):
         m.apply_expert_edit((1.2, 1.0, 0.5, 2.0), (1.1, 0.5, 0.4, 2.0), None, n_experts=3, strength=1.0)
     res3, log3 = one.forward(toks, rb, rp, cap, last)
     res4, log4 = ep.forward(toks, rb, rp, cap, last)
+    # row_normalization = full: every edited expert's rank-2 delta, its sketch
+    # seeded by the matrix's index on one device whichever rank owns it
+    for m in (one, ep):
+        m.set_row_normalization("full", lora_rank=2, seed=5)
+        m.apply_expert_edit((1.2, 1.0, 0.5, 2.0), (1.1, 0.5, 0.4, 2.0), None, n_experts=3, strength=1.0)
+    res5, log5 = one.forward(toks, rb, rp, cap, last)
+    res6, log6 = ep.forward(toks, rb, rp, cap, last)
+    for m in (one, ep):
+        m.set_row_normalization("none")
     order1 = one.rank_experts(1, dirs[2])
     order2 = ep.rank_experts(1, dirs[2])
     group.barrier()
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), res1=res1, log1=log1, res2=res2, log2=log2, res3=res3, log3=log3,
-             res4=res4, log4=log4, order1=np.asarray(order1[0]), order2=np.asarray(order2[0]))
+             res4=res4, log4=log4, res5=res5, log5=log5, res6=res6, log6=log6, order1=np.asarray(order1[0]),
+             order2=np.asarray(order2[0]))
     ep.close()
     one.close()
     dist.barrier()
@@ -101,8 +111,10 @@ def test_expert_parallel_forward_equals_one_gpu(tmp_path):
     mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
     for r in range(2):
         z = np.load(tmp_path / f"r{r}.npz")
-        for a, b in (("res1", "res2"), ("log1", "log2"), ("res3", "res4"), ("log3", "log4")):
+        for a, b in (("res1", "res2"), ("log1", "log2"), ("res3", "res4"), ("log3", "log4"), ("res5", "res6"),
+                     ("log5", "log6")):
             diff = float(np.abs(z[a] - z[b]).max()) if z[a].size else 0.0
             assert np.array_equal(z[a], z[b]), (r, a, b, diff)
         assert not np.array_equal(z["log1"], z["log3"]), "the edit changed nothing"
+        assert not np.array_equal(z["log3"], z["log5"]), "full row normalisation changed nothing"
         assert np.array_equal(z["order1"], z["order2"])
