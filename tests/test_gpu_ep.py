@@ -50,6 +50,7 @@ def _worker(rank, world, port, out_dir):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
     dev = ditch_b200.Device(rank)
+    dev.set_deterministic(True)  # K splits summed in a fixed order: the two models must agree bit for bit
     spec, f32, tensors = make_model(300, n_layers=2, hidden=256, head_dim=64, heads=4, kv_heads=2, fmt="mxfp4",
                                     moe=dict(experts=16, top_k=4, inter=128))
     ps = prompts(40 + rank, [40, 17, 64, 3, 70][: 5 - rank], spec["vocab"])
