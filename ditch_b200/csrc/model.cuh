@@ -177,6 +177,7 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n);
 size_t tp_group_bytes(const Config &c, size_t max_tokens);
 float *tp_send_rows(ditch_cuda_model *m);
 int tp_allreduce_add(ditch_cuda_model *m, int n, float *x);
+int tp_row_norms(ditch_cuda_model *m, const Mat &w, float *out);
 
 // Expert scores of this rank's routed experts (`local` [e_loc]) gathered from
 // every rank of the model's peer group into `all` [n_experts].

@@ -573,13 +573,13 @@ int ensure_row_norms(ditch_cuda_model *m, Layer &L) {
     ditch_cuda_device *dev = m->dev;
     const int H = m->cfg.hidden;
     int s;
-    if (!L.o_rn.ptr) {
+    if (!L.o_rn.ptr) {  // under tensor parallelism summed over the column shards
         DITCH_CUDA(L.o_rn.reserve((size_t)H * 4));
-        if ((s = mat_row_norms(dev, L.o, 0, H, L.o_rn.as<float>()))) return s;
+        if ((s = tp_row_norms(m, L.o, L.o_rn.as<float>()))) return s;
     }
     if (!L.moe && !L.down_rn.ptr) {
         DITCH_CUDA(L.down_rn.reserve((size_t)H * 4));
-        if ((s = mat_row_norms(dev, L.down, 0, H, L.down_rn.as<float>()))) return s;
+        if ((s = tp_row_norms(m, L.down, L.down_rn.as<float>()))) return s;
     }
     if (L.moe && !L.e_rn.ptr) {
         const int E = m->cfg.e_loc;
@@ -1102,9 +1102,9 @@ int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_
     clear_error();
     REQUIRE(m, "null model");
     REQUIRE(mode >= 0 && mode <= 2, "row normalisation %d is not none (0), pre (1) or full (2)", mode);
-    if (mode != 0 && m->cfg.tp_world > 1) {
-        // a rank holds column shards of o_proj / down_proj: its row norms are partial
-        set_error("row normalisation under tensor parallelism is not supported");
+    if (mode == 2 && m->cfg.tp_world > 1) {
+        // the randomised SVD's products over column shards would need collectives of their own
+        set_error("row_normalization = full under tensor parallelism is not supported");
         return DITCH_CUDA_UNSUPPORTED;
     }
     if (mode == 2) {

@@ -53,7 +53,38 @@ __global__ void k_tp_gather_add(PeerPtrs pp, size_t red_off, long long total4, l
     }
 }
 
+__global__ void k_square(const float *x, float *y, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = x[i] * x[i];
+}
+
+__global__ void k_sqrt(float *x, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] = sqrtf(x[i]);
+}
+
 }  // namespace
+
+// Row norms of a row-parallel weight (o_proj, down_proj: each rank holds a
+// column shard of every row): the shard's norms, squared, summed over the
+// ranks, then the root. Every rank of the group calls this in the same order.
+int tp_row_norms(ditch_cuda_model *m, const Mat &w, float *out) {
+    ditch_cuda_device *dev = m->dev;
+    const int H = m->cfg.hidden;
+    int s;
+    if ((s = mat_row_norms(dev, w, 0, H, out))) return s;
+    if (m->cfg.tp_world <= 1) return DITCH_CUDA_OK;
+    if (!m->group || H % 4) {
+        set_error("row norms of a tensor-parallel model need its peer group (and hidden a multiple of 4)");
+        return DITCH_CUDA_INVALID;
+    }
+    const int grid = std::min((H + 255) / 256, 4 * dev->sms);
+    k_square<<<grid, 256, 0, dev->stream>>>(out, tp_send_rows(m), H);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    DITCH_CUDA(cudaMemsetAsync(out, 0, (size_t)H * 4, dev->stream));
+    if ((s = tp_allreduce_add(m, 1, out))) return s;
+    k_sqrt<<<grid, 256, 0, dev->stream>>>(out, H);
+    DITCH_LAUNCH(dev, cudaGetLastError());
+    return DITCH_CUDA_OK;
+}
 
 size_t tp_group_bytes(const Config &c, size_t max_tokens) {
     return 2 * align256(max_tokens * (size_t)c.hidden * 4);

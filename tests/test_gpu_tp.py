@@ -77,9 +77,18 @@ def _worker(rank, world, port, out_dir):
         m.apply_edit((1.2, 1.5, 0.5, 2.0), (1.1, 1.0, 0.4, 2.0), None)
     res3, log3 = one.forward(toks, rb, rp, cap, last)
     res4, log4 = tp.forward(toks, rb, rp, cap, last)
+    # row_normalization = pre: the row norms of o_proj / down_proj summed over
+    # the ranks' column shards (one all-reduce per matrix)
+    for m in (one, tp):
+        m.set_row_normalization("pre")
+        m.apply_edit((1.2, 1.5, 0.5, 2.0), (1.1, 1.0, 0.4, 2.0), None)
+    res5, log5 = one.forward(toks, rb, rp, cap, last)
+    res6, log6 = tp.forward(toks, rb, rp, cap, last)
+    for m in (one, tp):
+        m.set_row_normalization("none")
     group.barrier()
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), res1=res1, log1=log1, res2=res2, log2=log2, res3=res3, log3=log3,
-             res4=res4, log4=log4)
+             res4=res4, log4=log4, res5=res5, log5=log5, res6=res6, log6=log6)
     tp.close()
     one.close()
     dist.barrier()
@@ -96,12 +105,14 @@ def test_tensor_parallel_forward_matches_one_gpu(tmp_path):
         pytest.skip("needs two GPUs")
     mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
     z0, z1 = np.load(tmp_path / "r0.npz"), np.load(tmp_path / "r1.npz")
-    for key in ("res2", "log2", "res4", "log4"):
+    for key in ("res2", "log2", "res4", "log4", "res6", "log6"):
         assert np.array_equal(z0[key], z1[key]), key  # replicated streams are identical
-    for a, b in (("res1", "res2"), ("log1", "log2"), ("res3", "res4"), ("log3", "log4")):
+    for a, b in (("res1", "res2"), ("log1", "log2"), ("res3", "res4"), ("log3", "log4"), ("res5", "res6"),
+                 ("log5", "log6")):
         ref, got = z0[a], z0[b]
         err = float(np.abs(got - ref).max())
         bound = 2e-3 + 2e-2 * float(np.abs(ref).max())
         assert err <= bound, (a, b, err, bound)
         print(f"{a} vs {b}: max |err| {err:.3e} (bound {bound:.3e})")
     assert not np.array_equal(z0["log1"], z0["log3"]), "the edit changed nothing"
+    assert not np.array_equal(z0["log3"], z0["log5"]), "row normalisation changed nothing"
