@@ -308,8 +308,9 @@ int ditch_cuda_apply_edit(ditch_cuda_model *m, const ditch_cuda_params *attn_o, 
  * (Options.seed) from this library's own generator, not ditch's, so the two
  * agree to the SVD's accuracy. Routed experts get one such delta per edited
  * expert, the k of its seed counted as on one device, so expert-parallel
- * ranks agree with a single GPU. Tensor-parallel ranks (partial row norms)
- * return DITCH_CUDA_UNSUPPORTED. */
+ * ranks agree with a single GPU. On tensor-parallel ranks pre takes the row
+ * norms over all ranks' column shards (a collective of the group: every rank
+ * edits alike); full there returns DITCH_CUDA_UNSUPPORTED. */
 int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_rank, uint64_t seed);
 /* moe.applyExpertSelective, ranked selection (src/moe.zig:1373-1477): the
  * o_proj edit as above, then per MoE layer the top n_experts experts by
