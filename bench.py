@@ -169,9 +169,19 @@ def build_c2_model(dev, spec, seed, max_seq):
 class Clocks:
     def __init__(self, index):
         self.p = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{index}.csv")
+        self.keep = bool(os.environ.get("DITCH_BENCH_CLOCKS_DIR"))
+        import tempfile
+
+        # the samples go to a private temporary file; DITCH_BENCH_CLOCKS_DIR
+        # keeps them in a named folder instead
+        keep = os.environ.get("DITCH_BENCH_CLOCKS_DIR")
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            if keep:
+                os.makedirs(keep, exist_ok=True)
+                self.path = os.path.join(keep, f"clocks_bench_{index}_{os.getpid()}.csv")
+            else:
+                fd, self.path = tempfile.mkstemp(prefix=f"clocks_bench_{index}_", suffix=".csv")
+                os.close(fd)
             self.f = open(self.path, "w")
             self.p = subprocess.Popen(
                 ["nvidia-smi", "-i", str(index), "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
@@ -205,6 +215,11 @@ class Clocks:
             for n, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
+        if not self.keep:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
         if not sm:
             return None
         load = [s for s in sm if s > 0.5 * max(sm)] or sm

@@ -533,7 +533,7 @@ def build_c4_model(dev, spec, seed, max_seq, ep_rank=0, ep_world=1):
 
 
 def c4_flops(spec, tokens):
-    """Algorithmic FLOPs of one forward (SURVEY-style count: linear layers of
+    """Algorithmic FLOPs of one forward (counted per unit of work: linear layers of
     the attention, the router, top-k experts' SwiGLU, attention scores/values
     over causal prompts, the LM head on the last rows)."""
     H, L, E, k, mi = spec["hidden"], spec["n_layers"], spec["n_experts"], spec["top_k"], spec["moe_inter"]

@@ -247,6 +247,11 @@ int ditch_cuda_edit_weight_bf16(ditch_cuda_device *dev, void *w, size_t rows, si
                                 float alpha) {
     clear_error();
     REQUIRE(dev && w && r, "null argument");
+    // bf16 elements and f32 entries must sit on their own size; rows that are
+    // not 16-byte aligned take the kernels' 2-byte path
+    REQUIRE((reinterpret_cast<uintptr_t>(w) & 1) == 0, "w is not 2-byte aligned");
+    REQUIRE((reinterpret_cast<uintptr_t>(r) & 3) == 0, "r is not 4-byte aligned");
+    REQUIRE(rows <= (size_t)INT32_MAX && cols <= (size_t)INT32_MAX, "rows or cols above 2^31 - 1");
     if (rows == 0 || cols == 0) return DITCH_CUDA_OK;
     std::lock_guard<std::mutex> lk(dev->mu);
     DITCH_CUDA(cudaSetDevice(dev->ordinal));

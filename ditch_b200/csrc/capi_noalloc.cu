@@ -61,6 +61,12 @@ int ditch_cuda_edit_weight_bf16_noalloc(void *w, size_t rows, size_t cols, const
         ditch::set_error("edit_weight_bf16_noalloc: null argument");
         return DITCH_CUDA_INVALID;
     }
+    // bf16 elements and f32 entries must sit on their own size; rows that are
+    // not 16-byte aligned take the kernels' 2-byte path
+    if ((reinterpret_cast<uintptr_t>(w) & 1) || (reinterpret_cast<uintptr_t>(r) & 3)) {
+        ditch::set_error("edit_weight_bf16_noalloc: w must be 2-byte and r 4-byte aligned");
+        return DITCH_CUDA_INVALID;
+    }
     if (rows == 0 || cols == 0) return DITCH_CUDA_OK;
     if (rows > kNoAllocMaxRows || cols > kNoAllocMaxCols) {
         ditch::set_error("edit_weight_bf16_noalloc: %zu x %zu exceeds the fixed scratch (at most %zu rows and %zu "

@@ -74,12 +74,16 @@ inline int row_splits(int rows, int col_blocks, int min_rows = 64) {
 // (The reference skips rows with v[r] == 0, src/tensor.zig:1065-1068; for
 // finite weights those rows add exactly zero, so the stream reads every row
 // without a data-dependent branch and keeps four loads in flight.)
-__global__ void k_gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, int rows_per) {
+// `vec`: every row starts on a 16-byte boundary (w 16-byte aligned and cols a
+// multiple of 8), so a thread reads its 8 columns as one 16-byte load;
+// otherwise 2-byte loads.
+__global__ void k_gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, int rows_per,
+                              bool vec) {
     const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
     if (c0 >= cols) return;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (c0 + 8 <= cols && (cols & 7) == 0) {
+    if (vec && c0 + 8 <= cols) {
         const uint16_t *base = w + c0;
         int r = r0;
         for (; r + 4 <= r1; r += 4) {
@@ -546,7 +550,8 @@ cudaError_t gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, f
     const int cb = (cols + kGemvThreads * 8 - 1) / (kGemvThreads * 8);
     const int sp = row_splits(rows, cb);
     const int per = (rows + sp - 1) / sp;
-    k_gemv_t_bf16<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(w, rows, cols, v, out, per);
+    const bool vec = (cols & 7) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+    k_gemv_t_bf16<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(w, rows, cols, v, out, per, vec);
     return cudaGetLastError();
 }
 
@@ -615,7 +620,8 @@ cudaError_t row_norms_mxfp4(const uint8_t *blocks, const uint8_t *scales, int ro
 
 cudaError_t rank1_update_bf16(uint16_t *w, int rows, int cols, const float *b, const float *a, cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return cudaSuccess;
-    if ((cols & 7) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+    // 16-byte accesses need every row of w (and a) on a 16-byte boundary
+    if ((cols & 7) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
         const int cb = (cols + 2047) / 2048;
         int sp = std::max(1, (8 * 148 + cb - 1) / cb);
         sp = std::min(sp, std::max(1, rows / 16));

@@ -54,6 +54,9 @@ struct Layer {
     DevBuf e_edit_dev;                             // int [E]
     // row norms ||W_i|| for the pre-normalised edit (computed once; the base weights never change)
     DevBuf o_rn, down_rn, e_rn;                    // f32 [H], [H], [E][H]
+    // rn_pending: computed by the call in progress; rn_valid: by a call whose
+    // device status came back clean (only then are they reused)
+    bool rn_pending = false, rn_valid = false;
 };
 
 struct Config {

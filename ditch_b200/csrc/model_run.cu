@@ -568,25 +568,50 @@ int rank1_delta(ditch_cuda_model *m, const Mat &w, int row0, DevBuf &rn_cache, s
 }
 
 // Row norms of o_proj, down_proj and the routed experts' down projections of
-// layer li, computed on first use.
-int ensure_row_norms(ditch_cuda_model *m, Layer &L) {
+// one layer (under tensor parallelism summed over the ranks' column shards:
+// a collective). Marked pending; settle_row_norms marks them valid once the
+// call's device status is known to be clean.
+int compute_row_norms(ditch_cuda_model *m, Layer &L) {
     ditch_cuda_device *dev = m->dev;
     const int H = m->cfg.hidden;
     int s;
-    if (!L.o_rn.ptr) {  // under tensor parallelism summed over the column shards
-        DITCH_CUDA(L.o_rn.reserve((size_t)H * 4));
-        if ((s = tp_row_norms(m, L.o, L.o_rn.as<float>()))) return s;
-    }
-    if (!L.moe && !L.down_rn.ptr) {
+    L.rn_valid = false;
+    L.rn_pending = true;
+    DITCH_CUDA(L.o_rn.reserve((size_t)H * 4));
+    if ((s = tp_row_norms(m, L.o, L.o_rn.as<float>()))) return s;
+    if (!L.moe) {
         DITCH_CUDA(L.down_rn.reserve((size_t)H * 4));
         if ((s = tp_row_norms(m, L.down, L.down_rn.as<float>()))) return s;
-    }
-    if (L.moe && !L.e_rn.ptr) {
+    } else {
         const int E = m->cfg.e_loc;
         DITCH_CUDA(L.e_rn.reserve((size_t)E * H * 4));
         if ((s = mat_row_norms(dev, L.e_down, 0, E * H, L.e_rn.as<float>()))) return s;
     }
     return DITCH_CUDA_OK;
+}
+
+// Pending row norms become valid when the call that computed them ended with
+// a clean status (`ok`); otherwise (a peer wait that ran out, a failed step)
+// they are dropped and the next edit computes them again.
+void settle_row_norms(ditch_cuda_model *m, bool ok) {
+    for (Layer &L : m->layers)
+        if (L.rn_pending) {
+            L.rn_pending = false;
+            L.rn_valid = ok;
+        }
+}
+
+// The row norms of layer li, computed on first use. On a tensor-parallel
+// model they are a collective, so ditch_cuda_set_row_normalization computes
+// every layer's at once (every rank calls it once, in the same order) and an
+// edit never starts one.
+int ensure_row_norms(ditch_cuda_model *m, Layer &L) {
+    if (L.rn_valid || L.rn_pending) return DITCH_CUDA_OK;
+    if (m->cfg.tp_world > 1) {
+        set_error("row norms of this tensor-parallel model are missing: call set_row_normalization again");
+        return DITCH_CUDA_INVALID;
+    }
+    return compute_row_norms(m, L);
 }
 
 int apply_component_edit(ditch_cuda_model *m, int li, bool is_o, const float *v, float lambda) {
@@ -796,8 +821,8 @@ std::vector<uint32_t> rank(const std::vector<float> &s) {
     return order;
 }
 
-int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down, float di,
-                int use_di, bool selective, size_t n_experts, float strength) {
+int edit_body(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down, float di,
+              int use_di, bool selective, size_t n_experts, float strength) {
     const Config &c = m->cfg;
     clear_edits(m);
     m->seed_counter = 0;
@@ -837,6 +862,13 @@ int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditc
     }
     if ((s = upload_expert_flags(m))) return s;
     return check_status(m->dev, "apply_edit");
+}
+
+int edit_common(ditch_cuda_model *m, const ditch_cuda_params *attn_o, const ditch_cuda_params *mlp_down, float di,
+                int use_di, bool selective, size_t n_experts, float strength) {
+    const int s = edit_body(m, attn_o, mlp_down, di, use_di, selective, n_experts, strength);
+    settle_row_norms(m, s == DITCH_CUDA_OK);
+    return s;
 }
 
 int kl_score_impl(ditch_cuda_model *m, double *kl) {
@@ -1112,6 +1144,17 @@ int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_
                 kMaxDeltaRank);
     }
     std::lock_guard<std::mutex> lk(m->dev->mu);
+    if (mode >= 1 && m->cfg.tp_world > 1) {
+        // the shards' norms are summed over the group: every layer's now, in
+        // one call that every rank makes, so no edit issues a collective
+        DITCH_CUDA(cudaSetDevice(m->dev->ordinal));
+        int s = DITCH_CUDA_OK;
+        for (Layer &L : m->layers)
+            if (!L.rn_valid && (s = compute_row_norms(m, L))) break;
+        if (!s) s = check_status(m->dev, "set_row_normalization");
+        settle_row_norms(m, s == DITCH_CUDA_OK);
+        if (s) return s;
+    }
     m->row_norm = mode;
     if (mode == 2) {
         m->lora_rank = (int)lora_rank;

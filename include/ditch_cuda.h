@@ -336,7 +336,10 @@ int ditch_cuda_kl_score_prompts(ditch_cuda_model *m, const uint32_t *tokens, con
 
 /* The materialised rank-1 weight edit W <- W - alpha r (r^T W) on a bf16
  * matrix in device memory (GEMV-T then rank-1 update; the edited matrix of
- * src/abliterate.zig:544-552 rounded to bf16). r is a device f32 [rows]. */
+ * src/abliterate.zig:544-552 rounded to bf16). r is a device f32 [rows].
+ * w must be 2-byte and r 4-byte aligned (else DITCH_CUDA_INVALID); a w whose
+ * rows are not all 16-byte aligned (a view at an odd storage offset, or cols
+ * not a multiple of 8) is edited with 2-byte accesses, more slowly. */
 int ditch_cuda_edit_weight_bf16(ditch_cuda_device *dev, void *w, size_t rows, size_t cols, const float *r,
                                 float alpha);
 
@@ -349,7 +352,7 @@ int ditch_cuda_edit_weight_bf16(ditch_cuda_device *dev, void *w, size_t rows, si
  * the library, held by every GPU that loads it until the process exits; the
  * call itself allocates nothing. Limit: rows <= 65536 and cols <= 65536
  * (larger sizes return DITCH_CUDA_INVALID). w and r are device pointers of
- * the current device; the work is queued on `stream` (a cudaStream_t, NULL
+ * the current device, aligned as for ditch_cuda_edit_weight_bf16; the work is queued on `stream` (a cudaStream_t, NULL
  * for the default stream) and the call returns without waiting. The first
  * call on a device looks the array's device address up (cudaGetSymbolAddress)
  * with that device current; make that first call before any stream capture.

@@ -193,3 +193,14 @@ def test_edit_weight_bf16(device):
     want = oracle.materialize(wf, a, b)
     close(got, want, 2e-5, 8e-3)  # one bf16 rounding of the result
     assert np.abs(r @ got).max() < np.abs(r @ wf).max() * (1 - alpha) + 1e-3
+
+
+def test_edit_weight_bf16_rejects_odd_pointers(device):
+    """w must start on a 2-byte boundary and r on a 4-byte one; the check comes
+    before any launch (these dummy pointers are never dereferenced)."""
+    from ditch_b200 import DitchCudaError
+
+    with pytest.raises(DitchCudaError, match="aligned"):
+        device.edit_weight_bf16(17, 8, 8, 16, 1.0)
+    with pytest.raises(DitchCudaError, match="aligned"):
+        device.edit_weight_bf16(16, 8, 8, 18, 1.0)

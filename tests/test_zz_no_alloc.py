@@ -33,21 +33,31 @@ def test_no_alloc_edit_matches_edit_weight(device):
     lib = ditch_b200.lib()
     fn = lib.ditch_cuda_edit_weight_bf16_noalloc
     rng = np.random.default_rng(4242)
-    for rows, cols, alpha in ((512, 1536, 0.8), (96, 200, 1.3)):  # two calls in a row, the second smaller
+    # two calls in a row, the second smaller; the third edits a matrix that
+    # starts one element (2 bytes) past a 16-byte boundary, as a view at a
+    # storage offset does, which the kernels read and write 2 bytes at a time
+    for rows, cols, alpha, off in ((512, 1536, 0.8, 0), (96, 200, 1.3, 0), (64, 256, 0.9, 1)):
         w0 = oracle.f32_to_bf16_bits((rng.standard_normal((rows, cols)) * 0.02).astype(np.float32))
         r = rng.standard_normal(rows).astype(np.float32)
         r /= np.linalg.norm(r)
         rt = torch.from_numpy(r).cuda()
-        wa = torch.from_numpy(w0.view(np.int16).copy()).cuda()
-        wb = torch.from_numpy(w0.view(np.int16).copy()).cuda()
-        device.edit_weight_bf16(wa.data_ptr(), rows, cols, rt.data_ptr(), alpha)
+        flat = np.concatenate([np.zeros(off, np.uint16), w0.reshape(-1)])
+        wa = torch.from_numpy(flat.view(np.int16).copy()).cuda()
+        wb = torch.from_numpy(flat.view(np.int16).copy()).cuda()
+        pa, pb = wa.data_ptr() + 2 * off, wb.data_ptr() + 2 * off
+        assert (pb & 15) == (2 * off)  # torch's allocations start on 256-byte boundaries
+        device.edit_weight_bf16(pa, rows, cols, rt.data_ptr(), alpha)
         stream = torch.cuda.current_stream().cuda_stream
-        assert fn(C.c_void_p(wb.data_ptr()), rows, cols, C.c_void_p(rt.data_ptr()), alpha, C.c_void_p(stream)) == 0
+        assert fn(C.c_void_p(pb), rows, cols, C.c_void_p(rt.data_ptr()), alpha, C.c_void_p(stream)) == 0
         torch.cuda.synchronize()
-        got = oracle.bf16_bits_to_f32(wb.cpu().numpy().view(np.uint16))
-        want = oracle.bf16_bits_to_f32(wa.cpu().numpy().view(np.uint16))
+        got = oracle.bf16_bits_to_f32(wb.cpu().numpy().view(np.uint16)[off:].reshape(rows, cols))
+        want = oracle.bf16_bits_to_f32(wa.cpu().numpy().view(np.uint16)[off:].reshape(rows, cols))
         _close(got, want)
-        assert not np.array_equal(got, oracle.bf16_bits_to_f32(w0))  # the edit did something
+        # and against the oracle's f32 edit (src/abliterate.zig:264-280) rounded once to bf16
+        wf = oracle.bf16_bits_to_f32(w0)
+        a, b = oracle.compute_delta_none(wf, r, alpha)
+        _close(got, oracle.materialize(wf, a, b))
+        assert not np.array_equal(got, wf)  # the edit did something
 
 
 def test_no_alloc_edit_rejects_oversize():
@@ -56,3 +66,14 @@ def test_no_alloc_edit_rejects_oversize():
     dummy = C.c_void_p(16)  # never dereferenced: the size check comes first
     assert fn(dummy, 1 << 20, 8, dummy, 1.0, None) == cuda.INVALID
     assert b"exceeds the fixed scratch" in lib.ditch_cuda_last_error()
+
+
+def test_no_alloc_edit_rejects_odd_pointers():
+    """A bf16 matrix must start on a 2-byte boundary and r on a 4-byte one;
+    anything else is refused before a kernel is launched (the pointers here
+    are never dereferenced)."""
+    lib = ditch_b200.lib()
+    fn = lib.ditch_cuda_edit_weight_bf16_noalloc
+    assert fn(C.c_void_p(17), 8, 8, C.c_void_p(16), 1.0, None) == cuda.INVALID
+    assert b"aligned" in lib.ditch_cuda_last_error()
+    assert fn(C.c_void_p(16), 8, 8, C.c_void_p(18), 1.0, None) == cuda.INVALID
