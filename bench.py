@@ -49,11 +49,11 @@ def parse():
     ap.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline sample budget (seconds)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4", "c5", "gemm", "gen"],
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4", "c5", "gemm", "gen", "hbm"],
                     help="c2 (default): the FP8 dense trial loop; c1: the Qwen2-0.5B fp32 trial loop with the "
                          "whole-trial CPU baseline; c3: dequant + GEMM sweep; c4: the Qwen3-MoE MXFP4 "
                          "trial loop (expert-selective edit); c5: Llama-3-70B-shaped in-place edit sweep; gemm: one "
-                         "GEMM")
+                         "GEMM; hbm: the standalone decoders and the bf16 edit, one at a time")
     ap.add_argument("--max-new", type=int, default=100, help="gen: tokens generated per prompt")
     ap.add_argument("--row-normalization", default="none", choices=["none", "pre", "full"],
                     help="c1 / c2: the edit's row normalisation (full: rank-3 delta from the randomised SVD)")
@@ -336,7 +336,8 @@ def config_block(args):
                         "o_proj/down_proj + edited forward + first-token KL" % args.row_normalization,
             "row_normalization": args.row_normalization,
             "layers": args.layers, "prompts_per_gpu": args.prompts, "seq_len": args.seq, "vocab": C2["vocab"],
-            "parallelism": f"dp{args.gpus} (prompt batches)",
+            "parallelism": f"dp{args.gpus} (prompt batches; residual sums and KL summed over the ranks by the "
+                           "library's peer-group reduction over NVLink)",
             "l2": "inputs larger than L2 (7 GB of FP8 weights read per trial)",
             "fp8_decode": ("staged: each GEMM with >= %d tokens runs the bf16 GEMM over its FP8 weight decoded once "
                            "to bf16 (decoded on first use, the copy kept across trials: the weights never change, "
@@ -403,14 +404,27 @@ def main():
     bad = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
     kl_prompts = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
 
-    # one-off per study: capture, cross-rank residual sums, directions
+    # data parallel: the library sums the residuals and the KL over the ranks
+    # on the device (a peer group over NVLink); torch.distributed only carries
+    # the group's IPC handles and the timing barrier
+    group = None
+    if dist:
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+
+        group = ditch_b200.Group(dev, rank, world, model.dp_group_bytes(P), exchange)
+        model.set_dp_group(group)
+        group.barrier()
+        dist.barrier()
+
+    # one-off per study: capture (residual sums over every rank's prompts), directions
     dev.synchronize()
     dev.timer_start()
     gs, gc = model.residual_sums(good, window=1, batch_size=P)
     bs, bc = model.residual_sums(bad, window=1, batch_size=P)
-    gs, bs = all_reduce(dist, gs), all_reduce(dist, bs)
-    counts = all_reduce(dist, np.array([gc, bc], np.float64))
-    model.directions(gs, int(counts[0]), bs, int(counts[1]), True)
+    model.directions(gs, gc, bs, bc, True)
     capture_ms = dev.timer_stop()
     model.kl_init(kl_prompts)
     if args.row_normalization != "none":
@@ -425,9 +439,8 @@ def main():
     def step(e2e):
         po, pd, di = trial_params(trial_rng, L)
         model.apply_edit(po, pd, di)
-        kl = model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score()
-        tot = all_reduce(dist, np.array([kl * P, P], np.float64))
-        kls.append(tot[0] / tot[1])
+        # the mean KL over every rank's prompts (summed over the group on the device)
+        kls.append(model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score())
 
     def timed(e2e, steps):
         if dist:
@@ -489,7 +502,11 @@ def main():
         line["cpu_baseline"] = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in cb.items()}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    model.set_dp_group(None)
     model.close()
+    if group:
+        group.barrier()
+        group.close()
     dev.close()
     if dist:
         dist.barrier()

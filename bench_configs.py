@@ -324,6 +324,83 @@ def run_c5(args, dev):
           flush=True)
 
 
+def stored_bytes(fmt, rows, cols):
+    """Bytes of a weight as the library keeps it in HBM (the decoders' input):
+    FP8 codes + f32 128x128 block scales; MXFP4 nibbles + E8M0 per 32; INT4
+    words + f32 group scales + packed zero points (groups of 128); Q8_0
+    repacked to int8 codes + an f32 scale per 32; Q4_K repacked to nibbles +
+    an f32 (d*scale, dmin*min) pair per 32."""
+    n = rows * cols
+    if fmt == "fp8":
+        return n + (-(-rows // 128)) * (-(-cols // 128)) * 4
+    if fmt == "mxfp4":
+        return n // 2 + n // 32
+    if fmt == "int4":
+        g = cols // 128
+        return n // 2 + rows * g * 4 + (rows // 8) * g * 4
+    if fmt == "q8_0":
+        return n + n // 32 * 4
+    if fmt == "q4_k":
+        return n // 2 + n // 32 * 8
+    if fmt == "bf16":
+        return 2 * n
+    raise ValueError(fmt)
+
+
+def run_hbm(args, dev):
+    """The HBM-bound kernels one at a time, at sizes well above L2 (126 MB),
+    timed with CUDA events on the stream they run on:
+    * the standalone decoders (ditch_cuda_weight_decode: k_dequant_fp8_bf16,
+      k_dequant_mxfp4_bf16, k_dequant_int_bf16, k_stage_decode for the
+      repacked Q8_0 / Q4_K) of a 28672 x 8192 weight (C5's down_proj shape):
+      algorithmic bytes = stored bytes in + 2 B per element out;
+    * the in-place rank-1 edit of the same shape in bf16 (k_gemv_t_bf16 then
+      k_rank1_bf16): 3 x 2 B per element (GEMV-T read, update read + write).
+    One line per kernel family, GB/s against the measured HBM copy bandwidth."""
+    import torch
+
+    hbm, tf, src = _peaks()
+    rows, cols = args.rows if args.rows != 4096 else 28672, args.cols if args.cols != 4096 else 8192
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    out = torch.empty(rows, cols, dtype=torch.bfloat16, device="cuda")
+    results = []
+    for fmt in ("fp8", "mxfp4", "int4", "q8_0", "q4_k"):
+        W, _ = make_weight(dev, fmt, rows, cols, gen)
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            W.decode(out.data_ptr())
+        dev.synchronize()
+        dev.timer_start()
+        for _ in range(args.steps):
+            W.decode(out.data_ptr())
+        ms = dev.timer_stop() / args.steps
+        algo = stored_bytes(fmt, rows, cols) + 2 * rows * cols
+        r = {"kernel": f"decode {fmt} -> bf16", "shape": [rows, cols], "ms": round(ms, 4),
+             "algorithmic_bytes": algo, "gbs": round(algo / ms / 1e6, 1), "frac": round(algo / ms / 1e6 / hbm, 4)}
+        results.append(r)
+        print(json.dumps(r), flush=True)
+        W.close()
+        torch.cuda.empty_cache()
+    w = out
+    w.normal_(0.0, 0.02, generator=gen)
+    r_vec = torch.randn(rows, generator=gen, device="cuda")
+    r_vec /= r_vec.norm()
+    for _ in range(args.warmup):
+        dev.edit_weight_bf16(w.data_ptr(), rows, cols, r_vec.data_ptr(), 0.5)
+    dev.synchronize()
+    dev.timer_start()
+    for _ in range(args.steps):
+        dev.edit_weight_bf16(w.data_ptr(), rows, cols, r_vec.data_ptr(), 0.5)
+    ms = dev.timer_stop() / args.steps
+    algo = 3 * 2 * rows * cols
+    r = {"kernel": "edit bf16 (GEMV-T + rank-1 update)", "shape": [rows, cols], "ms": round(ms, 4),
+         "algorithmic_bytes": algo, "gbs": round(algo / ms / 1e6, 1), "frac": round(algo / ms / 1e6 / hbm, 4)}
+    results.append(r)
+    print(json.dumps(r), flush=True)
+    print(json.dumps({"config": "hbm", "kernels": len(results), "peak_gbs": hbm, "peak_source": src,
+                      "l2": "every input larger than L2 (126 MB)"}), flush=True)
+
+
 C1 = dict(n_layers=24, hidden=896, heads=14, kv_heads=2, head_dim=64, inter=4864, vocab=151936, eps=1e-6,
           rope_theta=1e6, tied=True)
 
@@ -898,6 +975,8 @@ def run(args):
         run_c5(args, dev)
     elif args.config == "gen":
         run_gen(args, dev)
+    elif args.config == "hbm":
+        run_hbm(args, dev)
     else:
         raise SystemExit(f"config {args.config} is not implemented")
     dev.close()

@@ -121,6 +121,9 @@ struct ditch_cuda_model {
     bool kl_ready = false;
     std::vector<size_t> kl_offsets;
     std::vector<uint32_t> kl_tokens_host;
+    // data parallelism: residual sums and KL combined over this group's ranks
+    ditch_cuda_group *dp_group = nullptr;
+    ditch::DevBuf dp_buf;  // f64 [2] reduced KL sum and count / [1 + entries * H] sums to reduce
     // expert parallelism: the peer group and this rank's receive-side scratch
     ditch_cuda_group *group = nullptr;
     size_t group_tokens = 0;  // most tokens per rank per forward

@@ -878,6 +878,18 @@ int kl_score_impl(ditch_cuda_model *m, double *kl) {
     if ((s = forward_batch(m, m->kl, 0, P))) return s;
     DITCH_CUDA(m->kl_vals.reserve((size_t)P * 8));
     DITCH_LAUNCH(dev, kl_rows(m->kl_base.as<float>(), m->logits.as<float>(), P, V, m->kl_vals.as<double>(), dev->stream));
+    if (m->dp_group) {
+        // data parallel: every rank's per-prompt values summed in rank order,
+        // then prompt order (one device's order over the concatenated prompts)
+        double tot[2] = {0.0, 0.0};
+        DITCH_CUDA(m->dp_buf.reserve(2 * 8));
+        if ((s = dp_ordered_sum(dev, m->dp_group, m->kl_vals.as<double>(), (size_t)P, m->dp_buf.as<double>())))
+            return s;
+        DITCH_CUDA(cudaMemcpyAsync(tot, m->dp_buf.ptr, 2 * 8, cudaMemcpyDeviceToHost, dev->stream));
+        if ((s = check_status(dev, "kl_score"))) return s;
+        *kl = tot[0] / std::max(tot[1], 1.0);
+        return DITCH_CUDA_OK;
+    }
     std::vector<double> per(P);
     DITCH_CUDA(cudaMemcpyAsync(per.data(), m->kl_vals.ptr, (size_t)P * 8, cudaMemcpyDeviceToHost, dev->stream));
     if ((s = check_status(dev, "kl_score"))) return s;
@@ -978,11 +990,24 @@ int ditch_cuda_residual_sums(ditch_cuda_model *m, const uint32_t *tokens, const 
                                         (int)np, m->sums.as<double>(), dev->stream));
         DITCH_CUDA(cudaStreamSynchronize(dev->stream));
     }
-    std::vector<double> hs(entries * H);
-    DITCH_CUDA(cudaMemcpyAsync(hs.data(), m->sums.ptr, hs.size() * 8, cudaMemcpyDeviceToHost, dev->stream));
+    const size_t n = entries * H;
+    std::vector<double> hs(n + 1);
+    if (m->dp_group) {
+        // data parallel: [sums, prompt count] summed over the group's ranks
+        DITCH_CUDA(m->dp_buf.reserve((2 * n + 2) * 8));
+        double *src = m->dp_buf.as<double>(), *dst = src + n + 1;
+        const double np = (double)n_prompts;
+        DITCH_CUDA(cudaMemcpyAsync(src, m->sums.ptr, n * 8, cudaMemcpyDeviceToDevice, dev->stream));
+        DITCH_CUDA(cudaMemcpyAsync(src + n, &np, 8, cudaMemcpyHostToDevice, dev->stream));
+        if ((s = dp_allreduce_sum(dev, m->dp_group, src, n + 1, dst))) return s;
+        DITCH_CUDA(cudaMemcpyAsync(hs.data(), dst, (n + 1) * 8, cudaMemcpyDeviceToHost, dev->stream));
+    } else {
+        DITCH_CUDA(cudaMemcpyAsync(hs.data(), m->sums.ptr, n * 8, cudaMemcpyDeviceToHost, dev->stream));
+        hs[n] = (double)n_prompts;
+    }
     if ((s = check_status(dev, "residual_sums"))) return s;
-    for (size_t i = 0; i < hs.size(); i++) sums[i] += hs[i];
-    *count += n_prompts;
+    for (size_t i = 0; i < n; i++) sums[i] += hs[i];
+    *count += (uint64_t)hs[n];
     return DITCH_CUDA_OK;
 }
 

@@ -54,6 +54,7 @@ struct ditch_cuda_group {
     ditch::PeerPtrs peers{};        // every rank's region in this process
     bool opened = false;
     uint64_t epoch = 0;             // last exchange started
+    uint64_t dp_calls = 0;          // data-parallel reductions so far (their half of the region alternates)
 };
 
 namespace ditch {
@@ -65,4 +66,15 @@ inline uint8_t *peer_data(uint8_t *region) { return region + kPeerFlagBytes; }
 // then wait (bounded by budget_s; then the status word reports a timeout)
 // until every peer has signalled it.
 int group_exchange(ditch_cuda_device *dev, ditch_cuda_group *g, double budget_s);
+
+// Data-parallel reductions over a group (dp.cu), on the device's stream.
+// dst[i] = sum over ranks, in rank order, of every rank's src[i] (device
+// pointers, n doubles; the same bits on every rank).
+int dp_allreduce_sum(ditch_cuda_device *dev, ditch_cuda_group *g, const double *src, size_t n, double *dst);
+// out[0] = the sum of every rank's `count` values taken one after another in
+// rank order, then in each rank's own order (the order one device would sum
+// the concatenated prompts in); out[1] = the total count.
+int dp_ordered_sum(ditch_cuda_device *dev, ditch_cuda_group *g, const double *vals, size_t count, double *out);
+// Region bytes a group needs for dp_ordered_sum of `count` values.
+size_t dp_ordered_bytes(size_t count);
 }  // namespace ditch

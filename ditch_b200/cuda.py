@@ -137,6 +137,9 @@ SIGNATURES = {
     "ditch_cuda_group_barrier": (C.c_int, [vp]),
     "ditch_cuda_model_group_bytes": (sz, [vp, sz]),
     "ditch_cuda_model_set_group": (C.c_int, [vp, vp, sz]),
+    "ditch_cuda_model_dp_group_bytes": (sz, [vp, sz]),
+    "ditch_cuda_model_set_dp_group": (C.c_int, [vp, vp]),
+    "ditch_cuda_group_allreduce_f64": (C.c_int, [vp, f64p, sz]),
     "ditch_cuda_set_profiling": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_gemm_stats": (C.c_int, [vp, f64p, u64p, f64p]),
     "ditch_cuda_reset_stats": (C.c_int, [vp]),
@@ -478,6 +481,13 @@ class Group:
     def barrier(self):
         check(lib().ditch_cuda_group_barrier(self.h))
 
+    def allreduce_f64(self, values):
+        """Every rank's f64 array summed over the group (rank order, the same
+        bits on every rank); returns a new array."""
+        out = np.array(values, np.float64, copy=True).reshape(-1)
+        check(lib().ditch_cuda_group_allreduce_f64(self.h, _p(out, f64p), out.size))
+        return out.reshape(np.shape(values))
+
     def close(self):
         if self.h:
             lib().ditch_cuda_group_free(self.h)
@@ -610,6 +620,15 @@ class Model:
         """Runs the model expert- or tensor-parallel (as loaded) over `group`."""
         check(lib().ditch_cuda_model_set_group(self.h, group.h, max_tokens))
         self._group = group  # the group outlives the model's use of it
+
+    def dp_group_bytes(self, max_prompts):
+        """Peer-group region bytes the data-parallel reductions need."""
+        return int(lib().ditch_cuda_model_dp_group_bytes(self.h, max_prompts))
+
+    def set_dp_group(self, group):
+        """Residual sums and KL combined over `group`'s ranks (None detaches)."""
+        check(lib().ditch_cuda_model_set_dp_group(self.h, group.h if group else None))
+        self._dp_group = group
 
     def forward(self, tokens, row_b, row_pos, capture_rows=(), logit_rows=()):
         s = self.spec

@@ -437,6 +437,28 @@ size_t ditch_cuda_model_group_bytes(const ditch_cuda_model *m, size_t max_tokens
  * the same experts on all ranks. Every rank must make the same calls in the
  * same order (forward, residual sums, edits, KL). */
 int ditch_cuda_model_set_group(ditch_cuda_model *m, ditch_cuda_group *g, size_t max_tokens);
+/* Data parallel (the prompt batches of src/engine.zig:383-435 split over the
+ * ranks, every rank holding the same weights and making the same edits):
+ * once a model has a data-parallel group, ditch_cuda_residual_sums returns
+ * the sums and the prompt count of every rank's prompts (each call's sums
+ * added over the ranks, in rank order), and ditch_cuda_kl_score /
+ * ditch_cuda_kl_score_prompts return the mean KL over every rank's prompts,
+ * the per-prompt values added in rank order and then prompt order, as
+ * src/scorers.zig:385-400 adds them for the concatenated prompts. The sums
+ * run on the device over NVLink (one exchange each); every rank gets the same
+ * bits. Every rank must make the same calls in the same order. The group must
+ * not be the model's tensor- or expert-parallel group; its region needs
+ * ditch_cuda_model_dp_group_bytes(m, most prompts per KL call) bytes. NULL
+ * detaches it. Replaces the host's own loops over prompt batches
+ * (src/engine.zig:314-438) and prompts (src/scorers.zig:378-402) when the
+ * prompts are spread over GPUs; no counterpart in the reference. */
+size_t ditch_cuda_model_dp_group_bytes(const ditch_cuda_model *m, size_t max_prompts);
+int ditch_cuda_model_set_dp_group(ditch_cuda_model *m, ditch_cuda_group *g);
+/* data[i] <- the sum over the group's ranks of data[i] (host f64 arrays, n
+ * values; added in rank order on the device, the same bits on every rank): a
+ * host-side counter or score summed over the ranks (a refusal count of
+ * src/scorers.zig:95-155, for instance). Every rank calls it with the same n. */
+int ditch_cuda_group_allreduce_f64(ditch_cuda_group *g, double *data, size_t n);
 
 /* ---- timing support (CUDA events on the device's stream) ---- */
 /* Accumulated device time and launch count of the weight GEMMs since the

@@ -117,6 +117,7 @@ def lib():
         L.or_residual_sums.argtypes = [f32p, C.c_size_t, C.c_size_t, C.c_size_t, szp, szp, C.c_size_t, f64p]
         L.or_kl_first_token.restype = C.c_double
         L.or_kl_first_token.argtypes = [f32p, f32p, C.c_size_t, C.c_size_t, f64p]
+        L.or_f32_to_bf16_array.argtypes = [f32p, C.c_size_t, u16p]
         L.or_set_threads.argtypes = [C.c_int]
         L.or_get_threads.restype = C.c_int
         _LIB = L
@@ -142,8 +143,14 @@ def bf16_bits_to_f32(bits):
 
 
 def f32_to_bf16_bits(x):
-    """src/tensor.zig:423-430 in numpy (round to nearest even, NaN kept quiet)."""
-    b = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    """src/tensor.zig:423-430 (round to nearest even, NaN kept quiet): in C
+    over all threads for large arrays, in numpy otherwise."""
+    x = np.ascontiguousarray(x, np.float32)
+    if x.size >= (1 << 20):
+        out = np.empty(x.shape, np.uint16)
+        lib().or_f32_to_bf16_array(ptr(x), x.size, ptr(out, u16p))
+        return out
+    b = x.view(np.uint32)
     nan = (b & 0x7FFFFFFF) > 0x7F800000
     r = ((b + np.uint32(0x7FFF) + ((b >> 16) & 1)) >> 16).astype(np.uint16)
     return np.where(nan, ((b >> 16) | 0x40).astype(np.uint16), r)

@@ -72,6 +72,7 @@ void or_quant_q4_k(const float *x, uint8_t *out, size_t n);
 
 /* ---- safetensors dequant to bf16 (src/dequant.zig:259-673) ---- */
 float or_e4m3_value(uint8_t code);
+void or_f32_to_bf16_array(const float *x, size_t n, uint16_t *out);
 float or_e8m0_scale(uint8_t b);
 /* bf16(e4m3[code] * scale[r / br][c / bc]) (src/dequant.zig:477-514). */
 void or_dequant_fp8(const uint8_t *codes, const float *scales, size_t rows, size_t cols,

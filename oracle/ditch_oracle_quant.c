@@ -265,7 +265,8 @@ static const float e2m1[16] = {0, 0.5f, 1, 1.5f, 2, 3, 4, 6, -0.0f, -0.5f, -1, -
 void or_dequant_fp8(const uint8_t *codes, const float *scales, size_t rows, size_t cols,
                     size_t br, size_t bc, uint16_t *out) {
     size_t scols = (cols + bc - 1) / bc;
-    for (size_t r = 0; r < rows; r++)
+#pragma omp parallel for schedule(static) num_threads(or_get_threads())
+    for (long r = 0; r < (long)rows; r++)
         for (size_t c = 0; c < cols; c++)
             out[r * cols + c] = or_f32_to_bf16(or_e4m3_value(codes[r * cols + c]) * scales[(r / br) * scols + c / bc]);
 }
@@ -319,7 +320,8 @@ void or_dequant_int_packed(const uint32_t *packed, size_t wpr, const float *scal
 void or_dequant_mxfp4_packed(const uint8_t *blocks, const uint8_t *scales, size_t rows,
                              size_t cols, uint16_t *out) {
     size_t nblk = cols / 32, rb = cols / 2;
-    for (size_t r = 0; r < rows; r++)
+#pragma omp parallel for schedule(static) num_threads(or_get_threads())
+    for (long r = 0; r < (long)rows; r++)
         for (size_t k = 0; k < nblk; k++) {
             float sc = or_e8m0_scale(scales[r * nblk + k]);
             for (int j = 0; j < 16; j++) {
@@ -346,24 +348,39 @@ void or_dequant_mxfp4_transposed(const uint8_t *blocks, const uint8_t *scales,
 }
 
 /* ---- synthetic-data quantisers: tools/make_fixture.py ---- */
+/* The nearest code with the first code winning a tie, as an argmin over all
+ * 256 codes in code order gives: the magnitudes of codes 0..126 ascend and
+ * the negative codes 128..254 mirror them, so |x| is placed among the 127
+ * magnitudes (a tie goes to the smaller one, the lower code) and the sign
+ * bit is added for x < 0 unless the nearest magnitude is zero (+0, code 0,
+ * comes before -0). |x - t| is sign-symmetric in float, so the distances are
+ * the ones the full scan compares. */
+static float g_e4m3_mag[127];
+static int g_e4m3_ready = 0;
+
+static void e4m3_table(void) {
+    if (g_e4m3_ready) return;
+    for (int c = 0; c < 127; c++) g_e4m3_mag[c] = or_e4m3_value((uint8_t)c);
+    g_e4m3_ready = 1;
+}
+
 static uint8_t nearest_e4m3(float x) {
-    float best = INFINITY;
-    int bi = 0;
-    for (int c = 0; c < 256; c++) {
-        float t = or_e4m3_value((uint8_t)c);
-        if (isnan(t)) continue;
-        float d = fabsf(x - t);
-        if (d < best) { best = d; bi = c; } /* argmin keeps the first */
+    const float a = fabsf(x);
+    int lo = 0, hi = 126;  /* first k with mag[k] >= a, or 126 */
+    while (lo < hi) {
+        int mid = (lo + hi) / 2;
+        if (g_e4m3_mag[mid] >= a) hi = mid; else lo = mid + 1;
     }
-    return (uint8_t)bi;
+    int k = lo;
+    if (k > 0 && fabsf(a - g_e4m3_mag[k - 1]) <= fabsf(a - g_e4m3_mag[k])) k--;
+    return (uint8_t)(x < 0 && k > 0 ? (0x80 | k) : k);
 }
 
 /* quant_fp8_block: make_fixture.py:109-127 (scale = max(amax, 1e-12) / 448). */
 void or_quant_fp8_block(const float *w, size_t rows, size_t cols, size_t br, size_t bc,
                         uint8_t *codes, float *scales) {
     size_t nb0 = (rows + br - 1) / br, nb1 = (cols + bc - 1) / bc;
-    uint8_t lut_ready = 0;
-    (void)lut_ready;
+    e4m3_table();
 #pragma omp parallel for schedule(dynamic) num_threads(or_get_threads())
     for (long bi = 0; bi < (long)(nb0 * nb1); bi++) {
         size_t i = (size_t)bi / nb1, j = (size_t)bi % nb1;
@@ -444,4 +461,10 @@ void or_quant_int_packed(const float *w, size_t rows, size_t cols, int bits, siz
             zeros[wd * groups + g] |= uz << off;
             if (off + bits > 32) zeros[(wd + 1) * groups + g] |= uz >> (32 - off);
         }
+}
+
+/* f32 -> bf16 bits over an array (src/tensor.zig:423-430 per element). */
+void or_f32_to_bf16_array(const float *x, size_t n, uint16_t *out) {
+#pragma omp parallel for schedule(static) num_threads(or_get_threads())
+    for (long i = 0; i < (long)n; i++) out[i] = or_f32_to_bf16(x[i]);
 }

@@ -8,19 +8,40 @@ import oracle
 
 
 def make_model(seed, n_layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, inter=512, vocab=300,
-               qk_norm=False, qkv_bias=False, fmt="bf16", block=(128, 128), moe=None):
+               qk_norm=False, qkv_bias=False, fmt="bf16", block=(128, 128), moe=None, eps=1e-6, rope_theta=1e4,
+               share_embed_data=False, device_normals=False):
+    """share_embed_data: the LM head is given the embedding's values (still
+    two tensors, loaded and read separately), which halves the host memory
+    of the large-vocabulary shapes. device_normals: the N(0, 1) draws come
+    from torch's seeded CUDA generator and are copied to the host (the
+    billion-value shapes take minutes with numpy's generator)."""
     from ditch_b200 import Tensor
 
     rng = np.random.default_rng(seed)
+    gen = None
+    if device_normals:
+        import torch
+
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+
+    def normal(shape):
+        if gen is None:
+            return rng.standard_normal(shape, dtype=np.float32)
+        import torch
+
+        return torch.randn(shape, generator=gen, device="cuda", dtype=torch.float32).cpu().numpy()
     spec = dict(n_layers=n_layers, hidden=hidden, heads=heads, kv_heads=kv_heads, head_dim=head_dim, inter=inter,
-                vocab=vocab, eps=1e-6, rope_theta=1e4, qk_norm=int(qk_norm), tied=False)
+                vocab=vocab, eps=eps, rope_theta=rope_theta, qk_norm=int(qk_norm), tied=False)
     if moe:
         spec.update(n_experts=moe["experts"], top_k=moe["top_k"], moe_inter=moe["inter"], norm_topk=1,
                     moe_layers=[True] * n_layers)
     f32, tensors = {}, []
 
     def bf16(shape, scale=0.02):
-        bits = oracle.f32_to_bf16_bits((rng.standard_normal(shape) * scale).astype(np.float32))
+        x = normal(shape)
+        x *= np.float32(scale)
+        bits = oracle.f32_to_bf16_bits(x)
+        del x
         return bits, oracle.bf16_bits_to_f32(bits)
 
     def add(name, rows, cols, quant=False, slabs=None):
@@ -61,7 +82,11 @@ def make_model(seed, n_layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, i
 
     qd, kvd = heads * head_dim, kv_heads * head_dim
     add("embed", vocab, hidden)
-    add("lm_head", vocab, hidden)
+    if share_embed_data:
+        f32["lm_head"] = f32["embed"]
+        tensors.append(Tensor("lm_head", "bf16", vocab, hidden, tensors[-1].data))
+    else:
+        add("lm_head", vocab, hidden)
     vec("final_norm", hidden)
     for i in range(n_layers):
         vec(f"L{i}.input_norm", hidden)
