@@ -137,9 +137,12 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_attention_decode(DecodeAttnP
         }
     }
     __syncthreads();
-    uint16_t *dst = p.out + (long long)r * qd + kvh * groups * hd;
-    for (int i = threadIdx.x; i < groups * hd; i += blockDim.x)
-        dst[i] = f32_to_bf16_bits(acc[i] * (1.0f / ml[2 * (i / hd) + 1]));
+    const long long o0 = (long long)r * qd + kvh * groups * hd;
+    for (int i = threadIdx.x; i < groups * hd; i += blockDim.x) {
+        const float y = acc[i] * (1.0f / ml[2 * (i / hd) + 1]);
+        if (p.out_f32) p.out_f32[o0 + i] = y;
+        else p.out[o0 + i] = f32_to_bf16_bits(y);
+    }
 }
 
 // ---- single-token attention, register path (head size 64 / 128) -----------
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(kRegWarps * 32) k_attention_decode_reg(DecodeA
 #pragma unroll
         for (int d = 0; d < D; d++) s_acc[warp][h][lane * D + d] = acc[h][d];
     __syncthreads();
-    uint16_t *dst = p.out + (long long)r * qd + (long long)kvh * G * HD;
+    const long long o0 = (long long)r * qd + (long long)kvh * G * HD;
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int h = i / HD, d = i - h * HD;
         float mx = -INFINITY;
@@ -273,7 +276,8 @@ __global__ void __launch_bounds__(kRegWarps * 32) k_attention_decode_reg(DecodeA
             num = fmaf(s_acc[w][h][d], e, num);
             den = fmaf(s_l[w][h], e, den);
         }
-        dst[i] = f32_to_bf16_bits(num / den);
+        if (p.out_f32) p.out_f32[o0 + i] = num / den;
+        else p.out[o0 + i] = f32_to_bf16_bits(num / den);
     }
 }
 

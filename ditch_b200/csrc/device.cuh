@@ -98,6 +98,7 @@ struct ditch_cuda_device {
     int stage_min_tokens = 1024;
     bool deterministic = false;  // K splits summed in a fixed order (no atomics)
     bool decode_cache = true;    // staged GEMMs keep their weight's bf16 copy
+    bool f32_split = false;      // models loaded next run f32-level split-bf16 products
     // profiling of GEMMs
     bool profiling = false;
     std::vector<ditch::GemmEvent> events;

@@ -41,7 +41,7 @@ __global__ void k_embed(const void *table, int table_bf16, const uint32_t *token
 // out = x * inv * w) to bf16; the captured copy is the un-normalised row.
 template <int HIDDEN_MAX>
 __global__ void k_rmsnorm_bf16(const float *x, const float *w, int n, int hidden, float eps, uint16_t *h,
-                               const int *cap_slot, float *res, const int *row_index) {
+                               const int *cap_slot, float *res, const int *row_index, int split_k) {
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= n) return;
@@ -58,9 +58,22 @@ __global__ void k_rmsnorm_bf16(const float *x, const float *w, int n, int hidden
     }
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / (float)hidden + eps);
-    uint16_t *hr = h + (long long)row * hidden;
     const int slot = cap_slot ? cap_slot[src] : -1;
     float *cr = slot >= 0 ? res + (long long)slot * hidden : nullptr;
+    if (split_k > 0) {  // f32-level operand: [hi | hi | lo] segments of split_k columns (padding zero)
+        uint16_t *hr = h + (long long)row * 3 * split_k;
+        for (int i = lane; i < split_k; i += 32) {
+            const float v = i < hidden ? xr[i] : 0.0f;
+            const float y = i < hidden ? v * inv * w[i] : 0.0f;
+            const uint16_t hi = f32_to_bf16_bits(y);
+            hr[i] = hi;
+            hr[split_k + i] = hi;
+            hr[2 * split_k + i] = f32_to_bf16_bits(y - bf16_bits_to_f32(hi));
+            if (cr && i < hidden) cr[i] = v;
+        }
+        return;
+    }
+    uint16_t *hr = h + (long long)row * hidden;
     if ((hidden & 3) == 0) {  // four elements per lane and access
         for (int i = lane * 4; i < hidden; i += 128) {
             const float4 v = *reinterpret_cast<const float4 *>(xr + i);
@@ -199,8 +212,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnParams p) {
         }
         if (active) {
             const float inv = 1.0f / l;
-            uint16_t *dst = p.out + (long long)(start + qi) * qd + h * hd;
-            for (int i = lane; i < hd; i += 32) dst[i] = f32_to_bf16_bits(acc[i] * inv);
+            if (p.out_f32) {
+                float *dst = p.out_f32 + (long long)(start + qi) * qd + h * hd;
+                for (int i = lane; i < hd; i += 32) dst[i] = acc[i] * inv;
+            } else {
+                uint16_t *dst = p.out + (long long)(start + qi) * qd + h * hd;
+                for (int i = lane; i < hd; i += 32) dst[i] = f32_to_bf16_bits(acc[i] * inv);
+            }
         }
         __syncwarp();
     }
@@ -460,6 +478,15 @@ __global__ void __launch_bounds__(128) k_attention_mma(AttnParams p) {
 #pragma unroll
         for (int d = 0; d < HD / 8; d++) {
             const int dim = h * HD + 8 * d + 2 * t;
+            if (p.out_f32) {
+                if (row_a < len)
+                    *reinterpret_cast<float2 *>(p.out_f32 + (long long)(start + row_a) * qd + dim) =
+                        make_float2(o[d][0] * inv_a, o[d][1] * inv_a);
+                if (row_b < len)
+                    *reinterpret_cast<float2 *>(p.out_f32 + (long long)(start + row_b) * qd + dim) =
+                        make_float2(o[d][2] * inv_b, o[d][3] * inv_b);
+                continue;
+            }
             if (row_a < len)
                 *reinterpret_cast<uint32_t *>(p.out + (long long)(start + row_a) * qd + dim) =
                     pack_bf16x2(o[d][0] * inv_a, o[d][1] * inv_a);
@@ -547,9 +574,9 @@ cudaError_t embed_rows(const void *table, int table_bf16, const uint32_t *tokens
 }
 
 cudaError_t rmsnorm_rows_bf16(const float *x, const float *w, int n, int hidden, float eps, uint16_t *h,
-                              const int *cap_slot, float *res, const int *row_index, cudaStream_t st) {
+                              const int *cap_slot, float *res, const int *row_index, cudaStream_t st, int split_k) {
     if (n <= 0) return cudaSuccess;
-    k_rmsnorm_bf16<0><<<(n + 7) / 8, 256, 0, st>>>(x, w, n, hidden, eps, h, cap_slot, res, row_index);
+    k_rmsnorm_bf16<0><<<(n + 7) / 8, 256, 0, st>>>(x, w, n, hidden, eps, h, cap_slot, res, row_index, split_k);
     return cudaGetLastError();
 }
 
@@ -561,8 +588,8 @@ cudaError_t rmsnorm_rows_f32(const float *x, const float *w, int n, int len, flo
 }
 
 cudaError_t gather_rmsnorm_bf16(const float *x, const int *rows, int n, int hidden, float eps, const float *w,
-                                uint16_t *h, cudaStream_t st) {
-    return rmsnorm_rows_bf16(x, w, n, hidden, eps, h, nullptr, nullptr, rows, st);
+                                uint16_t *h, cudaStream_t st, int split_k) {
+    return rmsnorm_rows_bf16(x, w, n, hidden, eps, h, nullptr, nullptr, rows, st, split_k);
 }
 
 bool attention_prefill_preps_in_place(int head_dim, int force_generic) {
@@ -599,6 +626,113 @@ cudaError_t rowdot_bf16_strided(const uint16_t *act, const float *a, int m, int 
                                 cudaStream_t st) {
     if (m <= 0) return cudaSuccess;
     k_rowdot_bf16<<<(m + 7) / 8, 256, 0, st>>>(act, a, m, k, xa, stride);
+    return cudaGetLastError();
+}
+
+// ---- split operands -------------------------------------------------------
+namespace {
+
+__device__ __forceinline__ void split_store(uint16_t *row, int kp, int c, float v, bool weight) {
+    const uint16_t hi = f32_to_bf16_bits(v);
+    const uint16_t lo = f32_to_bf16_bits(v - bf16_bits_to_f32(hi));
+    row[c] = hi;
+    row[kp + c] = weight ? lo : hi;
+    row[2 * kp + c] = weight ? hi : lo;
+}
+
+// One thread per (row, column < kp); columns past k are zero.
+__global__ void k_split_rows(const float *x, long long rows, int k, int kp, uint16_t *out, bool weight) {
+    const long long total = rows * kp;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / kp;
+        const int c = (int)(e - r * kp);
+        split_store(out + r * 3 * kp, kp, c, c < k ? x[r * k + c] : 0.0f, weight);
+    }
+}
+
+// silu(g) * u with the scalar exp (src/tensor.zig:1212-1214, 1334-1337).
+__global__ void k_swiglu_split(const float *gu, long long n, int inter, int kp, float *act32, uint16_t *act) {
+    const long long total = n * kp;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / kp;
+        const int c = (int)(e - r * kp);
+        float y = 0.0f;
+        if (c < inter) {
+            const float g = gu[r * 2 * inter + c], u = gu[r * 2 * inter + inter + c];
+            y = g / (1.0f + expf(-g)) * u;
+        }
+        act32[r * kp + c] = y;
+        split_store(act + r * 3 * kp, kp, c, y, false);
+    }
+}
+
+// Warp per row.
+__global__ void k_rowdot_f32(const float *x, const float *a, int m, int k, float *xa, int stride) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= m) return;
+    const float *xr = x + (long long)row * k;
+    float s = 0.0f;
+    for (int i = lane; i < k; i += 32) s = fmaf(xr[i], a[i], s);
+    s = warp_sum(s);
+    if (lane == 0) xa[(long long)row * stride] = s;
+}
+
+__global__ void k_add_split_halves(const float *s, int kp, float *out) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c < kp) out[c] = s[c] + s[kp + c];
+}
+
+__global__ void k_merge_split(const uint16_t *split, long long rows, int kp, float *out) {
+    const long long total = rows * kp;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / kp;
+        const int c = (int)(e - r * kp);
+        const uint16_t *row = split + r * 3 * kp;
+        out[e] = bf16_bits_to_f32(row[c]) + bf16_bits_to_f32(row[kp + c]);
+    }
+}
+
+int grid_for(long long total) { return (int)std::min<long long>((total + 255) / 256, 148LL * 16); }
+
+}  // namespace
+
+cudaError_t split_weight_rows(const float *w, int rows, int k, int kp, uint16_t *out, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_split_rows<<<grid_for((long long)rows * kp), 256, 0, st>>>(w, rows, k, kp, out, true);
+    return cudaGetLastError();
+}
+
+cudaError_t split_act_rows(const float *x, int n, int k, int kp, uint16_t *out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_split_rows<<<grid_for((long long)n * kp), 256, 0, st>>>(x, n, k, kp, out, false);
+    return cudaGetLastError();
+}
+
+cudaError_t swiglu_split(const float *gu, int n, int inter, int kp, float *act32, uint16_t *act, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_swiglu_split<<<grid_for((long long)n * kp), 256, 0, st>>>(gu, n, inter, kp, act32, act);
+    return cudaGetLastError();
+}
+
+cudaError_t rowdot_f32_strided(const float *x, const float *a, int m, int k, float *xa, int stride, cudaStream_t st) {
+    if (m <= 0) return cudaSuccess;
+    k_rowdot_f32<<<(m + 7) / 8, 256, 0, st>>>(x, a, m, k, xa, stride);
+    return cudaGetLastError();
+}
+
+cudaError_t merge_split_rows(const uint16_t *split, int rows, int kp, float *out, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_merge_split<<<grid_for((long long)rows * kp), 256, 0, st>>>(split, rows, kp, out);
+    return cudaGetLastError();
+}
+
+cudaError_t add_split_halves(const float *s, int kp, float *out, cudaStream_t st) {
+    if (kp <= 0) return cudaSuccess;
+    k_add_split_halves<<<(kp + 255) / 256, 256, 0, st>>>(s, kp, out);
     return cudaGetLastError();
 }
 

@@ -53,19 +53,44 @@ cudaError_t embed_rows(const void *table, int table_bf16, const uint32_t *tokens
 
 // h = bf16(rmsnorm(x) * w) per row; rows with cap_slot[i] >= 0 are also
 // copied (pre-norm, f32) to res[cap_slot][H] (the residual capture of the
-// previous layer's output, src/model.zig:4856-4862).
+// previous layer's output, src/model.zig:4856-4862). split_k > 0: each row of
+// h is [hi | hi | lo] of split_k columns each (the f32-level operand, zero
+// padded), where hi = bf16(y) and lo = bf16(y - hi).
 cudaError_t rmsnorm_rows_bf16(const float *x, const float *w, int n, int hidden, float eps, uint16_t *h,
-                              const int *cap_slot, float *res, const int *row_index, cudaStream_t st);
+                              const int *cap_slot, float *res, const int *row_index, cudaStream_t st,
+                              int split_k = 0);
 // f32 in/out RMSNorm of n rows (the VTable rmsnormRows, src/tensor.zig:1167-1179).
 cudaError_t rmsnorm_rows_f32(const float *x, const float *w, int n, int len, float eps, int gemma, float *out,
                              cudaStream_t st);
 // Gather rows then RMSNorm to bf16 (final norm of the logit rows).
 cudaError_t gather_rmsnorm_bf16(const float *x, const int *rows, int n, int hidden, float eps, const float *w,
-                                uint16_t *h, cudaStream_t st);
+                                uint16_t *h, cudaStream_t st, int split_k = 0);
+
+// ---- f32-level products from bf16 tensor cores (split operands) ----------
+// A weight W [rows][k] (f32) becomes [hi | lo | hi] and an activation row
+// [hi | hi | lo], segments of kp >= k columns (zero padded), with hi =
+// bf16(v) and lo = bf16(v - hi); one GEMM over 3 kp then adds hi.hi + hi.lo
+// + lo.hi with f32 accumulation, about 2^-16 relative per product (the
+// missing lo.lo term is below that).
+// W rows (f32, ld = k) -> out rows of 3 kp.
+cudaError_t split_weight_rows(const float *w, int rows, int k, int kp, uint16_t *out, cudaStream_t st);
+// Activations x [n][k] (f32) -> out [n][3 kp].
+cudaError_t split_act_rows(const float *x, int n, int k, int kp, uint16_t *out, cudaStream_t st);
+// SwiGLU of a plain gate | up product gu [n][2 inter] (f32): act32 [n][kp] =
+// silu(gate) * up (f32, zero padded) and act [n][3 kp] its split operand.
+cudaError_t swiglu_split(const float *gu, int n, int inter, int kp, float *act32, uint16_t *act, cudaStream_t st);
+// xa[row * stride] = sum_k x[row][k] a[k] (f32 x, ld = k).
+cudaError_t rowdot_f32_strided(const float *x, const float *a, int m, int k, float *xa, int stride, cudaStream_t st);
+// out[c] = s[c] + s[kp + c] for c < kp: the v^T W of a split operand's hi and
+// lo segments (from a GEMV-T over all 3 kp columns).
+cudaError_t add_split_halves(const float *s, int kp, float *out, cudaStream_t st);
+// out [rows][kp] f32 = hi + lo of a split weight operand [rows][3 kp].
+cudaError_t merge_split_rows(const uint16_t *split, int rows, int kp, float *out, cudaStream_t st);
 
 struct AttnParams {
     const float *qkv;       // [n][qd + 2 kvd] (q | k | v), biases already added
     uint16_t *out;          // [n][qd] bf16
+    float *out_f32;         // when set: [n][qd] f32 instead of out
     const int *seq_start;   // per prompt: first row
     const int *seq_len;     // per prompt: rows
     int n_prompts;
@@ -107,6 +132,7 @@ cudaError_t kv_store(const KvParams &p, cudaStream_t st);
 struct DecodeAttnParams {
     const float *qkv;            // [n][qd + 2 kvd], queries normed and roped
     uint16_t *out;               // [n][qd] bf16
+    float *out_f32;              // when set: [n][qd] f32 instead of out
     const int *row_b, *row_pos;  // per row: cache slot and position
     int n, max_len;
     int heads, kv_heads, head_dim;

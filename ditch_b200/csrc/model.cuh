@@ -26,6 +26,11 @@ struct Mat {
     // staged GEMM and kept (the weights never change: edits are deltas).
     mutable DevBuf decoded;
     mutable int decoded_row0 = -1, decoded_rows = 0;
+    // f32-level products (a model loaded in split mode): the weight as
+    // [hi | lo | hi] bf16 segments of split_k columns each, [rows][3 split_k],
+    // the operand the GEMM reads; `data` keeps the hi part for the rest
+    DevBuf split;
+    int split_k = 0;
     bool empty() const { return data.ptr == nullptr; }
     size_t bytes() const { return data.bytes + scales.bytes + zeros.bytes; }
 };
@@ -105,6 +110,10 @@ struct ditch_cuda_model {
     // workspace
     int ws_tokens = 0;
     ditch::DevBuf x, h, qkv, att, act, xa;
+    // split mode (f32-level products for f32 / f16 weights): h, att, act and
+    // hl hold [hi | hi | lo] operand rows; att32 / gu32 / act32 the f32 values
+    bool split3 = false;
+    ditch::DevBuf att32, gu32, act32;
     ditch::DevBuf res, hl, logits;
     // MoE workspace
     ditch::DevBuf moe_h3, moe_logits, moe_sel, moe_w, moe_counts, moe_offsets, moe_perm, moe_pw, moe_pexp, moe_slot,

@@ -116,6 +116,44 @@ int decode_seg_bf16(ditch_cuda_model *m, const Seg &s, uint16_t *dst) {
     return DITCH_CUDA_OK;
 }
 
+// Decodes one segment to f32 rows at `dst` (rows x cols): f32 / f16 / bf16
+// values as stored, ggml blocks to f32 as src/quant.zig decodes them, the
+// other quantised formats to their bf16 values (src/dequant.zig's output).
+int decode_seg_f32(ditch_cuda_model *m, const Seg &s, float *dst) {
+    const ditch_cuda_tensor *t = s.t;
+    ditch_cuda_device *dev = m->dev;
+    const size_t n = t->rows * t->cols;
+    const size_t db = slab_bytes(t->data_bytes, t->slabs);
+    switch (t->format) {
+    case DITCH_FMT_F32:
+        DITCH_CUDA(copy_in(m, dst, t->data, db * s.slab, n * 4, t));
+        return DITCH_CUDA_OK;
+    case DITCH_FMT_F16:
+    case DITCH_FMT_Q8_0:
+    case DITCH_FMT_Q4_K: {
+        DevBuf raw;
+        DITCH_CUDA(raw.reserve(db));
+        DITCH_CUDA(copy_in(m, raw.ptr, t->data, db * s.slab, db, t));
+        if (t->format == DITCH_FMT_F16)
+            DITCH_LAUNCH(dev, f16_to_f32(raw.as<uint16_t>(), dst, (long long)n, dev->stream));
+        else
+            DITCH_LAUNCH(dev, dequant_ggml_f32(t->format == DITCH_FMT_Q8_0 ? DITCH_DTYPE_Q8_0 : DITCH_DTYPE_Q4_K,
+                                               raw.as<uint8_t>(), (long long)n, dst, dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(dev->stream));  // raw is freed on return
+        return DITCH_CUDA_OK;
+    }
+    default: {
+        DevBuf b16;
+        DITCH_CUDA(b16.reserve(n * 2));
+        int st = decode_seg_bf16(m, s, b16.as<uint16_t>());
+        if (st) return st;
+        DITCH_LAUNCH(dev, bf16_to_f32(b16.as<uint16_t>(), dst, (long long)n, dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(dev->stream));
+        return DITCH_CUDA_OK;
+    }
+    }
+}
+
 // Whether the segments can stay in a GEMM-decoded quantised format.
 int native_format(const std::vector<Seg> &segs) {
     const ditch_cuda_tensor *t0 = segs[0].t;
@@ -169,7 +207,8 @@ int build_mat(ditch_cuda_model *m, const std::vector<Seg> &segs, int slabs, Mat 
     out.rows = (int)(rows / slabs);
     out.cols = (int)cols;
     out.slabs = slabs;
-    const int fmt = native_format(segs);
+    // split mode decodes every format once (the split operand is bf16)
+    const int fmt = m->split3 ? -1 : native_format(segs);
     if (fmt == kFmtFp8) {
         const ditch_cuda_tensor *t0 = segs[0].t;
         out.fmt = kFmtFp8;
@@ -303,6 +342,24 @@ int build_mat(ditch_cuda_model *m, const std::vector<Seg> &segs, int slabs, Mat 
             }
             r += s.t->rows;
         }
+        if (m->split3) {
+            // the f32-level operand [hi | lo | hi] from the values as ditch holds them
+            out.split_k = (int)kp;
+            DITCH_CUDA(out.split.reserve(rows * 3 * kp * 2));
+            size_t mx = 0;
+            for (const Seg &s : segs) mx = std::max(mx, s.t->rows);
+            DevBuf f;
+            DITCH_CUDA(f.reserve(mx * cols * 4));
+            r = 0;
+            for (const Seg &s : segs) {
+                int st = decode_seg_f32(m, s, f.as<float>());
+                if (st) return st;
+                DITCH_LAUNCH(dev, split_weight_rows(f.as<float>(), (int)s.t->rows, (int)cols, (int)kp,
+                                                    out.split.as<uint16_t>() + r * 3 * kp, dev->stream));
+                DITCH_CUDA(cudaStreamSynchronize(dev->stream));  // f is reused
+                r += s.t->rows;
+            }
+        }
     }
     DITCH_CUDA(cudaStreamSynchronize(dev->stream));
     return DITCH_CUDA_OK;
@@ -428,6 +485,16 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
     c.tp_world = cfg->tp_world > 1 ? cfg->tp_world : 1;
     c.tp_rank = c.tp_world > 1 ? cfg->tp_rank : 0;
     REQUIRE(c.tp_rank >= 0 && c.tp_rank < c.tp_world, "tp_rank out of range");
+    m->split3 = dev->f32_split;
+    if (m->split3) {
+        bool any_moe = false;
+        for (uint8_t f : c.moe_layers) any_moe |= f != 0;
+        if (any_moe || c.tp_world > 1 || c.ep_world > 1) {
+            set_error("f32 split products are for dense models on one GPU (no routed experts, no tensor or expert "
+                      "parallelism)");
+            return DITCH_CUDA_UNSUPPORTED;
+        }
+    }
     if (c.tp_world > 1) {
         bool any_moe = false;
         for (uint8_t f : c.moe_layers) any_moe |= f != 0;
@@ -624,10 +691,11 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
     if ((st = build_rope(m.get()))) return st;
     DITCH_CUDA(m->dirs.reserve((size_t)(c.n_layers + 1) * H * 4));
     DITCH_CUDA(m->vtmp.reserve((size_t)H * 4));
-    uint64_t bytes = m->embed.bytes + m->final_norm.bytes + m->lm_head.bytes();
+    uint64_t bytes = m->embed.bytes + m->final_norm.bytes + m->lm_head.bytes() + m->lm_head.split.bytes;
     for (const Layer &L : m->layers)
         bytes += L.qkv.bytes() + L.o.bytes() + L.gate_up.bytes() + L.down.bytes() + L.router.bytes() +
-                 L.e_gate_up.bytes() + L.e_down.bytes();
+                 L.e_gate_up.bytes() + L.e_down.bytes() + L.qkv.split.bytes + L.o.split.bytes +
+                 L.gate_up.split.bytes + L.down.split.bytes;
     m->bytes = bytes;
     DITCH_CUDA(cudaDeviceSynchronize());
     *out = m.release();

@@ -70,6 +70,17 @@ namespace ditch {
 
 int gemv_t_mat(ditch_cuda_model *m, const Mat &w, int row0, int rows, const float *v, float *out) {
     ditch_cuda_device *dev = m->dev;
+    if (w.split.ptr) {
+        // v^T (hi + lo): the GEMV-T over the split operand's segments, then
+        // the hi and lo sums added (the third segment repeats hi)
+        const int kp = w.split_k;
+        DITCH_CUDA(m->gemv_part.reserve((size_t)3 * kp * 4));
+        DITCH_CUDA(cudaMemsetAsync(m->gemv_part.ptr, 0, (size_t)3 * kp * 4, dev->stream));
+        DITCH_LAUNCH(dev, gemv_t_bf16(w.split.as<uint16_t>() + (size_t)row0 * 3 * kp, rows, 3 * kp, v,
+                                      m->gemv_part.as<float>(), dev->stream));
+        DITCH_LAUNCH(dev, add_split_halves(m->gemv_part.as<float>(), kp, out, dev->stream));
+        return DITCH_CUDA_OK;
+    }
     DITCH_CUDA(cudaMemsetAsync(out, 0, (size_t)w.cols * 4, dev->stream));
     switch (w.fmt) {
     case kFmtBf16:
@@ -127,15 +138,23 @@ int ensure_workspace(ditch_cuda_model *m, int n, int nc, int nl) {
     const Config &c = m->cfg;
     const size_t N = (size_t)std::max(n, 1), H = c.hidden;
     const size_t inter = (std::max(c.inter, 1) + 7) / 8 * 8;
+    // split mode: GEMM inputs are [hi | hi | lo] rows of 8-aligned segments
+    const size_t sf = m->split3 ? 3 : 1;
+    const size_t hk = m->split3 ? (H + 7) / 8 * 8 : H, qk = m->split3 ? ((size_t)c.qd() + 7) / 8 * 8 : c.qd();
     DITCH_CUDA(m->x.reserve(N * H * 4));
-    DITCH_CUDA(m->h.reserve(N * H * 2));
+    DITCH_CUDA(m->h.reserve(N * hk * sf * 2));
     DITCH_CUDA(m->qkv.reserve(N * c.qkv_width() * 4));
-    DITCH_CUDA(m->att.reserve(N * c.qd() * 2));
-    DITCH_CUDA(m->act.reserve(N * inter * 2));
+    DITCH_CUDA(m->att.reserve(N * qk * sf * 2));
+    DITCH_CUDA(m->act.reserve(N * inter * sf * 2));
     DITCH_CUDA(m->xa.reserve(N * 4 * kMaxDeltaRank));
+    if (m->split3) {
+        DITCH_CUDA(m->att32.reserve(N * c.qd() * 4));
+        DITCH_CUDA(m->gu32.reserve(N * 2 * (size_t)c.inter * 4));
+        DITCH_CUDA(m->act32.reserve(N * inter * 4));
+    }
     if (nc > 0) DITCH_CUDA(m->res.reserve((size_t)(c.n_layers + 1) * nc * H * 4));
     if (nl > 0) {
-        DITCH_CUDA(m->hl.reserve((size_t)nl * H * 2));
+        DITCH_CUDA(m->hl.reserve((size_t)nl * hk * sf * 2));
         DITCH_CUDA(m->logits.reserve((size_t)nl * c.vocab * 4));
     }
     return DITCH_CUDA_OK;
@@ -205,6 +224,15 @@ cudaError_t decode_rows_bf16(ditch_cuda_device *dev, const Mat &w, int row0, int
 }
 
 int mat_row_norms(ditch_cuda_device *dev, const Mat &w, int row0, int rows, float *out) {
+    if (w.split.ptr) {  // the norms of hi + lo
+        DevBuf f;
+        DITCH_CUDA(f.reserve((size_t)rows * w.split_k * 4));
+        DITCH_LAUNCH(dev, merge_split_rows(w.split.as<uint16_t>() + (size_t)row0 * 3 * w.split_k, rows, w.split_k,
+                                           f.as<float>(), dev->stream));
+        DITCH_LAUNCH(dev, row_norms_f32(f.as<float>(), rows, w.split_k, out, dev->stream));
+        DITCH_CUDA(cudaStreamSynchronize(dev->stream));  // f is freed on return
+        return DITCH_CUDA_OK;
+    }
     if (w.fmt == kFmtBf16) {
         DITCH_LAUNCH(dev, row_norms_bf16(w.data.as<uint16_t>() + (size_t)row0 * w.cols, rows, w.cols, out, dev->stream));
         return DITCH_CUDA_OK;
@@ -239,8 +267,12 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         set_error("delta rank %d is not within 1..%d", delta_rank, kMaxDeltaRank);
         return DITCH_CUDA_INVALID;
     }
-    GemmOperand A{w.data.ptr, w.rows * w.slabs, w.cols, w.row_bytes};
-    GemmOperand B{act, n_tok, w.cols, (long long)w.cols * 2};
+    // split mode: the weight's [hi | lo | hi] operand against [hi | hi | lo]
+    // activation rows, K three segments long
+    const bool split = w.split.ptr != nullptr;
+    const int K = split ? 3 * w.split_k : w.cols;
+    GemmOperand A{split ? w.split.ptr : w.data.ptr, w.rows * w.slabs, K, split ? (long long)K * 2 : w.row_bytes};
+    GemmOperand B{act, n_tok, K, (long long)K * 2};
     int fmt = w.fmt;
     const bool dual = (flags & kEpiSwiglu) != 0;
     // Staged decode. The fused transform decodes every weight element once per
@@ -287,7 +319,7 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     GemmParams p{};
     p.m_w = m_rows;
     p.n_tok = n_tok;
-    p.k = w.cols;
+    p.k = K;
     p.k_splits = 1;
     if (ex) {
         p.k_splits = ex->k_splits > 0 ? ex->k_splits : 1;
@@ -302,9 +334,9 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     // partial sums are added atomically, or in deterministic mode left in
     // sk_ws and added in split order by the last block of each row block
     const int sk = skinny_chunk(fmt);
-    if (!p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16) && n_tok <= 16 && sk && w.cols % sk == 0 &&
+    if (!p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16) && n_tok <= 16 && sk && K % sk == 0 &&
         !(fmt == kFmtFp8 && w.bc % 16) && !(fmt == kFmtInt4 && w.group % 32)) {
-        const int bx = (m_rows + 15) / 16, chunks = w.cols / sk;
+        const int bx = (m_rows + 15) / 16, chunks = K / sk;
         const int ks = std::max(1, std::min(chunks, (2 * dev->sms + bx - 1) / bx));  // about one wave
         if (ks > 1 && !dev->deterministic) {
             if (!(flags & kEpiResidual))
@@ -356,7 +388,7 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     // CTA that brings its last part, for any epilogue.
     const int bn = gemm_token_tile(n_tok, dual, fmt != kFmtBf16);
     const long long tiles = (long long)((m_rows + 127) / 128) * ((n_tok + bn - 1) / bn);
-    const int k_tiles = (w.cols + 63) / 64;
+    const int k_tiles = (K + 63) / 64;
     if (!dev->deterministic && !p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16) &&
         tiles < dev->sms && k_tiles >= 8) {
         // as many splits as still fit one wave: a second, nearly empty wave
@@ -430,16 +462,21 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
     const size_t entry = (size_t)nc * H;
     DITCH_LAUNCH(dev, embed_rows(m->embed.ptr, m->embed_bf16 ? 1 : 0, b.tokens.as<uint32_t>(), n, H, x, cap, res,
                                  dev->status, c.vocab, st));
+    // split mode: the norms write [hi | hi | lo] operand rows of kh columns a
+    // segment; attention and SwiGLU go through f32 first
+    const bool sp = m->split3;
+    const int kh = sp ? (H + 7) / 8 * 8 : 0;
     for (int li = 0; li < c.n_layers; li++) {
         Layer &L = m->layers[li];
         // input norm; entry li (the previous layer's output) is captured here
         DITCH_LAUNCH(dev, rmsnorm_rows_bf16(x, L.input_norm.as<float>(), n, H, c.eps, h, li > 0 ? cap : nullptr,
-                                            li > 0 && res ? res + (size_t)li * entry : nullptr, nullptr, st));
+                                            li > 0 && res ? res + (size_t)li * entry : nullptr, nullptr, st, kh));
         if ((s = gemm_weight(m, L.qkv, 0, W, h, n, m->qkv.ptr, W, 0, L.qkv_bias.as<float>(), nullptr, nullptr, 0)))
             return s;
         AttnParams ap{};
         ap.qkv = m->qkv.as<float>();
         ap.out = m->att.as<uint16_t>();
+        ap.out_f32 = sp ? m->att32.as<float>() : nullptr;
         ap.seq_start = b.seq_start.as<int>();
         ap.seq_len = b.seq_len.as<int>();
         ap.n_prompts = b.prompts;
@@ -484,6 +521,7 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
                 DecodeAttnParams dp{};
                 dp.qkv = m->qkv.as<float>();
                 dp.out = m->att.as<uint16_t>();
+                dp.out_f32 = ap.out_f32;
                 dp.row_b = kp.row_b;
                 dp.row_pos = kp.row_pos;
                 dp.n = n;
@@ -501,10 +539,16 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
                 DITCH_LAUNCH(dev, kv_store(kp, st));
             }
         }
+        if (sp) DITCH_LAUNCH(dev, split_act_rows(m->att32.as<float>(), n, qd, L.o.split_k, m->att.as<uint16_t>(), st));
         if (L.o_edit)
-            for (int t = 0; t < L.o_rank; t++)
-                DITCH_LAUNCH(dev, rowdot_bf16_strided(m->att.as<uint16_t>(), L.o_a.as<float>() + (size_t)t * qd, n, qd,
-                                                      m->xa.as<float>() + t, L.o_rank, st));
+            for (int t = 0; t < L.o_rank; t++) {
+                if (sp)
+                    DITCH_LAUNCH(dev, rowdot_f32_strided(m->att32.as<float>(), L.o_a.as<float>() + (size_t)t * qd, n, qd,
+                                                         m->xa.as<float>() + t, L.o_rank, st));
+                else
+                    DITCH_LAUNCH(dev, rowdot_bf16_strided(m->att.as<uint16_t>(), L.o_a.as<float>() + (size_t)t * qd, n,
+                                                          qd, m->xa.as<float>() + t, L.o_rank, st));
+            }
         // tensor parallel: the partial sum goes to the group's send rows, then the all-reduce adds it to x
         const bool tp = m->group && c.tp_world > 1;
         if ((s = gemm_weight(m, L.o, 0, H, m->att.as<uint16_t>(), n, tp ? tp_send_rows(m) : x, H, tp ? 0 : kEpiResidual,
@@ -515,15 +559,30 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
         if (L.moe) {
             if ((s = moe_mlp(m, L, li, n))) return s;
         } else {
-            DITCH_LAUNCH(dev, rmsnorm_rows_bf16(x, L.post_norm.as<float>(), n, H, c.eps, h, nullptr, nullptr, nullptr, st));
+            DITCH_LAUNCH(dev, rmsnorm_rows_bf16(x, L.post_norm.as<float>(), n, H, c.eps, h, nullptr, nullptr, nullptr, st,
+                                                kh));
             const int I = c.inter, Ip = L.down.cols;  // Ip: the stored (8-aligned) width
-            if (Ip != I) DITCH_CUDA(cudaMemsetAsync(m->act.ptr, 0, (size_t)n * Ip * 2, st));
-            if ((s = gemm_weight(m, L.gate_up, 0, I, h, n, m->act.ptr, Ip, kEpiSwiglu, nullptr, nullptr, nullptr, I)))
-                return s;
+            if (sp) {
+                // the gate | up product in f32, then silu(gate) * up and its split operand
+                if ((s = gemm_weight(m, L.gate_up, 0, 2 * I, h, n, m->gu32.ptr, 2 * I, 0, nullptr, nullptr, nullptr, 0)))
+                    return s;
+                DITCH_LAUNCH(dev, swiglu_split(m->gu32.as<float>(), n, I, L.down.split_k, m->act32.as<float>(),
+                                               m->act.as<uint16_t>(), st));
+            } else {
+                if (Ip != I) DITCH_CUDA(cudaMemsetAsync(m->act.ptr, 0, (size_t)n * Ip * 2, st));
+                if ((s = gemm_weight(m, L.gate_up, 0, I, h, n, m->act.ptr, Ip, kEpiSwiglu, nullptr, nullptr, nullptr, I)))
+                    return s;
+            }
             if (L.down_edit)
-                for (int t = 0; t < L.down_rank; t++)
-                    DITCH_LAUNCH(dev, rowdot_bf16_strided(m->act.as<uint16_t>(), L.down_a.as<float>() + (size_t)t * Ip, n,
-                                                          Ip, m->xa.as<float>() + t, L.down_rank, st));
+                for (int t = 0; t < L.down_rank; t++) {
+                    if (sp)
+                        DITCH_LAUNCH(dev, rowdot_f32_strided(m->act32.as<float>(), L.down_a.as<float>() + (size_t)t * Ip,
+                                                             n, Ip, m->xa.as<float>() + t, L.down_rank, st));
+                    else
+                        DITCH_LAUNCH(dev, rowdot_bf16_strided(m->act.as<uint16_t>(),
+                                                              L.down_a.as<float>() + (size_t)t * Ip, n, Ip,
+                                                              m->xa.as<float>() + t, L.down_rank, st));
+                }
             if ((s = gemm_weight(m, L.down, 0, H, m->act.as<uint16_t>(), n, tp ? tp_send_rows(m) : x, H,
                                  tp ? 0 : kEpiResidual, nullptr, L.down_edit ? m->xa.as<float>() : nullptr,
                                  L.down_edit ? L.down_b.as<float>() : nullptr, 0, L.down_edit ? L.down_rank : 1)))
@@ -537,7 +596,7 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
     }
     if (nl > 0) {
         DITCH_LAUNCH(dev, gather_rmsnorm_bf16(x, b.logit_rows.as<int>(), nl, H, c.eps, m->final_norm.as<float>(),
-                                              m->hl.as<uint16_t>(), st));
+                                              m->hl.as<uint16_t>(), st, kh));
         if ((s = gemm_weight(m, m->lm_head, 0, c.vocab, m->hl.as<uint16_t>(), nl, m->logits.ptr, c.vocab, 0, nullptr,
                              nullptr, nullptr, 0)))
             return s;

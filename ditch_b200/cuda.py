@@ -129,6 +129,7 @@ SIGNATURES = {
     "ditch_cuda_weight_decode": (C.c_int, [vp, vp]),
     "ditch_cuda_set_decode_staging": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_deterministic": (C.c_int, [vp, C.c_int]),
+    "ditch_cuda_set_f32_split": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_decode_cache": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_peer_handle_bytes": (sz, []),
     "ditch_cuda_group_create": (C.c_int, [vp, C.c_int, C.c_int, sz, C.POINTER(vp), vp]),
@@ -345,6 +346,11 @@ class Device:
         """Dense GEMMs over quantised weights with at least `min_tokens` tokens
         decode the weight once to bf16 scratch; 0 keeps every decode in the GEMM."""
         check(lib().ditch_cuda_set_decode_staging(self.h, int(min_tokens)))
+
+    def set_f32_split(self, on):
+        """Models loaded afterwards run f32-level split-bf16 products for their
+        f32 / f16 weights (three times the tensor-core work)."""
+        check(lib().ditch_cuda_set_f32_split(self.h, int(bool(on))))
 
     def set_decode_cache(self, on):
         """Staged GEMMs keep their weight's decoded bf16 copy (default on)."""

@@ -405,6 +405,21 @@ int ditch_cuda_set_decode_cache(ditch_cuda_device *dev, int enabled);
  * group turns it on for its device (the ranks' replicated results must
  * agree bit for bit). Default off. No counterpart in the reference. */
 int ditch_cuda_set_deterministic(ditch_cuda_device *dev, int enabled);
+/* f32-level products for f32 and f16 weights. By default a resident model
+ * rounds f32 / f16 weights to bf16 at load and rounds every GEMM input to
+ * bf16 (tensor-core products with f32 accumulation), about 2^-9 relative per
+ * operand. With this on, models loaded afterwards keep each dense weight W
+ * as [hi | lo | hi] bf16 segments (hi = bf16(W), lo = bf16(W - hi)) and
+ * every GEMM input x as [hi | hi | lo], so one bf16 GEMM over three times
+ * the K adds hi.hi + hi.lo + lo.hi in f32: about 2^-16 relative per product,
+ * the f32 engine's results to about 1e-5 (src/tensor.zig:1023-1045), at three
+ * times the tensor-core work and 6 more bytes per weight. The edit deltas
+ * read the same operand (A = v^T (hi + lo)) and the f32 activations; the
+ * full-mode sketch products read the hi part. Dense models with f32 / f16 /
+ * bf16 weights only (quantised weights, routed experts and tensor
+ * parallelism are refused at load). Default off. No counterpart in the
+ * reference, whose CPU engine multiplies in f32. */
+int ditch_cuda_set_f32_split(ditch_cuda_device *dev, int enabled);
 
 /* ---- peer groups and expert parallelism (one process per GPU of one node;
  * no counterpart in ditch, which runs on one host) ---- */
