@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--max-new", type=int, default=100, help="gen: tokens generated per prompt")
     ap.add_argument("--row-normalization", default="none", choices=["none", "pre", "full"],
                     help="c1 / c2: the edit's row normalisation (full: rank-3 delta from the randomised SVD)")
+    ap.add_argument("--cta-pairs", type=int, default=0,
+                    help="1: dense bf16 GEMMs of 512+ tokens on CTA pairs (tcgen05 cta_group::2)")
     ap.add_argument("--deterministic", type=int, default=0,
                     help="1: K splits summed in a fixed order (stream-K) instead of atomically")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
@@ -335,6 +337,8 @@ def config_block(args):
     return {"workload": "C2: Llama-3-8B-shaped, FP8 E4M3 128x128 block-scaled weights, trial = %s-mode edit of "
                         "o_proj/down_proj + edited forward + first-token KL" % args.row_normalization,
             "row_normalization": args.row_normalization,
+            "gemm": ("CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles) for dense GEMMs of 512+ tokens"
+                     if args.cta_pairs else "one CTA per 128-row tile (tcgen05 cta_group::1)"),
             "layers": args.layers, "prompts_per_gpu": args.prompts, "seq_len": args.seq, "vocab": C2["vocab"],
             "parallelism": f"dp{args.gpus} (prompt batches; residual sums and KL summed over the ranks by the "
                            "library's peer-group reduction over NVLink)",
@@ -393,6 +397,7 @@ def main():
     if args.stage_min_tokens is not None:
         dev.set_decode_staging(args.stage_min_tokens)
     dev.set_deterministic(args.deterministic)
+    dev.set_cta_pairs(args.cta_pairs)
     spec = dict(C2, n_layers=args.layers)
     L, V, P, S = spec["n_layers"], spec["vocab"], args.prompts, args.seq
     t0 = time.time()

@@ -622,7 +622,8 @@ def c4_flops(spec, tokens):
 def run_c4(args, dev, world=1, rank=0, dist=None):
     """C4 on `world` GPUs: expert-parallel (each rank owns 128 / world experts,
     rows exchanged over NVLink peer memory) and data-parallel over prompts
-    (each rank routes its own 256 prompts; residual sums and KL all-reduced)."""
+    (each rank routes its own 256 prompts; the library sums the residuals and
+    the KL over the ranks through a second peer group)."""
     import torch
 
     import ditch_b200
@@ -642,6 +643,8 @@ def run_c4(args, dev, world=1, rank=0, dist=None):
 
         group = ditch_b200.Group(dev, rank, world, model.group_bytes(P * S), exchange)
         model.set_group(group, P * S)
+        dp_group = ditch_b200.Group(dev, rank, world, model.dp_group_bytes(P), exchange)
+        model.set_dp_group(dp_group)
         dist.barrier()
     load_s = time.time() - t0
     rng = np.random.default_rng(args.seed + 1000 * (rank + 1))
@@ -650,11 +653,9 @@ def run_c4(args, dev, world=1, rank=0, dist=None):
     kl_prompts = [rng.integers(0, V, S).astype(np.uint32) for _ in range(P)]
     dev.synchronize()
     dev.timer_start()
-    gs, gc = model.residual_sums(good, window=1, batch_size=P)
+    gs, gc = model.residual_sums(good, window=1, batch_size=P)  # every rank's prompts (data-parallel group)
     bs, bc = model.residual_sums(bad, window=1, batch_size=P)
-    gs, bs = all_reduce(dist, gs), all_reduce(dist, bs)
-    counts = all_reduce(dist, np.array([gc, bc], np.float64))
-    model.directions(gs, int(counts[0]), bs, int(counts[1]), True)
+    model.directions(gs, gc, bs, bc, True)
     capture_ms = dev.timer_stop()
     model.kl_init(kl_prompts)
     tokens_flat = np.concatenate(kl_prompts).astype(np.uint32)
@@ -666,9 +667,8 @@ def run_c4(args, dev, world=1, rank=0, dist=None):
     def step(e2e):
         po, pd, di = trial_params(trial_rng, L)
         model.apply_expert_edit(po, pd, di, n_experts=spec["top_k"], strength=1.0)
-        kl = model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score()
-        tot = all_reduce(dist, np.array([kl * P, P], np.float64))
-        kls.append(tot[0] / tot[1])
+        # the mean KL over every rank's prompts
+        kls.append(model.kl_score_prompts(tokens_flat, offs, P) if e2e else model.kl_score())
 
     def timed(e2e, steps):
         if dist:
@@ -708,7 +708,8 @@ def run_c4(args, dev, world=1, rank=0, dist=None):
                                "(o_proj + top-8 expert down per layer) + edited forward + first-token KL",
                    "layers": L, "prompts_per_gpu": P, "seq_len": S, "vocab": V,
                    "parallelism": (f"ep{world} (experts {spec['n_experts'] // world} per GPU, rows exchanged over "
-                                   f"NVLink peer memory) x dp{world} (prompts)" if world > 1 else "dp1"),
+                                   f"NVLink peer memory) x dp{world} (prompts; residual sums and KL summed by the "
+                                   f"library's peer-group reduction)" if world > 1 else "dp1"),
                    "l2": "inputs larger than L2 (15.4 GB of MXFP4 experts per forward)"},
         "e2e": {"value": round(tokens * world * args.steps / (ms_e2e / 1000.0), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(tokens * 4 + (P + 1) * 8), "d2h_bytes_per_step": 8,
@@ -726,10 +727,12 @@ def run_c4(args, dev, world=1, rank=0, dist=None):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    model.set_dp_group(None)
     model.close()
     if group is not None:
         dist.barrier()
         group.close()
+        dp_group.close()
 
 
 C5 = dict(n_layers=80, hidden=8192, heads=64, kv_heads=8, head_dim=128, inter=28672, vocab=128256, eps=1e-5,
@@ -955,6 +958,7 @@ def run(args):
     if args.stage_min_tokens is not None:
         dev.set_decode_staging(args.stage_min_tokens)
     dev.set_deterministic(args.deterministic)
+    dev.set_cta_pairs(args.cta_pairs)
     if args.config == "c4" or (args.config == "c5" and world > 1):
         if args.config == "c4":
             run_c4(args, dev, world, rank, dist)

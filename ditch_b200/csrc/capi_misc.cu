@@ -282,6 +282,13 @@ int ditch_cuda_set_decode_cache(ditch_cuda_device *dev, int enabled) {
     return DITCH_CUDA_OK;
 }
 
+int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int enabled) {
+    REQUIRE(dev, "null device");
+    std::lock_guard<std::mutex> lk(dev->mu);
+    dev->cta_pairs = enabled != 0;
+    return DITCH_CUDA_OK;
+}
+
 int ditch_cuda_set_f32_split(ditch_cuda_device *dev, int enabled) {
     REQUIRE(dev, "null device");
     std::lock_guard<std::mutex> lk(dev->mu);

@@ -1217,6 +1217,12 @@ cudaError_t dispatch_fmt(int fmt, const GemmOperand &a, const GemmOperand *a2, c
 
 }  // namespace
 
+bool gemm_map_bf16(CUtensorMap *map, const void *ptr, uint64_t cols, uint64_t rows, uint64_t row_bytes,
+                   uint32_t box_rows) {
+    return make_map(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cols, rows, row_bytes, BK, box_rows,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 size_t skinny_split_bytes(int rows, int splits) { return (size_t)((rows + 15) / 16) * splits * 256 * sizeof(float); }
 
 size_t gemm_stream_k_bytes(int grid, int bn, bool dual) {
@@ -1296,6 +1302,7 @@ cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, co
                         int num_sms, cudaStream_t stream) {
     const bool dual = (p.flags & kEpiSwiglu) != 0;
     if (dual && !a2) return cudaErrorInvalidValue;
+    if (p.cta_pairs && !p.bn && gemm_pair_fits(p, fmt, p.k, num_sms)) return launch_gemm_pair(a, a2, b, p, num_sms, stream);
     const int bn = p.bn ? p.bn : gemm_token_tile(p.n_tok, dual, fmt != kFmtBf16);
     if (dual) {
         if (bn == 32) return dispatch_fmt<32, true>(fmt, a, a2, b, p, num_sms, stream);

@@ -81,6 +81,10 @@ struct GemmParams {
     int stream_k;
     float *sk_ws;  // [grid][2][accumulators][128][bn] f32 partial sums
     int *sk_cnt;   // [tiles] arrival counters, zero between launches
+    // Dense bf16 products over many tokens may run on CTA pairs
+    // (cta_group::2, gemm2.cu): 256-row output tiles, each CTA of the pair
+    // loading half the weight rows and half the token rows.
+    int cta_pairs;
 };
 
 // Device bytes of the weight-streaming product's split partial sums (in
@@ -105,6 +109,14 @@ struct GemmOperand {
     int cols;           // K (elements)
     long long row_bytes;
 };
+
+// The CTA-pair GEMM (gemm2.cu): whether it takes this product, and its launch.
+bool gemm_pair_fits(const GemmParams &p, int fmt, int k, int num_sms);
+cudaError_t launch_gemm_pair(const GemmOperand &a, const GemmOperand *a2, const GemmOperand &b, GemmParams p,
+                             int num_sms, cudaStream_t stream);
+// The 128B-swizzled K-major bf16 tensor map of the GEMMs (64 x box_rows boxes).
+bool gemm_map_bf16(CUtensorMap *map, const void *ptr, uint64_t cols, uint64_t rows, uint64_t row_bytes,
+                   uint32_t box_rows);
 
 cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, const GemmOperand &b,
                         GemmParams p, int num_sms, cudaStream_t stream);

@@ -130,6 +130,7 @@ SIGNATURES = {
     "ditch_cuda_set_decode_staging": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_deterministic": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_f32_split": (C.c_int, [vp, C.c_int]),
+    "ditch_cuda_set_cta_pairs": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_decode_cache": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_peer_handle_bytes": (sz, []),
     "ditch_cuda_group_create": (C.c_int, [vp, C.c_int, C.c_int, sz, C.POINTER(vp), vp]),
@@ -346,6 +347,10 @@ class Device:
         """Dense GEMMs over quantised weights with at least `min_tokens` tokens
         decode the weight once to bf16 scratch; 0 keeps every decode in the GEMM."""
         check(lib().ditch_cuda_set_decode_staging(self.h, int(min_tokens)))
+
+    def set_cta_pairs(self, on):
+        """Wide dense bf16 GEMMs on CTA pairs (cta_group::2)."""
+        check(lib().ditch_cuda_set_cta_pairs(self.h, int(bool(on))))
 
     def set_f32_split(self, on):
         """Models loaded afterwards run f32-level split-bf16 products for their

@@ -55,13 +55,16 @@ def test_one_rank_group_matches_single_device(deterministic):
     kl0 = m.kl_score()
     g = ditch_b200.Group(device, 0, 1, m.dp_group_bytes(len(ps)), lambda h: [h])
     m.set_dp_group(g)
+    m.reset_edits()  # the residual pass of the base model, as above
     sums1, n1 = m.residual_sums(ps, window=2, batch_size=5)
+    m.apply_edit((1.2, 1.0, 0.5, 2.0), (0.9, 0.0, 0.3, 2.0))
     kl1 = m.kl_score()
     assert n1 == n0 == len(ps)
     assert np.array_equal(sums1, sums0)
     assert kl1 == kl0 and kl0 > 0
     # and twice more: the reductions alternate between the two halves of the region
     assert m.kl_score() == kl0
+    m.reset_edits()
     assert np.array_equal(m.residual_sums(ps, window=2, batch_size=5)[0], sums0)
     np.testing.assert_array_equal(g.allreduce_f64([1.5, -2.0, 3.25]), [1.5, -2.0, 3.25])
     m.set_dp_group(None)

@@ -1,7 +1,8 @@
-"""Expert parallelism over a peer group on two GPUs (one process each).
+"""Expert parallelism over a peer group on 2, 4 and 8 GPUs (one process each).
 
-Each rank keeps half of the routed experts, routes its own prompts and
-exchanges (token, expert) rows with the other rank over NVLink; the combine
+Each rank keeps 1 / world of the routed experts (16 experts: 8, 4 or 2 per
+rank), routes its own prompts and
+exchanges (token, expert) rows with the other ranks over NVLink; the combine
 runs in the same expert-index order as on one GPU, and every per-row product
 is the same product, so the expert-parallel forward must equal the
 single-GPU forward of the same prompts bit for bit. After the
@@ -10,7 +11,7 @@ gathered scores must pick the same experts as one GPU does and the edited
 forwards must agree bit for bit too: each expert's A = v^T W_down comes from
 the same fixed row chunks summed in the same order on either layout.
 
-Needs two GPUs; skipped otherwise. The ranks exchange IPC handles over a
+Each world size needs that many GPUs; skipped otherwise. The ranks exchange IPC handles over a
 gloo process group on 127.0.0.1."""
 import os
 import socket
@@ -53,7 +54,7 @@ def _worker(rank, world, port, out_dir):
     dev.set_deterministic(True)  # K splits summed in a fixed order: the two models must agree bit for bit
     spec, f32, tensors = make_model(300, n_layers=2, hidden=256, head_dim=64, heads=4, kv_heads=2, fmt="mxfp4",
                                     moe=dict(experts=16, top_k=4, inter=128))
-    ps = prompts(40 + rank, [40, 17, 64, 3, 70][: 5 - rank], spec["vocab"])
+    ps = prompts(40 + rank, [40, 17, 64, 3, 70][: 5 - rank % 4], spec["vocab"])  # a different batch per rank
     toks, rb, rp, cap, first, take, last = flatten_batch(ps, 2)
     max_tokens = 256
 
@@ -103,14 +104,16 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_expert_parallel_forward_equals_one_gpu(tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_expert_parallel_forward_equals_one_gpu(tmp_path, world):
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
-    for r in range(2):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
         z = np.load(tmp_path / f"r{r}.npz")
         for a, b in (("res1", "res2"), ("log1", "log2"), ("res3", "res4"), ("log3", "log4"), ("res5", "res6"),
                      ("log5", "log6")):

@@ -1,8 +1,8 @@
-"""Tensor parallelism over a peer group on two GPUs (one process each).
+"""Tensor parallelism over a peer group on 2, 4 and 8 GPUs (one process each).
 
-Each rank loads the whole tensors and keeps its shard: half the query and kv
-heads (q / k / v rows, o columns) and half the MLP columns (gate / up rows,
-down columns). The o_proj and down_proj partial sums are all-reduced over
+Each rank loads the whole tensors and keeps its shard: 1 / world of the query
+and kv heads (q / k / v rows, o columns) and of the MLP columns (gate / up
+rows, down columns). The o_proj and down_proj partial sums are all-reduced over
 NVLink peer memory after every layer. Both ranks run the same prompts and
 must hold identical residual streams and logits (every element is one sum in
 rank order); against the single-GPU model the products are split over K, so
@@ -12,7 +12,7 @@ closer. The none-mode edit of o_proj / down_proj is local to each shard
 (src/abliterate.zig:264-280: A = v^T W splits by columns with W), so the
 edited forward must agree the same way.
 
-Needs two GPUs; skipped otherwise."""
+Each world size needs that many GPUs; skipped otherwise."""
 import os
 import socket
 
@@ -51,7 +51,8 @@ def _worker(rank, world, port, out_dir):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
     dev = ditch_b200.Device(rank)
-    spec, f32, tensors = make_model(500, n_layers=3, hidden=256, head_dim=64, heads=4, kv_heads=2, inter=512,
+    # 8 query and 8 kv heads and 512 MLP columns: shards for every world size up to 8
+    spec, f32, tensors = make_model(500, n_layers=3, hidden=256, head_dim=64, heads=8, kv_heads=8, inter=512,
                                     qkv_bias=True)
     ps = prompts(77, [40, 17, 64, 3, 70], spec["vocab"])  # the same prompts on every rank
     toks, rb, rp, cap, first, take, last = flatten_batch(ps, 2)
@@ -97,16 +98,20 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_tensor_parallel_forward_matches_one_gpu(tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_forward_matches_one_gpu(tmp_path, world):
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
-    z0, z1 = np.load(tmp_path / "r0.npz"), np.load(tmp_path / "r1.npz")
-    for key in ("res2", "log2", "res4", "log4", "res6", "log6"):
-        assert np.array_equal(z0[key], z1[key]), key  # replicated streams are identical
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    z = [np.load(tmp_path / f"r{r}.npz") for r in range(world)]
+    z0 = z[0]
+    for r in range(1, world):
+        for key in ("res2", "log2", "res4", "log4", "res6", "log6"):
+            assert np.array_equal(z0[key], z[r][key]), (r, key)  # replicated streams are identical
     for a, b in (("res1", "res2"), ("log1", "log2"), ("res3", "res4"), ("log3", "log4"), ("res5", "res6"),
                  ("log5", "log6")):
         ref, got = z0[a], z0[b]
