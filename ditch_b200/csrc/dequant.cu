@@ -9,6 +9,11 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// A block per row, at most eight per SM at a time (grid-stride over rows).
+inline int row_grid(int rows) { return rows < 148 * 8 ? (rows < 1 ? 1 : rows) : 148 * 8; }
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 inline int blocks_for(long long n, int per_thread) {
     long long t = (n + per_thread - 1) / per_thread;
     long long b = (t + kThreads - 1) / kThreads;
@@ -67,6 +72,116 @@ __global__ void k_dequant_fp8(const uint8_t *codes, const float *scales, int row
     }
 }
 
+// ---- streaming decoders: a block per row (grid-stride over rows), a thread
+// per 16-byte chunk of codes, two chunks in flight per thread. The values
+// come from the exact packed conversions (cvt e4m3x2 / e2m1x2 to f16x2), the
+// f32 product with the scale and one round to bf16, as the rules above; the
+// codes the packed path does not follow (E4M3 NaN codes, the E8M0 255 scale)
+// take the element rules.
+
+// true when one of the word's four E4M3 codes is a NaN (0x7f or 0xff)
+__device__ __forceinline__ bool e4m3_nan_in(uint32_t w) {
+    const uint32_t t = (w & 0x7f7f7f7fu) ^ 0x7f7f7f7fu;  // a zero byte marks a NaN code
+    return ((t - 0x01010101u) & ~t & 0x80808080u) != 0;
+}
+
+// 16 FP8 codes (one 16-byte chunk) with one block scale to 16 bf16.
+__device__ __forceinline__ void fp8_chunk16(const uint4 q, float s, uint16_t *dst) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        o[2 * i] = scale_pack(e4m3x2_f32(w[i] & 0xffff), s);
+        o[2 * i + 1] = scale_pack(e4m3x2_f32(w[i] >> 16), s);
+        if (e4m3_nan_in(w[i])) {
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const uint32_t code = (w[i] >> (8 * b)) & 0xff;
+                if ((code & 0x7f) == 0x7f) {
+                    uint32_t &word = o[2 * i + (b >> 1)];
+                    const int sh = 16 * (b & 1);
+                    word = (word & ~(0xffffu << sh)) | ((uint32_t)e4m3_nan_bf16(code) << sh);
+                }
+            }
+        }
+    }
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    d[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    d[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// cols a multiple of 16 and block columns a multiple of 16 (one scale per chunk)
+__global__ void __launch_bounds__(256) k_dequant_fp8_rows(const uint8_t *codes, const float *scales, int rows,
+                                                          int cols, int br, int bc, int scols, uint16_t *out) {
+    const int chunks = cols / 16;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const uint8_t *crow = codes + (long long)r * cols;
+        const float *srow = scales + (long long)(r / br) * scols;
+        uint16_t *orow = out + (long long)r * cols;
+        for (int c = threadIdx.x; c < chunks; c += 2 * blockDim.x) {
+            const int c2 = c + blockDim.x;
+            const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(crow) + c);
+            const uint4 q1 = c2 < chunks ? __ldg(reinterpret_cast<const uint4 *>(crow) + c2) : make_uint4(0, 0, 0, 0);
+            fp8_chunk16(q0, __ldg(srow + (c * 16) / bc), orow + c * 16);
+            if (c2 < chunks) fp8_chunk16(q1, __ldg(srow + (c2 * 16) / bc), orow + c2 * 16);
+        }
+    }
+}
+
+// 32 MXFP4 elements (16 bytes, one E8M0 scale b) to 32 bf16.
+__device__ __forceinline__ void mxfp4_chunk32(const uint4 q, uint32_t b, uint16_t *dst);
+
+__global__ void __launch_bounds__(256) k_dequant_mxfp4_rows(const uint8_t *blocks, const uint8_t *scales, int rows,
+                                                            int cols, uint16_t *out) {
+    const int chunks = cols / 32;  // 16 bytes and one scale each
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const uint8_t *brow = blocks + (long long)r * (cols / 2);
+        const uint8_t *srow = scales + (long long)r * chunks;
+        uint16_t *orow = out + (long long)r * cols;
+        for (int c = threadIdx.x; c < chunks; c += 2 * blockDim.x) {
+            const int c2 = c + blockDim.x;
+            const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(brow) + c);
+            const uint4 q1 = c2 < chunks ? __ldg(reinterpret_cast<const uint4 *>(brow) + c2) : make_uint4(0, 0, 0, 0);
+            const uint32_t b0 = __ldg(srow + c), b1 = c2 < chunks ? __ldg(srow + c2) : 0u;
+            mxfp4_chunk32(q0, b0, orow + c * 32);
+            if (c2 < chunks) mxfp4_chunk32(q1, b1, orow + c2 * 32);
+        }
+    }
+}
+
+// INT4 pack-quantized without g_idx, groups a multiple of 32: 32 fields (one
+// 16-byte chunk) share a group's scale and zero point;
+// bf16(f32(q - zq) * scale) with q, zq the raw fields (the offset cancels).
+__global__ void __launch_bounds__(256) k_dequant_int4_rows(const uint32_t *packed, long long wpr, const float *scales,
+                                                           const uint32_t *zeros, int groups, int rows, int cols,
+                                                           int group, uint16_t *out) {
+    const int chunks = cols / 32;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const uint4 *prow = reinterpret_cast<const uint4 *>(packed + (long long)r * wpr);
+        const float *srow = scales + (long long)r * groups;
+        uint16_t *orow = out + (long long)r * cols;
+        for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+            const uint4 q = __ldg(prow + c);
+            const int g = (c * 32) / group;
+            const float s = __ldg(srow + g);
+            int zq = 8;
+            if (zeros) zq = (int)((__ldg(zeros + (long long)(r >> 3) * groups + g) >> ((r & 7) * 4)) & 0xf);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+            uint4 *d = reinterpret_cast<uint4 *>(orow + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                uint32_t o[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int lo = (int)((w[i] >> (8 * e)) & 0xf) - zq, hi = (int)((w[i] >> (8 * e + 4)) & 0xf) - zq;
+                    o[e] = scale_pack(make_float2((float)lo, (float)hi), s);
+                }
+                d[i] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        }
+    }
+}
+
 // unpackField (src/dequant.zig:313-321): field i of `bits` bits in a
 // little-endian u32 word stream.
 __device__ __forceinline__ uint32_t unpack_field(const uint32_t *words, long long i, int bits) {
@@ -114,6 +229,29 @@ __device__ __forceinline__ uint16_t mxfp4_elem(uint32_t nib, uint32_t b) {
     }
     const float s = __uint_as_float(b == 0 ? 0x00400000u : (b << 23));
     return f32_to_bf16_bits(kE2M1v[nib] * s);
+}
+
+__device__ __forceinline__ void mxfp4_chunk32(const uint4 q, uint32_t b, uint16_t *dst) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    if (b == 255) {  // the +inf scale: the element rule's NaN / inf
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const uint32_t byte = (w[i] >> (8 * e)) & 0xff;
+                o[e] = (uint32_t)mxfp4_elem(byte & 0xf, b) | ((uint32_t)mxfp4_elem(byte >> 4, b) << 16);
+            }
+            d[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        return;
+    }
+    const float s = e8m0_scale(b);
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        d[i] = make_uint4(scale_pack(e2m1x2_f32(w[i] & 0xff), s), scale_pack(e2m1x2_f32((w[i] >> 8) & 0xff), s),
+                          scale_pack(e2m1x2_f32((w[i] >> 16) & 0xff), s), scale_pack(e2m1x2_f32(w[i] >> 24), s));
 }
 
 __global__ void k_dequant_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, uint16_t *out) {
@@ -370,6 +508,10 @@ cudaError_t dequant_fp8_bf16(const uint8_t *codes, const float *scales, int rows
     if (br <= 0 || bc <= 0) return cudaErrorInvalidValue;
     const int scols = (cols + bc - 1) / bc;
     const long long n = (long long)rows * cols;
+    if (cols % 16 == 0 && bc % 16 == 0 && aligned16(codes) && aligned16(out)) {
+        k_dequant_fp8_rows<<<row_grid(rows), kThreads, 0, st>>>(codes, scales, rows, cols, br, bc, scols, out);
+        return cudaGetLastError();
+    }
     k_dequant_fp8<<<blocks_for(n, (cols % 16) ? 1 : 16), kThreads, 0, st>>>(codes, scales, rows, cols, br, bc, scols,
                                                                             out);
     return cudaGetLastError();
@@ -379,6 +521,12 @@ cudaError_t dequant_int_bf16(const uint32_t *packed, long long wpr, const float 
                              const uint32_t *g_idx, int groups, int rows, int cols, int bits, int group,
                              uint16_t *out, cudaStream_t st) {
     if (bits < 1 || bits > 8 || (!g_idx && group <= 0)) return cudaErrorInvalidValue;
+    if (bits == 4 && !g_idx && group % 32 == 0 && cols % 32 == 0 && wpr == cols / 8 && aligned16(packed) &&
+        aligned16(out)) {
+        k_dequant_int4_rows<<<row_grid(rows), kThreads, 0, st>>>(packed, wpr, scales, zeros, groups, rows, cols, group,
+                                                                 out);
+        return cudaGetLastError();
+    }
     k_dequant_int<<<blocks_for((long long)rows * cols, 1), kThreads, 0, st>>>(packed, wpr, scales, zeros, g_idx, groups,
                                                                             rows, cols, bits, group, out);
     return cudaGetLastError();
@@ -387,6 +535,10 @@ cudaError_t dequant_int_bf16(const uint32_t *packed, long long wpr, const float 
 cudaError_t dequant_mxfp4_bf16(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, uint16_t *out,
                                cudaStream_t st) {
     if (cols % 32) return cudaErrorInvalidValue;
+    if (aligned16(blocks) && aligned16(out)) {
+        k_dequant_mxfp4_rows<<<row_grid(rows), kThreads, 0, st>>>(blocks, scales, rows, cols, out);
+        return cudaGetLastError();
+    }
     k_dequant_mxfp4<<<blocks_for((long long)rows * cols / 2, 1), kThreads, 0, st>>>(blocks, scales, rows, cols, out);
     return cudaGetLastError();
 }

@@ -172,44 +172,43 @@ __global__ void k_gemv_t_fp8(const uint8_t *codes, const float *scales, int rows
     for (int j = 0; j < 16; j++) acc[j] = 0.0f;
     const bool vec = (cols & 15) == 0 && (bc & 15) == 0;
     if (vec) {
-        // Rows four at a time, all loads of a group issued before the math
-        // (no skip of v[r] == 0 rows: they add exactly zero for finite weights).
+        // Rows four at a time; the next group's loads are issued before this
+        // group's math (software pipelined), and each element is decoded with
+        // the packed conversions: bf16(code * scale) as the GEMM operand, then
+        // v[r] times it (no skip of v[r] == 0 rows: they add exactly zero for
+        // finite weights).
         const int sc = c0 / bc;
-        int r = r0;
-        for (; r + 4 <= r1; r += 4) {
+        uint4 qn[4];
+        float vn[4], sn[4];
+        auto fetch = [&](int r) {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const bool ok = r + u < r1;
+                qn[u] = ok ? __ldg(reinterpret_cast<const uint4 *>(codes + (long long)(r + u) * cols + c0))
+                           : make_uint4(0, 0, 0, 0);
+                vn[u] = ok ? __ldg(v + r + u) : 0.0f;
+                sn[u] = ok ? __ldg(scales + (long long)((r + u) / br) * scols + sc) : 0.0f;
+            }
+        };
+        fetch(r0);
+        for (int r = r0; r < r1; r += 4) {
             uint4 q[4];
             float vr[4], s[4];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                q[u] = __ldg(reinterpret_cast<const uint4 *>(codes + (long long)(r + u) * cols + c0));
-                vr[u] = __ldg(v + r + u);
-                s[u] = __ldg(scales + (long long)((r + u) / br) * scols + sc);
-            }
+            for (int u = 0; u < 4; u++) q[u] = qn[u], vr[u] = vn[u], s[u] = sn[u];
+            if (r + 4 < r1) fetch(r + 4);
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 const uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    float f[4];
-                    e4m3x4(wd[j], f);
-#pragma unroll
-                    for (int e = 0; e < 4; e++)
-                        acc[4 * j + e] =
-                            fmaf(vr[u], bf16_bits_to_f32(f32_to_bf16_bits(f[e] * s[u])), acc[4 * j + e]);
+                    const uint32_t p0 = scale_pack(e4m3x2_f32(wd[j] & 0xffff), s[u]);
+                    const uint32_t p1 = scale_pack(e4m3x2_f32(wd[j] >> 16), s[u]);
+                    acc[4 * j] = fmaf(vr[u], __uint_as_float(p0 << 16), acc[4 * j]);
+                    acc[4 * j + 1] = fmaf(vr[u], __uint_as_float(p0 & 0xffff0000u), acc[4 * j + 1]);
+                    acc[4 * j + 2] = fmaf(vr[u], __uint_as_float(p1 << 16), acc[4 * j + 2]);
+                    acc[4 * j + 3] = fmaf(vr[u], __uint_as_float(p1 & 0xffff0000u), acc[4 * j + 3]);
                 }
-            }
-        }
-        for (; r < r1; r++) {
-            const float vr = __ldg(v + r), s = __ldg(scales + (long long)(r / br) * scols + sc);
-            const uint4 q = __ldg(reinterpret_cast<const uint4 *>(codes + (long long)r * cols + c0));
-            const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float f[4];
-                e4m3x4(wd[j], f);
-#pragma unroll
-                for (int e = 0; e < 4; e++)
-                    acc[4 * j + e] = fmaf(vr, bf16_bits_to_f32(f32_to_bf16_bits(f[e] * s)), acc[4 * j + e]);
             }
         }
     } else {
@@ -419,39 +418,83 @@ __global__ void k_scale_vec(const float *v, float lambda, int n, float *b) {
 }
 
 // ---- scoring ----
-__device__ float row_lse(const float *x, int vocab, float *shf, double *shd) {
+// ---- log-softmax and KL over row chunks ----
+// A vocabulary row (C2: 128256 logits) is split into `chunks` pieces so the
+// whole GPU works on a batch of prompts: piece (row, c) finds its maximum
+// m_c and s_c = sum exp(x - m_c) in f64; the row's log-sum-exp combines the
+// pieces in order, lse = m + log(sum_c s_c exp(m_c - m)) with m = max m_c, as
+// src/tensor.zig:1203-1210 (f64 sum of the f64 exps, the result in f32); the
+// KL pieces then add exp(b)(b - (x - lse)) in f64 (src/scorers.zig:385-400)
+// and one thread per row adds the pieces in order.
+__global__ void __launch_bounds__(256) k_lse_part(const float *x, int vocab, int per, double2 *part) {
+    __shared__ float shf[32];
+    __shared__ double shd[32];
+    const int row = blockIdx.y, c = blockIdx.x, chunks = gridDim.x;
+    const float *xr = x + (long long)row * vocab;
+    const int lo = c * per, hi = min(vocab, lo + per);
     float m = -INFINITY;
-    for (int j = threadIdx.x; j < vocab; j += blockDim.x) m = fmaxf(m, x[j]);
+#pragma unroll 4
+    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) m = fmaxf(m, xr[j]);
     m = block_max(m, shf);
     double s = 0.0;
-    for (int j = threadIdx.x; j < vocab; j += blockDim.x) s += exp((double)(x[j] - m));
+    if (m > -INFINITY) {
+#pragma unroll 4
+        for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) s += exp((double)(xr[j] - m));
+    }
     s = block_sum_d(s, shd);
+    if (threadIdx.x == 0) part[(long long)row * chunks + c] = make_double2((double)m, s);
+}
+
+__device__ __forceinline__ float row_lse_from_parts(const double2 *part, int chunks) {
+    float m = -INFINITY;
+    for (int c = 0; c < chunks; c++) m = fmaxf(m, (float)part[c].x);
+    double s = 0.0;
+    for (int c = 0; c < chunks; c++)
+        if (part[c].x > -INFINITY) s += part[c].y * exp(part[c].x - (double)m);
     return m + (float)log(s);
 }
 
-__global__ void k_log_softmax(const float *x, int vocab, float *out) {
-    __shared__ float shf[32];
-    __shared__ double shd[32];
-    const float *xr = x + (long long)blockIdx.x * vocab;
-    const float lse = row_lse(xr, vocab, shf, shd);
-    float *o = out + (long long)blockIdx.x * vocab;
-    for (int j = threadIdx.x; j < vocab; j += blockDim.x) o[j] = xr[j] - lse;
+__global__ void __launch_bounds__(256) k_log_softmax_part(const float *x, int vocab, int per, const double2 *part,
+                                                          float *out) {
+    __shared__ float s_lse;
+    const int row = blockIdx.y, c = blockIdx.x, chunks = gridDim.x;
+    if (threadIdx.x == 0) s_lse = row_lse_from_parts(part + (long long)row * chunks, chunks);
+    __syncthreads();
+    const float lse = s_lse;
+    const float *xr = x + (long long)row * vocab;
+    float *o = out + (long long)row * vocab;
+    const int lo = c * per, hi = min(vocab, lo + per);
+    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) o[j] = xr[j] - lse;
 }
 
-__global__ void k_kl(const float *base, const float *logits, int vocab, double *kl) {
-    __shared__ float shf[32];
+__global__ void __launch_bounds__(256) k_kl_part(const float *base, const float *logits, int vocab, int per,
+                                                 const double2 *part, double *kl_part) {
+    __shared__ float s_lse;
     __shared__ double shd[32];
-    const float *xr = logits + (long long)blockIdx.x * vocab;
-    const float *lb = base + (long long)blockIdx.x * vocab;
-    const float lse = row_lse(xr, vocab, shf, shd);
+    const int row = blockIdx.y, c = blockIdx.x, chunks = gridDim.x;
+    if (threadIdx.x == 0) s_lse = row_lse_from_parts(part + (long long)row * chunks, chunks);
+    __syncthreads();
+    const float lse = s_lse;
+    const float *xr = logits + (long long)row * vocab;
+    const float *lb = base + (long long)row * vocab;
+    const int lo = c * per, hi = min(vocab, lo + per);
     double s = 0.0;
-    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+#pragma unroll 4
+    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) {
         const double b = (double)lb[j];
         const float lt = xr[j] - lse;
         s += exp(b) * (b - (double)lt);
     }
     s = block_sum_d(s, shd);
-    if (threadIdx.x == 0) kl[blockIdx.x] = s;
+    if (threadIdx.x == 0) kl_part[(long long)row * chunks + c] = s;
+}
+
+__global__ void k_kl_rows_sum(const double *kl_part, int rows, int chunks, double *kl) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows) return;
+    double s = 0.0;
+    for (int c = 0; c < chunks; c++) s += kl_part[(long long)row * chunks + c];
+    kl[row] = s;
 }
 
 // ---- capture and directions ----
@@ -655,15 +698,36 @@ cudaError_t scale_vec(const float *v, float lambda, int n, float *b, cudaStream_
     return cudaGetLastError();
 }
 
-cudaError_t log_softmax_rows(const float *x, int rows, int vocab, float *out, cudaStream_t st) {
+int kl_chunks(int rows, int vocab) {
+    // about four blocks per SM over the batch, pieces of at least 4096 logits
+    int c = (4 * 148 + std::max(rows, 1) - 1) / std::max(rows, 1);
+    c = std::min(c, std::max(1, vocab / 4096));
+    return std::max(1, std::min(c, 64));
+}
+
+size_t kl_scratch_bytes(int rows, int vocab) {
+    const size_t n = (size_t)std::max(rows, 1) * kl_chunks(rows, vocab);
+    return n * sizeof(double2) + n * sizeof(double);
+}
+
+cudaError_t log_softmax_rows(const float *x, int rows, int vocab, float *out, void *scratch, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    k_log_softmax<<<rows, 1024, 0, st>>>(x, vocab, out);
+    const int chunks = kl_chunks(rows, vocab), per = (vocab + chunks - 1) / chunks;
+    double2 *part = static_cast<double2 *>(scratch);
+    k_lse_part<<<dim3(chunks, rows), 256, 0, st>>>(x, vocab, per, part);
+    k_log_softmax_part<<<dim3(chunks, rows), 256, 0, st>>>(x, vocab, per, part, out);
     return cudaGetLastError();
 }
 
-cudaError_t kl_rows(const float *baseline, const float *logits, int rows, int vocab, double *kl, cudaStream_t st) {
+cudaError_t kl_rows(const float *baseline, const float *logits, int rows, int vocab, double *kl, void *scratch,
+                    cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    k_kl<<<rows, 1024, 0, st>>>(baseline, logits, vocab, kl);
+    const int chunks = kl_chunks(rows, vocab), per = (vocab + chunks - 1) / chunks;
+    double2 *part = static_cast<double2 *>(scratch);
+    double *kl_part = reinterpret_cast<double *>(part + (size_t)rows * chunks);
+    k_lse_part<<<dim3(chunks, rows), 256, 0, st>>>(logits, vocab, per, part);
+    k_kl_part<<<dim3(chunks, rows), 256, 0, st>>>(baseline, logits, vocab, per, part, kl_part);
+    k_kl_rows_sum<<<(rows + 127) / 128, 128, 0, st>>>(kl_part, rows, chunks, kl);
     return cudaGetLastError();
 }
 

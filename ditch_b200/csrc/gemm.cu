@@ -223,30 +223,6 @@ __device__ __forceinline__ TileInfo tile_info(const GemmParams &p, int tile, int
 // half h = t >> 7 of it: output chunks 4h .. 4h + 3 (16 bytes = 8 elements
 // each); chunk j lands at (j ^ (r & 7)) within the row's 128 bytes.
 
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-    uint64_t ra, rb, rd;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
-    float2 d;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
-    return d;
-}
-
-// Two E4M3 codes (low byte first) to two f32, exactly (via f16x2).
-__device__ __forceinline__ float2 e4m3x2_f32(uint32_t two) {
-    uint32_t h;
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, lo;\n\t}" : "=r"(h) : "r"(two));
-    return __half22float2(*reinterpret_cast<__half2 *>(&h));
-}
-
-// bf16x2 of (a, b) * s, each product rounded to f32 first (the reference's
-// f32 multiply then round-to-nearest-even to bf16).
-__device__ __forceinline__ uint32_t scale_pack(float2 v, float s) {
-    const float2 r = mul2(v, make_float2(s, s));
-    return pack_bf16x2(r.x, r.y);
-}
-
 // Four E4M3 codes (one word, low byte first) times one block scale s, as two
 // bf16x2 words (codes 0, 1 and 2, 3). (Measured on B200: building the f32
 // values with integer shifts and one multiply by s * 2^120, exact but with
@@ -287,17 +263,6 @@ __device__ __forceinline__ void xform_fp8(const uint8_t *raw, uint8_t *atile, in
             put_chunk(atile, r, j, o);
         }
     }
-}
-
-__device__ __forceinline__ float e8m0_scale(uint32_t b) {
-    return __uint_as_float(b == 0 ? 0x00400000u : (b << 23));
-}
-
-// Two E2M1 nibbles (one byte, low nibble first) to two f32, exactly (via f16x2).
-__device__ __forceinline__ float2 e2m1x2_f32(uint32_t byte) {
-    uint32_t h;
-    asm("{\n\t.reg .b8 b;\n\tcvt.u8.u32 b, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b;\n\t}" : "=r"(h) : "r"(byte));
-    return __half22float2(*reinterpret_cast<__half2 *>(&h));
 }
 
 // MXFP4 (natural layout): bf16(e2m1[nibble] * 2^(e - 127)), low nibble first.

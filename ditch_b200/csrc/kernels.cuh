@@ -105,9 +105,6 @@ struct AttnParams {
 // Causal attention within each prompt with GQA, RoPE (neox) and optional q/k
 // norms (src/model.zig:4226-4374, attentionWorker 2935-2986).
 cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st);
-// True when attention_prefill leaves the q and k columns of the QKV rows
-// normed and roped in place (the tensor-core path, head sizes 64 and 128).
-bool attention_prefill_preps_in_place(int head_dim, int force_generic);
 
 // ---- greedy decode with a KV cache (src/model.zig:5378-5444) ---------------
 // One layer's cache: keys (normed and roped) and values, f32
@@ -122,7 +119,7 @@ struct KvParams {
     const float *q_norm, *k_norm;
     float eps;
     float *cache_k, *cache_v;
-    int prep_k;  // 1: norm and rope the keys while storing them (0: the attention already did, in place)
+    int prep_k;  // 1: norm and rope the keys while storing them (0: they are stored as given)
     int prep_q;  // 1: norm and rope the queries in place (decode rows)
     int *status;
 };
@@ -186,10 +183,14 @@ cudaError_t prenorm_vec(const float *v, const float *n, float lambda, int len, f
 cudaError_t scale_vec(const float *v, float lambda, int n, float *b, cudaStream_t st);
 
 // ---- scoring ----------------------------------------------------------------
-// Per row: logSoftmax with an f64 sum (src/tensor.zig:1203-1210).
-cudaError_t log_softmax_rows(const float *x, int rows, int vocab, float *out, cudaStream_t st);
+// Per row: logSoftmax with an f64 sum (src/tensor.zig:1203-1210). Rows are
+// split into pieces over the SMs; `scratch` holds kl_scratch_bytes(rows,
+// vocab) bytes.
+cudaError_t log_softmax_rows(const float *x, int rows, int vocab, float *out, void *scratch, cudaStream_t st);
 // Per row: sum_j exp(lb_j) (lb_j - logsoftmax(x)_j) in f64 (src/scorers.zig:378-402).
-cudaError_t kl_rows(const float *baseline, const float *logits, int rows, int vocab, double *kl, cudaStream_t st);
+cudaError_t kl_rows(const float *baseline, const float *logits, int rows, int vocab, double *kl, void *scratch,
+                    cudaStream_t st);
+size_t kl_scratch_bytes(int rows, int vocab);
 
 // ---- capture and directions -------------------------------------------------
 // sums[l][h] += mean over take[b] captures of prompt b (f64), per prompt and

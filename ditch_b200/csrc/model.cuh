@@ -126,7 +126,7 @@ struct ditch_cuda_model {
     ditch::DevBuf gemv_part;  // partial sums of the deterministic GEMV-T
     // KL prompts
     ditch::Batch kl;
-    ditch::DevBuf kl_base, kl_vals;
+    ditch::DevBuf kl_base, kl_vals, kl_part;  // kl_part: the row pieces' log-sum-exp and KL sums
     bool kl_ready = false;
     std::vector<size_t> kl_offsets;
     std::vector<uint32_t> kl_tokens_host;

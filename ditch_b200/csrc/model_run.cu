@@ -535,7 +535,7 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
                 DITCH_LAUNCH(dev, attention_decode(dp, st));
             } else {
                 DITCH_LAUNCH(dev, attention_prefill(ap, st));
-                kp.prep_k = attention_prefill_preps_in_place(c.head_dim, 0) ? 0 : 1;
+                kp.prep_k = 1;  // the prefill attention leaves the QKV rows as the GEMM wrote them
                 DITCH_LAUNCH(dev, kv_store(kp, st));
             }
         }
@@ -936,7 +936,9 @@ int kl_score_impl(ditch_cuda_model *m, double *kl) {
     int s;
     if ((s = forward_batch(m, m->kl, 0, P))) return s;
     DITCH_CUDA(m->kl_vals.reserve((size_t)P * 8));
-    DITCH_LAUNCH(dev, kl_rows(m->kl_base.as<float>(), m->logits.as<float>(), P, V, m->kl_vals.as<double>(), dev->stream));
+    DITCH_CUDA(m->kl_part.reserve(kl_scratch_bytes(P, V)));
+    DITCH_LAUNCH(dev, kl_rows(m->kl_base.as<float>(), m->logits.as<float>(), P, V, m->kl_vals.as<double>(),
+                              m->kl_part.ptr, dev->stream));
     if (m->dp_group) {
         // data parallel: every rank's per-prompt values summed in rank order,
         // then prompt order (one device's order over the concatenated prompts)
@@ -1182,7 +1184,8 @@ int ditch_cuda_kl_init(ditch_cuda_model *m, const uint32_t *tokens, const size_t
     if (s) return s;
     if ((s = upload_expert_flags(m))) return s;
     DITCH_CUDA(m->kl_base.reserve((size_t)P * V * 4));
-    DITCH_LAUNCH(dev, log_softmax_rows(m->logits.as<float>(), P, V, m->kl_base.as<float>(), dev->stream));
+    DITCH_CUDA(m->kl_part.reserve(kl_scratch_bytes(P, V)));
+    DITCH_LAUNCH(dev, log_softmax_rows(m->logits.as<float>(), P, V, m->kl_base.as<float>(), m->kl_part.ptr, dev->stream));
     if ((s = check_status(dev, "kl_init"))) return s;
     m->kl_ready = true;
     return DITCH_CUDA_OK;

@@ -28,7 +28,8 @@ def same_bits(a, b):
 
 
 # ---- decoders ----
-@pytest.mark.parametrize("rows,cols,br,bc", [(128, 256, 128, 128), (37, 40, 16, 8), (1, 16, 1, 16), (300, 128, 128, 128)])
+@pytest.mark.parametrize("rows,cols,br,bc", [(128, 256, 128, 128), (37, 40, 16, 8), (1, 16, 1, 16), (300, 128, 128, 128),
+                                         (3, 8240, 128, 128), (5, 4128, 2, 32)])
 def test_dequant_fp8_bit_exact(device, rows, cols, br, bc):
     codes = rng.integers(0, 256, (rows, cols), dtype=np.uint8)
     codes.flat[:256 if codes.size >= 256 else codes.size] = np.arange(min(256, codes.size), dtype=np.uint8)
@@ -36,10 +37,10 @@ def test_dequant_fp8_bit_exact(device, rows, cols, br, bc):
     same_bits(device.dequant_fp8(codes, scales, br, bc), oracle.dequant_fp8(codes, scales, br, bc))
 
 
-@pytest.mark.parametrize("bits,group,actorder", [(4, 128, False), (4, 16, False), (8, 32, False), (3, 32, False),
-                                                 (4, 16, True)])
-def test_dequant_int_bit_exact(device, bits, group, actorder):
-    rows, cols = 24, 128
+@pytest.mark.parametrize("bits,group,actorder,cols", [(4, 128, False, 128), (4, 16, False, 128), (8, 32, False, 128),
+                                                      (3, 32, False, 128), (4, 16, True, 128), (4, 32, False, 8224)])
+def test_dequant_int_bit_exact(device, bits, group, actorder, cols):
+    rows = 24
     wpr = -(-cols * bits // 32)
     packed = rng.integers(0, 2 ** 32, (rows, wpr), dtype=np.uint64).astype(np.uint32)
     groups = cols // group
@@ -53,9 +54,8 @@ def test_dequant_int_bit_exact(device, bits, group, actorder):
               oracle.dequant_int_packed(packed, scales, None, rows, cols, bits, group, g_idx))
 
 
-@pytest.mark.parametrize("transposed", [False, True])
-def test_dequant_mxfp4_bit_exact(device, transposed):
-    rows, cols = 40, 96
+@pytest.mark.parametrize("transposed,rows,cols", [(False, 40, 96), (True, 40, 96), (False, 3, 8320)])
+def test_dequant_mxfp4_bit_exact(device, transposed, rows, cols):
     blocks = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
     scales = rng.integers(100, 140, (rows, cols // 32), dtype=np.uint8)
     scales[0, 0], scales[1, 1], scales[2, 2] = 0, 255, 254  # subnormal, infinite and largest scales
