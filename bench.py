@@ -247,12 +247,15 @@ def host_threads():
 
 
 def cpu_baseline(args, reps=None, warmup=0):
-    """Times ditch's CPU engine restated in C (oracle/, f32, VL=16 FMA, all
-    host threads) on a bounded sample: one decoder layer of the C2 shape over
-    a few prompts, the LM head rows, the per-layer edit GEMVs and the KL rows,
-    extrapolated to the whole trial (32 layers, `--prompts` prompts). Weights
-    are random f32 (timing does not depend on values; the FP8 decode happens
-    once at load in the reference's mapped mode and is not timed)."""
+    """Times ditch's CPU engine restated in C (oracle/, VL=16 FMA, all host
+    threads) on a bounded sample: one decoder layer of the C2 shape over 8
+    prompts, the LM head rows, the per-layer edit GEMVs and the KL rows,
+    extrapolated to the whole trial (32 layers, `--prompts` prompts). The
+    linear weights and the LM head are bf16, multiplied through ditch's
+    half-precision path (rows converted to f32 per task, then the f32 tiles:
+    src/tensor.zig:827-883), which is how ditch holds an FP8 checkpoint in
+    mapped mode (decoded to bf16 once at load, src/dequant.zig:477-514; the
+    decode is not timed). Values are random (timing does not depend on them)."""
     import oracle
     from oracle.model import OracleModel, flatten_batch
 
@@ -265,14 +268,14 @@ def cpu_baseline(args, reps=None, warmup=0):
     rng = np.random.default_rng(args.seed)
 
     def w(r, c):
-        return (rng.standard_normal((r, c), dtype=np.float32) * 0.02)
+        return oracle.f32_to_bf16_bits(rng.standard_normal((r, c), dtype=np.float32) * np.float32(0.02))
 
     big = w(V, H)
     ones = np.ones(H, np.float32)
-    weights = {"embed": big, "lm_head": big, "final_norm": ones, "L0.input_norm": ones, "L0.post_norm": ones,
-               "L0.q": w(qd, H), "L0.k": w(kvd, H), "L0.v": w(kvd, H), "L0.o": w(H, qd), "L0.gate": w(I, H),
-               "L0.up": w(I, H), "L0.down": w(H, I)}
-    m = OracleModel(spec, weights)
+    weights = {"embed": oracle.bf16_bits_to_f32(big), "lm_head": big, "final_norm": ones, "L0.input_norm": ones,
+               "L0.post_norm": ones, "L0.q": w(qd, H), "L0.k": w(kvd, H), "L0.v": w(kvd, H), "L0.o": w(H, qd),
+               "L0.gate": w(I, H), "L0.up": w(I, H), "L0.down": w(H, I)}
+    m = OracleModel(spec, weights, weights_bf16=True)
     p_cpu = 8
     sample = [rng.integers(0, V, args.seq).astype(np.uint32) for _ in range(p_cpu)]
     toks, rb, rp, cap, first, take, last = flatten_batch(sample)
@@ -289,16 +292,17 @@ def cpu_baseline(args, reps=None, warmup=0):
     t_layer = (time.perf_counter() - t0) / reps
     hl = rng.standard_normal((p_cpu, H), dtype=np.float32)
     t0 = time.perf_counter()
-    logits = oracle.matmul_t(hl, big)
+    logits = oracle.matmul_t_bf16(hl, big)
     t_lm = time.perf_counter() - t0
     base = oracle.log_softmax(logits)
     t0 = time.perf_counter()
     oracle.kl_first_token(base, logits)
     t_kl = time.perf_counter() - t0
     v = rng.standard_normal(H).astype(np.float32)
-    t0 = time.perf_counter()
-    oracle.compute_delta_none(weights["L0.o"], v, 1.0)
-    oracle.compute_delta_none(weights["L0.down"], v, 1.0)
+    wo, wd = oracle.bf16_bits_to_f32(weights["L0.o"]), oracle.bf16_bits_to_f32(weights["L0.down"])
+    t0 = time.perf_counter()  # the GEMV-T of the edit over the rows as f32 (the conversion is not timed)
+    oracle.compute_delta_none(wo, v, 1.0)
+    oracle.compute_delta_none(wd, v, 1.0)
     t_edit = time.perf_counter() - t0
     scale = args.prompts / p_cpu
     nl = args.layers
@@ -307,14 +311,15 @@ def cpu_baseline(args, reps=None, warmup=0):
     return {
         "value": tokens / s_trial, "unit": "tokens/s", "cores": cores, "kind": "port",
         "s_per_trial": s_trial,
-        "sample": (f"oracle (C restatement of ditch's f32 CPU engine), {cores} threads: 1 C2 decoder layer over "
-                   f"{p_cpu} prompts x {args.seq} tokens ({reps} reps, {t_layer:.3f} s), LM head + KL on {p_cpu} "
-                   f"rows, o/down edit GEMVs of one layer; extrapolated to {nl} layers x {args.prompts} prompts"),
+        "sample": (f"oracle (C restatement of ditch's CPU engine, bf16 weights through its half-precision path as "
+                   f"in mapped mode), {cores} threads: 1 C2 decoder layer over {p_cpu} prompts x {args.seq} tokens "
+                   f"({reps} reps, {t_layer:.3f} s), LM head + KL on {p_cpu} rows, o/down edit GEMVs of one layer; "
+                   f"extrapolated to {nl} layers x {args.prompts} prompts"),
     }
 
 
 def reference_arm(args):
-    # one step = one timed sample (a C2 decoder layer over 2 prompts, the LM
+    # one step = one timed sample (a C2 decoder layer over 8 prompts, the LM
     # head and KL rows, the edit GEMVs), after `warmup` untimed ones
     cb = cpu_baseline(args, reps=max(1, args.steps), warmup=args.warmup)
     tokens = args.prompts * args.seq
@@ -323,7 +328,7 @@ def reference_arm(args):
         "impl": "reference", "metric": "trial-eval forward tokens/s", "value": round(v, 3), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(tokens / v * 1000.0, 3), "s_per_trial": round(cb["s_per_trial"], 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 weights, f32 arithmetic", "data": "synthetic",
         "config": config_block(args),
         "cpu_baseline": cb,
         "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

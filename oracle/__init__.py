@@ -48,7 +48,7 @@ class Layer(C.Structure):
 
 class Model(C.Structure):
     _fields_ = [("c", Config), ("embed", f32p), ("final_norm", f32p), ("lm_head", f32p),
-                ("layers", C.POINTER(Layer))]
+                ("layers", C.POINTER(Layer)), ("w_bf16", C.c_int)]
 
 
 class Params(C.Structure):
@@ -118,6 +118,8 @@ def lib():
         L.or_kl_first_token.restype = C.c_double
         L.or_kl_first_token.argtypes = [f32p, f32p, C.c_size_t, C.c_size_t, f64p]
         L.or_f32_to_bf16_array.argtypes = [f32p, C.c_size_t, u16p]
+        L.or_matmul_t_bf16.argtypes = [f32p, f32p, C.c_size_t, u16p, C.c_size_t, C.c_size_t, f32p, f32p,
+                                       C.c_size_t]
         L.or_set_threads.argtypes = [C.c_int]
         L.or_get_threads.restype = C.c_int
         _LIB = L
@@ -165,6 +167,17 @@ def matmul_t(x, w, da=None, db=None):
     da = None if da is None else f32(da)
     db = None if db is None else f32(db)
     lib().or_matmul_t(ptr(out), ptr(x), n, ptr(w), rows, cols, ptr(da), ptr(db), rank)
+    return out
+
+
+def matmul_t_bf16(x, w_bits):
+    """matmulT over bf16 weights (bit array [rows][cols]) through ditch's
+    half-precision path (src/tensor.zig:827-883, 449-486)."""
+    x = f32(x)
+    w_bits = np.ascontiguousarray(w_bits, np.uint16)
+    n, rows = x.shape[0], w_bits.shape[0]
+    out = np.zeros((n, rows), np.float32)
+    lib().or_matmul_t_bf16(ptr(out), ptr(x), n, ptr(w_bits, u16p), rows, w_bits.shape[1], None, None, 0)
     return out
 
 

@@ -37,6 +37,12 @@ float or_dot(const float *a, const float *b, size_t n);
  * delta A [rank][cols], B [rows][rank] (NULL / rank 0 = none). */
 void or_matmul_t(float *out, const float *x, size_t n, const float *w, size_t rows,
                  size_t cols, const float *da, const float *db, size_t rank);
+/* The same product over bf16 weights (src/tensor.zig:827-883, 449-486): each
+ * task converts its weight rows to f32, then the f32 tiles; for at most four
+ * inputs ditch's fused path (src/tensor.zig:919-1020) gives the same dot
+ * products (every row a VL-lane FMA dot). */
+void or_matmul_t_bf16(float *out, const float *x, size_t n, const uint16_t *w, size_t rows,
+                      size_t cols, const float *da, const float *db, size_t rank);
 /* out[q][cols] = y[q][rows] . W (src/tensor.zig:1079-1094). */
 void or_matvec_t_multi(float *out, const float *w, size_t rows, size_t cols,
                        const float *y, size_t q);
@@ -132,6 +138,11 @@ typedef struct {
     const float *final_norm; /* [H] */
     const float *lm_head;    /* [V][H] */
     const or_layer *layers;
+    /* 1: the linear weights (q, k, v, o, gate, up, down, router, expert stacks
+     * and lm_head) are bf16 bit arrays (uint16), multiplied through ditch's
+     * half-precision path (or_matmul_t_bf16), as a checkpoint held in bf16
+     * is in mapped mode */
+    int w_bf16;
 } or_model;
 
 /* One batched forward (src/model.zig:4619 `forward` + ForwardOptions 3136-3144).

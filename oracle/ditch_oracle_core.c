@@ -181,6 +181,49 @@ void or_matmul_t(float *out, const float *x, size_t n, const float *w, size_t ro
     }
 }
 
+void or_matmul_t_bf16(float *out, const float *x, size_t n, const uint16_t *w, size_t rows,
+                      size_t cols, const float *da, const float *db, size_t rank) {
+    if (rows == 0 || n == 0) return;
+    const int fast =
+#if defined(__x86_64__)
+        have_avx512();
+#else
+        0;
+#endif
+    const long rblocks = (long)((rows + 3) / 4);
+#pragma omp parallel num_threads(or_get_threads())
+    {
+        float *buf = (float *)malloc(sizeof(float) * 4 * cols);  /* this task's rows as f32 */
+#pragma omp for schedule(dynamic, 4)
+        for (long rb = 0; rb < rblocks; rb++) {
+            size_t r0 = (size_t)rb * 4;
+            size_t nr = rows - r0 < 4 ? rows - r0 : 4;
+            for (size_t k = 0; k < nr; k++)
+                for (size_t c = 0; c < cols; c++) buf[k * cols + c] = or_bf16_to_f32(w[(r0 + k) * cols + c]);
+            size_t i = 0;
+#if defined(__x86_64__)
+            if (fast && nr == 4)
+                for (; i + 4 <= n; i += 4) tile4x4_avx512(buf, x + i * cols, cols, rows, out + i * rows + r0);
+#endif
+            for (; i < n; i++)
+                for (size_t k = 0; k < nr; k++) out[i * rows + r0 + k] = or_dot(buf + k * cols, x + i * cols, cols);
+        }
+        free(buf);
+    }
+    if (da && db && rank > 0) {
+        float *xa = (float *)malloc(sizeof(float) * n * rank);
+        for (size_t i = 0; i < n; i++)
+            for (size_t j = 0; j < rank; j++) xa[i * rank + j] = or_dot(da + j * cols, x + i * cols, cols);
+        for (size_t i = 0; i < n; i++)
+            for (size_t r = 0; r < rows; r++) {
+                float v = 0;
+                for (size_t j = 0; j < rank; j++) v += db[r * rank + j] * xa[i * rank + j];
+                out[i * rows + r] += v;
+            }
+        free(xa);
+    }
+}
+
 /* matvecTMulti with one accumulator slot: out[j] = sum_r y[j][r] * W_r,
  * rows with y == 0 skipped, `axpy` unfused (src/tensor.zig:560-570,
  * 1056-1094). The column range is split across threads; each column keeps

@@ -52,6 +52,16 @@ static void attend(const float *q, const float *kbase, const float *vbase, size_
 }
 
 /* topk (src/moe.zig:971-985): the first maximum wins ties. */
+/* A weight product: f32 weights, or (m->w_bf16) bf16 bit arrays through
+ * ditch's half-precision path; `off` elements into the weight (expert slabs). */
+static void mm(const or_model *m, float *out, const float *x, size_t n, const float *w, size_t off, size_t rows,
+               size_t cols, const float *da, const float *db, size_t rank) {
+    if (m->w_bf16)
+        or_matmul_t_bf16(out, x, n, (const uint16_t *)(const void *)w + off, rows, cols, da, db, rank);
+    else
+        or_matmul_t(out, x, n, w + off, rows, cols, da, db, rank);
+}
+
 static void topk(const float *scores, float *sel, size_t ne, size_t k, size_t *idx, float *wts) {
     for (size_t j = 0; j < k; j++) {
         size_t best = 0;
@@ -69,7 +79,7 @@ static void moe_forward(const or_model *m, const or_layer *L, const float *h, si
     const or_config *c = &m->c;
     size_t H = (size_t)c->hidden, E = (size_t)c->n_experts, k = (size_t)c->top_k, mi = (size_t)c->moe_inter;
     float *logits = malloc(sizeof(float) * n * E);
-    or_matmul_t(logits, h, n, L->router, E, H, NULL, NULL, 0);
+    mm(m, logits, h, n, L->router, 0, E, H, NULL, NULL, 0);
     size_t *sel = malloc(sizeof(size_t) * n * k);
     float *selw = malloc(sizeof(float) * n * k), *choice = malloc(sizeof(float) * E);
     for (size_t t = 0; t < n; t++) {
@@ -94,13 +104,13 @@ static void moe_forward(const or_model *m, const or_layer *L, const float *h, si
                 if (sel[t * k + j] == e) { tok[ne] = t; w[ne] = selw[t * k + j]; ne++; }
         if (ne == 0) continue;
         for (size_t j = 0; j < ne; j++) memcpy(xg + j * H, h + tok[j] * H, sizeof(float) * H);
-        or_matmul_t(g, xg, ne, L->e_gate + e * mi * H, mi, H, NULL, NULL, 0);
-        or_matmul_t(u, xg, ne, L->e_up + e * mi * H, mi, H, NULL, NULL, 0);
+        mm(m, g, xg, ne, L->e_gate, e * mi * H, mi, H, NULL, NULL, 0);
+        mm(m, u, xg, ne, L->e_up, e * mi * H, mi, H, NULL, NULL, 0);
         or_gated_silu(g, g, u, ne, mi, mi, mi);
         const float *da = L->e_down_da ? L->e_down_da[e] : NULL;
         const float *db = L->e_down_db ? L->e_down_db[e] : NULL;
         const size_t dr = L->e_down_rank ? L->e_down_rank[e] : 1;
-        or_matmul_t(eo, g, ne, L->e_down + e * H * mi, H, mi, da, db, da && db ? dr : 0);
+        mm(m, eo, g, ne, L->e_down, e * H * mi, H, mi, da, db, da && db ? dr : 0);
         for (size_t j = 0; j < ne; j++) axpy(out + tok[j] * H, w[j], eo + j * H, H);
     }
     free(logits); free(sel); free(selw); free(choice); free(xg); free(g); free(u); free(eo);
@@ -144,10 +154,10 @@ int or_forward(const or_model *m, const uint32_t *tokens, const uint32_t *row_b,
     for (int li = 0; li < c->n_layers; li++) {
         const or_layer *L = &m->layers[li];
         for (size_t i = 0; i < n; i++) or_rmsnorm(h + i * H, x + i * H, L->input_norm, H, c->eps);
-        or_matmul_t(q, h, n, L->q, qd, H, NULL, NULL, 0);
+        mm(m, q, h, n, L->q, 0, qd, H, NULL, NULL, 0);
         add_bias(q, n, qd, L->qb);
-        or_matmul_t(kk, h, n, L->k, kvd, H, NULL, NULL, 0);
-        or_matmul_t(vv, h, n, L->v, kvd, H, NULL, NULL, 0);
+        mm(m, kk, h, n, L->k, 0, kvd, H, NULL, NULL, 0);
+        mm(m, vv, h, n, L->v, 0, kvd, H, NULL, NULL, 0);
         add_bias(kk, n, kvd, L->kb);
         add_bias(vv, n, kvd, L->vb);
         for (size_t i = 0; i < n; i++) {
@@ -178,16 +188,16 @@ int or_forward(const or_model *m, const uint32_t *tokens, const uint32_t *row_b,
             }
             free(scores);
         }
-        or_matmul_t(o, att, n, L->o, H, qd, L->o_da, L->o_db, L->o_rank);
+        mm(m, o, att, n, L->o, 0, H, qd, L->o_da, L->o_db, L->o_rank);
         for (size_t i = 0; i < n; i++) axpy(x + i * H, 1.0f, o + i * H, H);
         for (size_t i = 0; i < n; i++) or_rmsnorm(h + i * H, x + i * H, L->post_norm, H, c->eps);
         if (L->router) {
             moe_forward(m, L, h, n, mo);
         } else {
-            or_matmul_t(gate, h, n, L->gate, I, H, NULL, NULL, 0);
-            or_matmul_t(up, h, n, L->up, I, H, NULL, NULL, 0);
+            mm(m, gate, h, n, L->gate, 0, I, H, NULL, NULL, 0);
+            mm(m, up, h, n, L->up, 0, I, H, NULL, NULL, 0);
             or_gated_silu(gate, gate, up, n, I, I, I);
-            or_matmul_t(mo, gate, n, L->down, H, I, L->down_da, L->down_db, L->down_rank);
+            mm(m, mo, gate, n, L->down, 0, H, I, L->down_da, L->down_db, L->down_rank);
         }
         for (size_t i = 0; i < n; i++) axpy(x + i * H, 1.0f, mo + i * H, H);
         if (residuals)
@@ -197,7 +207,7 @@ int or_forward(const or_model *m, const uint32_t *tokens, const uint32_t *row_b,
     if (nl > 0 && logits) {
         float *hl = malloc(sizeof(float) * nl * H);
         for (size_t i = 0; i < nl; i++) or_rmsnorm(hl + i * H, x + logit_rows[i] * H, m->final_norm, H, c->eps);
-        or_matmul_t(logits, hl, nl, m->lm_head, V, H, NULL, NULL, 0);
+        mm(m, logits, hl, nl, m->lm_head, 0, V, H, NULL, NULL, 0);
         free(hl);
     }
     free(x); free(h); free(q); free(kk); free(vv); free(att); free(o); free(gate); free(up);

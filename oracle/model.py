@@ -15,10 +15,24 @@ import numpy as np
 from . import Config, Layer, Model, f32, f32p, lib, ptr, szp, u32p
 
 
+LINEAR = ("q", "k", "v", "o", "gate", "up", "down", "router", "e_gate", "e_up", "e_down")
+
+
 class OracleModel:
-    def __init__(self, spec, weights):
+    def __init__(self, spec, weights, weights_bf16=False):
+        """weights_bf16: the linear weights and lm_head are given as bf16 bit
+        arrays (uint16) and multiplied through ditch's half-precision path, as
+        a checkpoint held in bf16 is (mapped mode); the rest stays f32."""
         self.spec = spec
-        self.w = {k: f32(v) for k, v in weights.items()}
+        self.w_bf16 = bool(weights_bf16)
+
+        def keep(k, v):
+            linear = k == "lm_head" or k.split(".")[-1] in LINEAR
+            if self.w_bf16 and linear:
+                return np.ascontiguousarray(v, np.uint16)
+            return f32(v)
+
+        self.w = {k: keep(k, v) for k, v in weights.items()}
         self._keep = []
         self.deltas = {}  # (layer, "o"|"down"|("e", e)) -> (a [cols], b [rows])
 
@@ -44,7 +58,9 @@ class OracleModel:
 
         def g(name):
             a = self.w.get(name)
-            return None if a is None else ptr(a)
+            if a is None:
+                return None
+            return C.cast(a.ctypes.data_as(C.c_void_p), f32p) if a.dtype == np.uint16 else ptr(a)
 
         for i in range(s["n_layers"]):
             L = layers[i]
@@ -72,7 +88,7 @@ class OracleModel:
                 L.e_down_rank = C.cast(dr, szp)
                 keep += [da, db, dr]
         m = Model(c=cfg, embed=g("embed"), final_norm=g("final_norm"), lm_head=g("lm_head"),
-                  layers=C.cast(layers, C.POINTER(Layer)))
+                  layers=C.cast(layers, C.POINTER(Layer)), w_bf16=int(self.w_bf16))
         self._keep = [layers, keep]
         return m
 
