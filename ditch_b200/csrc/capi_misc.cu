@@ -282,10 +282,11 @@ int ditch_cuda_set_decode_cache(ditch_cuda_device *dev, int enabled) {
     return DITCH_CUDA_OK;
 }
 
-int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int enabled) {
+int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int level) {
     REQUIRE(dev, "null device");
+    REQUIRE(level >= 0 && level <= 2, "CTA-pair level must be 0, 1 or 2");
     std::lock_guard<std::mutex> lk(dev->mu);
-    dev->cta_pairs = enabled != 0;
+    dev->cta_pairs = level;
     return DITCH_CUDA_OK;
 }
 

@@ -55,7 +55,7 @@ cudaError_t run_skinny(ditch_cuda_device *dev, int fmt, const GemmOperand &a, co
                        const GemmParams &p0, int k_splits) {
     GemmParams p = p0;
     p.status = dev->status;
-    p.cta_pairs = dev->cta_pairs ? 1 : 0;
+    p.cta_pairs = dev->cta_pairs;
     GemmEvent *ev = nullptr;
     if (dev->profiling) {
         if (dev->n_events == dev->events.size()) {
@@ -78,7 +78,7 @@ cudaError_t run_gemm(ditch_cuda_device *dev, int fmt, const GemmOperand &a, cons
                      const GemmOperand &b, const GemmParams &p0) {
     GemmParams p = p0;
     p.status = dev->status;
-    p.cta_pairs = dev->cta_pairs ? 1 : 0;
+    p.cta_pairs = dev->cta_pairs;
     GemmEvent *ev = nullptr;
     if (dev->profiling) {
         if (dev->n_events == dev->events.size()) {

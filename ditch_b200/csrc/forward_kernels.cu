@@ -224,14 +224,63 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attention(AttnParams p) {
     }
 }
 
+// ---- q/k norm and RoPE, once per (token, head) ---------------------------
+// Warp per (token, head slot) with the head's values in registers: lane l
+// holds elements l, l + 32, ... (the order rms_inplace and rope_neox_inplace
+// use), so the arithmetic is theirs. Applied in place to the q and k columns
+// of the QKV rows before the tiled attention reads them.
+template <int HD>
+__global__ void __launch_bounds__(256) k_qk_prep(float *qkv, AttnParams p) {
+    constexpr int V = HD / 32, H2 = V / 2;  // values per lane; pair (k, k + H2) = (i, i + HD / 2)
+    const int b = blockIdx.x;
+    const int start = p.seq_start[b], len = p.seq_len[b];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos = blockIdx.y * 8 + warp;
+    if (pos >= len) return;
+    const int nh = p.heads, nkv = p.kv_heads;
+    const int width = (nh + 2 * nkv) * HD;
+    float *row = qkv + (long long)(start + pos) * width;
+    const float *c = p.rope_cos + (long long)pos * (HD / 2);
+    const float *sn = p.rope_sin + (long long)pos * (HD / 2);
+    float cs[H2], ss[H2];
+#pragma unroll
+    for (int k = 0; k < H2; k++) {
+        cs[k] = __ldg(c + lane + 32 * k);
+        ss[k] = __ldg(sn + lane + 32 * k);
+    }
+    for (int slot = 0; slot < nh + nkv; slot++) {  // q heads, then k heads
+        float *v = row + slot * HD;
+        const float *nw = slot < nh ? p.q_norm : p.k_norm;
+        float x[V];
+#pragma unroll
+        for (int k = 0; k < V; k++) x[k] = v[lane + 32 * k];
+        if (nw) {
+            float sq = 0.0f;
+#pragma unroll
+            for (int k = 0; k < V; k++) sq += x[k] * x[k];
+            sq = warp_sum(sq);
+            const float inv = 1.0f / sqrtf(sq / (float)HD + p.eps);
+#pragma unroll
+            for (int k = 0; k < V; k++) x[k] = x[k] * inv * __ldg(nw + lane + 32 * k);
+        }
+#pragma unroll
+        for (int k = 0; k < H2; k++) {
+            const float x1 = x[k], x2 = x[k + H2];
+            x[k] = x1 * cs[k] - x2 * ss[k];
+            x[k + H2] = x2 * cs[k] + x1 * ss[k];
+        }
+#pragma unroll
+        for (int k = 0; k < V; k++) v[lane + 32 * k] = x[k];
+    }
+}
+
 // ---- tensor-core attention for head_dim 64 / 128 -------------------------
 // Block = (prompt, kv head and part of its group, chunk of 64 query
 // positions); 4 warps, warp w owns query rows 16w .. 16w + 15 of the chunk.
 // Up to kMaxHeads query heads of the group run one after another, so a prompt
 // whose keys fit one 64-key chunk stages K and V once for them. Q, K and V
-// are staged in shared memory (Q and K normed and roped on the way in, see
-// prep_qk4) as bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi));
-// every product is
+// (already normed and roped by k_qk_prep) are staged in shared memory as
+// bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi)); every product is
 // hi*hi + hi*lo + lo*hi on mma.sync m16n8k16 with f32 accumulation, which
 // keeps the scores and the P.V sums to about 2^-16 relative (f32-like). The
 // scores never leave registers: the S accumulator fragments are the A
@@ -254,39 +303,6 @@ __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uin
     hi = pack_bf16x2(a, b);
     const float ah = __uint_as_float(hi << 16), bh = __uint_as_float(hi & 0xffff0000u);
     lo = pack_bf16x2(a - ah, b - bh);
-}
-
-// q / k RMSNorm (optional) and neox RoPE of one 4-element piece while it is
-// staged: the HD / 4 lanes of a row (a warp for HD 128, a half-warp for 64)
-// hold its consecutive float4 pieces, so the norm is a shuffle reduction over
-// them and element d's RoPE partner d +- HD/2 sits HD/8 lanes away. Every lane
-// of the warp takes part (rows past the prompt carry zeros).
-template <int HD>
-__device__ __forceinline__ float4 prep_qk4(float4 x, int pos, int c4, const float *nw, bool valid, const AttnParams &p) {
-    constexpr int C4 = HD / 4, HALF = HD / 2;
-    if (nw) {
-        float sq = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
-#pragma unroll
-        for (int off = C4 / 2; off >= 1; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-        const float inv = 1.0f / sqrtf(sq / (float)HD + p.eps);
-        const float4 g = *reinterpret_cast<const float4 *>(nw + 4 * c4);
-        x = make_float4(x.x * inv * g.x, x.y * inv * g.y, x.z * inv * g.z, x.w * inv * g.w);
-    }
-    float4 y;
-    y.x = __shfl_xor_sync(0xffffffffu, x.x, C4 / 2);
-    y.y = __shfl_xor_sync(0xffffffffu, x.y, C4 / 2);
-    y.z = __shfl_xor_sync(0xffffffffu, x.z, C4 / 2);
-    y.w = __shfl_xor_sync(0xffffffffu, x.w, C4 / 2);
-    const int d0 = 4 * c4;
-    const bool first = d0 < HALF;
-    float4 c = make_float4(0.0f, 0.0f, 0.0f, 0.0f), s = c;
-    if (valid) {
-        const long long t = (long long)pos * HALF + (first ? d0 : d0 - HALF);
-        c = __ldg(reinterpret_cast<const float4 *>(p.rope_cos + t));
-        s = __ldg(reinterpret_cast<const float4 *>(p.rope_sin + t));
-    }
-    if (first) return make_float4(x.x * c.x - y.x * s.x, x.y * c.y - y.y * s.y, x.z * c.z - y.z * s.z, x.w * c.w - y.w * s.w);
-    return make_float4(x.x * c.x + y.x * s.x, x.y * c.y + y.y * s.y, x.z * c.z + y.z * s.z, x.w * c.w + y.w * s.w);
 }
 
 template <int HD>
@@ -322,7 +338,6 @@ __global__ void __launch_bounds__(128) k_attention_mma(AttnParams p) {
             const int r = idx / C4, c4 = idx % C4, i = i0 + r;
             float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             if (i < len) q = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + i) * width + h * HD + 4 * c4);
-            q = prep_qk4<HD>(q, i, c4, p.q_norm, i < len, p);
             uint2 hi, lo;
             split_bf16x2(q.x, q.y, hi.x, lo.x);
             split_bf16x2(q.z, q.w, hi.y, lo.y);
@@ -343,7 +358,6 @@ __global__ void __launch_bounds__(128) k_attention_mma(AttnParams p) {
                     if (j < len)
                         k = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd + kvh * HD +
                                                               4 * c4);
-                    k = prep_qk4<HD>(k, j, c4, p.k_norm, j < len, p);
                     uint2 hi, lo;
                     split_bf16x2(k.x, k.y, hi.x, lo.x);
                     split_bf16x2(k.z, k.w, hi.y, lo.y);
@@ -494,8 +508,11 @@ cudaError_t launch_attention_tiled(const AttnParams &p, cudaStream_t st) {
         configured = true;
     }
     int max_len = p.max_len > 0 ? p.max_len : kQB;
-    // q / k norms and RoPE are applied while Q and K are staged (prep_qk4);
-    // the QKV rows stay as the GEMM wrote them
+    // q / k norm and RoPE in place on the workspace rows (the buffer is the
+    // forward's own QKV output, read only by this attention)
+    k_qk_prep<HD><<<dim3(p.n_prompts, (max_len + 7) / 8), 256, 0, st>>>(const_cast<float *>(p.qkv), p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
     const int groups = p.heads / p.kv_heads, parts = (groups + kMaxHeads - 1) / kMaxHeads;
     dim3 grid(p.n_prompts, p.kv_heads * parts, (max_len + kQB - 1) / kQB);
     k_attention_mma<HD><<<grid, 128, smem, st>>>(p);
@@ -573,6 +590,10 @@ cudaError_t rmsnorm_rows_f32(const float *x, const float *w, int n, int len, flo
 cudaError_t gather_rmsnorm_bf16(const float *x, const int *rows, int n, int hidden, float eps, const float *w,
                                 uint16_t *h, cudaStream_t st, int split_k) {
     return rmsnorm_rows_bf16(x, w, n, hidden, eps, h, nullptr, nullptr, rows, st, split_k);
+}
+
+bool attention_prefill_preps_in_place(int head_dim, int force_generic) {
+    return !force_generic && (head_dim == 128 || head_dim == 64);
 }
 
 cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st) {

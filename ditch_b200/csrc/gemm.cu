@@ -1267,7 +1267,7 @@ cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, co
                         int num_sms, cudaStream_t stream) {
     const bool dual = (p.flags & kEpiSwiglu) != 0;
     if (dual && !a2) return cudaErrorInvalidValue;
-    if (p.cta_pairs && !p.bn && gemm_pair_fits(p, fmt, p.k, num_sms)) return launch_gemm_pair(a, a2, b, p, num_sms, stream);
+    if (!p.bn && gemm_pair_fits(p, fmt, p.k, num_sms)) return launch_gemm_pair(a, a2, b, p, num_sms, stream);
     const int bn = p.bn ? p.bn : gemm_token_tile(p.n_tok, dual, fmt != kFmtBf16);
     if (dual) {
         if (bn == 32) return dispatch_fmt<32, true>(fmt, a, a2, b, p, num_sms, stream);

@@ -83,7 +83,8 @@ struct GemmParams {
     int *sk_cnt;   // [tiles] arrival counters, zero between launches
     // Dense bf16 products over many tokens may run on CTA pairs
     // (cta_group::2, gemm2.cu): 256-row output tiles, each CTA of the pair
-    // loading half the weight rows and half the token rows.
+    // loading half the weight rows and half the token rows. 0 never, 1
+    // single-accumulator products, 2 SwiGLU products too.
     int cta_pairs;
 };
 

@@ -424,17 +424,22 @@ cudaError_t launch_pair_t(const GemmOperand &a, const GemmOperand *a2, const Gem
 
 bool gemm_pair_fits(const GemmParams &p, int fmt, int k, int num_sms) {
     // dense bf16 products over at least one full pair tile of weights and
-    // enough token tiles to fill the pairs; no K splits, stream-K or atomics
-    return fmt == kFmtBf16 && !p.sched && p.k_splits <= 1 && !p.stream_k && !(p.flags & kEpiAtomic) &&
-           p.m_w >= 2 * PBM && p.n_tok >= 512 && k >= 4 * PBK && num_sms >= 2;
+    // enough token tiles to fill the pairs; no K splits, stream-K or atomics;
+    // SwiGLU pairs only at level 2
+    const bool dual = (p.flags & kEpiSwiglu) != 0;
+    return p.cta_pairs >= (dual ? 2 : 1) && fmt == kFmtBf16 && !p.sched && p.k_splits <= 1 && !p.stream_k &&
+           !(p.flags & kEpiAtomic) && p.m_w >= 2 * PBM && p.n_tok >= 512 && k >= 4 * PBK && num_sms >= 2;
 }
 
 cudaError_t launch_gemm_pair(const GemmOperand &a, const GemmOperand *a2, const GemmOperand &b, GemmParams p,
                              int num_sms, cudaStream_t stream) {
     const bool dual = (p.flags & kEpiSwiglu) != 0;
     if (dual) {
+        // gate and up accumulators of 256 tokens fill TMEM (one buffer): the
+        // epilogue does not overlap the next tile, but each SM moves 48 KB
+        // per 2 x 128 x 256 x 64 products
         if (!a2) return cudaErrorInvalidValue;
-        return launch_pair_t<128, true>(a, a2, b, p, num_sms, stream);
+        return launch_pair_t<256, true>(a, a2, b, p, num_sms, stream);
     }
     return launch_pair_t<256, false>(a, a2, b, p, num_sms, stream);
 }

@@ -105,6 +105,9 @@ struct AttnParams {
 // Causal attention within each prompt with GQA, RoPE (neox) and optional q/k
 // norms (src/model.zig:4226-4374, attentionWorker 2935-2986).
 cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st);
+// True when attention_prefill leaves the q and k columns of the QKV rows
+// normed and roped in place (the tensor-core path, head sizes 64 and 128).
+bool attention_prefill_preps_in_place(int head_dim, int force_generic);
 
 // ---- greedy decode with a KV cache (src/model.zig:5378-5444) ---------------
 // One layer's cache: keys (normed and roped) and values, f32
@@ -119,7 +122,7 @@ struct KvParams {
     const float *q_norm, *k_norm;
     float eps;
     float *cache_k, *cache_v;
-    int prep_k;  // 1: norm and rope the keys while storing them (0: they are stored as given)
+    int prep_k;  // 1: norm and rope the keys while storing them (0: the attention already did, in place)
     int prep_q;  // 1: norm and rope the queries in place (decode rows)
     int *status;
 };

@@ -535,7 +535,7 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
                 DITCH_LAUNCH(dev, attention_decode(dp, st));
             } else {
                 DITCH_LAUNCH(dev, attention_prefill(ap, st));
-                kp.prep_k = 1;  // the prefill attention leaves the QKV rows as the GEMM wrote them
+                kp.prep_k = attention_prefill_preps_in_place(c.head_dim, 0) ? 0 : 1;
                 DITCH_LAUNCH(dev, kv_store(kp, st));
             }
         }

@@ -348,9 +348,10 @@ class Device:
         decode the weight once to bf16 scratch; 0 keeps every decode in the GEMM."""
         check(lib().ditch_cuda_set_decode_staging(self.h, int(min_tokens)))
 
-    def set_cta_pairs(self, on):
-        """Wide dense bf16 GEMMs on CTA pairs (cta_group::2)."""
-        check(lib().ditch_cuda_set_cta_pairs(self.h, int(bool(on))))
+    def set_cta_pairs(self, level):
+        """Wide dense bf16 GEMMs on CTA pairs (cta_group::2): 0 never, 1
+        single-accumulator products, 2 the SwiGLU products too."""
+        check(lib().ditch_cuda_set_cta_pairs(self.h, int(level)))
 
     def set_f32_split(self, on):
         """Models loaded afterwards run f32-level split-bf16 products for their

@@ -409,10 +409,12 @@ int ditch_cuda_set_deterministic(ditch_cuda_device *dev, int enabled);
  * of a prefill-sized forward, staged FP8 / MXFP4 / INT4 weights included) run
  * on CTA pairs: two SMs share each 256 x 256 output tile (tcgen05 with
  * cta_group::2), each loading half the weight rows and half the tokens, which
- * cuts the operand traffic per SM by a third. The same products either way
- * (f32 accumulation of the same bf16 operands). No counterpart in the
- * reference (a tuning knob of this backend). */
-int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int enabled);
+ * cuts the operand traffic per SM by a third. Level 0: never; 1: products
+ * with one accumulator (qkv, o_proj, down_proj, LM head); 2: the SwiGLU
+ * gate / up products too (256-token tiles, their two accumulators filling
+ * TMEM). The same products either way (f32 accumulation of the same bf16
+ * operands). No counterpart in the reference (a tuning knob of this backend). */
+int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int level);
 /* f32-level products for f32 and f16 weights. By default a resident model
  * rounds f32 / f16 weights to bf16 at load and rounds every GEMM input to
  * bf16 (tensor-core products with f32 accumulation), about 2^-9 relative per

@@ -25,7 +25,7 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture
 def pairs(device):
     yield device
-    device.set_cta_pairs(False)
+    device.set_cta_pairs(0)
 
 
 @pytest.mark.parametrize("rows,cols,m", [(256, 256, 512), (4096 + 128, 1024 + 64, 1000), (6144, 4096, 2048),
@@ -37,8 +37,8 @@ def test_pair_gemm_matches_one_cta(pairs, rows, cols, m):
     x = torch.randn(m, cols, generator=g, device="cuda").to(torch.bfloat16)
     W = ditch_b200.Weight(pairs, ditch_b200.Tensor("w", "bf16", rows, cols, w))
     outs = []
-    for on in (False, True):
-        pairs.set_cta_pairs(on)
+    for level in (0, 1):
+        pairs.set_cta_pairs(level)
         out = torch.full((m, rows), float("nan"), device="cuda")
         torch.cuda.synchronize()
         W.gemm(x.data_ptr(), m, out.data_ptr())
@@ -61,8 +61,8 @@ def test_pair_forward_matches_one_cta_and_oracle(pairs):
     dirs = rng.standard_normal((spec["n_layers"] + 1, spec["hidden"])).astype(np.float32)
     dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
     got = []
-    for on in (False, True):
-        pairs.set_cta_pairs(on)
+    for level in (0, 2):  # one CTA per tile; every dense product on pairs, SwiGLU included
+        pairs.set_cta_pairs(level)
         m = ditch_b200.Model(pairs, spec, tensors, max_seq=128)
         m.set_directions(dirs)
         m.apply_edit((1.2, 1.0, 0.5, 2.0), (0.9, 0.0, 0.3, 2.0))  # rank-1 deltas in the o / down epilogues
