@@ -288,6 +288,7 @@ __global__ void __launch_bounds__(256) k_qk_prep(float *qkv, AttnParams p) {
 // causal limit skips the 8-key tiles and 16-key steps above each warp's rows.
 constexpr int kQB = 64, kKB = 64;
 constexpr int kMaxHeads = 4;  // query heads per block
+constexpr int kBatch = 4;     // staging loads in flight per thread
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
@@ -334,15 +335,26 @@ __global__ void __launch_bounds__(128) k_attention_mma(AttnParams p) {
     for (int gh = gh0; gh < gh1; gh++) {
         const int h = kvh * groups + gh;
         __syncthreads();  // the previous head's reads of the buffers are done
-        for (int idx = tid; idx < kQB * C4; idx += 128) {
-            const int r = idx / C4, c4 = idx % C4, i = i0 + r;
-            float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (i < len) q = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + i) * width + h * HD + 4 * c4);
-            uint2 hi, lo;
-            split_bf16x2(q.x, q.y, hi.x, lo.x);
-            split_bf16x2(q.z, q.w, hi.y, lo.y);
-            *reinterpret_cast<uint2 *>(qh + r * QS + 4 * c4) = hi;
-            *reinterpret_cast<uint2 *>(ql + r * QS + 4 * c4) = lo;
+        // staging: kBatch loads in flight per thread before their conversions
+        // (a load per conversion waits one memory round trip each)
+#pragma unroll
+        for (int b0 = 0; b0 < kQB * C4 / 128; b0 += kBatch) {
+            float4 q[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; u++) {
+                const int idx = tid + 128 * (b0 + u), r = idx / C4, c4 = idx % C4, i = i0 + r;
+                q[u] = i < len ? *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + i) * width + h * HD + 4 * c4)
+                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < kBatch; u++) {
+                const int idx = tid + 128 * (b0 + u), r = idx / C4, c4 = idx % C4;
+                uint2 hi, lo;
+                split_bf16x2(q[u].x, q[u].y, hi.x, lo.x);
+                split_bf16x2(q[u].z, q[u].w, hi.y, lo.y);
+                *reinterpret_cast<uint2 *>(qh + r * QS + 4 * c4) = hi;
+                *reinterpret_cast<uint2 *>(ql + r * QS + 4 * c4) = lo;
+            }
         }
         float o[HD / 8][4];
 #pragma unroll
@@ -352,30 +364,46 @@ __global__ void __launch_bounds__(128) k_attention_mma(AttnParams p) {
         for (int k0 = 0; k0 <= last_q; k0 += kKB) {
             if (!one_chunk || gh == gh0) {
                 if (k0 > 0) __syncthreads();  // the previous chunk's reads of the K / V tiles are done
-                for (int idx = tid; idx < kKB * C4; idx += 128) {
-                    const int r = idx / C4, c4 = idx % C4, j = k0 + r;
-                    float4 k = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (j < len)
-                        k = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd + kvh * HD +
-                                                              4 * c4);
-                    uint2 hi, lo;
-                    split_bf16x2(k.x, k.y, hi.x, lo.x);
-                    split_bf16x2(k.z, k.w, hi.y, lo.y);
-                    *reinterpret_cast<uint2 *>(kh + r * QS + 4 * c4) = hi;
-                    *reinterpret_cast<uint2 *>(kl + r * QS + 4 * c4) = lo;
-                }
-                for (int idx = tid; idx < kKB * C4; idx += 128) {  // keys across lanes: conflict-free transposed stores
-                    const int r = idx % kKB, c4 = idx / kKB, j = k0 + r;
-                    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (j < len)
-                        v = *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd + kvd +
-                                                              kvh * HD + 4 * c4);
-                    const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const uint16_t hb = f32_to_bf16_bits(vv[e]);
-                        vh[(4 * c4 + e) * VS + r] = hb;
-                        vl[(4 * c4 + e) * VS + r] = f32_to_bf16_bits(vv[e] - bf16_bits_to_f32(hb));
+                for (int b0 = 0; b0 < kKB * C4 / 128; b0 += kBatch) {
+                    float4 k[kBatch];
+#pragma unroll
+                    for (int u = 0; u < kBatch; u++) {
+                        const int idx = tid + 128 * (b0 + u), r = idx / C4, c4 = idx % C4, j = k0 + r;
+                        k[u] = j < len ? *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd +
+                                                                           kvh * HD + 4 * c4)
+                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    }
+#pragma unroll
+                    for (int u = 0; u < kBatch; u++) {
+                        const int idx = tid + 128 * (b0 + u), r = idx / C4, c4 = idx % C4;
+                        uint2 hi, lo;
+                        split_bf16x2(k[u].x, k[u].y, hi.x, lo.x);
+                        split_bf16x2(k[u].z, k[u].w, hi.y, lo.y);
+                        *reinterpret_cast<uint2 *>(kh + r * QS + 4 * c4) = hi;
+                        *reinterpret_cast<uint2 *>(kl + r * QS + 4 * c4) = lo;
+                    }
+                }
+#pragma unroll
+                for (int b0 = 0; b0 < kKB * C4 / 128; b0 += kBatch) {  // keys across lanes: conflict-free transposed stores
+                    float4 v[kBatch];
+#pragma unroll
+                    for (int u = 0; u < kBatch; u++) {
+                        const int idx = tid + 128 * (b0 + u), r = idx % kKB, c4 = idx / kKB, j = k0 + r;
+                        v[u] = j < len ? *reinterpret_cast<const float4 *>(p.qkv + (long long)(start + j) * width + qd +
+                                                                           kvd + kvh * HD + 4 * c4)
+                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    }
+#pragma unroll
+                    for (int u = 0; u < kBatch; u++) {
+                        const int idx = tid + 128 * (b0 + u), r = idx % kKB, c4 = idx / kKB;
+                        const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const uint16_t hb = f32_to_bf16_bits(vv[e]);
+                            vh[(4 * c4 + e) * VS + r] = hb;
+                            vl[(4 * c4 + e) * VS + r] = f32_to_bf16_bits(vv[e] - bf16_bits_to_f32(hb));
+                        }
                     }
                 }
             }

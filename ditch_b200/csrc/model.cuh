@@ -218,6 +218,13 @@ struct GemmExtra {
     int bn = 0;
 };
 
+// A routed-expert stack in a quantised format (MXFP4, FP8, INT4) decoded once
+// to bf16 and kept (while the decode cache is on, staging is not off and
+// more than 4 GiB stays free): grouped products then run the bf16 GEMM over
+// the copy, as ditch holds its experts (decoded at load, src/dequant.zig).
+// Returns whether the copy exists (decoding it on first use).
+bool expert_stack_cached(ditch_cuda_device *dev, const Mat &w);
+
 int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
              void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
              int a2_row_offset, const GemmExtra *ex, int delta_rank = 1);

@@ -259,6 +259,24 @@ int gemm_weight(ditch_cuda_model *m, const Mat &w, int slab_row0, int m_rows, co
                     delta_rank);
 }
 
+bool expert_stack_cached(ditch_cuda_device *dev, const Mat &w) {
+    if (w.fmt == kFmtBf16 || !dev->decode_cache || dev->stage_min_tokens <= 0) return false;
+    const int rows = w.rows * w.slabs;
+    if (w.decoded.ptr) return w.decoded_row0 == 0 && w.decoded_rows == rows;
+    const size_t bytes = (size_t)rows * w.cols * 2;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess || free_b <= bytes + (4ull << 30)) return false;
+    if (w.decoded.reserve(bytes) != cudaSuccess) return false;
+    if (decode_rows_bf16(dev, w, 0, rows, w.decoded.as<uint16_t>()) != cudaSuccess) {
+        w.decoded.release();
+        return false;
+    }
+    dev->launches.fetch_add(1, std::memory_order_relaxed);
+    w.decoded_row0 = 0;
+    w.decoded_rows = rows;
+    return true;
+}
+
 int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, const uint16_t *act, int n_tok,
              void *out, long long ldo, int flags, const float *bias, const float *xa, const float *db,
              int a2_row_offset, const GemmExtra *ex, int delta_rank) {
@@ -286,7 +304,14 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
     const int st_rows = (dual ? a2_row_offset : 0) + m_rows;
     const bool cached = fmt != kFmtBf16 && !(ex && ex->sched) && w.decoded.ptr && w.decoded_row0 == slab_row0 &&
                         w.decoded_rows == st_rows;
-    if (cached && n_tok > 16 && n_tok < dev->stage_min_tokens) {
+    const bool stack_cached = fmt != kFmtBf16 && ex && ex->sched && w.decoded.ptr && w.decoded_row0 == 0 &&
+                              w.decoded_rows == w.rows * w.slabs;
+    if (stack_cached) {
+        // the grouped (routed-expert) product over the kept bf16 copy of the
+        // whole expert stack (expert_stack_cached): the same slab rows
+        A = GemmOperand{w.decoded.ptr, w.rows * w.slabs, w.cols, (long long)w.cols * 2};
+        fmt = kFmtBf16;
+    } else if (cached && n_tok > 16 && n_tok < dev->stage_min_tokens) {
         A = GemmOperand{w.decoded.ptr, st_rows, w.cols, (long long)w.cols * 2};
         fmt = kFmtBf16;
         slab_row0 = 0;

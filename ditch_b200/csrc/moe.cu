@@ -529,8 +529,11 @@ int moe_mlp(ditch_cuda_model *m, Layer &L, int li, int n) {
     const int mip = L.e_down.cols;  // stored (8-aligned) expert width: the act row stride
     const int cp = (H + 63) / 64 * 64;
     const int avg = (nk + E - 1) / E;
-    const int bn_gu = tile_for(avg, true, L.e_gate_up.fmt != kFmtBf16);
-    const int bn_d = tile_for(avg, false, L.e_down.fmt != kFmtBf16);
+    // quantised expert stacks with a kept bf16 copy run the bf16 grouped GEMM
+    const bool gu_q = L.e_gate_up.fmt != kFmtBf16 && !expert_stack_cached(dev, L.e_gate_up);
+    const bool d_q = L.e_down.fmt != kFmtBf16 && !expert_stack_cached(dev, L.e_down);
+    const int bn_gu = tile_for(avg, true, gu_q);
+    const int bn_d = tile_for(avg, false, d_q);
     const int wt_gu = (mi + 127) / 128, wt_d = (H + 127) / 128;
     const int max_gu = (nk / bn_gu + E) * wt_gu, max_d = (nk / bn_d + E) * wt_d;
     DITCH_CUDA(m->moe_h3.reserve((size_t)n * 3 * cp * 2));
@@ -649,8 +652,11 @@ int moe_mlp_ep(ditch_cuda_model *m, Layer &L, int n) {
     const int mip = L.e_down.cols;
     const int cp = (H + 63) / 64 * 64;
     const int avg = (int)(((long long)W * nk + E - 1) / E);  // rows per expert with balanced routing
-    const int bn_gu = tile_for(avg, true, L.e_gate_up.fmt != kFmtBf16);
-    const int bn_d = tile_for(avg, false, L.e_down.fmt != kFmtBf16);
+    // quantised expert stacks with a kept bf16 copy run the bf16 grouped GEMM
+    const bool gu_q = L.e_gate_up.fmt != kFmtBf16 && !expert_stack_cached(dev, L.e_gate_up);
+    const bool d_q = L.e_down.fmt != kFmtBf16 && !expert_stack_cached(dev, L.e_down);
+    const int bn_gu = tile_for(avg, true, gu_q);
+    const int bn_d = tile_for(avg, false, d_q);
     const int wt_gu = (mi + 127) / 128, wt_d = (H + 127) / 128;
     const int src_gu = (nk / bn_gu + E) * wt_gu, src_d = (nk / bn_d + E) * wt_d;
     const int max_gu = (cap / bn_gu + El) * wt_gu, max_d = (cap / bn_d + El) * wt_d;

@@ -54,12 +54,42 @@ def test_synthetic_dense_forward(device, case):
     check_forward(device, spec, f32, tensors, ps)
 
 
-@pytest.mark.parametrize("fmt", ["bf16", "mxfp4"])
-def test_synthetic_moe_forward(device, fmt):
+@pytest.mark.parametrize("fmt,staging", [("bf16", 1024), ("mxfp4", 1024), ("mxfp4", 0)])
+def test_synthetic_moe_forward(device, fmt, staging):
+    """MXFP4 experts with the default plan (each expert stack decoded once to
+    bf16 and kept, the grouped GEMM over the copy) and with staging off (the
+    grouped GEMM decoding MXFP4 tile by tile)."""
     spec, f32, tensors = make_model(300, hidden=256, head_dim=64, heads=4, kv_heads=2, fmt=fmt,
                                     moe=dict(experts=16, top_k=4, inter=128))
     ps = prompts(31, [40, 17, 64, 3, 70], spec["vocab"])
-    check_forward(device, spec, f32, tensors, ps, max_bad_rows=0.2)
+    device.set_decode_staging(staging)
+    try:
+        check_forward(device, spec, f32, tensors, ps, max_bad_rows=0.2)
+    finally:
+        device.set_decode_staging(1024)
+
+
+def test_moe_expert_copy_equals_in_gemm_decode(device):
+    """The grouped GEMM over the kept bf16 copy of an MXFP4 expert stack and
+    the grouped GEMM decoding tile by tile see the same bf16 operand: the
+    forwards agree bit for bit."""
+    spec, f32, tensors = make_model(301, hidden=256, head_dim=64, heads=4, kv_heads=2, fmt="mxfp4",
+                                    moe=dict(experts=16, top_k=4, inter=128))
+    ps = prompts(32, [40, 17, 64, 3, 70], spec["vocab"])
+    from oracle.model import flatten_batch as fb
+    toks, rb, rp, cap, first, take, last = fb(ps, 2)
+    outs = []
+    device.set_deterministic(True)
+    try:
+        for staging in (1024, 0):
+            device.set_decode_staging(staging)
+            m = ditch_b200.Model(device, spec, tensors, max_seq=128)
+            outs.append(m.forward(toks, rb, rp, cap, last))
+            m.close()
+    finally:
+        device.set_decode_staging(1024)
+        device.set_deterministic(False)
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
 
 
 @pytest.mark.parametrize("case", [2, 3])
