@@ -57,8 +57,9 @@ def parse():
     ap.add_argument("--max-new", type=int, default=100, help="gen: tokens generated per prompt")
     ap.add_argument("--row-normalization", default="none", choices=["none", "pre", "full"],
                     help="c1 / c2: the edit's row normalisation (full: rank-3 delta from the randomised SVD)")
-    ap.add_argument("--cta-pairs", type=int, default=0,
-                    help="1: dense bf16 GEMMs of 512+ tokens on CTA pairs (tcgen05 cta_group::2)")
+    ap.add_argument("--cta-pairs", type=int, default=1,
+                    help="dense bf16 GEMMs of 512+ tokens on CTA pairs (tcgen05 cta_group::2): 0 never, 1 products "
+                         "with one accumulator (the library's default), 2 SwiGLU products too")
     ap.add_argument("--deterministic", type=int, default=0,
                     help="1: K splits summed in a fixed order (stream-K) instead of atomically")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
@@ -342,8 +343,10 @@ def config_block(args):
     return {"workload": "C2: Llama-3-8B-shaped, FP8 E4M3 128x128 block-scaled weights, trial = %s-mode edit of "
                         "o_proj/down_proj + edited forward + first-token KL" % args.row_normalization,
             "row_normalization": args.row_normalization,
-            "gemm": ("CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles) for dense GEMMs of 512+ tokens"
-                     if args.cta_pairs else "one CTA per 128-row tile (tcgen05 cta_group::1)"),
+            "gemm": {0: "one CTA per 128-row tile (tcgen05 cta_group::1)",
+                     1: "CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles) for qkv, o_proj and down_proj; SwiGLU "
+                        "gate / up on one CTA per tile",
+                     2: "CTA pairs for every dense GEMM of 512+ tokens"}[args.cta_pairs],
             "layers": args.layers, "prompts_per_gpu": args.prompts, "seq_len": args.seq, "vocab": C2["vocab"],
             "parallelism": f"dp{args.gpus} (prompt batches; residual sums and KL summed over the ranks by the "
                            "library's peer-group reduction over NVLink)",
