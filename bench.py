@@ -370,14 +370,17 @@ def all_reduce(dist, arr, op="sum"):
 
 
 def traffic_from_profiles():
-    """Per-launch DRAM bytes of the dominant GEMM from the committed ncu summary."""
+    """DRAM bytes (read + write) per GEMM launch of the C2 trial, from the
+    committed ncu summary of one decoder layer's GEMMs (every launch of the
+    layer captured: qkv, o_proj, gate/up, down_proj, each at its own shape);
+    the LM head's single launch per step is left out of the average."""
     import re
 
-    rel = os.path.join("profiles", "gemm_bf16_staged_c2.md")
+    rel = os.path.join("profiles", "gemm_traffic_c2.md")
     p = os.path.join(ROOT, rel)
     if not os.path.exists(p):
         return None, None
-    m = re.search(r"traffic_bytes_per_gflop:\s*([0-9.eE+-]+)", open(p).read())
+    m = re.search(r"traffic_bytes_per_layer_launch:\s*([0-9.eE+-]+)", open(p).read())
     return (float(m.group(1)), rel) if m else (None, None)
 
 
@@ -485,8 +488,7 @@ def main():
     value_e2e = tokens * world * args.steps / (ms_e2e / 1000.0)
     hbm, tf_burst, tf_sust, src = measured_peaks()
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
-    tpg, tsrc = traffic_from_profiles()
-    traffic = tpg * gemm_flops / 1e9 / max(gemm_launches, 1) if tpg else None
+    traffic, tsrc = traffic_from_profiles()
     staged = args.stage_min_tokens != 0 and P * S >= (args.stage_min_tokens or 1024)
     kernel_name = ("gemm_kernel: tcgen05 bf16 MMA over bf16 copies of the FP8 weights (decoded on first use and "
                    "kept; staged plan)" if staged else "gemm_kernel: tcgen05 bf16 MMA, FP8 decoded per tile inside the GEMM")
