@@ -433,6 +433,71 @@ const JVal *path_get(const JVal &v, std::initializer_list<const char *> keys) {
 // families of the device path (llama, mistral, qwen2, qwen3, qwen3_moe,
 // mixtral), with the fp8 / compressed-tensors quantization_config of
 // src/dequant.zig:108-233.
+// parseRopeScaling (src/arch.zig:1646-1720): the rope_scaling dictionary
+// `rs` of config `j` into the device config's RoPE fields. Values are read
+// as f32, as the reference stores them.
+int rope_scaling_config(const JVal &j, const JVal &rs, ditch_cuda_model_config &c, Built &b) {
+    auto f32 = [](double v) { return (double)(float)v; };
+    const std::string ty = rs.string("rope_type", rs.string("type"));
+    const int half = c.head_dim / 2;
+    if (ty == "llama3") {
+        c.rope_scaling = 1;
+        c.rope_factor = f32(rs.number("factor", 8.0));
+        c.rope_low_ff = f32(rs.number("low_freq_factor", 1.0));
+        c.rope_high_ff = f32(rs.number("high_freq_factor", 4.0));
+        c.rope_orig_max = f32(rs.number("original_max_position_embeddings", 8192));
+    } else if (ty == "linear") {
+        c.rope_scaling = 2;
+        c.rope_factor = f32(rs.number("factor", 1.0));
+    } else if (ty == "yarn") {
+        const double factor = f32(rs.number("factor", 1.0));
+        const double mscale = f32(rs.number("mscale", 1.0)), all_dim = f32(rs.number("mscale_all_dim", 0.0));
+        // yarnMscale (src/arch.zig:1722-1725), in f32
+        auto ms = [&](double m) { return factor <= 1 ? 1.0 : f32(f32(0.1 * m * std::log((float)factor)) + 1.0); };
+        const JVal *af = rs.get("attention_factor");
+        c.rope_scaling = 3;
+        c.rope_factor = factor;
+        c.rope_attention_factor = af && af->kind == JVal::Num ? f32(af->num)
+                                  : (mscale != 0 && all_dim != 0) ? f32(ms(mscale) / ms(all_dim))
+                                                                  : ms(1.0);
+        c.rope_orig_max = f32(rs.number("original_max_position_embeddings",
+                                        j.number("original_max_position_embeddings", 4096)));
+        c.rope_beta_fast = f32(rs.number("beta_fast", 32));
+        c.rope_beta_slow = f32(rs.number("beta_slow", 1));
+        c.rope_truncate = rs.number("truncate", 1) != 0;
+    } else if (ty == "longrope") {
+        // the short factors for every position, as the reference does
+        const double max_pos = j.number("max_position_embeddings", 4096);
+        const double orig = f32(j.number("original_max_position_embeddings",
+                                         rs.number("original_max_position_embeddings", max_pos)));
+        b.rope_factors.assign(half, 1.0f);
+        if (const JVal *sf = rs.get("short_factor"))
+            for (size_t i = 0; i < sf->arr.size() && (int)i < half; i++)
+                if (sf->arr[i].kind == JVal::Num) b.rope_factors[i] = (float)sf->arr[i].num;
+        const JVal *fv = rs.get("factor");
+        const double factor = fv && fv->kind == JVal::Num ? f32(fv->num) : f32(max_pos / orig);
+        const JVal *af = rs.get("attention_factor");
+        c.rope_scaling = 4;
+        c.rope_attention_factor = af && af->kind == JVal::Num ? f32(af->num)
+                                  : factor <= 1 ? 1.0
+                                                : f32(std::sqrt(1.0f + std::log((float)factor) / std::log((float)orig)));
+    } else if (ty == "ditch_factors") {
+        // per-frequency divisors written by ditch's GGUF config (src/gguf_model.zig:326-335)
+        b.rope_factors.clear();
+        if (const JVal *fa = rs.get("factors"))
+            for (const JVal &v : fa->arr) b.rope_factors.push_back(v.kind == JVal::Num ? (float)v.num : 1.0f);
+        if (!b.rope_factors.empty()) c.rope_scaling = 4;
+    } else if (ty == "proportional") {
+        // a factor divides the frequencies like linear scaling
+        const double factor = f32(rs.number("factor", 1.0));
+        if (factor != 1) c.rope_scaling = 2, c.rope_factor = factor;
+    }
+    // anything else (dynamic NTK, mrope over text positions, default, types
+    // the reference does not know) is plain RoPE, as the reference reads it
+    (void)j;
+    return DITCH_CUDA_OK;
+}
+
 int hf_config(const JVal &j, Built &b) {
     ditch_cuda_model_config &c = b.cfg;
     const std::string mt = j.string("model_type");
@@ -453,20 +518,16 @@ int hf_config(const JVal &j, Built &b) {
     c.rope_theta = j.number("rope_theta", 10000.0);
     c.qk_norm = mt == "qwen3" || mt == "qwen3_moe";
     b.tied = j.number("tie_word_embeddings", 0) != 0;
-    if (const JVal *rs = j.get("rope_scaling"))
-        if (rs->kind == JVal::Obj) {
-            const std::string ty = rs->string("rope_type", rs->string("type"));
-            if (ty == "llama3") {
-                c.rope_scaling = 1;
-                c.rope_factor = rs->number("factor", 1.0);
-                c.rope_low_ff = rs->number("low_freq_factor", 1.0);
-                c.rope_high_ff = rs->number("high_freq_factor", 1.0);
-                c.rope_orig_max = rs->number("original_max_position_embeddings", 8192);
-            } else if (!ty.empty() && ty != "default") {
-                set_error("rope_scaling type '%s' is not taken by the device path (llama3 is)", ty.c_str());
-                return DITCH_CUDA_UNSUPPORTED;
-            }
-        }
+    const JVal *rs = j.get("rope_scaling");
+    if (!rs || rs->kind != JVal::Obj) {
+        // rope_parameters (newer configs): the full-attention entry when split
+        const JVal *rp = j.get("rope_parameters");
+        rs = rp && rp->kind == JVal::Obj ? (rp->get("full_attention") ? rp->get("full_attention") : rp) : nullptr;
+        if (rs && rs->kind != JVal::Obj) rs = nullptr;
+        if (rs && !j.get("rope_theta")) c.rope_theta = rs->number("rope_theta", c.rope_theta);
+    }
+    if (rs)
+        if (const int st = rope_scaling_config(j, *rs, c, b)) return st;
     if (mt == "qwen3_moe") {
         c.n_experts = (int)j.number("num_experts", 0);
         c.top_k = (int)j.number("num_experts_per_tok", 0);
@@ -534,10 +595,11 @@ int gguf_config(const Checkpoint &ck, Built &b) {
     c.eps = (float)j.number(a + "attention.layer_norm_rms_epsilon", 1e-6);
     c.rope_theta = j.number(a + "rope.freq_base", 10000.0);
     c.qk_norm = b.family == "qwen3" || b.family == "qwen3_moe";
-    const std::string scaling = j.string(a + "rope.scaling.type");
-    if (scaling == "linear") {
-        set_error("GGUF linear rope scaling is not taken by the device path");
-        return DITCH_CUDA_UNSUPPORTED;
+    // rope.scaling.type linear (src/gguf_model.zig:305-309); other types read
+    // as plain RoPE, and rope_freqs.weight is read below when none is set
+    if (j.string(a + "rope.scaling.type") == "linear") {
+        c.rope_scaling = 2;
+        c.rope_factor = (double)(float)j.number(a + "rope.scaling.factor", 1.0);
     }
     const RawTensor *emb = ck.find("token_embd.weight");
     CK_REQUIRE(emb && emb->shape.size() == 2, "GGUF without a 2-D token_embd.weight");
@@ -600,16 +662,17 @@ int build_config(Checkpoint &ck, Built &b) {
             const size_t n = rf->bytes / 4;
             float factor = 1.f;
             for (size_t i = 0; i < n; i++) factor = std::max(factor, f[i]);
-            if (!llama3_factors_match(f, n, (float)c.rope_theta, c.head_dim, factor)) {
-                set_error("GGUF rope frequency factors (rope_freqs.weight) other than Llama 3's standard scaling "
-                          "are not taken");
-                return DITCH_CUDA_UNSUPPORTED;
+            if (llama3_factors_match(f, n, (float)c.rope_theta, c.head_dim, factor)) {
+                c.rope_scaling = 1;
+                c.rope_factor = factor;
+                c.rope_low_ff = 1.0;
+                c.rope_high_ff = 4.0;
+                c.rope_orig_max = 8192.0;
+            } else {
+                // other factors: the divisors themselves (src/gguf_model.zig:227-228, 326-335)
+                b.rope_factors.assign(f, f + n);
+                c.rope_scaling = 4;
             }
-            c.rope_scaling = 1;
-            c.rope_factor = factor;
-            c.rope_low_ff = 1.0;
-            c.rope_high_ff = 4.0;
-            c.rope_orig_max = 8192.0;
         }
     } else if ((s = hf_config(ck.config, b))) {
         return s;
@@ -618,6 +681,8 @@ int build_config(Checkpoint &ck, Built &b) {
                "incomplete model config (layers %d, hidden %d, heads %d / %d, vocab %d)", c.n_layers, c.hidden, c.heads,
                c.kv_heads, c.vocab);
     c.moe_layers = b.moe_layers.empty() ? nullptr : b.moe_layers.data();
+    c.rope_factors = b.rope_factors.empty() ? nullptr : b.rope_factors.data();
+    c.n_rope_factors = b.rope_factors.size();
     return DITCH_CUDA_OK;
 }
 
@@ -979,7 +1044,8 @@ using namespace ditch::ckpt;
 extern "C" {
 
 int ditch_cuda_checkpoint_inspect(const char *path, ditch_cuda_model_config *cfg, size_t *n_tensors,
-                                  uint8_t *moe_layers, size_t moe_layers_len) {
+                                  uint8_t *moe_layers, size_t moe_layers_len, float *rope_factors,
+                                  size_t rope_factors_len) {
     clear_error();
     CK_REQUIRE(path && cfg && n_tensors, "null argument");
     Checkpoint ck;
@@ -988,8 +1054,11 @@ int ditch_cuda_checkpoint_inspect(const char *path, ditch_cuda_model_config *cfg
     if ((s = open_checkpoint(path, ck, b))) return s;
     *cfg = b.cfg;
     cfg->moe_layers = nullptr;
+    cfg->rope_factors = nullptr;
     if (moe_layers)
         for (size_t i = 0; i < moe_layers_len && i < b.moe_layers.size(); i++) moe_layers[i] = b.moe_layers[i];
+    if (rope_factors)
+        for (size_t i = 0; i < rope_factors_len && i < b.rope_factors.size(); i++) rope_factors[i] = b.rope_factors[i];
     *n_tensors = b.tensors.size();
     return DITCH_CUDA_OK;
 }

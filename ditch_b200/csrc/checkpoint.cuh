@@ -94,6 +94,7 @@ size_t dtype_size(const std::string &d);
 struct Built {
     ditch_cuda_model_config cfg{};
     std::vector<uint8_t> moe_layers;
+    std::vector<float> rope_factors;  // per-frequency RoPE divisors (rope_scaling 4)
     std::vector<ditch_cuda_tensor> tensors;
     std::vector<std::unique_ptr<std::string>> names;
     bool tied = false;

@@ -72,12 +72,16 @@ __global__ void k_dequant_fp8(const uint8_t *codes, const float *scales, int row
     }
 }
 
-// ---- streaming decoders: a block per row (grid-stride over rows), a thread
-// per 16-byte chunk of codes, two chunks in flight per thread. The values
-// come from the exact packed conversions (cvt e4m3x2 / e2m1x2 to f16x2), the
-// f32 product with the scale and one round to bf16, as the rules above; the
-// codes the packed path does not follow (E4M3 NaN codes, the E8M0 255 scale)
-// take the element rules.
+// ---- streaming decoders: a block per row (grid-stride over rows); a row is
+// cut into pieces of 8 elements (16 bytes of bf16 out) and thread t of the
+// block takes pieces t, t + 256, t + 512, t + 768 of each run of 1024, so
+// every warp store writes 512 contiguous bytes and every warp load reads 256
+// (FP8: 8 codes) or 128 (MXFP4 / INT4: 4 bytes) contiguous bytes; the four
+// loads of a run are issued before any conversion. The values come from the
+// exact packed conversions (cvt e4m3x2 / e2m1x2 to f16x2), the f32 product
+// with the scale and one round to bf16, as the rules above; the codes the
+// packed path does not follow (E4M3 NaN codes, the E8M0 255 scale) take the
+// element rules.
 
 // true when one of the word's four E4M3 codes is a NaN (0x7f or 0xff)
 __device__ __forceinline__ bool e4m3_nan_in(uint32_t w) {
@@ -85,98 +89,136 @@ __device__ __forceinline__ bool e4m3_nan_in(uint32_t w) {
     return ((t - 0x01010101u) & ~t & 0x80808080u) != 0;
 }
 
-// 16 FP8 codes (one 16-byte chunk) with one block scale to 16 bf16.
-__device__ __forceinline__ void fp8_chunk16(const uint4 q, float s, uint16_t *dst) {
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    uint32_t o[8];
+// four E4M3 codes of one word with one block scale to two bf16x2 words
+__device__ __forceinline__ void fp8_word(uint32_t w, float s, uint32_t &o0, uint32_t &o1) {
+    o0 = scale_pack(e4m3x2_f32(w & 0xffff), s);
+    o1 = scale_pack(e4m3x2_f32(w >> 16), s);
+    if (e4m3_nan_in(w)) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        o[2 * i] = scale_pack(e4m3x2_f32(w[i] & 0xffff), s);
-        o[2 * i + 1] = scale_pack(e4m3x2_f32(w[i] >> 16), s);
-        if (e4m3_nan_in(w[i])) {
-#pragma unroll
-            for (int b = 0; b < 4; b++) {
-                const uint32_t code = (w[i] >> (8 * b)) & 0xff;
-                if ((code & 0x7f) == 0x7f) {
-                    uint32_t &word = o[2 * i + (b >> 1)];
-                    const int sh = 16 * (b & 1);
-                    word = (word & ~(0xffffu << sh)) | ((uint32_t)e4m3_nan_bf16(code) << sh);
-                }
+        for (int b = 0; b < 4; b++) {
+            const uint32_t code = (w >> (8 * b)) & 0xff;
+            if ((code & 0x7f) == 0x7f) {
+                uint32_t &word = (b >> 1) ? o1 : o0;
+                const int sh = 16 * (b & 1);
+                word = (word & ~(0xffffu << sh)) | ((uint32_t)e4m3_nan_bf16(code) << sh);
             }
         }
     }
-    uint4 *d = reinterpret_cast<uint4 *>(dst);
-    d[0] = make_uint4(o[0], o[1], o[2], o[3]);
-    d[1] = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
-// cols a multiple of 16 and block columns a multiple of 16 (one scale per chunk)
-__global__ void __launch_bounds__(256) k_dequant_fp8_rows(const uint8_t *codes, const float *scales, int rows,
-                                                          int cols, int br, int bc, int scols, uint16_t *out) {
-    const int chunks = cols / 16;
-    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
-        const uint8_t *crow = codes + (long long)r * cols;
-        const float *srow = scales + (long long)(r / br) * scols;
-        uint16_t *orow = out + (long long)r * cols;
-        for (int c = threadIdx.x; c < chunks; c += 2 * blockDim.x) {
-            const int c2 = c + blockDim.x;
-            const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(crow) + c);
-            const uint4 q1 = c2 < chunks ? __ldg(reinterpret_cast<const uint4 *>(crow) + c2) : make_uint4(0, 0, 0, 0);
-            fp8_chunk16(q0, __ldg(srow + (c * 16) / bc), orow + c * 16);
-            if (c2 < chunks) fp8_chunk16(q1, __ldg(srow + (c2 * 16) / bc), orow + c2 * 16);
-        }
-    }
-}
+__device__ __forceinline__ uint16_t mxfp4_elem(uint32_t nib, uint32_t b);
 
-// 32 MXFP4 elements (16 bytes, one E8M0 scale b) to 32 bf16.
-__device__ __forceinline__ void mxfp4_chunk32(const uint4 q, uint32_t b, uint16_t *dst);
-
-__global__ void __launch_bounds__(256) k_dequant_mxfp4_rows(const uint8_t *blocks, const uint8_t *scales, int rows,
-                                                            int cols, uint16_t *out) {
-    const int chunks = cols / 32;  // 16 bytes and one scale each
-    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
-        const uint8_t *brow = blocks + (long long)r * (cols / 2);
-        const uint8_t *srow = scales + (long long)r * chunks;
-        uint16_t *orow = out + (long long)r * cols;
-        for (int c = threadIdx.x; c < chunks; c += 2 * blockDim.x) {
-            const int c2 = c + blockDim.x;
-            const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(brow) + c);
-            const uint4 q1 = c2 < chunks ? __ldg(reinterpret_cast<const uint4 *>(brow) + c2) : make_uint4(0, 0, 0, 0);
-            const uint32_t b0 = __ldg(srow + c), b1 = c2 < chunks ? __ldg(srow + c2) : 0u;
-            mxfp4_chunk32(q0, b0, orow + c * 32);
-            if (c2 < chunks) mxfp4_chunk32(q1, b1, orow + c2 * 32);
-        }
-    }
-}
-
-// INT4 pack-quantized without g_idx, groups a multiple of 32: 32 fields (one
-// 16-byte chunk) share a group's scale and zero point;
-// bf16(f32(q - zq) * scale) with q, zq the raw fields (the offset cancels).
-__global__ void __launch_bounds__(256) k_dequant_int4_rows(const uint32_t *packed, long long wpr, const float *scales,
-                                                           const uint32_t *zeros, int groups, int rows, int cols,
-                                                           int group, uint16_t *out) {
-    const int chunks = cols / 32;
-    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
-        const uint4 *prow = reinterpret_cast<const uint4 *>(packed + (long long)r * wpr);
-        const float *srow = scales + (long long)r * groups;
-        uint16_t *orow = out + (long long)r * cols;
-        for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-            const uint4 q = __ldg(prow + c);
-            const int g = (c * 32) / group;
-            const float s = __ldg(srow + g);
-            int zq = 8;
-            if (zeros) zq = (int)((__ldg(zeros + (long long)(r >> 3) * groups + g) >> ((r & 7) * 4)) & 0xf);
-            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-            uint4 *d = reinterpret_cast<uint4 *>(orow + c * 32);
+// eight E2M1 nibbles (one word, low nibble first) with E8M0 scale b
+__device__ __forceinline__ uint4 mxfp4_word(uint32_t w, uint32_t b) {
+    if (b == 255) {  // the +inf scale: the element rule's NaN / inf
+        uint32_t o[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
+        for (int e = 0; e < 4; e++) {
+            const uint32_t byte = (w >> (8 * e)) & 0xff;
+            o[e] = (uint32_t)mxfp4_elem(byte & 0xf, b) | ((uint32_t)mxfp4_elem(byte >> 4, b) << 16);
+        }
+        return make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    const float s = e8m0_scale(b);
+    return make_uint4(scale_pack(e2m1x2_f32(w & 0xff), s), scale_pack(e2m1x2_f32((w >> 8) & 0xff), s),
+                      scale_pack(e2m1x2_f32((w >> 16) & 0xff), s), scale_pack(e2m1x2_f32(w >> 24), s));
+}
+
+constexpr int kPieceSlots = 4;
+
+// FP8 block-scaled; cols and the column block a multiple of 8
+__global__ void __launch_bounds__(kThreads) k_dequant_fp8_rows(const uint8_t *codes, const float *scales, int rows,
+                                                               int cols, int br, int bc, int scols, uint16_t *out) {
+    const int pieces = cols / 8;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const uint2 *crow = reinterpret_cast<const uint2 *>(codes + (long long)r * cols);
+        const float *srow = scales + (long long)(r / br) * scols;
+        uint4 *orow = reinterpret_cast<uint4 *>(out + (long long)r * cols);
+        for (int p0 = threadIdx.x; p0 < pieces; p0 += kPieceSlots * kThreads) {
+            uint2 q[kPieceSlots];
+            float sc[kPieceSlots];
+#pragma unroll
+            for (int k = 0; k < kPieceSlots; k++) {
+                const int p = p0 + k * kThreads;
+                q[k] = p < pieces ? __ldg(crow + p) : make_uint2(0, 0);
+                sc[k] = p < pieces ? __ldg(srow + (p * 8) / bc) : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < kPieceSlots; k++) {
+                const int p = p0 + k * kThreads;
+                if (p >= pieces) break;
+                uint4 o;
+                fp8_word(q[k].x, sc[k], o.x, o.y);
+                fp8_word(q[k].y, sc[k], o.z, o.w);
+                orow[p] = o;
+            }
+        }
+    }
+}
+
+// MXFP4 natural layout; cols a multiple of 32 (a piece lies in one scale block)
+__global__ void __launch_bounds__(kThreads) k_dequant_mxfp4_rows(const uint8_t *blocks, const uint8_t *scales, int rows,
+                                                                 int cols, uint16_t *out) {
+    const int pieces = cols / 8;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const uint32_t *brow = reinterpret_cast<const uint32_t *>(blocks + (long long)r * (cols / 2));
+        const uint8_t *srow = scales + (long long)r * (cols / 32);
+        uint4 *orow = reinterpret_cast<uint4 *>(out + (long long)r * cols);
+        for (int p0 = threadIdx.x; p0 < pieces; p0 += kPieceSlots * kThreads) {
+            uint32_t q[kPieceSlots], b[kPieceSlots];
+#pragma unroll
+            for (int k = 0; k < kPieceSlots; k++) {
+                const int p = p0 + k * kThreads;
+                q[k] = p < pieces ? __ldg(brow + p) : 0u;
+                b[k] = p < pieces ? __ldg(srow + p / 4) : 0u;
+            }
+#pragma unroll
+            for (int k = 0; k < kPieceSlots; k++) {
+                const int p = p0 + k * kThreads;
+                if (p >= pieces) break;
+                orow[p] = mxfp4_word(q[k], b[k]);
+            }
+        }
+    }
+}
+
+// INT4 pack-quantized without g_idx, groups a multiple of 8: the 8 fields of
+// a word share a group's scale and zero point; bf16(f32(q - zq) * scale)
+// with q, zq the raw fields (the offset cancels).
+__global__ void __launch_bounds__(kThreads) k_dequant_int4_rows(const uint32_t *packed, long long wpr,
+                                                                const float *scales, const uint32_t *zeros,
+                                                                int groups, int rows, int cols, int group,
+                                                                uint16_t *out) {
+    const int pieces = cols / 8;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const uint32_t *prow = packed + (long long)r * wpr;
+        const float *srow = scales + (long long)r * groups;
+        const uint32_t *zrow = zeros ? zeros + (long long)(r >> 3) * groups : nullptr;
+        const int zsh = (r & 7) * 4;
+        uint4 *orow = reinterpret_cast<uint4 *>(out + (long long)r * cols);
+        for (int p0 = threadIdx.x; p0 < pieces; p0 += kPieceSlots * kThreads) {
+            uint32_t q[kPieceSlots];
+            float sc[kPieceSlots];
+            int zq[kPieceSlots];
+#pragma unroll
+            for (int k = 0; k < kPieceSlots; k++) {
+                const int p = p0 + k * kThreads;
+                const int g = (p * 8) / group;
+                q[k] = p < pieces ? __ldg(prow + p) : 0u;
+                sc[k] = p < pieces ? __ldg(srow + g) : 0.0f;
+                zq[k] = (zrow && p < pieces) ? (int)((__ldg(zrow + g) >> zsh) & 0xf) : 8;
+            }
+#pragma unroll
+            for (int k = 0; k < kPieceSlots; k++) {
+                const int p = p0 + k * kThreads;
+                if (p >= pieces) break;
                 uint32_t o[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const int lo = (int)((w[i] >> (8 * e)) & 0xf) - zq, hi = (int)((w[i] >> (8 * e + 4)) & 0xf) - zq;
-                    o[e] = scale_pack(make_float2((float)lo, (float)hi), s);
+                    const int lo = (int)((q[k] >> (8 * e)) & 0xf) - zq[k], hi = (int)((q[k] >> (8 * e + 4)) & 0xf) - zq[k];
+                    o[e] = scale_pack(make_float2((float)lo, (float)hi), sc[k]);
                 }
-                d[i] = make_uint4(o[0], o[1], o[2], o[3]);
+                orow[p] = make_uint4(o[0], o[1], o[2], o[3]);
             }
         }
     }
@@ -229,29 +271,6 @@ __device__ __forceinline__ uint16_t mxfp4_elem(uint32_t nib, uint32_t b) {
     }
     const float s = __uint_as_float(b == 0 ? 0x00400000u : (b << 23));
     return f32_to_bf16_bits(kE2M1v[nib] * s);
-}
-
-__device__ __forceinline__ void mxfp4_chunk32(const uint4 q, uint32_t b, uint16_t *dst) {
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    uint4 *d = reinterpret_cast<uint4 *>(dst);
-    if (b == 255) {  // the +inf scale: the element rule's NaN / inf
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const uint32_t byte = (w[i] >> (8 * e)) & 0xff;
-                o[e] = (uint32_t)mxfp4_elem(byte & 0xf, b) | ((uint32_t)mxfp4_elem(byte >> 4, b) << 16);
-            }
-            d[i] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        return;
-    }
-    const float s = e8m0_scale(b);
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-        d[i] = make_uint4(scale_pack(e2m1x2_f32(w[i] & 0xff), s), scale_pack(e2m1x2_f32((w[i] >> 8) & 0xff), s),
-                          scale_pack(e2m1x2_f32((w[i] >> 16) & 0xff), s), scale_pack(e2m1x2_f32(w[i] >> 24), s));
 }
 
 __global__ void k_dequant_mxfp4(const uint8_t *blocks, const uint8_t *scales, int rows, int cols, uint16_t *out) {
@@ -508,7 +527,7 @@ cudaError_t dequant_fp8_bf16(const uint8_t *codes, const float *scales, int rows
     if (br <= 0 || bc <= 0) return cudaErrorInvalidValue;
     const int scols = (cols + bc - 1) / bc;
     const long long n = (long long)rows * cols;
-    if (cols % 16 == 0 && bc % 16 == 0 && aligned16(codes) && aligned16(out)) {
+    if (cols % 8 == 0 && bc % 8 == 0 && aligned16(codes) && aligned16(out)) {
         k_dequant_fp8_rows<<<row_grid(rows), kThreads, 0, st>>>(codes, scales, rows, cols, br, bc, scols, out);
         return cudaGetLastError();
     }
@@ -521,7 +540,7 @@ cudaError_t dequant_int_bf16(const uint32_t *packed, long long wpr, const float 
                              const uint32_t *g_idx, int groups, int rows, int cols, int bits, int group,
                              uint16_t *out, cudaStream_t st) {
     if (bits < 1 || bits > 8 || (!g_idx && group <= 0)) return cudaErrorInvalidValue;
-    if (bits == 4 && !g_idx && group % 32 == 0 && cols % 32 == 0 && wpr == cols / 8 && aligned16(packed) &&
+    if (bits == 4 && !g_idx && group % 8 == 0 && cols % 8 == 0 && wpr == cols / 8 && aligned16(packed) &&
         aligned16(out)) {
         k_dequant_int4_rows<<<row_grid(rows), kThreads, 0, st>>>(packed, wpr, scales, zeros, groups, rows, cols, group,
                                                                  out);

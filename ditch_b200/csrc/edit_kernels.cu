@@ -70,57 +70,20 @@ inline int row_splits(int rows, int col_blocks, int min_rows = 64) {
     return s > max_s ? (max_s < 1 ? 1 : max_s) : s;
 }
 
-// out[c] += sum_{r in split} v[r] W[r][c]; thread = 8 consecutive bf16 columns.
-// (The reference skips rows with v[r] == 0, src/tensor.zig:1065-1068; for
-// finite weights those rows add exactly zero, so the stream reads every row
-// without a data-dependent branch and keeps four loads in flight.)
-// `vec`: every row starts on a 16-byte boundary (w 16-byte aligned and cols a
-// multiple of 8), so a thread reads its 8 columns as one 16-byte load;
-// otherwise 2-byte loads.
-__global__ void k_gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, int rows_per,
-                              bool vec) {
+// out[c] += sum_{r in split} v[r] W[r][c]; thread = 8 consecutive bf16
+// columns, 2-byte loads: the form for rows that are not 16-byte aligned (the
+// piece kernel below takes the rest). Rows with v[r] == 0 are skipped, as
+// src/tensor.zig:1065-1068.
+__global__ void k_gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, int rows_per) {
     const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
     if (c0 >= cols) return;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (vec && c0 + 8 <= cols) {
-        const uint16_t *base = w + c0;
-        int r = r0;
-        for (; r + 4 <= r1; r += 4) {
-            uint4 q[4];
-            float vr[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                q[u] = __ldg(reinterpret_cast<const uint4 *>(base + (long long)(r + u) * cols));
-                vr[u] = __ldg(v + r + u);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    acc[2 * j] = fmaf(vr[u], __uint_as_float(wd[j] << 16), acc[2 * j]);
-                    acc[2 * j + 1] = fmaf(vr[u], __uint_as_float(wd[j] & 0xffff0000u), acc[2 * j + 1]);
-                }
-            }
-        }
-        for (; r < r1; r++) {
-            const float vr = __ldg(v + r);
-            uint4 q = __ldg(reinterpret_cast<const uint4 *>(base + (long long)r * cols));
-            const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                acc[2 * j] = fmaf(vr, __uint_as_float(wd[j] << 16), acc[2 * j]);
-                acc[2 * j + 1] = fmaf(vr, __uint_as_float(wd[j] & 0xffff0000u), acc[2 * j + 1]);
-            }
-        }
-    } else {
-        for (int r = r0; r < r1; r++) {
-            const float vr = v[r];
-            if (vr == 0.0f) continue;
-            for (int j = 0; j < 8 && c0 + j < cols; j++)
-                acc[j] = fmaf(vr, bf16_bits_to_f32(w[(long long)r * cols + c0 + j]), acc[j]);
-        }
+    for (int r = r0; r < r1; r++) {
+        const float vr = v[r];
+        if (vr == 0.0f) continue;
+        for (int j = 0; j < 8 && c0 + j < cols; j++)
+            acc[j] = fmaf(vr, bf16_bits_to_f32(w[(long long)r * cols + c0 + j]), acc[j]);
     }
     for (int j = 0; j < 8 && c0 + j < cols; j++) atomicAdd(out + c0 + j, acc[j]);
 }
@@ -161,7 +124,9 @@ __device__ __forceinline__ void e4m3x4(uint32_t w, float *f) {
 }
 
 // FP8 weights: each element is the decoded bf16 value bf16(code * scale),
-// as the reference's materialised weight (src/dequant.zig:505-511).
+// as the reference's materialised weight (src/dequant.zig:505-511). The
+// byte-wise form, for shapes the piece kernel below does not take (columns or
+// column blocks not a multiple of 16, or codes not 16-byte aligned).
 __global__ void k_gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int cols, int br, int bc,
                              int scols, const float *v, float *out, int rows_per) {
     const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 16;
@@ -170,59 +135,106 @@ __global__ void k_gemv_t_fp8(const uint8_t *codes, const float *scales, int rows
     float acc[16];
 #pragma unroll
     for (int j = 0; j < 16; j++) acc[j] = 0.0f;
-    const bool vec = (cols & 15) == 0 && (bc & 15) == 0;
-    if (vec) {
-        // Rows four at a time; the next group's loads are issued before this
-        // group's math (software pipelined), and each element is decoded with
-        // the packed conversions: bf16(code * scale) as the GEMM operand, then
-        // v[r] times it (no skip of v[r] == 0 rows: they add exactly zero for
-        // finite weights).
-        const int sc = c0 / bc;
+    for (int r = r0; r < r1; r++) {
+        const float vr = v[r];
+        const float *srow = scales + (long long)(r / br) * scols;
+        for (int j = 0; j < 16 && c0 + j < cols; j++) {
+            float f[4];
+            e4m3x4(codes[(long long)r * cols + c0 + j], f);
+            acc[j] = fmaf(vr, bf16_bits_to_f32(f32_to_bf16_bits(f[0] * srow[(c0 + j) / bc])), acc[j]);
+        }
+    }
+    for (int j = 0; j < 16 && c0 + j < cols; j++) atomicAdd(out + c0 + j, acc[j]);
+}
+
+
+
+// ---- streaming GEMV-T over 16-byte row pieces ----
+// out[c] += sum_{r in the block's rows} v[r] W[r][c] for bf16 weights (8
+// columns per 16-byte piece) or FP8 block-scaled ones (16 columns, each
+// element the decoded bf16(code * scale) of src/dequant.zig:505-511, the
+// operand the reference multiplies). Block = 32 column lanes (x) by 8 row
+// lanes (y): a warp reads 512 contiguous bytes of one row; row lane y takes
+// rows r0 + y, r0 + y + 8, ..., four of them per step with the next four
+// loaded before this step's math. The 8 row lanes are added in shared memory
+// in lane order and the block adds each column's sum to out with one atomic
+// (a block covers 256 / 512 columns and a run of rows; the runs are sized for
+// the blocks one SM holds at once: three bf16 ones, two FP8 ones). Needs 16-byte aligned rows (w aligned, cols a
+// multiple of the piece) and, for FP8, column blocks a multiple of 16. Rows
+// with v[r] == 0 are not skipped (the reference skips them,
+// src/tensor.zig:1065-1068): for finite weights they add exactly zero, and
+// the stream keeps its loads in flight without a data-dependent branch.
+constexpr int kRowLanes = 8;
+
+template <bool FP8>
+__global__ void __launch_bounds__(32 * kRowLanes, FP8 ? 2 : 3)
+    k_gemv_t_pieces(const uint8_t *w, const float *scales, int rows, int cols, int br, int bc, int scols,
+                    const float *v, float *out, int rows_per) {
+    constexpr int E = FP8 ? 16 : 8;        // columns per piece
+    constexpr int kBytes = FP8 ? 1 : 2;    // per element
+    __shared__ float red[kRowLanes][E][33];
+    const int x = threadIdx.x, y = threadIdx.y;
+    const int cblk = blockIdx.x * 32 * E;
+    const int c0 = cblk + x * E;
+    const int r0 = blockIdx.y * rows_per, r1 = min(rows, r0 + rows_per);
+    float acc[E];
+#pragma unroll
+    for (int j = 0; j < E; j++) acc[j] = 0.0f;
+    if (c0 < cols) {
+        const uint8_t *base = w + (long long)c0 * kBytes;
+        const long long pitch = (long long)cols * kBytes;
+        const int sc = FP8 ? c0 / bc : 0;
         uint4 qn[4];
         float vn[4], sn[4];
-        auto fetch = [&](int r) {
+        auto fetch = [&](int rb) {
 #pragma unroll
             for (int u = 0; u < 4; u++) {
-                const bool ok = r + u < r1;
-                qn[u] = ok ? __ldg(reinterpret_cast<const uint4 *>(codes + (long long)(r + u) * cols + c0))
-                           : make_uint4(0, 0, 0, 0);
-                vn[u] = ok ? __ldg(v + r + u) : 0.0f;
-                sn[u] = ok ? __ldg(scales + (long long)((r + u) / br) * scols + sc) : 0.0f;
+                const int r = rb + kRowLanes * u;
+                const bool ok = r < r1;
+                qn[u] = ok ? __ldg(reinterpret_cast<const uint4 *>(base + (long long)r * pitch)) : make_uint4(0, 0, 0, 0);
+                vn[u] = ok ? __ldg(v + r) : 0.0f;
+                sn[u] = (FP8 && ok) ? __ldg(scales + (long long)(r / br) * scols + sc) : 0.0f;
             }
         };
-        fetch(r0);
-        for (int r = r0; r < r1; r += 4) {
+        fetch(r0 + y);
+        for (int rb = r0 + y; rb < r1; rb += 4 * kRowLanes) {
             uint4 q[4];
-            float vr[4], s[4];
+            float vr[4], s4[4];
 #pragma unroll
-            for (int u = 0; u < 4; u++) q[u] = qn[u], vr[u] = vn[u], s[u] = sn[u];
-            if (r + 4 < r1) fetch(r + 4);
+            for (int u = 0; u < 4; u++) q[u] = qn[u], vr[u] = vn[u], s4[u] = sn[u];
+            if (rb + 4 * kRowLanes < r1) fetch(rb + 4 * kRowLanes);
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 const uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const uint32_t p0 = scale_pack(e4m3x2_f32(wd[j] & 0xffff), s[u]);
-                    const uint32_t p1 = scale_pack(e4m3x2_f32(wd[j] >> 16), s[u]);
-                    acc[4 * j] = fmaf(vr[u], __uint_as_float(p0 << 16), acc[4 * j]);
-                    acc[4 * j + 1] = fmaf(vr[u], __uint_as_float(p0 & 0xffff0000u), acc[4 * j + 1]);
-                    acc[4 * j + 2] = fmaf(vr[u], __uint_as_float(p1 << 16), acc[4 * j + 2]);
-                    acc[4 * j + 3] = fmaf(vr[u], __uint_as_float(p1 & 0xffff0000u), acc[4 * j + 3]);
+                    if (FP8) {
+                        const uint32_t p0 = scale_pack(e4m3x2_f32(wd[j] & 0xffff), s4[u]);
+                        const uint32_t p1 = scale_pack(e4m3x2_f32(wd[j] >> 16), s4[u]);
+                        acc[4 * j] = fmaf(vr[u], __uint_as_float(p0 << 16), acc[4 * j]);
+                        acc[4 * j + 1] = fmaf(vr[u], __uint_as_float(p0 & 0xffff0000u), acc[4 * j + 1]);
+                        acc[4 * j + 2] = fmaf(vr[u], __uint_as_float(p1 << 16), acc[4 * j + 2]);
+                        acc[4 * j + 3] = fmaf(vr[u], __uint_as_float(p1 & 0xffff0000u), acc[4 * j + 3]);
+                    } else {
+                        acc[2 * j] = fmaf(vr[u], __uint_as_float(wd[j] << 16), acc[2 * j]);
+                        acc[2 * j + 1] = fmaf(vr[u], __uint_as_float(wd[j] & 0xffff0000u), acc[2 * j + 1]);
+                    }
                 }
             }
         }
-    } else {
-        for (int r = r0; r < r1; r++) {
-            const float vr = v[r];
-            const float *srow = scales + (long long)(r / br) * scols;
-            for (int j = 0; j < 16 && c0 + j < cols; j++) {
-                float f[4];
-                e4m3x4(codes[(long long)r * cols + c0 + j], f);
-                acc[j] = fmaf(vr, bf16_bits_to_f32(f32_to_bf16_bits(f[0] * srow[(c0 + j) / bc])), acc[j]);
-            }
-        }
     }
-    for (int j = 0; j < 16 && c0 + j < cols; j++) atomicAdd(out + c0 + j, acc[j]);
+#pragma unroll
+    for (int j = 0; j < E; j++) red[y][j][x] = acc[j];
+    __syncthreads();
+    for (int cc = y * 32 + x; cc < 32 * E; cc += 32 * kRowLanes) {
+        const int col = cblk + cc;
+        if (col >= cols) break;
+        const int xx = cc / E, j = cc % E;
+        float t = 0.0f;
+#pragma unroll
+        for (int l = 0; l < kRowLanes; l++) t += red[l][j][xx];
+        atomicAdd(out + col, t);
+    }
 }
 
 __device__ __constant__ float kE2M1e[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f,
@@ -418,28 +430,64 @@ __global__ void k_scale_vec(const float *v, float lambda, int n, float *b) {
 }
 
 // ---- scoring ----
-// ---- log-softmax and KL over row chunks ----
-// A vocabulary row (C2: 128256 logits) is split into `chunks` pieces so the
-// whole GPU works on a batch of prompts: piece (row, c) finds its maximum
-// m_c and s_c = sum exp(x - m_c) in f64; the row's log-sum-exp combines the
-// pieces in order, lse = m + log(sum_c s_c exp(m_c - m)) with m = max m_c, as
-// src/tensor.zig:1203-1210 (f64 sum of the f64 exps, the result in f32); the
-// KL pieces then add exp(b)(b - (x - lse)) in f64 (src/scorers.zig:385-400)
-// and one thread per row adds the pieces in order.
-__global__ void __launch_bounds__(256) k_lse_part(const float *x, int vocab, int per, double2 *part) {
+// ---- log-softmax and KL over row pieces ----
+// A vocabulary row (C2: 128256 logits) is split into pieces of kKlPiece
+// logits, one block each (16 per thread, read once and kept in registers for
+// both the maximum and the sum): piece (row, c) finds its maximum m_c and
+// s_c = sum exp(x - m_c) in f64; the row's log-sum-exp combines the pieces in
+// order, lse = m + log(sum_c s_c exp(m_c - m)) with m = max m_c, as
+// src/tensor.zig:1203-1210 (an f64 sum, the result in f32). Each term is
+// f32 expf of the f32 difference, widened to f64 before it is added (the
+// reference takes the exp in f64: the terms differ by one f32 rounding, about
+// 6e-8 relative, far below the f32 result's own rounding after the log).
+// The KL pieces then add exp(b)(b - (x - lse)) in f64 (src/scorers.zig:
+// 385-400; exp(b) again f32 expf widened) and one thread per row adds the
+// pieces in order. The pieces depend only on the vocabulary size, so the sums
+// are the same for any batch.
+constexpr int kKlThreads = 256, kKlEach = 16, kKlPiece = kKlThreads * kKlEach;
+
+// this thread's 16 logits of a piece (out-of-row slots get `fill`): four
+// 16-byte loads when rows are 16-byte aligned (vocab a multiple of 4 on an
+// aligned base), else strided scalar loads.
+__device__ __forceinline__ void kl_load(const float *xr, int lo, int vocab, bool vec, float fill,
+                                        float (&v)[kKlEach]) {
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int j = lo + (k * kKlThreads + (int)threadIdx.x) * 4;
+            float4 q = make_float4(fill, fill, fill, fill);
+            if (j < vocab) q = __ldg(reinterpret_cast<const float4 *>(xr + j));  // j + 3 < vocab
+            v[4 * k] = q.x, v[4 * k + 1] = q.y, v[4 * k + 2] = q.z, v[4 * k + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < kKlEach; k++) {
+            const int j = lo + k * kKlThreads + (int)threadIdx.x;
+            v[k] = j < vocab ? __ldg(xr + j) : fill;
+        }
+    }
+}
+
+// the column of slot k of this thread (the layout kl_load reads)
+__device__ __forceinline__ int kl_col(int lo, bool vec, int k) {
+    return vec ? lo + ((k >> 2) * kKlThreads + (int)threadIdx.x) * 4 + (k & 3) : lo + k * kKlThreads + (int)threadIdx.x;
+}
+
+__global__ void __launch_bounds__(kKlThreads) k_lse_part(const float *x, int vocab, bool vec, double2 *part) {
     __shared__ float shf[32];
     __shared__ double shd[32];
     const int row = blockIdx.y, c = blockIdx.x, chunks = gridDim.x;
     const float *xr = x + (long long)row * vocab;
-    const int lo = c * per, hi = min(vocab, lo + per);
+    float v[kKlEach];
+    kl_load(xr, c * kKlPiece, vocab, vec, -INFINITY, v);
     float m = -INFINITY;
-#pragma unroll 4
-    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) m = fmaxf(m, xr[j]);
+#pragma unroll
+    for (int k = 0; k < kKlEach; k++) m = fmaxf(m, v[k]);
     m = block_max(m, shf);
     double s = 0.0;
     if (m > -INFINITY) {
-#pragma unroll 4
-        for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) s += exp((double)(xr[j] - m));
+#pragma unroll
+        for (int k = 0; k < kKlEach; k++) s += (double)expf(v[k] - m);
     }
     s = block_sum_d(s, shd);
     if (threadIdx.x == 0) part[(long long)row * chunks + c] = make_double2((double)m, s);
@@ -454,8 +502,8 @@ __device__ __forceinline__ float row_lse_from_parts(const double2 *part, int chu
     return m + (float)log(s);
 }
 
-__global__ void __launch_bounds__(256) k_log_softmax_part(const float *x, int vocab, int per, const double2 *part,
-                                                          float *out) {
+__global__ void __launch_bounds__(kKlThreads) k_log_softmax_part(const float *x, int vocab, bool vec,
+                                                                 const double2 *part, float *out) {
     __shared__ float s_lse;
     const int row = blockIdx.y, c = blockIdx.x, chunks = gridDim.x;
     if (threadIdx.x == 0) s_lse = row_lse_from_parts(part + (long long)row * chunks, chunks);
@@ -463,27 +511,43 @@ __global__ void __launch_bounds__(256) k_log_softmax_part(const float *x, int vo
     const float lse = s_lse;
     const float *xr = x + (long long)row * vocab;
     float *o = out + (long long)row * vocab;
-    const int lo = c * per, hi = min(vocab, lo + per);
-    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) o[j] = xr[j] - lse;
+    const int lo = c * kKlPiece;
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int j = lo + (k * kKlThreads + (int)threadIdx.x) * 4;
+            if (j < vocab) {
+                const float4 q = __ldg(reinterpret_cast<const float4 *>(xr + j));
+                *reinterpret_cast<float4 *>(o + j) = make_float4(q.x - lse, q.y - lse, q.z - lse, q.w - lse);
+            }
+        }
+    } else {
+        for (int k = 0; k < kKlEach; k++) {
+            const int j = lo + k * kKlThreads + (int)threadIdx.x;
+            if (j < vocab) o[j] = xr[j] - lse;
+        }
+    }
 }
 
-__global__ void __launch_bounds__(256) k_kl_part(const float *base, const float *logits, int vocab, int per,
-                                                 const double2 *part, double *kl_part) {
+__global__ void __launch_bounds__(kKlThreads) k_kl_part(const float *base, const float *logits, int vocab, bool vec,
+                                                        const double2 *part, double *kl_part) {
     __shared__ float s_lse;
     __shared__ double shd[32];
     const int row = blockIdx.y, c = blockIdx.x, chunks = gridDim.x;
     if (threadIdx.x == 0) s_lse = row_lse_from_parts(part + (long long)row * chunks, chunks);
+    const int lo = c * kKlPiece;
+    float x[kKlEach], b[kKlEach];
+    kl_load(logits + (long long)row * vocab, lo, vocab, vec, 0.0f, x);
+    kl_load(base + (long long)row * vocab, lo, vocab, vec, 0.0f, b);
     __syncthreads();
     const float lse = s_lse;
-    const float *xr = logits + (long long)row * vocab;
-    const float *lb = base + (long long)row * vocab;
-    const int lo = c * per, hi = min(vocab, lo + per);
     double s = 0.0;
-#pragma unroll 4
-    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) {
-        const double b = (double)lb[j];
-        const float lt = xr[j] - lse;
-        s += exp(b) * (b - (double)lt);
+#pragma unroll
+    for (int k = 0; k < kKlEach; k++) {
+        if (kl_col(lo, vec, k) < vocab) {
+            const float lt = x[k] - lse;
+            s += (double)expf(b[k]) * ((double)b[k] - (double)lt);
+        }
     }
     s = block_sum_d(s, shd);
     if (threadIdx.x == 0) kl_part[(long long)row * chunks + c] = s;
@@ -498,23 +562,33 @@ __global__ void k_kl_rows_sum(const double *kl_part, int rows, int chunks, doubl
 }
 
 // ---- capture and directions ----
-// One thread per (entry, 4 hidden coordinates); prompts in order.
+// Prompt b's mean over its take[b] captures is an f32 running sum of
+// (1 / take) * r in token order, added to the entry's f64 sum in prompt order
+// (src/engine.zig:414-431). The prompts are split into `groups` consecutive
+// runs (blockIdx.y): a thread handles one (entry, 4 hidden coordinates) of
+// one run, its prompts in order, and stores the run's f64 sum; a second pass
+// adds the runs in order. Every prompt's f32 mean is the reference's; only
+// the f64 additions are grouped (runs, then their totals).
 __global__ void k_residual_sums(const float *res, int entries, int nc, int hidden, const int *first, const int *take,
-                                int prompts, double *sums) {
+                                int prompts, int per_group, double *part) {
     const int h4 = hidden / 4;
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     const bool vec = (hidden & 3) == 0;
     const int per_entry = vec ? h4 : hidden;
     if (idx >= entries * per_entry) return;
     const int l = idx / per_entry, j = idx % per_entry;
+    const int b0 = blockIdx.y * per_group, b1 = min(prompts, b0 + per_group);
+    double *o = part + ((long long)blockIdx.y * entries + l) * hidden;
     if (vec) {
         double s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-        for (int b = 0; b < prompts; b++) {
+        for (int b = b0; b < b1; b++) {
             const int tk = take[b];
             const float inv = 1.0f / (float)(tk > 0 ? tk : 1);
+            const float4 *src = reinterpret_cast<const float4 *>(res + ((long long)l * nc + first[b]) * hidden) + j;
             float v0 = 0, v1 = 0, v2 = 0, v3 = 0;
+#pragma unroll 4
             for (int t = 0; t < tk; t++) {
-                const float4 r = *reinterpret_cast<const float4 *>(res + ((long long)l * nc + first[b] + t) * hidden + 4 * j);
+                const float4 r = __ldg(src + (long long)t * h4);
                 v0 = v0 + inv * r.x;
                 v1 = v1 + inv * r.y;
                 v2 = v2 + inv * r.z;
@@ -525,22 +599,28 @@ __global__ void k_residual_sums(const float *res, int entries, int nc, int hidde
             s2 += v2;
             s3 += v3;
         }
-        double *o = sums + (long long)l * hidden + 4 * j;
-        o[0] += s0;
-        o[1] += s1;
-        o[2] += s2;
-        o[3] += s3;
+        *reinterpret_cast<double2 *>(o + 4 * j) = make_double2(s0, s1);
+        *reinterpret_cast<double2 *>(o + 4 * j + 2) = make_double2(s2, s3);
     } else {
         double s = 0;
-        for (int b = 0; b < prompts; b++) {
+        for (int b = b0; b < b1; b++) {
             const int tk = take[b];
             const float inv = 1.0f / (float)(tk > 0 ? tk : 1);
             float v = 0;
             for (int t = 0; t < tk; t++) v = v + inv * res[((long long)l * nc + first[b] + t) * hidden + j];
             s += v;
         }
-        sums[(long long)l * hidden + j] += s;
+        o[j] = s;
     }
+}
+
+// sums[i] += the runs' sums in run order
+__global__ void k_residual_groups_sum(const double *part, long long n, int groups, double *sums) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    double s = 0;
+    for (int g = 0; g < groups; g++) s += part[(long long)g * n + i];
+    sums[i] += s;
 }
 
 // One block per entry: means, difference, normalisation, orthogonalisation.
@@ -588,13 +668,29 @@ __global__ void k_directions(const double *gs, double gc, const double *bs, doub
 
 }  // namespace
 
+// Row runs for the piece kernels: one wave of `per_sm` blocks per SM, at
+// least 64 rows (8 per row lane) per block.
+static int piece_splits(int rows, int col_blocks, int per_sm) {
+    int s = (per_sm * 148 + col_blocks - 1) / col_blocks;
+    s = std::min(s, (rows + 63) / 64);
+    return std::max(1, std::min(s, 65535));
+}
+
 cudaError_t gemv_t_bf16(const uint16_t *w, int rows, int cols, const float *v, float *out, cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return cudaSuccess;
+    const bool vec = (cols & 7) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+    if (vec) {
+        const int cb = (cols + 255) / 256;
+        const int sp = piece_splits(rows, cb, 3);
+        const int per = (rows + sp - 1) / sp;
+        k_gemv_t_pieces<false><<<dim3(cb, (rows + per - 1) / per), dim3(32, kRowLanes), 0, st>>>(
+            reinterpret_cast<const uint8_t *>(w), nullptr, rows, cols, 1, 1, 1, v, out, per);
+        return cudaGetLastError();
+    }
     const int cb = (cols + kGemvThreads * 8 - 1) / (kGemvThreads * 8);
     const int sp = row_splits(rows, cb);
     const int per = (rows + sp - 1) / sp;
-    const bool vec = (cols & 7) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
-    k_gemv_t_bf16<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(w, rows, cols, v, out, per, vec);
+    k_gemv_t_bf16<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(w, rows, cols, v, out, per);
     return cudaGetLastError();
 }
 
@@ -610,11 +706,20 @@ cudaError_t gemv_t_f32(const float *w, int rows, int cols, const float *v, float
 cudaError_t gemv_t_fp8(const uint8_t *codes, const float *scales, int rows, int cols, int br, int bc,
                        const float *v, float *out, cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return cudaSuccess;
+    const int scols = (cols + bc - 1) / bc;
+    if ((cols & 15) == 0 && (bc & 15) == 0 && (reinterpret_cast<uintptr_t>(codes) & 15) == 0) {
+        const int cb = (cols + 511) / 512;
+        const int sp = piece_splits(rows, cb, 2);
+        const int per = (rows + sp - 1) / sp;
+        k_gemv_t_pieces<true><<<dim3(cb, (rows + per - 1) / per), dim3(32, kRowLanes), 0, st>>>(
+            codes, scales, rows, cols, br, bc, scols, v, out, per);
+        return cudaGetLastError();
+    }
     const int cb = (cols + kGemvThreads * 16 - 1) / (kGemvThreads * 16);
     const int sp = row_splits(rows, cb, 16);
     const int per = (rows + sp - 1) / sp;
-    k_gemv_t_fp8<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(codes, scales, rows, cols, br, bc,
-                                                                          (cols + bc - 1) / bc, v, out, per);
+    k_gemv_t_fp8<<<dim3(cb, (rows + per - 1) / per), kGemvThreads, 0, st>>>(codes, scales, rows, cols, br, bc, scols,
+                                                                          v, out, per);
     return cudaGetLastError();
 }
 
@@ -699,10 +804,8 @@ cudaError_t scale_vec(const float *v, float lambda, int n, float *b, cudaStream_
 }
 
 int kl_chunks(int rows, int vocab) {
-    // about four blocks per SM over the batch, pieces of at least 4096 logits
-    int c = (4 * 148 + std::max(rows, 1) - 1) / std::max(rows, 1);
-    c = std::min(c, std::max(1, vocab / 4096));
-    return std::max(1, std::min(c, 64));
+    (void)rows;
+    return std::max(1, (vocab + kKlPiece - 1) / kKlPiece);
 }
 
 size_t kl_scratch_bytes(int rows, int vocab) {
@@ -710,33 +813,60 @@ size_t kl_scratch_bytes(int rows, int vocab) {
     return n * sizeof(double2) + n * sizeof(double);
 }
 
+static bool kl_vec(const void *a, const void *b, int vocab) {
+    return (vocab & 3) == 0 && ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) == 0;
+}
+
 cudaError_t log_softmax_rows(const float *x, int rows, int vocab, float *out, void *scratch, cudaStream_t st) {
-    if (rows <= 0) return cudaSuccess;
-    const int chunks = kl_chunks(rows, vocab), per = (vocab + chunks - 1) / chunks;
+    if (rows <= 0 || vocab <= 0) return cudaSuccess;
+    if (rows > 65535) return cudaErrorInvalidValue;  // rows are the grid's y
+    const int chunks = kl_chunks(rows, vocab);
+    const bool vec = kl_vec(x, out, vocab);
     double2 *part = static_cast<double2 *>(scratch);
-    k_lse_part<<<dim3(chunks, rows), 256, 0, st>>>(x, vocab, per, part);
-    k_log_softmax_part<<<dim3(chunks, rows), 256, 0, st>>>(x, vocab, per, part, out);
+    k_lse_part<<<dim3(chunks, rows), kKlThreads, 0, st>>>(x, vocab, vec, part);
+    k_log_softmax_part<<<dim3(chunks, rows), kKlThreads, 0, st>>>(x, vocab, vec, part, out);
     return cudaGetLastError();
 }
 
 cudaError_t kl_rows(const float *baseline, const float *logits, int rows, int vocab, double *kl, void *scratch,
                     cudaStream_t st) {
-    if (rows <= 0) return cudaSuccess;
-    const int chunks = kl_chunks(rows, vocab), per = (vocab + chunks - 1) / chunks;
+    if (rows <= 0 || vocab <= 0) return cudaSuccess;
+    if (rows > 65535) return cudaErrorInvalidValue;  // rows are the grid's y
+    const int chunks = kl_chunks(rows, vocab);
+    const bool vec = kl_vec(baseline, logits, vocab);
     double2 *part = static_cast<double2 *>(scratch);
     double *kl_part = reinterpret_cast<double *>(part + (size_t)rows * chunks);
-    k_lse_part<<<dim3(chunks, rows), 256, 0, st>>>(logits, vocab, per, part);
-    k_kl_part<<<dim3(chunks, rows), 256, 0, st>>>(baseline, logits, vocab, per, part, kl_part);
+    k_lse_part<<<dim3(chunks, rows), kKlThreads, 0, st>>>(logits, vocab, vec, part);
+    k_kl_part<<<dim3(chunks, rows), kKlThreads, 0, st>>>(baseline, logits, vocab, vec, part, kl_part);
     k_kl_rows_sum<<<(rows + 127) / 128, 128, 0, st>>>(kl_part, rows, chunks, kl);
     return cudaGetLastError();
 }
 
+// Runs of at least four prompts, enough of them for about 2048 threads per SM.
+static int residual_groups(int entries, int hidden, int prompts) {
+    const long long threads = (long long)entries * ((hidden & 3) == 0 ? hidden / 4 : hidden);
+    long long g = (148LL * 2048 + threads - 1) / std::max(threads, 1LL);
+    g = std::min<long long>(g, (prompts + 3) / 4);
+    return (int)std::max(1LL, std::min(g, 65535LL));
+}
+
+size_t residual_scratch_bytes(int entries, int hidden, int prompts) {
+    return (size_t)residual_groups(entries, hidden, prompts) * std::max(entries, 0) * std::max(hidden, 0) * 8;
+}
+
 cudaError_t residual_sums(const float *res, int entries, int nc, int hidden, const int *first, const int *take,
-                          int prompts, double *sums, cudaStream_t st) {
+                          int prompts, double *sums, double *scratch, cudaStream_t st) {
     const int per = (hidden & 3) == 0 ? hidden / 4 : hidden;
     const int total = entries * per;
-    if (total <= 0) return cudaSuccess;
-    k_residual_sums<<<(total + 127) / 128, 128, 0, st>>>(res, entries, nc, hidden, first, take, prompts, sums);
+    if (total <= 0 || prompts <= 0) return cudaSuccess;
+    if ((hidden & 3) == 0 && (reinterpret_cast<uintptr_t>(res) & 15)) return cudaErrorInvalidValue;
+    const int groups = residual_groups(entries, hidden, prompts);
+    const int per_group = (prompts + groups - 1) / groups;
+    const int used = (prompts + per_group - 1) / per_group;
+    k_residual_sums<<<dim3((total + 127) / 128, used), 128, 0, st>>>(res, entries, nc, hidden, first, take, prompts,
+                                                                     per_group, scratch);
+    const long long n = (long long)entries * hidden;
+    k_residual_groups_sum<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(scratch, n, used, sums);
     return cudaGetLastError();
 }
 

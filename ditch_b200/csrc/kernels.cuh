@@ -197,9 +197,11 @@ size_t kl_scratch_bytes(int rows, int vocab);
 
 // ---- capture and directions -------------------------------------------------
 // sums[l][h] += mean over take[b] captures of prompt b (f64), per prompt and
-// entry (src/engine.zig:414-431).
+// entry (src/engine.zig:414-431); `scratch` holds residual_scratch_bytes(
+// entries, hidden, prompts) bytes (the prompt runs' partial sums).
 cudaError_t residual_sums(const float *res, int entries, int nc, int hidden, const int *first, const int *take,
-                          int prompts, double *sums, cudaStream_t st);
+                          int prompts, double *sums, double *scratch, cudaStream_t st);
+size_t residual_scratch_bytes(int entries, int hidden, int prompts);
 // dirs[e] = normalize(bad - good) (orthogonalised against normalize(good)),
 // from f64 sums and counts (src/abliterate.zig:88-109, engine.zig:334-336).
 cudaError_t directions_from_sums(const double *good_sums, double good_count, const double *bad_sums,

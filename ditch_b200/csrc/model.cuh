@@ -70,6 +70,9 @@ struct Config {
     double rope_theta;
     int rope_scaling;
     double rope_factor, rope_low_ff, rope_high_ff, rope_orig_max;
+    std::vector<float> rope_factors;  // per-frequency divisors (rope_scaling 4)
+    double rope_attention_factor = 1.0, rope_beta_fast = 32.0, rope_beta_slow = 1.0;
+    int rope_truncate = 1;
     int qk_norm;
     int n_experts, top_k, moe_inter, norm_topk;
     std::vector<uint8_t> moe_layers;
@@ -148,7 +151,8 @@ struct ditch_cuda_model {
     ditch::DevBuf vn;    // f32 [H]: v / ||W_i|| of the pre-normalised edit
     ditch::DevBuf fn_act, fn_out, fn_y, fn_x, fn_a, fn_s;  // full-mode scratch
     ditch::Batch work;   // scratch batch for forward / residual passes
-    ditch::DevBuf sums;  // f64 residual sums
+    ditch::DevBuf sums;       // f64 residual sums
+    ditch::DevBuf sums_part;  // the prompt runs' partial sums of one batch
     uint64_t bytes = 0;
 };
 

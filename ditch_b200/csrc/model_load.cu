@@ -387,13 +387,18 @@ int load_vec(ditch_cuda_model *m, const ditch_cuda_tensor *t, size_t n, DevBuf &
     return DITCH_CUDA_OK;
 }
 
-// llama3 frequency scaling and the f64 angle table (src/model.zig:2200-2282).
+// The inverse frequencies with the config's scaling and the f64 angle table
+// (src/model.zig:2200-2282): llama3's smoothed divisor, linear, YaRN's ramp
+// between interpolated and extrapolated frequencies (Hugging Face's
+// correction dims, optionally truncated), or per-frequency divisors; cos /
+// sin times the attention factor (YaRN, LongRoPE).
 int build_rope(ditch_cuda_model *m) {
     const Config &c = m->cfg;
     const int half = c.head_dim / 2;
     const int len = std::max(c.max_seq, 1);
     std::vector<double> inv(half);
     for (int i = 0; i < half; i++) inv[i] = 1.0 / std::pow(c.rope_theta, (double)(2 * i) / (double)c.head_dim);
+    double attn = 1.0;
     if (c.rope_scaling == 1) {
         const double low_wl = c.rope_orig_max / c.rope_low_ff, high_wl = c.rope_orig_max / c.rope_high_ff;
         for (int i = 0; i < half; i++) {
@@ -406,13 +411,37 @@ int build_rope(ditch_cuda_model *m) {
                 inv[i] = (1.0 - smooth) * inv[i] / c.rope_factor + smooth * inv[i];
             }
         }
+    } else if (c.rope_scaling == 2) {
+        for (int i = 0; i < half; i++) inv[i] /= c.rope_factor;
+    } else if (c.rope_scaling == 3) {
+        const double dim = (double)c.head_dim, base = c.rope_theta;
+        auto corr_dim = [&](double rot) {
+            return dim * std::log(c.rope_orig_max / (rot * 2.0 * M_PI)) / (2.0 * std::log(base));
+        };
+        double low = corr_dim(c.rope_beta_fast), high = corr_dim(c.rope_beta_slow);
+        if (c.rope_truncate) {
+            low = std::floor(low);
+            high = std::ceil(high);
+        }
+        low = std::max(low, 0.0);
+        high = std::min(high, dim - 1);
+        if (low == high) high += 0.001;
+        for (int i = 0; i < half; i++) {
+            const double ramp = std::min(1.0, std::max(0.0, ((double)i - low) / (high - low)));
+            const double extrap = 1.0 - ramp;
+            inv[i] = inv[i] / c.rope_factor * (1.0 - extrap) + inv[i] * extrap;
+        }
+        attn = c.rope_attention_factor;
+    } else if (c.rope_scaling == 4) {
+        for (int i = 0; i < half && i < (int)c.rope_factors.size(); i++) inv[i] /= (double)c.rope_factors[i];
+        attn = c.rope_attention_factor;
     }
     std::vector<float> cs((size_t)len * half), sn((size_t)len * half);
     for (int p = 0; p < len; p++)
         for (int i = 0; i < half; i++) {
             const double a = (double)p * inv[i];
-            cs[(size_t)p * half + i] = (float)std::cos(a);
-            sn[(size_t)p * half + i] = (float)std::sin(a);
+            cs[(size_t)p * half + i] = (float)(std::cos(a) * attn);
+            sn[(size_t)p * half + i] = (float)(std::sin(a) * attn);
         }
     DITCH_CUDA(m->rope_cos.reserve(cs.size() * 4));
     DITCH_CUDA(m->rope_sin.reserve(sn.size() * 4));
@@ -466,6 +495,18 @@ int ditch_cuda_model_load(ditch_cuda_device *dev, const ditch_cuda_model_config 
     c.rope_low_ff = cfg->rope_low_ff;
     c.rope_high_ff = cfg->rope_high_ff;
     c.rope_orig_max = cfg->rope_orig_max;
+    REQUIRE(c.rope_scaling >= 0 && c.rope_scaling <= 4, "rope_scaling %d is not 0 to 4", c.rope_scaling);
+    REQUIRE(c.rope_scaling != 4 || cfg->n_rope_factors == 0 || cfg->rope_factors,
+            "rope_factors is null with n_rope_factors > 0");
+    if (c.rope_scaling == 4 && cfg->n_rope_factors)
+        c.rope_factors.assign(cfg->rope_factors, cfg->rope_factors + cfg->n_rope_factors);
+    c.rope_attention_factor = cfg->rope_attention_factor != 0 ? cfg->rope_attention_factor : 1.0;
+    c.rope_beta_fast = cfg->rope_beta_fast;
+    c.rope_beta_slow = cfg->rope_beta_slow;
+    c.rope_truncate = cfg->rope_truncate;
+    REQUIRE(c.rope_scaling != 3 || (c.rope_factor > 0 && c.rope_orig_max > 0 && c.rope_beta_fast > 0 &&
+                                    c.rope_beta_slow > 0 && c.rope_theta > 1),
+            "yarn rope scaling needs a positive factor, original length and betas");
     c.qk_norm = cfg->qk_norm;
     c.n_experts = cfg->n_experts;
     c.top_k = cfg->top_k;

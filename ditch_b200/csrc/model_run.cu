@@ -1072,8 +1072,9 @@ int ditch_cuda_residual_sums(ditch_cuda_model *m, const uint32_t *tokens, const 
         if ((s = forward_batch(m, m->work, nc, 0))) return s;
         DITCH_CUDA(upload_vec(dfirst, first, dev->stream));
         DITCH_CUDA(upload_vec(dtake, take, dev->stream));
+        DITCH_CUDA(m->sums_part.reserve(residual_scratch_bytes((int)entries, (int)H, (int)np)));
         DITCH_LAUNCH(dev, residual_sums(m->res.as<float>(), (int)entries, nc, (int)H, dfirst.as<int>(), dtake.as<int>(),
-                                        (int)np, m->sums.as<double>(), dev->stream));
+                                        (int)np, m->sums.as<double>(), m->sums_part.as<double>(), dev->stream));
         DITCH_CUDA(cudaStreamSynchronize(dev->stream));
     }
     const size_t n = entries * H;

@@ -48,7 +48,14 @@ class ModelConfig(C.Structure):
         ("qk_norm", C.c_int), ("n_experts", C.c_int), ("top_k", C.c_int), ("moe_inter", C.c_int),
         ("norm_topk", C.c_int), ("moe_layers", C.POINTER(C.c_uint8)), ("max_seq", C.c_int),
         ("ep_rank", C.c_int), ("ep_world", C.c_int), ("tp_rank", C.c_int), ("tp_world", C.c_int),
+        ("rope_factors", C.POINTER(C.c_float)), ("n_rope_factors", C.c_size_t),
+        ("rope_attention_factor", C.c_double), ("rope_beta_fast", C.c_double), ("rope_beta_slow", C.c_double),
+        ("rope_truncate", C.c_int),
     ]
+
+
+# spec keys of the RoPE scaling fields beyond the llama3 ones, with their defaults
+ROPE_EXTRA = dict(rope_attention_factor=1.0, rope_beta_fast=32.0, rope_beta_slow=1.0, rope_truncate=1)
 
 
 class TensorDesc(C.Structure):
@@ -100,7 +107,7 @@ SIGNATURES = {
     "ditch_cuda_model_free": (None, [vp]),
     "ditch_cuda_model_load_checkpoint": (C.c_int, [vp, C.c_char_p, C.c_int, C.POINTER(vp)]),
     "ditch_cuda_checkpoint_inspect": (C.c_int, [C.c_char_p, C.POINTER(ModelConfig), C.POINTER(sz),
-                                                C.POINTER(C.c_uint8), sz]),
+                                                C.POINTER(C.c_uint8), sz, f32p, sz]),
     "ditch_cuda_model_bytes": (C.c_uint64, [vp]),
     "ditch_cuda_export_checkpoint": (C.c_int, [vp, C.c_char_p, C.c_char_p, C.c_int, C.c_uint64]),
     "ditch_cuda_export_config": (C.c_int, [C.c_char_p, sz, C.c_int, C.c_int, C.c_char_p, sz, C.POINTER(sz)]),
@@ -518,11 +525,17 @@ def inspect_checkpoint(path):
     cfg = ModelConfig()
     n = sz(0)
     flags = (C.c_uint8 * 4096)()
-    check(lib().ditch_cuda_checkpoint_inspect(str(path).encode(), C.byref(cfg), C.byref(n), flags, 4096))
+    factors = np.zeros(4096, np.float32)
+    check(lib().ditch_cuda_checkpoint_inspect(str(path).encode(), C.byref(cfg), C.byref(n), flags, 4096,
+                                              _p(factors, f32p), factors.size))
     spec = dict(n_layers=cfg.n_layers, hidden=cfg.hidden, heads=cfg.heads, kv_heads=cfg.kv_heads,
                 head_dim=cfg.head_dim, inter=cfg.inter, vocab=cfg.vocab, eps=cfg.eps, rope_theta=cfg.rope_theta,
                 rope_scaling=cfg.rope_scaling, rope_factor=cfg.rope_factor, rope_low_ff=cfg.rope_low_ff,
                 rope_high_ff=cfg.rope_high_ff, rope_orig_max=cfg.rope_orig_max, qk_norm=cfg.qk_norm)
+    if cfg.rope_scaling in (3, 4):
+        spec.update({k: getattr(cfg, k) for k in ROPE_EXTRA})
+    if cfg.n_rope_factors:
+        spec["rope_factors"] = factors[: cfg.n_rope_factors].copy()
     if cfg.n_experts:
         spec.update(n_experts=cfg.n_experts, top_k=cfg.top_k, moe_inter=cfg.moe_inter, norm_topk=cfg.norm_topk,
                     moe_layers=[bool(flags[i]) for i in range(cfg.n_layers)])
@@ -598,7 +611,13 @@ class Model:
             rope_high_ff=spec.get("rope_high_ff", 1.0), rope_orig_max=spec.get("rope_orig_max", 1.0),
             qk_norm=int(spec.get("qk_norm", 0)), n_experts=spec.get("n_experts", 0), top_k=spec.get("top_k", 0),
             moe_inter=spec.get("moe_inter", 0), norm_topk=int(spec.get("norm_topk", 1)), max_seq=max_seq,
-            ep_rank=ep_rank, ep_world=ep_world, tp_rank=tp_rank, tp_world=tp_world)
+            ep_rank=ep_rank, ep_world=ep_world, tp_rank=tp_rank, tp_world=tp_world,
+            **{k: spec.get(k, v) for k, v in ROPE_EXTRA.items()})
+        self._rope = None
+        if spec.get("rope_factors") is not None:
+            self._rope = np.ascontiguousarray(spec["rope_factors"], np.float32)
+            cfg.rope_factors = _p(self._rope, f32p)
+            cfg.n_rope_factors = self._rope.size
         self._moe = None
         if spec.get("moe_layers"):
             self._moe = np.array([1 if x else 0 for x in spec["moe_layers"]], np.uint8)

@@ -128,7 +128,14 @@ typedef struct {
     int n_layers, hidden, heads, kv_heads, head_dim, inter, vocab;
     float eps;
     double rope_theta;
-    int rope_scaling; /* 0 none, 1 llama3 (src/model.zig:2222-2235) */
+    /* RoPE frequency scaling (src/model.zig:2200-2282): 0 none; 1 llama3
+     * (rope_factor, rope_low_ff, rope_high_ff, rope_orig_max); 2 linear
+     * (inv_freq / rope_factor); 3 yarn (rope_factor, rope_orig_max,
+     * rope_beta_fast, rope_beta_slow, rope_truncate, rope_attention_factor);
+     * 4 per-frequency divisors inv_freq[i] / rope_factors[i] for i <
+     * n_rope_factors (a GGUF rope_freqs.weight, ditch's "ditch_factors", or
+     * LongRoPE's short factors with its rope_attention_factor). */
+    int rope_scaling;
     double rope_factor, rope_low_ff, rope_high_ff, rope_orig_max;
     int qk_norm; /* per-head q/k RMSNorm before RoPE (Qwen3) */
     int n_experts, top_k, moe_inter, norm_topk;
@@ -146,6 +153,13 @@ typedef struct {
      * (the loader takes this rank's slice) or already sharded. o / down
      * partial sums are all-reduced over the peer group after each layer. */
     int tp_rank, tp_world;
+    /* RoPE scaling, continued (read for rope_scaling 3 and 4): cos / sin are
+     * multiplied by rope_attention_factor (0 is read as 1); rope_factors is
+     * read during the load only. */
+    const float *rope_factors;
+    size_t n_rope_factors;
+    double rope_attention_factor, rope_beta_fast, rope_beta_slow;
+    int rope_truncate;
 } ditch_cuda_model_config;
 
 /* Storage formats of a resident tensor. */
@@ -198,18 +212,23 @@ void ditch_cuda_model_free(ditch_cuda_model *m);
  * down_proj in either orientation) or a GGUF file (general.architecture
  * llama, with experts mixtral, qwen2, qwen3 or qwen3moe; F32, F16, BF16, Q8_0,
  * Q4_K; llama's permuted q / k rows and biases restored; stacked ffn_*_exps
- * experts; an embedded ditch.hf.config_json; rope_freqs.weight only as Llama
- * 3's standard scaling). Quantised groups reach the device raw. The files
+ * experts; an embedded ditch.hf.config_json; rope_freqs.weight as Llama 3's
+ * scaling when it matches the standard settings, else as per-frequency
+ * divisors). rope_scaling types llama3, linear, yarn, longrope,
+ * ditch_factors; dynamic, mrope and default read as plain RoPE. Quantised groups reach the device raw. The files
  * are memory-mapped during the call. A directory holding an export's
  * .incomplete marker is refused.
  * max_seq: the RoPE table rows (0 = 4096). Anything else returns
  * DITCH_CUDA_UNSUPPORTED with the reason in ditch_cuda_last_error(). */
 int ditch_cuda_model_load_checkpoint(ditch_cuda_device *dev, const char *path, int max_seq, ditch_cuda_model **out);
 /* The config and tensor count the loader would use, without a device
- * (moe_layers, when given, receives up to moe_layers_len flags; cfg's own
- * moe_layers pointer is left NULL). */
+ * (moe_layers, when given, receives up to moe_layers_len flags; rope_factors
+ * up to rope_factors_len per-frequency RoPE divisors, their count in
+ * cfg->n_rope_factors; cfg's own moe_layers and rope_factors pointers are
+ * left NULL). */
 int ditch_cuda_checkpoint_inspect(const char *path, ditch_cuda_model_config *cfg, size_t *n_tensors,
-                                  uint8_t *moe_layers, size_t moe_layers_len);
+                                  uint8_t *moe_layers, size_t moe_layers_len, float *rope_factors,
+                                  size_t rope_factors_len);
 /* Device bytes the resident model holds. */
 uint64_t ditch_cuda_model_bytes(const ditch_cuda_model *m);
 

@@ -28,6 +28,8 @@ class Config(C.Structure):
         ("rope_factor", C.c_double), ("rope_low_ff", C.c_double), ("rope_high_ff", C.c_double),
         ("rope_orig_max", C.c_double), ("n_experts", C.c_int), ("top_k", C.c_int),
         ("moe_inter", C.c_int), ("norm_topk", C.c_int),
+        ("rope_factors", f32p), ("n_rope_factors", C.c_size_t), ("rope_attention_factor", C.c_double),
+        ("rope_beta_fast", C.c_double), ("rope_beta_slow", C.c_double), ("rope_truncate", C.c_int),
     ]
 
 

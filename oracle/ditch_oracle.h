@@ -60,9 +60,21 @@ void or_exp_vec16(const float *x, float *out); /* expVec on 16 lanes */
 void or_gated_silu(float *out, const float *gate, const float *up, size_t n, size_t len,
                    size_t in_stride, size_t out_stride);
 void or_apply_rope(float *x, const float *cos_row, const float *sin_row, size_t dim);
-/* [len][dim/2] RoPE table, f64 angles cast to f32 (src/model.zig:2200-2282).
- * scaling 0 = none, 1 = llama3 (factor, low/high frequency factors and the
- * original context length, src/model.zig:2222-2235). */
+/* RoPE frequency scaling (src/arch.zig:132-142): 0 none, 1 llama3 (factor,
+ * low/high frequency factors, original context length), 2 linear (factor),
+ * 3 yarn (factor, orig_max, beta_fast, beta_slow, truncate,
+ * attention_factor), 4 per-frequency divisors (factors, attention_factor). */
+typedef struct {
+    int scaling;
+    double factor, low_ff, high_ff, orig_max;
+    const float *factors;
+    size_t n_factors;
+    double attention_factor, beta_fast, beta_slow;
+    int truncate;
+} or_rope;
+/* [len][dim/2] RoPE table, f64 angles cast to f32 (src/model.zig:2200-2282). */
+void or_rope_table_ex(float *cos_t, float *sin_t, size_t len, size_t dim, double theta, const or_rope *r);
+/* the same for scaling 0 / 1 / 2 from plain arguments */
 void or_rope_table(float *cos_t, float *sin_t, size_t len, size_t dim, double theta,
                    int scaling, double factor, double low_ff, double high_ff, double orig_max);
 
@@ -113,9 +125,13 @@ typedef struct {
     float eps;
     double rope_theta;
     int qk_norm;           /* 1: per-head RMSNorm of q and k before RoPE (Qwen3) */
-    int rope_scaling;      /* 0 none, 1 llama3 */
+    int rope_scaling;      /* or_rope's scaling codes */
     double rope_factor, rope_low_ff, rope_high_ff, rope_orig_max;
     int n_experts, top_k, moe_inter, norm_topk;
+    const float *rope_factors;
+    size_t n_rope_factors;
+    double rope_attention_factor, rope_beta_fast, rope_beta_slow;
+    int rope_truncate;
 } or_config;
 
 typedef struct {

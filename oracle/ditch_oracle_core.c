@@ -361,29 +361,61 @@ void or_apply_rope(float *x, const float *c, const float *s, size_t dim) {
     }
 }
 
-void or_rope_table(float *cos_t, float *sin_t, size_t len, size_t dim, double theta,
-                   int scaling, double factor, double low_ff, double high_ff, double orig_max) {
+/* fillRope (src/model.zig:2200-2282): inverse frequencies theta^(-2i/dim),
+ * scaled per r->scaling, then cos / sin of the f64 angles times the
+ * attention factor, cast to f32. */
+void or_rope_table_ex(float *cos_t, float *sin_t, size_t len, size_t dim, double theta, const or_rope *r) {
     size_t half = dim / 2;
     double *inv = (double *)malloc(sizeof(double) * (half ? half : 1));
+    double attn = 1.0;
     for (size_t i = 0; i < half; i++) inv[i] = 1.0 / pow(theta, (double)(2 * i) / (double)dim);
-    if (scaling == 1) {
-        double low_wavelen = orig_max / low_ff, high_wavelen = orig_max / high_ff;
+    if (r->scaling == 1) { /* llama3 */
+        double low_wavelen = r->orig_max / r->low_ff, high_wavelen = r->orig_max / r->high_ff;
         for (size_t i = 0; i < half; i++) {
             double wavelen = 2.0 * M_PI / inv[i];
             if (wavelen < high_wavelen) {
             } else if (wavelen > low_wavelen) {
-                inv[i] /= factor;
+                inv[i] /= r->factor;
             } else {
-                double smooth = (orig_max / wavelen - low_ff) / (high_ff - low_ff);
-                inv[i] = (1.0 - smooth) * inv[i] / factor + smooth * inv[i];
+                double smooth = (r->orig_max / wavelen - r->low_ff) / (r->high_ff - r->low_ff);
+                inv[i] = (1.0 - smooth) * inv[i] / r->factor + smooth * inv[i];
             }
         }
+    } else if (r->scaling == 2) { /* linear */
+        for (size_t i = 0; i < half; i++) inv[i] /= r->factor;
+    } else if (r->scaling == 3) { /* yarn: ramp between the correction dims */
+        double d = (double)dim;
+        double lo = d * log(r->orig_max / (r->beta_fast * 2.0 * M_PI)) / (2.0 * log(theta));
+        double hi = d * log(r->orig_max / (r->beta_slow * 2.0 * M_PI)) / (2.0 * log(theta));
+        if (r->truncate) {
+            lo = floor(lo);
+            hi = ceil(hi);
+        }
+        if (lo < 0) lo = 0;
+        if (hi > d - 1) hi = d - 1;
+        if (lo == hi) hi += 0.001;
+        for (size_t i = 0; i < half; i++) {
+            double ramp = ((double)i - lo) / (hi - lo);
+            ramp = ramp < 0 ? 0 : (ramp > 1 ? 1 : ramp);
+            double keep = 1.0 - ramp;
+            inv[i] = inv[i] / r->factor * (1.0 - keep) + inv[i] * keep;
+        }
+        attn = r->attention_factor;
+    } else if (r->scaling == 4) { /* per-frequency divisors */
+        for (size_t i = 0; i < half && i < r->n_factors; i++) inv[i] /= (double)r->factors[i];
+        attn = r->attention_factor;
     }
     for (size_t p = 0; p < len; p++)
         for (size_t i = 0; i < half; i++) {
             double a = (double)p * inv[i];
-            cos_t[p * half + i] = (float)cos(a);
-            sin_t[p * half + i] = (float)sin(a);
+            cos_t[p * half + i] = (float)(cos(a) * attn);
+            sin_t[p * half + i] = (float)(sin(a) * attn);
         }
     free(inv);
+}
+
+void or_rope_table(float *cos_t, float *sin_t, size_t len, size_t dim, double theta,
+                   int scaling, double factor, double low_ff, double high_ff, double orig_max) {
+    or_rope r = {scaling, factor, low_ff, high_ff, orig_max, NULL, 0, 1.0, 32.0, 1.0, 1};
+    or_rope_table_ex(cos_t, sin_t, len, dim, theta, &r);
 }

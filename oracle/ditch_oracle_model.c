@@ -140,8 +140,13 @@ int or_forward(const or_model *m, const uint32_t *tokens, const uint32_t *row_b,
     float *mo = malloc(sizeof(float) * n * H);
     float *kc = malloc(sizeof(float) * B * maxp * kvd), *vc = malloc(sizeof(float) * B * maxp * kvd);
     float *cos_t = malloc(sizeof(float) * maxp * hd / 2), *sin_t = malloc(sizeof(float) * maxp * hd / 2);
-    or_rope_table(cos_t, sin_t, maxp, hd, c->rope_theta, c->rope_scaling, c->rope_factor,
-                  c->rope_low_ff, c->rope_high_ff, c->rope_orig_max);
+    {
+        or_rope r = {c->rope_scaling, c->rope_factor, c->rope_low_ff, c->rope_high_ff, c->rope_orig_max,
+                     c->rope_factors, c->n_rope_factors,
+                     c->rope_attention_factor != 0 ? c->rope_attention_factor : 1.0, c->rope_beta_fast,
+                     c->rope_beta_slow, c->rope_truncate};
+        or_rope_table_ex(cos_t, sin_t, maxp, hd, c->rope_theta, &r);
+    }
     float scale = 1.0f / sqrtf((float)hd);
 
     for (size_t i = 0; i < n; i++) {

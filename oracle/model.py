@@ -52,9 +52,15 @@ class OracleModel:
             rope_low_ff=s.get("rope_low_ff", 1.0), rope_high_ff=s.get("rope_high_ff", 1.0),
             rope_orig_max=s.get("rope_orig_max", 1.0), n_experts=s.get("n_experts", 0),
             top_k=s.get("top_k", 0), moe_inter=s.get("moe_inter", 0),
-            norm_topk=int(s.get("norm_topk", 1)))
+            norm_topk=int(s.get("norm_topk", 1)), rope_attention_factor=s.get("rope_attention_factor", 1.0),
+            rope_beta_fast=s.get("rope_beta_fast", 32.0), rope_beta_slow=s.get("rope_beta_slow", 1.0),
+            rope_truncate=int(s.get("rope_truncate", 1)))
         layers = (Layer * s["n_layers"])()
         keep = []
+        if s.get("rope_factors") is not None:
+            rf = np.ascontiguousarray(s["rope_factors"], np.float32)
+            keep.append(rf)
+            cfg.rope_factors, cfg.n_rope_factors = ptr(rf), rf.size
 
         def g(name):
             a = self.w.get(name)

@@ -84,14 +84,16 @@ def write_gguf(path, arch, meta, tensors):
 
 
 def write_gguf_fixture(path, family):
-    """A GGUF family of the fixtures (qwen2_gguf) as its own GGUF file."""
+    """A GGUF family of the fixtures (qwen2_gguf, llama_gguf: its q / k rows in
+    llama.cpp's order and its rope_freqs.weight, as stored) as its own GGUF file."""
     config, dtypes, shapes, raw = fixture(family)
-    meta = _meta(config, "qwen2")
+    arch = config["model_type"]
+    meta = _meta(config, arch)
     tensors = {}
     for n in sorted(raw):
         shp = shapes.get(n) or list(raw[n].shape)
         tensors[n] = (dtypes[n], raw[n], shp)
-    return write_gguf(path, "qwen2", meta, tensors)
+    return write_gguf(path, arch, meta, tensors)
 
 
 def _meta(config, arch):

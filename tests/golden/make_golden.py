@@ -55,7 +55,7 @@ def read_safetensors(path):
 # ggml type -> (name, elements per block, bytes per block)
 GGML = {0: ("F32", 1, 4), 1: ("F16", 1, 2), 8: ("GGML_Q8_0", 32, 34), 12: ("GGML_Q4_K", 256, 144),
         14: ("GGML_Q6_K", 256, 210), 30: ("BF16", 1, 2)}
-GGUF_FAMILIES = ["qwen2_gguf"]
+GGUF_FAMILIES = ["qwen2_gguf", "llama_gguf"]
 
 
 def read_gguf(path):

@@ -83,6 +83,9 @@ class Golden:
         if rs and rs.get("rope_type") == "llama3":
             s.update(rope_scaling=1, rope_factor=rs["factor"], rope_low_ff=rs["low_freq_factor"],
                      rope_high_ff=rs["high_freq_factor"], rope_orig_max=rs["original_max_position_embeddings"])
+        elif self.gguf and "rope_freqs.weight" in self.raw:
+            # a GGUF file's per-frequency divisors (src/gguf_model.zig:227-228)
+            s.update(rope_scaling=4, rope_factors=np.asarray(self.raw["rope_freqs.weight"], np.float32).ravel())
         if c["model_type"] == "qwen3_moe":
             s.update(n_experts=c["num_experts"], top_k=c["num_experts_per_tok"], moe_inter=c["moe_intermediate_size"],
                      norm_topk=int(c.get("norm_topk_prob", True)))
@@ -94,9 +97,32 @@ class Golden:
                      norm_topk=1, moe_layers=[True] * s["n_layers"])
         return s
 
+    def _heads_permuted(self, name):
+        """Heads of a llama.cpp-permuted q / k tensor of a llama GGUF file, else 0."""
+        if not (self.gguf and self.config["model_type"] in ("llama", "mistral", "mixtral")):
+            return 0
+        if name.endswith("attn_q.weight"):
+            return self.spec["heads"]
+        if name.endswith("attn_k.weight"):
+            return self.spec["kv_heads"]
+        return 0
+
+    @staticmethod
+    def unpermute(a, n_head):
+        """llama.cpp's q / k row permutation undone (src/gguf_model.zig:141-143,
+        700-800): GGUF row (h, i, half) holds Hugging Face row (h, half, i)."""
+        rows = a.shape[0]
+        return np.ascontiguousarray(a.reshape(n_head, rows // n_head // 2, 2, -1).swapaxes(1, 2).reshape(a.shape))
+
     # ---- decoding to f32 (the oracle's view of every weight) ----
     def _dense(self, name):
         """f32 values of a stored weight, decoded like src/dequant.zig does at load."""
+        nh = self._heads_permuted(name)
+        if nh:
+            return self.unpermute(self._dense_raw(name), nh)
+        return self._dense_raw(name)
+
+    def _dense_raw(self, name):
         if name in self.raw:
             dt = self.dtypes[name]
             a = self.raw[name]
@@ -192,6 +218,8 @@ class Golden:
         if first in self.raw:
             dt = self.dtypes[first]
             a = np.stack([self.raw[n] for n in names]) if stack else self.raw[first]
+            if not stack and self._heads_permuted(first):
+                a = self.unpermute(a, self._heads_permuted(first))
             rows, cols = (a.shape[-2], a.shape[-1]) if a.ndim >= 2 else (a.shape[0], 1)
             if dt == "BF16":
                 return Tensor(canon, "bf16", rows, cols, a, slabs=slabs)

@@ -30,7 +30,8 @@ HF_FAMILIES = ["qwen2", "qwen2_fp8", "qwen2_int4", "qwen3", "llama", "mixtral", 
 # permuted llama q / k, stacked experts)
 GGUF_FROM_HF = {"qwen2_bf16_gguf": "qwen2", "llama_gguf": "llama", "qwen3_gguf": "qwen3",
                 "qwen3_moe_gguf": "qwen3_moe", "mixtral_gguf": "mixtral"}
-FILES = HF_FAMILIES + ["qwen2_gguf", "qwen2_gguf_pkg", "llama_gguf_embedded", "llama_gguf_rope_freqs"] + list(GGUF_FROM_HF)
+FILES = HF_FAMILIES + ["qwen2_gguf", "llama_gguf_fixture", "qwen2_gguf_pkg", "llama_gguf_embedded",
+                       "llama_gguf_rope_freqs"] + list(GGUF_FROM_HF)
 # Llama 3's theta: with head_dim 8 its longest wavelength passes 8192 positions,
 # so the largest factor is the scaling factor itself (how ditch recognises it)
 LLAMA3_THETA = 500000.0
@@ -45,6 +46,8 @@ def checkpoint(tmp_path, family):
     path = str(tmp_path / "model.gguf")
     if family == "qwen2_gguf":
         return write_gguf_fixture(path, family)
+    if family == "llama_gguf_fixture":  # the reference's own llama GGUF fixture (per-frequency rope divisors)
+        return write_gguf_fixture(path, "llama_gguf")
     if family == "qwen2_gguf_pkg":
         return write_gguf_with_package(path)
     if family == "llama_gguf_embedded":  # the HF config (llama3 rope included) inside the file
@@ -59,7 +62,8 @@ def checkpoint(tmp_path, family):
 
 
 def golden_spec(family):
-    base = {"qwen2_gguf_pkg": "qwen2_gguf", "llama_gguf_embedded": "llama", "llama_gguf_rope_freqs": "llama"}
+    base = {"qwen2_gguf_pkg": "qwen2_gguf", "llama_gguf_embedded": "llama", "llama_gguf_rope_freqs": "llama",
+            "llama_gguf_fixture": "llama_gguf"}
     g = Golden(base.get(family) or GGUF_FROM_HF.get(family) or family)
     s = dict(g.spec)
     if family in GGUF_FROM_HF:  # GGUF metadata carries no llama3 rope keys
@@ -171,8 +175,9 @@ def test_refusals(tmp_path):
 
 def test_gguf_rope_freqs(tmp_path):
     """rope_freqs.weight equal to Llama 3's standard scaling (low 1, high 4,
-    8192 positions, any factor) becomes that scaling, as ditch recognises it;
-    any other factors are refused rather than dropped."""
+    8192 positions, any factor) becomes that scaling, as ditch recognises it
+    (src/gguf_model.zig:311-326); any other factors are kept as per-frequency
+    divisors (src/gguf_model.zig:227-228, 326-335)."""
     c, _, _, _ = fixture("llama")
     half = c["head_dim"] // 2
     ones = write_llama_gguf(str(tmp_path / "ones.gguf"),
@@ -187,17 +192,48 @@ def test_gguf_rope_freqs(tmp_path):
             spec["rope_orig_max"]) == (1, 32.0, 1.0, 4.0, 8192.0)
     odd = np.arange(1, half + 1, dtype=np.float32)
     path = write_llama_gguf(str(tmp_path / "f.gguf"), extra={"rope_freqs.weight": ("F32", odd, [half])})
-    with pytest.raises(ditch_b200.Unsupported, match="rope_freqs"):
-        ditch_b200.inspect_checkpoint(path)
+    spec, _ = ditch_b200.inspect_checkpoint(path)
+    assert spec["rope_scaling"] == 4
+    np.testing.assert_array_equal(spec["rope_factors"], odd)
 
 
-def test_unsupported_rope_scaling_refused(tmp_path):
+def _rope_of(tmp_path, name, rope_scaling, **extra):
     config, _, _, _ = fixture("qwen2")
-    d = write_hf_dir(str(tmp_path / "dyn"), "qwen2")
+    d = write_hf_dir(str(tmp_path / name), "qwen2")
     with open(os.path.join(d, "config.json"), "w") as f:
-        json.dump(dict(config, rope_scaling={"rope_type": "dynamic", "factor": 2.0}), f)
-    with pytest.raises(ditch_b200.Unsupported, match="dynamic"):
-        ditch_b200.inspect_checkpoint(d)
+        json.dump(dict(config, rope_scaling=rope_scaling, **extra), f)
+    return ditch_b200.inspect_checkpoint(d)[0]
+
+
+def test_rope_scaling_types(tmp_path):
+    """parseRopeScaling (src/arch.zig:1646-1720) for every type the reference
+    reads: linear, yarn (with its default attention factor 0.1 ln(factor) + 1,
+    arch.zig:1722-1725, or mscale / mscale_all_dim), longrope (the short
+    factors, attention factor sqrt(1 + ln(factor) / ln(original))),
+    ditch_factors; dynamic and unknown types read as plain RoPE."""
+    f32 = lambda x: float(np.float32(x))
+    s = _rope_of(tmp_path, "lin", {"rope_type": "linear", "factor": 2.5})
+    assert (s["rope_scaling"], s["rope_factor"]) == (2, 2.5)
+    s = _rope_of(tmp_path, "yarn", {"rope_type": "yarn", "factor": 4.0, "original_max_position_embeddings": 2048})
+    assert (s["rope_scaling"], s["rope_factor"], s["rope_orig_max"]) == (3, 4.0, 2048.0)
+    assert (s["rope_beta_fast"], s["rope_beta_slow"], s["rope_truncate"]) == (32.0, 1.0, 1)
+    assert s["rope_attention_factor"] == pytest.approx(f32(0.1 * np.log(np.float32(4.0)) + 1.0), rel=1e-7)
+    s = _rope_of(tmp_path, "yarn2", {"type": "yarn", "factor": 40, "mscale": 1.0, "mscale_all_dim": 1.0,
+                                     "beta_fast": 16, "beta_slow": 2, "truncate": False})
+    assert s["rope_attention_factor"] == 1.0 and (s["rope_beta_fast"], s["rope_beta_slow"], s["rope_truncate"]) == \
+        (16.0, 2.0, 0)
+    half = fixture("qwen2")[0]["hidden_size"] // fixture("qwen2")[0]["num_attention_heads"] // 2
+    short = [1.0 + 0.25 * i for i in range(half - 1)]  # one short: the last divisor stays 1
+    s = _rope_of(tmp_path, "lr", {"rope_type": "longrope", "short_factor": short, "long_factor": [9.0] * half},
+                 max_position_embeddings=8192, original_max_position_embeddings=2048)
+    assert s["rope_scaling"] == 4
+    np.testing.assert_array_equal(s["rope_factors"], np.asarray(short + [1.0], np.float32))
+    assert s["rope_attention_factor"] == pytest.approx(np.sqrt(1 + np.log(4.0) / np.log(2048.0)), rel=1e-6)
+    s = _rope_of(tmp_path, "df", {"rope_type": "ditch_factors", "factors": [1, 2, 3]})
+    assert s["rope_scaling"] == 4
+    np.testing.assert_array_equal(s["rope_factors"], np.asarray([1, 2, 3], np.float32))
+    for name, rs in (("dyn", {"rope_type": "dynamic", "factor": 2.0}), ("unk", {"rope_type": "su", "factor": 2.0})):
+        assert _rope_of(tmp_path, name, rs).get("rope_scaling", 0) == 0
 
 
 def test_safetensors_header_is_parsed_not_trusted(tmp_path):

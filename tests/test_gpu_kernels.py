@@ -195,6 +195,50 @@ def test_edit_weight_bf16(device):
     assert np.abs(r @ got).max() < np.abs(r @ wf).max() * (1 - alpha) + 1e-3
 
 
+@pytest.mark.parametrize("rows,cols", [(37, 264), (130, 8), (1000, 4104), (4099, 520)])
+def test_edit_weight_bf16_shapes(device, rows, cols):
+    """The piece-wise GEMV-T and the rank-1 update at ragged shapes: rows not a
+    multiple of the 8 row lanes or of a 64-row run, columns that leave the
+    last 256-column block part empty."""
+    torch = pytest.importorskip("torch")
+    w32 = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    wb = oracle.f32_to_bf16_bits(w32)
+    r = rng.standard_normal(rows).astype(np.float32)
+    r /= np.linalg.norm(r)
+    wt = torch.from_numpy(wb.view(np.int16).copy()).cuda()
+    device.edit_weight_bf16(wt.data_ptr(), rows, cols, torch.from_numpy(r).cuda().data_ptr(), 0.5)
+    got = oracle.bf16_bits_to_f32(wt.cpu().numpy().view(np.uint16))
+    wf = oracle.bf16_bits_to_f32(wb)
+    a, b = oracle.compute_delta_none(wf, r, 0.5)
+    close(got, oracle.materialize(wf, a, b), 2e-5, 8e-3)
+
+
+@pytest.mark.parametrize("hidden,inter,block", [(256, 1040, (128, 16)), (200, 520, (64, 128)), (512, 4608, (128, 128)),
+                                                (264, 4128, (16, 32))])
+def test_edit_delta_fp8_matches_oracle(device, hidden, inter, block):
+    """A = v^T W over FP8 block-scaled weights (the decoded bf16 operand) at
+    shapes that take the piece kernel (columns a multiple of 16) and the
+    byte-wise one (520 columns), against the oracle's matvecTMulti."""
+    from synth import make_model
+    import ditch_b200
+    spec, w, tensors = make_model(970 + hidden, n_layers=1, hidden=hidden, heads=4, kv_heads=2,
+                                  head_dim=hidden // 4, inter=inter, fmt="fp8", block=block)
+    m = ditch_b200.Model(device, spec, tensors, max_seq=16)
+    dirs = rng.standard_normal((2, hidden)).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    m.set_directions(dirs)
+    p = (1.0, 0.0, 1.0, 1.0)
+    lam = oracle.kernel_weight(p, 0)
+    assert lam is not None
+    m.apply_edit(p, p)
+    for comp, name in (("o", "attn_o_proj"), ("down", "mlp_down_proj")):
+        a, _ = oracle.compute_delta_none(w[f"L0.{comp}"], dirs[1], lam)
+        da, _ = m.delta(0, name)
+        got = np.asarray(da[0][: a.size])
+        assert np.abs(got - a).max() <= 1e-5 * np.abs(a).max() + 1e-8, comp
+    m.close()
+
+
 def test_edit_weight_bf16_rejects_odd_pointers(device):
     """w must start on a 2-byte boundary and r on a 4-byte one; the check comes
     before any launch (these dummy pointers are never dereferenced)."""

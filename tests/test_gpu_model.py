@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 
 FWD_ATOL, FWD_RTOL = 2e-3, 2e-2
 DENSE = ["qwen2", "llama", "qwen3", "qwen2_fp8", "qwen2_int4", "qwen3_moe", "qwen3_moe_big", "qwen3_moe_fused",
-         "qwen3_moe_fused_t", "mixtral", "qwen2_gguf"]
+         "qwen3_moe_fused_t", "mixtral", "qwen2_gguf", "llama_gguf"]
 
 
 def bound(want):

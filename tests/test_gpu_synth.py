@@ -1,7 +1,7 @@
 """The resident forward on seeded synthetic models against the oracle, at the
 shapes the reference fixtures do not reach: head sizes 64 and 128 (the tiled
 attention kernel), prompts longer than one 64-row chunk, GQA, q/k norms, FP8
-block weights, and MXFP4 routed experts.
+block weights, MXFP4 routed experts, and every RoPE scaling type.
 
 Tolerance as in test_gpu_model.py: max |err| <= 2e-3 + 2e-2 * max |ref|."""
 import numpy as np
@@ -52,6 +52,36 @@ def test_synthetic_dense_forward(device, case):
     spec, f32, tensors = make_model(100 + case, **kw)
     ps = prompts(7 + case, [1, 5, 64, 65, 150, 33], spec["vocab"])
     check_forward(device, spec, f32, tensors, ps)
+
+
+ROPES = [
+    dict(rope_scaling=2, rope_factor=2.5),
+    dict(rope_scaling=3, rope_factor=4.0, rope_orig_max=32.0, rope_beta_fast=32.0, rope_beta_slow=1.0,
+         rope_truncate=1, rope_attention_factor=float(np.float32(0.1 * np.log(4.0) + 1.0))),
+    dict(rope_scaling=3, rope_factor=8.0, rope_orig_max=64.0, rope_beta_fast=16.0, rope_beta_slow=2.0,
+         rope_truncate=0, rope_attention_factor=1.2),
+    dict(rope_scaling=4, rope_factors=32, rope_attention_factor=1.0),
+    dict(rope_scaling=4, rope_factors=27, rope_attention_factor=1.15),  # fewer divisors than frequencies
+]
+
+
+@pytest.mark.parametrize("case", range(len(ROPES)))
+def test_rope_scalings_match_oracle(device, case):
+    """Linear, YaRN (truncated and not) and per-frequency divisors (GGUF
+    rope_freqs, LongRoPE) against the oracle's fillRope (src/model.zig:
+    2200-2282); plain RoPE is outside the bound at these positions, so the
+    scaling is what the check measures."""
+    spec, f32, tensors = make_model(200 + case, head_dim=64, heads=4, kv_heads=2, hidden=256)
+    r = dict(ROPES[case])
+    if "rope_factors" in r:
+        r["rope_factors"] = np.random.default_rng(210 + case).uniform(1.0, 8.0, r["rope_factors"]).astype(np.float32)
+    scaled = dict(spec, **r)
+    ps = prompts(220 + case, [1, 40, 150], spec["vocab"])
+    check_forward(device, scaled, f32, tensors, ps)
+    toks, rb, rp, cap, first, take, last = flatten_batch(ps, 2)
+    _, a = OracleModel(scaled, f32).forward(toks, rb, rp, cap, last)
+    _, b = OracleModel(spec, f32).forward(toks, rb, rp, cap, last)
+    assert max(np.abs(a[i] - b[i]).max() - (2e-3 + 2e-2 * np.abs(a[i]).max()) for i in range(len(ps))) > 0
 
 
 @pytest.mark.parametrize("fmt,staging", [("bf16", 1024), ("mxfp4", 1024), ("mxfp4", 0)])

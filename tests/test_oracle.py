@@ -15,7 +15,7 @@ from golden_loader import Golden
 from oracle.model import OracleModel, flatten_batch
 
 FAMILIES = ["qwen2", "llama", "qwen3", "qwen3_moe", "qwen2_fp8", "qwen2_int4", "qwen3_moe_big", "qwen3_moe_fused",
-            "qwen3_moe_fused_t", "mixtral", "qwen2_gguf"]
+            "qwen3_moe_fused_t", "mixtral", "qwen2_gguf", "llama_gguf"]
 
 
 @pytest.mark.parametrize("family", FAMILIES)
