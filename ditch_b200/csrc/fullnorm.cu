@@ -10,6 +10,16 @@
 // host in f32 in the reference's order. The random test matrix is seeded
 // (SplitMix64 and Box-Muller) but is not the reference's random sequence: the
 // two sketches give the same delta up to the randomised SVD's accuracy.
+//
+// Under tensor parallelism a rank holds a column shard of the matrix (o_proj
+// and down_proj are split by columns). The products over columns (W a, D X,
+// a . x) are partial sums on each rank, summed over the group in rank order;
+// the column-space vectors (a, the D^T Y sketches) are gathered whole, so
+// Gram-Schmidt, the Gram matrices and the eigenproblem run on full vectors,
+// the same on every rank; each rank keeps its columns of the delta's A and
+// all of B. The random test matrix is drawn for all columns, so the sketch
+// is the one a single GPU draws; the results agree with one GPU up to the
+// order of the partial sums.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -196,13 +206,56 @@ struct Operator {
     }
 };
 
+// Tensor-parallel helpers: the sum of every rank's `v` in rank order (f32
+// widened to f64 for the group's reduction, the same bits on every rank),
+// and the concatenation of every rank's column slice.
+int tp_sum(ditch_cuda_model *m, std::vector<float> &v) {
+    ditch_cuda_device *dev = m->dev;
+    std::vector<double> h(v.begin(), v.end());
+    DITCH_CUDA(m->fn_red.reserve(2 * h.size() * 8));
+    double *src = m->fn_red.as<double>(), *dst = src + h.size();
+    DITCH_CUDA(cudaMemcpyAsync(src, h.data(), h.size() * 8, cudaMemcpyHostToDevice, dev->stream));
+    int s;
+    if ((s = dp_allreduce_sum(dev, m->group, src, h.size(), dst))) return s;
+    DITCH_CUDA(cudaMemcpyAsync(h.data(), dst, h.size() * 8, cudaMemcpyDeviceToHost, dev->stream));
+    if ((s = check_status(dev, "tensor-parallel full normalisation"))) return s;
+    for (size_t i = 0; i < v.size(); i++) v[i] = (float)h[i];
+    return DITCH_CUDA_OK;
+}
+
+// local [q][cols] (columns [rank cols, (rank + 1) cols) of the whole) to
+// full [q][world cols]
+int tp_gather(ditch_cuda_model *m, const std::vector<float> &local, int q, int cols, std::vector<float> &full) {
+    const int W = m->cfg.tp_world, r = m->cfg.tp_rank;
+    full.assign((size_t)q * cols * W, 0.0f);
+    for (int j = 0; j < q; j++)
+        std::memcpy(&full[((size_t)j * W + r) * cols], &local[(size_t)j * cols], (size_t)cols * 4);
+    return tp_sum(m, full);
+}
+
+void tp_slice(const std::vector<float> &full, int q, int cols, int W, int r, std::vector<float> &local) {
+    local.resize((size_t)q * cols);
+    for (int j = 0; j < q; j++)
+        std::memcpy(&local[(size_t)j * cols], &full[((size_t)j * W + r) * cols], (size_t)cols * 4);
+}
+
 }  // namespace
 
 int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn, const float *v_dev, float lambda,
                     int lora_rank, uint64_t seed, float *a_out, float *b_out, int *rank_out) {
     ditch_cuda_device *dev = m->dev;
     const int rows = m->cfg.hidden, cols = w.cols;
+    const bool tp = m->cfg.tp_world > 1;
+    const int W = tp ? m->cfg.tp_world : 1, tr = tp ? m->cfg.tp_rank : 0, cols_all = cols * W;
     int s;
+    if (tp) {
+        if (!m->group) {
+            set_error("tensor-parallel model without its peer group");
+            return DITCH_CUDA_INVALID;
+        }
+        // every peer has finished reading the region (the forward's last reduction)
+        if ((s = group_exchange(dev, m->group, 30.0))) return s;
+    }
     // a = (v / n)^T W on the device, then n, v, a on the host
     DITCH_CUDA(m->vn.reserve((size_t)rows * 4));
     DevBuf &scratch = m->fn_s, &adev = m->fn_a;
@@ -217,12 +270,17 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
     DITCH_CUDA(cudaStreamSynchronize(dev->stream));
     // wa = W a (through the operator with c = 1, d = 0), gram = a . a
     std::vector<float> ones(rows, 1.0f), zeros(rows, 0.0f), c(rows), d(rows);
-    std::vector<float> wa;
+    std::vector<float> wa, a_all;
     {
         Operator plain{m, w, row0, rows, cols, a, ones, zeros, m->fn_act, m->fn_out, m->fn_y, m->fn_x};
         if ((s = plain.apply(a, 1, wa))) return s;
     }
-    const float gram = dotf(a.data(), a.data(), cols);
+    if (tp) {
+        if ((s = tp_sum(m, wa))) return s;
+        if ((s = tp_gather(m, a, 1, cols, a_all))) return s;
+    }
+    const std::vector<float> &af = tp ? a_all : a;
+    const float gram = dotf(af.data(), af.data(), cols_all);
     for (int i = 0; i < rows; i++) {
         const float bij = -lambda * v[i];
         const float wn_dot_a = n[i] > 0.0f ? wa[i] / n[i] : 0.0f;
@@ -235,30 +293,48 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
     }
     // randomised SVD of D (q sketch vectors, 6 power iterations)
     const int r = std::max(lora_rank, 1);
-    const int q = std::min(2 * r + 4, std::min(rows, cols));
+    const int q = std::min(2 * r + 4, std::min(rows, cols_all));
     Operator op{m, w, row0, rows, cols, a, c, d, m->fn_act, m->fn_out, m->fn_y, m->fn_x};
     Normal rng{seed};
-    std::vector<float> omega((size_t)q * cols), qy, qx, bt;
+    std::vector<float> omega((size_t)q * cols_all), qy, qx, bt, full;
     for (float &x : omega) x = rng();
-    if ((s = op.apply(omega, q, qy))) return s;
+    // D X over this rank's columns, summed over the group
+    auto apply = [&](const std::vector<float> &x_all, std::vector<float> &y) -> int {
+        int st;
+        if (!tp) return op.apply(x_all, q, y);
+        std::vector<float> x;
+        tp_slice(x_all, q, cols, W, tr, x);
+        if ((st = op.apply(x, q, y))) return st;
+        return tp_sum(m, y);
+    };
+    // D^T Y, this rank's columns gathered whole
+    auto apply_t = [&](const std::vector<float> &y, std::vector<float> &x_all) -> int {
+        int st;
+        if (!tp) return op.apply_t(y, q, x_all);
+        std::vector<float> x;
+        if ((st = op.apply_t(y, q, x))) return st;
+        return tp_gather(m, x, q, cols, x_all);
+    };
+    if ((s = apply(omega, qy))) return s;
     orthonormalize(qy, q, rows);
     for (int it = 0; it < 6; it++) {
-        if ((s = op.apply_t(qy, q, qx))) return s;
-        orthonormalize(qx, q, cols);
-        if ((s = op.apply(qx, q, qy))) return s;
+        if ((s = apply_t(qy, qx))) return s;
+        orthonormalize(qx, q, cols_all);
+        if ((s = apply(qx, qy))) return s;
         orthonormalize(qy, q, rows);
     }
-    if ((s = op.apply_t(qy, q, bt))) return s;  // B^T = D^T Q
+    if ((s = apply_t(qy, bt))) return s;  // B^T = D^T Q
     std::vector<float> bbt((size_t)q * q), evecs;
     for (int i = 0; i < q; i++)
-        for (int j = 0; j < q; j++) bbt[(size_t)i * q + j] = dotf(&bt[(size_t)i * cols], &bt[(size_t)j * cols], cols);
+        for (int j = 0; j < q; j++)
+            bbt[(size_t)i * q + j] = dotf(&bt[(size_t)i * cols_all], &bt[(size_t)j * cols_all], cols_all);
     jacobi_eigen(bbt, evecs, q);
     std::vector<int> order(q);
     std::iota(order.begin(), order.end(), 0);
     std::stable_sort(order.begin(), order.end(),
                      [&](int x, int y) { return bbt[(size_t)x * q + x] > bbt[(size_t)y * q + y]; });
     const int rank = std::min(r, q);
-    std::vector<float> la((size_t)rank * cols, 0.0f), lb((size_t)rows * rank, 0.0f), uk(rows), vk(cols);
+    std::vector<float> la((size_t)rank * cols_all, 0.0f), lb((size_t)rows * rank, 0.0f), uk(rows), vk(cols_all);
     for (int k = 0; k < rank; k++) {
         const int src = order[k];
         const float sk = std::sqrt(std::max(bbt[(size_t)src * q + src], 0.0f));
@@ -266,7 +342,7 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
         std::fill(vk.begin(), vk.end(), 0.0f);
         for (int i = 0; i < q; i++) {
             axpyf(uk.data(), evecs[(size_t)i * q + src], &qy[(size_t)i * rows], rows);
-            axpyf(vk.data(), evecs[(size_t)i * q + src], &bt[(size_t)i * cols], cols);
+            axpyf(vk.data(), evecs[(size_t)i * q + src], &bt[(size_t)i * cols_all], cols_all);
         }
         if (sk > 1e-12f) {
             const float inv = 1.0f / sk;
@@ -275,8 +351,15 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
             std::fill(vk.begin(), vk.end(), 0.0f);
         }
         const float sq = std::sqrt(std::max(sk, 0.0f));
-        for (int j = 0; j < cols; j++) la[(size_t)k * cols + j] = sq * vk[j];
+        for (int j = 0; j < cols_all; j++) la[(size_t)k * cols_all + j] = sq * vk[j];
         for (int i = 0; i < rows; i++) lb[(size_t)i * rank + k] = uk[i] * sq;
+    }
+    if (tp) {
+        std::vector<float> mine;
+        tp_slice(la, rank, cols, W, tr, mine);
+        la.swap(mine);
+        // every peer has finished reading the region before the next forward writes it
+        if ((s = group_exchange(dev, m->group, 30.0))) return s;
     }
     DITCH_CUDA(cudaMemcpyAsync(a_out, la.data(), la.size() * 4, cudaMemcpyHostToDevice, dev->stream));
     DITCH_CUDA(cudaMemcpyAsync(b_out, lb.data(), lb.size() * 4, cudaMemcpyHostToDevice, dev->stream));

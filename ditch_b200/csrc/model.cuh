@@ -150,6 +150,7 @@ struct ditch_cuda_model {
     uint64_t edit_seed = 0, seed_counter = 0;  // full: the sketch seed of each matrix is seed + its index
     ditch::DevBuf vn;    // f32 [H]: v / ||W_i|| of the pre-normalised edit
     ditch::DevBuf fn_act, fn_out, fn_y, fn_x, fn_a, fn_s;  // full-mode scratch
+    ditch::DevBuf fn_red;                                  // full mode under TP: the group reductions' f64 values
     ditch::Batch work;   // scratch batch for forward / residual passes
     ditch::DevBuf sums;       // f64 residual sums
     ditch::DevBuf sums_part;  // the prompt runs' partial sums of one batch
@@ -201,6 +202,9 @@ int tp_row_norms(ditch_cuda_model *m, const Mat &w, float *out);
 // Expert scores of this rank's routed experts (`local` [e_loc]) gathered from
 // every rank of the model's peer group into `all` [n_experts].
 int ep_allgather_scores(ditch_cuda_model *m, const std::vector<float> &local, std::vector<float> &all);
+// Whether any rank of the model's expert-parallel group still has prompts to
+// decode (one exchange; every rank calls it at the same step).
+int ep_any_active(ditch_cuda_model *m, size_t local_active, bool *any);
 
 // The split-bf16 router operand from f32 router weights [E][hidden] (device).
 int build_router_split(ditch_cuda_device *dev, const float *router_f32, int E, int hidden, Mat &out);

@@ -1247,11 +1247,6 @@ int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_
     clear_error();
     REQUIRE(m, "null model");
     REQUIRE(mode >= 0 && mode <= 2, "row normalisation %d is not none (0), pre (1) or full (2)", mode);
-    if (mode == 2 && m->cfg.tp_world > 1) {
-        // the randomised SVD's products over column shards would need collectives of their own
-        set_error("row_normalization = full under tensor parallelism is not supported");
-        return DITCH_CUDA_UNSUPPORTED;
-    }
     if (mode == 2) {
         REQUIRE(lora_rank >= 1 && lora_rank <= (size_t)kMaxDeltaRank, "lora_rank %zu is not within 1..%d", lora_rank,
                 kMaxDeltaRank);
@@ -1287,11 +1282,14 @@ int ditch_cuda_generate(ditch_cuda_model *m, const uint32_t *tokens, const size_
     std::lock_guard<std::mutex> lk(dev->mu);
     DITCH_CUDA(cudaSetDevice(dev->ordinal));
     const Config &c = m->cfg;
-    if (c.ep_world > 1) {
-        // ranks would leave the per-layer exchanges at different steps
-        set_error("generation under expert parallelism is not supported");
-        return DITCH_CUDA_UNSUPPORTED;
-    }
+    // Expert parallelism: every rank generates for its own prompts, and every
+    // MoE layer of every step exchanges rows with every rank, so all ranks
+    // take the same number of decode steps: before each step they agree
+    // whether any rank still has an active prompt, and a rank whose prompts
+    // have all finished runs the step on one placeholder row (slot 0,
+    // position 0, token 0; its cache entry and logits are never read).
+    const bool ep = c.ep_world > 1;
+    REQUIRE(!ep || m->group, "expert parallelism without a peer group (ditch_cuda_model_set_group)");
     const size_t P = n_prompts;
     size_t longest = 0;
     for (size_t p = 0; p < P; p++) {
@@ -1353,7 +1351,14 @@ int ditch_cuda_generate(ditch_cuda_model *m, const uint32_t *tokens, const size_
     // decode steps over the active prompts, one row each at its next position
     std::vector<uint32_t> toks;
     std::vector<int> lr;
-    for (size_t step = 1; step < max_new_tokens && n_active > 0; step++) {
+    for (size_t step = 1; step < max_new_tokens; step++) {
+        if (ep) {
+            bool any = false;
+            if ((s = ep_any_active(m, n_active, &any))) return s;
+            if (!any) break;
+        } else if (n_active == 0) {
+            break;
+        }
         toks.clear();
         rb.clear();
         rp.clear();
@@ -1364,6 +1369,12 @@ int ditch_cuda_generate(ditch_cuda_model *m, const uint32_t *tokens, const size_
             toks.push_back(out_tokens[i * stride + count[i] - 1]);
             rb.push_back((int)i);
             rp.push_back((int)pos[i]);
+        }
+        if (toks.empty()) {  // expert parallelism: the placeholder row
+            lr.push_back(0);
+            toks.push_back(0);
+            rb.push_back(0);
+            rp.push_back(0);
         }
         const int n = (int)toks.size();
         b.n = n;
@@ -1378,6 +1389,7 @@ int ditch_cuda_generate(ditch_cuda_model *m, const uint32_t *tokens, const size_
         DITCH_LAUNCH(dev, argmax_rows(m->logits.as<float>(), n, V, m->gen_next.as<uint32_t>(), st));
         DITCH_CUDA(cudaMemcpyAsync(next.data(), m->gen_next.ptr, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
         DITCH_CUDA(cudaStreamSynchronize(st));
+        if (n_active == 0) continue;  // the placeholder's token is dropped
         int j = 0;
         for (size_t i = 0; i < P; i++) {
             if (!active[i]) continue;

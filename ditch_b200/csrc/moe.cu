@@ -774,25 +774,49 @@ int moe_mlp_ep(ditch_cuda_model *m, Layer &L, int n) {
     return DITCH_CUDA_OK;
 }
 
-int ep_allgather_scores(ditch_cuda_model *m, const std::vector<float> &local, std::vector<float> &all) {
+// Every rank's `per_rank` values (this rank's `local`) gathered in rank order
+// through the layout's score area (two halves used in turn: a rank is at most
+// one exchange ahead of another, so it never overwrites the half a peer is
+// still reading).
+static int ep_allgather_f32(ditch_cuda_model *m, const float *local, int per_rank, std::vector<float> &all) {
     ditch_cuda_device *dev = m->dev;
     cudaStream_t st = dev->stream;
     const Config &c = m->cfg;
     ditch_cuda_group *g = m->group;
-    const int E = c.n_experts, El = c.e_loc;
-    EP_REQUIRE((int)local.size() == El, "local scores size");
+    const int E = c.n_experts, W = g->world;
+    EP_REQUIRE(per_rank >= 0 && (size_t)per_rank * W <= (size_t)E, "%d values per rank exceed the score area",
+               per_rank);
     const EpLayout lay = ep_layout(c, m->group_tokens);
     const size_t off = lay.scores + (size_t)m->ep_score_parity * E * 4;
     m->ep_score_parity ^= 1;
-    DITCH_CUDA(m->ep_scores.reserve((size_t)El * 4));
-    DITCH_CUDA(cudaMemcpyAsync(m->ep_scores.ptr, local.data(), (size_t)El * 4, cudaMemcpyHostToDevice, st));
-    k_ep_put_scores<<<g->world, 256, 0, st>>>(m->ep_scores.as<float>(), El, g->rank, g->peers, off);
+    DITCH_CUDA(m->ep_scores.reserve((size_t)std::max(per_rank, 1) * 4));
+    DITCH_CUDA(cudaMemcpyAsync(m->ep_scores.ptr, local, (size_t)per_rank * 4, cudaMemcpyHostToDevice, st));
+    k_ep_put_scores<<<W, 256, 0, st>>>(m->ep_scores.as<float>(), per_rank, g->rank, g->peers, off);
     DITCH_LAUNCH(dev, cudaGetLastError());
     int s;
     if ((s = ep_exchange(m))) return s;
-    all.assign(E, 0.0f);
-    DITCH_CUDA(cudaMemcpyAsync(all.data(), peer_data(g->base) + off, (size_t)E * 4, cudaMemcpyDeviceToHost, st));
-    return check_status(dev, "expert score exchange");
+    all.assign((size_t)per_rank * W, 0.0f);
+    DITCH_CUDA(cudaMemcpyAsync(all.data(), peer_data(g->base) + off, all.size() * 4, cudaMemcpyDeviceToHost, st));
+    DITCH_CUDA(cudaStreamSynchronize(st));
+    return DITCH_CUDA_OK;
+}
+
+int ep_allgather_scores(ditch_cuda_model *m, const std::vector<float> &local, std::vector<float> &all) {
+    EP_REQUIRE((int)local.size() == m->cfg.e_loc, "local scores size");
+    int s;
+    if ((s = ep_allgather_f32(m, local.data(), m->cfg.e_loc, all))) return s;
+    return check_status(m->dev, "expert score exchange");
+}
+
+int ep_any_active(ditch_cuda_model *m, size_t local_active, bool *any) {
+    const float v = local_active ? 1.0f : 0.0f;
+    std::vector<float> all;
+    int s;
+    if ((s = ep_allgather_f32(m, &v, 1, all))) return s;
+    if ((s = check_status(m->dev, "generation step agreement"))) return s;
+    *any = false;
+    for (float x : all) *any |= x != 0.0f;
+    return DITCH_CUDA_OK;
 }
 
 }  // namespace ditch

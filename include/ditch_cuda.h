@@ -280,9 +280,13 @@ int ditch_cuda_forward(ditch_cuda_model *m, const uint32_t *tokens, const uint32
  * (row-major), their number per prompt to out_counts [n_prompts]. The
  * argmax keeps the first maximum (src/model.zig:5194-5204). The longest
  * prompt plus max_new_tokens must fit the positions the model was loaded
- * for. Under expert parallelism it returns DITCH_CUDA_UNSUPPORTED. This is
- * the device half of KeywordRate (src/scorers.zig:95-155); detokenising and
- * the keyword match stay on the host. */
+ * for. Under expert parallelism every rank of the group calls it at the same
+ * time with its own prompts (at least one) and the same max_new_tokens: the
+ * ranks agree before each decode step whether any rank still decodes, and a
+ * rank whose prompts have finished runs that step on one placeholder row so
+ * the MoE exchanges stay matched; the prefill's tokens must fit the group's
+ * max_tokens. This is the device half of KeywordRate (src/scorers.zig:95-155);
+ * detokenising and the keyword match stay on the host. */
 int ditch_cuda_generate(ditch_cuda_model *m, const uint32_t *tokens, const size_t *prompt_offsets, size_t n_prompts,
                         size_t max_new_tokens, const uint32_t *eos_ids, size_t n_eos, uint32_t *out_tokens,
                         size_t *out_counts);
@@ -329,7 +333,10 @@ int ditch_cuda_apply_edit(ditch_cuda_model *m, const ditch_cuda_params *attn_o, 
  * expert, the k of its seed counted as on one device, so expert-parallel
  * ranks agree with a single GPU. On tensor-parallel ranks pre takes the row
  * norms over all ranks' column shards (a collective of the group: every rank
- * edits alike); full there returns DITCH_CUDA_UNSUPPORTED. */
+ * edits alike), and full runs the randomised SVD over the shards: the
+ * products over columns summed over the group, the column vectors gathered
+ * whole, the same sketch as one GPU (collectives of the group in every edit:
+ * every rank applies the same edits in the same order). */
 int ditch_cuda_set_row_normalization(ditch_cuda_model *m, int mode, size_t lora_rank, uint64_t seed);
 /* moe.applyExpertSelective, ranked selection (src/moe.zig:1373-1477): the
  * o_proj edit as above, then per MoE layer the top n_experts experts by

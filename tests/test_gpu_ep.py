@@ -92,10 +92,20 @@ def _worker(rank, world, port, out_dir):
         m.set_row_normalization("none")
     order1 = one.rank_experts(1, dirs[2])
     order2 = ep.rank_experts(1, dirs[2])
+    # greedy generation with the edited experts: the same tokens as one GPU.
+    # Odd ranks stop early on an EOS (the second token of each of their
+    # prompts), so their later steps run on the placeholder row while the
+    # other ranks still decode.
+    first = one.generate(ps, 6)
+    eos = sorted({int(t[1]) for t in first if len(t) > 1}) if rank % 2 else []
+    gen1 = one.generate(ps, 6, eos_ids=eos)
+    gen2 = ep.generate(ps, 6, eos_ids=eos)
+    flat = lambda g: np.concatenate([np.asarray(t, np.int64) for t in g] + [np.asarray([len(t) for t in g])])
     group.barrier()
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), res1=res1, log1=log1, res2=res2, log2=log2, res3=res3, log3=log3,
              res4=res4, log4=log4, res5=res5, log5=log5, res6=res6, log6=log6, order1=np.asarray(order1[0]),
-             order2=np.asarray(order2[0]))
+             order2=np.asarray(order2[0]), gen1=flat(gen1), gen2=flat(gen2),
+             early=np.asarray([int(rank % 2 == 1 and any(len(t) < 6 for t in gen1))]))
     ep.close()
     one.close()
     dist.barrier()
@@ -122,3 +132,5 @@ def test_expert_parallel_forward_equals_one_gpu(tmp_path, world):
         assert not np.array_equal(z["log1"], z["log3"]), "the edit changed nothing"
         assert not np.array_equal(z["log3"], z["log5"]), "full row normalisation changed nothing"
         assert np.array_equal(z["order1"], z["order2"])
+        assert np.array_equal(z["gen1"], z["gen2"]), r
+    assert any(int(np.load(tmp_path / f"r{r}.npz")["early"][0]) for r in range(1, world, 2)), "no rank stopped early"

@@ -10,7 +10,9 @@ the results agree to rounding: within the forward bound of
 `test_gpu_model.py`, max |err| <= 2e-3 + 2e-2 max |ref|, and in practice far
 closer. The none-mode edit of o_proj / down_proj is local to each shard
 (src/abliterate.zig:264-280: A = v^T W splits by columns with W), so the
-edited forward must agree the same way.
+edited forward must agree the same way; so must the pre-normalised edit (row
+norms summed over the shards) and the full one (src/abliterate.zig:324-350:
+its randomised SVD over the column shards, the same sketch as one GPU).
 
 Each world size needs that many GPUs; skipped otherwise."""
 import os
@@ -85,11 +87,20 @@ def _worker(rank, world, port, out_dir):
         m.apply_edit((1.2, 1.5, 0.5, 2.0), (1.1, 1.0, 0.4, 2.0), None)
     res5, log5 = one.forward(toks, rb, rp, cap, last)
     res6, log6 = tp.forward(toks, rb, rp, cap, last)
+    # row_normalization = full (the product default): the randomised SVD of
+    # each matrix's delta over the column shards, with the partial sums over
+    # columns reduced over the group and the column vectors gathered whole
+    for m in (one, tp):
+        m.set_row_normalization("full", lora_rank=2, seed=5)
+        m.apply_edit((1.2, 1.5, 0.5, 2.0), (1.1, 1.0, 0.4, 2.0), None)
+    res7, log7 = one.forward(toks, rb, rp, cap, last)
+    res8, log8 = tp.forward(toks, rb, rp, cap, last)
     for m in (one, tp):
         m.set_row_normalization("none")
     group.barrier()
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), res1=res1, log1=log1, res2=res2, log2=log2, res3=res3, log3=log3,
-             res4=res4, log4=log4, res5=res5, log5=log5, res6=res6, log6=log6)
+             res4=res4, log4=log4, res5=res5, log5=log5, res6=res6, log6=log6, res7=res7, log7=log7, res8=res8,
+             log8=log8)
     tp.close()
     one.close()
     dist.barrier()
@@ -110,10 +121,10 @@ def test_tensor_parallel_forward_matches_one_gpu(tmp_path, world):
     z = [np.load(tmp_path / f"r{r}.npz") for r in range(world)]
     z0 = z[0]
     for r in range(1, world):
-        for key in ("res2", "log2", "res4", "log4", "res6", "log6"):
+        for key in ("res2", "log2", "res4", "log4", "res6", "log6", "res8", "log8"):
             assert np.array_equal(z0[key], z[r][key]), (r, key)  # replicated streams are identical
     for a, b in (("res1", "res2"), ("log1", "log2"), ("res3", "res4"), ("log3", "log4"), ("res5", "res6"),
-                 ("log5", "log6")):
+                 ("log5", "log6"), ("res7", "res8"), ("log7", "log8")):
         ref, got = z0[a], z0[b]
         err = float(np.abs(got - ref).max())
         bound = 2e-3 + 2e-2 * float(np.abs(ref).max())
@@ -121,3 +132,4 @@ def test_tensor_parallel_forward_matches_one_gpu(tmp_path, world):
         print(f"{a} vs {b}: max |err| {err:.3e} (bound {bound:.3e})")
     assert not np.array_equal(z0["log1"], z0["log3"]), "the edit changed nothing"
     assert not np.array_equal(z0["log3"], z0["log5"]), "row normalisation changed nothing"
+    assert not np.array_equal(z0["log5"], z0["log7"]), "full row normalisation changed nothing"
