@@ -441,8 +441,9 @@ __global__ void k_scale_vec(const float *v, float lambda, int n, float *b) {
 // reference takes the exp in f64: the terms differ by one f32 rounding, about
 // 6e-8 relative, far below the f32 result's own rounding after the log).
 // The KL pieces then add exp(b)(b - (x - lse)) in f64 (src/scorers.zig:
-// 385-400; exp(b) again f32 expf widened) and one thread per row adds the
-// pieces in order. The pieces depend only on the vocabulary size, so the sums
+// 385-400: the reference forms each term in f64; here the term is an f32
+// product of f32 expf and the f32 difference, widened before the f64 sum)
+// and one thread per row adds the pieces in order. The pieces depend only on the vocabulary size, so the sums
 // are the same for any batch.
 constexpr int kKlThreads = 256, kKlEach = 16, kKlPiece = kKlThreads * kKlEach;
 
@@ -493,12 +494,18 @@ __global__ void __launch_bounds__(kKlThreads) k_lse_part(const float *x, int voc
     if (threadIdx.x == 0) part[(long long)row * chunks + c] = make_double2((double)m, s);
 }
 
-__device__ __forceinline__ float row_lse_from_parts(const double2 *part, int chunks) {
+// The row's log-sum-exp from its pieces, by one whole warp (each lane a
+// stride of the pieces, then shuffles): the same bits wherever it is called,
+// so the baseline's log-probs and the KL's see the same value.
+__device__ __forceinline__ float row_lse_warp(const double2 *part, int chunks) {
+    const int lane = threadIdx.x & 31;
     float m = -INFINITY;
-    for (int c = 0; c < chunks; c++) m = fmaxf(m, (float)part[c].x);
+    for (int c = lane; c < chunks; c += 32) m = fmaxf(m, (float)part[c].x);
+    m = warp_max(m);
     double s = 0.0;
-    for (int c = 0; c < chunks; c++)
+    for (int c = lane; c < chunks; c += 32)
         if (part[c].x > -INFINITY) s += part[c].y * exp(part[c].x - (double)m);
+    s = warp_sum_d(s);
     return m + (float)log(s);
 }
 
@@ -506,7 +513,10 @@ __global__ void __launch_bounds__(kKlThreads) k_log_softmax_part(const float *x,
                                                                  const double2 *part, float *out) {
     __shared__ float s_lse;
     const int row = blockIdx.y, c = blockIdx.x, chunks = gridDim.x;
-    if (threadIdx.x == 0) s_lse = row_lse_from_parts(part + (long long)row * chunks, chunks);
+    if (threadIdx.x < 32) {
+        const float l = row_lse_warp(part + (long long)row * chunks, chunks);
+        if (threadIdx.x == 0) s_lse = l;
+    }
     __syncthreads();
     const float lse = s_lse;
     const float *xr = x + (long long)row * vocab;
@@ -534,7 +544,10 @@ __global__ void __launch_bounds__(kKlThreads) k_kl_part(const float *base, const
     __shared__ float s_lse;
     __shared__ double shd[32];
     const int row = blockIdx.y, c = blockIdx.x, chunks = gridDim.x;
-    if (threadIdx.x == 0) s_lse = row_lse_from_parts(part + (long long)row * chunks, chunks);
+    if (threadIdx.x < 32) {
+        const float l = row_lse_warp(part + (long long)row * chunks, chunks);
+        if (threadIdx.x == 0) s_lse = l;
+    }
     const int lo = c * kKlPiece;
     float x[kKlEach], b[kKlEach];
     kl_load(logits + (long long)row * vocab, lo, vocab, vec, 0.0f, x);
@@ -545,8 +558,12 @@ __global__ void __launch_bounds__(kKlThreads) k_kl_part(const float *base, const
 #pragma unroll
     for (int k = 0; k < kKlEach; k++) {
         if (kl_col(lo, vec, k) < vocab) {
+            // b - lt is exact in f32 wherever the two are within a factor of
+            // two (Sterbenz), i.e. wherever the edit moved the log-prob by
+            // less than that; the product takes one f32 rounding (about
+            // 6e-8 relative) before the f64 sum
             const float lt = x[k] - lse;
-            s += (double)expf(b[k]) * ((double)b[k] - (double)lt);
+            s += (double)(expf(b[k]) * (b[k] - lt));
         }
     }
     s = block_sum_d(s, shd);
@@ -668,10 +685,11 @@ __global__ void k_directions(const double *gs, double gc, const double *bs, doub
 
 }  // namespace
 
-// Row runs for the piece kernels: one wave of `per_sm` blocks per SM, at
-// least 64 rows (8 per row lane) per block.
+// Row runs for the piece kernels: at most one wave of `per_sm` blocks per SM
+// (a partial second wave would double the time), at least 64 rows (8 per
+// row lane) per block.
 static int piece_splits(int rows, int col_blocks, int per_sm) {
-    int s = (per_sm * 148 + col_blocks - 1) / col_blocks;
+    int s = (per_sm * 148) / col_blocks;
     s = std::min(s, (rows + 63) / 64);
     return std::max(1, std::min(s, 65535));
 }
