@@ -29,6 +29,20 @@ __global__ void k_embed(const void *table, int table_bf16, const uint32_t *token
         for (int i = lane; i < hidden; i += 32) xr[i] = 0.0f;
         return;
     }
+    if (table_bf16 && (hidden & 3) == 0 &&
+        ((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(res)) & 15) ==
+            0) {
+        // four elements per lane and access: 8-byte reads of the bf16 row, 16-byte writes
+        const uint2 *tr = reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(table) + (long long)t * hidden);
+        for (int i = lane; i < hidden / 4; i += 32) {
+            const uint2 q = __ldg(tr + i);
+            const float4 v = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u),
+                                         __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xffff0000u));
+            reinterpret_cast<float4 *>(xr)[i] = v;
+            if (cr) reinterpret_cast<float4 *>(cr)[i] = v;
+        }
+        return;
+    }
     for (int i = lane; i < hidden; i += 32) {
         const float v = table_bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(table)[(long long)t * hidden + i])
                                    : reinterpret_cast<const float *>(table)[(long long)t * hidden + i];
@@ -90,6 +104,51 @@ __global__ void k_rmsnorm_bf16(const float *x, const float *w, int n, int hidden
         const float v = xr[i];
         hr[i] = f32_to_bf16_bits(v * inv * w[i]);
         if (cr) cr[i] = v;
+    }
+}
+
+// The same RMSNorm with a block per row and the row held in registers (up
+// to 8 float4 per thread, element i = 4 (v blockDim + tid) + e): x is read
+// once, where the warp-per-row form above reads it twice (once for the sum
+// of squares, once for the output, the second mostly missing L1 at 16 KB
+// per row). hidden a multiple of 4, at most 32 x blockDim.
+__global__ void __launch_bounds__(1024) k_rmsnorm_row(const float *x, const float *w, int hidden, float eps,
+                                                      uint16_t *h, const int *cap_slot, float *res,
+                                                      const int *row_index) {
+    __shared__ float sh[32];
+    const int row = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    const int src = row_index ? row_index[row] : row;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)src * hidden);
+    const int n4 = hidden / 4;
+    float4 v[8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int i = k * nt + tid;
+        v[k] = i < n4 ? xr[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) sh[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int k = 0; k < (nt + 31) / 32; k++) tot += sh[k];
+    const float inv = 1.0f / sqrtf(tot / (float)hidden + eps);
+    const int slot = cap_slot ? cap_slot[src] : -1;
+    float4 *cr = slot >= 0 ? reinterpret_cast<float4 *>(res + (long long)slot * hidden) : nullptr;
+    uint2 *hr = reinterpret_cast<uint2 *>(h + (long long)row * hidden);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int i = k * nt + tid;
+        if (i >= n4) break;
+        const float4 g = __ldg(w4 + i);
+        uint2 o;
+        o.x = pack_bf16x2(v[k].x * inv * g.x, v[k].y * inv * g.y);
+        o.y = pack_bf16x2(v[k].z * inv * g.z, v[k].w * inv * g.w);
+        hr[i] = o;
+        if (cr) cr[i] = v[k];
     }
 }
 
@@ -604,6 +663,13 @@ cudaError_t embed_rows(const void *table, int table_bf16, const uint32_t *tokens
 cudaError_t rmsnorm_rows_bf16(const float *x, const float *w, int n, int hidden, float eps, uint16_t *h,
                               const int *cap_slot, float *res, const int *row_index, cudaStream_t st, int split_k) {
     if (n <= 0) return cudaSuccess;
+    const int nt = ((hidden + 31) / 32 + 31) / 32 * 32;  // threads: 32 elements each, whole warps
+    if (split_k == 0 && (hidden & 3) == 0 && nt <= 1024 &&
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(h) |
+          reinterpret_cast<uintptr_t>(res)) & 15) == 0) {
+        k_rmsnorm_row<<<n, nt, 0, st>>>(x, w, hidden, eps, h, cap_slot, res, row_index);
+        return cudaGetLastError();
+    }
     k_rmsnorm_bf16<0><<<(n + 7) / 8, 256, 0, st>>>(x, w, n, hidden, eps, h, cap_slot, res, row_index, split_k);
     return cudaGetLastError();
 }
