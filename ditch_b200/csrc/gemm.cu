@@ -487,29 +487,22 @@ __global__ void __launch_bounds__(256) k_stage_decode(const StageArgs a) {
 
 // ---- weight-streaming product for at most 16 tokens ----------------------
 // out[m][n] = x[m] . W[n] for m < M <= 16, the weight read once in its
-// stored format. A block takes 128 weight rows (8 warps x 16 rows) over one
-// K range of the grid's split; its tokens' slice of that range is staged in
-// shared memory once, already in the MMA's fragment order, so the 8 warps
-// share it. Each warp streams its 16 rows over the range chunk by chunk
-// (lane (g, t): 16 bytes of rows g and g + 8 per chunk, four lanes per row),
-// with four chunks of weight loads and their scales in flight ahead of the
-// math, decodes them to bf16 pairs with the in-GEMM arithmetic and feeds
+// stored format. Block = 8 warps over 16 weight rows (two n8 tiles); the
+// warps share the block's K range chunk by chunk and their partial sums are
+// added in shared memory (then across grid.y K splits: atomically, or in
+// split order in deterministic mode). Lane
+// (g, t) streams 16 bytes of row g (and g + 8) per chunk with plain loads,
+// decodes them to bf16 pairs with the in-GEMM arithmetic, and feeds
 // mma.sync m16n8k16 with the tokens as A (rows g, g + 8) and the weight as B.
 // K is permuted consistently for A and B: the lane's EPL consecutive weight
 // elements fill k-positions {2t, 2t + 1, 2t + 8, 2t + 9} of EPL / 4 steps,
-// and its A fragments are the same x elements. A dot product does not
-// depend on the order of its K terms. The K splits add their partial sums
-// atomically, or in deterministic mode leave them in sk_ws for the block
-// that arrives last to add in split order.
+// and its A fragments read the same x elements (one 8-byte load per row and
+// step). A dot product does not depend on the order of its K terms.
 template <int FMT>
 struct Skinny {
     static constexpr int kEPL = FMT == kFmtBf16 ? 8 : (FMT == kFmtFp8 || FMT == kFmtQ8_0) ? 16 : 32;
-    static constexpr int kSteps = kEPL / 4;
     static constexpr int kChunk = 4 * kEPL;  // K per chunk (four lanes per row)
 };
-constexpr int kSkRows = 128;       // weight rows per block (8 warps x 16)
-constexpr int kSkRing = 4;         // chunks of loads in flight per warp
-constexpr int kSkXBytes = 64 << 10;  // shared memory for the staged tokens: 16 x 2048 bf16
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -520,198 +513,147 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// The per-lane side data of one 16-byte piece (its block scale, zero point),
-// loaded together with the piece so no load waits behind the decode.
-struct SkSide {
-    float a, b;
-    int z;
-};
-
+// The EPL / 2 bf16 pairs of one lane's 16 raw bytes of weight row `row` at
+// element k0 (a multiple of EPL).
 template <int FMT>
-__device__ __forceinline__ SkSide skinny_side(int row, int k0, const GemmParams &p) {
-    SkSide s{0.0f, 0.0f, 8};
-    if (FMT == kFmtFp8) {
-        s.a = __ldg(p.scales + (long long)(row / p.blk_rows) * p.scale_cols + k0 / p.blk_cols);
-    } else if (FMT == kFmtQ8_0) {
-        s.a = __ldg(p.scales + (long long)row * p.scale_cols + k0 / 32);
-    } else if (FMT == kFmtMxfp4) {
-        s.z = __ldg(p.scales_u8 + (long long)row * (p.k / 32) + k0 / 32);
-    } else if (FMT == kFmtQ4K) {
-        const float2 dm = __ldg(reinterpret_cast<const float2 *>(p.scales) + (long long)row * p.scale_cols + k0 / 32);
-        s.a = dm.x;
-        s.b = dm.y;
-    } else if (FMT == kFmtInt4) {
-        const int g = k0 / p.blk_cols;
-        s.a = __ldg(p.scales + (long long)row * p.scale_cols + g);
-        if (p.zeros) s.z = (__ldg(p.zeros + (long long)(row >> 3) * p.scale_cols + g) >> ((row & 7) * 4)) & 0xf;
-    }
-    return s;
-}
-
-// The EPL / 2 bf16 pairs of one lane's 16 raw bytes with their side data.
-template <int FMT>
-__device__ __forceinline__ void skinny_decode(const uint4 q, const SkSide sd, uint32_t *pr) {
+__device__ __forceinline__ void skinny_decode(const uint4 q, int row, int k0, const GemmParams &p, uint32_t *pr) {
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
     if (FMT == kFmtBf16) {
 #pragma unroll
         for (int i = 0; i < 4; i++) pr[i] = w[i];
     } else if (FMT == kFmtFp8) {
+        const float s = __ldg(p.scales + (long long)(row / p.blk_rows) * p.scale_cols + k0 / p.blk_cols);
 #pragma unroll
-        for (int i = 0; i < 4; i++) e4m3x4_scaled(w[i], sd.a, pr[2 * i], pr[2 * i + 1]);
+        for (int i = 0; i < 4; i++) e4m3x4_scaled(w[i], s, pr[2 * i], pr[2 * i + 1]);
     } else if (FMT == kFmtQ8_0) {
-        const uint4 a = q8x8_bf16(w[0], w[1], sd.a), b = q8x8_bf16(w[2], w[3], sd.a);
+        const float d = __ldg(p.scales + (long long)row * p.scale_cols + k0 / 32);
+        const uint4 a = q8x8_bf16(w[0], w[1], d), b = q8x8_bf16(w[2], w[3], d);
         pr[0] = a.x; pr[1] = a.y; pr[2] = a.z; pr[3] = a.w;
         pr[4] = b.x; pr[5] = b.y; pr[6] = b.z; pr[7] = b.w;
     } else if (FMT == kFmtMxfp4) {
-        const float s = e8m0_scale((uint32_t)sd.z);
+        const float s = e8m0_scale(__ldg(p.scales_u8 + (long long)row * (p.k / 32) + k0 / 32));
 #pragma unroll
         for (int i = 0; i < 16; i++) pr[i] = scale_pack(e2m1x2_f32((w[i >> 2] >> (8 * (i & 3))) & 0xff), s);
     } else if (FMT == kFmtQ4K) {
+        const float2 dm = __ldg(reinterpret_cast<const float2 *>(p.scales) + (long long)row * p.scale_cols + k0 / 32);
 #pragma unroll
         for (int i = 0; i < 16; i++) {
             const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xff;
-            pr[i] = q4k_pair(byte & 0xf, byte >> 4, sd.a, sd.b);
+            pr[i] = q4k_pair(byte & 0xf, byte >> 4, dm.x, dm.y);
         }
     } else {  // kFmtInt4
+        const int g = k0 / p.blk_cols;
+        const float s = __ldg(p.scales + (long long)row * p.scale_cols + g);
+        int zq = 8;
+        if (p.zeros) zq = (__ldg(p.zeros + (long long)(row >> 3) * p.scale_cols + g) >> ((row & 7) * 4)) & 0xf;
 #pragma unroll
         for (int i = 0; i < 16; i++) {
             const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xff;
-            pr[i] = scale_pack(make_float2((float)((int)(byte & 0xf) - sd.z), (float)((int)(byte >> 4) - sd.z)), sd.a);
+            pr[i] = scale_pack(make_float2((float)((int)(byte & 0xf) - zq), (float)((int)(byte >> 4) - zq)), s);
         }
     }
-}
-
-// bias, rank-r delta (once per output) and the store of one output
-__device__ __forceinline__ void skinny_store(const GemmParams &p, int m, int n, float r) {
-    if (p.xa && p.db) {
-        const int drank = p.delta_rank > 1 ? p.delta_rank : 1;
-        for (int t = 0; t < drank; t++) r += p.xa[m * drank + t] * p.db[(long long)n * drank + t];
-    }
-    if (p.bias) r += p.bias[n];
-    float *o = reinterpret_cast<float *>(p.out) + (long long)m * p.ldo + n;
-    if (p.flags & kEpiResidual) *o = *o + r;
-    else *o = r;
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(256, 2) k_skinny(const uint8_t *wdata, long long row_bytes, const uint16_t *x,
-                                                   long long ldx, const GemmParams p, int chunks_per_split) {
+__global__ void __launch_bounds__(256) k_skinny(const uint8_t *wdata, long long row_bytes, const uint16_t *x,
+                                                long long ldx, const GemmParams p, int chunks_per_split) {
     using S = Skinny<FMT>;
-    constexpr int EPL = S::kEPL, STEPS = S::kSteps;
-    // [chunk][step][lane]: {x[g] elements 0-3, x[g + 8] elements 0-3} of the
-    // lane's four k-positions, i.e. the A fragment (a0, a2, a1, a3)
-    extern __shared__ uint4 xs[];
-    __shared__ int s_last;
+    constexpr int EPL = S::kEPL, STEPS = EPL / 4;
+    constexpr int kNum = EPL == 8 ? 2 : 1, kDen = EPL == 32 ? 2 : 1;  // bytes per element = kNum / kDen
+    __shared__ float red[8][16][17];  // [warp][row of 16][token]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int M = p.n_tok;
-    const int n_chunks = p.k / S::kChunk;
+    const int n0 = blockIdx.x * 16;
     const int c_lo = blockIdx.y * chunks_per_split;
-    const int nc = min(n_chunks, c_lo + chunks_per_split) - c_lo;  // > 0: the grid covers whole splits
-
-    // ---- the tokens' slice of this K range, in fragment order ----
-    // element (m, k) with k - c_lo kChunk = c kChunk + tt EPL + 4 s2 + e (e < 4)
-    // goes to lane 4 (m & 7) + tt of step (c, s2), half m >> 3 of its uint4
-    {
-        const int quads = nc * S::kChunk / 4;  // groups of 4 elements per token row
-        const int rows = M > 8 ? 16 : 8;
-        uint2 *xs2 = reinterpret_cast<uint2 *>(xs);
-        const uint16_t *xb = x + (long long)c_lo * S::kChunk;
-        for (int i = threadIdx.x; i < rows * quads; i += blockDim.x) {
-            const int m = i / quads, kk = (i % quads) * 4;
-            const int c = kk / S::kChunk, w = kk % S::kChunk;
-            uint2 v = make_uint2(0u, 0u);
-            if (m < M) v = __ldg(reinterpret_cast<const uint2 *>(xb + (long long)m * ldx + kk));
-            xs2[(((size_t)c * STEPS + (w % EPL) / 4) * 32 + (m & 7) * 4 + w / EPL) * 2 + (m >> 3)] = v;
-        }
-        if (M <= 8)  // the upper token rows of every fragment are zero
-            for (int i = threadIdx.x; i < nc * STEPS * 32; i += blockDim.x) xs2[(size_t)i * 2 + 1] = make_uint2(0u, 0u);
-    }
-    __syncthreads();
-
-    // ---- this warp's 16 weight rows over the range ----
-    const int rowb = blockIdx.x * kSkRows + warp * 16;
-    const int rows[2] = {min(rowb + g, p.m_w - 1), min(rowb + 8 + g, p.m_w - 1)};  // clamped: stores are masked
-    const uint8_t *wrow[2] = {wdata + (long long)(p.a_row0 + rows[0]) * row_bytes + (long long)c_lo * 64 + t * 16,
-                              wdata + (long long)(p.a_row0 + rows[1]) * row_bytes + (long long)c_lo * 64 + t * 16};
-    const int kb = c_lo * S::kChunk + t * EPL;  // this lane's first element of the range
+    const int c_hi = min((p.k + S::kChunk - 1) / S::kChunk, c_lo + chunks_per_split);
+    const int M = p.n_tok;
     float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-    uint4 q[kSkRing][2];
-    SkSide sd[kSkRing][2];
+    const int rows[2] = {min(n0 + g, p.m_w - 1), min(n0 + 8 + g, p.m_w - 1)};  // clamped: stores are masked
+    const uint16_t *xa = x + (long long)min(g, M - 1) * ldx, *xb = x + (long long)min(g + 8, M - 1) * ldx;
+    const bool va = g < M, vb = g + 8 < M;
+    // kU chunks per round: all their weight loads are issued before any is
+    // decoded, so each lane keeps 2 kU 16-byte loads in flight
+    constexpr int kU = 4;
+    const uint8_t *wrow[2] = {wdata + (long long)(p.a_row0 + rows[0]) * row_bytes,
+                              wdata + (long long)(p.a_row0 + rows[1]) * row_bytes};
+    for (int c0 = c_lo + warp; c0 < c_hi; c0 += 8 * kU) {
+        uint4 q[kU][2];
 #pragma unroll
-    for (int u = 0; u < kSkRing; u++)
-        if (u < nc)
+        for (int u = 0; u < kU; u++) {
+            const int c = c0 + 8 * u;
+            const long long off = (long long)(c * S::kChunk + t * EPL) * kNum / kDen;
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                q[u][j] = __ldg(reinterpret_cast<const uint4 *>(wrow[j] + u * 64));
-                sd[u][j] = skinny_side<FMT>(p.a_row0 + rows[j], kb + u * S::kChunk, p);
+            for (int j = 0; j < 2; j++)
+                q[u][j] = c < c_hi ? __ldg(reinterpret_cast<const uint4 *>(wrow[j] + off)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int c = c0 + 8 * u;
+            if (c >= c_hi) break;
+            const int k0 = c * S::kChunk + t * EPL;  // this lane's first element
+            uint2 ax[STEPS], bx[STEPS];
+#pragma unroll
+            for (int s2 = 0; s2 < STEPS; s2++) {
+                ax[s2] = va ? *reinterpret_cast<const uint2 *>(xa + k0 + 4 * s2) : make_uint2(0, 0);
+                bx[s2] = vb ? *reinterpret_cast<const uint2 *>(xb + k0 + 4 * s2) : make_uint2(0, 0);
             }
-    for (int c0 = 0; c0 < nc; c0 += kSkRing) {
-#pragma unroll
-        for (int u = 0; u < kSkRing; u++) {
-            const int c = c0 + u;
-            if (c >= nc) break;  // warp-uniform
-            const uint4 cq[2] = {q[u][0], q[u][1]};
-            const SkSide cs[2] = {sd[u][0], sd[u][1]};
-            if (c + kSkRing < nc)  // the slot's next chunk, in flight while this one is used
-#pragma unroll
-                for (int j = 0; j < 2; j++) {
-                    q[u][j] = __ldg(reinterpret_cast<const uint4 *>(wrow[j] + (c + kSkRing) * 64));
-                    sd[u][j] = skinny_side<FMT>(p.a_row0 + rows[j], kb + (c + kSkRing) * S::kChunk, p);
-                }
-            uint4 a[STEPS];
-#pragma unroll
-            for (int s2 = 0; s2 < STEPS; s2++) a[s2] = xs[((size_t)c * STEPS + s2) * 32 + lane];
 #pragma unroll
             for (int j = 0; j < 2; j++) {
                 uint32_t pr[EPL / 2];
-                skinny_decode<FMT>(cq[j], cs[j], pr);
+                skinny_decode<FMT>(q[u][j], p.a_row0 + rows[j], k0, p, pr);
 #pragma unroll
                 for (int s2 = 0; s2 < STEPS; s2++)
-                    mma_16816(acc[j], a[s2].x, a[s2].z, a[s2].y, a[s2].w, pr[2 * s2], pr[2 * s2 + 1]);
+                    mma_16816(acc[j], ax[s2].x, bx[s2].x, ax[s2].y, bx[s2].y, pr[2 * s2], pr[2 * s2 + 1]);
             }
         }
     }
-
-    // acc[j]: tokens (g, g + 8) x weight rows rowb + 8 j + 2 t, + 1
-    if (gridDim.y == 1) {
+    // acc[j]: tokens (g, g + 8) x weight rows 8 j + 2 t, + 1 -> red[warp][row][token]
 #pragma unroll
-        for (int j = 0; j < 2; j++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int m = g + 8 * (e >> 1), n = rowb + 8 * j + 2 * t + (e & 1);
-                if (m < M && n < p.m_w) skinny_store(p, m, n, acc[j][e]);
-            }
-        return;
+    for (int j = 0; j < 2; j++) {
+        red[warp][8 * j + 2 * t][g] = acc[j][0];
+        red[warp][8 * j + 2 * t + 1][g] = acc[j][1];
+        red[warp][8 * j + 2 * t][g + 8] = acc[j][2];
+        red[warp][8 * j + 2 * t + 1][g + 8] = acc[j][3];
     }
-    // K split over the grid: each block leaves its partial sums in sk_ws
-    // ([row block][split][128 rows][16 tokens]); the block that arrives last
-    // adds them in split order (the result does not depend on timing) and
-    // stores them
-    float *ws = p.sk_ws + (size_t)blockIdx.x * gridDim.y * (kSkRows * 16);
+    __syncthreads();
+    // thread (row, token): warps added in order
+    const int row = threadIdx.x >> 4, m = threadIdx.x & 15, n = n0 + row;
+    float r = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 2; j++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int m = g + 8 * (e >> 1), rl = warp * 16 + 8 * j + 2 * t + (e & 1);
-            __stcg(ws + (size_t)blockIdx.y * (kSkRows * 16) + rl * 16 + m, acc[j][e]);
+    for (int w2 = 0; w2 < 8; w2++) r += red[w2][row][m];
+    if (gridDim.y > 1 && p.sk_ws) {
+        // K split over the grid, deterministic mode: each block leaves its
+        // partial sums in sk_ws; the block that arrives last adds them in
+        // split order (the result does not depend on timing) and runs the
+        // epilogue. Otherwise every split adds its sum atomically.
+        __shared__ int s_last;
+        float *ws = p.sk_ws + (size_t)blockIdx.x * 256;
+        const size_t split_stride = (size_t)gridDim.x * 256;
+        __stcg(ws + blockIdx.y * split_stride + threadIdx.x, r);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const int old = atomicAdd(p.sk_cnt + blockIdx.x, 1);
+            s_last = old == (int)gridDim.y - 1;
+            if (s_last) p.sk_cnt[blockIdx.x] = 0;  // every split has arrived: ready for the next launch
         }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const int old = atomicAdd(p.sk_cnt + blockIdx.x, 1);
-        s_last = old == (int)gridDim.y - 1;
-        if (s_last) p.sk_cnt[blockIdx.x] = 0;  // every split has arrived: ready for the next launch
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        r = 0.0f;
+        for (int y = 0; y < (int)gridDim.y; y++) r += __ldcg(ws + y * split_stride + threadIdx.x);
     }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int i = threadIdx.x; i < kSkRows * 16; i += blockDim.x) {
-        const int rl = i >> 4, m = i & 15, n = blockIdx.x * kSkRows + rl;
-        if (m >= M || n >= p.m_w) continue;
-        float r = 0.0f;
-        for (int y = 0; y < (int)gridDim.y; y++) r += __ldcg(ws + (size_t)y * (kSkRows * 16) + i);
-        skinny_store(p, m, n, r);
+    if (m >= M || n >= p.m_w) return;
+    if (blockIdx.y == 0 || p.sk_ws) {  // bias and delta once per output
+        if (p.xa && p.db) {
+            const int drank = p.delta_rank > 1 ? p.delta_rank : 1;
+            for (int t = 0; t < drank; t++) r += p.xa[m * drank + t] * p.db[(long long)n * drank + t];
+        }
+        if (p.bias) r += p.bias[n];
     }
+    float *o = reinterpret_cast<float *>(p.out) + (long long)m * p.ldo + n;
+    if (p.flags & kEpiAtomic) atomicAdd(o, r);
+    else if (p.flags & kEpiResidual) *o = *o + r;
+    else *o = r;
 }
 
 template <int BN, bool DUAL, int FMT>
@@ -1246,11 +1188,7 @@ bool gemm_map_bf16(CUtensorMap *map, const void *ptr, uint64_t cols, uint64_t ro
                     CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-size_t skinny_split_bytes(int rows, int splits) {
-    return (size_t)((rows + kSkRows - 1) / kSkRows) * splits * (kSkRows * 16) * sizeof(float);
-}
-
-int skinny_row_blocks(int rows) { return (rows + kSkRows - 1) / kSkRows; }
+size_t skinny_split_bytes(int rows, int splits) { return (size_t)((rows + 15) / 16) * splits * 256 * sizeof(float); }
 
 size_t gemm_stream_k_bytes(int grid, int bn, bool dual) {
     return (size_t)grid * 2 * (dual ? 2 : 1) * BM * bn * sizeof(float);
@@ -1299,63 +1237,30 @@ int skinny_chunk(int fmt) {
     }
 }
 
-// K splits of the weight-streaming product: each split's token slice must
-// fit the staged shared memory (kSkXBytes: 2048 elements of 16 tokens), and
-// the grid should hold about two blocks per SM (no partial second wave)
-// with at least one ring of chunks per split.
-int skinny_splits(int fmt, int rows, int k, int num_sms) {
-    const int chunk = skinny_chunk(fmt);
-    if (!chunk) return 1;
-    const int chunks = k / chunk;
-    const int max_per = kSkXBytes / (chunk * 32);
-    const int bx = skinny_row_blocks(rows);
-    int s = std::max(1, (2 * num_sms) / bx);
-    s = std::min(s, std::max(1, chunks / kSkRing));
-    s = std::max(s, (chunks + max_per - 1) / max_per);
-    const int per = (chunks + s - 1) / s;
-    return (chunks + per - 1) / per;
-}
-
-template <int FMT>
-static cudaError_t launch_skinny_t(const uint8_t *w, long long row_bytes, const uint16_t *x, long long ldx,
-                                   const GemmParams &p, dim3 grid, int per, cudaStream_t stream) {
-    const size_t smem = (size_t)per * Skinny<FMT>::kChunk * 32;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(k_skinny<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSkXBytes);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
-    k_skinny<FMT><<<grid, 256, smem, stream>>>(w, row_bytes, x, ldx, p, per);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_skinny(int fmt, const GemmOperand &a, const GemmOperand &b, const GemmParams &p, int k_splits,
                           cudaStream_t stream) {
     const int chunk = skinny_chunk(fmt);
     if (!chunk || p.n_tok < 1 || p.n_tok > 16 || p.k % chunk) return cudaErrorInvalidValue;
     if (fmt == kFmtFp8 && p.blk_cols % 16) return cudaErrorInvalidValue;
     if (fmt == kFmtInt4 && p.blk_cols % 32) return cudaErrorInvalidValue;
-    if (b.row_bytes % 8 || (reinterpret_cast<uintptr_t>(b.ptr) & 7)) return cudaErrorInvalidValue;  // 8-byte token loads
-    if (p.flags & (kEpiAtomic | kEpiSwiglu | kEpiOutBf16)) return cudaErrorInvalidValue;
     const int chunks = p.k / chunk;
     k_splits = std::max(1, std::min(k_splits, chunks));
     const int per = (chunks + k_splits - 1) / k_splits;
-    if ((size_t)per * chunk * 32 > (size_t)kSkXBytes) return cudaErrorInvalidValue;
-    dim3 grid(skinny_row_blocks(p.m_w), (chunks + per - 1) / per);
-    if (grid.y > 1 && (!p.sk_ws || !p.sk_cnt)) return cudaErrorInvalidValue;
+    dim3 grid((p.m_w + 15) / 16, (chunks + per - 1) / per);
+    if (grid.y > 1 && (p.sk_ws ? !p.sk_cnt : !(p.flags & kEpiAtomic))) return cudaErrorInvalidValue;
     const uint8_t *w = static_cast<const uint8_t *>(a.ptr);
     const uint16_t *x = static_cast<const uint16_t *>(b.ptr);
     const long long ldx = b.row_bytes / 2;
     switch (fmt) {
-    case kFmtBf16: return launch_skinny_t<kFmtBf16>(w, a.row_bytes, x, ldx, p, grid, per, stream);
-    case kFmtFp8: return launch_skinny_t<kFmtFp8>(w, a.row_bytes, x, ldx, p, grid, per, stream);
-    case kFmtQ8_0: return launch_skinny_t<kFmtQ8_0>(w, a.row_bytes, x, ldx, p, grid, per, stream);
-    case kFmtMxfp4: return launch_skinny_t<kFmtMxfp4>(w, a.row_bytes, x, ldx, p, grid, per, stream);
-    case kFmtInt4: return launch_skinny_t<kFmtInt4>(w, a.row_bytes, x, ldx, p, grid, per, stream);
-    case kFmtQ4K: return launch_skinny_t<kFmtQ4K>(w, a.row_bytes, x, ldx, p, grid, per, stream);
+    case kFmtBf16: k_skinny<kFmtBf16><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtFp8: k_skinny<kFmtFp8><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtQ8_0: k_skinny<kFmtQ8_0><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtMxfp4: k_skinny<kFmtMxfp4><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtInt4: k_skinny<kFmtInt4><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
+    case kFmtQ4K: k_skinny<kFmtQ4K><<<grid, 256, 0, stream>>>(w, a.row_bytes, x, ldx, p, per); break;
     default: return cudaErrorInvalidValue;
     }
+    return cudaGetLastError();
 }
 
 cudaError_t launch_gemm(int fmt, const GemmOperand &a, const GemmOperand *a2, const GemmOperand &b, GemmParams p,

@@ -89,10 +89,8 @@ struct GemmParams {
 };
 
 // Device bytes of the weight-streaming product's split partial sums (in
-// sk_ws; the per-row-block counters are the first skinny_row_blocks(rows) of
-// sk_cnt, zero before the first launch and left zero by every launch).
+// sk_ws; the per-row-block counters are the first (rows + 15) / 16 of sk_cnt).
 size_t skinny_split_bytes(int rows, int splits);
-int skinny_row_blocks(int rows);
 // Device bytes of the stream-K partial sums for a grid of `grid` CTAs.
 size_t gemm_stream_k_bytes(int grid, int bn, bool dual);
 // Whether a dense GEMM of `tiles` whole output tiles runs stream-K on `sms`
@@ -143,14 +141,11 @@ struct StageArgs {
 cudaError_t launch_stage_decode(const StageArgs &a, int num_sms, cudaStream_t stream);
 
 // Weight-streaming product for 1..16 tokens (decode-like calls): the weight
-// read once in its stored format (bf16, FP8, Q8_0, MXFP4, INT4, Q4_K),
-// tensor-core mma.sync with the tokens as the 16-row operand. Plain f32
-// output or residual add (p.flags), bias and rank-r delta. K must be a
-// multiple of skinny_chunk(fmt) (0 = format not supported); with more than
-// one K split (skinny_splits) p.sk_ws / p.sk_cnt hold the partial sums,
-// added in split order by the last block of each row block.
+// read once in its stored format (bf16, FP8, Q8_0, MXFP4, INT4), tensor-core
+// mma.sync with the tokens as the 16-row operand. Plain f32 output, residual
+// add or atomic add (p.flags), bias and rank-1 delta (split 0). K must be a
+// multiple of skinny_chunk(fmt); 0 = format not supported.
 int skinny_chunk(int fmt);
-int skinny_splits(int fmt, int rows, int k, int num_sms);
 cudaError_t launch_skinny(int fmt, const GemmOperand &a, const GemmOperand &b, const GemmParams &p, int k_splits,
                           cudaStream_t stream);
 

@@ -355,16 +355,21 @@ int gemm_mat(ditch_cuda_device *dev, const Mat &w, int slab_row0, int m_rows, co
         p.db_stride = ex->db_stride;
         p.bn = ex->bn;
     }
-    // 1..16 tokens: the weight-streaming product, K split over the grid; the
-    // splits leave their partial sums in sk_ws and the last block of each
-    // row block adds them in split order (the same bits on every run)
+    // 1..16 tokens: the weight-streaming product, K split over the grid: the
+    // partial sums are added atomically, or in deterministic mode left in
+    // sk_ws and added in split order by the last block of each row block
     const int sk = skinny_chunk(fmt);
-    if (!p.sched && p.k_splits == 1 && !dual && !(flags & (kEpiOutBf16 | kEpiAtomic)) && n_tok <= 16 && sk &&
-        K % sk == 0 && !(fmt == kFmtFp8 && w.bc % 16) && !(fmt == kFmtInt4 && w.group % 32)) {
-        const int ks = skinny_splits(fmt, m_rows, K, dev->sms);
-        if (ks > 1) {
-            const int bx = skinny_row_blocks(m_rows);
-            DITCH_CUDA(dev->sk_ws.reserve(skinny_split_bytes(m_rows, ks)));
+    if (!p.sched && p.k_splits == 1 && !dual && !(flags & kEpiOutBf16) && n_tok <= 16 && sk && K % sk == 0 &&
+        !(fmt == kFmtFp8 && w.bc % 16) && !(fmt == kFmtInt4 && w.group % 32)) {
+        const int bx = (m_rows + 15) / 16, chunks = K / sk;
+        const int ks = std::max(1, std::min(chunks, (2 * dev->sms + bx - 1) / bx));  // about one wave
+        if (ks > 1 && !dev->deterministic) {
+            if (!(flags & kEpiResidual))
+                DITCH_CUDA(cudaMemset2DAsync(out, (size_t)ldo * 4, 0, (size_t)m_rows * 4, n_tok, dev->stream));
+            flags = (flags & ~kEpiResidual) | kEpiAtomic;
+        } else if (ks > 1) {
+            const int per = (chunks + ks - 1) / ks, splits = (chunks + per - 1) / per;
+            DITCH_CUDA(dev->sk_ws.reserve(skinny_split_bytes(m_rows, splits)));
             if (dev->sk_tiles < bx) {
                 DITCH_CUDA(dev->sk_cnt.reserve((size_t)bx * sizeof(int)));
                 DITCH_CUDA(cudaMemsetAsync(dev->sk_cnt.ptr, 0, (size_t)bx * sizeof(int), dev->stream));

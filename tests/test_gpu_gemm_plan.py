@@ -226,11 +226,10 @@ def test_fp8_operand_is_ditchs_decode(device):
 @pytest.mark.parametrize("rows,cols", [(1000, 1024), (4160, 4096), (264, 14336)])
 def test_weight_streaming_small_m(device, fmt, m, rows, cols):
     """1..16 tokens take the weight-streaming product (mma.sync over the
-    decoded stored format, the tokens staged in shared memory per K range,
-    K split across the grid and the splits added in order): equal to x . W^T
-    over the decoded weight up to f32 accumulation order, and the same bits
-    on a second call. Shapes: a partial last row block, one full wave of row
-    blocks, and few rows over a long K (many splits, a partial last one)."""
+    decoded stored format, K split across the grid): equal to x . W^T over
+    the decoded weight up to f32 accumulation order. Shapes: a partial last
+    16-row block, many row blocks, and few rows over a long K (many
+    splits, a partial last one)."""
     torch.backends.cuda.matmul.allow_tf32 = False
     gen = torch.Generator(device="cuda").manual_seed(31 + m)
     W, _ = make_weight(device, fmt, rows, cols, gen)
@@ -246,9 +245,4 @@ def test_weight_streaming_small_m(device, fmt, m, rows, cols):
     device.synchronize()
     err = (out - ref).abs()
     assert bool((err <= _bound(x, dec)).all()), float(err.max())
-    again = torch.full((m, rows), float("nan"), device="cuda", dtype=torch.float32)
-    torch.cuda.synchronize()
-    W.gemm(x.data_ptr(), m, again.data_ptr())
-    device.synchronize()
-    assert torch.equal(out, again)
     W.close()
