@@ -81,7 +81,7 @@ int dp_allreduce_sum(ditch_cuda_device *dev, ditch_cuda_group *g, const double *
         const size_t len = std::min(cap, n - off);
         const size_t half_off = (g->dp_calls++ & 1) * half_bytes(g);
         DITCH_CUDA(cudaMemcpyAsync(peer_data(g->base) + half_off, src + off, len * 8, cudaMemcpyDeviceToDevice, st));
-        if ((s = group_exchange(dev, g, 30.0))) return s;
+        if ((s = group_exchange(dev, g, g->wait_s))) return s;
         const int grid = (int)std::min<size_t>((len + 255) / 256, (size_t)dev->sms * 2);
         k_dp_sum<<<std::max(grid, 1), 256, 0, st>>>(g->peers, g->world, half_off, (long long)len, dst + off);
         DITCH_LAUNCH(dev, cudaGetLastError());
@@ -102,7 +102,7 @@ int dp_ordered_sum(ditch_cuda_device *dev, ditch_cuda_group *g, const double *va
     k_dp_put<<<std::max(grid, 1), 256, 0, st>>>(own, vals, (long long)count);
     DITCH_LAUNCH(dev, cudaGetLastError());
     int s;
-    if ((s = group_exchange(dev, g, 30.0))) return s;
+    if ((s = group_exchange(dev, g, g->wait_s))) return s;
     k_dp_ordered_sum<<<1, 256, 0, st>>>(g->peers, g->world, half_off, out);
     DITCH_LAUNCH(dev, cudaGetLastError());
     return DITCH_CUDA_OK;

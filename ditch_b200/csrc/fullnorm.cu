@@ -254,7 +254,7 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
             return DITCH_CUDA_INVALID;
         }
         // every peer has finished reading the region (the forward's last reduction)
-        if ((s = group_exchange(dev, m->group, 30.0))) return s;
+        if ((s = group_exchange(dev, m->group, m->group->wait_s))) return s;
     }
     // a = (v / n)^T W on the device, then n, v, a on the host
     DITCH_CUDA(m->vn.reserve((size_t)rows * 4));
@@ -359,7 +359,7 @@ int full_norm_delta(ditch_cuda_model *m, const Mat &w, int row0, const float *rn
         tp_slice(la, rank, cols, W, tr, mine);
         la.swap(mine);
         // every peer has finished reading the region before the next forward writes it
-        if ((s = group_exchange(dev, m->group, 30.0))) return s;
+        if ((s = group_exchange(dev, m->group, m->group->wait_s))) return s;
     }
     DITCH_CUDA(cudaMemcpyAsync(a_out, la.data(), la.size() * 4, cudaMemcpyHostToDevice, dev->stream));
     DITCH_CUDA(cudaMemcpyAsync(b_out, lb.data(), lb.size() * 4, cudaMemcpyHostToDevice, dev->stream));

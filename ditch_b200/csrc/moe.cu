@@ -627,7 +627,7 @@ namespace {
 
 // One exchange of the model's peer group: signal this rank's epoch to every
 // peer, then wait (bounded) until every peer has signalled it.
-int ep_exchange(ditch_cuda_model *m) { return group_exchange(m->dev, m->group, 30.0); }
+int ep_exchange(ditch_cuda_model *m) { return group_exchange(m->dev, m->group, m->group->wait_s); }
 
 }  // namespace
 

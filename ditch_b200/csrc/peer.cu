@@ -32,9 +32,12 @@ __global__ void k_peer_signal(PeerPtrs pp, int rank, int world, uint64_t epoch) 
 }
 
 // Thread s < world waits until this rank's slot s holds at least `epoch`.
+// Once a wait of the current call has run out (the status word says so),
+// the later waits of that call return at once: the call fails anyway.
 __global__ void k_peer_wait(uint8_t *own, int world, uint64_t epoch, int *status, uint64_t budget_ns) {
     const int s = threadIdx.x;
     if (s >= world) return;
+    if (status && *reinterpret_cast<volatile int *>(status) == kKernelWaitTimeout) return;
     const uint64_t *flag = reinterpret_cast<const uint64_t *>(own) + s;
     const uint64_t t0 = global_ns();
     while (ld_acquire_sys(flag) < epoch) {
@@ -147,9 +150,17 @@ int ditch_cuda_group_barrier(ditch_cuda_group *g) {
     DITCH_CUDA(cudaSetDevice(dev->ordinal));
     const uint64_t ep = ++g->epoch;
     DITCH_LAUNCH(dev, peer_signal(g->peers, g->rank, g->world, ep, dev->stream));
-    DITCH_LAUNCH(dev, peer_wait(g->base, g->world, ep, dev->status, 20.0, dev->stream));
+    DITCH_LAUNCH(dev, peer_wait(g->base, g->world, ep, dev->status, g->wait_s, dev->stream));
     DITCH_CUDA(cudaStreamSynchronize(dev->stream));
     return check_status(dev, "group barrier");
+}
+
+int ditch_cuda_group_set_wait_budget(ditch_cuda_group *g, double seconds) {
+    clear_error();
+    REQUIRE(g, "null group");
+    REQUIRE(seconds > 0.0 && seconds <= 600.0, "wait budget %g s is not within (0, 600]", seconds);
+    g->wait_s = seconds;
+    return DITCH_CUDA_OK;
 }
 
 }  // extern "C"

@@ -55,6 +55,7 @@ struct ditch_cuda_group {
     bool opened = false;
     uint64_t epoch = 0;             // last exchange started
     uint64_t dp_calls = 0;          // data-parallel reductions so far (their half of the region alternates)
+    double wait_s = 30.0;           // budget of every wait of an exchange (ditch_cuda_group_set_wait_budget)
 };
 
 namespace ditch {

@@ -100,11 +100,11 @@ int tp_allreduce_add(ditch_cuda_model *m, int n, float *x) {
     const long long total4 = (long long)n * m->cfg.hidden / 4;
     const long long chunk4 = (total4 + g->world - 1) / g->world;
     int s;
-    if ((s = group_exchange(dev, g, 30.0))) return s;
+    if ((s = group_exchange(dev, g, g->wait_s))) return s;
     const int grid = (int)std::min<long long>((chunk4 + 255) / 256, 2 * dev->sms);
     k_tp_reduce<<<std::max(grid, 1), 256, 0, st>>>(g->peers, g->world, g->rank, send_off, red_off, total4, chunk4);
     DITCH_LAUNCH(dev, cudaGetLastError());
-    if ((s = group_exchange(dev, g, 30.0))) return s;
+    if ((s = group_exchange(dev, g, g->wait_s))) return s;
     const int grid2 = (int)std::min<long long>((total4 + 255) / 256, 4 * dev->sms);
     k_tp_gather_add<<<std::max(grid2, 1), 256, 0, st>>>(g->peers, red_off, total4, chunk4,
                                                          reinterpret_cast<float4 *>(x));

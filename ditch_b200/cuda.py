@@ -144,6 +144,7 @@ SIGNATURES = {
     "ditch_cuda_group_open": (C.c_int, [vp, vp]),
     "ditch_cuda_group_free": (None, [vp]),
     "ditch_cuda_group_barrier": (C.c_int, [vp]),
+    "ditch_cuda_group_set_wait_budget": (C.c_int, [vp, C.c_double]),
     "ditch_cuda_model_group_bytes": (sz, [vp, sz]),
     "ditch_cuda_model_set_group": (C.c_int, [vp, vp, sz]),
     "ditch_cuda_model_dp_group_bytes": (sz, [vp, sz]),
@@ -499,6 +500,10 @@ class Group:
 
     def barrier(self):
         check(lib().ditch_cuda_group_barrier(self.h))
+
+    def set_wait_budget(self, seconds):
+        """Budget of every wait of the group's exchanges (30 s by default)."""
+        check(lib().ditch_cuda_group_set_wait_budget(self.h, float(seconds)))
 
     def allreduce_f64(self, values):
         """Every rank's f64 array summed over the group (rank order, the same

@@ -473,8 +473,17 @@ int ditch_cuda_group_create(ditch_cuda_device *dev, int rank, int world, size_t 
 int ditch_cuda_group_open(ditch_cuda_group *g, const void *handles);
 void ditch_cuda_group_free(ditch_cuda_group *g);
 /* A device-side barrier over the group (bounded: returns
- * DITCH_CUDA_DEVICE_FAILED when a peer does not arrive within 20 s). */
+ * DITCH_CUDA_DEVICE_FAILED when a peer does not arrive within the group's
+ * wait budget). */
 int ditch_cuda_group_barrier(ditch_cuda_group *g);
+/* The budget of every wait of the group's exchanges (barrier, expert and
+ * tensor-parallel layers, data-parallel reductions, the full-mode
+ * collectives): 30 s by default, (0, 600]. A wait that runs out sets the
+ * device's status word; the call returns DITCH_CUDA_DEVICE_FAILED, its
+ * later waits return at once, and no result of the call is kept (cached
+ * row norms included). The ranks' epochs then disagree: free the models
+ * and the group on every rank and build them again. */
+int ditch_cuda_group_set_wait_budget(ditch_cuda_group *g, double seconds);
 /* Region bytes that a model loaded with ep_world > 1 or tp_world > 1 needs
  * for forwards of at most max_tokens tokens per rank (0 without either). */
 size_t ditch_cuda_model_group_bytes(const ditch_cuda_model *m, size_t max_tokens);

@@ -133,3 +133,71 @@ def test_tensor_parallel_forward_matches_one_gpu(tmp_path, world):
     assert not np.array_equal(z0["log1"], z0["log3"]), "the edit changed nothing"
     assert not np.array_equal(z0["log3"], z0["log5"]), "row normalisation changed nothing"
     assert not np.array_equal(z0["log5"], z0["log7"]), "full row normalisation changed nothing"
+
+
+def _timeout_worker(rank, world, port, out_dir):
+    import sys
+
+    for p in (ROOT, os.path.join(ROOT, "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ditch_b200
+    from synth import make_model
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    dev = ditch_b200.Device(rank)
+    spec, f32, tensors = make_model(510, n_layers=2, hidden=256, head_dim=64, heads=8, kv_heads=8, inter=512)
+
+    def exchange(h):
+        out = [None] * world
+        dist.all_gather_object(out, h)
+        return out
+
+    tp = ditch_b200.Model(dev, spec, tensors, max_seq=64, tp_rank=rank, tp_world=world)
+    group = ditch_b200.Group(dev, rank, world, tp.group_bytes(64), exchange)
+    tp.set_group(group, 64)
+    group.set_wait_budget(1.0)
+    dist.barrier()
+    codes = []
+    if rank == 0:
+        # rank 1 never joins: the row-norm collective runs out of its budget
+        # (a flag nothing sets), twice: the failed call kept no norms
+        for _ in range(2):
+            try:
+                tp.set_row_normalization("pre")
+                codes.append(0)
+            except ditch_b200.DitchCudaError as e:
+                codes.append(e.code)
+        # the context is still usable: a decode on the device after the failures
+        q = np.arange(256, dtype=np.uint8).reshape(16, 16) & 0x77  # no NaN codes
+        got = dev.dequant_fp8(q, np.full((1, 1), 0.5, np.float32), 16, 16)
+        codes.append(int(np.asarray(got).any()))
+    np.save(os.path.join(out_dir, f"t{rank}.npy"), np.asarray(codes, np.int64))
+    dist.barrier()  # no kernel of either rank is in flight past this point
+    tp.close()
+    group.close()
+    dev.close()
+    dist.destroy_process_group()
+
+
+def test_tensor_parallel_wait_runs_out_and_keeps_no_norms(tmp_path):
+    """A rank that does not join a collective makes the peer's waits run out
+    after the group's budget (1 s here): set_row_normalization returns
+    DITCH_CUDA_DEVICE_FAILED, and a second call fails the same way instead of
+    reusing row norms from the failed one. The device stays usable."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_timeout_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    codes = np.load(tmp_path / "t0.npy")
+    assert list(codes) == [2, 2, 1], codes  # DEVICE_FAILED twice, then a decode that ran
