@@ -714,7 +714,10 @@ def run_c4(args, dev, world=1, rank=0, dist=None):
         "e2e": {"value": round(tokens * world * args.steps / (ms_e2e / 1000.0), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(tokens * 4 + (P + 1) * 8), "d2h_bytes_per_step": 8,
                 "ms_per_step": round(ms_e2e / args.steps, 3)},
-        "roofline": {"bound": "tensor", "kernel": "gemm_kernel: tcgen05 grouped GEMM, MXFP4 decoded per tile",
+        "roofline": {"bound": "tensor",
+                     "kernel": ("gemm_kernel: tcgen05 grouped GEMM, MXFP4 decoded per tile" if args.stage_min_tokens == 0
+                                else "gemm_kernel: tcgen05 grouped GEMM over each expert stack's bf16 copy (MXFP4 "
+                                     "decoded once at first use and kept, memory permitting)"),
                      "achieved": round(achieved, 1), "peak": tf_sust, "unit": "TFLOP/s",
                      "frac": round(achieved / tf_sust, 4), "peak_source": f"{src} bf16 sustained", "traffic": None,
                      "gemm_ms_per_step": round(gemm_ms / args.steps, 3),

@@ -307,12 +307,21 @@ __global__ void __launch_bounds__(256) k_qk_prep(float *qkv, AttnParams p) {
         cs[k] = __ldg(c + lane + 32 * k);
         ss[k] = __ldg(sn + lane + 32 * k);
     }
-    for (int slot = 0; slot < nh + nkv; slot++) {  // q heads, then k heads
+    // q heads, then k heads; the next head's values load while this one is
+    // normed and rotated
+    const int slots = nh + nkv;
+    float xn[V];
+#pragma unroll
+    for (int k = 0; k < V; k++) xn[k] = row[lane + 32 * k];
+    for (int slot = 0; slot < slots; slot++) {
         float *v = row + slot * HD;
         const float *nw = slot < nh ? p.q_norm : p.k_norm;
         float x[V];
 #pragma unroll
-        for (int k = 0; k < V; k++) x[k] = v[lane + 32 * k];
+        for (int k = 0; k < V; k++) x[k] = xn[k];
+        if (slot + 1 < slots)
+#pragma unroll
+            for (int k = 0; k < V; k++) xn[k] = v[HD + lane + 32 * k];
         if (nw) {
             float sq = 0.0f;
 #pragma unroll
