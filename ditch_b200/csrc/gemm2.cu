@@ -31,7 +31,13 @@ namespace {
 
 constexpr int PBM = 128;  // weight rows per CTA (256 per pair)
 constexpr int PBK = 64;
+// epilogue warps: 4 (one per TMEM lane quarter), 8 for SwiGLU (two per lane
+// quarter, each taking half the token columns: the two accumulators' SwiGLU
+// is the heavier epilogue, and with one accumulator buffer it does not
+// overlap the next tile's MMAs)
 constexpr int kPEpiWarps = 4;
+template <bool DUAL>
+constexpr int pair_epi_warps() { return DUAL ? 8 : 4; }
 constexpr int kPSmemBudget = 224 * 1024;
 
 template <int BN, bool DUAL>
@@ -46,7 +52,8 @@ struct PairCfg {
     static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
     static constexpr int kTmemColsRaw = kAccBufs * kAccCols;
     static constexpr int kTmemCols = kTmemColsRaw < 32 ? 32 : kTmemColsRaw;
-    static constexpr int kWarps = 2 + kPEpiWarps;
+    static constexpr int kEpi = pair_epi_warps<DUAL>();
+    static constexpr int kWarps = 2 + kEpi;
     static constexpr int kThreads = kWarps * 32;
     // full, empty, 2 tfull, 2 tempty; then the TMEM base and the abort word
     static constexpr int kBarBytes = (8 * (2 * kStages + 4) + 16 + 63) / 64 * 64;
@@ -211,7 +218,7 @@ __global__ void __launch_bounds__(PairCfg<BN, DUAL>::kThreads, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&L.tfull[b], 1);
-            mbar_init(&L.tempty[b], 2 * kPEpiWarps);  // both CTAs' epilogue warps (used in the even CTA)
+            mbar_init(&L.tempty[b], 2 * C::kEpi);  // both CTAs' epilogue warps (used in the even CTA)
         }
         *L.abort = 0;
         fence_barrier_init();
@@ -292,7 +299,9 @@ __global__ void __launch_bounds__(PairCfg<BN, DUAL>::kThreads, 1)
         }
     } else {
         // ---------------- epilogue (both CTAs: their own 128 rows) ----------------
-        const int q = warp & 3;
+        const int q = warp & 3;                   // TMEM lane quarter of this warp
+        const int part = (warp - 2) / 4;          // column half (8 epilogue warps) or 0
+        const int c_beg = part * (BN * 4 / C::kEpi), c_end = c_beg + BN * 4 / C::kEpi;
         const int trow = q * 32 + lane;
         const uint32_t tempty0 = mapa_shared(smem_u32(&L.tempty[0]), 0);
         int local = 0;
@@ -317,7 +326,7 @@ __global__ void __launch_bounds__(PairCfg<BN, DUAL>::kThreads, 1)
             const uint32_t tbase = tmem + buf * C::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
             const int m_end = min(p.n_tok, tok0 + BN);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = c_beg; c0 < c_end; c0 += 32) {
                 if (tok0 + c0 >= m_end) break;  // warp-uniform
                 float v[32], u[32];
                 tmem_ld32(tbase + c0, v);
