@@ -11,7 +11,7 @@
 // kernel's 16 + BN/8 KB for 128 x BN x 64: a third less operand traffic at
 // BN = 256, which is what limits the one-CTA kernel's tensor-pipe occupancy.
 //
-// Roles per CTA (192 threads): warp 0 TMA producer (both CTAs: their own
+// Roles per CTA (192 threads, 320 for SwiGLU): warp 0 TMA producer (both CTAs: their own
 // halves, completing on the even CTA's stage barrier); warp 1 TMEM
 // allocator (both, a pair allocation) and MMA issuer (even CTA only); warps
 // 2-5 epilogue (both: their own 128 rows). The even CTA's MMA commits free a
@@ -35,7 +35,6 @@ constexpr int PBK = 64;
 // quarter, each taking half the token columns: the two accumulators' SwiGLU
 // is the heavier epilogue, and with one accumulator buffer it does not
 // overlap the next tile's MMAs)
-constexpr int kPEpiWarps = 4;
 template <bool DUAL>
 constexpr int pair_epi_warps() { return DUAL ? 8 : 4; }
 constexpr int kPSmemBudget = 224 * 1024;
