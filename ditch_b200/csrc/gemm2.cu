@@ -14,7 +14,7 @@
 // Roles per CTA (192 threads, 320 for SwiGLU): warp 0 TMA producer (both CTAs: their own
 // halves, completing on the even CTA's stage barrier); warp 1 TMEM
 // allocator (both, a pair allocation) and MMA issuer (even CTA only); warps
-// 2-5 epilogue (both: their own 128 rows). The even CTA's MMA commits free a
+// 2-5 (2-9 for SwiGLU) epilogue (both: their own 128 rows). The even CTA's MMA commits free a
 // stage and hand over an accumulator in both CTAs at once (multicast commit).
 // No TMA multicast: each CTA loads only its own tiles from this GPU's memory.
 //
