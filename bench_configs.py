@@ -697,6 +697,12 @@ def run_c4(args, dev, world=1, rank=0, dist=None):
     hbm, tf_burst, tf_sust, src = measured_peaks()
     tokens = P * S
     fl = c4_flops(spec, tokens)
+    if world > 1:
+        # expert parallel: the owners' grouped GEMMs run over the exchange's
+        # receive capacity (their row counts stay on the device), so the
+        # launch records overcount; each rank's GEMM work is its own tokens'
+        # linear layers (balanced routing), counted analytically
+        gemm_flops = fl * args.steps
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
     line = {
         "metric": "trial-eval forward tokens/s", "value": round(tokens * world * args.steps / (ms / 1000.0), 1),
