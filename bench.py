@@ -57,9 +57,9 @@ def parse():
     ap.add_argument("--max-new", type=int, default=100, help="gen: tokens generated per prompt")
     ap.add_argument("--row-normalization", default="none", choices=["none", "pre", "full"],
                     help="c1 / c2: the edit's row normalisation (full: rank-3 delta from the randomised SVD)")
-    ap.add_argument("--cta-pairs", type=int, default=1,
+    ap.add_argument("--cta-pairs", type=int, default=2,
                     help="dense bf16 GEMMs of 512+ tokens on CTA pairs (tcgen05 cta_group::2): 0 never, 1 products "
-                         "with one accumulator (the library's default), 2 SwiGLU products too")
+                         "with one accumulator, 2 SwiGLU products too (the library's default)")
     ap.add_argument("--deterministic", type=int, default=0,
                     help="1: K splits summed in a fixed order (stream-K) instead of atomically")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")

@@ -99,7 +99,7 @@ struct ditch_cuda_device {
     bool deterministic = false;  // K splits summed in a fixed order (no atomics)
     bool decode_cache = true;    // staged GEMMs keep their weight's bf16 copy
     bool f32_split = false;      // models loaded next run f32-level split-bf16 products
-    int cta_pairs = 1;           // wide dense bf16 GEMMs on CTA pairs (cta_group::2): 1 single-accumulator, 2 + SwiGLU
+    int cta_pairs = 2;           // wide dense bf16 GEMMs on CTA pairs (cta_group::2): 1 single-accumulator, 2 + SwiGLU
     // profiling of GEMMs
     bool profiling = false;
     std::vector<ditch::GemmEvent> events;

@@ -436,10 +436,10 @@ __global__ void k_scale_vec(const float *v, float lambda, int n, float *b) {
 // both the maximum and the sum): piece (row, c) finds its maximum m_c and
 // s_c = sum exp(x - m_c) in f64; the row's log-sum-exp combines the pieces in
 // order, lse = m + log(sum_c s_c exp(m_c - m)) with m = max m_c, as
-// src/tensor.zig:1203-1210 (an f64 sum, the result in f32). Each term is
-// f32 expf of the f32 difference, widened to f64 before it is added (the
-// reference takes the exp in f64: the terms differ by one f32 rounding, about
-// 6e-8 relative, far below the f32 result's own rounding after the log).
+// src/tensor.zig:1203-1210 (the f32 difference, its exp and the sum in f64,
+// the result in f32). The exp stays in f64: the KL moves one for one with
+// the f32 lse, so an f32 exp (6e-8 relative per term) would flip the lse's
+// last bit on some rows and move a small KL by a few 1e-4 relative.
 // The KL pieces then add exp(b)(b - (x - lse)) in f64 (src/scorers.zig:
 // 385-400: the reference forms each term in f64; here the term is an f32
 // product of f32 expf and the f32 difference, widened before the f64 sum)
@@ -488,7 +488,7 @@ __global__ void __launch_bounds__(kKlThreads) k_lse_part(const float *x, int voc
     double s = 0.0;
     if (m > -INFINITY) {
 #pragma unroll
-        for (int k = 0; k < kKlEach; k++) s += (double)expf(v[k] - m);
+        for (int k = 0; k < kKlEach; k++) s += exp((double)(v[k] - m));
     }
     s = block_sum_d(s, shd);
     if (threadIdx.x == 0) part[(long long)row * chunks + c] = make_double2((double)m, s);

@@ -444,8 +444,8 @@ cudaError_t launch_gemm_pair(const GemmOperand &a, const GemmOperand *a2, const 
     const bool dual = (p.flags & kEpiSwiglu) != 0;
     if (dual) {
         // gate and up accumulators of 256 tokens fill TMEM (one buffer): the
-        // epilogue does not overlap the next tile, but each SM moves 48 KB
-        // per 2 x 128 x 256 x 64 products
+        // epilogue does not overlap the next tile (eight epilogue warps keep
+        // it short), but each SM moves 48 KB per 2 x 128 x 256 x 64 products
         if (!a2) return cudaErrorInvalidValue;
         return launch_pair_t<256, true>(a, a2, b, p, num_sms, stream);
     }

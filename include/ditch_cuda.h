@@ -438,9 +438,10 @@ int ditch_cuda_set_deterministic(ditch_cuda_device *dev, int enabled);
  * cuts the operand traffic per SM by a third. Level 0: never; 1: products
  * with one accumulator (qkv, o_proj, down_proj, LM head); 2: the SwiGLU
  * gate / up products too (256-token tiles, their two accumulators filling
- * TMEM). The same products either way (f32 accumulation of the same bf16
- * operands). Default 1 (measured on B200, C2 trial: 0 115.9 ms, 1 113.2 ms,
- * 2 117.6 ms: the 256-token SwiGLU tiles leave the epilogue unoverlapped).
+ * TMEM; their epilogue runs on eight warps). The same products either way
+ * (f32 accumulation of the same bf16 operands). Default 2 (measured on B200,
+ * C2 trial: 1 108.6 ms, 2 106.5 ms; the pairs move less operand traffic, so
+ * under the power cap they also hold a higher clock).
  * No counterpart in the reference (a tuning knob of this backend). */
 int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int level);
 /* f32-level products for f32 and f16 weights. By default a resident model

@@ -25,7 +25,7 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture
 def pairs(device):
     yield device
-    device.set_cta_pairs(1)  # the library's default
+    device.set_cta_pairs(2)  # the library's default
 
 
 @pytest.mark.parametrize("rows,cols,m", [(256, 256, 512), (4096 + 128, 1024 + 64, 1000), (6144, 4096, 2048),
