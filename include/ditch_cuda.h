@@ -440,8 +440,9 @@ int ditch_cuda_set_deterministic(ditch_cuda_device *dev, int enabled);
  * gate / up products too (256-token tiles, their two accumulators filling
  * TMEM; their epilogue runs on eight warps). The same products either way
  * (f32 accumulation of the same bf16 operands). Default 2 (measured on B200,
- * C2 trial: 1 108.6 ms, 2 106.5 ms; the pairs move less operand traffic, so
- * under the power cap they also hold a higher clock).
+ * C2 trial at about 1.52 GHz: 108.5 ms at either level; the SwiGLU pair
+ * tile moves a third less operand traffic per FLOP, 1.48 ms per launch
+ * under ncu against 1.49 for one CTA per tile).
  * No counterpart in the reference (a tuning knob of this backend). */
 int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int level);
 /* f32-level products for f32 and f16 weights. By default a resident model
