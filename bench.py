@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--cta-pairs", type=int, default=2,
                     help="dense bf16 GEMMs of 512+ tokens on CTA pairs (tcgen05 cta_group::2): 0 never, 1 products "
                          "with one accumulator, 2 SwiGLU products too (the library's default)")
+    ap.add_argument("--attention-tc", type=int, default=2,
+                    help="prefill attention of prompts up to 128 tokens on tcgen05: 0 never (mma.sync), 1 one CTA per "
+                         "SM, 2 two CTAs per SM for prompts up to 64 tokens (the library's default)")
     ap.add_argument("--deterministic", type=int, default=0,
                     help="1: K splits summed in a fixed order (stream-K) instead of atomically")
     ap.add_argument("--fmt", default="fp8", help="gemm mode: bf16 | fp8 | mxfp4 | int4")
@@ -350,6 +353,9 @@ def config_block(args):
                      1: "CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles) for qkv, o_proj and down_proj; SwiGLU "
                         "gate / up on one CTA per tile",
                      2: "CTA pairs for every dense GEMM of 512+ tokens"}[args.cta_pairs],
+            "attention": {0: "mma.sync (bf16 hi/lo products)",
+                          1: "tcgen05, one CTA per SM (bf16 hi/lo products, TMEM accumulators)",
+                          2: "tcgen05, two CTAs per SM (bf16 hi/lo products, TMEM accumulators)"}[args.attention_tc],
             "layers": args.layers, "prompts_per_gpu": args.prompts, "seq_len": args.seq, "vocab": C2["vocab"],
             "parallelism": f"dp{args.gpus} (prompt batches; residual sums and KL summed over the ranks by the "
                            "library's peer-group reduction over NVLink)",
@@ -412,6 +418,7 @@ def main():
         dev.set_decode_staging(args.stage_min_tokens)
     dev.set_deterministic(args.deterministic)
     dev.set_cta_pairs(args.cta_pairs)
+    dev.set_attention_tc(args.attention_tc)
     spec = dict(C2, n_layers=args.layers)
     L, V, P, S = spec["n_layers"], spec["vocab"], args.prompts, args.seq
     t0 = time.time()

@@ -968,6 +968,7 @@ def run(args):
         dev.set_decode_staging(args.stage_min_tokens)
     dev.set_deterministic(args.deterministic)
     dev.set_cta_pairs(args.cta_pairs)
+    dev.set_attention_tc(args.attention_tc)
     if args.config == "c4" or (args.config == "c5" and world > 1):
         if args.config == "c4":
             run_c4(args, dev, world, rank, dist)

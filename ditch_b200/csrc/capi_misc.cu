@@ -290,6 +290,14 @@ int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int level) {
     return DITCH_CUDA_OK;
 }
 
+int ditch_cuda_set_attention_tc(ditch_cuda_device *dev, int level) {
+    REQUIRE(dev, "null device");
+    REQUIRE(level >= 0 && level <= 2, "attention level must be 0, 1 or 2");
+    std::lock_guard<std::mutex> lk(dev->mu);
+    dev->attn_tc = level;
+    return DITCH_CUDA_OK;
+}
+
 int ditch_cuda_set_f32_split(ditch_cuda_device *dev, int enabled) {
     REQUIRE(dev, "null device");
     std::lock_guard<std::mutex> lk(dev->mu);

@@ -100,6 +100,7 @@ struct ditch_cuda_device {
     bool decode_cache = true;    // staged GEMMs keep their weight's bf16 copy
     bool f32_split = false;      // models loaded next run f32-level split-bf16 products
     int cta_pairs = 2;           // wide dense bf16 GEMMs on CTA pairs (cta_group::2): 1 single-accumulator, 2 + SwiGLU
+    int attn_tc = 2;             // prefill attention on tcgen05: 0 off, 1 one CTA per item, 2 two per SM (<= 64 tokens)
     // profiling of GEMMs
     bool profiling = false;
     std::vector<ditch::GemmEvent> events;

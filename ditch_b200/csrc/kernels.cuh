@@ -101,6 +101,8 @@ struct AttnParams {
     int *status;
     int max_len;        // longest prompt of the batch
     int force_generic;  // use the one-warp-per-query kernel for any head size
+    int tc;             // prompts of at most 128 tokens on tcgen05 (attention_tc.cu): 0 off, 1 a CTA per
+                        // (prompt, kv head), 2 two CTAs per SM for prompts of at most 64 tokens
 };
 // Causal attention within each prompt with GQA, RoPE (neox) and optional q/k
 // norms (src/model.zig:4226-4374, attentionWorker 2935-2986).
@@ -108,6 +110,10 @@ cudaError_t attention_prefill(const AttnParams &p, cudaStream_t st);
 // True when attention_prefill leaves the q and k columns of the QKV rows
 // normed and roped in place (the tensor-core path, head sizes 64 and 128).
 bool attention_prefill_preps_in_place(int head_dim, int force_generic);
+// The tcgen05 kernel for batches whose prompts are all at most 128 tokens
+// (head sizes 64 and 128, bf16 output); q and k already normed and roped.
+bool attention_tc_eligible(const AttnParams &p);
+cudaError_t attention_tc(const AttnParams &p, cudaStream_t st);
 
 // ---- greedy decode with a KV cache (src/model.zig:5378-5444) ---------------
 // One layer's cache: keys (normed and roped) and values, f32

@@ -516,6 +516,7 @@ int forward_batch(ditch_cuda_model *m, Batch &b, int nc, int nl, int mode) {
         ap.scale = 1.0f / std::sqrt((float)c.head_dim);
         ap.status = dev->status;
         ap.max_len = b.h_len.empty() ? 1 : *std::max_element(b.h_len.begin(), b.h_len.end());
+        ap.tc = dev->attn_tc;
         if (mode == kFwdPrompts) {
             DITCH_LAUNCH(dev, attention_prefill(ap, st));
         } else {

@@ -138,6 +138,7 @@ SIGNATURES = {
     "ditch_cuda_set_deterministic": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_f32_split": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_cta_pairs": (C.c_int, [vp, C.c_int]),
+    "ditch_cuda_set_attention_tc": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_set_decode_cache": (C.c_int, [vp, C.c_int]),
     "ditch_cuda_peer_handle_bytes": (sz, []),
     "ditch_cuda_group_create": (C.c_int, [vp, C.c_int, C.c_int, sz, C.POINTER(vp), vp]),
@@ -360,6 +361,12 @@ class Device:
         """Wide dense bf16 GEMMs on CTA pairs (cta_group::2): 0 never, 1
         single-accumulator products, 2 the SwiGLU products too."""
         check(lib().ditch_cuda_set_cta_pairs(self.h, int(level)))
+
+    def set_attention_tc(self, level):
+        """Prefill attention of prompts up to 128 tokens on tcgen05: 0 never
+        (the mma.sync kernel), 1 one CTA per (prompt, kv head), 2 (default)
+        two CTAs per SM for prompts of at most 64 tokens."""
+        check(lib().ditch_cuda_set_attention_tc(self.h, int(level)))
 
     def set_f32_split(self, on):
         """Models loaded afterwards run f32-level split-bf16 products for their

@@ -445,6 +445,17 @@ int ditch_cuda_set_deterministic(ditch_cuda_device *dev, int enabled);
  * under ncu against 1.49 for one CTA per tile).
  * No counterpart in the reference (a tuning knob of this backend). */
 int ditch_cuda_set_cta_pairs(ditch_cuda_device *dev, int level);
+/* Prefill attention of batches whose prompts are all at most 128 tokens on
+ * the tcgen05 tensor cores (Q.K^T and P.V with TMEM accumulators, head sizes
+ * 64 and 128). Level 0: never (the mma.sync kernel); 1: one CTA per (prompt,
+ * kv head) with the whole 128-row Q tile staged; 2: as 1, and prompts of at
+ * most 64 tokens on a kernel that stages Q by 64-dim halves so that two CTAs
+ * share each SM (one's loads overlap the other's products). Longer prompts, other head sizes and the f32-level
+ * split mode use the mma.sync kernel. Every kernel splits the operands into
+ * bf16 hi + lo and sums hi*hi + hi*lo + lo*hi in f32, so they agree to f32
+ * rounding. Default 2. No counterpart in the reference (a tuning knob of
+ * this backend). */
+int ditch_cuda_set_attention_tc(ditch_cuda_device *dev, int level);
 /* f32-level products for f32 and f16 weights. By default a resident model
  * rounds f32 / f16 weights to bf16 at load and rounds every GEMM input to
  * bf16 (tensor-core products with f32 accumulation), about 2^-9 relative per
