@@ -113,7 +113,10 @@ __device__ __forceinline__ SmemLayout<C> carve(uint8_t *smem_raw) {
     return L;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// silu with the approximate exponential and division of the SFU (a few ulp
+// of f32, far below the bf16 rounding of the product that follows; the
+// CTA-pair kernel forms it the same way)
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // Where a tile's operands and outputs live, in dense or grouped mode.
 struct TileInfo {

@@ -32,9 +32,9 @@ namespace {
 constexpr int PBM = 128;  // weight rows per CTA (256 per pair)
 constexpr int PBK = 64;
 // epilogue warps: 4 (one per TMEM lane quarter), 8 for SwiGLU (two per lane
-// quarter, each taking half the token columns: the two accumulators' SwiGLU
-// is the heavier epilogue, and with one accumulator buffer it does not
-// overlap the next tile's MMAs)
+// quarter, each taking half the token columns: the two accumulators fill
+// TMEM, so the next tile's MMAs wait until the SwiGLU values are in
+// registers; the stores follow the hand-back)
 template <bool DUAL>
 constexpr int pair_epi_warps() { return DUAL ? 8 : 4; }
 constexpr int kPSmemBudget = 224 * 1024;
@@ -184,7 +184,45 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     }
 }
 
-__device__ __forceinline__ float silu_p(float x) { return x / (1.0f + __expf(-x)); }
+// silu with the approximate exponential and division of the SFU (a few ulp
+// of f32, far below the bf16 rounding of the product that follows)
+__device__ __forceinline__ float silu_p(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// 32 lanes x 16 columns of TMEM into registers, without waiting: the values
+// are defined only after tmem_wait_pass on the same array.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+#define DITCH_R8(a, i) "+r"(a[i]), "+r"(a[i + 1]), "+r"(a[i + 2]), "+r"(a[i + 3]), \
+    "+r"(a[i + 4]), "+r"(a[i + 5]), "+r"(a[i + 6]), "+r"(a[i + 7])
+
+// Waits for every TMEM load this thread issued. Both arrays pass through the
+// asm statement, so no use of their values can be scheduled above the wait.
+__device__ __forceinline__ void tmem_wait_pass(uint32_t (&a)[16], uint32_t (&b)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : DITCH_R8(a, 0), DITCH_R8(a, 8), DITCH_R8(b, 0), DITCH_R8(b, 8)
+                 :
+                 : "memory");
+}
+#undef DITCH_R8
+
+// silu(g + bias) * u over 16 columns, rounded to bf16 (to nearest even, as
+// f32_to_bf16_bits for every non-NaN value) and packed two per word.
+__device__ __forceinline__ void swiglu16_bf16(const uint32_t (&g)[16], const uint32_t (&u)[16], float bias,
+                                              uint32_t (&pk)[8]) {
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float lo = silu_p(__uint_as_float(g[2 * j]) + bias) * __uint_as_float(u[2 * j]);
+        const float hi = silu_p(__uint_as_float(g[2 * j + 1]) + bias) * __uint_as_float(u[2 * j + 1]);
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk[j]) : "f"(hi), "f"(lo));
+    }
+}
 
 // Pair tile `tile`: weight tile (256 rows) and token tile (BN), in bands of
 // 8 token tiles run weight tile by weight tile (the tiles the 74 pairs hold
@@ -324,60 +362,117 @@ __global__ void __launch_bounds__(PairCfg<BN, DUAL>::kThreads, 1)
             }
             const uint32_t tbase = tmem + buf * C::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
             const int m_end = min(p.n_tok, tok0 + BN);
-#pragma unroll 1
-            for (int c0 = c_beg; c0 < c_end; c0 += 32) {
-                if (tok0 + c0 >= m_end) break;  // warp-uniform
-                float v[32], u[32];
-                tmem_ld32(tbase + c0, v);
-                if (DUAL) tmem_ld32(tbase + BN + c0, u);
-                const int m0 = tok0 + c0;
-                const int mv = min(32, m_end - m0);
-                // every load of a chunk before its first store (see the one-CTA kernel)
-                float r[32];
+            if constexpr (DUAL) {
+                // One accumulator buffer: the next tile's MMAs wait for it.
+                // So the warp reads its gate and up columns (both loads of a
+                // chunk in flight together), forms silu(gate) * up as bf16 in
+                // registers, hands the accumulator back, and only then stores.
+                constexpr int kCh = BN * 4 / C::kEpi / 16;  // 16-column chunks per warp
+                static_assert(kCh % 2 == 0, "chunks go in pairs");
+                uint32_t pk[kCh][8];                         // bf16 pairs (even token low)
+                const uint32_t tw = tbase + c_beg;
+                // chunk ci holds tokens from tok0 + c_beg + 16 ci; once one is past
+                // the last token, so are the later ones (warp-uniform)
+                auto live = [&](int ci) { return tok0 + c_beg + ci * 16 < m_end; };
+                // the next chunk's two loads are in flight while this chunk is formed
+                uint32_t ga[16], ua[16], gb[16], ub[16];
+                if (live(0)) {
+                    tmem_ld16_issue(tw, ga);
+                    tmem_ld16_issue(tw + BN, ua);
+                }
 #pragma unroll
-                for (int j = 0; j < 32; j++) r[j] = v[j];
-                if (p.xa && any_delta) {
-#pragma unroll 1
-                    for (int t = 0; t < drank; t++) {
-                        float xa[32];
-#pragma unroll
-                        for (int j = 0; j < 32; j++) xa[j] = j < mv ? __ldg(p.xa + (long long)(m0 + j) * drank + t) : 0.0f;
-#pragma unroll
-                        for (int j = 0; j < 32; j++) r[j] += xa[j] * dbn[t];
+                for (int ci = 0; ci < kCh; ci += 2) {
+                    if (live(ci)) {
+                        tmem_wait_pass(ga, ua);
+                        if (live(ci + 1)) {
+                            tmem_ld16_issue(tw + (ci + 1) * 16, gb);
+                            tmem_ld16_issue(tw + BN + (ci + 1) * 16, ub);
+                        }
+                        swiglu16_bf16(ga, ua, bias, pk[ci]);
+                    }
+                    if (live(ci + 1)) {
+                        tmem_wait_pass(gb, ub);
+                        if (ci + 2 < kCh && live(ci + 2)) {
+                            tmem_ld16_issue(tw + (ci + 2) * 16, ga);
+                            tmem_ld16_issue(tw + BN + (ci + 2) * 16, ua);
+                        }
+                        swiglu16_bf16(gb, ub, bias, pk[ci + 1]);
                     }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);  // the even CTA's tempty[buf]
+                if (n_ok) {
+                    uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + n;
 #pragma unroll
-                for (int j = 0; j < 32; j++) r[j] += bias;
-                const long long o0 = (long long)m0 * p.ldo + n;
-                if (!n_ok) {
-                } else if (DUAL) {
-                    uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + o0;
+                    for (int ci = 0; ci < kCh; ci++) {
+                        const int m0 = tok0 + c_beg + ci * 16;
+                        if (m0 < m_end) {
+                            const int mv = min(16, m_end - m0);
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (j < mv) ob[(long long)j * p.ldo] = f32_to_bf16_bits(silu_p(r[j]) * u[j]);
-                } else if (p.flags & kEpiResidual) {
-                    float *of = reinterpret_cast<float *>(p.out) + o0;
-                    float old[32];
-#pragma unroll
-                    for (int j = 0; j < 32; j++) old[j] = j < mv ? of[(long long)j * p.ldo] : 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (j < mv) of[(long long)j * p.ldo] = old[j] + r[j];
-                } else if (p.flags & kEpiOutBf16) {
-                    uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + o0;
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (j < mv) ob[(long long)j * p.ldo] = f32_to_bf16_bits(r[j]);
-                } else {
-                    float *of = reinterpret_cast<float *>(p.out) + o0;
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (j < mv) of[(long long)j * p.ldo] = r[j];
+                            for (int j = 0; j < 16; j++)
+                                if (j < mv)
+                                    ob[(long long)(m0 + j) * p.ldo] =
+                                        static_cast<uint16_t>((j & 1) ? (pk[ci][j >> 1] >> 16) : pk[ci][j >> 1]);
+                        }
+                    }
                 }
+            } else {
+#pragma unroll 1
+                for (int c0 = c_beg; c0 < c_end; c0 += 32) {
+                    if (tok0 + c0 >= m_end) break;  // warp-uniform
+                    float v[32], u[32];
+                    tmem_ld32(tbase + c0, v);
+                    if (DUAL) tmem_ld32(tbase + BN + c0, u);
+                    const int m0 = tok0 + c0;
+                    const int mv = min(32, m_end - m0);
+                    // every load of a chunk before its first store (see the one-CTA kernel)
+                    float r[32];
+#pragma unroll
+                    for (int j = 0; j < 32; j++) r[j] = v[j];
+                    if (p.xa && any_delta) {
+#pragma unroll 1
+                        for (int t = 0; t < drank; t++) {
+                            float xa[32];
+#pragma unroll
+                            for (int j = 0; j < 32; j++) xa[j] = j < mv ? __ldg(p.xa + (long long)(m0 + j) * drank + t) : 0.0f;
+#pragma unroll
+                            for (int j = 0; j < 32; j++) r[j] += xa[j] * dbn[t];
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; j++) r[j] += bias;
+                    const long long o0 = (long long)m0 * p.ldo + n;
+                    if (!n_ok) {
+                    } else if (DUAL) {
+                        uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + o0;
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < mv) ob[(long long)j * p.ldo] = f32_to_bf16_bits(silu_p(r[j]) * u[j]);
+                    } else if (p.flags & kEpiResidual) {
+                        float *of = reinterpret_cast<float *>(p.out) + o0;
+                        float old[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) old[j] = j < mv ? of[(long long)j * p.ldo] : 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < mv) of[(long long)j * p.ldo] = old[j] + r[j];
+                    } else if (p.flags & kEpiOutBf16) {
+                        uint16_t *ob = reinterpret_cast<uint16_t *>(p.out) + o0;
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < mv) ob[(long long)j * p.ldo] = f32_to_bf16_bits(r[j]);
+                    } else {
+                        float *of = reinterpret_cast<float *>(p.out) + o0;
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < mv) of[(long long)j * p.ldo] = r[j];
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);  // the even CTA's tempty[buf]
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);  // the even CTA's tempty[buf]
         }
     }
     __syncwarp();
@@ -435,7 +530,9 @@ bool gemm_pair_fits(const GemmParams &p, int fmt, int k, int num_sms) {
     // enough token tiles to fill the pairs; no K splits, stream-K or atomics;
     // SwiGLU pairs only at level 2
     const bool dual = (p.flags & kEpiSwiglu) != 0;
-    return p.cta_pairs >= (dual ? 2 : 1) && fmt == kFmtBf16 && !p.sched && p.k_splits <= 1 && !p.stream_k &&
+    // (a SwiGLU product with a delta term, which no caller makes, takes the one-CTA kernel)
+    return p.cta_pairs >= (dual ? 2 : 1) && !(dual && p.xa) && fmt == kFmtBf16 && !p.sched && p.k_splits <= 1 &&
+           !p.stream_k &&
            !(p.flags & kEpiAtomic) && p.m_w >= 2 * PBM && p.n_tok >= 512 && k >= 4 * PBK && num_sms >= 2;
 }
 
