@@ -225,10 +225,13 @@ __device__ __forceinline__ void swiglu16_bf16(const uint32_t (&g)[16], const uin
 }
 
 // Pair tile `tile`: weight tile (256 rows) and token tile (BN), in bands of
-// 8 token tiles run weight tile by weight tile (the tiles the 74 pairs hold
-// at once share a few operand tiles, which stay in L2).
+// 16 token tiles run weight tile by weight tile (the tiles the 74 pairs hold
+// at once share a few operand tiles, which stay in L2). Measured on the C2
+// trial over two boxes: bands of 16 took 1.3-1.7 % less time per trial than
+// bands of 8; 4, 24 and 32 were slower than 8 or level with it; 12 came
+// within run-to-run noise of 16.
 __device__ __forceinline__ void pair_tile(const GemmParams &p, int tile, int bn, int &wt, int &tok0) {
-    constexpr int kBand = 8;
+    constexpr int kBand = 16;
     const int band = tile / (kBand * p.w_tiles);
     const int idx = tile - band * kBand * p.w_tiles;
     const int g = min(kBand, p.t_tiles - band * kBand);
